@@ -1,0 +1,176 @@
+/*
+ * tsds.h - C ABI of libtsds.so, the sm_100a speculative-decoding hot path.
+ *
+ * Every entry point takes device pointers, sizes and a cudaStream_t, launches
+ * asynchronously on that stream, never allocates, never synchronises, and
+ * returns TSDS_OK or a TSDS_E_* code (bad shape / alignment, launch error).
+ * The caller owns every buffer, including the workspace some entry points
+ * take (query its size with the matching *_workspace_bytes function).
+ * Calls on different streams with different workspaces may run
+ * concurrently; calls that share a workspace must be ordered.
+ *
+ * Element types: bf16 buffers are "const void*" / "void*" holding
+ * __nv_bfloat16; token ids are int64 (torch.long); lengths, positions and
+ * accept lengths are int32.
+ *
+ * Layouts (row-major):
+ *   activations  x[M][N]        M = B*T token rows, sequence b owns rows b*T..b*T+T-1
+ *   weights      W[out][in]     the HF nn.Linear layout ("in" contiguous)
+ *   KV cache     C[B][Hkv][S][D] one tensor per layer (qwen_model.py:86-94)
+ *   RoPE tables  cos/sin[P][D/2] bf16 (qwen_model.py:8-14)
+ *
+ * Each declaration names the reference interface it replaces (file:line in
+ * the reference project, Mog9/tri-sds).
+ */
+#ifndef TSDS_H
+#define TSDS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tsds_stream_t; /* == cudaStream_t */
+
+enum {
+  TSDS_OK = 0,
+  TSDS_E_INVALID = 1,     /* shape / argument out of the supported range */
+  TSDS_E_ALIGN = 2,       /* pointer or leading dimension not 16-byte aligned */
+  TSDS_E_LAUNCH = 3,      /* the CUDA launch itself failed */
+  TSDS_E_WORKSPACE = 4,   /* workspace smaller than *_workspace_bytes */
+  TSDS_E_TIMEOUT = 5,     /* a device-side bounded wait gave up (status word) */
+  TSDS_E_UNSUPPORTED = 6, /* no kernel instantiated for this configuration */
+  TSDS_E_DEVICE = 7       /* device query failed / not an sm_100 device */
+};
+
+/* Human-readable name of a status code (static string). */
+const char* tsds_status_string(int status);
+/* ABI version: bumps on any signature change. */
+int tsds_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Embedding gather: out[m][:] = table[ids[m * ids_stride]][:]; an id outside
+ * [0, vocab) gives a zero row.
+ * Replaces state.embed_w[input_ids] (qwen_model.py:188,199; eagle_head.py:113).
+ */
+int tsds_embed(const int64_t* ids, int ids_stride, const void* table, void* out, int M, int N,
+               int vocab, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm: out = x * rsqrt(mean(x^2) + eps) * w in fp32, one cast to bf16.
+ * Replaces rms_norm / _rms_norm_kernel (norm.py:42-72).
+ * x, out: [rows][n] with row strides ldx, ldo (elements).
+ */
+int tsds_rms_norm(const void* x, const void* w, void* out, int rows, int n, int ldx, int ldo,
+                  float eps, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Sequence bookkeeping for one forward of T new tokens per sequence (chain):
+ *   starts[b]    = base[b] + offset      (first cache row written)
+ *   positions[m] = starts[b] + t         (RoPE position of row m = b*T+t)
+ * Replaces the host-side start_pos / positions of qwen_model.py:102,185.
+ */
+int tsds_prep_chain(const int32_t* base, int offset, int B, int T, int32_t* starts,
+                    int32_t* positions, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Projection of the new tokens into q and the KV cache, after the fused
+ * GEMM has produced qkv[M][Hq*D + 2*Hkv*D] (bf16):
+ *   q, k <- RMSNorm_D(q, q_norm_w), RMSNorm_D(k, k_norm_w)   (skipped if NULL)
+ *   q, k <- rotate-half RoPE at positions[m], bf16 rounding as the reference
+ *   q_out[m][h*D..]                       = q
+ *   k_cache[b][kvh][starts[b]+t][..]      = k ;  v_cache likewise = v
+ *   (rows with starts[b]+t or positions[m] outside [0, S) are skipped;
+ *    S is also the length of the RoPE tables)
+ * Replaces the QK-norm (absent in the reference), apply_rope and the cache
+ * stores of qwen_model.py:109-119 / 154-164, and the RoPE + KV-write half
+ * of _rmsnorm_qkv_rope_kernel (fused_qwen_decode.py:212-250).
+ */
+int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                         const void* cos, const void* sin, const int32_t* positions,
+                         const int32_t* starts, void* q_out, void* k_cache, void* v_cache,
+                         int B, int T, int Hq, int Hkv, int D, int S, float eps,
+                         tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Skinny GEMM family, out[m][j] = epilogue(sum_k W[j][k] * x[m][k]), fp32
+ * accumulation.  x: [M][K] (row stride ldx), W: [n_out][K], K % 8 == 0.
+ * Picks the CUDA-core GEMV for small M and the tcgen05 path above it.
+ *
+ * tsds_linear:           out = bf16(acc)                         (qwen_model.py:108,153)
+ * tsds_linear_residual:  out = bf16(res + bf16(acc))              (fused_qwen_decode.py:308-324,
+ *                                                                  422-438; qwen_model.py:133-134,143-144)
+ *                        out may alias res (in-place residual stream).
+ * tsds_linear_swiglu:    W = [gate; up] ([2*n_out][K]);
+ *                        out = bf16(bf16(silu(bf16(acc_g))) * bf16(acc_u))
+ *                                                                 (fused_qwen_decode.py:371-387;
+ *                                                                  qwen_model.py:139-142)
+ */
+size_t tsds_linear_workspace_bytes(int M, int n_out, int K);
+int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
+                void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,
+                         int M, int n_out, int K, void* workspace, size_t workspace_bytes,
+                         tsds_stream_t stream);
+int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out,
+                       int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Verify / decode attention of T new tokens per sequence over the KV cache.
+ * q: [B*T][Hq][D] (RoPE applied); k/v cache [B][Hkv][S][D] holding the new
+ * tokens at rows starts[b]..starts[b]+T-1; out: [B*T][Hq][D] bf16.
+ * Query t of sequence b sees every row below starts[b] and, among the new
+ * rows, row starts[b]+j when bit j of tree_mask[b*T+t] is set; tree_mask
+ * NULL means causal (j <= t).  fp32 online softmax, scale = softmax scale.
+ * Keys are split into fixed chunks of split_keys rows (a multiple of 64);
+ * the split boundaries depend only on the key index, so a query's result
+ * does not depend on T or B.  max_kv bounds starts[b]+T (sizes the grid).
+ * Replaces attention_gqa / _decode_attn_gqa_kernel (attention.py:236-318)
+ * and the verify SDPA of qwen_model.py:121-131.  D = 128, T <= 32, T*Hq/Hkv <= 1024.
+ */
+size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int max_kv,
+                                      int split_keys);
+int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                          const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq,
+                          int Hkv, int D, int S, int max_kv, int split_keys, float scale,
+                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * LM head + greedy pick: logits[m][v] = bf16(sum_k x[m][k] * W[v][k]);
+ * argmax_out[m * argmax_stride] = lowest index of the largest bf16 logit
+ * (torch.argmax semantics).
+ * x is the final-normed hidden state.  logits_out may be NULL.
+ * Replaces the LM head + argmax of qwen_model.py:192,205 and
+ * eagle_head.py:120-121.
+ */
+size_t tsds_lm_head_workspace_bytes(int M, int vocab);
+int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
+                        int argmax_stride, int M, int vocab, int K, void* workspace,
+                        size_t workspace_bytes, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Greedy acceptance + KV commit for one chain cycle (replaces the verify /
+ * accept step that tri_sds/worker.py:76-78 leaves unimplemented).
+ *   draft[B][K], target[B][K+1]  (argmax ids)
+ *   n = longest prefix with draft[b][i] == target[b][i]
+ *   accept_len[b] = n;  tokens[b][i] = target[b][i] for i <= n, else -1
+ *   target_len[b] += n + 1               (commit: rows past it are stale)
+ *   last[b] = token at position target_len-1 (cur if n == 0 else draft[n-1])
+ *   cur[b]  = target[b][n]               (the bonus token)
+ */
+int tsds_accept_greedy(const int64_t* draft, const int64_t* target, int32_t* accept_len,
+                       int64_t* tokens, int32_t* target_len, int64_t* last, int64_t* cur, int B,
+                       int K, tsds_stream_t stream);
+
+/* Build the verify input ids[b][0..K] = cur[b], draft[b][0..K-1]; and the
+ * draft's first-step input ids2[b] = last[b], cur[b]. */
+int tsds_gather_ids(const int64_t* cur, const int64_t* last, const int64_t* draft, int64_t* verify_ids,
+                    int64_t* draft_ids2, int B, int K, tsds_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TSDS_H */

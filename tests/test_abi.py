@@ -1,0 +1,42 @@
+"""The C-ABI library loads and exports every symbol include/tsds.h declares (no GPU needed)."""
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "tsds.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(tsds_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_matches_binding_table():
+    from tri_sds_b200 import _lib
+    assert _declared() == sorted(_lib.exported_symbols())
+
+
+def test_library_exports_every_symbol():
+    from tri_sds_b200 import _lib
+    from tri_sds_b200.build import LIB, build
+    if not os.path.exists(LIB):
+        build()
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.tsds_abi_version() == 1
+    assert lib.tsds_status_string(0) == b"ok"
+
+
+def test_argument_validation_without_gpu():
+    """Shape checks run on the host before any launch and return codes."""
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    assert lib.tsds_rms_norm(None, None, None, 0, 128, 128, 128, 1e-6, None) == 1          # INVALID
+    assert lib.tsds_linear(None, 8, None, None, 8, 1, 8, 8, None, 0, None) == 1
+    assert lib.tsds_qk_norm_rope_kv(None, None, None, None, None, None, None, None, None, None,
+                                    1, 1, 8, 2, 64, 16, 1e-6, None) == 6                     # UNSUPPORTED D
+    assert lib.tsds_verify_attention(None, None, None, None, None, None, 1, 40, 8, 2, 128, 64, 64, 64,
+                                     0.1, None, 0, None, None) == 1                           # T > 32

@@ -1,0 +1,78 @@
+"""ctypes binding of libtsds.so (the C ABI declared in include/tsds.h).
+
+The library is built in-tree (``python -m tri_sds_b200.build``).  There is
+no fallback: a missing or unloadable library raises at first use, and every
+non-zero status becomes a RuntimeError naming the entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("TSDS_LIB", os.path.join(_HERE, "libtsds.so"))
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_Z = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/tsds.h
+SIGNATURES = {
+    "tsds_status_string": (ctypes.c_char_p, [_I]),
+    "tsds_abi_version": (_I, []),
+    "tsds_embed": (_I, [_P, _I, _P, _P, _I, _I, _I, _P]),
+    "tsds_rms_norm": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _P]),
+    "tsds_prep_chain": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
+    "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
+    "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
+    "tsds_lm_head_workspace_bytes": (_Z, [_I, _I]),
+    "tsds_lm_head_argmax": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_accept_greedy": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "tsds_gather_ids": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Load libtsds.so once and attach the ABI signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libtsds.so not found at {LIB_PATH}: build it with `python -m tri_sds_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def call(name: str, *args) -> None:
+    """Call an int-returning entry point; raise on a non-zero status."""
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != 0:
+        msg = lib.tsds_status_string(st).decode()
+        raise RuntimeError(f"{name} failed: status {st} ({msg})")
+
+
+def query(name: str, *args):
+    return getattr(load(), name)(*args)

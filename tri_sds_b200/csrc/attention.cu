@@ -1,0 +1,394 @@
+// Verify / decode attention over the KV cache (GQA), head_dim 128.
+//
+// Work unit = (sequence b, kv head, key split).  The R = T * (Hq/Hkv) query
+// rows that share a kv head (T new tokens x the q heads of the group) are
+// processed together, so every K/V byte is read from HBM once per step
+// (the reference's GQA kernel re-reads K/V once per q head,
+// attention.py:330-368; its verify path materialises repeat_interleave
+// copies, qwen_model.py:122-123).
+//
+// * K/V tiles of 64 keys x 128 dims are staged by TMA (cp.async.bulk.tensor,
+//   128-byte swizzle, two 64-column boxes per tile) into a STAGES-deep
+//   shared-memory ring, completion tracked by mbarriers (bounded waits).
+// * Each warp owns 16 query rows.  S = Q K^T and O += P V run on the
+//   tensor cores (mma.m16n8k16 bf16 -> fp32); Q fragments stay in
+//   registers; K / V fragments come from the swizzled tiles by ldmatrix.
+// * fp32 online softmax in the exp2 domain; row max / sum across the four
+//   lanes sharing a row by shuffles.
+// * Keys are split into fixed chunks of `split_keys` rows.  A split writes
+//   its unnormalised O with (m, l) to the workspace and a combine pass merges
+//   the splits in index order.  Split boundaries depend only on the key
+//   index, and masked / empty splits contribute exact zeros, so a query's
+//   output is bit-identical whether it is verified with T tokens or decoded
+//   alone.
+#include "common.cuh"
+
+using namespace tsds;
+
+namespace {
+
+constexpr int D = 128;
+constexpr int TILE = 64;                    // keys per tile
+constexpr int HALF_BYTES = TILE * 128;      // one 64x64 bf16 box = 8 KB
+constexpr int TILE_BYTES = 4 * HALF_BYTES;  // K lo/hi + V lo/hi = 32 KB
+constexpr float LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// Byte offset of (key, 16-byte chunk c16 in [0,16)) inside a K or V tile
+// stored as two swizzled 64-column halves (TMA SWIZZLE_128B pattern:
+// chunk index XOR (row & 7) within each 128-byte row).
+__device__ __forceinline__ uint32_t tile_off(int key, int c16) {
+  const int half = c16 >> 3, c = c16 & 7;
+  return half * HALF_BYTES + key * 128 + ((c ^ (key & 7)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct AttnArgs {
+  const bf16* q;
+  bf16* out;
+  const int32_t* starts;
+  const uint32_t* tree_mask;
+  float* ws_o;    // [B*Hkv][nsplit][Rpad][D]
+  float2* ws_ml;  // [B*Hkv][nsplit][Rpad]
+  int32_t* status;
+  int B, T, Hq, Hkv, S, G, R, Rpad, nsplit, split_keys, nrb;
+  float scale_log2;
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                          const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full_bar[STAGES];
+
+  // blockIdx.x = split * nrb + row block (128 query rows per row block)
+  const int rb = blockIdx.x % a.nrb, split = blockIdx.x / a.nrb;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int start = a.starts[b];
+  const int kv_len = start + a.T;
+  const int key_begin = split * a.split_keys;
+  const int key_end = min(key_begin + a.split_keys, kv_len);
+  const int ntiles = key_end > key_begin ? (key_end - key_begin + TILE - 1) / TILE : 0;
+  const int64_t slab_row = ((int64_t)b * a.Hkv + kvh) * a.S;  // first cache row of this (b, kvh)
+  const int64_t unit = ((int64_t)b * a.Hkv + kvh) * a.nsplit + split;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full_bar[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int tile) {
+    const int s = tile % STAGES;
+    uint8_t* dst = smem + s * TILE_BYTES;
+    const int row = (int)(slab_row + key_begin + tile * TILE);
+    mbar_arrive_expect_tx(&full_bar[s], TILE_BYTES);
+    tma_load_2d(dst + 0 * HALF_BYTES, &kmap, &full_bar[s], 0, row);
+    tma_load_2d(dst + 1 * HALF_BYTES, &kmap, &full_bar[s], 64, row);
+    tma_load_2d(dst + 2 * HALF_BYTES, &vmap, &full_bar[s], 0, row);
+    tma_load_2d(dst + 3 * HALF_BYTES, &vmap, &full_bar[s], 64, row);
+  };
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    for (int t = 0; t < ntiles && t < STAGES; ++t) issue(t);
+  }
+
+  // ---- this warp's 16 query rows: r = t*G + gh ------------------------------
+  const int r0 = rb * 128 + warp * 16 + g, r1 = r0 + 8;
+  const int t0 = r0 / a.G, t1 = r1 / a.G;
+  const bool v0 = r0 < a.R, v1 = r1 < a.R;
+  uint32_t qa[8][4];
+  {
+    const bf16* q0 = a.q + (((int64_t)b * a.T + (v0 ? t0 : 0)) * a.Hq + kvh * a.G + (v0 ? r0 % a.G : 0)) * D;
+    const bf16* q1 = a.q + (((int64_t)b * a.T + (v1 ? t1 : 0)) * a.Hq + kvh * a.G + (v1 ? r1 % a.G : 0)) * D;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = kk * 16 + 2 * tig;
+      qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+  }
+  const uint32_t mask0 = (a.tree_mask && v0) ? a.tree_mask[b * a.T + t0] : 0u;
+  const uint32_t mask1 = (a.tree_mask && v1) ? a.tree_mask[b * a.T + t1] : 0u;
+  const bool tree = a.tree_mask != nullptr;
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  const uint32_t smem_base = smem_u32(smem);
+  bool aborted = false;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int s = tile % STAGES;
+    // every thread polls; the CTA agrees on the outcome before anyone moves on
+    const int ok = mbar_wait(&full_bar[s], (tile / STAGES) & 1) ? 1 : 0;
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
+      aborted = true;
+      break;
+    }
+    const uint32_t kbase = smem_base + s * TILE_BYTES;
+    const uint32_t vbase = kbase + 2 * HALF_BYTES;
+    const int key0 = key_begin + tile * TILE;
+
+    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2) {
+        const int mi = lane >> 3, ri = lane & 7;
+        const int key = j * 8 + ri;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + tile_off(key, 2 * kk + mi), b0, b1, b2, b3);
+        mma_bf16(sc[j], qa[kk], b0, b1);
+        mma_bf16(sc[j], qa[kk + 1], b2, b3);
+      }
+    }
+    // mask + row max
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int kabs = key0 + j * 8 + 2 * tig + e;
+        const int rel = kabs - start;
+        bool vis0 = v0 && kabs < kv_len, vis1 = v1 && kabs < kv_len;
+        if (rel >= 0) {
+          vis0 = vis0 && (tree ? ((mask0 >> rel) & 1u) : (rel <= t0));
+          vis1 = vis1 && (tree ? ((mask1 >> rel) & 1u) : (rel <= t1));
+        }
+        sc[j][e] = vis0 ? sc[j][e] * a.scale_log2 : -INFINITY;
+        sc[j][2 + e] = vis1 ? sc[j][2 + e] * a.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, sc[j][e]);
+        mx1 = fmaxf(mx1, sc[j][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    // rows with nothing visible so far keep m = -inf and p = 0
+    const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    const float sub0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float sub1 = mn1 == -INFINITY ? 0.f : mn1;
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sc[j][0] = exp2f(sc[j][0] - sub0);
+      sc[j][1] = exp2f(sc[j][1] - sub0);
+      sc[j][2] = exp2f(sc[j][2] - sub1);
+      sc[j][3] = exp2f(sc[j][3] - sub1);
+      ps0 += sc[j][0] + sc[j][1];
+      ps1 += sc[j][2] + sc[j][3];
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    // O += P V: 4 k-steps of 16 keys, 16 n-tiles of 8 dims.
+#pragma unroll
+    for (int kq = 0; kq < 4; ++kq) {
+      uint32_t pa[4];
+      pa[0] = pack2(sc[2 * kq][0], sc[2 * kq][1]);
+      pa[1] = pack2(sc[2 * kq][2], sc[2 * kq][3]);
+      pa[2] = pack2(sc[2 * kq + 1][0], sc[2 * kq + 1][1]);
+      pa[3] = pack2(sc[2 * kq + 1][2], sc[2 * kq + 1][3]);
+#pragma unroll
+      for (int n = 0; n < 16; n += 2) {
+        const int mi = lane >> 3, ri = lane & 7;
+        const int key = kq * 16 + (mi & 1) * 8 + ri;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + tile_off(key, n + (mi >> 1)), b0, b1, b2, b3);
+        mma_bf16(o[n], pa, b0, b1);
+        mma_bf16(o[n + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (threadIdx.x == 0 && tile + STAGES < ntiles) issue(tile + STAGES);
+  }
+  if (aborted) return;
+
+  // quad-reduce the row sums
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  if (a.nsplit == 1) {
+    // single split: normalise in place (same expression as the combine pass)
+    const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+    if (v0) {
+      bf16* dst = a.out + (((int64_t)b * a.T + t0) * a.Hq + kvh * a.G + r0 % a.G) * D;
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][0] * inv0, o[n][1] * inv0);
+    }
+    if (v1) {
+      bf16* dst = a.out + (((int64_t)b * a.T + t1) * a.Hq + kvh * a.G + r1 % a.G) * D;
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][2] * inv1, o[n][3] * inv1);
+    }
+    return;
+  }
+  float* wo = a.ws_o + unit * a.Rpad * D;
+  float2* wml = a.ws_ml + unit * a.Rpad;
+  if (v0) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+      *reinterpret_cast<float2*>(wo + (int64_t)r0 * D + n * 8 + 2 * tig) = make_float2(o[n][0], o[n][1]);
+    if (tig == 0) wml[r0] = make_float2(m0, l0);
+  }
+  if (v1) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+      *reinterpret_cast<float2*>(wo + (int64_t)r1 * D + n * 8 + 2 * tig) = make_float2(o[n][2], o[n][3]);
+    if (tig == 0) wml[r1] = make_float2(m1, l1);
+  }
+}
+
+// Merge the splits of one (b, kvh, row): splits with m = -inf hold nothing.
+__global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
+  const int r = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int d = threadIdx.x;
+  const int t = r / a.G;
+  const int start = a.starts[b];
+  const int used = min(a.nsplit, (start + a.T + a.split_keys - 1) / a.split_keys);
+  const int64_t base = ((int64_t)b * a.Hkv + kvh) * a.nsplit;
+  float mmax = -INFINITY;
+  for (int s = 0; s < used; ++s) mmax = fmaxf(mmax, a.ws_ml[(base + s) * a.Rpad + r].x);
+  float acc = 0.f, lsum = 0.f;
+  if (mmax != -INFINITY) {
+    for (int s = 0; s < used; ++s) {
+      const float2 ml = a.ws_ml[(base + s) * a.Rpad + r];
+      if (ml.x == -INFINITY) continue;
+      const float w = exp2f(ml.x - mmax);
+      lsum += w * ml.y;
+      acc += w * a.ws_o[((base + s) * a.Rpad + r) * D + d];
+    }
+  }
+  const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+  a.out[(((int64_t)b * a.T + t) * a.Hq + kvh * a.G + r % a.G) * D + d] = f2bf(acc * inv);
+}
+
+constexpr int kStages = 2;
+
+size_t attn_smem_bytes() { return (size_t)kStages * TILE_BYTES + 1024; }
+
+}  // namespace
+
+extern "C" size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int Dd, int max_kv, int split_keys) {
+  if (B <= 0 || T <= 0 || Hkv <= 0 || Hq % Hkv || Dd != D || split_keys <= 0) return 0;
+  const int R = T * (Hq / Hkv);
+  const int Rpad = (R + 15) / 16 * 16;
+  const int nsplit = (max_kv + split_keys - 1) / split_keys;
+  if (nsplit <= 1) return 0;
+  return (size_t)B * Hkv * nsplit * Rpad * (D * sizeof(float) + sizeof(float2));
+}
+
+extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                     const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq, int Hkv,
+                                     int Dd, int S, int max_kv, int split_keys, float scale, void* workspace,
+                                     size_t workspace_bytes, int32_t* status, tsds_stream_t stream) {
+  TSDS_RETURN_IF(Dd != D, TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF(B <= 0 || T <= 0 || T > 32 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0 || S <= 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(max_kv <= 0 || max_kv > S || split_keys <= 0 || (split_keys % TILE) != 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!q || !k_cache || !v_cache || !out || !starts || !status, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!tsds_aligned16(q) || !tsds_aligned16(k_cache) || !tsds_aligned16(v_cache) || !tsds_aligned16(out),
+                 TSDS_E_ALIGN);
+  const int G = Hq / Hkv;
+  const int R = T * G;
+  TSDS_RETURN_IF(R > 1024, TSDS_E_UNSUPPORTED);
+  const int Rpad = (R + 15) / 16 * 16;
+  const int nrb = (Rpad + 127) / 128;
+  const int warps = Rpad >= 128 ? 8 : Rpad / 16;
+  const int nsplit = (max_kv + split_keys - 1) / split_keys;
+  const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
+  TSDS_RETURN_IF(need > workspace_bytes || (need > 0 && workspace == nullptr), TSDS_E_WORKSPACE);
+
+  CUtensorMap kmap, vmap;
+  const uint64_t rows = (uint64_t)B * Hkv * S;
+  int st = tsds_make_tmap_2d_bf16(&kmap, k_cache, D, rows, D * 2, 64, TILE, 1);
+  if (st != TSDS_OK) return st;
+  st = tsds_make_tmap_2d_bf16(&vmap, v_cache, D, rows, D * 2, 64, TILE, 1);
+  if (st != TSDS_OK) return st;
+
+  AttnArgs a;
+  a.q = (const bf16*)q;
+  a.out = (bf16*)out;
+  a.starts = starts;
+  a.tree_mask = tree_mask;
+  a.ws_o = (float*)workspace;
+  a.ws_ml = nsplit > 1 ? reinterpret_cast<float2*>((char*)workspace + (size_t)B * Hkv * nsplit * Rpad * D * sizeof(float))
+                       : nullptr;
+  a.status = status;
+  a.B = B;
+  a.T = T;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.S = S;
+  a.G = G;
+  a.R = R;
+  a.Rpad = Rpad;
+  a.nsplit = nsplit;
+  a.split_keys = split_keys;
+  a.nrb = nrb;
+  a.scale_log2 = scale * LOG2E;
+
+  const size_t smem = attn_smem_bytes();
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(verify_attn_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return TSDS_E_LAUNCH;
+    attr_set = true;
+  }
+  dim3 grid(nsplit * nrb, Hkv, B);
+  verify_attn_kernel<kStages><<<grid, warps * 32, smem, stream>>>(kmap, vmap, a);
+  st = tsds_launch_status();
+  if (st != TSDS_OK || nsplit == 1) return st;
+  attn_combine_kernel<<<dim3(R, Hkv, B), 128, 0, stream>>>(a);
+  return tsds_launch_status();
+}

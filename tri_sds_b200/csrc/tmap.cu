@@ -1,0 +1,52 @@
+// Host-side TMA tensor-map encoding and ABI-wide helpers.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+static int load_encode_tiled() {
+  if (g_encode_tiled) return TSDS_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr) {
+    cudaGetLastError();
+    return TSDS_E_DEVICE;
+  }
+  g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return TSDS_OK;
+}
+
+int tsds_make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                           uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                           int swizzle_128b) {
+  int st = load_encode_tiled();
+  if (st != TSDS_OK) return st;
+  if (!tsds_aligned16(base) || (row_stride_bytes % 16) != 0) return TSDS_E_ALIGN;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle_128b ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TSDS_OK : TSDS_E_INVALID;
+}
+
+extern "C" const char* tsds_status_string(int status) {
+  switch (status) {
+    case TSDS_OK: return "ok";
+    case TSDS_E_INVALID: return "invalid argument or shape";
+    case TSDS_E_ALIGN: return "pointer or leading dimension not 16-byte aligned";
+    case TSDS_E_LAUNCH: return "kernel launch failed";
+    case TSDS_E_WORKSPACE: return "workspace too small";
+    case TSDS_E_TIMEOUT: return "device-side bounded wait timed out";
+    case TSDS_E_UNSUPPORTED: return "unsupported configuration";
+    case TSDS_E_DEVICE: return "device / driver query failed";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int tsds_abi_version(void) { return 1; }

@@ -1,0 +1,85 @@
+"""TriSDSWorker: the spec worker the plugin installs (tri_sds/worker.py:19-78).
+
+Same class name, base class, methods and ``SDS_ENABLED`` gate as the
+reference.  With ``SDS_ENABLED=1`` the three methods run this package's
+device path instead of SGLang's:
+
+* ``forward_batch_generation(batch)``: one full speculative cycle (draft ->
+  verify -> accept -> commit) for the batch's sequences; returns the
+  emitted tokens ``[B, K+1]`` (-1 padded) and accept lengths ``[B]``.
+  (The reference raises NotImplementedError here, worker.py:59-61.)
+* ``draft(batch)``: the K draft tokens ``[B, K]`` of the next cycle
+  (the reference returns the GPT-2 draft's logits, worker.py:63-74).
+* ``verify(batch)``: the target's verify pass + acceptance over the drafts
+  of the last ``draft`` call (the reference raises, worker.py:76-78).
+
+The engine is attached with ``attach_engine`` (or built lazily by the
+subclass hook ``_init_engine``); it owns the weights and KV caches.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .sglang_compat import ScheduleBatch, StandaloneWorker
+
+
+class TriSDSWorker(StandaloneWorker):
+    sds_enabled: bool = False
+    engine = None
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.sds_enabled = os.environ.get("SDS_ENABLED", "0") == "1"
+        self._prefilled = False
+
+    # -- engine ----------------------------------------------------------------
+    def attach_engine(self, engine):
+        self.engine = engine
+        self._prefilled = False
+
+    def _init_engine(self):
+        raise RuntimeError("TriSDSWorker needs an engine: call attach_engine(SpecEngine(...))")
+
+    def _ensure(self, batch: ScheduleBatch):
+        if self.engine is None:
+            self._init_engine()
+        if not self._prefilled:
+            ids = torch.as_tensor(batch.input_ids)
+            if ids.dim() == 1:
+                ids = ids.unsqueeze(0)
+            self.engine.prepare(ids)
+            self._prefilled = True
+
+    # -- dispatch (worker.py:42-55) -------------------------------------------
+    def forward_batch_generation(self, batch: ScheduleBatch):
+        if not self.sds_enabled:
+            return super().forward_batch_generation(batch)
+        return self._forward_batch_generation_sds(batch)
+
+    def draft(self, batch: ScheduleBatch):
+        if not self.sds_enabled:
+            return super().draft(batch)
+        return self._draft_sds(batch)
+
+    def verify(self, batch: ScheduleBatch):
+        if not self.sds_enabled:
+            return super().verify(batch)
+        return self._verify_sds(batch)
+
+    # -- SDS implementations ---------------------------------------------------
+    def _forward_batch_generation_sds(self, batch: ScheduleBatch):
+        """One speculative cycle: (tokens [B, K+1] padded -1, accept_len [B])."""
+        self._ensure(batch)
+        tokens, n = self.engine.step()
+        return tokens.clone(), n.clone()
+
+    def _draft_sds(self, batch: ScheduleBatch):
+        self._ensure(batch)
+        return self.engine.run_draft().clone()
+
+    def _verify_sds(self, batch: ScheduleBatch):
+        self._ensure(batch)
+        tokens, n = self.engine.run_verify()
+        return tokens.clone(), n.clone()
