@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark: greedy chain speculative decoding, Qwen3-4B-shape draft -> Qwen3-32B-shape target.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl tsds|reference]
+
+One step = one speculative cycle over B sequences: K=4 draft forwards
+(Qwen3-4B shape, 36 layers), one target verify forward over K+1 tokens per
+sequence (Qwen3-32B shape, 64 layers), greedy acceptance and KV commit.
+Weights are random N(0, 0.02) (no checkpoints offline), prompts are 512
+seeded uniform ids.  The metric is whole-job tokens/s (emitted tokens,
+i.e. sum over sequences of accept_len + 1 per cycle).
+
+N > 1 (torchrun) runs one independent replica per GPU; the time is the max
+over ranks and the value the sum of all ranks' tokens over that time.
+
+``--impl reference`` times the reference's PyTorch algorithm on the host
+CPU cores (the CPU oracle: a restatement of tri_sds/triton_kernels/
+qwen_model.py), on a bounded sample of each cycle scaled to the full cycle.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="tsds", choices=["tsds", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--k", type=int, default=4)
+    ap.add_argument("--prompt", type=int, default=512)
+    # smaller depth for profiler captures only (never for reported numbers)
+    ap.add_argument("--target-layers", type=int, default=None)
+    ap.add_argument("--draft-layers", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+METRIC = "Qwen3-32B spec-decode tok/s at B={B} ({n} GPU); verify-step us"
+DATA = "synthetic: seeded uniform prompt ids, random-init N(0,0.02) weights (no checkpoint offline)"
+
+
+def _workload(a) -> str:
+    return (f"greedy chain spec decode: Qwen3-4B-shape draft (36L) -> Qwen3-32B-shape target (64L), "
+            f"K={a.k}, prompt {a.prompt}, B={a.batch}")
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm (oracle) on a bounded sample
+# ---------------------------------------------------------------------------
+
+class CpuCycle:
+    """One full cycle on the host CPU, estimated from a bounded sample: one
+    target layer verify (T=K+1 over a cache of the prompt), one draft layer
+    step (T=1), and each model's final norm + LM head, timed with the
+    oracle and scaled to 64 target and 36 x K draft layers."""
+
+    def __init__(self, a):
+        import torch
+        from dataclasses import replace
+        from oracle.qwen import QWEN3_32B, QWEN3_4B, QwenOracle, random_qwen_weights
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        B, K, P = a.batch, a.k, a.prompt
+        self.a = a
+        self.models = {}
+        for name, shape in (("target", QWEN3_32B), ("draft", QWEN3_4B)):
+            one = replace(shape, n_layers=1)
+            st = QwenOracle(one, random_qwen_weights(one, seed=1), batch=B, max_seq=P + 2 * K + 4)
+            ids = torch.randint(0, shape.vocab, (B, P), generator=torch.Generator().manual_seed(2))
+            with torch.no_grad():
+                st.layer(0, st.embed_w[ids], torch.zeros(B, dtype=torch.int64), torch.arange(P), None)
+            self.models[name] = (st, ids, shape.n_layers)
+        self.sample = (f"oracle bf16 on {self.threads} threads: 1 Qwen3-32B-shape layer verify (T={K + 1}) x64 "
+                       f"+ LM head; 1 Qwen3-4B-shape layer decode x36 x K={K} + {K} LM heads; B={B}, cache {P}")
+
+    def seconds(self) -> float:
+        import torch
+        B, K, P = self.a.batch, self.a.k, self.a.prompt
+        total = 0.0
+        for name, (st, ids, n_layers) in self.models.items():
+            T = K + 1 if name == "target" else 1
+            xs = st.embed_w[ids[:, :T]]
+            starts = torch.full((B,), P, dtype=torch.int64)
+            with torch.no_grad():
+                t0 = time.perf_counter()
+                st.layer(0, xs, starts, torch.arange(P, P + T), None)
+                t_layer = time.perf_counter() - t0
+                t0 = time.perf_counter()
+                st.logits(xs)
+                t_head = time.perf_counter() - t0
+            if name == "target":
+                total += t_layer * n_layers + t_head
+            else:
+                total += (t_layer * n_layers + t_head) * K
+        return total
+
+
+# ---------------------------------------------------------------------------
+
+def run_reference(a, rank: int, world: int):
+    """--impl reference: the reference's CPU path (oracle port), rank 0 only."""
+    if rank != 0:
+        return
+    cc = CpuCycle(a)
+    threads, sample = cc.threads, cc.sample
+    times = []
+    for i in range(a.warmup + a.steps):
+        t = cc.seconds()
+        if i >= a.warmup:
+            times.append(t)
+    cyc = statistics.mean(times)
+    # tokens per cycle: one per sequence (the bonus) plus accepted drafts; with
+    # independent random-init models the acceptance is ~0 (measured on the device arm)
+    tok_s = a.batch / cyc
+    line = {"impl": "reference", "metric": METRIC.format(B=a.batch, n=1), "value": tok_s, "unit": "tok/s",
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": cyc * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": _workload(a), "global_batch": a.batch, "seq_len": a.prompt,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_tsds(a, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    from dataclasses import replace
+    from tri_sds_b200 import _lib
+    from tri_sds_b200.engine import SpecEngine
+    from tri_sds_b200.model import QwenModel
+    from tri_sds_b200.shapes import QWEN3_32B, QWEN3_4B
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B, K, P = a.batch, a.k, a.prompt
+    tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
+    dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
+    max_seq = P + (a.warmup + a.steps) * (K + 1) * 2 + 4 * (K + 1) + 64
+    max_seq = (max_seq + 63) // 64 * 64
+    target = QwenModel(tshape, B, max_seq, max_rows=B * (K + 1), device=dev, seed=1000 + rank)
+    draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000 + rank)
+    engine = SpecEngine(target, draft, K)
+    prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7 + rank))
+    lc0 = _lib.query("tsds_launch_count")
+    engine.prepare(prompt)
+    launches_per_cycle = None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed cycles (inputs resident in HBM) -------------------------
+    hist = torch.zeros(a.warmup + a.steps, B, dtype=torch.int32, device=dev)
+    for i in range(a.warmup):
+        engine.step()
+        hist[i].copy_(engine.accept_len)
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record()
+        for i in range(a.steps):
+            engine.step()
+            hist[a.warmup + i].copy_(engine.accept_len)
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    acc = hist[a.warmup:].float().cpu()
+    tokens = float((acc + 1).sum())
+    t = torch.tensor([ms, tokens], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_max, tokens_all = float(mx[0]), float(sm[1])
+    else:
+        ms_max, tokens_all = ms, tokens
+    value = tokens_all / (ms_max / 1e3)
+    launches_per_cycle = engine.plan_launches
+
+    # ---- verify step alone (target forward over K+1 tokens) ------------------
+    vplan = target.forward_plan(engine.verify_ids, 1, B, K + 1, target.lengths, 0, engine.target_argmax, 1)
+    vplan.run()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        vplan.run()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    nv = 10
+    for _ in range(nv):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    verify_us = e0.elapsed_time(e1) * 1e3 / nv
+    del g
+
+    # ---- dominant kernel: the target's gate/up + SiLU projection -------------
+    from tri_sds_b200 import ops
+    M = B * (K + 1)
+    xin = torch.randn(M, tshape.hidden, device=dev).to(torch.bfloat16)
+    hout = torch.empty(M, tshape.intermediate, dtype=torch.bfloat16, device=dev)
+    for L in target.layers[:2]:
+        ops.linear_swiglu(xin, L.w_gu, out=hout)
+    torch.cuda.synchronize()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for L in target.layers:
+        ops.linear_swiglu(xin, L.w_gu, out=hout)
+    k1.record()
+    torch.cuda.synchronize()
+    kern_us = k0.elapsed_time(k1) * 1e3 / len(target.layers)
+    kbytes = target.layers[0].w_gu.numel() * 2 + xin.numel() * 2 + hout.numel() * 2
+    peak, peak_kind = _peaks()
+    achieved = kbytes / (kern_us * 1e-6) / 1e9
+
+    # ---- end to end through the worker API (host buffers) --------------------
+    e2e = None
+    if not a.no_e2e:
+        os.environ["SDS_ENABLED"] = "1"
+        worker = TriSDSWorker()
+        worker.attach_engine(engine)
+        worker._prefilled = True  # the engine is prepared; continue from its state
+        cur_host = engine.cur.cpu().reshape(B, 1)
+        for _ in range(a.warmup):
+            toks, n = worker.forward_batch_generation(ScheduleBatch(input_ids=cur_host))
+            cur_host = toks.gather(1, n.long().unsqueeze(1))
+        barrier()
+        t0 = time.perf_counter()
+        e_tokens = 0
+        for _ in range(a.steps):
+            toks, n = worker.forward_batch_generation(ScheduleBatch(input_ids=cur_host))
+            cur_host = toks.gather(1, n.long().unsqueeze(1))
+            e_tokens += int(n.sum()) + B
+        el = time.perf_counter() - t0
+        tt = torch.tensor([el, e_tokens], dtype=torch.float64, device=dev)
+        if world > 1:
+            mx = tt.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            sm = tt.clone()
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            el, e_tokens = float(mx[0]), float(sm[1])
+        e2e = {"value": e_tokens / el, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
+               "d2h_bytes_per_step": 8 * B * (K + 1) + 4 * B}
+
+    # ---- CPU baseline (rank 0, N=1) ------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cc = CpuCycle(a)
+        cyc = statistics.mean(cc.seconds() for _ in range(3))
+        mean_tok = tokens / a.steps
+        cpu = {"value": mean_tok / cyc, "unit": "tok/s", "cores": cc.threads, "kind": "port",
+               "sample": cc.sample + f"; {mean_tok:.2f} tokens per cycle as measured on the device"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC.format(B=B, n=world), "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": _workload(a), "global_batch": B * world, "seq_len": P,
+                       "parallelism": "tp1" if world == 1 else f"tp1 x {world} replicas",
+                       "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
+                       "target_layers": tshape.n_layers, "draft_layers": dshape.n_layers},
+            "verify_step_us": verify_us,
+            "accept_len_mean": float(acc.mean()),
+            "roofline": {"bound": "hbm", "kernel": "tsds_linear_swiglu (target gate/up, M=%d)" % M,
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": kbytes,
+                         "launch_us": kern_us},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": launches_per_cycle * a.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    a = _args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if a.impl == "tsds" else "gloo"
+        if backend == "nccl":
+            import torch
+            torch.cuda.set_device(local_rank)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+    try:
+        if a.impl == "reference":
+            run_reference(a, rank, world)
+        else:
+            run_tsds(a, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

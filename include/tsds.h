@@ -49,6 +49,9 @@ enum {
 const char* tsds_status_string(int status);
 /* ABI version: bumps on any signature change. */
 int tsds_abi_version(void);
+/* Number of kernels this library has enqueued in the process so far (host
+ * counter; a launch recorded into a CUDA graph counts once, at capture). */
+int64_t tsds_launch_count(void);
 
 /* ---------------------------------------------------------------------------
  * Embedding gather: out[m][:] = table[ids[m * ids_stride]][:]; an id outside
@@ -108,7 +111,14 @@ int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_no
  *                                                                 (fused_qwen_decode.py:371-387;
  *                                                                  qwen_model.py:139-142)
  */
+/* Workspace: 0 bytes on the GEMV path; otherwise a status word (int32 at
+ * offset 0: TSDS_E_TIMEOUT if a device wait gave up), tile counters that
+ * must be zero before the first use (every launch leaves them zero) and
+ * fp32 split-K partials.  Zero-fill a fresh workspace once. */
 size_t tsds_linear_workspace_bytes(int M, int n_out, int K);
+/* Largest M served by the CUDA-core GEMV (0..8; above it the tcgen05 GEMM).
+ * Process-wide; read by the *_workspace_bytes functions too. */
+void tsds_set_gemv_max_rows(int rows);
 int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                 void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,
@@ -146,6 +156,8 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
  * Replaces the LM head + argmax of qwen_model.py:192,205 and
  * eagle_head.py:120-121.
  */
+/* Workspace: per-row candidates, plus the tcgen05 workspace when M is above
+ * the GEMV limit (zero-fill a fresh workspace once, as for tsds_linear). */
 size_t tsds_lm_head_workspace_bytes(int M, int vocab);
 int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
                         int argmax_stride, int M, int vocab, int K, void* workspace,

@@ -22,11 +22,13 @@ _Z = ctypes.c_size_t
 SIGNATURES = {
     "tsds_status_string": (ctypes.c_char_p, [_I]),
     "tsds_abi_version": (_I, []),
+    "tsds_launch_count": (ctypes.c_int64, []),
     "tsds_embed": (_I, [_P, _I, _P, _P, _I, _I, _I, _P]),
     "tsds_rms_norm": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _P]),
     "tsds_prep_chain": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
+    "tsds_set_gemv_max_rows": (None, [_I]),
     "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

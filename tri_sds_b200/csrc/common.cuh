@@ -15,8 +15,12 @@ typedef __nv_bfloat16 bf16;
     if (cond) return (code);       \
   } while (0)
 
-// Map the launch's own error (not a sticky earlier one) to a status code.
+void tsds_count_launch();
+
+// Map the launch's own error (not a sticky earlier one) to a status code;
+// every kernel launch in the library is followed by exactly one call.
 static inline int tsds_launch_status() {
+  tsds_count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TSDS_OK : TSDS_E_LAUNCH;
 }

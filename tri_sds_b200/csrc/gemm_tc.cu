@@ -1,0 +1,450 @@
+// Persistent tcgen05 skinny GEMM for the linear layers and the LM head (sm_100a).
+//
+//   D[j][m] = sum_k W[j][k] * X[m][k]      (swap-AB: weight rows j fill the MMA's
+//                                            M = 128, token rows m are its N)
+//
+// * One CTA per SM.  The work (tiles of 128 weight rows x k-tiles of 64) is
+//   split stream-K style: CTA p owns the contiguous iteration range
+//   [W*p/P, W*(p+1)/P) of the flattened (tile, k-tile) space, so every SM
+//   streams the same number of weight bytes whatever the layer shape.
+// * Warp 0 (one lane) issues TMA loads of the weight tile (two 64x64 boxes,
+//   128-byte swizzle) and of the X tile (64 x Npad box; rows past M are
+//   zero-filled by TMA) into a STAGES-deep ring (mbarrier full/empty).
+// * Warp 1 (one lane) issues tcgen05.mma kind::f16 (bf16 in, fp32 out,
+//   M=128, N=Npad, K=16 per instruction) into one of two TMEM accumulators
+//   and commits completion to the ring's empty barriers / the accumulator's
+//   full barrier.
+// * Warps 2-5 drain TMEM with tcgen05.ld (lane quarter = warp % 4) and run
+//   the epilogue: bf16 store, residual add, SwiGLU (gate rows 0-63 and up
+//   rows 64-127 of the same tile), or LM-head argmax candidates.
+// * A tile split across CTAs is finished by the last contributor (atomic
+//   counter): it sums the fp32 partials in CTA order, so the result is
+//   deterministic and - since the split depends only on (n_out, K, P) -
+//   a row's result never depends on M or on the other rows.
+// Every mbarrier wait is bounded; on a timeout the CTA records
+// TSDS_E_TIMEOUT in the status word and unwinds.
+#include "common.cuh"
+#include "linear.cuh"
+
+using namespace tsds;
+
+namespace {
+
+constexpr int BK = 64;                     // k per stage: one 128-byte swizzle row
+constexpr int TILE_J = 128;                // MMA M
+constexpr int A_STAGE = TILE_J * BK * 2;   // 16 KB
+constexpr int MAX_STAGES = 16;
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BUDGET = 220 * 1024;
+
+struct TcParams {
+  int M, Npad, n_out, K, KT, tiles, P;
+  long long W;
+  int epi, up_off, ldo;
+  const bf16* res;
+  bf16* out;
+  float* ws;
+  int* counters;
+  int32_t* status;
+  float* cand_val;
+  int* cand_idx;
+  int ldc;
+  int stages, b_stage_bytes;
+  uint32_t idesc;
+  int tmem_cols;
+};
+
+// ---- tcgen05 / descriptor helpers ------------------------------------------
+// Shared-memory matrix descriptor: K-major operand in 128-byte-swizzled
+// rows, 8-row core groups 1024 bytes apart (SBO), descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// ---- stream-K bookkeeping ---------------------------------------------------
+__device__ __forceinline__ long long it_begin(int p, int P, long long W) { return (W * p) / P; }
+
+// CTA whose range holds iteration x
+__device__ __forceinline__ int owner_of(long long x, int P, long long W) {
+  int q = (int)((x * P) / W);
+  if (q > P - 1) q = P - 1;
+  while (q + 1 < P && it_begin(q + 1, P, W) <= x) ++q;
+  while (q > 0 && it_begin(q, P, W) > x) --q;
+  return q;
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+struct Smem {
+  uint64_t full_bar[MAX_STAGES];
+  uint64_t empty_bar[MAX_STAGES];
+  uint64_t tfull_bar[2];
+  uint64_t tempty_bar[2];
+  uint32_t tmem_base;
+  int abort;
+  int go;
+  int last;
+  float xch[64][17];
+  float red_v[4][16];
+  int red_i[4][16];
+};
+
+// Final epilogue for 16 accumulator columns m0..m0+15 of tile row r.
+__device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t, int r, int m0, const float (&v)[16]) {
+  const int eq = r >> 5, lane = r & 31;
+  if (p.epi == EPI_STORE || p.epi == EPI_RESIDUAL) {
+    const int j = t * TILE_J + r;
+    if (j < p.n_out) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int m = m0 + jj;
+        if (m < p.M) {
+          const int64_t o = (int64_t)m * p.ldo + j;
+          p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[o]) + rbf(v[jj]));
+        }
+      }
+    }
+  } else if (p.epi == EPI_SWIGLU) {
+    if (r >= 64) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) sh.xch[r - 64][jj] = rbf(v[jj]);
+    }
+    epi_bar();
+    const int j = t * 64 + r;
+    if (r < 64 && j < p.n_out) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int m = m0 + jj;
+        if (m < p.M) {
+          const float g = rbf(v[jj]);
+          const float s = rbf(g / (1.0f + expf(-g)));
+          p.out[(int64_t)m * p.ldo + j] = f2bf(s * sh.xch[r][jj]);
+        }
+      }
+    }
+    epi_bar();
+  } else {  // EPI_ARGMAX (LM head): bf16 logits, per-tile candidates
+    const int j = t * TILE_J + r;
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+      const int m = m0 + jj;
+      float lv = j < p.n_out ? rbf(v[jj]) : -INFINITY;
+      if (p.out && j < p.n_out && m < p.M) p.out[(int64_t)m * p.ldo + j] = f2bf(lv);
+      int li = j;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, lv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, li, o);
+        if (better(ov, oi, lv, li)) {
+          lv = ov;
+          li = oi;
+        }
+      }
+      if (lane == 0) {
+        sh.red_v[eq][jj] = lv;
+        sh.red_i[eq][jj] = li;
+      }
+    }
+    epi_bar();
+    if (r < 16 && m0 + r < p.M) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int q = 0; q < 4; ++q)
+        if (better(sh.red_v[q][r], sh.red_i[q][r], bv, bi)) {
+          bv = sh.red_v[q][r];
+          bi = sh.red_i[q][r];
+        }
+      p.cand_val[(int64_t)(m0 + r) * p.ldc + t] = bv;
+      p.cand_idx[(int64_t)(m0 + r) * p.ldc + t] = bi;
+    }
+    epi_bar();
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Smem sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pc = blockIdx.x;
+  const long long b = it_begin(pc, p.P, p.W), e = it_begin(pc + 1, p.P, p.W);
+  const int KT = p.KT;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&sh.full_bar[s], 1);
+      mbar_init(&sh.empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.tfull_bar[i], 1);
+      mbar_init(&sh.tempty_bar[i], 4);
+    }
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                 "r"(2 * p.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  uint8_t* a_smem = smem;
+  uint8_t* b_smem = smem + p.stages * A_STAGE;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && b < e) {
+      prefetch_tmap(&amap);
+      prefetch_tmap(&bmap);
+      int i = 0;
+      for (long long it = b; it < e; ++it, ++i) {
+        const int t = (int)(it / KT), kt = (int)(it % KT);
+        const int s = i % p.stages, r = i / p.stages;
+        if (r > 0 && !mbar_wait(&sh.empty_bar[s], (r - 1) & 1)) {
+          atomicExch(p.status, TSDS_E_TIMEOUT);
+          sh.abort = 1;
+          break;
+        }
+        if (*(volatile int*)&sh.abort) break;
+        mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+        const int row0 = p.epi == EPI_SWIGLU ? t * 64 : t * TILE_J;
+        const int row1 = p.epi == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
+        tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
+        tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
+        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], kt * BK, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && b < e) {
+      int i = 0, seg = 0;
+      bool ok = true;
+      for (int t = (int)(b / KT); ok && t <= (int)((e - 1) / KT); ++t, ++seg) {
+        const long long tb = (long long)t * KT;
+        const int k0 = (int)((b > tb ? b : tb) - tb);
+        const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
+        const int buf = seg & 1, use = seg >> 1;
+        if (use > 0 && !mbar_wait(&sh.tempty_bar[buf], (use - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * p.tmem_cols;
+        for (int kt = k0; kt < k1; ++kt, ++i) {
+          const int s = i % p.stages, r = i / p.stages;
+          if (!mbar_wait(&sh.full_bar[s], r & 1) || *(volatile int*)&sh.abort) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(a_smem + s * A_STAGE);
+          const uint32_t b_base = smem_u32(b_smem + s * p.b_stage_bytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                      (kt > k0 || kk > 0) ? 1u : 0u);
+          umma_commit(&sh.empty_bar[s]);
+        }
+        if (!ok) break;
+        umma_commit(&sh.tfull_bar[buf]);
+      }
+      if (!ok) {
+        atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2-5) ----------------
+    const int eq = warp & 3;
+    const int r = eq * 32 + lane;  // tile row == TMEM lane
+    const int nchunk = p.Npad / 16;
+    int seg = 0;
+    bool alive = b < e;
+    for (int t = (int)(b / KT); alive && t <= (int)((e - 1) / KT); ++t, ++seg) {
+      const long long tb = (long long)t * KT;
+      const int k0 = (int)((b > tb ? b : tb) - tb);
+      const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
+      const int buf = seg & 1, use = seg >> 1;
+      const int ok = mbar_wait(&sh.tfull_bar[buf], use & 1) ? 1 : 0;
+      if (!ok) {
+        atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+      // the four epilogue warps take one decision from one snapshot
+      epi_bar();
+      if (r == 0) sh.go = !*(volatile int*)&sh.abort;
+      epi_bar();
+      if (!sh.go) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const bool full = (k0 == 0 && k1 == KT);
+      const uint32_t taddr = tmem + buf * p.tmem_cols + ((uint32_t)(eq * 32) << 16);
+      const int slot = (t == (int)(b / KT)) ? 0 : 1;
+      float* part = p.ws + ((size_t)(pc * 2 + slot) * p.Npad) * TILE_J;
+      for (int c = 0; c < nchunk; ++c) {
+        float v[16];
+        tmem_ld16(taddr + c * 16, v);
+        if (full) {
+          finish_chunk(p, sh, t, r, c * 16, v);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) part[(size_t)(c * 16 + jj) * TILE_J + r] = v[jj];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty_bar[buf]);
+      if (!full) {
+        // contributors of tile t: CTAs q_lo..q_hi, in order
+        const int q_lo = owner_of(tb, p.P, p.W), q_hi = owner_of(tb + KT - 1, p.P, p.W);
+        __threadfence();
+        epi_bar();
+        if (r == 0) sh.last = (atomicAdd(&p.counters[t], 1) == q_hi - q_lo);
+        epi_bar();
+        if (sh.last) {
+          __threadfence();
+          for (int c = 0; c < nchunk; ++c) {
+            float v[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
+            for (int q = q_lo; q <= q_hi; ++q) {
+              const int qs = (t == (int)(it_begin(q, p.P, p.W) / KT)) ? 0 : 1;
+              const float* src = p.ws + ((size_t)(q * 2 + qs) * p.Npad + c * 16) * TILE_J + r;
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) v[jj] += __ldcg(src + (size_t)jj * TILE_J);
+            }
+            finish_chunk(p, sh, t, r, c * 16, v);
+          }
+          if (r == 0) p.counters[t] = 0;  // ready for the next launch
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+  }
+}
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      g_num_sms = 148;
+    }
+  }
+  return g_num_sms;
+}
+
+int pow2_at_least(int x) {
+  int v = 32;
+  while (v < x) v <<= 1;
+  return v;
+}
+
+}  // namespace
+
+// Workspace layout: [status int32, padding to 64 B][counters: 2048 ints][partials: P x 2 x Npad x 128 fp32].
+// The counters must be zero before the first use; every launch leaves them zero.
+size_t tsds_tc_workspace_bytes(int M) {
+  const int npad = (M + 15) / 16 * 16;
+  return 64 + 2048 * sizeof(int) + (size_t)num_sms() * 2 * npad * TILE_J * sizeof(float);
+}
+
+int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, bf16* out, int ldo,
+                 int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val, int* cand_idx,
+                 int ldc, cudaStream_t stream) {
+  TSDS_RETURN_IF(M <= 0 || M > 256, TSDS_E_INVALID);
+  TSDS_RETURN_IF(workspace == nullptr || workspace_bytes < tsds_tc_workspace_bytes(M), TSDS_E_WORKSPACE);
+  TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
+  int32_t* status = (int32_t*)workspace;
+  TcParams p;
+  p.M = M;
+  p.Npad = (M + 15) / 16 * 16;
+  p.n_out = n_out;
+  p.K = K;
+  p.KT = (K + BK - 1) / BK;
+  p.tiles = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + TILE_J - 1) / TILE_J;
+  TSDS_RETURN_IF(p.tiles > 2048, TSDS_E_UNSUPPORTED);
+  p.W = (long long)p.tiles * p.KT;
+  p.P = (int)(p.W < num_sms() ? p.W : num_sms());
+  p.epi = epi;
+  p.up_off = n_out;
+  p.ldo = ldo;
+  p.res = res;
+  p.out = out;
+  p.counters = (int*)((char*)workspace + 64);
+  p.ws = (float*)((char*)workspace + 64 + 2048 * sizeof(int));
+  p.status = status;
+  p.cand_val = cand_val;
+  p.cand_idx = cand_idx;
+  p.ldc = ldc;
+  p.b_stage_bytes = p.Npad * BK * 2;
+  p.stages = (SMEM_BUDGET - 1024) / (A_STAGE + p.b_stage_bytes);
+  if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) | ((uint32_t)(TILE_J >> 4) << 24);
+  p.tmem_cols = pow2_at_least(p.Npad);
+
+  CUtensorMap amap, bmap;
+  int st = tsds_make_tmap_2d_bf16(&amap, W, K, w_rows, (uint64_t)K * 2, BK, 64, 1);
+  if (st != TSDS_OK) return st;
+  st = tsds_make_tmap_2d_bf16(&bmap, x, K, M, (uint64_t)ldx * 2, BK, p.Npad, 1);
+  if (st != TSDS_OK) return st;
+  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET) !=
+        cudaSuccess)
+      return TSDS_E_LAUNCH;
+    attr = true;
+  }
+  tc_gemm_kernel<<<p.P, NUM_THREADS, smem, stream>>>(amap, bmap, p);
+  return tsds_launch_status();
+}

@@ -10,21 +10,36 @@ int check_linear(const void* x, int ldx, const void* W, const void* out, int ldo
   return TSDS_OK;
 }
 
+int g_gemv_max_rows = 4;
+
 int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, void* out, int ldo, int M, int n_out,
                int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
-  return tsds_gemv_dispatch(epi, (const bf16*)x, ldx, (const bf16*)W, (const bf16*)res, (bf16*)out, ldo, M, n_out, K,
-                            stream);
+  if (M <= g_gemv_max_rows)
+    return tsds_gemv_dispatch(epi, (const bf16*)x, ldx, (const bf16*)W, (const bf16*)res, (bf16*)out, ldo, M, n_out,
+                              K, stream);
+  const int w_rows = epi == EPI_SWIGLU ? 2 * n_out : n_out;
+  for (int m0 = 0; m0 < M; m0 += 256) {  // rows beyond 256 (prefill-sized) in chunks
+    const int mc = M - m0 < 256 ? M - m0 : 256;
+    const bf16* res_c = res ? (const bf16*)res + (int64_t)m0 * ldo : nullptr;
+    int st = tsds_tc_gemm(epi, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, w_rows, res_c,
+                          (bf16*)out + (int64_t)m0 * ldo, ldo, mc, n_out, K, workspace, workspace_bytes, nullptr,
+                          nullptr, 0, stream);
+    if (st != TSDS_OK) return st;
+  }
+  return TSDS_OK;
 }
 
 }  // namespace
 
+int tsds_gemv_rows_limit() { return g_gemv_max_rows; }
+
+extern "C" void tsds_set_gemv_max_rows(int rows) { g_gemv_max_rows = rows < 0 ? 0 : (rows > 8 ? 8 : rows); }
+
 extern "C" size_t tsds_linear_workspace_bytes(int M, int n_out, int K) {
-  (void)M;
   (void)n_out;
   (void)K;
-  return 0;
+  if (M <= g_gemv_max_rows) return 0;
+  return tsds_tc_workspace_bytes(M < 256 ? M : 256);
 }
 
 extern "C" int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,

@@ -6,6 +6,7 @@
 // gemv.cu) and leaves one (value, index) candidate per CTA and token row;
 // pass 2 reduces the candidates per row in CTA order.
 #include "common.cuh"
+#include "linear.cuh"
 
 using namespace tsds;
 
@@ -133,10 +134,21 @@ int lm_blocks(int mt, int vocab) {
 
 }  // namespace
 
+// [candidates: M x ldc values][M x ldc indices][tcgen05 workspace]
+static int lm_ldc(int vocab) {
+  const int a = lm_blocks(8, vocab), b = (vocab + 127) / 128;
+  return a > b ? a : b;
+}
+
+static size_t lm_cand_bytes(int M, int vocab) {
+  return ((size_t)M * lm_ldc(vocab) * (sizeof(float) + sizeof(int)) + 255) / 256 * 256;
+}
+
 extern "C" size_t tsds_lm_head_workspace_bytes(int M, int vocab) {
   if (M <= 0 || vocab <= 0) return 0;
-  // candidates for all M rows at the smallest rows-per-warp (most CTAs)
-  return (size_t)M * lm_blocks(8, vocab) * (sizeof(float) + sizeof(int));
+  size_t b = lm_cand_bytes(M, vocab);
+  if (M > tsds_gemv_rows_limit()) b += tsds_tc_workspace_bytes(M < 256 ? M : 256);
+  return b;
 }
 
 extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
@@ -147,9 +159,26 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
                  TSDS_E_INVALID);
   TSDS_RETURN_IF(!tsds_aligned16(x) || !tsds_aligned16(W) || (ldx % 8), TSDS_E_ALIGN);
   TSDS_RETURN_IF(workspace_bytes < tsds_lm_head_workspace_bytes(M, vocab) || !workspace, TSDS_E_WORKSPACE);
-  const int ldc = lm_blocks(8, vocab);
+  const int ldc = lm_ldc(vocab);
   float* cval = (float*)workspace;
   int* cidx = (int*)((char*)workspace + (size_t)M * ldc * sizeof(float));
+  if (M > tsds_gemv_rows_limit()) {
+    char* tcws = (char*)workspace + lm_cand_bytes(M, vocab);
+    const size_t tcb = workspace_bytes - lm_cand_bytes(M, vocab);
+    const int tiles = (vocab + 127) / 128;
+    for (int m0 = 0; m0 < M; m0 += 256) {
+      const int mc = M - m0 < 256 ? M - m0 : 256;
+      int st = tsds_tc_gemm(EPI_ARGMAX, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, vocab, nullptr,
+                            logits_out ? (bf16*)logits_out + (int64_t)m0 * vocab : nullptr, vocab, mc, vocab, K, tcws,
+                            tcb, cval + (int64_t)m0 * ldc, cidx + (int64_t)m0 * ldc, ldc, stream);
+      if (st != TSDS_OK) return st;
+      lm_head_pass2<<<mc, 256, 0, stream>>>(cval + (int64_t)m0 * ldc, cidx + (int64_t)m0 * ldc, tiles, ldc,
+                                            argmax_out + (int64_t)m0 * argmax_stride, argmax_stride);
+      st = tsds_launch_status();
+      if (st != TSDS_OK) return st;
+    }
+    return TSDS_OK;
+  }
   for (int m0 = 0; m0 < M; m0 += 8) {
     const int mt = M - m0 < 8 ? M - m0 : 8;
     const bf16* xs = (const bf16*)x + (int64_t)m0 * ldx;

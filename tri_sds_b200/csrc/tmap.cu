@@ -50,3 +50,8 @@ extern "C" const char* tsds_status_string(int status) {
 }
 
 extern "C" int tsds_abi_version(void) { return 1; }
+
+#include <atomic>
+static std::atomic<long long> g_launches{0};
+void tsds_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+extern "C" int64_t tsds_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -41,6 +41,7 @@ class SpecEngine:
         self.cur = torch.zeros(B, **i64)
         self.use_graph = use_graph
         self.graph = None
+        self.plan_launches = None
         self.draft_plan = self._draft_plan()
         self.verify_plan = self._verify_plan()
         self.plan = Plan()
@@ -86,7 +87,10 @@ class SpecEngine:
         return first
 
     def _capture(self):
+        from . import _lib
+        c0 = _lib.query("tsds_launch_count")
         self.plan.run()  # eager warm-up (module loading, attributes) before capture
+        self.plan_launches = _lib.query("tsds_launch_count") - c0
         torch.cuda.synchronize()
         # restore nothing: capture only records; callers re-prefill after
         g = torch.cuda.CUDAGraph()
@@ -111,6 +115,17 @@ class SpecEngine:
         else:
             self.plan.run()
         return self.tokens, self.accept_len
+
+    def step_host(self, cur_host: torch.Tensor, tokens_host: torch.Tensor, accept_host: torch.Tensor):
+        """One cycle driven from the host: copy the current tokens [B] in
+        (pinned -> device), run the cycle, copy tokens / accept lengths out
+        (device -> pinned) and wait for them."""
+        self.cur.copy_(cur_host, non_blocking=True)
+        self.step()
+        tokens_host.copy_(self.tokens, non_blocking=True)
+        accept_host.copy_(self.accept_len, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return tokens_host, accept_host
 
     def prepare(self, prompt: torch.Tensor):
         """Prefill, capture the cycle graph (its warm-up run disturbs the

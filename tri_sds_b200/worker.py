@@ -70,8 +70,24 @@ class TriSDSWorker(StandaloneWorker):
 
     # -- SDS implementations ---------------------------------------------------
     def _forward_batch_generation_sds(self, batch: ScheduleBatch):
-        """One speculative cycle: (tokens [B, K+1] padded -1, accept_len [B])."""
+        """One speculative cycle: (tokens [B, K+1] padded -1, accept_len [B]).
+
+        The first call prefills from ``batch.input_ids`` ([B, P] prompt).
+        Later calls may carry the current token of each sequence
+        (``input_ids`` of shape [B, 1], e.g. the previous cycle's bonus
+        token, on the host); the results come back on the host then."""
+        first = not self._prefilled
         self._ensure(batch)
+        ids = batch.input_ids
+        if not first and isinstance(ids, torch.Tensor) and not ids.is_cuda and ids.dim() == 2 and ids.shape[1] == 1:
+            B, K = self.engine.tokens.shape[0], self.engine.k
+            if getattr(self, "_host_bufs", None) is None:
+                self._host_bufs = (torch.empty(B, dtype=torch.int64).pin_memory(),
+                                   torch.empty(B, K + 1, dtype=torch.int64).pin_memory(),
+                                   torch.empty(B, dtype=torch.int32).pin_memory())
+            cur_h, tok_h, acc_h = self._host_bufs
+            cur_h.copy_(ids[:, 0])
+            return self.engine.step_host(cur_h, tok_h, acc_h)
         tokens, n = self.engine.step()
         return tokens.clone(), n.clone()
 
