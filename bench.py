@@ -46,6 +46,9 @@ def _args():
     ap.add_argument("--draft-layers", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
+    ap.add_argument("--gemv-max-rows", type=int, default=None,
+                    help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 4)")
     return ap.parse_args()
 
 
@@ -206,6 +209,10 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     B, K, P = a.batch, a.k, a.prompt
+    if a.gemv_max_rows is not None:
+        _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
+    if a.ctas_per_sm is not None:
+        _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     max_seq = P + (a.warmup + a.steps) * (K + 1) * 2 + 4 * (K + 1) + 64
@@ -231,12 +238,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        torch.cuda.nvtx.range_push("tsds_timed")
         ev0.record()
         for i in range(a.steps):
             engine.step()
             hist[a.warmup + i].copy_(engine.accept_len)
         ev1.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     barrier()
     ms = ev0.elapsed_time(ev1)
     acc = hist[a.warmup:].float().cpu()
@@ -348,6 +357,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "e2e": e2e,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_cycle * a.steps,
+            "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
         }
         print(json.dumps(line), flush=True)
 

@@ -116,9 +116,14 @@ int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_no
  * must be zero before the first use (every launch leaves them zero) and
  * fp32 split-K partials.  Zero-fill a fresh workspace once. */
 size_t tsds_linear_workspace_bytes(int M, int n_out, int K);
-/* Largest M served by the CUDA-core GEMV (0..8; above it the tcgen05 GEMM).
- * Process-wide; read by the *_workspace_bytes functions too. */
+/* Largest M served by the CUDA-core GEMV (0..8; above it the tcgen05 GEMM;
+ * default 0: tcgen05 for every M).  Process-wide; read by the
+ * *_workspace_bytes functions too. */
 void tsds_set_gemv_max_rows(int rows);
+int tsds_get_gemv_max_rows(void);
+/* Resident CTAs per SM of the tcgen05 GEMM (1..4, default 2; lowered
+ * automatically when the accumulators would not fit in TMEM).  Tuning knob. */
+void tsds_set_gemm_ctas_per_sm(int n);
 int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                 void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,

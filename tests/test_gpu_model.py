@@ -57,6 +57,18 @@ def test_verify_forward_matches_oracle():
 def test_spec_engine_lossless_and_matches_oracle():
     """Greedy spec decoding on the device equals greedy autoregressive
     decoding on the device, and the oracle's greedy continuation."""
+    from tri_sds_b200 import ops
+    from tri_sds_b200.engine import AutoregressiveEngine, SpecEngine
+    # verify (M = B*(K+1)) and autoregressive decode (M = B) must run the same
+    # kernel family for a bit-exact comparison: tcgen05 for every M
+    ops.set_gemv_max_rows(0)
+    try:
+        _spec_vs_ar_case()
+    finally:
+        ops.set_gemv_max_rows(0)
+
+
+def _spec_vs_ar_case():
     from tri_sds_b200.engine import AutoregressiveEngine, SpecEngine
     oshape, dshape = _shapes()
     wt = oq.random_qwen_weights(oshape, seed=3, std=0.08)

@@ -29,6 +29,8 @@ SIGNATURES = {
     "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "tsds_set_gemv_max_rows": (None, [_I]),
+    "tsds_get_gemv_max_rows": (_I, []),
+    "tsds_set_gemm_ctas_per_sm": (None, [_I]),
     "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

@@ -115,12 +115,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-// Bounded wait: ~limit polls (each try_wait may itself suspend briefly).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t limit = (1u << 22)) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase: gives up after `limit_ns` of wall time
+// (default 2 s, far above any legitimate wait in these kernels).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, phase)) {
+    if (global_ns() - t0 > limit_ns) return false;
   }
-  return false;
+  return true;
 }
 
 // 2-D TMA tile load into shared memory, completion counted on `bar`.

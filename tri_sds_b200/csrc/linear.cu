@@ -10,7 +10,9 @@ int check_linear(const void* x, int ldx, const void* W, const void* out, int ldo
   return TSDS_OK;
 }
 
-int g_gemv_max_rows = 4;
+// Measured on B200: the TMA-fed tcgen05 GEMM streams weights faster than the
+// CUDA-core GEMV even at M = 1, so the GEMV is opt-in (tsds_set_gemv_max_rows).
+int g_gemv_max_rows = 0;
 
 int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, void* out, int ldo, int M, int n_out,
                int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -32,6 +34,8 @@ int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, 
 }  // namespace
 
 int tsds_gemv_rows_limit() { return g_gemv_max_rows; }
+
+extern "C" int tsds_get_gemv_max_rows(void) { return g_gemv_max_rows; }
 
 extern "C" void tsds_set_gemv_max_rows(int rows) { g_gemv_max_rows = rows < 0 ? 0 : (rows > 8 ? 8 : rows); }
 

@@ -134,21 +134,25 @@ int lm_blocks(int mt, int vocab) {
 
 }  // namespace
 
-// [candidates: M x ldc values][M x ldc indices][tcgen05 workspace]
+// Workspace: [tcgen05 region at offset 0: status word and tile counters at
+// fixed offsets (they persist across calls), then M-dependent partials]
+// [candidates: M x ldc values][M x ldc indices].  Whatever M a call has,
+// nothing but the counters themselves ever writes the counter words.
 static int lm_ldc(int vocab) {
   const int a = lm_blocks(8, vocab), b = (vocab + 127) / 128;
   return a > b ? a : b;
 }
 
-static size_t lm_cand_bytes(int M, int vocab) {
-  return ((size_t)M * lm_ldc(vocab) * (sizeof(float) + sizeof(int)) + 255) / 256 * 256;
+static size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+static size_t lm_cand_offset(int M) {
+  const size_t header = tsds_tc_workspace_bytes(0);  // status + counters, no partials
+  return round256(M > tsds_gemv_rows_limit() ? tsds_tc_workspace_bytes(M < 256 ? M : 256) : header);
 }
 
 extern "C" size_t tsds_lm_head_workspace_bytes(int M, int vocab) {
   if (M <= 0 || vocab <= 0) return 0;
-  size_t b = lm_cand_bytes(M, vocab);
-  if (M > tsds_gemv_rows_limit()) b += tsds_tc_workspace_bytes(M < 256 ? M : 256);
-  return b;
+  return lm_cand_offset(M) + (size_t)M * lm_ldc(vocab) * (sizeof(float) + sizeof(int));
 }
 
 extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
@@ -160,11 +164,11 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
   TSDS_RETURN_IF(!tsds_aligned16(x) || !tsds_aligned16(W) || (ldx % 8), TSDS_E_ALIGN);
   TSDS_RETURN_IF(workspace_bytes < tsds_lm_head_workspace_bytes(M, vocab) || !workspace, TSDS_E_WORKSPACE);
   const int ldc = lm_ldc(vocab);
-  float* cval = (float*)workspace;
-  int* cidx = (int*)((char*)workspace + (size_t)M * ldc * sizeof(float));
+  float* cval = (float*)((char*)workspace + lm_cand_offset(M));
+  int* cidx = (int*)((char*)cval + (size_t)M * ldc * sizeof(float));
   if (M > tsds_gemv_rows_limit()) {
-    char* tcws = (char*)workspace + lm_cand_bytes(M, vocab);
-    const size_t tcb = workspace_bytes - lm_cand_bytes(M, vocab);
+    char* tcws = (char*)workspace;
+    const size_t tcb = lm_cand_offset(M);
     const int tiles = (vocab + 127) / 128;
     for (int m0 = 0; m0 < M; m0 += 256) {
       const int mc = M - m0 < 256 ? M - m0 : 256;

@@ -154,10 +154,13 @@ class QwenModel:
                        split_keys) for t in range(1, T_max + 1))
         self.attn_ws = torch.empty(max(self.attn_ws_bytes, 16), dtype=torch.uint8, device=dev)
         lin = [(s.qkv_dim, s.hidden), (s.hidden, s.q_dim), (s.intermediate, s.hidden), (s.hidden, s.intermediate)]
-        self.lin_ws_bytes = max(_lib.query("tsds_linear_workspace_bytes", M, o, k) for o, k in lin)
-        self.lin_ws = torch.empty(max(self.lin_ws_bytes, 16), dtype=torch.uint8, device=dev)
-        self.lm_ws_bytes = _lib.query("tsds_lm_head_workspace_bytes", M, s.vocab)
-        self.lm_ws = torch.empty(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
+        self.lin_ws_bytes = max(_lib.query("tsds_linear_workspace_bytes", m, o, k) for o, k in lin
+                                for m in range(1, M + 1))
+        # zero-filled once: the tcgen05 tile counters live in these and every
+        # launch leaves them zero again
+        self.lin_ws = torch.zeros(max(self.lin_ws_bytes, 16), dtype=torch.uint8, device=dev)
+        self.lm_ws_bytes = max(_lib.query("tsds_lm_head_workspace_bytes", m, s.vocab) for m in range(1, M + 1))
+        self.lm_ws = torch.zeros(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
 
     # -- launch plans ---------------------------------------------------------
     def layers_plan(self, B: int, T: int, tree_mask: torch.Tensor | None = None) -> Plan:

@@ -48,17 +48,19 @@ def _bf16_cuda(*ts):
 
 
 class _Scratch:
-    """Grow-only per-device workspace and status word for the op-level API."""
+    """Grow-only, zero-initialised workspaces (one per device and op kind:
+    the tcgen05 tile counters of one op must not be overwritten by another's
+    scratch data) and a status word, for the op-level API."""
 
     def __init__(self):
         self.buf = {}
         self.status = {}
 
-    def get(self, nbytes: int, device) -> torch.Tensor:
-        key = torch.device(device).index
+    def get(self, nbytes: int, device, kind: str = "linear") -> torch.Tensor:
+        key = (torch.device(device).index, kind)
         b = self.buf.get(key)
         if b is None or b.numel() < nbytes:
-            b = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            b = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
             self.buf[key] = b
         return b
 
@@ -82,6 +84,12 @@ def _out_in(w_t: torch.Tensor) -> torch.Tensor:
 
 
 # ---------------------------------------------------------------------------
+
+def set_gemv_max_rows(rows: int) -> None:
+    """Largest row count served by the CUDA-core GEMV; above it the tcgen05
+    GEMM runs (process-wide; 0 sends every linear layer to tcgen05)."""
+    _lib.load().tsds_set_gemv_max_rows(int(rows))
+
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None):
     """norm.py:61-72 over the rows of a 2-D tensor."""
@@ -206,7 +214,7 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     scale = D ** -0.5 if scale is None else float(scale)
     out = torch.empty_like(q) if out is None else out
     nb = _lib.query("tsds_attention_workspace_bytes", B, T, Hq, Hkv, D, max_kv, split_keys)
-    ws = _scratch.get(nb, q.device) if nb else None
+    ws = _scratch.get(nb, q.device, "attention") if nb else None
     status = _scratch.status_word(q.device)
     _lib.call("tsds_verify_attention", _p(q), _p(k_cache), _p(v_cache), _p(out), _p(starts), _p(tree_mask),
               B, T, Hq, Hkv, D, S, max_kv, split_keys, scale, _p(ws), nb, _p(status), _stream())
@@ -233,7 +241,7 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, return_logits: bool = False
     out = torch.empty(M, dtype=torch.int64, device=x.device) if out is None else out
     logits = torch.empty(M, V, dtype=torch.bfloat16, device=x.device) if return_logits else None
     nb = _lib.query("tsds_lm_head_workspace_bytes", M, V)
-    ws = _scratch.get(nb, x.device)
+    ws = _scratch.get(nb, x.device, "lm_head")
     _lib.call("tsds_lm_head_argmax", _p(x), x.stride(0), _p(w), _p(logits), _p(out), out.stride(0), M, V, K,
               _p(ws), nb, _stream())
     return (out, logits) if return_logits else out
