@@ -47,6 +47,7 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
                     help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 4)")
     return ap.parse_args()
@@ -213,6 +214,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
     if a.ctas_per_sm is not None:
         _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
+    if a.no_pdl:
+        _lib.load().tsds_set_pdl(0)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     max_seq = P + (a.warmup + a.steps) * (K + 1) * 2 + 4 * (K + 1) + 64

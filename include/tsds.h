@@ -49,6 +49,10 @@ enum {
 const char* tsds_status_string(int status);
 /* ABI version: bumps on any signature change. */
 int tsds_abi_version(void);
+/* Programmatic dependent launch of the library's kernels (default on): a
+ * kernel may start while the previous one in the stream drains; each waits
+ * (griddepcontrol.wait) before touching data earlier kernels produce. */
+void tsds_set_pdl(int on);
 /* Number of kernels this library has enqueued in the process so far (host
  * counter; a launch recorded into a CUDA graph counts once, at capture). */
 int64_t tsds_launch_count(void);

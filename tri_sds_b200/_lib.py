@@ -23,6 +23,7 @@ SIGNATURES = {
     "tsds_status_string": (ctypes.c_char_p, [_I]),
     "tsds_abi_version": (_I, []),
     "tsds_launch_count": (ctypes.c_int64, []),
+    "tsds_set_pdl": (None, [_I]),
     "tsds_embed": (_I, [_P, _I, _P, _P, _I, _I, _I, _P]),
     "tsds_rms_norm": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _P]),
     "tsds_prep_chain": (_I, [_P, _I, _I, _I, _P, _P, _P]),

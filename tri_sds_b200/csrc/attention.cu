@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
   // blockIdx.x = split * nrb + row block (128 query rows per row block)
   const int rb = blockIdx.x % a.nrb, split = blockIdx.x / a.nrb;
   const int kvh = blockIdx.y, b = blockIdx.z;
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int start = a.starts[b];
@@ -293,6 +295,8 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
 __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
   const int r = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int d = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   const int t = r / a.G;
   const int start = a.starts[b];
   const int used = min(a.nsplit, (start + a.T + a.split_keys - 1) / a.split_keys);
@@ -386,9 +390,9 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
     attr_set = true;
   }
   dim3 grid(nsplit * nrb, Hkv, B);
-  verify_attn_kernel<kStages><<<grid, warps * 32, smem, stream>>>(kmap, vmap, a);
+  tsds_launch(verify_attn_kernel<kStages>, grid, dim3(warps * 32), smem, stream, kmap, vmap, a);
   st = tsds_launch_status();
   if (st != TSDS_OK || nsplit == 1) return st;
-  attn_combine_kernel<<<dim3(R, Hkv, B), 128, 0, stream>>>(a);
+  tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);
   return tsds_launch_status();
 }

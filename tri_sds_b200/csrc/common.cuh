@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/tsds.h"
 
 typedef __nv_bfloat16 bf16;
@@ -27,7 +29,33 @@ static inline int tsds_launch_status() {
 
 static inline bool tsds_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Programmatic dependent launch: every kernel of the library is launched so
+// that it may start while the previous kernel in the stream drains; each
+// kernel executes griddepcontrol.wait before touching memory the previous
+// kernels write (and griddepcontrol.launch_dependents once all its CTAs are
+// resident).  tsds_set_pdl(0) turns the attribute off.
+int tsds_pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+static inline void tsds_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = tsds_pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 namespace tsds {
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // bf16 pairs packed in a 32-bit word -> fp32 (exact).
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }

@@ -10,6 +10,8 @@ using namespace tsds;
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const int64_t* __restrict__ ids, int ids_stride, const bf16* __restrict__ table,
                              bf16* __restrict__ out, int N, int vocab) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const int64_t id = ids[(int64_t)m * ids_stride];
   const bool ok = id >= 0 && id < vocab;
@@ -22,7 +24,7 @@ extern "C" int tsds_embed(const int64_t* ids, int ids_stride, const void* table,
                           int vocab, tsds_stream_t stream) {
   TSDS_RETURN_IF(M <= 0 || N <= 0 || (N % 8) != 0 || vocab <= 0 || ids_stride <= 0, TSDS_E_INVALID);
   TSDS_RETURN_IF(!tsds_aligned16(table) || !tsds_aligned16(out), TSDS_E_ALIGN);
-  embed_kernel<<<M, 128, 0, stream>>>(ids, ids_stride, (const bf16*)table, (bf16*)out, N, vocab);
+  tsds_launch(embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, (const bf16*)table, (bf16*)out, N, vocab);
   return tsds_launch_status();
 }
 
@@ -46,6 +48,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                        bf16* __restrict__ out, int n, int ldx, int ldo, float eps) {
   __shared__ float red[8];
+  pdl_wait();
+  pdl_trigger();
   const bf16* xr = x + (int64_t)blockIdx.x * ldx;
   bf16* orow = out + (int64_t)blockIdx.x * ldo;
   float ss = 0.f;
@@ -79,7 +83,8 @@ extern "C" int tsds_rms_norm(const void* x, const void* w, void* out, int rows, 
   TSDS_RETURN_IF(rows <= 0 || n <= 0 || (n % 8) != 0 || ldx < n || ldo < n, TSDS_E_INVALID);
   TSDS_RETURN_IF(!tsds_aligned16(x) || !tsds_aligned16(w) || !tsds_aligned16(out) || (ldx % 8) || (ldo % 8),
                  TSDS_E_ALIGN);
-  rms_norm_kernel<<<rows, 256, 0, stream>>>((const bf16*)x, (const bf16*)w, (bf16*)out, n, ldx, ldo, eps);
+  tsds_launch(rms_norm_kernel, dim3(rows), dim3(256), 0, stream, (const bf16*)x, (const bf16*)w, (bf16*)out, n, ldx,
+              ldo, eps);
   return tsds_launch_status();
 }
 
@@ -88,6 +93,8 @@ extern "C" int tsds_rms_norm(const void* x, const void* w, void* out, int rows, 
 // ---------------------------------------------------------------------------
 __global__ void prep_chain_kernel(const int32_t* __restrict__ base, int offset, int B, int T,
                                   int32_t* __restrict__ starts, int32_t* __restrict__ positions) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= B * T) return;
   const int b = i / T, t = i - b * T;
@@ -100,7 +107,7 @@ extern "C" int tsds_prep_chain(const int32_t* base, int offset, int B, int T, in
                                tsds_stream_t stream) {
   TSDS_RETURN_IF(B <= 0 || T <= 0 || base == nullptr, TSDS_E_INVALID);
   const int n = B * T;
-  prep_chain_kernel<<<(n + 127) / 128, 128, 0, stream>>>(base, offset, B, T, starts, positions);
+  tsds_launch(prep_chain_kernel, dim3((n + 127) / 128), dim3(128), 0, stream, base, offset, B, T, starts, positions);
   return tsds_launch_status();
 }
 
@@ -130,6 +137,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const int32_t* __restrict__ starts, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
     bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, float eps) {
   constexpr int D = 128;
+  pdl_wait();
+  pdl_trigger();
   const int slots = Hq + 2 * Hkv;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= M * slots) return;
@@ -185,7 +194,7 @@ extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const
   TSDS_RETURN_IF(!qkv || !cos || !sin || !positions || !starts || !q_out || !k_cache || !v_cache, TSDS_E_INVALID);
   const int M = B * T;
   const int warps = M * (Hq + 2 * Hkv);
-  qk_norm_rope_kv_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(
+  tsds_launch(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream,
       (const bf16*)qkv, (const bf16*)q_norm_w, (const bf16*)k_norm_w, (const bf16*)cos, (const bf16*)sin, positions,
       starts, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, M, T, Hq, Hkv, S, eps);
   return tsds_launch_status();
@@ -198,6 +207,8 @@ __global__ void accept_greedy_kernel(const int64_t* __restrict__ draft, const in
                                      int32_t* __restrict__ accept_len, int64_t* __restrict__ tokens,
                                      int32_t* __restrict__ target_len, int64_t* __restrict__ last,
                                      int64_t* __restrict__ cur, int B, int K) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int64_t* d = draft + (int64_t)b * K;
@@ -216,14 +227,16 @@ extern "C" int tsds_accept_greedy(const int64_t* draft, const int64_t* target, i
                                   int32_t* target_len, int64_t* last, int64_t* cur, int B, int K,
                                   tsds_stream_t stream) {
   TSDS_RETURN_IF(B <= 0 || K < 0, TSDS_E_INVALID);
-  accept_greedy_kernel<<<(B + 63) / 64, 64, 0, stream>>>(draft, target, accept_len, tokens, target_len, last, cur, B,
-                                                          K);
+  tsds_launch(accept_greedy_kernel, dim3((B + 63) / 64), dim3(64), 0, stream, draft, target, accept_len, tokens,
+              target_len, last, cur, B, K);
   return tsds_launch_status();
 }
 
 __global__ void gather_ids_kernel(const int64_t* __restrict__ cur, const int64_t* __restrict__ last,
                                   const int64_t* __restrict__ draft, int64_t* __restrict__ verify_ids,
                                   int64_t* __restrict__ draft_ids2, int B, int K) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (verify_ids) {
@@ -241,6 +254,7 @@ extern "C" int tsds_gather_ids(const int64_t* cur, const int64_t* last, const in
   TSDS_RETURN_IF(B <= 0 || K < 0 || !cur, TSDS_E_INVALID);
   TSDS_RETURN_IF(verify_ids && !draft && K > 0, TSDS_E_INVALID);
   TSDS_RETURN_IF(draft_ids2 && !last, TSDS_E_INVALID);
-  gather_ids_kernel<<<(B + 63) / 64, 64, 0, stream>>>(cur, last, draft, verify_ids, draft_ids2, B, K);
+  tsds_launch(gather_ids_kernel, dim3((B + 63) / 64), dim3(64), 0, stream, cur, last, draft, verify_ids, draft_ids2, B,
+              K);
   return tsds_launch_status();
 }

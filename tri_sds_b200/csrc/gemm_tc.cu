@@ -229,29 +229,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = sh.tmem_base;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + p.stages * A_STAGE;
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // The weights do not depend on earlier kernels: the first `stages` weight
+    // tiles are requested before the dependency wait, so they stream in
+    // while the previous kernel drains; X (its output) only after the wait.
     if (lane == 0 && b < e) {
       prefetch_tmap(&amap);
       prefetch_tmap(&bmap);
-      int i = 0;
-      for (long long it = b; it < e; ++it, ++i) {
+      const int npre = (int)((e - b) < p.stages ? (e - b) : p.stages);
+      auto load_a = [&](long long it, int s) {
         const int t = (int)(it / KT), kt = (int)(it % KT);
+        const int row0 = p.epi == EPI_SWIGLU ? t * 64 : t * TILE_J;
+        const int row1 = p.epi == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
+        tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
+        tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
+      };
+      auto load_b = [&](long long it, int s) {
+        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], (int)(it % KT) * BK, 0);
+      };
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive_expect_tx(&sh.full_bar[i], A_STAGE + p.b_stage_bytes);
+        load_a(b + i, i);
+      }
+      pdl_wait();
+      for (int i = 0; i < npre; ++i) load_b(b + i, i);
+      int i = npre;
+      for (long long it = b + npre; it < e; ++it, ++i) {
         const int s = i % p.stages, r = i / p.stages;
-        if (r > 0 && !mbar_wait(&sh.empty_bar[s], (r - 1) & 1)) {
+        if (!mbar_wait(&sh.empty_bar[s], (r - 1) & 1)) {
           atomicExch(p.status, TSDS_E_TIMEOUT);
           sh.abort = 1;
           break;
         }
         if (*(volatile int*)&sh.abort) break;
         mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
-        const int row0 = p.epi == EPI_SWIGLU ? t * 64 : t * TILE_J;
-        const int row1 = p.epi == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
-        tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
-        tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
-        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], kt * BK, 0);
+        load_a(it, s);
+        load_b(it, s);
       }
+    } else {
+      pdl_wait();
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -294,6 +313,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2-5) ----------------
+    pdl_wait();  // reads the residual, writes outputs and the shared workspace
     const int eq = warp & 3;
     const int r = eq * 32 + lane;  // tile row == TMEM lane
     const int nchunk = p.Npad / 16;
@@ -464,6 +484,6 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
       return TSDS_E_LAUNCH;
     attr = true;
   }
-  tc_gemm_kernel<<<p.P, NUM_THREADS, smem, stream>>>(amap, bmap, p);
+  tsds_launch(tc_gemm_kernel, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
   return tsds_launch_status();
 }

@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, i
                                                    const bf16* res, bf16* out, int ldo, int n_out, int K) {
   constexpr int R = GemvCfg<MT>::R;
   constexpr int OUT_PER_WARP = EPI == EPI_SWIGLU ? R / 2 : R;
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j0 = (blockIdx.x * 8 + warp) * OUT_PER_WARP;
   if (j0 >= n_out) return;
@@ -117,7 +119,8 @@ int launch_gemv_rows(const bf16* x, int ldx, const bf16* W, const bf16* res, bf1
     constexpr int R = GemvCfg<MTV>::R;                                                               \
     constexpr int OPW = EPI == EPI_SWIGLU ? R / 2 : R;                                               \
     const int warps = (n_out + OPW - 1) / OPW;                                                       \
-    gemv_kernel<MTV, EPI><<<(warps + 7) / 8, 256, 0, stream>>>(xs, ldx, W, rs, os, ldo, n_out, K); \
+    tsds_launch(gemv_kernel<MTV, EPI>, dim3((warps + 7) / 8), dim3(256), 0, stream, xs, ldx, W, rs, os, ldo, n_out, \
+                K);                                                                                   \
     break;                                                                                           \
   }
     switch (mt) {

@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(256) lm_head_pass1(const bf16* __restrict__ x,
   constexpr int R = LmCfg<MT>::R;
   __shared__ float s_val[8][MT];
   __shared__ int s_idx[8][MT];
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int v0 = (blockIdx.x * 8 + warp) * R;
   float2 acc[R][MT];
@@ -102,6 +104,8 @@ __global__ void __launch_bounds__(256) lm_head_pass2(const float* __restrict__ c
                                                      int64_t* __restrict__ out, int out_stride) {
   __shared__ float s_val[256];
   __shared__ int s_idx[256];
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -176,8 +180,9 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
                             logits_out ? (bf16*)logits_out + (int64_t)m0 * vocab : nullptr, vocab, mc, vocab, K, tcws,
                             tcb, cval + (int64_t)m0 * ldc, cidx + (int64_t)m0 * ldc, ldc, stream);
       if (st != TSDS_OK) return st;
-      lm_head_pass2<<<mc, 256, 0, stream>>>(cval + (int64_t)m0 * ldc, cidx + (int64_t)m0 * ldc, tiles, ldc,
-                                            argmax_out + (int64_t)m0 * argmax_stride, argmax_stride);
+      tsds_launch(lm_head_pass2, dim3(mc), dim3(256), 0, stream, (const float*)(cval + (int64_t)m0 * ldc),
+                  (const int*)(cidx + (int64_t)m0 * ldc), tiles, ldc, argmax_out + (int64_t)m0 * argmax_stride,
+                  argmax_stride);
       st = tsds_launch_status();
       if (st != TSDS_OK) return st;
     }
@@ -192,7 +197,8 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
     int* ci = cidx + (int64_t)m0 * ldc;
 #define TSDS_LM_CASE(MTV)                                                                                    \
   case MTV:                                                                                                  \
-    lm_head_pass1<MTV><<<nb, 256, 0, stream>>>(xs, ldx, (const bf16*)W, ls, vocab, K, cv, ci, ldc); \
+    tsds_launch(lm_head_pass1<MTV>, dim3(nb), dim3(256), 0, stream, xs, ldx, (const bf16*)W, ls, vocab, K, cv, ci, \
+                ldc);                                                                                   \
     break;
     switch (mt) {
       TSDS_LM_CASE(1)
@@ -207,7 +213,8 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
 #undef TSDS_LM_CASE
     int st = tsds_launch_status();
     if (st != TSDS_OK) return st;
-    lm_head_pass2<<<mt, 256, 0, stream>>>(cv, ci, nb, ldc, argmax_out + (int64_t)m0 * argmax_stride, argmax_stride);
+    tsds_launch(lm_head_pass2, dim3(mt), dim3(256), 0, stream, (const float*)cv, (const int*)ci, nb, ldc,
+                argmax_out + (int64_t)m0 * argmax_stride, argmax_stride);
     st = tsds_launch_status();
     if (st != TSDS_OK) return st;
   }

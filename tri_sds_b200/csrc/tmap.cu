@@ -55,3 +55,7 @@ extern "C" int tsds_abi_version(void) { return 1; }
 static std::atomic<long long> g_launches{0};
 void tsds_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 extern "C" int64_t tsds_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+static int g_pdl = 1;
+int tsds_pdl_enabled() { return g_pdl; }
+extern "C" void tsds_set_pdl(int on) { g_pdl = on ? 1 : 0; }
