@@ -42,7 +42,8 @@ enum {
   TSDS_E_WORKSPACE = 4,   /* workspace smaller than *_workspace_bytes */
   TSDS_E_TIMEOUT = 5,     /* a device-side bounded wait gave up (status word) */
   TSDS_E_UNSUPPORTED = 6, /* no kernel instantiated for this configuration */
-  TSDS_E_DEVICE = 7       /* device query failed / not an sm_100 device */
+  TSDS_E_DEVICE = 7,      /* device query failed / not an sm_100 device */
+  TSDS_E_SCRATCH_LIMIT = 8 /* request larger than a built-in scratch area */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -156,6 +157,33 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
                           int Hkv, int D, int S, int max_kv, int split_keys, float scale,
                           void* workspace, size_t workspace_bytes, int32_t* status,
                           tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * tsds_verify_attention for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some callers may not cudaMalloc at all:
+ * a plugin hosted by a serving framework that reserved the GPU's memory for
+ * itself (SGLang sizes its KV pool to a fixed share of the device), or code
+ * that must not allocate while a stream is being captured.  This variant
+ * takes no workspace: its split-KV partials live in a built-in device array
+ * of tsds_verify_attention_noalloc_limit() bytes (8 MiB, plus a 256-byte
+ * status header), which every GPU that loads the library keeps until exit.
+ * The caller still passes inputs and outputs; arguments as for
+ * tsds_verify_attention.
+ *  - The first call on a device looks the array's device address up (that
+ *    device must be current); make it before any stream capture.
+ *  - All calls share the array and it keeps the last call's contents; the
+ *    status word is cleared at every call.  Calls that overlap on the GPU
+ *    race: order them on one stream.
+ *  - Requests whose partials exceed the limit return TSDS_E_SCRATCH_LIMIT.
+ * tsds_verify_attention_noalloc_status copies the status word of the last
+ * call to the host (synchronous).
+ */
+size_t tsds_verify_attention_noalloc_limit(void);
+int tsds_verify_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                  const int32_t* starts, const uint32_t* tree_mask, int B, int T,
+                                  int Hq, int Hkv, int D, int S, int max_kv, int split_keys,
+                                  float scale, tsds_stream_t stream);
+int tsds_verify_attention_noalloc_status(int32_t* host_status);
 
 /* ---------------------------------------------------------------------------
  * LM head + greedy pick: logits[m][v] = bf16(sum_k x[m][k] * W[v][k]);

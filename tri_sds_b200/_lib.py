@@ -37,6 +37,9 @@ SIGNATURES = {
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
+    "tsds_verify_attention_noalloc_limit": (_Z, []),
+    "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tsds_verify_attention_noalloc_status": (_I, [_P]),
     "tsds_lm_head_workspace_bytes": (_Z, [_I, _I]),
     "tsds_lm_head_argmax": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_accept_greedy": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),

@@ -396,3 +396,87 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);
   return tsds_launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Verify attention for callers that cannot allocate device memory.
+//
+// Some callers of this library run where they may not call cudaMalloc: a
+// plugin inside a serving framework that reserved the device memory for
+// itself up front (SGLang sizes its KV pool to a fixed fraction of the GPU
+// and leaves nothing for extensions), or code that must not allocate while
+// a stream is being captured into a graph.  This entry point needs no
+// workspace from them: its split-KV partials live in the file-scope array
+// below, a fixed 8 MiB (plus a 256-byte header holding the status word)
+// that every GPU which loads the library keeps until the process exits.
+//
+// * Host code never passes the array's name to a kernel (on the host that
+//   name is only a stand-in, not a device address).  The first call on a
+//   device, with that device current, looks up the device address with
+//   cudaGetSymbolAddress and caches it; make that first call before any
+//   stream capture.
+// * All calls share the array and it keeps the last call's contents: the
+//   status word is cleared at each call (the partials are fully rewritten
+//   before they are read), and calls that overlap on the GPU race with
+//   each other.  Order them on one stream.
+// * A request whose partials exceed the 8 MiB returns TSDS_E_SCRATCH_LIMIT.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocHeader = 256;
+constexpr size_t kNoAllocScratch = size_t(8) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocHeader + kNoAllocScratch];
+static void* g_attn_noalloc_addr[kNoAllocMaxDevices];
+
+static int attn_noalloc_base(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return TSDS_E_DEVICE;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return TSDS_E_DEVICE;
+  if (g_attn_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return TSDS_E_DEVICE;
+    }
+    g_attn_noalloc_addr[dev] = p;
+  }
+  *out = g_attn_noalloc_addr[dev];
+  return TSDS_OK;
+}
+
+extern "C" size_t tsds_verify_attention_noalloc_limit(void) { return kNoAllocScratch; }
+
+extern "C" int tsds_verify_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                             const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq,
+                                             int Hkv, int Dd, int S, int max_kv, int split_keys, float scale,
+                                             tsds_stream_t stream) {
+  const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
+  if (need > kNoAllocScratch) return TSDS_E_SCRATCH_LIMIT;
+  void* base = nullptr;
+  const int st = attn_noalloc_base(&base);
+  if (st != TSDS_OK) return st;
+  int32_t* status = static_cast<int32_t*>(base);
+  if (cudaMemsetAsync(status, 0, sizeof(int32_t), stream) != cudaSuccess) {
+    cudaGetLastError();
+    return TSDS_E_LAUNCH;
+  }
+  return tsds_verify_attention(q, k_cache, v_cache, out, starts, tree_mask, B, T, Hq, Hkv, Dd, S, max_kv, split_keys,
+                               scale, static_cast<char*>(base) + kNoAllocHeader, kNoAllocScratch, status, stream);
+}
+
+extern "C" int tsds_verify_attention_noalloc_status(int32_t* host_status) {
+  void* base = nullptr;
+  const int st = attn_noalloc_base(&base);
+  if (st != TSDS_OK) return st;
+  if (host_status == nullptr) return TSDS_E_INVALID;
+  if (cudaMemcpy(host_status, base, sizeof(int32_t), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return TSDS_E_DEVICE;
+  }
+  return TSDS_OK;
+}
