@@ -90,8 +90,8 @@ int tsds_prep_chain(const int32_t* base, int offset, int B, int T, int32_t* star
  *   q, k <- rotate-half RoPE at positions[m], bf16 rounding as the reference
  *   q_out[m][h*D..]                       = q
  *   k_cache[b][kvh][starts[b]+t][..]      = k ;  v_cache likewise = v
- *   (rows with starts[b]+t or positions[m] outside [0, S) are skipped;
- *    S is also the length of the RoPE tables)
+ *   (rows with starts[b]+t outside [0, S) or positions[m] outside
+ *    [0, rope_len) - the RoPE tables' length - are skipped)
  * Replaces the QK-norm (absent in the reference), apply_rope and the cache
  * stores of qwen_model.py:109-119 / 154-164, and the RoPE + KV-write half
  * of _rmsnorm_qkv_rope_kernel (fused_qwen_decode.py:212-250).
@@ -99,7 +99,7 @@ int tsds_prep_chain(const int32_t* base, int offset, int B, int T, int32_t* star
 int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
                          const void* cos, const void* sin, const int32_t* positions,
                          const int32_t* starts, void* q_out, void* k_cache, void* v_cache,
-                         int B, int T, int Hq, int Hkv, int D, int S, float eps,
+                         int B, int T, int Hq, int Hkv, int D, int S, int rope_len, float eps,
                          tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
@@ -136,26 +136,34 @@ int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res,
                          tsds_stream_t stream);
 int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out,
                        int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+/* out = bf16(bf16(acc) + bias[j]): the EAGLE head's fc (eagle_head.py:80). */
+int tsds_linear_bias(const void* x, int ldx, const void* W, const void* bias, void* out, int ldo,
+                     int M, int n_out, int K, void* workspace, size_t workspace_bytes,
+                     tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Verify / decode attention of T new tokens per sequence over the KV cache.
  * q: [B*T][Hq][D] (RoPE applied); k/v cache [B][Hkv][S][D] holding the new
  * tokens at rows starts[b]..starts[b]+T-1; out: [B*T][Hq][D] bf16.
- * Query t of sequence b sees every row below starts[b] and, among the new
- * rows, row starts[b]+j when bit j of tree_mask[b*T+t] is set; tree_mask
- * NULL means causal (j <= t).  fp32 online softmax, scale = softmax scale.
+ * Query t of sequence b sees the rows below starts[b]+T subject to a mask:
+ *  - tree_mask NULL: causal - every row below starts[b], then new rows
+ *    starts[b]+j for j <= t;
+ *  - tree_mask given: bit i of tree_mask[b*T+t] admits row base+i, where
+ *    base = starts[b] (mask_origin < 0, T <= 32) or base = mask_origin;
+ *    rows below base are visible to every query, rows base+32.. to none.
+ * fp32 online softmax, scale = softmax scale.
  * Keys are split into fixed chunks of split_keys rows (a multiple of 64);
  * the split boundaries depend only on the key index, so a query's result
  * does not depend on T or B.  max_kv bounds starts[b]+T (sizes the grid).
  * Replaces attention_gqa / _decode_attn_gqa_kernel (attention.py:236-318)
- * and the verify SDPA of qwen_model.py:121-131.  D = 128, T <= 32, T*Hq/Hkv <= 1024.
+ * and the verify SDPA of qwen_model.py:121-131.  D = 128, T*Hq/Hkv <= 1024.
  */
 size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int max_kv,
                                       int split_keys);
 int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
-                          const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq,
-                          int Hkv, int D, int S, int max_kv, int split_keys, float scale,
-                          void* workspace, size_t workspace_bytes, int32_t* status,
+                          const int32_t* starts, const uint32_t* tree_mask, int mask_origin, int B,
+                          int T, int Hq, int Hkv, int D, int S, int max_kv, int split_keys,
+                          float scale, void* workspace, size_t workspace_bytes, int32_t* status,
                           tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
@@ -180,9 +188,9 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
  */
 size_t tsds_verify_attention_noalloc_limit(void);
 int tsds_verify_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
-                                  const int32_t* starts, const uint32_t* tree_mask, int B, int T,
-                                  int Hq, int Hkv, int D, int S, int max_kv, int split_keys,
-                                  float scale, tsds_stream_t stream);
+                                  const int32_t* starts, const uint32_t* tree_mask, int mask_origin,
+                                  int B, int T, int Hq, int Hkv, int D, int S, int max_kv,
+                                  int split_keys, float scale, tsds_stream_t stream);
 int tsds_verify_attention_noalloc_status(int32_t* host_status);
 
 /* ---------------------------------------------------------------------------
@@ -218,6 +226,60 @@ int tsds_accept_greedy(const int64_t* draft, const int64_t* target, int32_t* acc
  * draft's first-step input ids2[b] = last[b], cur[b]. */
 int tsds_gather_ids(const int64_t* cur, const int64_t* last, const int64_t* draft, int64_t* verify_ids,
                     int64_t* draft_ids2, int B, int K, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Tree speculative decoding (EAGLE draft tree, verified in one target pass).
+ * No counterpart in the reference: its chain draft (eagle_head.py:100-129)
+ * stops at argmax tokens and tree drafting / acceptance / KV rollback live
+ * in SGLang (worker.py:76-78 raises).  Semantics: oracle/eagle.py.
+ *
+ * tsds_logits_topk: per logits row (bf16, row stride ld): the k largest
+ *   values (value desc, index asc) and log-sum-exp, fp32.  k in {1,2,4,8}.
+ * tsds_tree_state_bytes: bytes of the per-sequence tree state (opaque).
+ * tsds_tree_init: root = current token cur[b]; writes the root head pass's
+ *   inputs (token, feature row -1 = root feature, position, head-cache mask,
+ *   first head-cache row).
+ * tsds_tree_step: after a head pass over T frontier nodes per sequence
+ *   (their top-k at global rows row_base + b*T + t): add k children per
+ *   node (score = parent + logit - lse), choose the next_T best new nodes
+ *   as the next frontier (0: last pass) and write that pass's inputs.
+ * tsds_tree_finalize: keep the n_nodes best nodes (score desc, depth asc,
+ *   creation asc) and the root; write the verify ids / positions (L + depth)
+ *   / ancestor masks / head rows / children lists, and starts = lengths.
+ * tsds_accept_tree: walk the verified tree: U given -> rejection sampling
+ *   at temperature 1 (accept child x if U*q(x) < p(x); else p <- norm(max(p -
+ *   q, 0)), q <- q without x; bonus by inverse CDF); U NULL -> greedy
+ *   (child == target argmax).  Writes path node indices, accept lengths,
+ *   emitted tokens (accepted + bonus, -1 padded) and cur <- bonus.
+ *   scratch: B * 2 * V floats.
+ * tsds_tree_commit: move the accepted nodes' K/V rows L + path[j] -> L+1+j
+ *   in every layer, copy the last accepted node's hidden state to
+ *   root_feat, then lengths += accept_len + 1.
+ * tsds_eagle_inputs: the head pass input [feature | embedding(token)].
+ */
+int tsds_logits_topk(const void* logits, int ld, int M, int V, int k, float* vals, int32_t* idx,
+                     float* lse, tsds_stream_t stream);
+size_t tsds_tree_state_bytes(int B);
+int tsds_tree_init(void* states, const int64_t* cur, const int32_t* lengths, int64_t* pass_tok,
+                   int32_t* pass_featrow, int32_t* pass_pos, uint32_t* pass_mask, int32_t* pass_starts,
+                   int B, tsds_stream_t stream);
+int tsds_tree_step(void* states, const float* vals, const int32_t* idx, const float* lse, int row_base,
+                   int T, int k, int next_T, const int32_t* lengths, int64_t* pass_tok,
+                   int32_t* pass_featrow, int32_t* pass_pos, uint32_t* pass_mask, int32_t* pass_starts,
+                   int B, tsds_stream_t stream);
+int tsds_tree_finalize(const void* states, int n_nodes, int k, const int32_t* lengths, int64_t* ids,
+                       int32_t* positions, uint32_t* masks, int32_t* hrow, int32_t* children,
+                       int32_t* starts, int B, tsds_stream_t stream);
+int tsds_accept_tree(const void* target_logits, const int64_t* target_argmax, const void* head_logits,
+                     const int64_t* ids, const int32_t* hrow, const int32_t* children, const float* U,
+                     float* scratch, int32_t* path, int32_t* accept_len, int64_t* tokens, int64_t* cur,
+                     int B, int n_nodes, int V, int k, int depth, tsds_stream_t stream);
+int tsds_tree_commit(void* k_cache, void* v_cache, int layers, int B, int Hkv, int S, int D,
+                     int32_t* lengths, const int32_t* path, const int32_t* accept_len, int depth,
+                     const void* hidden, int n_nodes, int N, void* root_feat, tsds_stream_t stream);
+int tsds_eagle_inputs(const void* root_feat, const void* head_feat, const int32_t* featrow,
+                      const int64_t* tok, const void* embed, void* out, int B, int T, int N, int vocab,
+                      tsds_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -204,54 +204,51 @@ class Tree:
     mask: list          # [n] ancestor-or-self bitmask over tree indices
     head_row: list      # [n] head row whose q gives this node's children (-1: not expanded)
     children: list      # [n] list of child indices in draft-rank order
+    candidates: dict | None = None   # token path from the root -> cumulative score, every candidate
+    cutoff: float | None = None      # score of the last kept candidate
 
 
-def build_tree(head: EagleHeadQwen, embed_w, norm_w, lm_head_w, root_feat, root_tok, L, depth=5, topk=4,
-               n_nodes=25):
-    """Tree drafting for B sequences -> (list of Tree, list of head logits [rows, V] fp32)."""
-    B = root_feat.shape[0]
-    head.reset()
-    trees, all_logits = [], []
-    for b in range(B):
-        # candidates: token, parent candidate, depth, cumulative score, rank among
-        # its siblings, input feature, head row once processed
-        cand = [dict(tok=int(root_tok[b]), parent=-1, depth=0, score=0.0, rank=0, feat=root_feat[b], row=-1)]
-        row_mask = []      # attention mask of each processed head row
-        logits_rows = []
-        frontier = [0]
-        for d in range(depth):
-            rows, masks = [], []
-            for ci in frontier:
-                r = len(row_mask) + len(rows)
-                m = 1 << r
-                par = cand[ci]["parent"]
-                if par >= 0:
-                    m |= row_mask[cand[par]["row"]]
-                rows.append(r)
-                masks.append(m)
-            feats = torch.stack([cand[ci]["feat"] for ci in frontier]).unsqueeze(0)
-            toks = torch.tensor([cand[ci]["tok"] for ci in frontier])
-            pos = torch.tensor([[int(L[b]) + cand[ci]["depth"] for ci in frontier]])
-            f = _HeadView(head, b).forward(feats, embed_w[toks].unsqueeze(0), torch.tensor([rows]), pos,
-                                           torch.tensor([masks]))[0]
-            logits = (rms_norm(f, norm_w) @ lm_head_w.T).float()     # [T, V]
-            new = []
-            for t, ci in enumerate(frontier):
-                cand[ci]["row"] = rows[t]
-                row_mask.append(masks[t])
-                logits_rows.append(logits[t])
-                lse = torch.logsumexp(logits[t], 0)
-                for r, tok in enumerate(topk_desc(logits[t], topk).tolist()):
-                    new.append(dict(tok=tok, parent=ci, depth=cand[ci]["depth"] + 1,
-                                    score=cand[ci]["score"] + float(logits[t][tok] - lse), rank=r, feat=f[t],
-                                    row=-1))
-            base = len(cand)
-            cand.extend(new)
-            if d + 1 < depth:
-                order = sorted(range(len(new)), key=lambda i: (-new[i]["score"], i))[:topk]
-                frontier = [base + i for i in sorted(order)]
-        # keep the n_nodes best candidates (the root is always kept)
-        ids = sorted(range(1, len(cand)), key=lambda i: (-cand[i]["score"], cand[i]["depth"], i))[:n_nodes]
+class TreeBuilder:
+    """The tree-selection rules, fed one head pass at a time.
+
+    ``frontier()`` lists the candidates the next pass must run (creation
+    order); ``add_pass(logits)`` takes that pass's logits rows [T, V] in the
+    same order; ``finish()`` keeps the ``n_nodes`` best and returns the Tree.
+    Driving it with the device's own head logits checks the device's
+    selection logic exactly, independent of the head's numerics."""
+
+    def __init__(self, root_tok: int, depth: int = 5, topk: int = 4, n_nodes: int = 25):
+        self.depth, self.topk, self.n_nodes = depth, topk, n_nodes
+        self.cand = [dict(tok=int(root_tok), parent=-1, depth=0, score=0.0, rank=0, row=-1)]
+        self._frontier = [0]
+        self.passes = 0
+        self.rows = 0
+
+    def frontier(self) -> list:
+        return list(self._frontier)
+
+    def add_pass(self, logits: torch.Tensor):
+        logits = logits.float()
+        new = []
+        for t, ci in enumerate(self._frontier):
+            self.cand[ci]["row"] = self.rows + t
+            lse = torch.logsumexp(logits[t], 0)
+            for r, tok in enumerate(topk_desc(logits[t], self.topk).tolist()):
+                new.append(dict(tok=tok, parent=ci, depth=self.cand[ci]["depth"] + 1,
+                                score=self.cand[ci]["score"] + float(logits[t][tok] - lse), rank=r, row=-1))
+        self.rows += len(self._frontier)
+        base = len(self.cand)
+        self.cand.extend(new)
+        self.passes += 1
+        if self.passes < self.depth:
+            order = sorted(range(len(new)), key=lambda i: (-new[i]["score"], i))[:self.topk]
+            self._frontier = [base + i for i in sorted(order)]
+        else:
+            self._frontier = []
+
+    def finish(self) -> "Tree":
+        cand = self.cand
+        ids = sorted(range(1, len(cand)), key=lambda i: (-cand[i]["score"], cand[i]["depth"], i))[:self.n_nodes]
         keep = [0] + sorted(ids)
         pos_of = {ci: j for j, ci in enumerate(keep)}
         tokens = [cand[ci]["tok"] for ci in keep]
@@ -270,7 +267,54 @@ def build_tree(head: EagleHeadQwen, embed_w, norm_w, lm_head_w, root_feat, root_
             children[parent[j]].append(j)
         for j in range(len(keep)):
             children[j].sort(key=lambda c: cand[keep[c]]["rank"])
-        trees.append(Tree(tokens, parent, dep, mask, head_row, children))
+
+        def path_of(ci):
+            p = []
+            while ci > 0:
+                p.append(cand[ci]["tok"])
+                ci = cand[ci]["parent"]
+            return tuple(reversed(p))
+        cands = {path_of(ci): cand[ci]["score"] for ci in range(1, len(cand))}
+        cutoff = cand[ids[-1]]["score"] if ids else 0.0
+        return Tree(tokens, parent, dep, mask, head_row, children, cands, cutoff)
+
+
+def build_tree(head: EagleHeadQwen, embed_w, norm_w, lm_head_w, root_feat, root_tok, L, depth=5, topk=4,
+               n_nodes=25):
+    """Tree drafting for B sequences -> (list of Tree, list of head logits [rows, V] fp32)."""
+    B = root_feat.shape[0]
+    head.reset()
+    trees, all_logits = [], []
+    for b in range(B):
+        tb = TreeBuilder(int(root_tok[b]), depth, topk, n_nodes)
+        feat = {0: root_feat[b]}     # input feature of each candidate
+        row_of, row_mask, logits_rows = {}, [], []
+        while tb.frontier():
+            fr = tb.frontier()
+            rows, masks = [], []
+            for ci in fr:
+                r = len(row_mask) + len(rows)
+                m = 1 << r
+                par = tb.cand[ci]["parent"]
+                if par >= 0:
+                    m |= row_mask[row_of[par]]
+                rows.append(r)
+                masks.append(m)
+            feats = torch.stack([feat[ci] for ci in fr]).unsqueeze(0)
+            toks = torch.tensor([tb.cand[ci]["tok"] for ci in fr])
+            pos = torch.tensor([[int(L[b]) + tb.cand[ci]["depth"] for ci in fr]])
+            f = _HeadView(head, b).forward(feats, embed_w[toks].unsqueeze(0), torch.tensor([rows]), pos,
+                                           torch.tensor([masks]))[0]
+            logits = (rms_norm(f, norm_w) @ lm_head_w.T).float()
+            for t, ci in enumerate(fr):
+                row_of[ci] = rows[t]
+                row_mask.append(masks[t])
+                logits_rows.append(logits[t])
+            base = len(tb.cand)
+            tb.add_pass(logits)
+            for ci in range(base, len(tb.cand)):
+                feat[ci] = f[fr.index(tb.cand[ci]["parent"])]
+        trees.append(tb.finish())
         all_logits.append(torch.stack(logits_rows))
     return trees, all_logits
 

@@ -37,6 +37,6 @@ def test_argument_validation_without_gpu():
     assert lib.tsds_rms_norm(None, None, None, 0, 128, 128, 128, 1e-6, None) == 1          # INVALID
     assert lib.tsds_linear(None, 8, None, None, 8, 1, 8, 8, None, 0, None) == 1
     assert lib.tsds_qk_norm_rope_kv(None, None, None, None, None, None, None, None, None, None,
-                                    1, 1, 8, 2, 64, 16, 1e-6, None) == 6                     # UNSUPPORTED D
-    assert lib.tsds_verify_attention(None, None, None, None, None, None, 1, 40, 8, 2, 128, 64, 64, 64,
-                                     0.1, None, 0, None, None) == 1                           # T > 32
+                                    1, 1, 8, 2, 64, 16, 16, 1e-6, None) == 6                 # UNSUPPORTED D
+    assert lib.tsds_verify_attention(None, None, None, None, None, None, -1, 1, 4, 8, 2, 64, 64, 64, 64,
+                                     0.1, None, 0, None, None) == 6                           # UNSUPPORTED D

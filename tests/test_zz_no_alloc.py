@@ -44,9 +44,9 @@ def test_noalloc_attention_matches_workspace_entry_point():
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
         ref = torch.empty_like(q)
         got = torch.full_like(q, float("nan"))
-        assert lib.tsds_verify_attention(_p(q), _p(kc), _p(vc), _p(ref), _p(st), None, B, T, 64, 8, 128, S, S, split,
+        assert lib.tsds_verify_attention(_p(q), _p(kc), _p(vc), _p(ref), _p(st), None, -1, B, T, 64, 8, 128, S, S, split,
                                          128 ** -0.5, _p(ws), nb, _p(status), stream) == 0
-        assert lib.tsds_verify_attention_noalloc(_p(q), _p(kc), _p(vc), _p(got), _p(st), None, B, T, 64, 8, 128, S, S,
+        assert lib.tsds_verify_attention_noalloc(_p(q), _p(kc), _p(vc), _p(got), _p(st), None, -1, B, T, 64, 8, 128, S, S,
                                                  split, 128 ** -0.5, stream) == 0
         torch.cuda.synchronize()
         assert torch.equal(got, ref)          # same kernels, same key splits: bit-identical
@@ -60,7 +60,7 @@ def test_noalloc_attention_rejects_requests_beyond_its_scratch():
     lib = _lib.load()
     B, T, S, split = 8, 5, 4096, 64
     assert lib.tsds_attention_workspace_bytes(B, T, 64, 8, 128, S, split) > lib.tsds_verify_attention_noalloc_limit()
-    rc = lib.tsds_verify_attention_noalloc(None, None, None, None, None, None, B, T, 64, 8, 128, S, S, split,
+    rc = lib.tsds_verify_attention_noalloc(None, None, None, None, None, None, -1, B, T, 64, 8, 128, S, S, split,
                                            0.1, _P(torch.cuda.current_stream().cuda_stream))
     assert rc == 8  # TSDS_E_SCRATCH_LIMIT
     assert lib.tsds_status_string(rc) == b"request larger than the built-in scratch area"

@@ -27,7 +27,7 @@ SIGNATURES = {
     "tsds_embed": (_I, [_P, _I, _P, _P, _I, _I, _I, _P]),
     "tsds_rms_norm": (_I, [_P, _P, _P, _I, _I, _I, _I, _F, _P]),
     "tsds_prep_chain": (_I, [_P, _I, _I, _I, _P, _P, _P]),
-    "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "tsds_set_gemv_max_rows": (None, [_I]),
     "tsds_get_gemv_max_rows": (_I, []),
@@ -35,10 +35,19 @@ SIGNATURES = {
     "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_linear_bias": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_logits_topk": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "tsds_tree_state_bytes": (_Z, [_I]),
+    "tsds_tree_init": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
+    "tsds_tree_step": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P]),
+    "tsds_tree_finalize": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
+    "tsds_accept_tree": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "tsds_tree_commit": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _I, _P, _P]),
+    "tsds_eagle_inputs": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "tsds_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
-    "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
+    "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
     "tsds_verify_attention_noalloc_limit": (_Z, []),
-    "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_verify_attention_noalloc_status": (_I, [_P]),
     "tsds_lm_head_workspace_bytes": (_Z, [_I, _I]),
     "tsds_lm_head_argmax": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

@@ -74,7 +74,7 @@ struct AttnArgs {
   float* ws_o;    // [B*Hkv][nsplit][Rpad][D]
   float2* ws_ml;  // [B*Hkv][nsplit][Rpad]
   int32_t* status;
-  int B, T, Hq, Hkv, S, G, R, Rpad, nsplit, split_keys, nrb;
+  int B, T, Hq, Hkv, S, G, R, Rpad, nsplit, split_keys, nrb, mask_origin;
   float scale_log2;
 };
 
@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
       qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
     }
   }
+  const int mask_base = a.mask_origin >= 0 ? a.mask_origin : start;
   const uint32_t mask0 = (a.tree_mask && v0) ? a.tree_mask[b * a.T + t0] : 0u;
   const uint32_t mask1 = (a.tree_mask && v1) ? a.tree_mask[b * a.T + t1] : 0u;
   const bool tree = a.tree_mask != nullptr;
@@ -186,11 +187,19 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int kabs = key0 + j * 8 + 2 * tig + e;
-        const int rel = kabs - start;
         bool vis0 = v0 && kabs < kv_len, vis1 = v1 && kabs < kv_len;
-        if (rel >= 0) {
-          vis0 = vis0 && (tree ? ((mask0 >> rel) & 1u) : (rel <= t0));
-          vis1 = vis1 && (tree ? ((mask1 >> rel) & 1u) : (rel <= t1));
+        if (tree) {
+          // bit i of a row's mask covers key mask_base + i; keys below are shared context
+          const int rel = kabs - mask_base;
+          if (rel >= 0) {
+            const bool in = rel < 32;
+            vis0 = vis0 && in && ((mask0 >> (rel & 31)) & 1u);
+            vis1 = vis1 && in && ((mask1 >> (rel & 31)) & 1u);
+          }
+        } else {
+          const int rel = kabs - start;
+          vis0 = vis0 && rel <= t0;
+          vis1 = vis1 && rel <= t1;
         }
         sc[j][e] = vis0 ? sc[j][e] * a.scale_log2 : -INFINITY;
         sc[j][2 + e] = vis1 ? sc[j][2 + e] * a.scale_log2 : -INFINITY;
@@ -333,11 +342,12 @@ extern "C" size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, 
 }
 
 extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
-                                     const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq, int Hkv,
-                                     int Dd, int S, int max_kv, int split_keys, float scale, void* workspace,
-                                     size_t workspace_bytes, int32_t* status, tsds_stream_t stream) {
+                                     const int32_t* starts, const uint32_t* tree_mask, int mask_origin, int B, int T,
+                                     int Hq, int Hkv, int Dd, int S, int max_kv, int split_keys, float scale,
+                                     void* workspace, size_t workspace_bytes, int32_t* status, tsds_stream_t stream) {
   TSDS_RETURN_IF(Dd != D, TSDS_E_UNSUPPORTED);
-  TSDS_RETURN_IF(B <= 0 || T <= 0 || T > 32 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0 || S <= 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0 || S <= 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(tree_mask != nullptr && mask_origin < 0 && T > 32, TSDS_E_INVALID);
   TSDS_RETURN_IF(max_kv <= 0 || max_kv > S || split_keys <= 0 || (split_keys % TILE) != 0, TSDS_E_INVALID);
   TSDS_RETURN_IF(!q || !k_cache || !v_cache || !out || !starts || !status, TSDS_E_INVALID);
   TSDS_RETURN_IF(!tsds_aligned16(q) || !tsds_aligned16(k_cache) || !tsds_aligned16(v_cache) || !tsds_aligned16(out),
@@ -379,6 +389,7 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.nsplit = nsplit;
   a.split_keys = split_keys;
   a.nrb = nrb;
+  a.mask_origin = mask_origin;
   a.scale_log2 = scale * LOG2E;
 
   const size_t smem = attn_smem_bytes();
@@ -452,9 +463,9 @@ static int attn_noalloc_base(void** out) {
 extern "C" size_t tsds_verify_attention_noalloc_limit(void) { return kNoAllocScratch; }
 
 extern "C" int tsds_verify_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
-                                             const int32_t* starts, const uint32_t* tree_mask, int B, int T, int Hq,
-                                             int Hkv, int Dd, int S, int max_kv, int split_keys, float scale,
-                                             tsds_stream_t stream) {
+                                             const int32_t* starts, const uint32_t* tree_mask, int mask_origin, int B,
+                                             int T, int Hq, int Hkv, int Dd, int S, int max_kv, int split_keys,
+                                             float scale, tsds_stream_t stream) {
   const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
   if (need > kNoAllocScratch) return TSDS_E_SCRATCH_LIMIT;
   void* base = nullptr;
@@ -465,8 +476,9 @@ extern "C" int tsds_verify_attention_noalloc(const void* q, const void* k_cache,
     cudaGetLastError();
     return TSDS_E_LAUNCH;
   }
-  return tsds_verify_attention(q, k_cache, v_cache, out, starts, tree_mask, B, T, Hq, Hkv, Dd, S, max_kv, split_keys,
-                               scale, static_cast<char*>(base) + kNoAllocHeader, kNoAllocScratch, status, stream);
+  return tsds_verify_attention(q, k_cache, v_cache, out, starts, tree_mask, mask_origin, B, T, Hq, Hkv, Dd, S, max_kv,
+                               split_keys, scale, static_cast<char*>(base) + kNoAllocHeader, kNoAllocScratch, status,
+                               stream);
 }
 
 extern "C" int tsds_verify_attention_noalloc_status(int32_t* host_status) {

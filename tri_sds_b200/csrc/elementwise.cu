@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const bf16* __restrict__ qkv, const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w,
     const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const int32_t* __restrict__ positions,
     const int32_t* __restrict__ starts, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
-    bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, float eps) {
+    bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, int rope_len, float eps) {
   constexpr int D = 128;
   pdl_wait();
   pdl_trigger();
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   const int pos = positions[m];
   // rows / positions past the cache or the RoPE table are never written
   // (the host keeps lengths below S; this only prevents out-of-range stores)
-  if (row_in_seq < 0 || row_in_seq >= S || pos < 0 || pos >= S) return;
+  if (row_in_seq < 0 || row_in_seq >= S || pos < 0 || pos >= rope_len) return;
   if (h >= Hq + Hkv) {  // v head: copy into the cache
     const int kvh = h - Hq - Hkv;
     const int64_t row = ((int64_t)b * Hkv + kvh) * S + row_in_seq;
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
 extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
                                     const void* sin, const int32_t* positions, const int32_t* starts, void* q_out,
                                     void* k_cache, void* v_cache, int B, int T, int Hq, int Hkv, int D, int S,
-                                    float eps, tsds_stream_t stream) {
+                                    int rope_len, float eps, tsds_stream_t stream) {
   TSDS_RETURN_IF(D != 128, TSDS_E_UNSUPPORTED);
   TSDS_RETURN_IF(B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0 || S <= 0, TSDS_E_INVALID);
   TSDS_RETURN_IF(!qkv || !cos || !sin || !positions || !starts || !q_out || !k_cache || !v_cache, TSDS_E_INVALID);
@@ -196,7 +196,7 @@ extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const
   const int warps = M * (Hq + 2 * Hkv);
   tsds_launch(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream,
       (const bf16*)qkv, (const bf16*)q_norm_w, (const bf16*)k_norm_w, (const bf16*)cos, (const bf16*)sin, positions,
-      starts, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, M, T, Hq, Hkv, S, eps);
+      starts, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, M, T, Hq, Hkv, S, rope_len, eps);
   return tsds_launch_status();
 }
 

@@ -40,7 +40,7 @@ constexpr int SMEM_BUDGET = 220 * 1024;
 struct TcParams {
   int M, Npad, n_out, K, KT, tiles, P;
   long long W;
-  int epi, up_off, ldo;
+  int epi, up_off, ldo, res_ld;
   const bf16* res;
   bf16* out;
   float* ws;
@@ -135,7 +135,7 @@ __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t,
         const int m = m0 + jj;
         if (m < p.M) {
           const int64_t o = (int64_t)m * p.ldo + j;
-          p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[o]) + rbf(v[jj]));
+          p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[(int64_t)m * p.res_ld + j]) + rbf(v[jj]));
         }
       }
     }
@@ -431,9 +431,9 @@ size_t tsds_tc_workspace_bytes(int M) {
   return 64 + 2048 * sizeof(int) + (size_t)num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
 }
 
-int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, bf16* out, int ldo,
-                 int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val, int* cand_idx,
-                 int ldc, cudaStream_t stream) {
+int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
+                 int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
+                 int* cand_idx, int ldc, cudaStream_t stream) {
   TSDS_RETURN_IF(M <= 0 || M > 256, TSDS_E_INVALID);
   TSDS_RETURN_IF(workspace == nullptr || workspace_bytes < tsds_tc_workspace_bytes(M), TSDS_E_WORKSPACE);
   TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
@@ -455,6 +455,7 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.epi = epi;
   p.up_off = n_out;
   p.ldo = ldo;
+  p.res_ld = res_ld;
   p.res = res;
   p.out = out;
   p.counters = (int*)((char*)workspace + 64);

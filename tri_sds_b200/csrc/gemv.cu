@@ -31,7 +31,8 @@ struct GemvCfg {
 
 template <int MT, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, int ldx, const bf16* __restrict__ W,
-                                                   const bf16* res, bf16* out, int ldo, int n_out, int K) {
+                                                   const bf16* res, int res_ld, bf16* out, int ldo, int n_out,
+                                                   int K) {
   constexpr int R = GemvCfg<MT>::R;
   constexpr int OUT_PER_WARP = EPI == EPI_SWIGLU ? R / 2 : R;
   pdl_wait();
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, i
       if (EPI == EPI_STORE) {
         out[o] = f2bf(sum[r][m]);
       } else if (EPI == EPI_RESIDUAL) {
-        out[o] = f2bf(bf2f(res[o]) + rbf(sum[r][m]));
+        out[o] = f2bf(bf2f(res[(int64_t)m * res_ld + j]) + rbf(sum[r][m]));
       } else {  // SWIGLU: silu on the bf16 gate, product of bf16 values (qwen_model.py:139-142)
         const float g = rbf(sum[r][m]);
         const float u = rbf(sum[r + OUT_PER_WARP][m]);
@@ -106,21 +107,21 @@ __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, i
 }
 
 template <int EPI>
-int launch_gemv_rows(const bf16* x, int ldx, const bf16* W, const bf16* res, bf16* out, int ldo, int M, int n_out,
-                     int K, cudaStream_t stream) {
+int launch_gemv_rows(const bf16* x, int ldx, const bf16* W, const bf16* res, int res_ld, bf16* out, int ldo, int M,
+                     int n_out, int K, cudaStream_t stream) {
   // process up to 8 rows per launch
   for (int m0 = 0; m0 < M; m0 += 8) {
     const int mt = M - m0 < 8 ? M - m0 : 8;
     const bf16* xs = x + (int64_t)m0 * ldx;
-    const bf16* rs = res ? res + (int64_t)m0 * ldo : nullptr;
+    const bf16* rs = res ? res + (int64_t)m0 * res_ld : nullptr;
     bf16* os = out + (int64_t)m0 * ldo;
 #define TSDS_GEMV_CASE(MTV)                                                                          \
   case MTV: {                                                                                        \
     constexpr int R = GemvCfg<MTV>::R;                                                               \
     constexpr int OPW = EPI == EPI_SWIGLU ? R / 2 : R;                                               \
     const int warps = (n_out + OPW - 1) / OPW;                                                       \
-    tsds_launch(gemv_kernel<MTV, EPI>, dim3((warps + 7) / 8), dim3(256), 0, stream, xs, ldx, W, rs, os, ldo, n_out, \
-                K);                                                                                   \
+    tsds_launch(gemv_kernel<MTV, EPI>, dim3((warps + 7) / 8), dim3(256), 0, stream, xs, ldx, W, rs, res_ld, os, ldo, \
+                n_out, K);                                                                            \
     break;                                                                                           \
   }
     switch (mt) {
@@ -142,12 +143,12 @@ int launch_gemv_rows(const bf16* x, int ldx, const bf16* W, const bf16* res, bf1
 
 }  // namespace
 
-int tsds_gemv_dispatch(int epi, const bf16* x, int ldx, const bf16* W, const bf16* res, bf16* out, int ldo, int M,
-                       int n_out, int K, cudaStream_t stream) {
+int tsds_gemv_dispatch(int epi, const bf16* x, int ldx, const bf16* W, const bf16* res, int res_ld, bf16* out, int ldo,
+                       int M, int n_out, int K, cudaStream_t stream) {
   switch (epi) {
-    case EPI_STORE: return launch_gemv_rows<EPI_STORE>(x, ldx, W, res, out, ldo, M, n_out, K, stream);
-    case EPI_RESIDUAL: return launch_gemv_rows<EPI_RESIDUAL>(x, ldx, W, res, out, ldo, M, n_out, K, stream);
-    case EPI_SWIGLU: return launch_gemv_rows<EPI_SWIGLU>(x, ldx, W, res, out, ldo, M, n_out, K, stream);
+    case EPI_STORE: return launch_gemv_rows<EPI_STORE>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
+    case EPI_RESIDUAL: return launch_gemv_rows<EPI_RESIDUAL>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
+    case EPI_SWIGLU: return launch_gemv_rows<EPI_SWIGLU>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
   }
   return TSDS_E_INVALID;
 }

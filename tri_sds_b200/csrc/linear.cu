@@ -14,16 +14,16 @@ int check_linear(const void* x, int ldx, const void* W, const void* out, int ldo
 // CUDA-core GEMV even at M = 1, so the GEMV is opt-in (tsds_set_gemv_max_rows).
 int g_gemv_max_rows = 0;
 
-int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, void* out, int ldo, int M, int n_out,
-               int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, int res_ld, void* out, int ldo, int M,
+               int n_out, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (M <= g_gemv_max_rows)
-    return tsds_gemv_dispatch(epi, (const bf16*)x, ldx, (const bf16*)W, (const bf16*)res, (bf16*)out, ldo, M, n_out,
-                              K, stream);
+    return tsds_gemv_dispatch(epi, (const bf16*)x, ldx, (const bf16*)W, (const bf16*)res, res_ld, (bf16*)out, ldo, M,
+                              n_out, K, stream);
   const int w_rows = epi == EPI_SWIGLU ? 2 * n_out : n_out;
   for (int m0 = 0; m0 < M; m0 += 256) {  // rows beyond 256 (prefill-sized) in chunks
     const int mc = M - m0 < 256 ? M - m0 : 256;
-    const bf16* res_c = res ? (const bf16*)res + (int64_t)m0 * ldo : nullptr;
-    int st = tsds_tc_gemm(epi, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, w_rows, res_c,
+    const bf16* res_c = res ? (const bf16*)res + (int64_t)m0 * res_ld : nullptr;
+    int st = tsds_tc_gemm(epi, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, w_rows, res_c, res_ld,
                           (bf16*)out + (int64_t)m0 * ldo, ldo, mc, n_out, K, workspace, workspace_bytes, nullptr,
                           nullptr, 0, stream);
     if (st != TSDS_OK) return st;
@@ -50,7 +50,7 @@ extern "C" int tsds_linear(const void* x, int ldx, const void* W, void* out, int
                            void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
   int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
   if (st != TSDS_OK) return st;
-  return run_linear(EPI_STORE, x, ldx, W, nullptr, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+  return run_linear(EPI_STORE, x, ldx, W, nullptr, 0, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
 }
 
 extern "C" int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo, int M,
@@ -58,12 +58,20 @@ extern "C" int tsds_linear_residual(const void* x, int ldx, const void* W, const
   int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
   if (st != TSDS_OK) return st;
   TSDS_RETURN_IF(!res, TSDS_E_INVALID);
-  return run_linear(EPI_RESIDUAL, x, ldx, W, res, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+  return run_linear(EPI_RESIDUAL, x, ldx, W, res, ldo, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
 }
 
 extern "C" int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                                   void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
   int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
   if (st != TSDS_OK) return st;
-  return run_linear(EPI_SWIGLU, x, ldx, W, nullptr, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+  return run_linear(EPI_SWIGLU, x, ldx, W, nullptr, 0, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tsds_linear_bias(const void* x, int ldx, const void* W, const void* bias, void* out, int ldo, int M,
+                                int n_out, int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
+  int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
+  if (st != TSDS_OK) return st;
+  TSDS_RETURN_IF(!bias, TSDS_E_INVALID);
+  return run_linear(EPI_RESIDUAL, x, ldx, W, bias, 0, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
 }

@@ -5,16 +5,17 @@
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2 };
 
 // CUDA-core GEMV, any M (processed 8 rows per launch).
-int tsds_gemv_dispatch(int epi, const bf16* x, int ldx, const bf16* W, const bf16* res, bf16* out, int ldo, int M,
-                       int n_out, int K, cudaStream_t stream);
+// res[m * res_ld + j] is the residual (res_ld = 0: a bias broadcast over rows).
+int tsds_gemv_dispatch(int epi, const bf16* x, int ldx, const bf16* W, const bf16* res, int res_ld, bf16* out, int ldo,
+                       int M, int n_out, int K, cudaStream_t stream);
 
 // tcgen05 persistent GEMM, M <= 256.  epi also accepts EPI_ARGMAX (LM head:
 // bf16 logits to `out` when non-null, per-tile candidates to cand_*).
 enum { EPI_ARGMAX = 3 };
 size_t tsds_tc_workspace_bytes(int M);
-int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, bf16* out, int ldo,
-                 int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val, int* cand_idx,
-                 int ldc, cudaStream_t stream);
+int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
+                 int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
+                 int* cand_idx, int ldc, cudaStream_t stream);
 
 // Row count up to which the CUDA-core GEMV is used instead of tcgen05.
 int tsds_gemv_rows_limit();

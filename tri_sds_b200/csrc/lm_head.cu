@@ -176,7 +176,7 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
     const int tiles = (vocab + 127) / 128;
     for (int m0 = 0; m0 < M; m0 += 256) {
       const int mc = M - m0 < 256 ? M - m0 : 256;
-      int st = tsds_tc_gemm(EPI_ARGMAX, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, vocab, nullptr,
+      int st = tsds_tc_gemm(EPI_ARGMAX, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, vocab, nullptr, 0,
                             logits_out ? (bf16*)logits_out + (int64_t)m0 * vocab : nullptr, vocab, mc, vocab, K, tcws,
                             tcb, cval + (int64_t)m0 * ldc, cidx + (int64_t)m0 * ldc, ldc, stream);
       if (st != TSDS_OK) return st;

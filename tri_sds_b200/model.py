@@ -108,7 +108,8 @@ class QwenModel:
     """
 
     def __init__(self, shape: QwenShape, batch: int, max_seq: int, max_rows: int, device="cuda",
-                 weights: dict | None = None, seed: int = 0, split_keys: int = 256, qk_norm: bool | None = None):
+                 weights: dict | None = None, seed: int = 0, split_keys: int = 256, qk_norm: bool | None = None,
+                 share_embeddings: "QwenModel | None" = None, rope_len: int | None = None):
         self.shape = shape
         self.batch = batch
         self.max_seq = max_seq
@@ -120,19 +121,28 @@ class QwenModel:
         dev = self.device
         if weights is not None:
             self.layers = [pack_layer(L, dev) for L in weights["layers"]]
+        else:
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(seed)
+            self.layers = [random_layer_gpu(s, gen, dev) for _ in range(s.n_layers)]
+        if share_embeddings is not None:
+            # the EAGLE head runs on the target's embedding, final norm and LM head
+            self.embed_w, self.lm_head_w, self.norm_w = (share_embeddings.embed_w, share_embeddings.lm_head_w,
+                                                         share_embeddings.norm_w)
+        elif weights is not None:
             self.embed_w = weights["embed"].to(dev, torch.bfloat16).contiguous()
             self.lm_head_w = (self.embed_w if weights["lm_head"] is weights["embed"]
                               else weights["lm_head"].to(dev, torch.bfloat16).contiguous())
             self.norm_w = weights["norm"].to(dev, torch.bfloat16).contiguous()
         else:
-            gen = torch.Generator(device=dev)
-            gen.manual_seed(seed)
-            self.layers = [random_layer_gpu(s, gen, dev) for _ in range(s.n_layers)]
             self.embed_w = (torch.randn(s.vocab, s.hidden, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
             self.lm_head_w = self.embed_w if s.tie_embeddings else \
                 (torch.randn(s.vocab, s.hidden, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
             self.norm_w = (1.0 + 0.02 * torch.randn(s.hidden, device=dev, generator=gen)).to(torch.bfloat16)
-        self.cos, self.sin = precompute_rope(s.head_dim, max_seq, s.rope_theta, dev)
+        # RoPE tables cover absolute positions (the EAGLE head's small cache
+        # holds rows of a tree whose positions continue the sequence)
+        self.rope_len = max_seq if rope_len is None else rope_len
+        self.cos, self.sin = precompute_rope(s.head_dim, self.rope_len, s.rope_theta, dev)
         self.k_cache = torch.zeros(s.n_layers, batch, s.n_kv_heads, max_seq, s.head_dim, dtype=torch.bfloat16,
                                    device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -163,9 +173,13 @@ class QwenModel:
         self.lm_ws = torch.zeros(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
 
     # -- launch plans ---------------------------------------------------------
-    def layers_plan(self, B: int, T: int, tree_mask: torch.Tensor | None = None) -> Plan:
+    def layers_plan(self, B: int, T: int, tree_mask: torch.Tensor | None = None, mask_origin: int = -1,
+                    x: torch.Tensor | None = None, starts: torch.Tensor | None = None,
+                    positions: torch.Tensor | None = None) -> Plan:
         """All decoder layers over rows x[0:B*T] (embedded already), with
-        starts/positions already prepared."""
+        starts/positions already prepared.  ``x`` / ``starts`` /
+        ``positions`` default to the model's own buffers; ``tree_mask`` +
+        ``mask_origin`` select the attention mask (see tsds_verify_attention)."""
         s = self.shape
         M = B * T
         assert M <= self.max_rows and B == self.batch
@@ -173,35 +187,40 @@ class QwenModel:
         pl = Plan()
         lw, lb = self.lin_ws, self.lin_ws_bytes
         qn = self.qk_norm
+        xb = self.x if x is None else x
+        st = self.starts if starts is None else starts
+        ps = self.positions if positions is None else positions
         for i, L in enumerate(self.layers):
             kc, vc = self.k_cache[i], self.v_cache[i]
-            pl.add("tsds_rms_norm", _p(self.x), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
+            pl.add("tsds_rms_norm", _p(xb), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear", _p(self.xn), s.hidden, _p(L.w_qkv), _p(self.qkv), s.qkv_dim, M, s.qkv_dim,
                    s.hidden, _p(lw), lb)
             pl.add("tsds_qk_norm_rope_kv", _p(self.qkv), _p(L.q_norm) if qn else None,
-                   _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(self.positions), _p(self.starts),
-                   _p(self.q), _p(kc), _p(vc), B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq, eps)
-            pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(self.starts),
-                   _p(tree_mask), B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq, self.max_seq,
-                   self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
+                   _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(ps), _p(st),
+                   _p(self.q), _p(kc), _p(vc), B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq, self.rope_len,
+                   eps)
+            pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(st),
+                   _p(tree_mask), mask_origin, B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq,
+                   self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
                    _p(self.status))
-            pl.add("tsds_linear_residual", _p(self.attn), s.q_dim, _p(L.w_o), _p(self.x), _p(self.x), s.hidden, M,
+            pl.add("tsds_linear_residual", _p(self.attn), s.q_dim, _p(L.w_o), _p(xb), _p(xb), s.hidden, M,
                    s.hidden, s.q_dim, _p(lw), lb)
-            pl.add("tsds_rms_norm", _p(self.x), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
+            pl.add("tsds_rms_norm", _p(xb), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), s.intermediate, M,
                    s.intermediate, s.hidden, _p(lw), lb)
-            pl.add("tsds_linear_residual", _p(self.h), s.intermediate, _p(L.w_d), _p(self.x), _p(self.x), s.hidden,
+            pl.add("tsds_linear_residual", _p(self.h), s.intermediate, _p(L.w_d), _p(xb), _p(xb), s.hidden,
                    M, s.hidden, s.intermediate, _p(lw), lb)
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,
-                  logits_out: torch.Tensor | None = None) -> Plan:
+                  logits_out: torch.Tensor | None = None, x: torch.Tensor | None = None) -> Plan:
         """Final RMSNorm + LM head + argmax over all rows, or only the last
         row of each sequence."""
         s = self.shape
         pl = Plan()
+        xb = self.x if x is None else x
         rows, ld = (B, T * s.hidden) if last_only else (B * T, s.hidden)
-        src = self.x[T - 1:] if last_only else self.x
+        src = xb[T - 1:] if last_only else xb
         pl.add("tsds_rms_norm", _p(src), _p(self.norm_w), _p(self.xn), rows, s.hidden, ld, s.hidden, s.eps)
         pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(logits_out), _p(argmax_out),
                argmax_stride, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)

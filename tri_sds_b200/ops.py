@@ -180,7 +180,8 @@ def qk_norm_rope_kv(qkv, q_norm_w, k_norm_w, cos, sin, positions, starts, q_out,
     D = k_cache.shape[-1]
     S = k_cache.shape[-2]
     _lib.call("tsds_qk_norm_rope_kv", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin), _p(positions),
-              _p(starts), _p(q_out), _p(k_cache), _p(v_cache), B, T, Hq, Hkv, D, S, float(eps), _stream())
+              _p(starts), _p(q_out), _p(k_cache), _p(v_cache), B, T, Hq, Hkv, D, S, cos.shape[0], float(eps),
+              _stream())
 
 
 def fused_rmsnorm_qkv_rope(x, norm1_w, qkv_w_t, q_out, k_cache, v_cache, cos, sin, pos, N, q_dim, kv_dim,
@@ -199,7 +200,7 @@ def fused_rmsnorm_qkv_rope(x, norm1_w, qkv_w_t, q_out, k_cache, v_cache, cos, si
 
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, starts: torch.Tensor,
                      tree_mask: torch.Tensor | None = None, max_kv: int | None = None, split_keys: int = 256,
-                     scale: float | None = None, out: torch.Tensor | None = None):
+                     scale: float | None = None, out: torch.Tensor | None = None, mask_origin: int = -1):
     """Attention of q [B, T, Hq, D] over caches [B, Hkv, S, D] whose rows
     ``starts[b]..starts[b]+T-1`` hold the new tokens (qwen_model.py:121-131
     with per-sequence starts and an optional [B, T] tree bitmask)."""
@@ -217,7 +218,7 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     ws = _scratch.get(nb, q.device, "attention") if nb else None
     status = _scratch.status_word(q.device)
     _lib.call("tsds_verify_attention", _p(q), _p(k_cache), _p(v_cache), _p(out), _p(starts), _p(tree_mask),
-              B, T, Hq, Hkv, D, S, max_kv, split_keys, scale, _p(ws), nb, _p(status), _stream())
+              int(mask_origin), B, T, Hq, Hkv, D, S, max_kv, split_keys, scale, _p(ws), nb, _p(status), _stream())
     return out
 
 
