@@ -1,11 +1,19 @@
 #!/usr/bin/env python
-"""Benchmark: greedy chain speculative decoding, Qwen3-4B-shape draft -> Qwen3-32B-shape target.
+"""Benchmark: speculative decoding on a Qwen3-32B-shape target.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl tsds|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--mode eagle|chain]
+                    [--impl tsds|reference]
 
-One step = one speculative cycle over B sequences: K=4 draft forwards
-(Qwen3-4B shape, 36 layers), one target verify forward over K+1 tokens per
-sequence (Qwen3-32B shape, 64 layers), greedy acceptance and KV commit.
+One step = one speculative cycle over B sequences:
+
+* ``--mode eagle`` (default): EAGLE draft head (fc 2x5120->5120 + one
+  Qwen3-32B-shape decoder layer, the target's LM head), draft tree of depth
+  5 with top-4 expansion pruned to 25 nodes, one target pass over the tree
+  with the ancestor mask, rejection sampling at temperature 1 with seeded
+  uniforms, KV compaction;
+* ``--mode chain``: Qwen3-4B-shape draft model (36 layers), K=4 greedy
+  chain, target verify over K+1 tokens, greedy acceptance.
+
 Weights are random N(0, 0.02) (no checkpoints offline), prompts are 512
 seeded uniform ids.  The metric is whole-job tokens/s (emitted tokens,
 i.e. sum over sequences of accept_len + 1 per cycle).
@@ -40,6 +48,8 @@ def _args():
     ap.add_argument("--impl", default="tsds", choices=["tsds", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--k", type=int, default=4)
+    ap.add_argument("--mode", default="eagle", choices=["eagle", "chain"])
+    ap.add_argument("--greedy", action="store_true", help="eagle mode: greedy acceptance instead of sampling")
     ap.add_argument("--prompt", type=int, default=512)
     # smaller depth for profiler captures only (never for reported numbers)
     ap.add_argument("--target-layers", type=int, default=None)
@@ -58,6 +68,10 @@ DATA = "synthetic: seeded uniform prompt ids, random-init N(0,0.02) weights (no 
 
 
 def _workload(a) -> str:
+    if a.mode == "eagle":
+        acc = "greedy" if a.greedy else "rejection sampling T=1.0"
+        return (f"EAGLE tree spec decode: head fc 2x5120->5120 + 1 Qwen3-32B-shape layer, tree depth 5 / top-4 / "
+                f"25 nodes, {acc}, Qwen3-32B-shape target (64L), prompt {a.prompt}, B={a.batch}")
     return (f"greedy chain spec decode: Qwen3-4B-shape draft (36L) -> Qwen3-32B-shape target (64L), "
             f"K={a.k}, prompt {a.prompt}, B={a.batch}")
 
@@ -123,10 +137,15 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 class CpuCycle:
-    """One full cycle on the host CPU, estimated from a bounded sample: one
-    target layer verify (T=K+1 over a cache of the prompt), one draft layer
-    step (T=1), and each model's final norm + LM head, timed with the
-    oracle and scaled to 64 target and 36 x K draft layers."""
+    """One full cycle on the host CPU, estimated from a bounded sample timed
+    with the oracle: one layer of each model at the cycle's row counts plus
+    the final norm + LM heads, scaled to the layer counts of the cycle.
+
+    chain: 1 Qwen3-32B-shape layer verify (T=K+1) x64 + LM head, and
+           1 Qwen3-4B-shape layer decode x36 x K + K LM heads;
+    eagle: 1 Qwen3-32B-shape layer tree verify (T=26) x64 + LM head over 26
+           rows, and 5 head passes (fc 2N->N, 1 target-shape layer, LM head)
+           at T=1 then T=4."""
 
     def __init__(self, a):
         import torch
@@ -137,35 +156,58 @@ class CpuCycle:
         B, K, P = a.batch, a.k, a.prompt
         self.a = a
         self.models = {}
-        for name, shape in (("target", QWEN3_32B), ("draft", QWEN3_4B)):
+        shapes = (("target", QWEN3_32B),) if a.mode == "eagle" else (("target", QWEN3_32B), ("draft", QWEN3_4B))
+        for name, shape in shapes:
             one = replace(shape, n_layers=1)
-            st = QwenOracle(one, random_qwen_weights(one, seed=1), batch=B, max_seq=P + 2 * K + 4)
+            st = QwenOracle(one, random_qwen_weights(one, seed=1), batch=B, max_seq=P + 32)
             ids = torch.randint(0, shape.vocab, (B, P), generator=torch.Generator().manual_seed(2))
             with torch.no_grad():
                 st.layer(0, st.embed_w[ids], torch.zeros(B, dtype=torch.int64), torch.arange(P), None)
             self.models[name] = (st, ids, shape.n_layers)
-        self.sample = (f"oracle bf16 on {self.threads} threads: 1 Qwen3-32B-shape layer verify (T={K + 1}) x64 "
-                       f"+ LM head; 1 Qwen3-4B-shape layer decode x36 x K={K} + {K} LM heads; B={B}, cache {P}")
+        if a.mode == "eagle":
+            N = QWEN3_32B.hidden
+            self.fc = (torch.randn(2 * N, N) * 0.02).to(torch.bfloat16)
+            self.sample = (f"oracle bf16 on {self.threads} threads: 1 Qwen3-32B-shape layer tree verify (T=26) x64 "
+                           f"+ LM head over 26 rows; 5 EAGLE head passes (fc + 1 layer + LM head, T=1 then 4); "
+                           f"B={B}, cache {P}")
+        else:
+            self.sample = (f"oracle bf16 on {self.threads} threads: 1 Qwen3-32B-shape layer verify (T={K + 1}) x64 "
+                           f"+ LM head; 1 Qwen3-4B-shape layer decode x36 x K={K} + {K} LM heads; B={B}, cache {P}")
+
+    def _time(self, st, ids, T, P, B):
+        import torch
+        xs = st.embed_w[ids[:, :T]]
+        starts = torch.full((B,), P, dtype=torch.int64)
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            st.layer(0, xs, starts, torch.arange(P, P + T), None)
+            t_layer = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            st.logits(xs)
+            t_head = time.perf_counter() - t0
+        return t_layer, t_head
 
     def seconds(self) -> float:
         import torch
         B, K, P = self.a.batch, self.a.k, self.a.prompt
+        if self.a.mode == "eagle":
+            st, ids, n_layers = self.models["target"]
+            t_layer, t_head = self._time(st, ids, 26, P, B)
+            total = t_layer * n_layers + t_head
+            for T in (1, 4, 4, 4, 4):
+                x2 = torch.cat([st.embed_w[ids[:, :T]], st.embed_w[ids[:, :T]]], -1)
+                with torch.no_grad():
+                    t0 = time.perf_counter()
+                    x2 @ self.fc
+                    t_fc = time.perf_counter() - t0
+                h_layer, h_head = self._time(st, ids, T, P, B)
+                total += t_fc + h_layer + h_head
+            return total
         total = 0.0
         for name, (st, ids, n_layers) in self.models.items():
             T = K + 1 if name == "target" else 1
-            xs = st.embed_w[ids[:, :T]]
-            starts = torch.full((B,), P, dtype=torch.int64)
-            with torch.no_grad():
-                t0 = time.perf_counter()
-                st.layer(0, xs, starts, torch.arange(P, P + T), None)
-                t_layer = time.perf_counter() - t0
-                t0 = time.perf_counter()
-                st.logits(xs)
-                t_head = time.perf_counter() - t0
-            if name == "target":
-                total += t_layer * n_layers + t_head
-            else:
-                total += (t_layer * n_layers + t_head) * K
+            t_layer, t_head = self._time(st, ids, T, P, B)
+            total += t_layer * n_layers + t_head if name == "target" else (t_layer * n_layers + t_head) * K
         return total
 
 
@@ -218,11 +260,18 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_pdl(0)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
-    max_seq = P + (a.warmup + a.steps) * (K + 1) * 2 + 4 * (K + 1) + 64
+    per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
+    rows_verify = B * 26 if a.mode == "eagle" else B * (K + 1)
+    max_seq = P + (3 * a.warmup + 2 * a.steps) * per_cycle + 64 + 32
     max_seq = (max_seq + 63) // 64 * 64
-    target = QwenModel(tshape, B, max_seq, max_rows=B * (K + 1), device=dev, seed=1000 + rank)
-    draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000 + rank)
-    engine = SpecEngine(target, draft, K)
+    target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000 + rank)
+    if a.mode == "eagle":
+        from tri_sds_b200.eagle import EagleEngine, EagleHead
+        head = EagleHead(target, B, seed=2000 + rank)
+        engine = EagleEngine(target, head, greedy=a.greedy, seed=3000 + rank)
+    else:
+        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000 + rank)
+        engine = SpecEngine(target, draft, K)
     prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7 + rank))
     lc0 = _lib.query("tsds_launch_count")
     engine.prepare(prompt)
@@ -266,7 +315,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     launches_per_cycle = engine.plan_launches
 
     # ---- verify step alone (target forward over K+1 tokens) ------------------
-    vplan = target.forward_plan(engine.verify_ids, 1, B, K + 1, target.lengths, 0, engine.target_argmax, 1)
+    vplan = engine.verify_only_plan()
     vplan.run()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
@@ -286,7 +335,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
 
     # ---- dominant kernel: the target's gate/up + SiLU projection -------------
     from tri_sds_b200 import ops
-    M = B * (K + 1)
+    M = rows_verify
     xin = torch.randn(M, tshape.hidden, device=dev).to(torch.bfloat16)
     hout = torch.empty(M, tshape.intermediate, dtype=torch.bfloat16, device=dev)
     for L in target.layers[:2]:
@@ -330,7 +379,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             dist.all_reduce(sm, op=dist.ReduceOp.SUM)
             el, e_tokens = float(mx[0]), float(sm[1])
         e2e = {"value": e_tokens / el, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
-               "d2h_bytes_per_step": 8 * B * (K + 1) + 4 * B}
+               "d2h_bytes_per_step": engine.tokens.numel() * 8 + 4 * B}
 
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
@@ -349,7 +398,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "config": {"workload": _workload(a), "global_batch": B * world, "seq_len": P,
                        "parallelism": "tp1" if world == 1 else f"tp1 x {world} replicas",
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
-                       "target_layers": tshape.n_layers, "draft_layers": dshape.n_layers},
+                       "mode": a.mode, "target_layers": tshape.n_layers,
+                       "draft_layers": 0 if a.mode == "eagle" else dshape.n_layers},
             "verify_step_us": verify_us,
             "accept_len_mean": float(acc.mean()),
             "roofline": {"bound": "hbm", "kernel": "tsds_linear_swiglu (target gate/up, M=%d)" % M,

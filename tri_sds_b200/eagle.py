@@ -148,6 +148,30 @@ class EagleEngine:
                s.hidden, _p(self.root_feat))
         return pl
 
+    def verify_only_plan(self) -> Plan:
+        """The target's tree verify forward alone (for timing the verify step)."""
+        t = self.target
+        s = t.shape
+        B, NN = t.batch, self.n_nodes + 1
+        pl = Plan()
+        pl.add("tsds_embed", _p(self.ids), 1, _p(t.embed_w), _p(t.x), B * NN, s.hidden, s.vocab)
+        pl.extend(t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1))
+        pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits))
+        return pl
+
+    @property
+    def k(self):
+        return self.topk
+
+    def step_host(self, cur_host: torch.Tensor, tokens_host: torch.Tensor, accept_host: torch.Tensor):
+        """One cycle driven from the host (pinned buffers), as SpecEngine.step_host."""
+        self.cur.copy_(cur_host, non_blocking=True)
+        self.step()
+        tokens_host.copy_(self.tokens, non_blocking=True)
+        accept_host.copy_(self.accept_len, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return tokens_host, accept_host
+
     # -- driving -----------------------------------------------------------------
     @torch.no_grad()
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:

@@ -69,6 +69,11 @@ class SpecEngine:
                _p(self.tokens), _p(t.lengths), _p(self.last), _p(self.cur), B, K)
         return pl
 
+    def verify_only_plan(self) -> Plan:
+        """The target's verify forward alone (for timing the verify step)."""
+        t = self.target
+        return t.forward_plan(self.verify_ids, 1, t.batch, self.k + 1, t.lengths, 0, self.target_argmax, 1)
+
     def kernel_launches_per_cycle(self) -> int:
         return self.plan.kernel_count()
 

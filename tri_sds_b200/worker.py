@@ -80,10 +80,10 @@ class TriSDSWorker(StandaloneWorker):
         self._ensure(batch)
         ids = batch.input_ids
         if not first and isinstance(ids, torch.Tensor) and not ids.is_cuda and ids.dim() == 2 and ids.shape[1] == 1:
-            B, K = self.engine.tokens.shape[0], self.engine.k
+            B, W = self.engine.tokens.shape
             if getattr(self, "_host_bufs", None) is None:
                 self._host_bufs = (torch.empty(B, dtype=torch.int64).pin_memory(),
-                                   torch.empty(B, K + 1, dtype=torch.int64).pin_memory(),
+                                   torch.empty(B, W, dtype=torch.int64).pin_memory(),
                                    torch.empty(B, dtype=torch.int32).pin_memory())
             cur_h, tok_h, acc_h = self._host_bufs
             cur_h.copy_(ids[:, 0])
