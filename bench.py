@@ -18,8 +18,11 @@ Weights are random N(0, 0.02) (no checkpoints offline), prompts are 512
 seeded uniform ids.  The metric is whole-job tokens/s (emitted tokens,
 i.e. sum over sequences of accept_len + 1 per cycle).
 
-N > 1 (torchrun) runs one independent replica per GPU; the time is the max
-over ranks and the value the sum of all ranks' tokens over that time.
+N > 1 (torchrun): the target is tensor-parallel over the N GPUs (heads and
+FFN sharded, NCCL all-reduce after the O and down projections, vocab-parallel
+LM head); the draft model / EAGLE head is replicated.  The ranks serve the
+same B sequences, so the value is those tokens over the max-over-ranks time
+(strong scaling).
 
 ``--impl reference`` times the reference's PyTorch algorithm on the host
 CPU cores (the CPU oracle: a restatement of tri_sds/triton_kernels/
@@ -230,7 +233,7 @@ def run_reference(a, rank: int, world: int):
     tok_s = a.batch / cyc
     line = {"impl": "reference", "metric": METRIC.format(B=a.batch, n=1), "value": tok_s, "unit": "tok/s",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": cyc * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": a.batch, "seq_len": a.prompt,
                        "parallelism": "cpu"},
             "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
@@ -264,13 +267,21 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     rows_verify = B * 26 if a.mode == "eagle" else B * (K + 1)
     max_seq = P + (3 * a.warmup + 2 * a.steps) * per_cycle + 64 + 32
     max_seq = (max_seq + 63) // 64 * 64
-    target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000 + rank)
+    # N > 1: the target is tensor-parallel over all ranks (shards drawn per
+    # rank; replicated tensors from the same seed on every rank)
+    comm = None
+    if world > 1:
+        from tri_sds_b200.tp import Comm
+        comm = Comm()
+    target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
+                       tp_size=world, comm=comm)
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
-        head = EagleHead(target, B, seed=2000 + rank)
-        engine = EagleEngine(target, head, greedy=a.greedy, seed=3000 + rank)
+        head = EagleHead(target, B, seed=2000)
+        engine = EagleEngine(target, head, greedy=a.greedy, seed=3000)
     else:
-        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000 + rank)
+        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
+                          tp_layers=False, tp_vocab=False)
         engine = SpecEngine(target, draft, K)
     prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7 + rank))
     lc0 = _lib.query("tsds_launch_count")
@@ -302,15 +313,11 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     ms = ev0.elapsed_time(ev1)
     acc = hist[a.warmup:].float().cpu()
     tokens = float((acc + 1).sum())
-    t = torch.tensor([ms, tokens], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = t.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_max, tokens_all = float(mx[0]), float(sm[1])
-    else:
-        ms_max, tokens_all = ms, tokens
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # the ranks serve the same B sequences together: tokens are counted once
+    ms_max, tokens_all = float(t[0]), tokens
     value = tokens_all / (ms_max / 1e3)
     launches_per_cycle = engine.plan_launches
 
@@ -371,13 +378,10 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             cur_host = toks.gather(1, n.long().unsqueeze(1))
             e_tokens += int(n.sum()) + B
         el = time.perf_counter() - t0
-        tt = torch.tensor([el, e_tokens], dtype=torch.float64, device=dev)
+        tt = torch.tensor([el], dtype=torch.float64, device=dev)
         if world > 1:
-            mx = tt.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            sm = tt.clone()
-            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-            el, e_tokens = float(mx[0]), float(sm[1])
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            el = float(tt[0])
         e2e = {"value": e_tokens / el, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
                "d2h_bytes_per_step": engine.tokens.numel() * 8 + 4 * B}
 
@@ -394,9 +398,9 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         line = {
             "metric": METRIC.format(B=B, n=world), "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
-            "config": {"workload": _workload(a), "global_batch": B * world, "seq_len": P,
-                       "parallelism": "tp1" if world == 1 else f"tp1 x {world} replicas",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": _workload(a), "global_batch": B, "seq_len": P,
+                       "parallelism": f"tp{world}",
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
                        "mode": a.mode, "target_layers": tshape.n_layers,
                        "draft_layers": 0 if a.mode == "eagle" else dshape.n_layers},

@@ -136,6 +136,10 @@ int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res,
                          tsds_stream_t stream);
 int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out,
                        int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+/* out[m][j] = acc as fp32 (no rounding): a tensor-parallel rank's partial of
+ * a row-parallel projection, summed across ranks before the residual add. */
+int tsds_linear_f32(const void* x, int ldx, const void* W, float* out, int ldo, int M, int n_out,
+                    int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 /* out = bf16(bf16(acc) + bias[j]): the EAGLE head's fc (eagle_head.py:80). */
 int tsds_linear_bias(const void* x, int ldx, const void* W, const void* bias, void* out, int ldo,
                      int M, int n_out, int K, void* workspace, size_t workspace_bytes,
@@ -196,7 +200,7 @@ int tsds_verify_attention_noalloc_status(int32_t* host_status);
 /* ---------------------------------------------------------------------------
  * LM head + greedy pick: logits[m][v] = bf16(sum_k x[m][k] * W[v][k]);
  * argmax_out[m * argmax_stride] = lowest index of the largest bf16 logit
- * (torch.argmax semantics).
+ * (torch.argmax semantics); argmax_val[m] (optional) = that logit.
  * x is the final-normed hidden state.  logits_out may be NULL.
  * Replaces the LM head + argmax of qwen_model.py:192,205 and
  * eagle_head.py:120-121.
@@ -205,8 +209,8 @@ int tsds_verify_attention_noalloc_status(int32_t* host_status);
  * the GEMV limit (zero-fill a fresh workspace once, as for tsds_linear). */
 size_t tsds_lm_head_workspace_bytes(int M, int vocab);
 int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
-                        int argmax_stride, int M, int vocab, int K, void* workspace,
-                        size_t workspace_bytes, tsds_stream_t stream);
+                        int argmax_stride, float* argmax_val, int M, int vocab, int K,
+                        void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Greedy acceptance + KV commit for one chain cycle (replaces the verify /
@@ -226,6 +230,21 @@ int tsds_accept_greedy(const int64_t* draft, const int64_t* target, int32_t* acc
  * draft's first-step input ids2[b] = last[b], cur[b]. */
 int tsds_gather_ids(const int64_t* cur, const int64_t* last, const int64_t* draft, int64_t* verify_ids,
                     int64_t* draft_ids2, int B, int K, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel glue (one process per GPU; the collectives themselves are
+ * NCCL's, issued by the host between these calls).
+ * tsds_residual_add_f32: x = bf16(x + bf16(partial)) for the all-reduced
+ *   fp32 partial of a row-parallel projection (qwen_model.py:133-134,143-144).
+ * tsds_argmax_merge: per row, the best of tp per-rank (value, local index)
+ *   candidates, index offset r * vocab_shard, ties -> lowest global index.
+ * tsds_gather_shards: vocab-sharded logits [tp][M][vocab_shard] -> [M][V].
+ */
+int tsds_residual_add_f32(void* x, const float* partial, int M, int N, tsds_stream_t stream);
+int tsds_argmax_merge(const float* vals, const int64_t* idx, int M, int tp, int64_t vocab_shard,
+                      int64_t* out, int out_stride, tsds_stream_t stream);
+int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shard,
+                       tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Tree speculative decoding (EAGLE draft tree, verified in one target pass).

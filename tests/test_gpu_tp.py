@@ -1,0 +1,93 @@
+"""Tensor parallelism on 2 GPUs (NCCL): the TP=2 verify forward vs the
+oracle, and greedy speculative decoding == greedy autoregressive decoding
+under TP=2.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import qwen as oq
+
+pytestmark = pytest.mark.gpu
+SMALL = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=2, vocab=1000)
+
+
+def _worker(rank, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120))
+    try:
+        from tri_sds_b200 import ops
+        from tri_sds_b200.engine import AutoregressiveEngine, SpecEngine
+        from tri_sds_b200.model import QwenModel
+        from tri_sds_b200.shapes import QwenShape
+        from tri_sds_b200.tp import Comm
+        ops.set_gemv_max_rows(0)
+        dev = torch.device("cuda", rank)
+        comm = Comm()
+        oshape = oq.QwenShape(**SMALL)
+        shape = QwenShape(**SMALL)
+        w = oq.random_qwen_weights(oshape, seed=1, std=0.02)
+        B, P, T = 2, 12, 5
+        g = torch.Generator().manual_seed(2)
+        prompt = torch.randint(0, oshape.vocab, (B, P), generator=g)
+        step = torch.randint(0, oshape.vocab, (B, T), generator=g)
+        m = QwenModel(shape, B, 128, B * T, device=dev, weights=w, tp_rank=rank, tp_size=2, comm=comm)
+        m.prefill(prompt)
+        logits = torch.zeros(B * T, oshape.vocab, dtype=torch.bfloat16, device=dev)
+        am = torch.zeros(B * T, dtype=torch.int64, device=dev)
+        m.forward_plan(step.to(dev), 1, B, T, m.lengths, 0, am, 1, logits_out=logits).run()
+        torch.cuda.synchronize()
+        out = {"logits": logits.cpu(), "am": am.cpu()}
+        # greedy spec (target TP=2, draft replicated) vs greedy autoregressive (TP=2), CUDA graphs on
+        wt = oq.random_qwen_weights(oshape, seed=3, std=0.08)
+        wd = {**wt, "layers": wt["layers"][:1]}
+        dshape = QwenShape(**{**SMALL, "n_layers": 1})
+        K = 4
+        tgt = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        drf = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_size=2, tp_layers=False, tp_vocab=False)
+        spec, _ = SpecEngine(tgt, drf, K).generate(prompt, 16)
+        tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
+        out.update(spec=spec, ar=ar)
+        q.put((rank, out))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_verify_and_lossless_spec():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in (0, 1):
+        assert isinstance(res[r], dict), res[r]
+    # both ranks hold identical results
+    assert torch.equal(res[0]["logits"], res[1]["logits"]) and torch.equal(res[0]["spec"], res[1]["spec"])
+    oshape = oq.QwenShape(**SMALL)
+    w = oq.random_qwen_weights(oshape, seed=1, std=0.02)
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, oshape.vocab, (2, 12), generator=g)
+    step = torch.randint(0, oshape.vocab, (2, 5), generator=g)
+    ora = oq.QwenOracle(oshape, w, batch=2, max_seq=128)
+    ora.forward(prompt)
+    ora.lengths[:] = 12
+    ref, _ = ora.forward(step)
+    got = res[0]["logits"].float().reshape(2, 5, -1)
+    assert (got - ref.float()).abs().max().item() <= 2e-2
+    assert torch.equal(res[0]["am"], res[0]["logits"].float().argmax(-1))
+    assert torch.equal(res[0]["spec"], res[0]["ar"])

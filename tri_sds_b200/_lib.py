@@ -50,7 +50,11 @@ SIGNATURES = {
     "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_verify_attention_noalloc_status": (_I, [_P]),
     "tsds_lm_head_workspace_bytes": (_Z, [_I, _I]),
-    "tsds_lm_head_argmax": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_lm_head_argmax": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I, _I, _P, _Z, _P]),
+    "tsds_linear_f32": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_residual_add_f32": (_I, [_P, _P, _I, _I, _P]),
+    "tsds_argmax_merge": (_I, [_P, _P, _I, _I, ctypes.c_int64, _P, _I, _P]),
+    "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
     "tsds_accept_greedy": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "tsds_gather_ids": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
 }

@@ -127,7 +127,7 @@ struct Smem {
 // Final epilogue for 16 accumulator columns m0..m0+15 of tile row r.
 __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t, int r, int m0, const float (&v)[16]) {
   const int eq = r >> 5, lane = r & 31;
-  if (p.epi == EPI_STORE || p.epi == EPI_RESIDUAL) {
+  if (p.epi == EPI_STORE || p.epi == EPI_RESIDUAL || p.epi == EPI_STORE_F32) {
     const int j = t * TILE_J + r;
     if (j < p.n_out) {
 #pragma unroll
@@ -135,7 +135,10 @@ __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t,
         const int m = m0 + jj;
         if (m < p.M) {
           const int64_t o = (int64_t)m * p.ldo + j;
-          p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[(int64_t)m * p.res_ld + j]) + rbf(v[jj]));
+          if (p.epi == EPI_STORE_F32)
+            reinterpret_cast<float*>(p.out)[o] = v[jj];  // unrounded partial (tensor-parallel shards)
+          else
+            p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[(int64_t)m * p.res_ld + j]) + rbf(v[jj]));
         }
       }
     }

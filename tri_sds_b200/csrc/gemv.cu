@@ -94,6 +94,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, i
       const int64_t o = (int64_t)m * ldo + j;
       if (EPI == EPI_STORE) {
         out[o] = f2bf(sum[r][m]);
+      } else if (EPI == EPI_STORE_F32) {
+        reinterpret_cast<float*>(out)[o] = sum[r][m];
       } else if (EPI == EPI_RESIDUAL) {
         out[o] = f2bf(bf2f(res[(int64_t)m * res_ld + j]) + rbf(sum[r][m]));
       } else {  // SWIGLU: silu on the bf16 gate, product of bf16 values (qwen_model.py:139-142)
@@ -114,7 +116,8 @@ int launch_gemv_rows(const bf16* x, int ldx, const bf16* W, const bf16* res, int
     const int mt = M - m0 < 8 ? M - m0 : 8;
     const bf16* xs = x + (int64_t)m0 * ldx;
     const bf16* rs = res ? res + (int64_t)m0 * res_ld : nullptr;
-    bf16* os = out + (int64_t)m0 * ldo;
+    bf16* os = EPI == EPI_STORE_F32 ? reinterpret_cast<bf16*>(reinterpret_cast<float*>(out) + (int64_t)m0 * ldo)
+                                    : out + (int64_t)m0 * ldo;
 #define TSDS_GEMV_CASE(MTV)                                                                          \
   case MTV: {                                                                                        \
     constexpr int R = GemvCfg<MTV>::R;                                                               \
@@ -149,6 +152,8 @@ int tsds_gemv_dispatch(int epi, const bf16* x, int ldx, const bf16* W, const bf1
     case EPI_STORE: return launch_gemv_rows<EPI_STORE>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
     case EPI_RESIDUAL: return launch_gemv_rows<EPI_RESIDUAL>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
     case EPI_SWIGLU: return launch_gemv_rows<EPI_SWIGLU>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
+    case EPI_STORE_F32:
+      return launch_gemv_rows<EPI_STORE_F32>(x, ldx, W, res, res_ld, out, ldo, M, n_out, K, stream);
   }
   return TSDS_E_INVALID;
 }

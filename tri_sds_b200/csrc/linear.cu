@@ -23,9 +23,10 @@ int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, 
   for (int m0 = 0; m0 < M; m0 += 256) {  // rows beyond 256 (prefill-sized) in chunks
     const int mc = M - m0 < 256 ? M - m0 : 256;
     const bf16* res_c = res ? (const bf16*)res + (int64_t)m0 * res_ld : nullptr;
-    int st = tsds_tc_gemm(epi, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, w_rows, res_c, res_ld,
-                          (bf16*)out + (int64_t)m0 * ldo, ldo, mc, n_out, K, workspace, workspace_bytes, nullptr,
-                          nullptr, 0, stream);
+    bf16* out_c = epi == EPI_STORE_F32 ? reinterpret_cast<bf16*>((float*)out + (int64_t)m0 * ldo)
+                                       : (bf16*)out + (int64_t)m0 * ldo;
+    int st = tsds_tc_gemm(epi, (const bf16*)x + (int64_t)m0 * ldx, ldx, (const bf16*)W, w_rows, res_c, res_ld, out_c,
+                          ldo, mc, n_out, K, workspace, workspace_bytes, nullptr, nullptr, 0, stream);
     if (st != TSDS_OK) return st;
   }
   return TSDS_OK;
@@ -66,6 +67,13 @@ extern "C" int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* o
   int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
   if (st != TSDS_OK) return st;
   return run_linear(EPI_SWIGLU, x, ldx, W, nullptr, 0, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tsds_linear_f32(const void* x, int ldx, const void* W, float* out, int ldo, int M, int n_out, int K,
+                               void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
+  int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
+  if (st != TSDS_OK) return st;
+  return run_linear(EPI_STORE_F32, x, ldx, W, nullptr, 0, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
 }
 
 extern "C" int tsds_linear_bias(const void* x, int ldx, const void* W, const void* bias, void* out, int ldo, int M,

@@ -2,7 +2,7 @@
 #pragma once
 #include "common.cuh"
 
-enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_STORE_F32 = 4 };
 
 // CUDA-core GEMV, any M (processed 8 rows per launch).
 // res[m * res_ld + j] is the residual (res_ld = 0: a bias broadcast over rows).

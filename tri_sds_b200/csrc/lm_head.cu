@@ -101,7 +101,8 @@ __global__ void __launch_bounds__(256) lm_head_pass1(const bf16* __restrict__ x,
 
 __global__ void __launch_bounds__(256) lm_head_pass2(const float* __restrict__ cand_val,
                                                      const int* __restrict__ cand_idx, int ncand, int ldc,
-                                                     int64_t* __restrict__ out, int out_stride) {
+                                                     int64_t* __restrict__ out, int out_stride,
+                                                     float* __restrict__ out_val) {
   __shared__ float s_val[256];
   __shared__ int s_idx[256];
   pdl_wait();
@@ -128,7 +129,10 @@ __global__ void __launch_bounds__(256) lm_head_pass2(const float* __restrict__ c
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) out[(int64_t)m * out_stride] = s_idx[0] == 0x7fffffff ? 0 : s_idx[0];
+  if (threadIdx.x == 0) {
+    out[(int64_t)m * out_stride] = s_idx[0] == 0x7fffffff ? 0 : s_idx[0];
+    if (out_val) out_val[m] = s_val[0];
+  }
 }
 
 int lm_blocks(int mt, int vocab) {
@@ -160,8 +164,8 @@ extern "C" size_t tsds_lm_head_workspace_bytes(int M, int vocab) {
 }
 
 extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out, int64_t* argmax_out,
-                                   int argmax_stride, int M, int vocab, int K, void* workspace, size_t workspace_bytes,
-                                   tsds_stream_t stream) {
+                                   int argmax_stride, float* argmax_val, int M, int vocab, int K, void* workspace,
+                                   size_t workspace_bytes, tsds_stream_t stream) {
   TSDS_RETURN_IF(!x || !W || !argmax_out || M <= 0 || vocab <= 0 || K <= 0 || (K % 8) || ldx < K ||
                      argmax_stride <= 0,
                  TSDS_E_INVALID);
@@ -182,7 +186,7 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
       if (st != TSDS_OK) return st;
       tsds_launch(lm_head_pass2, dim3(mc), dim3(256), 0, stream, (const float*)(cval + (int64_t)m0 * ldc),
                   (const int*)(cidx + (int64_t)m0 * ldc), tiles, ldc, argmax_out + (int64_t)m0 * argmax_stride,
-                  argmax_stride);
+                  argmax_stride, argmax_val ? argmax_val + m0 : (float*)nullptr);
       st = tsds_launch_status();
       if (st != TSDS_OK) return st;
     }
@@ -214,7 +218,8 @@ extern "C" int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* 
     int st = tsds_launch_status();
     if (st != TSDS_OK) return st;
     tsds_launch(lm_head_pass2, dim3(mt), dim3(256), 0, stream, (const float*)cv, (const int*)ci, nb, ldc,
-                argmax_out + (int64_t)m0 * argmax_stride, argmax_stride);
+                argmax_out + (int64_t)m0 * argmax_stride, argmax_stride,
+                argmax_val ? argmax_val + m0 : (float*)nullptr);
     st = tsds_launch_status();
     if (st != TSDS_OK) return st;
   }

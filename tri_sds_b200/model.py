@@ -24,8 +24,11 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
+from dataclasses import replace
+
 from . import _lib
 from .shapes import QwenShape
+from .tp import LocalComm, local_dims, shard_layer, vocab_shard
 
 _VP = ctypes.c_void_p
 
@@ -80,11 +83,16 @@ def random_layer_gpu(shape: QwenShape, gen: torch.Generator, device, std=0.02, g
 
 @dataclass
 class Plan:
-    """A bound sequence of C-ABI calls; ``run`` appends the stream."""
+    """A bound sequence of C-ABI calls (``run`` appends the stream) and, for
+    tensor parallelism, collective steps (Python callables on the current
+    stream)."""
     calls: list = field(default_factory=list)
 
     def add(self, name: str, *args):
         self.calls.append((name, getattr(_lib.load(), name), args))
+
+    def add_py(self, name: str, fn):
+        self.calls.append((name, None, fn))
 
     def extend(self, other: "Plan"):
         self.calls.extend(other.calls)
@@ -93,12 +101,15 @@ class Plan:
         s = _VP(torch.cuda.current_stream().cuda_stream if stream is None else stream)
         lib = _lib.load()
         for name, fn, args in self.calls:
+            if fn is None:
+                args()
+                continue
             st = fn(*args, s)
             if st != 0:
                 raise RuntimeError(f"{name} failed: status {st} ({lib.tsds_status_string(st).decode()})")
 
     def kernel_count(self) -> int:
-        return len(self.calls)
+        return sum(1 for c in self.calls if c[1] is not None)
 
 
 class QwenModel:
@@ -109,8 +120,18 @@ class QwenModel:
 
     def __init__(self, shape: QwenShape, batch: int, max_seq: int, max_rows: int, device="cuda",
                  weights: dict | None = None, seed: int = 0, split_keys: int = 256, qk_norm: bool | None = None,
-                 share_embeddings: "QwenModel | None" = None, rope_len: int | None = None):
+                 share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
+                 tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None):
         self.shape = shape
+        # tensor parallelism: layers and/or vocabulary sharded over tp_size ranks
+        self.tp_rank = tp_rank
+        self.layer_tp = tp_size if tp_layers else 1
+        self.vocab_tp = share_embeddings.vocab_tp if share_embeddings is not None else (tp_size if tp_vocab else 1)
+        if comm is None:
+            comm = share_embeddings.comm if share_embeddings is not None else LocalComm()
+        self.comm = comm
+        self.lshape = replace(shape, **local_dims(shape, self.layer_tp)) if self.layer_tp > 1 else shape
+        self.vocab_local = shape.vocab // self.vocab_tp
         self.batch = batch
         self.max_seq = max_seq
         self.max_rows = max_rows
@@ -118,32 +139,41 @@ class QwenModel:
         self.split_keys = split_keys
         self.qk_norm = shape.qk_norm if qk_norm is None else qk_norm
         s = shape
+        ls = self.lshape
         dev = self.device
         if weights is not None:
-            self.layers = [pack_layer(L, dev) for L in weights["layers"]]
+            self.layers = [pack_layer(shard_layer(L, s, tp_rank, self.layer_tp), dev) for L in weights["layers"]]
         else:
             gen = torch.Generator(device=dev)
-            gen.manual_seed(seed)
-            self.layers = [random_layer_gpu(s, gen, dev) for _ in range(s.n_layers)]
+            gen.manual_seed(seed)   # replicated tensors: the same on every rank
+            lgen = torch.Generator(device=dev)
+            lgen.manual_seed(seed + 7919 * (1 + tp_rank) if self.layer_tp > 1 else seed + 1)
+            self.layers = [random_layer_gpu(ls, lgen, dev) for _ in range(s.n_layers)]
         if share_embeddings is not None:
             # the EAGLE head runs on the target's embedding, final norm and LM head
             self.embed_w, self.lm_head_w, self.norm_w = (share_embeddings.embed_w, share_embeddings.lm_head_w,
                                                          share_embeddings.norm_w)
         elif weights is not None:
             self.embed_w = weights["embed"].to(dev, torch.bfloat16).contiguous()
-            self.lm_head_w = (self.embed_w if weights["lm_head"] is weights["embed"]
-                              else weights["lm_head"].to(dev, torch.bfloat16).contiguous())
+            lm = self.embed_w if weights["lm_head"] is weights["embed"] else weights["lm_head"].to(dev, torch.bfloat16)
+            self.lm_head_w = vocab_shard(lm, tp_rank, self.vocab_tp) if self.vocab_tp > 1 else lm.contiguous()
             self.norm_w = weights["norm"].to(dev, torch.bfloat16).contiguous()
         else:
             self.embed_w = (torch.randn(s.vocab, s.hidden, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
-            self.lm_head_w = self.embed_w if s.tie_embeddings else \
-                (torch.randn(s.vocab, s.hidden, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+            if s.tie_embeddings:
+                self.lm_head_w = vocab_shard(self.embed_w, tp_rank, self.vocab_tp) if self.vocab_tp > 1 \
+                    else self.embed_w
+            else:
+                vgen = torch.Generator(device=dev)
+                vgen.manual_seed(seed + 104729 * (1 + tp_rank))
+                self.lm_head_w = (torch.randn(self.vocab_local, s.hidden, device=dev, generator=vgen) * 0.02
+                                  ).to(torch.bfloat16)
             self.norm_w = (1.0 + 0.02 * torch.randn(s.hidden, device=dev, generator=gen)).to(torch.bfloat16)
         # RoPE tables cover absolute positions (the EAGLE head's small cache
         # holds rows of a tree whose positions continue the sequence)
         self.rope_len = max_seq if rope_len is None else rope_len
         self.cos, self.sin = precompute_rope(s.head_dim, self.rope_len, s.rope_theta, dev)
-        self.k_cache = torch.zeros(s.n_layers, batch, s.n_kv_heads, max_seq, s.head_dim, dtype=torch.bfloat16,
+        self.k_cache = torch.zeros(s.n_layers, batch, ls.n_kv_heads, max_seq, s.head_dim, dtype=torch.bfloat16,
                                    device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)   # committed rows per sequence
@@ -151,25 +181,35 @@ class QwenModel:
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.x = torch.zeros(M, s.hidden, **bf)          # residual stream
         self.xn = torch.zeros(M, s.hidden, **bf)         # normed input of a projection
-        self.qkv = torch.zeros(M, s.qkv_dim, **bf)
-        self.q = torch.zeros(M, s.q_dim, **bf)
-        self.attn = torch.zeros(M, s.q_dim, **bf)
-        self.h = torch.zeros(M, s.intermediate, **bf)
+        self.qkv = torch.zeros(M, ls.qkv_dim, **bf)
+        self.q = torch.zeros(M, ls.q_dim, **bf)
+        self.attn = torch.zeros(M, ls.q_dim, **bf)
+        self.h = torch.zeros(M, ls.intermediate, **bf)
+        if self.layer_tp > 1:
+            self.part = torch.zeros(M, s.hidden, dtype=torch.float32, device=dev)   # row-parallel partials
+        if self.vocab_tp > 1:
+            tpv = self.vocab_tp
+            self.am_idx = torch.zeros(M, dtype=torch.int64, device=dev)
+            self.am_val = torch.zeros(M, dtype=torch.float32, device=dev)
+            self.am_idx_all = torch.zeros(tpv * M, dtype=torch.int64, device=dev)
+            self.am_val_all = torch.zeros(tpv * M, dtype=torch.float32, device=dev)
+            self.logits_local = None   # allocated on first use with full logits
         self.starts = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(M, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         T_max = max(1, M // batch)
         self.attn_ws_bytes = max(
-            _lib.query("tsds_attention_workspace_bytes", batch, t, s.n_heads, s.n_kv_heads, s.head_dim, max_seq,
+            _lib.query("tsds_attention_workspace_bytes", batch, t, ls.n_heads, ls.n_kv_heads, s.head_dim, max_seq,
                        split_keys) for t in range(1, T_max + 1))
         self.attn_ws = torch.empty(max(self.attn_ws_bytes, 16), dtype=torch.uint8, device=dev)
-        lin = [(s.qkv_dim, s.hidden), (s.hidden, s.q_dim), (s.intermediate, s.hidden), (s.hidden, s.intermediate)]
+        lin = [(ls.qkv_dim, s.hidden), (s.hidden, ls.q_dim), (ls.intermediate, s.hidden), (s.hidden, ls.intermediate)]
         self.lin_ws_bytes = max(_lib.query("tsds_linear_workspace_bytes", m, o, k) for o, k in lin
                                 for m in range(1, M + 1))
         # zero-filled once: the tcgen05 tile counters live in these and every
         # launch leaves them zero again
         self.lin_ws = torch.zeros(max(self.lin_ws_bytes, 16), dtype=torch.uint8, device=dev)
-        self.lm_ws_bytes = max(_lib.query("tsds_lm_head_workspace_bytes", m, s.vocab) for m in range(1, M + 1))
+        self.lm_ws_bytes = max(_lib.query("tsds_lm_head_workspace_bytes", m, self.vocab_local)
+                               for m in range(1, M + 1))
         self.lm_ws = torch.zeros(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
 
     # -- launch plans ---------------------------------------------------------
@@ -179,8 +219,10 @@ class QwenModel:
         """All decoder layers over rows x[0:B*T] (embedded already), with
         starts/positions already prepared.  ``x`` / ``starts`` /
         ``positions`` default to the model's own buffers; ``tree_mask`` +
-        ``mask_origin`` select the attention mask (see tsds_verify_attention)."""
-        s = self.shape
+        ``mask_origin`` select the attention mask (see tsds_verify_attention).
+        Under tensor parallelism the O and down projections produce fp32
+        partials that are all-reduced before the residual add."""
+        s, ls = self.shape, self.lshape
         M = B * T
         assert M <= self.max_rows and B == self.batch
         eps = s.eps
@@ -190,40 +232,73 @@ class QwenModel:
         xb = self.x if x is None else x
         st = self.starts if starts is None else starts
         ps = self.positions if positions is None else positions
+        tp = self.layer_tp > 1
+
+        def row_parallel(src, ld_src, w, k_in):
+            if not tp:
+                pl.add("tsds_linear_residual", _p(src), ld_src, _p(w), _p(xb), _p(xb), s.hidden, M, s.hidden, k_in,
+                       _p(lw), lb)
+                return
+            part = self.part[:M]
+            pl.add("tsds_linear_f32", _p(src), ld_src, _p(w), _p(part), s.hidden, M, s.hidden, k_in, _p(lw), lb)
+            pl.add_py("all_reduce", lambda part=part: self.comm.all_reduce(part))
+            pl.add("tsds_residual_add_f32", _p(xb), _p(part), M, s.hidden)
+
         for i, L in enumerate(self.layers):
             kc, vc = self.k_cache[i], self.v_cache[i]
             pl.add("tsds_rms_norm", _p(xb), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
-            pl.add("tsds_linear", _p(self.xn), s.hidden, _p(L.w_qkv), _p(self.qkv), s.qkv_dim, M, s.qkv_dim,
+            pl.add("tsds_linear", _p(self.xn), s.hidden, _p(L.w_qkv), _p(self.qkv), ls.qkv_dim, M, ls.qkv_dim,
                    s.hidden, _p(lw), lb)
             pl.add("tsds_qk_norm_rope_kv", _p(self.qkv), _p(L.q_norm) if qn else None,
                    _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(ps), _p(st),
-                   _p(self.q), _p(kc), _p(vc), B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq, self.rope_len,
-                   eps)
+                   _p(self.q), _p(kc), _p(vc), B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
+                   self.rope_len, eps)
             pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(st),
-                   _p(tree_mask), mask_origin, B, T, s.n_heads, s.n_kv_heads, s.head_dim, self.max_seq,
+                   _p(tree_mask), mask_origin, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
                    self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
                    _p(self.status))
-            pl.add("tsds_linear_residual", _p(self.attn), s.q_dim, _p(L.w_o), _p(xb), _p(xb), s.hidden, M,
-                   s.hidden, s.q_dim, _p(lw), lb)
+            row_parallel(self.attn, ls.q_dim, L.w_o, ls.q_dim)
             pl.add("tsds_rms_norm", _p(xb), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
-            pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), s.intermediate, M,
-                   s.intermediate, s.hidden, _p(lw), lb)
-            pl.add("tsds_linear_residual", _p(self.h), s.intermediate, _p(L.w_d), _p(xb), _p(xb), s.hidden,
-                   M, s.hidden, s.intermediate, _p(lw), lb)
+            pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), ls.intermediate, M,
+                   ls.intermediate, s.hidden, _p(lw), lb)
+            row_parallel(self.h, ls.intermediate, L.w_d, ls.intermediate)
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,
                   logits_out: torch.Tensor | None = None, x: torch.Tensor | None = None) -> Plan:
         """Final RMSNorm + LM head + argmax over all rows, or only the last
-        row of each sequence."""
+        row of each sequence.  With a vocab-parallel LM head each rank picks
+        its shard's best (value, index), the candidates are all-gathered and
+        merged (ties: lowest global index); full logits, when requested, are
+        all-gathered and reassembled."""
         s = self.shape
         pl = Plan()
         xb = self.x if x is None else x
         rows, ld = (B, T * s.hidden) if last_only else (B * T, s.hidden)
         src = xb[T - 1:] if last_only else xb
         pl.add("tsds_rms_norm", _p(src), _p(self.norm_w), _p(self.xn), rows, s.hidden, ld, s.hidden, s.eps)
-        pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(logits_out), _p(argmax_out),
-               argmax_stride, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
+        if self.vocab_tp == 1:
+            pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(logits_out), _p(argmax_out),
+                   argmax_stride, None, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
+            return pl
+        tpv, vl = self.vocab_tp, self.vocab_local
+        loc = None
+        if logits_out is not None:
+            need = rows * vl
+            if self.logits_local is None or self.logits_local.numel() < need:
+                self.logits_local = torch.zeros(self.max_rows * vl, dtype=torch.bfloat16, device=self.device)
+                self.logits_all = torch.zeros(tpv * self.max_rows * vl, dtype=torch.bfloat16, device=self.device)
+            loc = self.logits_local[:need]
+        pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(loc), _p(self.am_idx), 1,
+               _p(self.am_val), rows, vl, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
+        vi, vv = self.am_idx[:rows], self.am_val[:rows]
+        ai, av = self.am_idx_all[:tpv * rows], self.am_val_all[:tpv * rows]
+        pl.add_py("all_gather", lambda: (self.comm.all_gather(ai, vi), self.comm.all_gather(av, vv)))
+        pl.add("tsds_argmax_merge", _p(av), _p(ai), rows, tpv, vl, _p(argmax_out), argmax_stride)
+        if logits_out is not None:
+            allb = self.logits_all[:tpv * rows * vl]
+            pl.add_py("all_gather", lambda: self.comm.all_gather(allb, loc))
+            pl.add("tsds_gather_shards", _p(allb), _p(logits_out), tpv, rows, vl)
         return pl
 
     def forward_plan(self, ids: torch.Tensor, ids_stride: int, B: int, T: int, base: torch.Tensor, offset: int,
@@ -244,7 +319,7 @@ class QwenModel:
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
         """Process a [B, P] prompt from row 0; returns the hidden states
         [B, P, N] (pre final norm) and sets lengths = P."""
-        s = self.shape
+        s, ls = self.shape, self.lshape
         B, P = prompt.shape
         dev = self.device
         prompt = prompt.to(dev)
@@ -252,23 +327,32 @@ class QwenModel:
         pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(B)
         starts = torch.zeros(B, dtype=torch.int32, device=dev)
         from . import ops
-        q = torch.empty(B * P, s.q_dim, dtype=torch.bfloat16, device=dev)
+        q = torch.empty(B * P, ls.q_dim, dtype=torch.bfloat16, device=dev)
+
+        def row_parallel(inp, w):
+            y = inp @ w.T
+            if self.layer_tp > 1:
+                y = y.float()
+                self.comm.all_reduce(y)
+                y = y.to(torch.bfloat16)
+            return y
+
         for i, L in enumerate(self.layers):
             xn = ops.rms_norm(x, L.ln1, s.eps)
             qkv = xn @ L.w_qkv.T
             ops.qk_norm_rope_kv(qkv, L.q_norm if self.qk_norm else None, L.k_norm if self.qk_norm else None,
                                 self.cos, self.sin, pos, starts, q, self.k_cache[i], self.v_cache[i], B, P,
-                                s.n_heads, s.n_kv_heads, s.eps)
-            qh = q.reshape(B, P, s.n_heads, s.head_dim).transpose(1, 2)
+                                ls.n_heads, ls.n_kv_heads, s.eps)
+            qh = q.reshape(B, P, ls.n_heads, s.head_dim).transpose(1, 2)
             kh = self.k_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
             vh = self.v_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
             a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True)
-            a = a.transpose(1, 2).reshape(B * P, s.q_dim)
-            x = x + a @ L.w_o.T
+            a = a.transpose(1, 2).reshape(B * P, ls.q_dim)
+            x = x + row_parallel(a, L.w_o)
             xn = ops.rms_norm(x, L.ln2, s.eps)
             gu = xn @ L.w_gu.T
-            h = F.silu(gu[:, :s.intermediate]) * gu[:, s.intermediate:]
-            x = x + h @ L.w_d.T
+            h = F.silu(gu[:, :ls.intermediate]) * gu[:, ls.intermediate:]
+            x = x + row_parallel(h, L.w_d)
         self.lengths.fill_(P)
         return x.reshape(B, P, s.hidden)
 
@@ -276,7 +360,12 @@ class QwenModel:
         """Final norm + full bf16 logits (set-up / tests only)."""
         from . import ops
         xn = ops.rms_norm(hidden.reshape(-1, self.shape.hidden).contiguous(), self.norm_w, self.shape.eps)
-        return xn @ self.lm_head_w.T
+        loc = xn @ self.lm_head_w.T
+        if self.vocab_tp == 1:
+            return loc
+        allv = torch.empty(self.vocab_tp * loc.numel(), dtype=loc.dtype, device=loc.device)
+        self.comm.all_gather(allv, loc.contiguous().reshape(-1))
+        return allv.reshape(self.vocab_tp, *loc.shape).permute(1, 0, 2).reshape(loc.shape[0], -1)
 
     def check_status(self):
         st = int(self.status.item())

@@ -243,7 +243,7 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, return_logits: bool = False
     logits = torch.empty(M, V, dtype=torch.bfloat16, device=x.device) if return_logits else None
     nb = _lib.query("tsds_lm_head_workspace_bytes", M, V)
     ws = _scratch.get(nb, x.device, "lm_head")
-    _lib.call("tsds_lm_head_argmax", _p(x), x.stride(0), _p(w), _p(logits), _p(out), out.stride(0), M, V, K,
+    _lib.call("tsds_lm_head_argmax", _p(x), x.stride(0), _p(w), _p(logits), _p(out), out.stride(0), None, M, V, K,
               _p(ws), nb, _stream())
     return (out, logits) if return_logits else out
 
