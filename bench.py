@@ -67,6 +67,8 @@ def _args():
 
 
 METRIC = "Qwen3-32B spec-decode tok/s at B={B} ({n} GPU); verify-step us"
+# (hidden, intermediate, rows) -> dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch
+MEASURED_TRAFFIC = {(5120, 25600, 26): 541.7e6}   # profiles/tc_gemm_gate_up_qwen3_32b_m26.md
 DATA = "synthetic: seeded uniform prompt ids, random-init N(0,0.02) weights (no checkpoint offline)"
 
 
@@ -358,6 +360,9 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     kbytes = target.layers[0].w_gu.numel() * 2 + xin.numel() * 2 + hout.numel() * 2
     peak, peak_kind = _peaks()
     achieved = kbytes / (kern_us * 1e-6) / 1e9
+    # DRAM read+write bytes per launch of this kernel at this shape, from the
+    # ncu capture summarised in profiles/ (None where no capture exists)
+    traffic = MEASURED_TRAFFIC.get((tshape.hidden, tshape.intermediate, M)) if world == 1 else None
 
     # ---- end to end through the worker API (host buffers) --------------------
     e2e = None
@@ -408,7 +413,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "accept_len_mean": float(acc.mean()),
             "roofline": {"bound": "hbm", "kernel": "tsds_linear_swiglu (target gate/up, M=%d)" % M,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": kbytes,
+                         "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": kbytes,
                          "launch_us": kern_us},
             "cpu_baseline": cpu,
             "e2e": e2e,
