@@ -3,7 +3,7 @@
 //   D[j][m] = sum_k W[j][k] * X[m][k]      (swap-AB: weight rows j fill the MMA's
 //                                            M = 128, token rows m are its N)
 //
-// * One CTA per SM.  The work (tiles of 128 weight rows x k-tiles of 64) is
+// * Persistent CTAs (two per SM by default).  The work (tiles of 128 weight rows x k-tiles of 64) is
 //   split stream-K style: CTA p owns the contiguous iteration range
 //   [W*p/P, W*(p+1)/P) of the flattened (tile, k-tile) space, so every SM
 //   streams the same number of weight bytes whatever the layer shape.
@@ -39,8 +39,8 @@ constexpr int SMEM_BUDGET = 220 * 1024;
 
 struct TcParams {
   int M, Npad, n_out, K, KT, tiles, P;
-  long long W;
-  int epi, up_off, ldo, res_ld;
+  uint32_t W;  // tiles x KT; the host guarantees W * P < 2^32
+  int up_off, ldo, res_ld;
   const bf16* res;
   bf16* out;
   float* ws;
@@ -97,11 +97,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // ---- stream-K bookkeeping ---------------------------------------------------
-__device__ __forceinline__ long long it_begin(int p, int P, long long W) { return (W * p) / P; }
+// 32-bit arithmetic: W * P < 2^32 is checked on the host.
+__device__ __forceinline__ int it_begin(int p, int P, uint32_t W) { return (int)(((uint32_t)p * W) / (uint32_t)P); }
 
 // CTA whose range holds iteration x
-__device__ __forceinline__ int owner_of(long long x, int P, long long W) {
-  int q = (int)((x * P) / W);
+__device__ __forceinline__ int owner_of(int x, int P, uint32_t W) {
+  int q = (int)(((uint32_t)x * (uint32_t)P) / W);
   if (q > P - 1) q = P - 1;
   while (q + 1 < P && it_begin(q + 1, P, W) <= x) ++q;
   while (q > 0 && it_begin(q, P, W) > x) --q;
@@ -125,24 +126,35 @@ struct Smem {
 };
 
 // Final epilogue for 16 accumulator columns m0..m0+15 of tile row r.
+template <int EPI>
 __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t, int r, int m0, const float (&v)[16]) {
   const int eq = r >> 5, lane = r & 31;
-  if (p.epi == EPI_STORE || p.epi == EPI_RESIDUAL || p.epi == EPI_STORE_F32) {
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32) {
     const int j = t * TILE_J + r;
     if (j < p.n_out) {
+      // The residual may be the output buffer itself (in-place x += ...):
+      // read all of it before the first store so the loads are not
+      // serialised behind the stores.
+      float rv[16];
+      if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) rv[jj] = m0 + jj < p.M ? bf2f(p.res[(int64_t)(m0 + jj) * p.res_ld + j]) : 0.f;
+      }
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
         const int m = m0 + jj;
         if (m < p.M) {
           const int64_t o = (int64_t)m * p.ldo + j;
-          if (p.epi == EPI_STORE_F32)
+          if constexpr (EPI == EPI_STORE_F32)
             reinterpret_cast<float*>(p.out)[o] = v[jj];  // unrounded partial (tensor-parallel shards)
+          else if constexpr (EPI == EPI_STORE)
+            p.out[o] = f2bf(v[jj]);
           else
-            p.out[o] = p.epi == EPI_STORE ? f2bf(v[jj]) : f2bf(bf2f(p.res[(int64_t)m * p.res_ld + j]) + rbf(v[jj]));
+            p.out[o] = f2bf(rv[jj] + rbf(v[jj]));
         }
       }
     }
-  } else if (p.epi == EPI_SWIGLU) {
+  } else if constexpr (EPI == EPI_SWIGLU) {
     if (r >= 64) {
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) sh.xch[r - 64][jj] = rbf(v[jj]);
@@ -199,14 +211,15 @@ __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t,
   }
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Smem sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pc = blockIdx.x;
-  const long long b = it_begin(pc, p.P, p.W), e = it_begin(pc + 1, p.P, p.W);
+  const int b = it_begin(pc, p.P, p.W), e = it_begin(pc + 1, p.P, p.W);
   const int KT = p.KT;
 
   if (threadIdx.x == 0) {
@@ -242,16 +255,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0 && b < e) {
       prefetch_tmap(&amap);
       prefetch_tmap(&bmap);
-      const int npre = (int)((e - b) < p.stages ? (e - b) : p.stages);
-      auto load_a = [&](long long it, int s) {
-        const int t = (int)(it / KT), kt = (int)(it % KT);
-        const int row0 = p.epi == EPI_SWIGLU ? t * 64 : t * TILE_J;
-        const int row1 = p.epi == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
+      const int npre = (e - b) < p.stages ? (e - b) : p.stages;
+      auto load_a = [&](int it, int s) {
+        const int t = it / KT, kt = it % KT;
+        const int row0 = EPI == EPI_SWIGLU ? t * 64 : t * TILE_J;
+        const int row1 = EPI == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
         tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
         tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
       };
-      auto load_b = [&](long long it, int s) {
-        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], (int)(it % KT) * BK, 0);
+      auto load_b = [&](int it, int s) {
+        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], (it % KT) * BK, 0);
       };
       for (int i = 0; i < npre; ++i) {
         mbar_arrive_expect_tx(&sh.full_bar[i], A_STAGE + p.b_stage_bytes);
@@ -260,7 +273,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       pdl_wait();
       for (int i = 0; i < npre; ++i) load_b(b + i, i);
       int i = npre;
-      for (long long it = b + npre; it < e; ++it, ++i) {
+      for (int it = b + npre; it < e; ++it, ++i) {
         const int s = i % p.stages, r = i / p.stages;
         if (!mbar_wait(&sh.empty_bar[s], (r - 1) & 1)) {
           atomicExch(p.status, TSDS_E_TIMEOUT);
@@ -281,7 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int i = 0, seg = 0;
       bool ok = true;
       for (int t = (int)(b / KT); ok && t <= (int)((e - 1) / KT); ++t, ++seg) {
-        const long long tb = (long long)t * KT;
+        const int tb = t * KT;
         const int k0 = (int)((b > tb ? b : tb) - tb);
         const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
         const int buf = seg & 1, use = seg >> 1;
@@ -323,7 +336,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int seg = 0;
     bool alive = b < e;
     for (int t = (int)(b / KT); alive && t <= (int)((e - 1) / KT); ++t, ++seg) {
-      const long long tb = (long long)t * KT;
+      const int tb = t * KT;
       const int k0 = (int)((b > tb ? b : tb) - tb);
       const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
       const int buf = seg & 1, use = seg >> 1;
@@ -343,16 +356,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const bool full = (k0 == 0 && k1 == KT);
       const uint32_t taddr = tmem + buf * p.tmem_cols + ((uint32_t)(eq * 32) << 16);
-      const int slot = (t == (int)(b / KT)) ? 0 : 1;
-      float* part = p.ws + ((size_t)(pc * 2 + slot) * p.Npad) * TILE_J;
+      // partial of a split tile: slot 0 = this CTA's first segment, 1 = its
+      // last; layout [Npad/4][TILE_J][4] - a thread moves 4 columns of its row
+      // per access and a warp's access covers 512 contiguous bytes
+      const int slot = (t == b / KT) ? 0 : 1;
+      float4* part = reinterpret_cast<float4*>(p.ws + ((size_t)(pc * 2 + slot) * p.Npad) * TILE_J) + r;
       for (int c = 0; c < nchunk; ++c) {
         float v[16];
         tmem_ld16(taddr + c * 16, v);
         if (full) {
-          finish_chunk(p, sh, t, r, c * 16, v);
+          finish_chunk<EPI>(p, sh, t, r, c * 16, v);
         } else {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) part[(size_t)(c * 16 + jj) * TILE_J + r] = v[jj];
+          for (int q4 = 0; q4 < 4; ++q4)
+            part[(size_t)(c * 4 + q4) * TILE_J] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
       }
       tc_fence_before();
@@ -367,17 +384,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         epi_bar();
         if (sh.last) {
           __threadfence();
+          // Partials are summed in CTA order (deterministic); the loads of up
+          // to FIX_Q contributors are issued together so the tail costs one
+          // L2 round trip per FIX_Q partials instead of one per partial.
+          // Contributors after q_lo start inside tile t (their slot 0); q_lo
+          // holds it in slot 1 unless its range starts exactly at the tile.
+          constexpr int FIX_Q = EPI == EPI_RESIDUAL ? 5 : 6;
+          const int nq = q_hi - q_lo + 1;
+          const int lo_slot = it_begin(q_lo, p.P, p.W) < tb ? 1 : 0;
           for (int c = 0; c < nchunk; ++c) {
             float v[16];
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
-            for (int q = q_lo; q <= q_hi; ++q) {
-              const int qs = (t == (int)(it_begin(q, p.P, p.W) / KT)) ? 0 : 1;
-              const float* src = p.ws + ((size_t)(q * 2 + qs) * p.Npad + c * 16) * TILE_J + r;
+            for (int q0 = 0; q0 < nq; q0 += FIX_Q) {
+              float tmp[FIX_Q][16];
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) v[jj] += __ldcg(src + (size_t)jj * TILE_J);
+              for (int i = 0; i < FIX_Q; ++i) {
+                if (q0 + i < nq) {
+                  const int q = q_lo + q0 + i;
+                  const int qs = q0 + i == 0 ? lo_slot : 0;
+                  const float4* src =
+                      reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                      (size_t)c * 4 * TILE_J + r;
+#pragma unroll
+                  for (int q4 = 0; q4 < 4; ++q4) {
+                    const float4 f = __ldcg(src + (size_t)q4 * TILE_J);
+                    tmp[i][4 * q4] = f.x;
+                    tmp[i][4 * q4 + 1] = f.y;
+                    tmp[i][4 * q4 + 2] = f.z;
+                    tmp[i][4 * q4 + 3] = f.w;
+                  }
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < FIX_Q; ++i) {
+                if (q0 + i < nq) {
+#pragma unroll
+                  for (int jj = 0; jj < 16; ++jj) v[jj] += tmp[i][jj];
+                }
+              }
             }
-            finish_chunk(p, sh, t, r, c * 16, v);
+            finish_chunk<EPI>(p, sh, t, r, c * 16, v);
           }
           if (r == 0) p.counters[t] = 0;  // ready for the next launch
         }
@@ -419,6 +466,19 @@ extern "C" void tsds_set_gemm_ctas_per_sm(int n) { g_ctas_per_sm = n < 1 ? 1 : (
 
 namespace {
 
+template <int EPI>
+int launch_tc(const CUtensorMap& amap, const CUtensorMap& bmap, const TcParams& p, size_t smem, cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET) !=
+        cudaSuccess)
+      return TSDS_E_LAUNCH;
+    attr = true;
+  }
+  tsds_launch(tc_gemm_kernel<EPI>, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
+  return tsds_launch_status();
+}
+
 int pow2_at_least(int x) {
   int v = 32;
   while (v < x) v <<= 1;
@@ -449,13 +509,15 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.KT = (K + BK - 1) / BK;
   p.tiles = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + TILE_J - 1) / TILE_J;
   TSDS_RETURN_IF(p.tiles > 2048, TSDS_E_UNSUPPORTED);
-  p.W = (long long)p.tiles * p.KT;
+  const long long W64 = (long long)p.tiles * p.KT;
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = g_ctas_per_sm;
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
   const long long slots = (long long)num_sms() * ctas;
-  p.P = (int)(p.W < slots ? p.W : slots);
-  p.epi = epi;
+  p.P = (int)(W64 < slots ? W64 : slots);
+  // the kernel's stream-K bookkeeping is 32-bit
+  TSDS_RETURN_IF(W64 * p.P >= (1ll << 32), TSDS_E_UNSUPPORTED);
+  p.W = (uint32_t)W64;
   p.up_off = n_out;
   p.ldo = ldo;
   p.res_ld = res_ld;
@@ -481,13 +543,12 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   st = tsds_make_tmap_2d_bf16(&bmap, x, K, M, (uint64_t)ldx * 2, BK, p.Npad, 1);
   if (st != TSDS_OK) return st;
   const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET) !=
-        cudaSuccess)
-      return TSDS_E_LAUNCH;
-    attr = true;
+  switch (epi) {
+    case EPI_STORE: return launch_tc<EPI_STORE>(amap, bmap, p, smem, stream);
+    case EPI_RESIDUAL: return launch_tc<EPI_RESIDUAL>(amap, bmap, p, smem, stream);
+    case EPI_SWIGLU: return launch_tc<EPI_SWIGLU>(amap, bmap, p, smem, stream);
+    case EPI_STORE_F32: return launch_tc<EPI_STORE_F32>(amap, bmap, p, smem, stream);
+    case EPI_ARGMAX: return launch_tc<EPI_ARGMAX>(amap, bmap, p, smem, stream);
+    default: return TSDS_E_INVALID;
   }
-  tsds_launch(tc_gemm_kernel, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
-  return tsds_launch_status();
 }
