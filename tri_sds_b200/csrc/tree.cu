@@ -25,25 +25,63 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { retur
 template <int K>
 __device__ __forceinline__ void insert_topk(float (&v)[K], int (&ix)[K], float x, int i) {
   if (!better(x, i, v[K - 1], ix[K - 1])) return;
-  int p = K - 1;
-  while (p > 0 && better(x, i, v[p - 1], ix[p - 1])) {
-    v[p] = v[p - 1];
-    ix[p] = ix[p - 1];
-    --p;
+  // insertion with static register indices (no local-memory array)
+#pragma unroll
+  for (int p = K - 1; p >= 0; --p) {
+    if (p > 0 && better(x, i, v[p - 1], ix[p - 1])) {
+      v[p] = v[p - 1];
+      ix[p] = ix[p - 1];
+    } else {
+      v[p] = x;
+      ix[p] = i;
+      break;
+    }
   }
-  v[p] = x;
-  ix[p] = i;
 }
 
+// online log-sum-exp state (m, s): sum = s * exp(m)
+__device__ __forceinline__ void lse_merge(float& m, float& s, float om, float os) {
+  const float nm = fmaxf(m, om);
+  if (nm == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+  m = nm;
+}
+
+constexpr int TOPK_THREADS = 512;
+constexpr int TOPK_WARPS = TOPK_THREADS / 32;
+constexpr int TOPK_UNROLL = 8;   // 16-byte loads in flight per thread
+
 template <int K>
-__global__ void __launch_bounds__(512) topk_lse_kernel(const bf16* __restrict__ logits, int ld, int V,
-                                                       float* __restrict__ vals, int* __restrict__ idx,
-                                                       float* __restrict__ lse) {
+__device__ __forceinline__ void topk_take8(float (&tv)[K], int (&ti)[K], float& m, float& s, uint4 q, int i0) {
+  const bf16* e = reinterpret_cast<const bf16*>(&q);
+  float x[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    x[j] = bf2f(e[j]);
+    mx = fmaxf(mx, x[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) insert_topk<K>(tv, ti, x[j], i0 + j);
+  if (mx == -INFINITY) return;
+  float t = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) t += __expf(x[j] - mx);
+  lse_merge(m, s, mx, t);
+}
+
+// One CTA of TOPK_THREADS threads per row.  Rows whose start is 16-byte aligned are
+// read as 16-byte vectors, TOPK_UNROLL of them in flight per thread; the
+// reductions run in a fixed order, so the result is deterministic.
+template <int K>
+__global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* __restrict__ logits, int ld, int V,
+                                                                float* __restrict__ vals, int* __restrict__ idx,
+                                                                float* __restrict__ lse) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float s_v[16][K];
-  __shared__ int s_i[16][K];
-  __shared__ float s_m[16], s_s[16];
+  __shared__ float s_v[TOPK_WARPS][K];
+  __shared__ int s_i[TOPK_WARPS][K];
+  __shared__ float s_m[TOPK_WARPS], s_s[TOPK_WARPS];
   const bf16* row = logits + (int64_t)blockIdx.x * ld;
   float tv[K];
   int ti[K];
@@ -53,32 +91,44 @@ __global__ void __launch_bounds__(512) topk_lse_kernel(const bf16* __restrict__ 
     ti[k] = 0x7fffffff;
   }
   float m = -INFINITY, s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = bf2f(row[i]);
-    insert_topk<K>(tv, ti, x, i);
-    if (x > m) {
-      s = s * expf(m - x) + 1.f;
-      m = x;
-    } else {
-      s += expf(x - m);
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  const int nvec = vec ? V / 8 : 0;
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  for (int base = threadIdx.x; base < nvec; base += TOPK_UNROLL * TOPK_THREADS) {
+    uint4 q[TOPK_UNROLL];
+#pragma unroll
+    for (int u = 0; u < TOPK_UNROLL; ++u) {
+      const int i = base + u * TOPK_THREADS;
+      if (i < nvec) q[u] = __ldg(rv + i);
+    }
+#pragma unroll
+    for (int u = 0; u < TOPK_UNROLL; ++u) {
+      const int i = base + u * TOPK_THREADS;
+      if (i < nvec) topk_take8<K>(tv, ti, m, s, q[u], 8 * i);
     }
   }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += TOPK_THREADS) {
+    const float x = bf2f(row[i]);
+    insert_topk<K>(tv, ti, x, i);
+    lse_merge(m, s, x, 1.f);
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // log-sum-exp across the warp, then across warps
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
-    const float nm = fmaxf(m, om);
-    s = (m == -INFINITY ? 0.f : s * expf(m - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
-    m = nm;
+    lse_merge(m, s, om, os);
   }
   // top-k across the warp: K rounds of "best head wins, its owner pops"
-  float wv[K];
-  int wi[K];
   int head = 0;
   for (int k = 0; k < K; ++k) {
-    float bv = head < K ? tv[head] : -INFINITY;
-    int bi = head < K ? ti[head] : 0x7fffffff;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+      if (j == head) {
+        bv = tv[j];
+        bi = ti[j];
+      }
     int owner = lane;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -91,43 +141,48 @@ __global__ void __launch_bounds__(512) topk_lse_kernel(const bf16* __restrict__ 
         owner = oo;
       }
     }
-    wv[k] = bv;
-    wi[k] = bi;
+    if (lane == 0) {
+      s_v[warp][k] = bv;
+      s_i[warp][k] = bi;
+    }
     if (owner == lane) ++head;
   }
   if (lane == 0) {
     s_m[warp] = m;
     s_s[warp] = s;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      s_v[warp][k] = wv[k];
-      s_i[warp][k] = wi[k];
-    }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int nw = blockDim.x >> 5;
-    float M = -INFINITY, S = 0.f;
-    for (int w = 0; w < nw; ++w) {
-      const float nm = fmaxf(M, s_m[w]);
-      S = (M == -INFINITY ? 0.f : S * expf(M - nm)) + (s_m[w] == -INFINITY ? 0.f : s_s[w] * expf(s_m[w] - nm));
-      M = nm;
+  if (warp == 0) {
+    // lse over the warps (fixed order: the shuffle tree)
+    float wm = lane < TOPK_WARPS ? s_m[lane] : -INFINITY, ws = lane < TOPK_WARPS ? s_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, wm, o), os = __shfl_xor_sync(0xffffffffu, ws, o);
+      lse_merge(wm, ws, om, os);
     }
-    lse[blockIdx.x] = M + logf(S);
-    int hp[16];
-    for (int w = 0; w < nw; ++w) hp[w] = 0;
+    if (lane == 0) lse[blockIdx.x] = wm + logf(ws);
+    // top-k over the warps' lists: lane w holds warp w's list
+    int hp = lane < TOPK_WARPS ? 0 : K;
     for (int k = 0; k < K; ++k) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff, bw = 0;
-      for (int w = 0; w < nw; ++w)
-        if (hp[w] < K && better(s_v[w][hp[w]], s_i[w][hp[w]], bv, bi)) {
-          bv = s_v[w][hp[w]];
-          bi = s_i[w][hp[w]];
-          bw = w;
+      float bv = hp < K ? s_v[lane][hp] : -INFINITY;
+      int bi = hp < K ? s_i[lane][hp] : 0x7fffffff;
+      int owner = lane;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int oo = __shfl_xor_sync(0xffffffffu, owner, o);
+        if (better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+          owner = oo;
         }
-      ++hp[bw];
-      vals[(int64_t)blockIdx.x * K + k] = bv;
-      idx[(int64_t)blockIdx.x * K + k] = bi;
+      }
+      if (owner == lane) ++hp;
+      if (lane == 0) {
+        vals[(int64_t)blockIdx.x * K + k] = bv;
+        idx[(int64_t)blockIdx.x * K + k] = bi;
+      }
     }
   }
 }
@@ -191,14 +246,41 @@ __global__ void tree_init_kernel(TreeState* __restrict__ states, const long long
 
 // After a head pass over T frontier nodes per sequence (rows row_base + b*T + t):
 // add their top-k children as candidates and choose the next frontier.
-__global__ void tree_step_kernel(TreeState* __restrict__ states, const float* __restrict__ vals,
-                                 const int* __restrict__ idx, const float* __restrict__ lse, int row_base, int T,
-                                 int k, int next_T, const int* __restrict__ lengths, PassIO io, int B) {
+// The state is copied to shared memory by the CTA and back afterwards: the
+// serial bookkeeping then runs on shared-memory latency.
+constexpr int STATE_THREADS = 64;
+constexpr int STATE_WORDS = (int)(sizeof(TreeState) / 4);
+static_assert(sizeof(TreeState) % 4 == 0, "TreeState copies as 32-bit words");
+
+__device__ __forceinline__ void state_copy(uint32_t* dst, const uint32_t* src) {
+  for (int i = threadIdx.x; i < STATE_WORDS; i += blockDim.x) dst[i] = src[i];
+}
+
+__device__ void tree_step_one(TreeState& st, const float* __restrict__ vals, const int* __restrict__ idx,
+                              const float* __restrict__ lse, int row_base, int T, int k, int next_T, int L,
+                              const PassIO& io, int b);
+
+// One CTA per sequence.
+__global__ void __launch_bounds__(STATE_THREADS) tree_step_kernel(TreeState* __restrict__ states,
+                                                                  const float* __restrict__ vals,
+                                                                  const int* __restrict__ idx,
+                                                                  const float* __restrict__ lse, int row_base, int T,
+                                                                  int k, int next_T, const int* __restrict__ lengths,
+                                                                  PassIO io, int B) {
   pdl_wait();
   pdl_trigger();
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  TreeState& st = states[b];
+  __shared__ __align__(8) TreeState sst;
+  const int b = blockIdx.x;
+  state_copy(reinterpret_cast<uint32_t*>(&sst), reinterpret_cast<const uint32_t*>(&states[b]));
+  __syncthreads();
+  if (threadIdx.x == 0) tree_step_one(sst, vals, idx, lse, row_base, T, k, next_T, lengths[b], io, b);
+  __syncthreads();
+  state_copy(reinterpret_cast<uint32_t*>(&states[b]), reinterpret_cast<const uint32_t*>(&sst));
+}
+
+__device__ void tree_step_one(TreeState& st, const float* __restrict__ vals, const int* __restrict__ idx,
+                              const float* __restrict__ lse, int row_base, int T, int k, int next_T, int L,
+                              const PassIO& io, int b) {
   const int first_new = st.n_cand;
   for (int t = 0; t < T; ++t) {
     const int c = st.frontier[t];
@@ -239,7 +321,7 @@ __global__ void tree_step_kernel(TreeState* __restrict__ states, const float* __
     }
   for (int i = 0; i < nch; ++i) st.frontier[i] = chosen[i];
   st.n_frontier = nch;
-  write_pass(st, io, b, next_T, lengths[b]);
+  write_pass(st, io, b, next_T, L);
 }
 
 struct VerifyIO {
@@ -252,33 +334,48 @@ struct VerifyIO {
 };
 
 // Keep the n_nodes best candidates (score desc, depth asc, creation asc) plus
-// the root; emit them in creation order (parents first).
-__global__ void tree_finalize_kernel(const TreeState* __restrict__ states, int n_nodes, int k,
-                                     const int* __restrict__ lengths, VerifyIO io, int B) {
+// the root; emit them in creation order (parents first).  One CTA per
+// sequence: each thread ranks one candidate against all others, then one
+// thread lays out the kept nodes from shared memory.
+__global__ void __launch_bounds__(STATE_THREADS) tree_finalize_kernel(const TreeState* __restrict__ states,
+                                                                      int n_nodes, int k,
+                                                                      const int* __restrict__ lengths, VerifyIO io,
+                                                                      int B) {
   pdl_wait();
   pdl_trigger();
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  const TreeState& st = states[b];
-  const int NN = n_nodes + 1;
-  bool keep[MAXC];
-  for (int n = 0; n < st.n_cand; ++n) keep[n] = n == 0;
-  for (int sel = 0; sel < n_nodes && sel < st.n_cand - 1; ++sel) {
-    int best = -1;
-    for (int n = 1; n < st.n_cand; ++n) {
-      if (keep[n]) continue;
-      if (best < 0 || st.score[n] > st.score[best] ||
-          (st.score[n] == st.score[best] && st.depth[n] < st.depth[best]))
-        best = n;
+  __shared__ __align__(8) TreeState st;
+  __shared__ bool keep[MAXC];
+  __shared__ int ch[32][MAXK];
+  const int b = blockIdx.x;
+  state_copy(reinterpret_cast<uint32_t*>(&st), reinterpret_cast<const uint32_t*>(&states[b]));
+  __syncthreads();
+  const int nc = st.n_cand;
+  for (int n = threadIdx.x; n < nc; n += blockDim.x) {
+    if (n == 0) {
+      keep[0] = true;
+      continue;
     }
-    keep[best] = true;
+    int rank = 0;
+    const float sn = st.score[n];
+    const int dn = st.depth[n];
+    for (int m = 1; m < nc; ++m) {
+      const float sm = st.score[m];
+      const int dm = st.depth[m];
+      rank += (sm > sn || (sm == sn && (dm < dn || (dm == dn && m < n)))) ? 1 : 0;
+    }
+    keep[n] = rank < n_nodes;
   }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const int NN = n_nodes + 1;
   int pos_of[MAXC];
   int j = 0;
-  for (int n = 0; n < st.n_cand; ++n) pos_of[n] = keep[n] ? j++ : -1;
+  for (int n = 0; n < nc; ++n) pos_of[n] = keep[n] ? j++ : -1;
   const int L = lengths[b];
-  unsigned masks[MAXC];
-  for (int n = 0; n < st.n_cand; ++n) {
+  unsigned masks[32];
+  for (int v = 0; v < NN; ++v)
+    for (int r = 0; r < k; ++r) ch[v][r] = -1;
+  for (int n = 0; n < nc; ++n) {
     if (!keep[n]) continue;
     const int v = pos_of[n];
     const int p = st.parent[n];
@@ -287,27 +384,19 @@ __global__ void tree_finalize_kernel(const TreeState* __restrict__ states, int n
     io.pos[b * NN + v] = L + st.depth[n];
     io.mask[b * NN + v] = masks[v];
     io.hrow[b * NN + v] = st.hrow[n];
-    for (int r = 0; r < k; ++r) io.children[(b * NN + v) * k + r] = -1;
+    if (n > 0 && pos_of[p] >= 0) ch[pos_of[p]][st.rank[n]] = v;
   }
   for (int v = j; v < NN; ++v) {  // fewer candidates than nodes: pad with masked-out copies of the root
     io.ids[b * NN + v] = st.tok[0];
     io.pos[b * NN + v] = L;
     io.mask[b * NN + v] = 1u << v;
     io.hrow[b * NN + v] = -1;
-    for (int r = 0; r < k; ++r) io.children[(b * NN + v) * k + r] = -1;
   }
-  for (int n = 1; n < st.n_cand; ++n) {
-    if (!keep[n]) continue;
-    const int pv = pos_of[st.parent[n]];
-    if (pv >= 0) io.children[(b * NN + pv) * k + st.rank[n]] = pos_of[n];
-  }
-  // compact each children list (ranks of kept children, in rank order)
-  for (int v = 0; v < j; ++v) {
+  // children lists: kept children in rank order, then -1
+  for (int v = 0; v < NN; ++v) {
     int w = 0;
-    for (int r = 0; r < k; ++r) {
-      const int c = io.children[(b * NN + v) * k + r];
-      if (c >= 0) io.children[(b * NN + v) * k + w++] = c;
-    }
+    for (int r = 0; r < k; ++r)
+      if (ch[v][r] >= 0) io.children[(b * NN + v) * k + w++] = ch[v][r];
     for (; w < k; ++w) io.children[(b * NN + v) * k + w] = -1;
   }
   io.starts[b] = L;
@@ -316,90 +405,173 @@ __global__ void tree_finalize_kernel(const TreeState* __restrict__ states, int n
 // ---------------------------------------------------------------------------
 // acceptance on the verified tree
 // ---------------------------------------------------------------------------
-__device__ float block_reduce_sum(float v, float* red) {
+// Rejection sampling at one node works on p = softmax(target row) and
+// q = softmax(head row).  Rejecting child x_l turns (p_l, q_l) into
+//   p_{l+1} = max(p_l - q_l, 0) / Z_{l+1},   Z_{l+1} = sum_j max(p_l - q_l, 0)
+//   q_{l+1} = q_l without x_l, renormalised   (q_0(j) / (1 - sum_{i<=l} q_0(x_i)))
+// so p_r(j) and q_r(j) follow element-wise from the two bf16 logits, the two
+// log-sum-exps and the scalars Z_l: nothing of vocabulary size is stored.
+// One vocabulary pass per visited node (both log-sum-exps), one per
+// rejected child (its Z) and one for the bonus draw (inverse CDF).
+constexpr int ACC_THREADS = 512;
+constexpr int ACC_WARPS = ACC_THREADS / 32;
+
+struct AccNode {
+  float lse_t, lse_h;
+  int r;                  // children rejected so far
+  int X[MAXK];            // their tokens
+  float invZ[MAXK + 1];   // 1 / Z_l, l >= 1
+  float invQ[MAXK + 1];   // 1 / (1 - sum_{i<l} q_0(x_i)), invQ[0] = 1
+};
+
+__device__ __forceinline__ float acc_p(const AccNode& a, float tj, float hj, int j) {
+  float p = expf(tj - a.lse_t);
+  if (a.r == 0) return p;
+  const float q0 = expf(hj - a.lse_h);
+  bool ex = false;
+  for (int l = 0; l < a.r; ++l) {
+    const float ql = ex ? 0.f : q0 * a.invQ[l];
+    p = fmaxf(p - ql, 0.f) * a.invZ[l + 1];
+    ex |= a.X[l] == j;
+  }
+  return p;
+}
+
+__device__ __forceinline__ float acc_q(const AccNode& a, float hj, int j) {
+  for (int l = 0; l < a.r; ++l)
+    if (a.X[l] == j) return 0.f;
+  return expf(hj - a.lse_h) * a.invQ[a.r];
+}
+
+// deterministic block sum / lse merge (fixed shuffle tree, then warp order)
+__device__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  float t = 0.f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-  return t;
+  float t = lane < ACC_WARPS ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return __shfl_sync(0xffffffffu, t, 0);
 }
 
-__device__ float block_reduce_max(float v, float* red) {
-  v = warp_max(v);
+__device__ void block_lse(float& m, float& s, float* red_m, float* red_s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, om, os);
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = -INFINITY;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
-  return t;
-}
-
-// dst = softmax(row) over V (fp32), returns nothing; all threads participate
-__device__ void softmax_row(const bf16* __restrict__ row, float* __restrict__ dst, int V, float* red) {
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, bf2f(row[i]));
-  m = block_reduce_max(m, red);
-  float s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float e = expf(bf2f(row[i]) - m);
-    dst[i] = e;
-    s += e;
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_s[warp] = s;
   }
-  s = block_reduce_sum(s, red);
-  const float inv = 1.0f / s;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) dst[i] *= inv;
   __syncthreads();
+  m = lane < ACC_WARPS ? red_m[lane] : -INFINITY;
+  s = lane < ACC_WARPS ? red_s[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, om, os);
+  }
+  m = __shfl_sync(0xffffffffu, m, 0);
+  s = __shfl_sync(0xffffffffu, s, 0);
 }
 
-// First index whose inclusive prefix sum exceeds u * total (contiguous chunks per thread).
-__device__ int inverse_cdf(const float* __restrict__ p, int V, float u, float* red, int* s_idx) {
-  const int nt = blockDim.x;
-  const int chunk = (V + nt - 1) / nt;
-  const int lo = threadIdx.x * chunk, hi = min(V, lo + chunk);
-  float part = 0.f;
-  for (int i = lo; i < hi; ++i) part += p[i];
-  // inclusive scan of the per-thread parts (thread order = index order)
-  __shared__ float s_part[1024];
-  s_part[threadIdx.x] = part;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float run = 0.f;
-    for (int t = 0; t < nt; ++t) {
-      run += s_part[t];
-      s_part[t] = run;
+// Visit elements j of the two rows in strided 8-wide groups (coalesced 16-byte
+// loads, 4 groups in flight per thread); f(j, t_j, h_j).  h may be null.
+template <typename F>
+__device__ __forceinline__ void for_each_strided(const bf16* t, const bf16* h, int V, F f) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(t) | reinterpret_cast<uintptr_t>(h)) & 15u) == 0;
+  const int nvec = vec ? V / 8 : 0;
+  constexpr int U = 4;
+  for (int base = threadIdx.x; base < nvec; base += U * ACC_THREADS) {
+    uint4 qt[U], qh[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * ACC_THREADS;
+      if (i < nvec) {
+        qt[u] = __ldg(reinterpret_cast<const uint4*>(t) + i);
+        qh[u] = h ? __ldg(reinterpret_cast<const uint4*>(h) + i) : make_uint4(0, 0, 0, 0);
+      }
     }
-    *s_idx = -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * ACC_THREADS;
+      if (i < nvec) {
+        const bf16* et = reinterpret_cast<const bf16*>(&qt[u]);
+        const bf16* eh = reinterpret_cast<const bf16*>(&qh[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f(8 * i + e, bf2f(et[e]), bf2f(eh[e]));
+      }
+    }
+  }
+  for (int j = nvec * 8 + threadIdx.x; j < V; j += ACC_THREADS) f(j, bf2f(t[j]), h ? bf2f(h[j]) : 0.f);
+}
+
+// First index whose inclusive prefix sum of p_r exceeds u * total; if rounding
+// leaves none, the last index with mass (the oracle's inverse_cdf).
+__device__ int acc_inverse_cdf(const bf16* t, const bf16* h, int V, const AccNode& a, float u, float* red,
+                               int* s_pick) {
+  const int chunk = ((V + ACC_THREADS - 1) / ACC_THREADS + 7) / 8 * 8;
+  const int lo = min(V, (int)threadIdx.x * chunk), hi = min(V, lo + chunk);
+  float part = 0.f;
+  for (int j = lo; j < hi; ++j) part += acc_p(a, bf2f(t[j]), h ? bf2f(h[j]) : 0.f, j);
+  // inclusive scan over threads (thread order = index order)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float incl = part;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
   }
   __syncthreads();
-  const float total = s_part[nt - 1];
+  if (lane == 31) red[warp] = incl;
+  if (threadIdx.x == 0) *s_pick = -1;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < ACC_WARPS ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < ACC_WARPS) red[32 + lane] = w;   // inclusive warp prefix
+  }
+  __syncthreads();
+  const float wbase = warp == 0 ? 0.f : red[32 + warp - 1];
+  incl += wbase;
+  const float total = red[32 + ACC_WARPS - 1];
+  const float before = incl - part;
   const float thr = u * total;
-  const float before = threadIdx.x == 0 ? 0.f : s_part[threadIdx.x - 1];
-  if (before <= thr && s_part[threadIdx.x] > thr) {
+  if (lo < hi && before <= thr && incl > thr) {
     float run = before;
     int pick = hi - 1;
-    for (int i = lo; i < hi; ++i) {
-      run += p[i];
+    for (int j = lo; j < hi; ++j) {
+      run += acc_p(a, bf2f(t[j]), h ? bf2f(h[j]) : 0.f, j);
       if (run > thr) {
-        pick = i;
+        pick = j;
         break;
       }
     }
-    *s_idx = pick;
+    *s_pick = pick;
   }
   __syncthreads();
-  int r = *s_idx;
-  if (r < 0) {  // rounding left thr at or above the total: the last index with mass
-    if (threadIdx.x == 0) {
-      int i = V - 1;
-      while (i > 0 && p[i] == 0.f) --i;
-      *s_idx = i;
+  int r = *s_pick;
+  if (r < 0) {
+    // the last index with mass: the highest thread whose chunk holds some
+    if (threadIdx.x == 0) *s_pick = 0;
+    __syncthreads();
+    if (part > 0.f) atomicMax(s_pick, (int)threadIdx.x);
+    __syncthreads();
+    if (threadIdx.x == (unsigned)*s_pick) {
+      int i = hi - 1;
+      while (i > lo && acc_p(a, bf2f(t[i]), h ? bf2f(h[i]) : 0.f, i) == 0.f) --i;
+      red[96] = __int_as_float(max(i, 0));
     }
     __syncthreads();
-    r = *s_idx;
+    r = __float_as_int(red[96]);
   }
   __syncthreads();
   return r;
@@ -413,7 +585,7 @@ struct AcceptIO {
   const int* hrow;             // [B][NN]
   const int* children;         // [B][NN][k]
   const float* U;              // [B][depth+1][k+1] (NULL: greedy)
-  float* scratch;              // [B][2][V]
+  float* scratch;              // unused (kept for the ABI)
   int* path;                   // [B][depth+1] node indices (-1 pad)
   int* accept_len;             // [B]
   long long* tokens;           // [B][depth+2]: accepted tokens then the bonus (-1 pad)
@@ -421,16 +593,15 @@ struct AcceptIO {
   int NN, V, k, depth;
 };
 
-__global__ void __launch_bounds__(1024) accept_tree_kernel(AcceptIO io) {
+__global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[32];
-  __shared__ int s_idx, s_next, s_done;
-  __shared__ float s_px, s_qx;
+  __shared__ float red[128];
+  __shared__ int s_idx, s_next;
+  __shared__ AccNode s_node;
+  __shared__ int s_acc;
   const int b = blockIdx.x;
   const int NN = io.NN, V = io.V, k = io.k;
-  float* P = io.scratch + (size_t)b * 2 * V;
-  float* Q = P + V;
   int node = 0, d = 0, bonus = 0;
   for (;;) {
     const int* kids = io.children + ((size_t)b * NN + node) * k;
@@ -456,44 +627,58 @@ __global__ void __launch_bounds__(1024) accept_tree_kernel(AcceptIO io) {
       continue;
     }
     const float* u = io.U + ((size_t)b * (io.depth + 1) + d) * (k + 1);
-    softmax_row(io.target_logits + ((size_t)b * NN + node) * V, P, V, red);
     const bool has_kids = kids[0] >= 0;
-    if (has_kids) softmax_row(io.head_logits + (size_t)io.hrow[(size_t)b * NN + node] * V, Q, V, red);
+    const bf16* trow = io.target_logits + ((size_t)b * NN + node) * V;
+    const bf16* hrow = has_kids ? io.head_logits + (size_t)io.hrow[(size_t)b * NN + node] * V : nullptr;
+    // both log-sum-exps in one pass
+    float mt = -INFINITY, st = 0.f, mh = -INFINITY, sh = 0.f;
+    for_each_strided(trow, hrow, V, [&](int, float tj, float hj) {
+      lse_merge(mt, st, tj, 1.f);
+      if (hrow) lse_merge(mh, sh, hj, 1.f);
+    });
+    block_lse(mt, st, red, red + 32);
+    if (hrow) block_lse(mh, sh, red, red + 32);
+    if (threadIdx.x == 0) {
+      s_node.lse_t = mt + logf(st);
+      s_node.lse_h = hrow ? mh + logf(sh) : 0.f;
+      s_node.r = 0;
+      s_node.invQ[0] = 1.f;
+    }
+    __syncthreads();
     int nxt = -1;
+    float qrem = 1.f;
     for (int i = 0; i < k && has_kids && kids[i] >= 0; ++i) {
       const int c = kids[i];
       const int x = (int)io.ids[(size_t)b * NN + c];
       if (threadIdx.x == 0) {
-        s_px = P[x];
-        s_qx = Q[x];
+        const float tx = bf2f(trow[x]), hx = bf2f(hrow[x]);
+        s_acc = u[i] * acc_q(s_node, hx, x) < acc_p(s_node, tx, hx, x);
       }
       __syncthreads();
-      const bool acc = u[i] * s_qx < s_px;
+      const bool acc = s_acc;
       __syncthreads();
       if (acc) {
         nxt = c;
         break;
       }
-      // residual p <- norm(max(p - q, 0)); q <- q without x, renormalised
-      float sp = 0.f, sq = 0.f;
-      for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const float r = fmaxf(P[j] - Q[j], 0.f);
-        P[j] = r;
-        sp += r;
-        if (j == x) Q[j] = 0.f;
-        sq += Q[j];
-      }
-      sp = block_reduce_sum(sp, red);
-      sq = block_reduce_sum(sq, red);
-      const float ip = sp > 0.f ? 1.0f / sp : 0.f, iq = sq > 0.f ? 1.0f / sq : 0.f;
-      for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        P[j] *= ip;
-        Q[j] *= iq;
+      // rejected: Z_{r+1} over the vocabulary, then record x
+      float z = 0.f;
+      for_each_strided(trow, hrow, V, [&](int j, float tj, float hj) {
+        z += fmaxf(acc_p(s_node, tj, hj, j) - acc_q(s_node, hj, j), 0.f);
+      });
+      z = block_sum(z, red);
+      if (threadIdx.x == 0) {
+        const int r = s_node.r;
+        qrem -= expf(bf2f(hrow[x]) - s_node.lse_h);
+        s_node.invZ[r + 1] = z > 0.f ? 1.0f / z : 0.f;
+        s_node.invQ[r + 1] = qrem > 0.f ? 1.0f / qrem : 0.f;
+        s_node.X[r] = x;
+        s_node.r = r + 1;
       }
       __syncthreads();
     }
     if (nxt < 0) {
-      bonus = inverse_cdf(P, V, u[k], red, &s_idx);
+      bonus = acc_inverse_cdf(trow, hrow, V, s_node, u[k], red, &s_idx);
       break;
     }
     if (threadIdx.x == 0) io.path[b * (io.depth + 1) + d] = nxt;
@@ -563,10 +748,10 @@ extern "C" int tsds_logits_topk(const void* logits, int ld, int M, int V, int k,
                                 float* lse, tsds_stream_t stream) {
   TSDS_RETURN_IF(!logits || !vals || !idx || !lse || M <= 0 || V <= 0 || ld < V, TSDS_E_INVALID);
   switch (k) {
-    case 1: tsds_launch(topk_lse_kernel<1>, dim3(M), dim3(512), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 2: tsds_launch(topk_lse_kernel<2>, dim3(M), dim3(512), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 4: tsds_launch(topk_lse_kernel<4>, dim3(M), dim3(512), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 8: tsds_launch(topk_lse_kernel<8>, dim3(M), dim3(512), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 1: tsds_launch(topk_lse_kernel<1>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 2: tsds_launch(topk_lse_kernel<2>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 4: tsds_launch(topk_lse_kernel<4>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 8: tsds_launch(topk_lse_kernel<8>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
     default: return TSDS_E_UNSUPPORTED;
   }
   return tsds_launch_status();
@@ -588,7 +773,7 @@ extern "C" int tsds_tree_step(void* states, const float* vals, const int32_t* id
                               int B, tsds_stream_t stream) {
   TSDS_RETURN_IF(!states || B <= 0 || T <= 0 || k <= 0 || k > MAXK || next_T > MAXK, TSDS_E_INVALID);
   PassIO io{(long long*)pass_tok, pass_featrow, pass_pos, (unsigned*)pass_mask, pass_starts};
-  tsds_launch(tree_step_kernel, dim3((B + 63) / 64), dim3(64), 0, stream, (TreeState*)states, vals, (const int*)idx,
+  tsds_launch(tree_step_kernel, dim3(B), dim3(STATE_THREADS), 0, stream, (TreeState*)states, vals, (const int*)idx,
               lse, row_base, T, k, next_T, (const int*)lengths, io, B);
   return tsds_launch_status();
 }
@@ -598,7 +783,7 @@ extern "C" int tsds_tree_finalize(const void* states, int n_nodes, int k, const 
                                   int32_t* starts, int B, tsds_stream_t stream) {
   TSDS_RETURN_IF(!states || n_nodes < 1 || n_nodes + 1 > 32 || k < 1 || k > MAXK || B <= 0, TSDS_E_INVALID);
   VerifyIO io{(long long*)ids, positions, (unsigned*)masks, hrow, children, starts};
-  tsds_launch(tree_finalize_kernel, dim3((B + 63) / 64), dim3(64), 0, stream, (const TreeState*)states, n_nodes, k,
+  tsds_launch(tree_finalize_kernel, dim3(B), dim3(STATE_THREADS), 0, stream, (const TreeState*)states, n_nodes, k,
               (const int*)lengths, io, B);
   return tsds_launch_status();
 }
@@ -613,7 +798,7 @@ extern "C" int tsds_accept_tree(const void* target_logits, const int64_t* target
   AcceptIO io{(const bf16*)target_logits, (const long long*)target_argmax, (const bf16*)head_logits,
               (const long long*)ids, hrow, children, U, scratch, path, accept_len, (long long*)tokens,
               (long long*)cur, n_nodes + 1, V, k, depth};
-  tsds_launch(accept_tree_kernel, dim3(B), dim3(1024), 0, stream, io);
+  tsds_launch(accept_tree_kernel, dim3(B), dim3(ACC_THREADS), 0, stream, io);
   return tsds_launch_status();
 }
 
