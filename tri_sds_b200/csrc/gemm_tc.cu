@@ -111,6 +111,14 @@ __device__ __forceinline__ int owner_of(int x, int P, uint32_t W) {
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int MAX_TILES = 2048;   // tile counters; departure counters follow them
+
 struct Smem {
   uint64_t full_bar[MAX_STAGES];
   uint64_t empty_bar[MAX_STAGES];
@@ -333,6 +341,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const int eq = warp & 3;
     const int r = eq * 32 + lane;  // tile row == TMEM lane
     const int nchunk = p.Npad / 16;
+    // STORE / RESIDUAL / STORE_F32: split tiles are reduced by all their
+    // contributors (each sums a slice of rows) once every partial is stored;
+    // SWIGLU / ARGMAX need whole tiles and keep the last-arriver reduction.
+    constexpr bool DIST = EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32;
+    int pend0 = -1, pend1 = -1;  // split tiles of this CTA (registers, not an indexed array)
+    int npend = 0;
     int seg = 0;
     bool alive = b < e;
     for (int t = (int)(b / KT); alive && t <= (int)((e - 1) / KT); ++t, ++seg) {
@@ -375,7 +389,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tempty_bar[buf]);
-      if (!full) {
+      if (!full && DIST) {
+        // arrive without waiting: a split tile is only a first or a last
+        // segment, so there are at most two
+        __threadfence();
+        epi_bar();
+        if (r == 0) atomicAdd(&p.counters[t], 1);
+        if (npend++ == 0)
+          pend0 = t;
+        else
+          pend1 = t;
+      } else if (!full) {
         // contributors of tile t: CTAs q_lo..q_hi, in order
         const int q_lo = owner_of(tb, p.P, p.W), q_hi = owner_of(tb + KT - 1, p.P, p.W);
         __threadfence();
@@ -427,6 +451,93 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             finish_chunk<EPI>(p, sh, t, r, c * 16, v);
           }
           if (r == 0) p.counters[t] = 0;  // ready for the next launch
+        }
+      }
+    }
+    if constexpr (DIST) {
+      // Every arrival of this CTA is done, so no wait below can block
+      // another CTA's arrival (the grid is one resident wave).  Contributor
+      // c of nq sums rows [c*128/nq, (c+1)*128/nq) of the tile over all
+      // partials in CTA order; the last to leave resets the counters.
+      for (int pi = 0; alive && pi < npend; ++pi) {
+        const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
+        const int q_lo = owner_of(tb, p.P, p.W), q_hi = owner_of(tb + KT - 1, p.P, p.W);
+        const int nq = q_hi - q_lo + 1, c = pc - q_lo;
+        const int lo_slot = it_begin(q_lo, p.P, p.W) < tb ? 1 : 0;
+        const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
+        const int nel = R * (p.Npad / 4);
+        if (r == 0) {
+          int ok = 1;
+          if (ld_acquire(&p.counters[t]) < nq) {
+            const uint64_t t0 = global_ns();
+            while (ld_acquire(&p.counters[t]) < nq) {
+              if (global_ns() - t0 > 2000000000ull) {
+                ok = 0;
+                break;
+              }
+            }
+          }
+          if (!ok) atomicExch(p.status, TSDS_E_TIMEOUT);
+          sh.go = ok;
+        }
+        epi_bar();
+        const bool go = sh.go;
+        epi_bar();
+        if (!go) {
+          alive = false;
+          break;
+        }
+        for (int e0 = r; e0 < nel; e0 += 128) {
+          const int rr = rlo + e0 % R, g = e0 / R;
+          const int j = t * TILE_J + rr;
+          float rv[4] = {0.f, 0.f, 0.f, 0.f};
+          if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (j < p.n_out && 4 * g + i < p.M) rv[i] = bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j]);
+          }
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          constexpr int QB = 8;
+          for (int q0 = 0; q0 < nq; q0 += QB) {
+            float4 f[QB];
+#pragma unroll
+            for (int i = 0; i < QB; ++i)
+              if (q0 + i < nq) {
+                const int q = q_lo + q0 + i;
+                const int qs = q0 + i == 0 ? lo_slot : 0;
+                f[i] = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                              (size_t)g * TILE_J + rr);
+              }
+#pragma unroll
+            for (int i = 0; i < QB; ++i)
+              if (q0 + i < nq) {
+                acc.x += f[i].x;
+                acc.y += f[i].y;
+                acc.z += f[i].z;
+                acc.w += f[i].w;
+              }
+          }
+          if (j < p.n_out) {
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int m = 4 * g + i;
+              if (m < p.M) {
+                const int64_t o = (int64_t)m * p.ldo + j;
+                if constexpr (EPI == EPI_STORE_F32)
+                  reinterpret_cast<float*>(p.out)[o] = a4[i];
+                else if constexpr (EPI == EPI_STORE)
+                  p.out[o] = f2bf(a4[i]);
+                else
+                  p.out[o] = f2bf(rv[i] + rbf(a4[i]));
+              }
+            }
+          }
+        }
+        epi_bar();
+        if (r == 0 && atomicAdd(&p.counters[MAX_TILES + t], 1) == nq - 1) {
+          p.counters[t] = 0;  // every contributor has left: ready for the next launch
+          p.counters[MAX_TILES + t] = 0;
         }
       }
     }
@@ -487,11 +598,12 @@ int pow2_at_least(int x) {
 
 }  // namespace
 
-// Workspace layout: [status int32, padding to 64 B][counters: 2048 ints][partials: P x 2 x Npad x 128 fp32].
+// Workspace layout: [status int32, padding to 64 B][arrival counters: 2048 ints][departure counters:
+// 2048 ints][partials: P x 2 x Npad x 128 fp32].
 // The counters must be zero before the first use; every launch leaves them zero.
 size_t tsds_tc_workspace_bytes(int M) {
   const int npad = M <= 0 ? 0 : (M + 15) / 16 * 16;
-  return 64 + 2048 * sizeof(int) + (size_t)num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
+  return 64 + 2 * MAX_TILES * sizeof(int) + (size_t)num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
 }
 
 int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
@@ -508,7 +620,7 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.K = K;
   p.KT = (K + BK - 1) / BK;
   p.tiles = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + TILE_J - 1) / TILE_J;
-  TSDS_RETURN_IF(p.tiles > 2048, TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF(p.tiles > MAX_TILES, TSDS_E_UNSUPPORTED);
   const long long W64 = (long long)p.tiles * p.KT;
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = g_ctas_per_sm;
@@ -524,7 +636,7 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.res = res;
   p.out = out;
   p.counters = (int*)((char*)workspace + 64);
-  p.ws = (float*)((char*)workspace + 64 + 2048 * sizeof(int));
+  p.ws = (float*)((char*)workspace + 64 + 2 * MAX_TILES * sizeof(int));
   p.status = status;
   p.cand_val = cand_val;
   p.cand_idx = cand_idx;
