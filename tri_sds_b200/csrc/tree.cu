@@ -7,7 +7,11 @@
 // bookkeeping is per sequence and tiny (<= 72 candidates), so it runs in one
 // thread per sequence; the vocabulary-wide work (top-k, softmax, residual
 // distributions, inverse-CDF draws) runs on whole CTAs.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 using namespace tsds;
 
@@ -70,19 +74,30 @@ __device__ __forceinline__ void topk_take8(float (&tv)[K], int (&ti)[K], float& 
   lse_merge(m, s, mx, t);
 }
 
-// One CTA of TOPK_THREADS threads per row.  Rows whose start is 16-byte aligned are
-// read as 16-byte vectors, TOPK_UNROLL of them in flight per thread; the
+constexpr int TOPK_CL = 8;   // CTAs per row (one cluster)
+
+// One cluster of TOPK_CL CTAs per row (grid (TOPK_CL, rows)); CTA rank c
+// reads the vocabulary slice [c*vs, (c+1)*vs) as 16-byte vectors when the
+// row is aligned, TOPK_UNROLL of them in flight per thread.  Rank 0 merges
+// the ranks' lists and log-sum-exps from distributed shared memory.  All
 // reductions run in a fixed order, so the result is deterministic.
 template <int K>
-__global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* __restrict__ logits, int ld, int V,
-                                                                float* __restrict__ vals, int* __restrict__ idx,
-                                                                float* __restrict__ lse) {
+__global__ void __cluster_dims__(TOPK_CL, 1, 1) __launch_bounds__(TOPK_THREADS, 1)
+    topk_lse_kernel(const bf16* __restrict__ logits, int ld, int V, float* __restrict__ vals,
+                    int* __restrict__ idx, float* __restrict__ lse) {
   pdl_wait();
   pdl_trigger();
+  cg::cluster_group cl = cg::this_cluster();
   __shared__ float s_v[TOPK_WARPS][K];
   __shared__ int s_i[TOPK_WARPS][K];
   __shared__ float s_m[TOPK_WARPS], s_s[TOPK_WARPS];
-  const bf16* row = logits + (int64_t)blockIdx.x * ld;
+  __shared__ float c_v[K];   // this CTA's result, read by rank 0
+  __shared__ int c_i[K];
+  __shared__ float c_ms[2];
+  const int rank = blockIdx.x, rowi = blockIdx.y;
+  const int vs = ((V + TOPK_CL - 1) / TOPK_CL + 7) / 8 * 8;
+  const int v0 = min(V, rank * vs), v1 = min(V, v0 + vs);
+  const bf16* row = logits + (int64_t)rowi * ld;
   float tv[K];
   int ti[K];
 #pragma unroll
@@ -92,8 +107,8 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* _
   }
   float m = -INFINITY, s = 0.f;
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
-  const int nvec = vec ? V / 8 : 0;
-  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  const int nvec = vec ? (v1 - v0) / 8 : 0;
+  const uint4* rv = reinterpret_cast<const uint4*>(row + v0);
   for (int base = threadIdx.x; base < nvec; base += TOPK_UNROLL * TOPK_THREADS) {
     uint4 q[TOPK_UNROLL];
 #pragma unroll
@@ -104,10 +119,10 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* _
 #pragma unroll
     for (int u = 0; u < TOPK_UNROLL; ++u) {
       const int i = base + u * TOPK_THREADS;
-      if (i < nvec) topk_take8<K>(tv, ti, m, s, q[u], 8 * i);
+      if (i < nvec) topk_take8<K>(tv, ti, m, s, q[u], v0 + 8 * i);
     }
   }
-  for (int i = nvec * 8 + threadIdx.x; i < V; i += TOPK_THREADS) {
+  for (int i = v0 + nvec * 8 + threadIdx.x; i < v1; i += TOPK_THREADS) {
     const float x = bf2f(row[i]);
     insert_topk<K>(tv, ti, x, i);
     lse_merge(m, s, x, 1.f);
@@ -160,7 +175,10 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* _
       const float om = __shfl_xor_sync(0xffffffffu, wm, o), os = __shfl_xor_sync(0xffffffffu, ws, o);
       lse_merge(wm, ws, om, os);
     }
-    if (lane == 0) lse[blockIdx.x] = wm + logf(ws);
+    if (lane == 0) {
+      c_ms[0] = wm;
+      c_ms[1] = ws;
+    }
     // top-k over the warps' lists: lane w holds warp w's list
     int hp = lane < TOPK_WARPS ? 0 : K;
     for (int k = 0; k < K; ++k) {
@@ -180,11 +198,48 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_lse_kernel(const bf16* _
       }
       if (owner == lane) ++hp;
       if (lane == 0) {
-        vals[(int64_t)blockIdx.x * K + k] = bv;
-        idx[(int64_t)blockIdx.x * K + k] = bi;
+        c_v[k] = bv;
+        c_i[k] = bi;
       }
     }
   }
+  cl.sync();
+  if (rank == 0 && warp == 0) {
+    // lane q < TOPK_CL holds rank q's list and log-sum-exp
+    const float* rv_ = lane < TOPK_CL ? cl.map_shared_rank(c_v, lane) : nullptr;
+    const int* ri_ = lane < TOPK_CL ? cl.map_shared_rank(c_i, lane) : nullptr;
+    const float* rms = lane < TOPK_CL ? cl.map_shared_rank(c_ms, lane) : nullptr;
+    float wm = rms ? rms[0] : -INFINITY, ws = rms ? rms[1] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, wm, o), os = __shfl_xor_sync(0xffffffffu, ws, o);
+      lse_merge(wm, ws, om, os);
+    }
+    if (lane == 0) lse[rowi] = wm + logf(ws);
+    int hp = lane < TOPK_CL ? 0 : K;
+    for (int k = 0; k < K; ++k) {
+      float bv = hp < K ? rv_[hp] : -INFINITY;
+      int bi = hp < K ? ri_[hp] : 0x7fffffff;
+      int owner = lane;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int oo = __shfl_xor_sync(0xffffffffu, owner, o);
+        if (better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+          owner = oo;
+        }
+      }
+      if (owner == lane) ++hp;
+      if (lane == 0) {
+        vals[(int64_t)rowi * K + k] = bv;
+        idx[(int64_t)rowi * K + k] = bi;
+      }
+    }
+  }
+  cl.sync();  // the other ranks' shared memory stays valid until rank 0 is done
 }
 
 // ---------------------------------------------------------------------------
@@ -413,6 +468,13 @@ __global__ void __launch_bounds__(STATE_THREADS) tree_finalize_kernel(const Tree
 // log-sum-exps and the scalars Z_l: nothing of vocabulary size is stored.
 // One vocabulary pass per visited node (both log-sum-exps), one per
 // rejected child (its Z) and one for the bonus draw (inverse CDF).
+//
+// Each sequence runs on one cluster of ACC_CL CTAs; CTA rank c owns the
+// vocabulary slice [c*vs, (c+1)*vs).  CTA-level partial results are
+// exchanged through distributed shared memory and combined in rank order,
+// so every CTA holds bit-identical scalars and takes the same decisions;
+// rank 0 writes the outputs.
+constexpr int ACC_CL = 8;
 constexpr int ACC_THREADS = 512;
 constexpr int ACC_WARPS = ACC_THREADS / 32;
 
@@ -443,7 +505,7 @@ __device__ __forceinline__ float acc_q(const AccNode& a, float hj, int j) {
   return expf(hj - a.lse_h) * a.invQ[a.r];
 }
 
-// deterministic block sum / lse merge (fixed shuffle tree, then warp order)
+// deterministic block reductions (fixed shuffle tree, then warp order)
 __device__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -479,102 +541,49 @@ __device__ void block_lse(float& m, float& s, float* red_m, float* red_s) {
   s = __shfl_sync(0xffffffffu, s, 0);
 }
 
-// Visit elements j of the two rows in strided 8-wide groups (coalesced 16-byte
-// loads, 4 groups in flight per thread); f(j, t_j, h_j).  h may be null.
+// Cluster exchange: each CTA publishes up to 4 floats; after the barrier
+// every thread reads all ranks' values.  Double-buffered by phase: a CTA
+// can only rewrite a buffer after the next barrier, which every CTA reaches
+// after it has finished reading it.
+struct Xch {
+  float v[2][4];
+};
+
+__device__ __forceinline__ float* xch_publish(Xch& x, int phase) { return x.v[phase & 1]; }
+
+__device__ __forceinline__ const float* xch_remote(cg::cluster_group& cl, Xch& x, int phase, int rank) {
+  return cl.map_shared_rank(x.v[phase & 1], rank);
+}
+
+// Visit elements j in [v0, v1) of the two rows in strided 8-wide groups
+// (16-byte loads, 4 groups in flight per thread); f(j, t_j, h_j).  h may be null.
 template <typename F>
-__device__ __forceinline__ void for_each_strided(const bf16* t, const bf16* h, int V, F f) {
-  const bool vec = ((reinterpret_cast<uintptr_t>(t) | reinterpret_cast<uintptr_t>(h)) & 15u) == 0;
-  const int nvec = vec ? V / 8 : 0;
+__device__ __forceinline__ void for_each_strided(const bf16* t, const bf16* h, int v0, int v1, F f) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(t) | reinterpret_cast<uintptr_t>(h)) & 15u) == 0 && (v0 & 7) == 0;
+  const int g0 = v0 / 8, ng = vec ? (v1 - v0) / 8 : 0;
   constexpr int U = 4;
-  for (int base = threadIdx.x; base < nvec; base += U * ACC_THREADS) {
+  for (int base = threadIdx.x; base < ng; base += U * ACC_THREADS) {
     uint4 qt[U], qh[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int i = base + u * ACC_THREADS;
-      if (i < nvec) {
-        qt[u] = __ldg(reinterpret_cast<const uint4*>(t) + i);
-        qh[u] = h ? __ldg(reinterpret_cast<const uint4*>(h) + i) : make_uint4(0, 0, 0, 0);
+      if (i < ng) {
+        qt[u] = __ldg(reinterpret_cast<const uint4*>(t) + g0 + i);
+        qh[u] = h ? __ldg(reinterpret_cast<const uint4*>(h) + g0 + i) : make_uint4(0, 0, 0, 0);
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int i = base + u * ACC_THREADS;
-      if (i < nvec) {
+      if (i < ng) {
         const bf16* et = reinterpret_cast<const bf16*>(&qt[u]);
         const bf16* eh = reinterpret_cast<const bf16*>(&qh[u]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f(8 * i + e, bf2f(et[e]), bf2f(eh[e]));
+        for (int e = 0; e < 8; ++e) f(8 * (g0 + i) + e, bf2f(et[e]), bf2f(eh[e]));
       }
     }
   }
-  for (int j = nvec * 8 + threadIdx.x; j < V; j += ACC_THREADS) f(j, bf2f(t[j]), h ? bf2f(h[j]) : 0.f);
-}
-
-// First index whose inclusive prefix sum of p_r exceeds u * total; if rounding
-// leaves none, the last index with mass (the oracle's inverse_cdf).
-__device__ int acc_inverse_cdf(const bf16* t, const bf16* h, int V, const AccNode& a, float u, float* red,
-                               int* s_pick) {
-  const int chunk = ((V + ACC_THREADS - 1) / ACC_THREADS + 7) / 8 * 8;
-  const int lo = min(V, (int)threadIdx.x * chunk), hi = min(V, lo + chunk);
-  float part = 0.f;
-  for (int j = lo; j < hi; ++j) part += acc_p(a, bf2f(t[j]), h ? bf2f(h[j]) : 0.f, j);
-  // inclusive scan over threads (thread order = index order)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float incl = part;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  __syncthreads();
-  if (lane == 31) red[warp] = incl;
-  if (threadIdx.x == 0) *s_pick = -1;
-  __syncthreads();
-  if (warp == 0) {
-    float w = lane < ACC_WARPS ? red[lane] : 0.f;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    if (lane < ACC_WARPS) red[32 + lane] = w;   // inclusive warp prefix
-  }
-  __syncthreads();
-  const float wbase = warp == 0 ? 0.f : red[32 + warp - 1];
-  incl += wbase;
-  const float total = red[32 + ACC_WARPS - 1];
-  const float before = incl - part;
-  const float thr = u * total;
-  if (lo < hi && before <= thr && incl > thr) {
-    float run = before;
-    int pick = hi - 1;
-    for (int j = lo; j < hi; ++j) {
-      run += acc_p(a, bf2f(t[j]), h ? bf2f(h[j]) : 0.f, j);
-      if (run > thr) {
-        pick = j;
-        break;
-      }
-    }
-    *s_pick = pick;
-  }
-  __syncthreads();
-  int r = *s_pick;
-  if (r < 0) {
-    // the last index with mass: the highest thread whose chunk holds some
-    if (threadIdx.x == 0) *s_pick = 0;
-    __syncthreads();
-    if (part > 0.f) atomicMax(s_pick, (int)threadIdx.x);
-    __syncthreads();
-    if (threadIdx.x == (unsigned)*s_pick) {
-      int i = hi - 1;
-      while (i > lo && acc_p(a, bf2f(t[i]), h ? bf2f(h[i]) : 0.f, i) == 0.f) --i;
-      red[96] = __int_as_float(max(i, 0));
-    }
-    __syncthreads();
-    r = __float_as_int(red[96]);
-  }
-  __syncthreads();
-  return r;
+  for (int j = v0 + ng * 8 + threadIdx.x; j < v1; j += ACC_THREADS) f(j, bf2f(t[j]), h ? bf2f(h[j]) : 0.f);
 }
 
 struct AcceptIO {
@@ -593,19 +602,24 @@ struct AcceptIO {
   int NN, V, k, depth;
 };
 
-__global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io) {
+// grid (ACC_CL, B): blockIdx.x = rank in the sequence's cluster
+__global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float red[128];
-  __shared__ int s_idx, s_next;
+  cg::cluster_group cl = cg::this_cluster();
+  __shared__ float red[64];
+  __shared__ int s_next, s_idx, s_pick, s_last;
   __shared__ AccNode s_node;
-  __shared__ int s_acc;
-  const int b = blockIdx.x;
+  __shared__ Xch xch;
+  const int rank = blockIdx.x, b = blockIdx.y;
   const int NN = io.NN, V = io.V, k = io.k;
+  const int vs = ((V + ACC_CL - 1) / ACC_CL + 7) / 8 * 8;
+  const int v0 = min(V, rank * vs), v1 = min(V, v0 + vs);
+  int phase = 0;
   int node = 0, d = 0, bonus = 0;
   for (;;) {
     const int* kids = io.children + ((size_t)b * NN + node) * k;
-    if (io.U == nullptr) {  // greedy
+    if (io.U == nullptr) {  // greedy: no vocabulary work; every rank follows the same path
       if (threadIdx.x == 0) {
         const long long y = io.target_argmax[(size_t)b * NN + node];
         s_next = -1;
@@ -621,7 +635,7 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io
       bonus = s_idx;
       __syncthreads();
       if (nxt < 0) break;
-      if (threadIdx.x == 0) io.path[b * (io.depth + 1) + d] = nxt;
+      if (rank == 0 && threadIdx.x == 0) io.path[b * (io.depth + 1) + d] = nxt;
       node = nxt;
       ++d;
       continue;
@@ -630,14 +644,29 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io
     const bool has_kids = kids[0] >= 0;
     const bf16* trow = io.target_logits + ((size_t)b * NN + node) * V;
     const bf16* hrow = has_kids ? io.head_logits + (size_t)io.hrow[(size_t)b * NN + node] * V : nullptr;
-    // both log-sum-exps in one pass
+    // both log-sum-exps in one pass over this rank's slice, then across the cluster
     float mt = -INFINITY, st = 0.f, mh = -INFINITY, sh = 0.f;
-    for_each_strided(trow, hrow, V, [&](int, float tj, float hj) {
+    for_each_strided(trow, hrow, v0, v1, [&](int, float tj, float hj) {
       lse_merge(mt, st, tj, 1.f);
       if (hrow) lse_merge(mh, sh, hj, 1.f);
     });
     block_lse(mt, st, red, red + 32);
-    if (hrow) block_lse(mh, sh, red, red + 32);
+    block_lse(mh, sh, red, red + 32);
+    if (threadIdx.x == 0) {
+      float* o = xch_publish(xch, phase);
+      o[0] = mt;
+      o[1] = st;
+      o[2] = mh;
+      o[3] = sh;
+    }
+    cl.sync();
+    mt = -INFINITY, st = 0.f, mh = -INFINITY, sh = 0.f;
+    for (int q = 0; q < ACC_CL; ++q) {
+      const float* o = xch_remote(cl, xch, phase, q);
+      lse_merge(mt, st, o[0], o[1]);
+      lse_merge(mh, sh, o[2], o[3]);
+    }
+    ++phase;
     if (threadIdx.x == 0) {
       s_node.lse_t = mt + logf(st);
       s_node.lse_h = hrow ? mh + logf(sh) : 0.f;
@@ -650,23 +679,30 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io
     for (int i = 0; i < k && has_kids && kids[i] >= 0; ++i) {
       const int c = kids[i];
       const int x = (int)io.ids[(size_t)b * NN + c];
-      if (threadIdx.x == 0) {
+      // rank 0 decides and broadcasts: the ranks' control flow (and so their
+      // cluster barriers) cannot diverge
+      if (rank == 0 && threadIdx.x == 0) {
         const float tx = bf2f(trow[x]), hx = bf2f(hrow[x]);
-        s_acc = u[i] * acc_q(s_node, hx, x) < acc_p(s_node, tx, hx, x);
+        xch_publish(xch, phase)[0] = u[i] * acc_q(s_node, hx, x) < acc_p(s_node, tx, hx, x) ? 1.f : 0.f;
       }
-      __syncthreads();
-      const bool acc = s_acc;
-      __syncthreads();
+      cl.sync();
+      const bool acc = xch_remote(cl, xch, phase, 0)[0] != 0.f;
+      ++phase;
       if (acc) {
         nxt = c;
         break;
       }
       // rejected: Z_{r+1} over the vocabulary, then record x
       float z = 0.f;
-      for_each_strided(trow, hrow, V, [&](int j, float tj, float hj) {
+      for_each_strided(trow, hrow, v0, v1, [&](int j, float tj, float hj) {
         z += fmaxf(acc_p(s_node, tj, hj, j) - acc_q(s_node, hj, j), 0.f);
       });
       z = block_sum(z, red);
+      if (threadIdx.x == 0) xch_publish(xch, phase)[0] = z;
+      cl.sync();
+      z = 0.f;
+      for (int q = 0; q < ACC_CL; ++q) z += xch_remote(cl, xch, phase, q)[0];
+      ++phase;
       if (threadIdx.x == 0) {
         const int r = s_node.r;
         qrem -= expf(bf2f(hrow[x]) - s_node.lse_h);
@@ -677,15 +713,93 @@ __global__ void __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io
       }
       __syncthreads();
     }
-    if (nxt < 0) {
-      bonus = acc_inverse_cdf(trow, hrow, V, s_node, u[k], red, &s_idx);
-      break;
+    if (nxt >= 0) {
+      if (rank == 0 && threadIdx.x == 0) io.path[b * (io.depth + 1) + d] = nxt;
+      node = nxt;
+      ++d;
+      continue;
     }
-    if (threadIdx.x == 0) io.path[b * (io.depth + 1) + d] = nxt;
-    node = nxt;
-    ++d;
+    // bonus: first index whose inclusive prefix sum of p_r exceeds u[k] * total
+    // (contiguous chunks per thread inside the rank's slice); if rounding
+    // leaves none, the last index with mass (the oracle's inverse_cdf)
+    const int n = v1 - v0;
+    const int chunk = (n + ACC_THREADS - 1) / ACC_THREADS;
+    const int lo = v0 + min(n, (int)threadIdx.x * chunk), hi = v0 + min(n, ((int)threadIdx.x + 1) * chunk);
+    float part = 0.f;
+    int last = -1;
+    for (int j = lo; j < hi; ++j) {
+      const float pj = acc_p(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
+      part += pj;
+      if (pj > 0.f) last = j;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float incl = part;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (threadIdx.x == 0) {
+      s_pick = -1;
+      s_last = -1;
+    }
+    __syncthreads();
+    if (lane == 31) red[warp] = incl;
+    if (last >= 0) atomicMax(&s_last, last);
+    __syncthreads();
+    if (warp == 0) {
+      float w = lane < ACC_WARPS ? red[lane] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      if (lane < ACC_WARPS) red[32 + lane] = w;  // inclusive prefix over warps
+    }
+    __syncthreads();
+    const float cta_total = red[32 + ACC_WARPS - 1];
+    incl += warp == 0 ? 0.f : red[32 + warp - 1];
+    if (threadIdx.x == 0) {
+      float* o = xch_publish(xch, phase);
+      o[0] = cta_total;
+      o[1] = __int_as_float(s_last);
+    }
+    cl.sync();
+    float base = 0.f, total = 0.f;
+    int glast = -1;
+    for (int q = 0; q < ACC_CL; ++q) {
+      const float* o = xch_remote(cl, xch, phase, q);
+      if (q < rank) base += o[0];
+      total += o[0];
+      glast = max(glast, __float_as_int(o[1]));
+    }
+    ++phase;
+    const float thr = u[k] * total;
+    const float before = base + incl - part;
+    if (lo < hi && before <= thr && base + incl > thr) {
+      float run = before;
+      int pick = hi - 1;
+      for (int j = lo; j < hi; ++j) {
+        run += acc_p(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
+        if (run > thr) {
+          pick = j;
+          break;
+        }
+      }
+      s_pick = pick;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) xch_publish(xch, phase)[0] = __int_as_float(s_pick);
+    cl.sync();
+    int pick = -1;
+    for (int q = 0; q < ACC_CL && pick < 0; ++q) pick = __float_as_int(xch_remote(cl, xch, phase, q)[0]);
+    ++phase;
+    bonus = pick >= 0 ? pick : max(glast, 0);
+    break;
   }
-  if (threadIdx.x == 0) {
+  // no CTA may exit while another can still read its shared memory
+  cl.sync();
+  if (rank == 0 && threadIdx.x == 0) {
     for (int i = d; i < io.depth + 1; ++i) io.path[b * (io.depth + 1) + i] = -1;
     io.accept_len[b] = d;
     long long* tk = io.tokens + (size_t)b * (io.depth + 2);
@@ -748,10 +862,10 @@ extern "C" int tsds_logits_topk(const void* logits, int ld, int M, int V, int k,
                                 float* lse, tsds_stream_t stream) {
   TSDS_RETURN_IF(!logits || !vals || !idx || !lse || M <= 0 || V <= 0 || ld < V, TSDS_E_INVALID);
   switch (k) {
-    case 1: tsds_launch(topk_lse_kernel<1>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 2: tsds_launch(topk_lse_kernel<2>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 4: tsds_launch(topk_lse_kernel<4>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
-    case 8: tsds_launch(topk_lse_kernel<8>, dim3(M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 1: tsds_launch(topk_lse_kernel<1>, dim3(TOPK_CL, M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 2: tsds_launch(topk_lse_kernel<2>, dim3(TOPK_CL, M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 4: tsds_launch(topk_lse_kernel<4>, dim3(TOPK_CL, M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
+    case 8: tsds_launch(topk_lse_kernel<8>, dim3(TOPK_CL, M), dim3(TOPK_THREADS), 0, stream, (const bf16*)logits, ld, V, vals, idx, lse); break;
     default: return TSDS_E_UNSUPPORTED;
   }
   return tsds_launch_status();
@@ -798,7 +912,7 @@ extern "C" int tsds_accept_tree(const void* target_logits, const int64_t* target
   AcceptIO io{(const bf16*)target_logits, (const long long*)target_argmax, (const bf16*)head_logits,
               (const long long*)ids, hrow, children, U, scratch, path, accept_len, (long long*)tokens,
               (long long*)cur, n_nodes + 1, V, k, depth};
-  tsds_launch(accept_tree_kernel, dim3(B), dim3(ACC_THREADS), 0, stream, io);
+  tsds_launch(accept_tree_kernel, dim3(ACC_CL, B), dim3(ACC_THREADS), 0, stream, io);
   return tsds_launch_status();
 }
 
