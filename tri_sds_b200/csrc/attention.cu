@@ -301,6 +301,11 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
 }
 
 // Merge the splits of one (b, kvh, row): splits with m = -inf hold nothing.
+// Up to CMB_REG splits are loaded in one batch (every load in flight at
+// once); the arithmetic - max over splits, then the weighted sum in split
+// order - is the same for any split count.
+constexpr int CMB_REG = 32;
+
 __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
   const int r = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int d = threadIdx.x;
@@ -310,16 +315,40 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
   const int start = a.starts[b];
   const int used = min(a.nsplit, (start + a.T + a.split_keys - 1) / a.split_keys);
   const int64_t base = ((int64_t)b * a.Hkv + kvh) * a.nsplit;
-  float mmax = -INFINITY;
-  for (int s = 0; s < used; ++s) mmax = fmaxf(mmax, a.ws_ml[(base + s) * a.Rpad + r].x);
   float acc = 0.f, lsum = 0.f;
-  if (mmax != -INFINITY) {
-    for (int s = 0; s < used; ++s) {
-      const float2 ml = a.ws_ml[(base + s) * a.Rpad + r];
-      if (ml.x == -INFINITY) continue;
-      const float w = exp2f(ml.x - mmax);
-      lsum += w * ml.y;
-      acc += w * a.ws_o[((base + s) * a.Rpad + r) * D + d];
+  if (used <= CMB_REG) {
+    float2 ml[CMB_REG];
+    float ov[CMB_REG];
+#pragma unroll
+    for (int s = 0; s < CMB_REG; ++s)
+      if (s < used) {
+        ml[s] = a.ws_ml[(base + s) * a.Rpad + r];
+        ov[s] = a.ws_o[((base + s) * a.Rpad + r) * D + d];
+      }
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < CMB_REG; ++s)
+      if (s < used) mmax = fmaxf(mmax, ml[s].x);
+    if (mmax != -INFINITY) {
+#pragma unroll
+      for (int s = 0; s < CMB_REG; ++s)
+        if (s < used && ml[s].x != -INFINITY) {
+          const float w = exp2f(ml[s].x - mmax);
+          lsum += w * ml[s].y;
+          acc += w * ov[s];
+        }
+    }
+  } else {
+    float mmax = -INFINITY;
+    for (int s = 0; s < used; ++s) mmax = fmaxf(mmax, a.ws_ml[(base + s) * a.Rpad + r].x);
+    if (mmax != -INFINITY) {
+      for (int s = 0; s < used; ++s) {
+        const float2 ml = a.ws_ml[(base + s) * a.Rpad + r];
+        if (ml.x == -INFINITY) continue;
+        const float w = exp2f(ml.x - mmax);
+        lsum += w * ml.y;
+        acc += w * a.ws_o[((base + s) * a.Rpad + r) * D + d];
+      }
     }
   }
   const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;

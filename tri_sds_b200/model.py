@@ -119,7 +119,7 @@ class QwenModel:
     """
 
     def __init__(self, shape: QwenShape, batch: int, max_seq: int, max_rows: int, device="cuda",
-                 weights: dict | None = None, seed: int = 0, split_keys: int = 256, qk_norm: bool | None = None,
+                 weights: dict | None = None, seed: int = 0, split_keys: int = 128, qk_norm: bool | None = None,
                  share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
                  tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None):
         self.shape = shape
