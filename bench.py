@@ -436,7 +436,7 @@ def main():
         if backend == "nccl":
             import torch
             torch.cuda.set_device(local_rank)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
     try:
         if a.impl == "reference":
             run_reference(a, rank, world)

@@ -1,10 +1,11 @@
-"""Tensor-parallel shard rules on CPU: two gloo ranks, each holding the
+"""Tensor-parallel shard rules on CPU: 2 and 4 gloo ranks, each holding the
 tri_sds_b200.tp shards of an oracle layer, reproduce the unsharded layer
 (fp32) after the all-reduces, and the vocab-parallel argmax merge picks the
 full argmax (ties: lowest global index)."""
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -12,7 +13,7 @@ import torch.nn.functional as F
 
 from oracle.qwen import QwenOracle, QwenShape, apply_rope, random_qwen_weights, rms_norm
 
-SHAPE = QwenShape(hidden=64, n_heads=4, n_kv_heads=2, head_dim=16, intermediate=128, n_layers=1, vocab=96)
+SHAPE = QwenShape(hidden=64, n_heads=8, n_kv_heads=4, head_dim=16, intermediate=128, n_layers=1, vocab=96)
 
 
 def _tp_layer(L, x, pos, shape, rank, tp, cos, sin):
@@ -72,13 +73,14 @@ def _worker(rank, tp, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_layer_and_vocab_parallel_argmax_match_unsharded():
+@pytest.mark.parametrize("tp", [2, 4])
+def test_tp_layer_and_vocab_parallel_argmax_match_unsharded(tp):
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, tp, port, q)) for r in range(tp)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
