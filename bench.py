@@ -285,7 +285,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
                           tp_layers=False, tp_vocab=False)
         engine = SpecEngine(target, draft, K)
-    prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7 + rank))
+    # the same prompt on every rank: tensor-parallel ranks process the same tokens
+    prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7))
     lc0 = _lib.query("tsds_launch_count")
     engine.prepare(prompt)
     launches_per_cycle = None

@@ -1,6 +1,7 @@
 """Tensor parallelism on 2 GPUs (NCCL): the TP=2 verify forward vs the
-oracle, and greedy speculative decoding == greedy autoregressive decoding
-under TP=2.  Skipped with fewer than 2 GPUs."""
+oracle, and greedy speculative decoding (chain draft and EAGLE tree, whose
+commit compacts each rank's shard of the KV cache) == greedy autoregressive
+decoding under TP=2.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -54,6 +55,14 @@ def _worker(rank, port, q):
         tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
         ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
         out.update(spec=spec, ar=ar)
+        # EAGLE tree, greedy: the head replicated, the target TP=2
+        from oracle import eagle as oe
+        from tri_sds_b200.eagle import EagleEngine, EagleHead
+        we = oe.random_eagle_weights(oshape, seed=4, std=0.08)
+        tgt3 = QwenModel(shape, B, 128, B * 26, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        eng = EagleEngine(tgt3, EagleHead(tgt3, B, weights=we), greedy=True)
+        espec, _ = eng.generate(prompt, 16)
+        out.update(espec=espec)
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e)))
@@ -91,3 +100,5 @@ def test_tp2_verify_and_lossless_spec():
     assert (got - ref.float()).abs().max().item() <= 2e-2
     assert torch.equal(res[0]["am"], res[0]["logits"].float().argmax(-1))
     assert torch.equal(res[0]["spec"], res[0]["ar"])
+    assert torch.equal(res[0]["espec"], res[1]["espec"])
+    assert torch.equal(res[0]["espec"], res[0]["ar"])

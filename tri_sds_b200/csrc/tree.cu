@@ -63,6 +63,7 @@ __device__ __forceinline__ void topk_take8(float (&tv)[K], int (&ti)[K], float& 
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     x[j] = bf2f(e[j]);
+    if (x[j] != x[j]) x[j] = -INFINITY;  // NaN ranks last: every emitted index is a real token
     mx = fmaxf(mx, x[j]);
   }
 #pragma unroll
@@ -123,7 +124,8 @@ __global__ void __cluster_dims__(TOPK_CL, 1, 1) __launch_bounds__(TOPK_THREADS, 
     }
   }
   for (int i = v0 + nvec * 8 + threadIdx.x; i < v1; i += TOPK_THREADS) {
-    const float x = bf2f(row[i]);
+    float x = bf2f(row[i]);
+    if (x != x) x = -INFINITY;
     insert_topk<K>(tv, ti, x, i);
     lse_merge(m, s, x, 1.f);
   }
@@ -410,11 +412,15 @@ __global__ void __launch_bounds__(STATE_THREADS) tree_finalize_kernel(const Tree
       keep[0] = true;
       continue;
     }
+    // a strict total order (NaN scores rank last), so exactly
+    // min(n_nodes, nc - 1) candidates are kept
     int rank = 0;
-    const float sn = st.score[n];
+    float sn = st.score[n];
+    if (sn != sn) sn = -INFINITY;
     const int dn = st.depth[n];
     for (int m = 1; m < nc; ++m) {
-      const float sm = st.score[m];
+      float sm = st.score[m];
+      if (sm != sm) sm = -INFINITY;
       const int dm = st.depth[m];
       rank += (sm > sn || (sm == sn && (dm < dn || (dm == dn && m < n)))) ? 1 : 0;
     }
@@ -425,13 +431,13 @@ __global__ void __launch_bounds__(STATE_THREADS) tree_finalize_kernel(const Tree
   const int NN = n_nodes + 1;
   int pos_of[MAXC];
   int j = 0;
-  for (int n = 0; n < nc; ++n) pos_of[n] = keep[n] ? j++ : -1;
+  for (int n = 0; n < nc; ++n) pos_of[n] = keep[n] && j < NN ? j++ : -1;
   const int L = lengths[b];
   unsigned masks[32];
   for (int v = 0; v < NN; ++v)
     for (int r = 0; r < k; ++r) ch[v][r] = -1;
   for (int n = 0; n < nc; ++n) {
-    if (!keep[n]) continue;
+    if (pos_of[n] < 0) continue;
     const int v = pos_of[n];
     const int p = st.parent[n];
     masks[v] = (1u << v) | (p >= 0 && pos_of[p] >= 0 ? masks[pos_of[p]] : 0u);
@@ -679,10 +685,11 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
     for (int i = 0; i < k && has_kids && kids[i] >= 0; ++i) {
       const int c = kids[i];
       const int x = (int)io.ids[(size_t)b * NN + c];
+      const int xr = min(max(x, 0), V - 1);  // row index for the logits reads (ids come from top-k)
       // rank 0 decides and broadcasts: the ranks' control flow (and so their
       // cluster barriers) cannot diverge
       if (rank == 0 && threadIdx.x == 0) {
-        const float tx = bf2f(trow[x]), hx = bf2f(hrow[x]);
+        const float tx = bf2f(trow[xr]), hx = bf2f(hrow[xr]);
         xch_publish(xch, phase)[0] = u[i] * acc_q(s_node, hx, x) < acc_p(s_node, tx, hx, x) ? 1.f : 0.f;
       }
       cl.sync();
@@ -705,7 +712,7 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
       ++phase;
       if (threadIdx.x == 0) {
         const int r = s_node.r;
-        qrem -= expf(bf2f(hrow[x]) - s_node.lse_h);
+        qrem -= expf(bf2f(hrow[xr]) - s_node.lse_h);
         s_node.invZ[r + 1] = z > 0.f ? 1.0f / z : 0.f;
         s_node.invQ[r + 1] = qrem > 0.f ? 1.0f / qrem : 0.f;
         s_node.X[r] = x;

@@ -143,7 +143,9 @@ class EagleEngine:
                _p(self.ids), _p(self.hrow), _p(self.children), None if self.greedy else _p(self.U),
                _p(self.scratch), _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
                self.n_nodes, s.vocab, k, self.depth)
-        pl.add("tsds_tree_commit", _p(t.k_cache), _p(t.v_cache), s.n_layers, B, s.n_kv_heads, t.max_seq,
+        # the cache's own kv-head count: under tensor parallelism a rank holds
+        # only its shard of the kv heads
+        pl.add("tsds_tree_commit", _p(t.k_cache), _p(t.v_cache), s.n_layers, B, t.k_cache.shape[2], t.max_seq,
                s.head_dim, _p(t.lengths), _p(self.path), _p(self.accept_len), self.depth, _p(t.x), self.n_nodes,
                s.hidden, _p(self.root_feat))
         return pl
