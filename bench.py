@@ -233,7 +233,7 @@ def run_reference(a, rank: int, world: int):
     # tokens per cycle: one per sequence (the bonus) plus accepted drafts; with
     # independent random-init models the acceptance is ~0 (measured on the device arm)
     tok_s = a.batch / cyc
-    line = {"impl": "reference", "metric": METRIC.format(B=a.batch, n=1), "value": tok_s, "unit": "tok/s",
+    line = {"impl": "reference", "metric": METRIC.format(B=a.batch, n=world), "value": tok_s, "unit": "tok/s",
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": cyc * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": a.batch, "seq_len": a.prompt,
@@ -423,6 +423,9 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
         }
         print(json.dumps(line), flush=True)
+    # CUDA graphs that hold NCCL calls go before the process group does
+    engine.graph = None
+    torch.cuda.synchronize()
 
 
 def main():
@@ -437,16 +440,27 @@ def main():
         if backend == "nccl":
             import torch
             torch.cuda.set_device(local_rank)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            # the all-reduces here are small (<= 0.5 MB); NVLink SHARP buys nothing
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        # a short limit: a rank stuck in a collective fails instead of waiting
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     try:
         if a.impl == "reference":
             run_reference(a, rank, world)
         else:
             run_tsds(a, rank, world, local_rank)
-    finally:
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
+    except BaseException:
+        # a failed rank leaves without destroy_process_group: the CUDA graphs
+        # that hold NCCL calls may still be alive in the traceback, and the
+        # teardown would wait on them for good
+        import traceback
+        traceback.print_exc()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(1)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
