@@ -1,0 +1,89 @@
+"""The drop-in boundary on CPU: plugin registration (tri_sds/__init__.py:1-10)
+and TriSDSWorker's dispatch (tri_sds/worker.py:19-78) with a stand-in engine
+that records its calls (no GPU, no kernels)."""
+import pytest
+import torch
+
+
+class FakeEngine:
+    """The engine interface the worker drives: prepare / step / run_draft /
+    run_verify, with a tokens buffer of shape [B, depth+2]."""
+
+    def __init__(self, B=2, width=7):
+        self.calls = []
+        self.tokens = torch.full((B, width), -1, dtype=torch.int64)
+        self.accept_len = torch.zeros(B, dtype=torch.int32)
+
+    def prepare(self, prompt):
+        self.calls.append(("prepare", tuple(prompt.shape)))
+        return prompt[:, -1]
+
+    def step(self, U=None):
+        self.calls.append(("step",))
+        self.tokens[:, 0] = len(self.calls)
+        return self.tokens, self.accept_len
+
+    def run_draft(self):
+        self.calls.append(("draft",))
+        return torch.arange(8).reshape(2, 4)
+
+    def run_verify(self):
+        self.calls.append(("verify",))
+        return self.tokens, self.accept_len
+
+
+def test_create_plugin_registers_the_replacement():
+    import tri_sds_b200
+    from tri_sds_b200.sglang_compat import HAVE_SGLANG, HookRegistry, HookType
+    from tri_sds_b200.worker import TriSDSWorker
+    if HAVE_SGLANG:
+        pytest.skip("SGLang's own registry is installed")
+    tri_sds_b200.create_plugin()
+    assert HookRegistry.lookup(tri_sds_b200.STANDALONE_WORKER) == (TriSDSWorker, HookType.REPLACE)
+    assert tri_sds_b200.STANDALONE_WORKER == "sglang.srt.speculative.standalone_worker.StandaloneWorker"
+
+
+def test_sds_disabled_delegates_to_sglang(monkeypatch):
+    from tri_sds_b200.sglang_compat import HAVE_SGLANG, ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
+    if HAVE_SGLANG:
+        pytest.skip("needs the stand-in base class")
+    monkeypatch.delenv("SDS_ENABLED", raising=False)
+    w = TriSDSWorker()
+    eng = FakeEngine()
+    w.attach_engine(eng)
+    batch = ScheduleBatch(input_ids=torch.zeros(2, 5, dtype=torch.int64))
+    for meth in (w.forward_batch_generation, w.draft, w.verify):
+        with pytest.raises(NotImplementedError):
+            meth(batch)
+    assert eng.calls == []
+
+
+def test_sds_enabled_runs_the_engine(monkeypatch):
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
+    monkeypatch.setenv("SDS_ENABLED", "1")
+    w = TriSDSWorker()
+    eng = FakeEngine()
+    w.attach_engine(eng)
+    prompt = torch.randint(0, 100, (2, 5))
+    toks, n = w.forward_batch_generation(ScheduleBatch(input_ids=prompt))
+    # the first call prefills from the prompt, then runs one cycle
+    assert eng.calls == [("prepare", (2, 5)), ("step",)]
+    assert toks.shape == (2, 7) and n.shape == (2,)
+    # results are copies: the next cycle does not overwrite them
+    first = toks.clone()
+    w.forward_batch_generation(ScheduleBatch(input_ids=prompt))
+    assert eng.calls[-1] == ("step",) and eng.calls.count(("prepare", (2, 5))) == 1
+    assert torch.equal(toks, first)
+    assert w.draft(ScheduleBatch(input_ids=prompt)).shape == (2, 4)
+    w.verify(ScheduleBatch(input_ids=prompt))
+    assert eng.calls[-2:] == [("draft",), ("verify",)]
+
+
+def test_worker_without_engine_says_so(monkeypatch):
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
+    monkeypatch.setenv("SDS_ENABLED", "1")
+    with pytest.raises(RuntimeError, match="attach_engine"):
+        TriSDSWorker().forward_batch_generation(ScheduleBatch(input_ids=torch.zeros(1, 3, dtype=torch.int64)))
