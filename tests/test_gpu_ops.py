@@ -159,6 +159,19 @@ def test_verify_attention_vs_f32(ops, B, T, starts, S):
     assert (got - ref).abs().max().item() <= 1e-2
 
 
+@pytest.mark.parametrize("split_keys", [128, 64])
+def test_verify_attention_kv4096_b8(ops, split_keys):
+    """The isolated verify-attention configuration at its largest batch: B=8,
+    KV length 4096, 5 new tokens, 64/8 heads.  128-key splits give 32 splits
+    (the combine pass's batched-load path at its limit), 64-key splits 64
+    (its streaming path)."""
+    B, T, S = 8, 5, 4096
+    q, kc, vc, st = _attn_case(B, T, 64, 8, S, [S - T] * B, seed=13)
+    got = ops.verify_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), st.to(DEV), split_keys=split_keys).cpu().float()
+    ref = _attn_ref_f32(q, kc, vc, st)
+    assert (got - ref).abs().max().item() <= 1e-2
+
+
 def test_verify_attention_vs_oracle(ops):
     """Against the reference's own path (repeat_interleave + SDPA with its mask)."""
     B, T, S = 2, 5, 128

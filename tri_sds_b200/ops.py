@@ -199,7 +199,7 @@ def fused_rmsnorm_qkv_rope(x, norm1_w, qkv_w_t, q_out, k_cache, v_cache, cos, si
 
 
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, starts: torch.Tensor,
-                     tree_mask: torch.Tensor | None = None, max_kv: int | None = None, split_keys: int = 256,
+                     tree_mask: torch.Tensor | None = None, max_kv: int | None = None, split_keys: int = 128,
                      scale: float | None = None, out: torch.Tensor | None = None, mask_origin: int = -1):
     """Attention of q [B, T, Hq, D] over caches [B, Hkv, S, D] whose rows
     ``starts[b]..starts[b]+T-1`` hold the new tokens (qwen_model.py:121-131
