@@ -132,3 +132,38 @@ def test_worker_plugin_cycle():
         assert int(toks2[0, int(n2[0])]) >= 0
     finally:
         os.environ.pop("SDS_ENABLED", None)
+
+
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 5), (4, 5), (8, 5)])
+def test_layer_qwen3_4b_shape_random_positions(B, T):
+    """One Qwen3-4B-shape layer (hidden 2560, 32/8 heads of 128, SwiGLU 9728,
+    QK-norm, RoPE theta 1e6) over M = B*T in {1, 5, 20, 40} rows at random
+    positions below 4096, the K/V cache below each sequence's start filled with
+    the same random rows on both sides: the hidden state after the layer within
+    5e-2 (relative to its largest entry) of the oracle."""
+    from tri_sds_b200 import ops
+    ops.set_gemv_max_rows(0)
+    oshape, dshape = _shapes(hidden=2560, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=9728, n_layers=1,
+                             vocab=1000)
+    w = oq.random_qwen_weights(oshape, seed=B * 10 + T, std=0.02)
+    S = 4096
+    g = torch.Generator().manual_seed(B + T)
+    starts = torch.randint(0, S - T, (B,), generator=g)
+    ids = torch.randint(0, oshape.vocab, (B, T), generator=g)
+    kpre = torch.randn(B, 8, S, 128, generator=g).to(torch.bfloat16)
+    vpre = torch.randn(B, 8, S, 128, generator=g).to(torch.bfloat16)
+    ora = oq.QwenOracle(oshape, w, batch=B, max_seq=S)
+    ora.k_caches[0].copy_(kpre)
+    ora.v_caches[0].copy_(vpre)
+    _, ref_hidden = ora.forward(ids, starts=starts)
+    m = _model(dshape, w, B, max_rows=B * T, max_seq=S)
+    m.k_cache[0].copy_(kpre.to(DEV))
+    m.v_cache[0].copy_(vpre.to(DEV))
+    m.lengths.copy_(starts.to(torch.int32).to(DEV))
+    am = torch.zeros(B * T, dtype=torch.int64, device=DEV)
+    m.forward_plan(ids.to(DEV).contiguous(), 1, B, T, m.lengths, 0, am, 1).run()
+    torch.cuda.synchronize()
+    m.check_status()
+    hid = m.x[:B * T].cpu().float().reshape(B, T, -1)
+    ref = ref_hidden.float()
+    assert (hid - ref).abs().max().item() <= 5e-2 * ref.abs().max().item()
