@@ -270,7 +270,7 @@ int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shar
  *   q, 0)), q <- q without x; bonus by inverse CDF); U NULL -> greedy
  *   (child == target argmax).  Writes path node indices, accept lengths,
  *   emitted tokens (accepted + bonus, -1 padded) and cur <- bonus.
- *   scratch: B * 2 * V floats.
+ *   scratch: unused (nothing of vocabulary size is stored); may be NULL.
  * tsds_tree_commit: move the accepted nodes' K/V rows L + path[j] -> L+1+j
  *   in every layer, copy the last accepted node's hidden state to
  *   root_feat, then lengths += accept_len + 1.

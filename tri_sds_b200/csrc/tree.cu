@@ -600,7 +600,7 @@ struct AcceptIO {
   const int* hrow;             // [B][NN]
   const int* children;         // [B][NN][k]
   const float* U;              // [B][depth+1][k+1] (NULL: greedy)
-  float* scratch;              // unused (kept for the ABI)
+  float* scratch;              // unused (kept in the ABI; may be null)
   int* path;                   // [B][depth+1] node indices (-1 pad)
   int* accept_len;             // [B]
   long long* tokens;           // [B][depth+2]: accepted tokens then the bonus (-1 pad)
@@ -914,7 +914,7 @@ extern "C" int tsds_accept_tree(const void* target_logits, const int64_t* target
                                 float* scratch, int32_t* path, int32_t* accept_len, int64_t* tokens, int64_t* cur,
                                 int B, int n_nodes, int V, int k, int depth, tsds_stream_t stream) {
   TSDS_RETURN_IF(B <= 0 || n_nodes < 1 || V <= 0 || k < 1 || k > MAXK || depth < 1, TSDS_E_INVALID);
-  TSDS_RETURN_IF(U != nullptr && (!target_logits || !head_logits || !scratch), TSDS_E_INVALID);
+  TSDS_RETURN_IF(U != nullptr && (!target_logits || !head_logits), TSDS_E_INVALID);
   TSDS_RETURN_IF(U == nullptr && !target_argmax, TSDS_E_INVALID);
   AcceptIO io{(const bf16*)target_logits, (const long long*)target_argmax, (const bf16*)head_logits,
               (const long long*)ids, hrow, children, U, scratch, path, accept_len, (long long*)tokens,

@@ -88,7 +88,6 @@ class EagleEngine:
         self.target_logits = torch.zeros(B * NN, s.vocab, **bf)
         self.target_argmax = torch.zeros(B * NN, **i64)
         self.U = torch.zeros(B, depth + 1, topk + 1, **f32)
-        self.scratch = torch.zeros(B * 2 * s.vocab, **f32)
         self.path = torch.zeros(B * (depth + 1), **i32)
         self.accept_len = torch.zeros(B, **i32)
         self.tokens = torch.zeros(B, depth + 2, **i64)
@@ -141,7 +140,7 @@ class EagleEngine:
         pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits))
         pl.add("tsds_accept_tree", _p(self.target_logits), _p(self.target_argmax), _p(self.head_logits),
                _p(self.ids), _p(self.hrow), _p(self.children), None if self.greedy else _p(self.U),
-               _p(self.scratch), _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
+               None, _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
                self.n_nodes, s.vocab, k, self.depth)
         # the cache's own kv-head count: under tensor parallelism a rank holds
         # only its shard of the kv heads
