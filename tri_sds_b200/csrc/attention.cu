@@ -422,13 +422,9 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.scale_log2 = scale * LOG2E;
 
   const size_t smem = attn_smem_bytes();
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(verify_attn_kernel<kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return TSDS_E_LAUNCH;
-    attr_set = true;
-  }
+  static bool attr_set[TSDS_MAX_DEVICES] = {};
+  st = tsds_smem_limit_once(verify_attn_kernel<kStages>, (int)smem, attr_set);
+  if (st != TSDS_OK) return st;
   dim3 grid(nsplit * nrb, Hkv, B);
   tsds_launch(verify_attn_kernel<kStages>, grid, dim3(warps * 32), smem, stream, kmap, vmap, a);
   st = tsds_launch_status();

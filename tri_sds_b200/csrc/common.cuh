@@ -29,6 +29,26 @@ static inline int tsds_launch_status() {
 
 static inline bool tsds_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Raise a kernel's dynamic shared-memory limit on the current device, once per
+// device (the attribute is per device): `done` is the caller's per-kernel record.
+constexpr int TSDS_MAX_DEVICES = 64;
+template <typename Kernel>
+static inline int tsds_smem_limit_once(Kernel kernel, int bytes, bool (&done)[TSDS_MAX_DEVICES]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= TSDS_MAX_DEVICES) {
+    cudaGetLastError();
+    return TSDS_E_DEVICE;
+  }
+  if (!done[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return TSDS_E_LAUNCH;
+    }
+    done[dev] = true;
+  }
+  return TSDS_OK;
+}
+
 // Programmatic dependent launch: every kernel of the library is launched so
 // that it may start while the previous kernel in the stream drains; each
 // kernel executes griddepcontrol.wait before touching memory the previous

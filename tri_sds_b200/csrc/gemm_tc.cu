@@ -579,13 +579,9 @@ namespace {
 
 template <int EPI>
 int launch_tc(const CUtensorMap& amap, const CUtensorMap& bmap, const TcParams& p, size_t smem, cudaStream_t stream) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET) !=
-        cudaSuccess)
-      return TSDS_E_LAUNCH;
-    attr = true;
-  }
+  static bool attr[TSDS_MAX_DEVICES] = {};
+  const int st = tsds_smem_limit_once(tc_gemm_kernel<EPI>, SMEM_BUDGET, attr);
+  if (st != TSDS_OK) return st;
   tsds_launch(tc_gemm_kernel<EPI>, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
   return tsds_launch_status();
 }
