@@ -63,6 +63,10 @@ def _worker(rank, port, q):
         eng = EagleEngine(tgt3, EagleHead(tgt3, B, weights=we), greedy=True)
         espec, _ = eng.generate(prompt, 16)
         out.update(espec=espec)
+        # a CUDA graph holding NCCL calls must be gone before the process group
+        eng.graph = None
+        del eng
+        torch.cuda.synchronize()
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e)))
