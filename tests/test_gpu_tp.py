@@ -81,12 +81,16 @@ def test_tp2_verify_and_lossless_spec():
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(2)]
+    procs = [ctx.Process(daemon=True, target=_worker, args=(r, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in procs)
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        res = dict(q.get(timeout=600) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():  # a rank stuck in teardown must not keep the session waiting
+                p.terminate()
     for r in (0, 1):
         assert isinstance(res[r], dict), res[r]
     # both ranks hold identical results

@@ -83,12 +83,16 @@ def test_tp_layer_and_vocab_parallel_argmax_match_unsharded(tp):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, tp, port, q)) for r in range(tp)]
+    procs = [ctx.Process(daemon=True, target=_worker, args=(r, tp, port, q)) for r in range(tp)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=120) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
+    try:
+        res = [q.get(timeout=120) for _ in procs]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():  # a rank stuck in teardown must not keep the session waiting
+                p.terminate()
     for rank, err, ok in res:
         assert err <= 5e-5, (rank, err)  # fp32 sums over up to 8 rank partials
         assert ok, rank
