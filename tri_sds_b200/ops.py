@@ -47,6 +47,14 @@ def _bf16_cuda(*ts):
             _need(t.is_cuda and t.dtype == torch.bfloat16, "expected a bf16 CUDA tensor")
 
 
+def _cuda(dtype, *ts):
+    """Index / length tensors: on a CUDA device, of the kernel's integer type
+    (a host pointer handed to a kernel would fault the device)."""
+    for t in ts:
+        if t is not None:
+            _need(t.is_cuda and t.dtype == dtype, f"expected a {dtype} CUDA tensor")
+
+
 class _Scratch:
     """Grow-only, zero-initialised workspaces (one per device and op kind:
     the tcgen05 tile counters of one op must not be overwritten by another's
@@ -93,7 +101,7 @@ def set_gemv_max_rows(rows: int) -> None:
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None):
     """norm.py:61-72 over the rows of a 2-D tensor."""
-    _bf16_cuda(x, weight)
+    _bf16_cuda(x, weight, out)
     _need(x.dim() == 2 and x.stride(1) == 1, "x must be [rows, n] with unit inner stride")
     rows, n = x.shape
     out = torch.empty_like(x) if out is None else out
@@ -104,7 +112,8 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torc
 
 def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None):
     """table[ids] for a flat int64 id tensor."""
-    _bf16_cuda(table)
+    _bf16_cuda(table, out)
+    _cuda(torch.int64, ids)
     ids = ids.reshape(-1)
     _need(ids.dtype == torch.int64 and ids.is_cuda, "ids must be int64 CUDA")
     M = ids.numel()
@@ -120,7 +129,7 @@ def _lin_ws(M, n_out, K, device):
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None):
     """x [M, K] @ w[n_out, K]^T -> bf16 [M, n_out]."""
-    _bf16_cuda(x, w)
+    _bf16_cuda(x, w, out)
     M, K = x.shape
     n_out = w.shape[0]
     _need(w.shape[1] == K and w.is_contiguous(), "w must be contiguous [n_out, K]")
@@ -132,7 +141,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None):
 
 def linear_residual(x: torch.Tensor, w: torch.Tensor, res: torch.Tensor, out: torch.Tensor | None = None):
     """res + x @ w^T with the reference's rounding (bf16 product, bf16 sum)."""
-    _bf16_cuda(x, w, res)
+    _bf16_cuda(x, w, res, out)
     M, K = x.shape
     n_out = w.shape[0]
     _need(w.shape[1] == K and w.is_contiguous() and res.shape == (M, n_out), "shape mismatch")
@@ -146,7 +155,7 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, res: torch.Tensor, out: to
 
 def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | None = None):
     """silu(x @ gate^T) * (x @ up^T) for w_gate_up = [gate; up] ([2I, K])."""
-    _bf16_cuda(x, w_gate_up)
+    _bf16_cuda(x, w_gate_up, out)
     M, K = x.shape
     _need(w_gate_up.shape[0] % 2 == 0 and w_gate_up.shape[1] == K and w_gate_up.is_contiguous(), "bad gate/up")
     I = w_gate_up.shape[0] // 2
@@ -177,6 +186,7 @@ def qk_norm_rope_kv(qkv, q_norm_w, k_norm_w, cos, sin, positions, starts, q_out,
     """QK-norm + RoPE of the q/k heads of ``qkv`` [B*T, (Hq+2Hkv)*D]; q -> q_out,
     k/v -> the cache rows ``starts[b]+t``."""
     _bf16_cuda(qkv, q_norm_w, k_norm_w, cos, sin, q_out, k_cache, v_cache)
+    _cuda(torch.int32, positions, starts)
     D = k_cache.shape[-1]
     S = k_cache.shape[-2]
     _lib.call("tsds_qk_norm_rope_kv", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin), _p(positions),
@@ -204,7 +214,7 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     """Attention of q [B, T, Hq, D] over caches [B, Hkv, S, D] whose rows
     ``starts[b]..starts[b]+T-1`` hold the new tokens (qwen_model.py:121-131
     with per-sequence starts and an optional [B, T] tree bitmask)."""
-    _bf16_cuda(q, k_cache, v_cache)
+    _bf16_cuda(q, k_cache, v_cache, out)
     B, T, Hq, D = q.shape
     Hkv, S = k_cache.shape[1], k_cache.shape[2]
     _need(q.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous(), "contiguous tensors expected")
@@ -237,6 +247,7 @@ def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, return_logits: bool = False
     """argmax_v (x @ w^T) on bf16-rounded logits, lowest index on ties;
     optionally also the bf16 logits [M, V]."""
     _bf16_cuda(x, w)
+    _cuda(torch.int64, out)
     M, K = x.shape
     V = w.shape[0]
     out = torch.empty(M, dtype=torch.int64, device=x.device) if out is None else out
@@ -252,6 +263,8 @@ def accept_greedy(draft: torch.Tensor, target: torch.Tensor, target_len: torch.T
                   cur: torch.Tensor):
     """Greedy acceptance + commit (in place on target_len/last/cur);
     returns (accept_len [B] int32, tokens [B, K+1] int64 padded with -1)."""
+    _cuda(torch.int64, draft, target, last, cur)
+    _cuda(torch.int32, target_len)
     B, K = draft.shape
     acc = torch.empty(B, dtype=torch.int32, device=draft.device)
     tokens = torch.empty(B, K + 1, dtype=torch.int64, device=draft.device)
