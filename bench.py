@@ -61,6 +61,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
+                    help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
                     help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 4)")
     return ap.parse_args()
@@ -271,12 +273,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     max_seq = (max_seq + 63) // 64 * 64
     # N > 1: the target is tensor-parallel over all ranks (shards drawn per
     # rank; replicated tensors from the same seed on every rank)
-    comm = None
+    comm = peer = None
     if world > 1:
-        from tri_sds_b200.tp import Comm
+        from tri_sds_b200.tp import Comm, PeerAllReduce
         comm = Comm()
+        if a.allreduce == "peer":
+            peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden)
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
-                       tp_size=world, comm=comm)
+                       tp_size=world, comm=comm, peer=peer)
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         head = EagleHead(target, B, seed=2000)
@@ -406,7 +410,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": B, "seq_len": P,
-                       "parallelism": f"tp{world}",
+                       "parallelism": f"tp{world}", "allreduce": a.allreduce if world > 1 else None,
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
                        "mode": a.mode, "target_layers": tshape.n_layers,
                        "draft_layers": 0 if a.mode == "eagle" else dshape.n_layers},
@@ -426,6 +430,9 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     # CUDA graphs that hold NCCL calls go before the process group does
     engine.graph = None
     torch.cuda.synchronize()
+    if peer is not None:
+        barrier()   # no rank reads a peer buffer any more
+        peer.close()
 
 
 def main():

@@ -43,7 +43,8 @@ enum {
   TSDS_E_TIMEOUT = 5,     /* a device-side bounded wait gave up (status word) */
   TSDS_E_UNSUPPORTED = 6, /* no kernel instantiated for this configuration */
   TSDS_E_DEVICE = 7,      /* device query failed / not an sm_100 device */
-  TSDS_E_SCRATCH_LIMIT = 8 /* request larger than a built-in scratch area */
+  TSDS_E_SCRATCH_LIMIT = 8, /* request larger than a built-in scratch area */
+  TSDS_E_RUNTIME = 9        /* a CUDA runtime call (allocation, IPC mapping) failed */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -245,6 +246,41 @@ int tsds_argmax_merge(const float* vals, const int64_t* idx, int M, int tp, int6
                       int64_t* out, int out_stride, tsds_stream_t stream);
 int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shard,
                        tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Peer (NVLink) all-reduce of row-parallel partials, fused with the residual
+ * add: the TP exchange after the O and down projections without NCCL.
+ * Replaces the NCCL all-reduce + tsds_residual_add_f32 pair above.
+ *
+ * Each rank owns one peer buffer of tsds_peer_buffer_bytes(max_elems) bytes
+ * (tsds_peer_alloc: cudaMalloc, zero-filled), exports it with
+ * tsds_peer_export (tsds_peer_handle_bytes() bytes, a CUDA IPC handle) and
+ * maps every other rank's with tsds_peer_import (another process of the same
+ * node; close with tsds_peer_close, free its own with tsds_peer_free).
+ * Buffer layout: per-CTA call counters and flags in the first 16 KB, then two
+ * slots of max_elems fp32 at tsds_peer_slot_offset(max_elems, 0 / 1).
+ *
+ * tsds_peer_allreduce_residual: the partial [M][N] fp32 of every rank sits in
+ * slot `slot` of that rank's buffer (written there by tsds_linear_f32);
+ * x[M][N] bf16 = bf16(x + bf16(sum over ranks 0..tp-1 in order)), identical
+ * on every rank.  bufs: host array of tp device pointers, bufs[rank] this
+ * rank's own buffer, bufs[p] rank p's as mapped here.  Every rank must issue
+ * the same sequence of calls with the same M, N, and successive calls must
+ * alternate slots (a rank writes a slot again only two calls later).  The
+ * cross-rank wait is bounded (1 s): on timeout *status = TSDS_E_TIMEOUT and
+ * x is left unchanged.  tp <= 8, N % 4 == 0, M * N <= max_elems, x 8-byte
+ * aligned, buffers 16-byte aligned.
+ */
+size_t tsds_peer_buffer_bytes(int max_elems);
+size_t tsds_peer_slot_offset(int max_elems, int slot);
+size_t tsds_peer_handle_bytes(void);
+int tsds_peer_alloc(size_t bytes, void** buf);
+int tsds_peer_free(void* buf);
+int tsds_peer_export(const void* buf, void* handle);
+int tsds_peer_import(const void* handle, void** buf);
+int tsds_peer_close(void* buf);
+int tsds_peer_allreduce_residual(void* x, void* const* bufs, int rank, int tp, int slot, int M, int N,
+                                 int max_elems, int* status, tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Tree speculative decoding (EAGLE draft tree, verified in one target pass).

@@ -79,6 +79,10 @@ def extents(name, a):
         x, ldx, W, logits, am, stride, av, M, V, K, ws, wsb = a
         return [(0, ((M - 1) * ldx + K) * 2), (2, V * K * 2), (3, M * V * 2), (4, ((M - 1) * stride + 1) * 8),
                 (6, M * 4), (10, wsb)]
+    if name == "tsds_peer_allreduce_residual":
+        x, bufs, rank, tp, slot, M, N, max_elems, status = a
+        assert 0 <= rank < tp and slot in (0, 1) and M * N <= max_elems
+        return [(0, M * N * 2), (8, 4)]
     if name == "tsds_residual_add_f32":
         x, part, M, N = a
         return [(0, M * N * 2), (1, M * N * 4)]

@@ -1,7 +1,10 @@
-"""Tensor parallelism on 2 GPUs (NCCL): the TP=2 verify forward vs the
-oracle, and greedy speculative decoding (chain draft and EAGLE tree, whose
-commit compacts each rank's shard of the KV cache) == greedy autoregressive
-decoding under TP=2.  Skipped with fewer than 2 GPUs."""
+"""Tensor parallelism on 2 GPUs: the TP=2 verify forward vs the oracle, and
+greedy speculative decoding (chain draft and EAGLE tree, whose commit
+compacts each rank's shard of the KV cache) == greedy autoregressive
+decoding under TP=2, with the row-parallel all-reduces by NCCL or by the
+library's peer-memory kernel.  Skipped with fewer than 2 GPUs; the
+peer-memory variant runs only with TSDS_TEST_PEER=1 until it has been
+validated on GPUs."""
 import os
 import socket
 
@@ -15,7 +18,7 @@ pytestmark = pytest.mark.gpu
 SMALL = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=2, vocab=1000)
 
 
-def _worker(rank, port, q):
+def _worker(rank, port, q, allreduce):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -26,10 +29,12 @@ def _worker(rank, port, q):
         from tri_sds_b200.engine import AutoregressiveEngine, SpecEngine
         from tri_sds_b200.model import QwenModel
         from tri_sds_b200.shapes import QwenShape
-        from tri_sds_b200.tp import Comm
+        from tri_sds_b200.tp import Comm, PeerAllReduce
         ops.set_gemv_max_rows(0)
         dev = torch.device("cuda", rank)
         comm = Comm()
+        # one set of peer buffers for every TP model here (their calls run in stream order)
+        peer = PeerAllReduce(rank, 2, 2 * 26 * SMALL["hidden"]) if allreduce == "peer" else None
         oshape = oq.QwenShape(**SMALL)
         shape = QwenShape(**SMALL)
         w = oq.random_qwen_weights(oshape, seed=1, std=0.02)
@@ -37,7 +42,8 @@ def _worker(rank, port, q):
         g = torch.Generator().manual_seed(2)
         prompt = torch.randint(0, oshape.vocab, (B, P), generator=g)
         step = torch.randint(0, oshape.vocab, (B, T), generator=g)
-        m = QwenModel(shape, B, 128, B * T, device=dev, weights=w, tp_rank=rank, tp_size=2, comm=comm)
+        m = QwenModel(shape, B, 128, B * T, device=dev, weights=w, tp_rank=rank, tp_size=2, comm=comm,
+                      peer=peer)
         m.prefill(prompt)
         logits = torch.zeros(B * T, oshape.vocab, dtype=torch.bfloat16, device=dev)
         am = torch.zeros(B * T, dtype=torch.int64, device=dev)
@@ -49,17 +55,20 @@ def _worker(rank, port, q):
         wd = {**wt, "layers": wt["layers"][:1]}
         dshape = QwenShape(**{**SMALL, "n_layers": 1})
         K = 4
-        tgt = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        tgt = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
+                        peer=peer)
         drf = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_size=2, tp_layers=False, tp_vocab=False)
         spec, _ = SpecEngine(tgt, drf, K).generate(prompt, 16)
-        tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
+                         peer=peer)
         ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
         out.update(spec=spec, ar=ar)
         # EAGLE tree, greedy: the head replicated, the target TP=2
         from oracle import eagle as oe
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         we = oe.random_eagle_weights(oshape, seed=4, std=0.08)
-        tgt3 = QwenModel(shape, B, 128, B * 26, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm)
+        tgt3 = QwenModel(shape, B, 128, B * 26, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
+                         peer=peer)
         eng = EagleEngine(tgt3, EagleHead(tgt3, B, weights=we), greedy=True)
         espec, _ = eng.generate(prompt, 16)
         out.update(espec=espec)
@@ -67,6 +76,11 @@ def _worker(rank, port, q):
         eng.graph = None
         del eng
         torch.cuda.synchronize()
+        for mdl in (m, tgt, tgt2, tgt3):
+            mdl.check_status()
+        if peer is not None:
+            dist.barrier()   # neither rank reads the other's buffer any more
+            peer.close()
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e)))
@@ -75,13 +89,18 @@ def _worker(rank, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_verify_and_lossless_spec():
+@pytest.mark.parametrize("allreduce", [
+    "nccl",
+    pytest.param("peer", marks=pytest.mark.skipif(os.environ.get("TSDS_TEST_PEER") != "1",
+                                                  reason="peer all-reduce: set TSDS_TEST_PEER=1")),
+])
+def test_tp2_verify_and_lossless_spec(allreduce):
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(daemon=True, target=_worker, args=(r, port, q)) for r in range(2)]
+    procs = [ctx.Process(daemon=True, target=_worker, args=(r, port, q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     try:

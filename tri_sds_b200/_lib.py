@@ -55,6 +55,15 @@ SIGNATURES = {
     "tsds_residual_add_f32": (_I, [_P, _P, _I, _I, _P]),
     "tsds_argmax_merge": (_I, [_P, _P, _I, _I, ctypes.c_int64, _P, _I, _P]),
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
+    "tsds_peer_buffer_bytes": (_Z, [_I]),
+    "tsds_peer_slot_offset": (_Z, [_I, _I]),
+    "tsds_peer_handle_bytes": (_Z, []),
+    "tsds_peer_alloc": (_I, [_Z, ctypes.POINTER(_P)]),
+    "tsds_peer_free": (_I, [_P]),
+    "tsds_peer_export": (_I, [_P, _P]),
+    "tsds_peer_import": (_I, [_P, ctypes.POINTER(_P)]),
+    "tsds_peer_close": (_I, [_P]),
+    "tsds_peer_allreduce_residual": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "tsds_accept_greedy": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "tsds_gather_ids": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
 }

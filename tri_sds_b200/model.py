@@ -121,7 +121,8 @@ class QwenModel:
     def __init__(self, shape: QwenShape, batch: int, max_seq: int, max_rows: int, device="cuda",
                  weights: dict | None = None, seed: int = 0, split_keys: int = 128, qk_norm: bool | None = None,
                  share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
-                 tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None):
+                 tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None,
+                 peer=None):
         self.shape = shape
         # tensor parallelism: layers and/or vocabulary sharded over tp_size ranks
         self.tp_rank = tp_rank
@@ -130,6 +131,12 @@ class QwenModel:
         if comm is None:
             comm = share_embeddings.comm if share_embeddings is not None else LocalComm()
         self.comm = comm
+        # tp.PeerAllReduce: the row-parallel all-reduces run as this library's
+        # peer-memory kernel instead of NCCL's (layers sharded only)
+        self.peer = peer
+        if peer is not None:
+            assert tp_layers and tp_size > 1 and (peer.rank, peer.size) == (tp_rank, tp_size)
+            assert peer.max_elems >= max_rows * shape.hidden
         self.lshape = replace(shape, **local_dims(shape, self.layer_tp)) if self.layer_tp > 1 else shape
         self.vocab_local = shape.vocab // self.vocab_tp
         self.batch = batch
@@ -233,11 +240,21 @@ class QwenModel:
         st = self.starts if starts is None else starts
         ps = self.positions if positions is None else positions
         tp = self.layer_tp > 1
+        n_peer = [0]
 
         def row_parallel(src, ld_src, w, k_in):
             if not tp:
                 pl.add("tsds_linear_residual", _p(src), ld_src, _p(w), _p(xb), _p(xb), s.hidden, M, s.hidden, k_in,
                        _p(lw), lb)
+                return
+            if self.peer is not None:
+                # the partial goes straight into this rank's peer slot; calls alternate slots
+                slot = n_peer[0] % 2
+                n_peer[0] += 1
+                pl.add("tsds_linear_f32", _p(src), ld_src, _p(w), self.peer.slot_ptr(slot), s.hidden, M, s.hidden,
+                       k_in, _p(lw), lb)
+                pl.add("tsds_peer_allreduce_residual", _p(xb), self.peer.bufs, self.tp_rank, self.layer_tp, slot, M,
+                       s.hidden, self.peer.max_elems, _p(self.status))
                 return
             part = self.part[:M]
             pl.add("tsds_linear_f32", _p(src), ld_src, _p(w), _p(part), s.hidden, M, s.hidden, k_in, _p(lw), lb)
@@ -262,6 +279,7 @@ class QwenModel:
             pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), ls.intermediate, M,
                    ls.intermediate, s.hidden, _p(lw), lb)
             row_parallel(self.h, ls.intermediate, L.w_d, ls.intermediate)
+        assert n_peer[0] % 2 == 0   # the next plan run starts on slot 0 again
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,

@@ -15,13 +15,19 @@ Megatron-style split of a Qwen3 decoder layer across ``tp`` ranks:
 Exchange per layer: two all-reduces (sum) of the fp32 partials of O and
 down, followed by the residual add with the reference's rounding; at the
 LM head, an all-gather of each row's (value, index) argmax candidate (and,
-when full logits are needed, of the logits shards).  Collectives are NCCL's
-through ``torch.distributed``.
+when full logits are needed, of the logits shards).  The all-gathers are
+NCCL's through ``torch.distributed``; the all-reduces are NCCL's too, or
+(``PeerAllReduce``) this library's one-shot kernel over NVLink peer memory,
+fused with the residual add.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 def local_dims(shape, tp: int) -> dict:
@@ -77,3 +83,54 @@ class LocalComm:
 
     def all_gather(self, out, inp):
         out.copy_(inp)
+
+
+class PeerAllReduce:
+    """Peer buffers of the ranks of one node, for tsds_peer_allreduce_residual.
+
+    Allocates this rank's buffer (``max_elems`` fp32 per slot), exchanges
+    CUDA IPC handles over ``group`` (any backend: the handles are bytes) and
+    maps every other rank's buffer.  ``bufs`` is the host pointer table the
+    kernel takes; ``slot_ptr(s)`` is where this rank's row-parallel GEMM
+    writes its partial for a call on slot s.  Every rank must construct it at
+    the same point (the exchange is a collective)."""
+
+    def __init__(self, rank: int, size: int, max_elems: int, group=None):
+        assert 1 <= size <= 8 and 0 <= rank < size
+        self.rank, self.size = rank, size
+        self.max_elems = (max_elems + 63) // 64 * 64
+        self._own = ctypes.c_void_p()
+        self._imported: list[ctypes.c_void_p] = []
+        _lib.call("tsds_peer_alloc", _lib.query("tsds_peer_buffer_bytes", self.max_elems), ctypes.byref(self._own))
+        try:
+            hb = _lib.query("tsds_peer_handle_bytes")
+            mine = (ctypes.c_uint8 * hb)()
+            _lib.call("tsds_peer_export", self._own, mine)
+            handles = [None] * size
+            dist.all_gather_object(handles, bytes(mine), group=group)
+            ptrs = []
+            for p, h in enumerate(handles):
+                if p == rank:
+                    ptrs.append(self._own.value)
+                    continue
+                mapped = ctypes.c_void_p()
+                _lib.call("tsds_peer_import", (ctypes.c_uint8 * hb).from_buffer_copy(h), ctypes.byref(mapped))
+                self._imported.append(mapped)
+                ptrs.append(mapped.value)
+            self.bufs = (ctypes.c_void_p * size)(*ptrs)
+        except BaseException:
+            self.close()
+            raise
+
+    def slot_ptr(self, slot: int) -> ctypes.c_void_p:
+        return ctypes.c_void_p(self._own.value + _lib.query("tsds_peer_slot_offset", self.max_elems, slot))
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after every kernel
+        that uses them has finished on every rank)."""
+        for m in self._imported:
+            _lib.call("tsds_peer_close", m)
+        self._imported = []
+        if self._own.value:
+            _lib.call("tsds_peer_free", self._own)
+            self._own = ctypes.c_void_p()
