@@ -61,6 +61,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--fused-layers", action="store_true",
+                    help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v (N = 1)")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
@@ -280,14 +282,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         if a.allreduce == "peer":
             peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden)
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
-                       tp_size=world, comm=comm, peer=peer)
+                       tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers)
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         head = EagleHead(target, B, seed=2000)
         engine = EagleEngine(target, head, greedy=a.greedy, seed=3000)
     else:
         draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
-                          tp_layers=False, tp_vocab=False)
+                          tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers)
         engine = SpecEngine(target, draft, K)
     # the same prompt on every rank: tensor-parallel ranks process the same tokens
     prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7))
@@ -411,6 +413,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": B, "seq_len": P,
                        "parallelism": f"tp{world}", "allreduce": a.allreduce if world > 1 else None,
+                       "fused_layers": bool(target.fused_layers),
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
                        "mode": a.mode, "target_layers": tshape.n_layers,
                        "draft_layers": 0 if a.mode == "eagle" else dshape.n_layers},

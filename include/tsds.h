@@ -248,6 +248,68 @@ int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shar
                        tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused layer: several dependent phases of decoder layers in ONE persistent launch
+ * over the same M token rows, e.g. O (+residual) -> RMSNorm -> gate/up
+ * (+SwiGLU) -> down (+residual) -> RMSNorm -> q/k/v (+QK-norm + RoPE + K/V
+ * cache write).  GEMM phases are the tcgen05 skinny GEMM of tsds_linear*
+ * (same tiles, same split-tile reduction, same rounding); RMSNorm phases are
+ * tsds_rms_norm's arithmetic; the QKROPE epilogue is tsds_qk_norm_rope_kv's.
+ * Phases are separated by an in-kernel grid barrier; weight tiles of the next
+ * GEMM phase stream in while the previous phase finishes.  Replaces the
+ * per-op launches of fused_qwen_decode.py:151-309 / qwen_model.py:104-144
+ * (one launch instead of six) - no counterpart in the reference.
+ *
+ * Phase descriptors (host array, n_phases <= 8):
+ *  GEMM: out[m][j] = epilogue(sum_k w[j][k] * x[m][k]) for m < M, j < n_out;
+ *        epi TSDS_EPI_STORE (bf16), _RESIDUAL (bf16(res + bf16(acc)), res may
+ *        be out), _SWIGLU (w = [gate; up], 2*n_out rows), _STORE_F32 (fp32),
+ *        _QKROPE (n_out = (Hq + 2*Hkv) * 128; outputs as tsds_qk_norm_rope_kv
+ *        with the parameters in *qr; out unused; at most one such phase).
+ *  NORM: out[m][0:K] = RMSNorm(x[m][0:K]) * w, eps.
+ * Workspace: tsds_fused_layer_workspace_bytes(M) bytes, 16-byte aligned, zero-filled
+ * once (every launch leaves its counters zero again); word 0 is the status
+ * word (TSDS_E_TIMEOUT after a bounded device wait gave up).  M <= 256.
+ */
+enum { TSDS_PHASE_GEMM = 0, TSDS_PHASE_NORM = 1 };
+enum {
+  TSDS_EPI_STORE = 0,
+  TSDS_EPI_RESIDUAL = 1,
+  TSDS_EPI_SWIGLU = 2,
+  TSDS_EPI_STORE_F32 = 4,
+  TSDS_EPI_QKROPE = 5
+};
+typedef struct {
+  int kind;          /* TSDS_CHAIN_* */
+  int epi;           /* GEMM: TSDS_EPI_* */
+  const void* x;     /* GEMM: activations [M][K] bf16; NORM: input rows */
+  int ldx;           /* row stride of x (elements, multiple of 8) */
+  int K;             /* GEMM: reduction length; NORM: row length */
+  const void* w;     /* GEMM: weights [n_out][K] (SWIGLU [2*n_out][K]); NORM: gain [K] */
+  int n_out;         /* GEMM output columns */
+  int res_ld;        /* RESIDUAL: row stride of res */
+  const void* res;   /* RESIDUAL: residual rows */
+  void* out;         /* output rows (fp32 for STORE_F32) */
+  int ldo;           /* row stride of out */
+  float eps;         /* NORM */
+} tsds_fused_phase;
+typedef struct {
+  const void* q_norm_w;          /* [128] bf16, or NULL: no QK-norm */
+  const void* k_norm_w;
+  const void* cos;               /* [rope_len][64] bf16 */
+  const void* sin;
+  const int32_t* positions;      /* [M] */
+  const int32_t* starts;         /* [M / T] cache row of each sequence's first new token */
+  void* q_out;                   /* [M][Hq][128] bf16 */
+  void* k_cache;                 /* [M / T][Hkv][S][128] bf16 */
+  void* v_cache;
+  int T, Hq, Hkv, S, rope_len;
+  float eps;
+} tsds_qk_rope;
+size_t tsds_fused_layer_workspace_bytes(int M);
+int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
+               void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Peer (NVLink) all-reduce of row-parallel partials, fused with the residual
  * add: the TP exchange after the O and down projections without NCCL.
  * Replaces the NCCL all-reduce + tsds_residual_add_f32 pair above.

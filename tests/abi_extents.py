@@ -102,15 +102,43 @@ def extents(name, a):
     raise AssertionError(f"no extent rule for {name}")
 
 
+def fused_extents(a):
+    """tsds_fused_layer with its phases / rope given as dicts (see _fused_args):
+    [(ref, bytes)] pairs instead of argument indices."""
+    phases, n, M, rope, ws, wsb = a
+    out = [(ws, wsb)]
+    for ph in phases[:n]:
+        if ph["kind"] == 1:   # NORM
+            K = ph["K"]
+            out += [(ph["x"], ((M - 1) * ph["ldx"] + K) * 2), (ph["w"], K * 2), (ph["out"], ((M - 1) * ph["ldo"] + K) * 2)]
+            continue
+        epi, K, n_out = ph["epi"], ph["K"], ph["n_out"]
+        rows_w = 2 * n_out if epi == 2 else n_out
+        out += [(ph["x"], ((M - 1) * ph["ldx"] + K) * 2), (ph["w"], rows_w * K * 2)]
+        if epi != 5:
+            out.append((ph["out"], ((M - 1) * ph["ldo"] + n_out) * (4 if epi == 4 else 2)))
+        if epi == 1:
+            out.append((ph["res"], ((M - 1) * ph["res_ld"] + n_out) * 2))
+        if epi == 5:
+            r = rope
+            assert n_out == (r["Hq"] + 2 * r["Hkv"]) * 128 and M % r["T"] == 0
+            B = M // r["T"]
+            out += [(r["q_norm_w"], 256), (r["k_norm_w"], 256), (r["cos"], r["rope_len"] * 128),
+                    (r["sin"], r["rope_len"] * 128), (r["positions"], M * 4), (r["starts"], B * 4),
+                    (r["q_out"], M * r["Hq"] * 256), (r["k_cache"], B * r["Hkv"] * r["S"] * 256),
+                    (r["v_cache"], B * r["Hkv"] * r["S"] * 256)]
+    return out
+
+
 def check_call(name, args):
     """Assert every pointer of one recorded call reaches its extent; returns
     the number of pointers checked."""
     n = 0
-    for i, need in extents(name, args):
-        ref = args[i]
+    pairs = fused_extents(args) if name == "tsds_fused_layer" else [(args[i], need) for i, need in extents(name, args)]
+    for ref, need in pairs:
         if ref is None:
             continue
-        assert isinstance(ref, TRef), (name, i, ref)
-        assert need <= ref.bytes_left(), (name, i, need, ref.bytes_left())
+        assert isinstance(ref, TRef), (name, n, ref)
+        assert need <= ref.bytes_left(), (name, n, need, ref.bytes_left())
         n += 1
     return n

@@ -1,0 +1,141 @@
+"""The fused-layer kernel's host side on CPU (nothing runs on a device).
+
+* plans: one attention launch and one fused launch per layer, with the
+  phases of the per-op plan in the same order (the first is layer 0's
+  norm -> q/k/v, the last ends with the down projection);
+* every pointer a phase or its RoPE block hands the library reaches the
+  extent its sizes imply (pointers replaced by references to their tensors);
+* the ctypes structures have the C layout of include/tsds.h (compiled with
+  the host compiler);
+* the entry point rejects bad descriptors before any CUDA call."""
+import ctypes
+import os
+import subprocess
+
+import pytest
+import torch
+
+from abi_extents import TRef, check_call
+from tri_sds_b200.shapes import QwenShape
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SHAPE = QwenShape(hidden=256, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=1024, n_layers=3, vocab=1024)
+
+
+@pytest.fixture()
+def recorded(monkeypatch):
+    import tri_sds_b200.eagle as eagle
+    import tri_sds_b200.engine as engine
+    import tri_sds_b200.model as model
+    ref = lambda t: None if t is None else TRef(t)  # noqa: E731
+    for mod in (model, eagle, engine):
+        monkeypatch.setattr(mod, "_p", ref)
+    monkeypatch.setattr(model, "_fused_args", lambda phases, rope, M, ws, wsb: (phases, len(phases), M, rope, ws, wsb))
+    yield
+
+
+def _phase_names(phases):
+    names = {(0, 0): "store", (0, 1): "res", (0, 2): "swiglu", (0, 4): "f32", (0, 5): "qkrope"}
+    return ["norm" if ph["kind"] == 1 else names[(0, ph["epi"])] for ph in phases]
+
+
+@pytest.mark.parametrize("B,T", [(1, 26), (8, 26), (2, 5)])
+def test_fused_plan_shape_and_extents(recorded, B, T):
+    from tri_sds_b200.model import QwenModel
+    m = QwenModel(SHAPE, B, 96, B * T, device="cpu", fused_layers=True)
+    pl = m.layers_plan(B, T)
+    names = [n for n, fn, a in pl.calls]
+    L = SHAPE.n_layers
+    assert names == ["tsds_fused_layer"] + ["tsds_verify_attention", "tsds_fused_layer"] * L
+    fused = [a for n, fn, a in pl.calls if n == "tsds_fused_layer"]
+    assert _phase_names(fused[0][0]) == ["norm", "qkrope"]
+    for a in fused[1:-1]:
+        assert _phase_names(a[0]) == ["res", "norm", "swiglu", "res", "norm", "qkrope"]
+    assert _phase_names(fused[-1][0]) == ["res", "norm", "swiglu", "res"] and fused[-1][3] is None
+    # each layer's rope block writes that layer's caches
+    for i, a in enumerate(fused[:-1]):
+        assert a[3]["k_cache"].t.data_ptr() == m.k_cache[i].data_ptr()
+        assert a[3]["T"] == T and a[2] == B * T
+    for n, fn, a in pl.calls:
+        assert check_call(n, a) > 0
+    # the per-op plan of the same model: 8 library calls per layer
+    m.fused_layers = False
+    assert len(m.layers_plan(B, T).calls) == 8 * L
+
+
+def test_eagle_engine_plans_with_fused_layers(recorded):
+    from tri_sds_b200.eagle import EagleEngine, EagleHead
+    from tri_sds_b200.model import QwenModel
+    t = QwenModel(SHAPE, 2, 96, 2 * 26, device="cpu", fused_layers=True)
+    head = EagleHead(t, 2)
+    eng = EagleEngine(t, head, use_graph=False)
+    n_fused = sum(1 for n, fn, a in eng.plan.calls if n == "tsds_fused_layer")
+    assert n_fused >= SHAPE.n_layers + 1
+    for n, fn, a in eng.plan.calls:
+        if fn is not None:
+            check_call(n, a)
+
+
+def test_tensor_parallel_model_keeps_the_per_op_plan():
+    from tri_sds_b200.model import QwenModel
+
+    class _Comm:
+        rank, size = 0, 2
+
+    m = QwenModel(SHAPE, 1, 96, 26, device="cpu", tp_rank=0, tp_size=2, comm=_Comm(), fused_layers=True)
+    assert not m.fused_layers
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    from tri_sds_b200 import _lib
+    src = tmp_path / "layout.c"
+    src.write_text(f'''#include <stddef.h>
+#include <stdio.h>
+#include "{ROOT}/include/tsds.h"
+int main(void) {{
+  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(tsds_fused_phase), offsetof(tsds_fused_phase, w),
+         offsetof(tsds_fused_phase, res), offsetof(tsds_fused_phase, eps), sizeof(tsds_qk_rope),
+         offsetof(tsds_qk_rope, T));
+  return 0;
+}}
+''')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    P, Q = _lib.FusedPhase, _lib.QkRope
+    assert got == [ctypes.sizeof(P), P.w.offset, P.res.offset, P.eps.offset, ctypes.sizeof(Q), Q.T.offset]
+
+
+def test_entry_point_rejects_bad_descriptors():
+    """Every descriptor here fails a host-side check, so nothing is launched
+    (the pointers are not device memory) on a machine with or without a GPU."""
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    M = 26
+    nb = lib.tsds_fused_layer_workspace_bytes(M)
+    assert nb > 0 and lib.tsds_fused_layer_workspace_bytes(0) == 0 and lib.tsds_fused_layer_workspace_bytes(257) == 0
+    ws = ctypes.c_void_p(0x100000)
+
+    def ph(**kw):
+        d = dict(kind=0, epi=0, x=0x1000, ldx=256, K=256, w=0x2000, n_out=256, res_ld=0, res=None, out=0x3000,
+                 ldo=256, eps=0.0)
+        d.update(kw)
+        return _lib.FusedPhase(**d)
+
+    def run(phases, m=M, qr=None, wsb=nb):
+        arr = (_lib.FusedPhase * max(1, len(phases)))(*phases)
+        return lib.tsds_fused_layer(arr, len(phases), m, qr, ws, wsb, None)
+
+    assert run([]) == 1                                   # no phase
+    assert run([ph()] * 9) == 1                           # more than 8
+    assert run([ph()], m=0) == 1 and run([ph()], m=257) == 1
+    assert run([ph()], wsb=nb - 1) == 4                   # workspace too small
+    assert run([ph(epi=3)]) == 1                          # the LM-head epilogue is not a fused phase
+    assert run([ph(epi=1)]) == 1                          # residual without res
+    assert run([ph(epi=5)]) == 1                          # QKROPE without its parameters
+    qr = _lib.QkRope(cos=1, sin=1, positions=1, starts=1, q_out=1, k_cache=1, v_cache=1, T=26, Hq=4, Hkv=2, S=64,
+                     rope_len=64)
+    assert run([ph(epi=5, n_out=1152)], qr=ctypes.pointer(qr)) == 1    # n_out != (Hq + 2 Hkv) * 128
+    assert run([ph(kind=1, K=250)]) == 1                  # norm row not a multiple of 8
+    assert run([ph(kind=7)]) == 1
+    assert run([ph(x=0x1008)]) == 2                       # x not 16-byte aligned

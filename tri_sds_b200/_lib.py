@@ -18,6 +18,23 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
 
+PHASE_GEMM, PHASE_NORM = 0, 1
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32, EPI_QKROPE = 0, 1, 2, 4, 5
+
+
+class FusedPhase(ctypes.Structure):
+    """tsds_fused_phase (include/tsds.h)."""
+    _fields_ = [("kind", _I), ("epi", _I), ("x", _P), ("ldx", _I), ("K", _I), ("w", _P), ("n_out", _I),
+                ("res_ld", _I), ("res", _P), ("out", _P), ("ldo", _I), ("eps", _F)]
+
+
+class QkRope(ctypes.Structure):
+    """tsds_qk_rope (include/tsds.h)."""
+    _fields_ = [("q_norm_w", _P), ("k_norm_w", _P), ("cos", _P), ("sin", _P), ("positions", _P), ("starts", _P),
+                ("q_out", _P), ("k_cache", _P), ("v_cache", _P), ("T", _I), ("Hq", _I), ("Hkv", _I), ("S", _I),
+                ("rope_len", _I), ("eps", _F)]
+
+
 # name -> (restype, argtypes); mirrors include/tsds.h
 SIGNATURES = {
     "tsds_status_string": (ctypes.c_char_p, [_I]),
@@ -55,6 +72,8 @@ SIGNATURES = {
     "tsds_residual_add_f32": (_I, [_P, _P, _I, _I, _P]),
     "tsds_argmax_merge": (_I, [_P, _P, _I, _I, ctypes.c_int64, _P, _I, _P]),
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
+    "tsds_fused_layer_workspace_bytes": (_Z, [_I]),
+    "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _Z, _P]),
     "tsds_peer_buffer_bytes": (_Z, [_I]),
     "tsds_peer_slot_offset": (_Z, [_I, _I]),
     "tsds_peer_handle_bytes": (_Z, []),

@@ -1,6 +1,7 @@
 // Row-wise kernels of the verify step: embedding gather, RMSNorm,
 // QK-norm + RoPE + KV-cache write, chain bookkeeping, greedy acceptance.
 #include "common.cuh"
+#include "rowops.cuh"
 
 using namespace tsds;
 
@@ -119,18 +120,6 @@ extern "C" int tsds_prep_chain(const int32_t* base, int offset, int B, int T, in
 // RoPE follows qwen_model.py:17-24 in bf16: out1 = bf16(bf16(x1*c) - bf16(x2*s)),
 // out2 = bf16(bf16(x2*c) + bf16(x1*s)) with bf16 tables (qwen_model.py:8-14).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void qk_norm_pair(float (&v)[4], const bf16* __restrict__ gw, int lane, float eps) {
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
-  const float rstd = 1.0f / sqrtf(ss / 128.0f + eps);
-  const uint32_t g0 = *reinterpret_cast<const uint32_t*>(gw + 2 * lane);
-  const uint32_t g1 = *reinterpret_cast<const uint32_t*>(gw + 64 + 2 * lane);
-  v[0] = rbf(v[0] * rstd * bf_lo(g0));
-  v[1] = rbf(v[1] * rstd * bf_hi(g0));
-  v[2] = rbf(v[2] * rstd * bf_lo(g1));
-  v[3] = rbf(v[3] * rstd * bf_hi(g1));
-}
-
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const bf16* __restrict__ qkv, const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w,
     const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const int32_t* __restrict__ positions,
@@ -166,14 +155,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   const bool is_q = h < Hq;
   const bf16* nw = is_q ? q_norm_w : k_norm_w;
   if (nw) qk_norm_pair(v, nw, lane, eps);
-  const uint32_t cw = *reinterpret_cast<const uint32_t*>(cos_t + (int64_t)pos * (D / 2) + 2 * lane);
-  const uint32_t sw = *reinterpret_cast<const uint32_t*>(sin_t + (int64_t)pos * (D / 2) + 2 * lane);
-  const float c0 = bf_lo(cw), c1 = bf_hi(cw), s0 = bf_lo(sw), s1 = bf_hi(sw);
-  // pairs (v[0], v[2]) at index 2l and (v[1], v[3]) at index 2l+1
-  const float o0 = rbf(rbf(v[0] * c0) - rbf(v[2] * s0));
-  const float o2 = rbf(rbf(v[2] * c0) + rbf(v[0] * s0));
-  const float o1 = rbf(rbf(v[1] * c1) - rbf(v[3] * s1));
-  const float o3 = rbf(rbf(v[3] * c1) + rbf(v[1] * s1));
   bf16* dst;
   if (is_q) {
     dst = q_out + ((int64_t)m * Hq + h) * D;
@@ -181,8 +162,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const int kvh = h - Hq;
     dst = k_cache + (((int64_t)b * Hkv + kvh) * S + row_in_seq) * D;
   }
-  *reinterpret_cast<uint32_t*>(dst + 2 * lane) = pack_bf2(o0, o1);
-  *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = pack_bf2(o2, o3);
+  rope_store(v, cos_t, sin_t, pos, lane, dst);
 }
 
 extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,

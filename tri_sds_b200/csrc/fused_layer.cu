@@ -1,0 +1,752 @@
+// Fused-layer kernel: one persistent tcgen05 launch runs a sequence
+// of dependent phases over the same M token rows, e.g. for a decoder layer
+//
+//   O-proj (+residual) -> RMSNorm -> gate/up (+SwiGLU) -> down (+residual)
+//   -> RMSNorm (next layer) -> q/k/v (+QK-norm, RoPE, K/V cache write)
+//
+// Each GEMM phase is the skinny GEMM of gemm_tc.cu (swap-AB, TMA weight and
+// X tiles, tcgen05.mma into double-buffered TMEM accumulators, stream-K over
+// all CTAs, deterministic split-tile reduction); an RMSNorm phase normalises
+// M rows on the epilogue warps.  Phases are separated by a grid barrier (an
+// arrival counter; every CTA of the one resident wave arrives after its share
+// of a phase is written).  What a single kernel buys over one launch per
+// phase: the TMA warp requests the next GEMM phase's weight tiles as soon as
+// ring slots free up - weights never depend on the previous phase - and only
+// the activation tiles wait for the barrier, so HBM keeps streaming across
+// phase boundaries instead of draining at every kernel edge.
+//
+// Data produced inside the launch is read with L2-coherent loads (ld.cg) or
+// by TMA after a proxy fence, never through the non-coherent path.  Every
+// wait is bounded (2 s): a timeout records TSDS_E_TIMEOUT in the status word
+// and the CTA unwinds.  No TMA multicast, no peer memory.
+#include "common.cuh"
+#include "linear.cuh"
+#include "rowops.cuh"
+#include "tc_core.cuh"
+
+#include <string.h>
+
+using namespace tsds;
+using namespace tsds::tc;
+
+static_assert((int)TSDS_EPI_STORE == (int)EPI_STORE && (int)TSDS_EPI_RESIDUAL == (int)EPI_RESIDUAL &&
+                  (int)TSDS_EPI_SWIGLU == (int)EPI_SWIGLU && (int)TSDS_EPI_STORE_F32 == (int)EPI_STORE_F32 &&
+                  (int)TSDS_EPI_QKROPE == (int)EPI_QKROPE,
+              "ABI epilogue codes");
+
+namespace {
+
+constexpr int CH_THREADS = 192;
+constexpr int CH_MAX_PHASES = 8;
+constexpr int CH_MAX_COUNTERS = 8192;  // arrival + departure counters of all GEMM phases
+constexpr int CH_SMEM_BUDGET = 220 * 1024;
+constexpr int SMEM_PER_SM = 233472;
+constexpr int SMEM_RESERVE = 8192;
+constexpr uint64_t CH_WAIT_NS = 2000000000ull;
+enum { CH_GEMM = 0, CH_NORM = 1 };
+
+struct ChPhase {
+  int kind, epi;
+  // GEMM: out[m][j] (ldo) from weights [n_out (x2 for SwiGLU)][K] and X [M][K]
+  int n_out, K, KT, tiles;
+  uint32_t W;                  // tiles x KT (host: W * P < 2^32)
+  int up_off, ldo, res_ld, ctr;  // ctr: arrival counters at counters[ctr], departures at + tiles
+  const bf16* res;
+  bf16* out;
+  // NORM: out[m][0:n] (ldo) = RMSNorm(x[m][0:n]) * w
+  const bf16* x;
+  const bf16* w;
+  int n, ldx;
+  float eps;
+};
+
+struct ChRope {  // EPI_QKROPE: tile t = head slot t of [q heads | k heads | v heads]
+  const bf16* qn;
+  const bf16* kn;
+  const bf16* cos_t;
+  const bf16* sin_t;
+  const int32_t* pos;
+  const int32_t* starts;
+  bf16* q_out;
+  bf16* k_cache;
+  bf16* v_cache;
+  int T, Hq, Hkv, S, rope_len;
+  float eps;
+};
+
+struct ChParams {
+  int M, Npad, P, nph, stages, b_stage_bytes, tmem_cols;
+  uint32_t idesc;
+  float* ws;
+  int* counters;
+  int* gbar;  // [0] phase arrivals, [1] departures
+  int32_t* status;
+  ChPhase ph[CH_MAX_PHASES];
+  ChRope qr;
+};
+
+struct ChMaps {
+  CUtensorMap a[CH_MAX_PHASES];
+  CUtensorMap b[CH_MAX_PHASES];
+};
+
+struct ChSmem {
+  uint64_t full_bar[MAX_STAGES];
+  uint64_t empty_bar[MAX_STAGES];
+  uint64_t tfull_bar[2];
+  uint64_t tempty_bar[2];
+  uint32_t tmem_base;
+  int abort;
+  int go;
+  int last;
+  float xch[64][17];  // SwiGLU: up rows; QKROPE: a [128][8] exchange of 8 columns
+  float red[8];
+};
+
+__device__ __forceinline__ bool wait_count(const int* c, int target) {
+  if (ld_acquire(c) >= target) return true;
+  const uint64_t t0 = global_ns();
+  while (ld_acquire(c) < target) {
+    if (global_ns() - t0 > CH_WAIT_NS) return false;
+  }
+  return true;
+}
+
+// generic-proxy writes of this thread (and those it observed) before later
+// async-proxy (TMA) reads of the same global memory
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ float ldcg_bf(const bf16* p) {
+  return __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(p)) << 16);
+}
+
+// ---- epilogue of 16 accumulator columns m0..m0+15 of tile row r -------------
+template <int EPI>
+__device__ __forceinline__ void ch_finish(const ChParams& p, const ChPhase& ph, ChSmem& sh, int t, int r, int m0,
+                                          const float (&v)[16]) {
+  if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32) {
+    const int j = t * TILE_J + r;
+    if (j < ph.n_out) {
+      float rv[16];
+      if constexpr (EPI == EPI_RESIDUAL) {  // read before any store: out may alias res
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+          rv[jj] = m0 + jj < p.M ? ldcg_bf(ph.res + (int64_t)(m0 + jj) * ph.res_ld + j) : 0.f;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int m = m0 + jj;
+        if (m < p.M) {
+          const int64_t o = (int64_t)m * ph.ldo + j;
+          if constexpr (EPI == EPI_STORE_F32)
+            reinterpret_cast<float*>(ph.out)[o] = v[jj];
+          else if constexpr (EPI == EPI_STORE)
+            ph.out[o] = f2bf(v[jj]);
+          else
+            ph.out[o] = f2bf(rv[jj] + rbf(v[jj]));
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    if (r >= 64) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) sh.xch[r - 64][jj] = rbf(v[jj]);
+    }
+    epi_bar();
+    const int j = t * 64 + r;
+    if (r < 64 && j < ph.n_out) {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int m = m0 + jj;
+        if (m < p.M) {
+          const float g = rbf(v[jj]);
+          const float s = rbf(g / (1.0f + expf(-g)));
+          ph.out[(int64_t)m * ph.ldo + j] = f2bf(s * sh.xch[r][jj]);
+        }
+      }
+    }
+    epi_bar();
+  } else {  // EPI_QKROPE: the arithmetic of qk_norm_rope_kv_kernel, lane for lane
+    const ChRope& q = p.qr;
+    constexpr int D = 128;
+    float(*xq)[8] = reinterpret_cast<float(*)[8]>(&sh.xch[0][0]);
+    const int w = r >> 5, lane = r & 31;
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) xq[r][jj] = rbf(v[half * 8 + jj]);  // the bf16 q/k/v projection
+      epi_bar();
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = w * 2 + cc;
+        const int m = m0 + half * 8 + col;
+        if (m >= p.M) continue;  // uniform over the warp
+        const int b = m / q.T, tt = m - b * q.T;
+        const int row_in_seq = q.starts[b] + tt;
+        const int pos = q.pos[m];
+        if (row_in_seq < 0 || row_in_seq >= q.S || pos < 0 || pos >= q.rope_len) continue;
+        float e[4] = {xq[2 * lane][col], xq[2 * lane + 1][col], xq[64 + 2 * lane][col], xq[65 + 2 * lane][col]};
+        if (t >= q.Hq + q.Hkv) {  // v head: into the cache as is
+          const int kvh = t - q.Hq - q.Hkv;
+          bf16* dst = q.v_cache + (((int64_t)b * q.Hkv + kvh) * q.S + row_in_seq) * D;
+          *reinterpret_cast<uint32_t*>(dst + 2 * lane) = pack_bf2(e[0], e[1]);
+          *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = pack_bf2(e[2], e[3]);
+          continue;
+        }
+        const bool is_q = t < q.Hq;
+        const bf16* nw = is_q ? q.qn : q.kn;
+        if (nw) qk_norm_pair(e, nw, lane, q.eps);
+        bf16* dst = is_q ? q.q_out + ((int64_t)m * q.Hq + t) * D
+                         : q.k_cache + (((int64_t)b * q.Hkv + (t - q.Hq)) * q.S + row_in_seq) * D;
+        rope_store(e, q.cos_t, q.sin_t, pos, lane, dst);
+      }
+      epi_bar();
+    }
+  }
+}
+
+// ---- RMSNorm phase (epilogue warps): rows pc, pc + P, ... ----------------------
+// The arithmetic of rms_norm_kernel (256 threads) with 128 threads: thread r
+// plays virtual threads r and r + 128, so every partial sum and the order of
+// the block reduction are the same.
+__device__ void ch_norm(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc, int r) {
+  const int eq = r >> 5, lane = r & 31;
+  const int n8 = ph.n / 8;
+  for (int m = pc; m < p.M; m += p.P) {
+    const bf16* xr = ph.x + (int64_t)m * ph.ldx;
+    bf16* orow = ph.out + (int64_t)m * ph.ldo;
+    float ssa = 0.f, ssb = 0.f;
+    for (int c = r; c < n8; c += 256) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xr + c * 8));
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = bf_lo(u[i]), b = bf_hi(u[i]);
+        ssa = fmaf(a, a, ssa);
+        ssa = fmaf(b, b, ssa);
+      }
+    }
+    for (int c = r + 128; c < n8; c += 256) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xr + c * 8));
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = bf_lo(u[i]), b = bf_hi(u[i]);
+        ssb = fmaf(a, a, ssb);
+        ssb = fmaf(b, b, ssb);
+      }
+    }
+    ssa = warp_sum(ssa);
+    ssb = warp_sum(ssb);
+    if (lane == 0) {
+      sh.red[eq] = ssa;
+      sh.red[eq + 4] = ssb;
+    }
+    epi_bar();
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += sh.red[i];
+    epi_bar();
+    const float rstd = 1.0f / sqrtf(ss / (float)ph.n + ph.eps);
+    for (int c = r; c < n8; c += 128) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xr + c * 8));
+      const uint4 g = ldg16(ph.w + c * 8);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        o[i] = pack_bf2(bf_lo(u[i]) * rstd * bf_lo(gw[i]), bf_hi(u[i]) * rstd * bf_hi(gw[i]));
+      *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ---- one GEMM phase on the epilogue warps --------------------------------------
+template <int EPI>
+__device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& sh, uint32_t tmem, int pc, int r,
+                                 int& seg, bool& alive) {
+  const int eq = r >> 5, lane = r & 31;
+  const int nchunk = p.Npad / 16;
+  const int KT = ph.KT;
+  const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+  int* arr = p.counters + ph.ctr;
+  int* dep = arr + ph.tiles;
+  // STORE / RESIDUAL / STORE_F32: split tiles reduced by all contributors;
+  // SWIGLU / QKROPE need whole tiles: the last arriver finishes them
+  constexpr bool DIST = EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32;
+  int pend0 = -1, pend1 = -1, npend = 0;
+  if (b < e) {
+    for (int t = b / KT; alive && t <= (e - 1) / KT; ++t, ++seg) {
+      const int tb = t * KT;
+      const int k0 = (b > tb ? b : tb) - tb;
+      const int k1 = (e < tb + KT ? e : tb + KT) - tb;
+      const int buf = seg & 1, use = seg >> 1;
+      if (!mbar_wait(&sh.tfull_bar[buf], use & 1)) {
+        atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+      epi_bar();
+      if (r == 0) sh.go = !*(volatile int*)&sh.abort;
+      epi_bar();
+      if (!sh.go) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const bool full = (k0 == 0 && k1 == KT);
+      const uint32_t taddr = tmem + buf * p.tmem_cols + ((uint32_t)(eq * 32) << 16);
+      const int slot = (t == b / KT) ? 0 : 1;
+      float4* part = reinterpret_cast<float4*>(p.ws + ((size_t)(pc * 2 + slot) * p.Npad) * TILE_J) + r;
+      for (int c = 0; c < nchunk; ++c) {
+        float v[16];
+        tmem_ld16(taddr + c * 16, v);
+        if (full) {
+          ch_finish<EPI>(p, ph, sh, t, r, c * 16, v);
+        } else {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            part[(size_t)(c * 4 + q4) * TILE_J] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty_bar[buf]);
+      if (!full && DIST) {
+        __threadfence();
+        epi_bar();
+        if (r == 0) atomicAdd(&arr[t], 1);
+        if (npend++ == 0)
+          pend0 = t;
+        else
+          pend1 = t;
+      } else if (!full) {
+        const int q_lo = owner_of(tb, p.P, ph.W), q_hi = owner_of(tb + KT - 1, p.P, ph.W);
+        __threadfence();
+        epi_bar();
+        if (r == 0) sh.last = (atomicAdd(&arr[t], 1) == q_hi - q_lo);
+        epi_bar();
+        if (sh.last) {
+          __threadfence();
+          const int nq = q_hi - q_lo + 1;
+          const int lo_slot = it_begin(q_lo, p.P, ph.W) < tb ? 1 : 0;
+          for (int c = 0; c < nchunk; ++c) {
+            float v[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
+            for (int qi = 0; qi < nq; ++qi) {  // CTA order: deterministic
+              const int q = q_lo + qi;
+              const int qs = qi == 0 ? lo_slot : 0;
+              const float4* src = reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                                  (size_t)c * 4 * TILE_J + r;
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 f = __ldcg(src + (size_t)q4 * TILE_J);
+                v[4 * q4] += f.x;
+                v[4 * q4 + 1] += f.y;
+                v[4 * q4 + 2] += f.z;
+                v[4 * q4 + 3] += f.w;
+              }
+            }
+            ch_finish<EPI>(p, ph, sh, t, r, c * 16, v);
+          }
+          if (r == 0) arr[t] = 0;  // ready for the next launch
+        }
+      }
+    }
+  }
+  if constexpr (DIST) {
+    for (int pi = 0; alive && pi < npend; ++pi) {
+      const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
+      const int q_lo = owner_of(tb, p.P, ph.W), q_hi = owner_of(tb + KT - 1, p.P, ph.W);
+      const int nq = q_hi - q_lo + 1, c = pc - q_lo;
+      const int lo_slot = it_begin(q_lo, p.P, ph.W) < tb ? 1 : 0;
+      const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
+      const int nel = R * (p.Npad / 4);
+      if (r == 0) {
+        const bool ok = wait_count(&arr[t], nq);
+        if (!ok) atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.go = ok;
+      }
+      epi_bar();
+      const bool go = sh.go;
+      epi_bar();
+      if (!go) {
+        alive = false;
+        break;
+      }
+      for (int e0 = r; e0 < nel; e0 += 128) {
+        const int rr = rlo + e0 % R, g = e0 / R;
+        const int j = t * TILE_J + rr;
+        float rv[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (j < ph.n_out && 4 * g + i < p.M) rv[i] = ldcg_bf(ph.res + (int64_t)(4 * g + i) * ph.res_ld + j);
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int qi = 0; qi < nq; ++qi) {
+          const int q = q_lo + qi;
+          const int qs = qi == 0 ? lo_slot : 0;
+          const float4 f = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                                  (size_t)g * TILE_J + rr);
+          acc.x += f.x;
+          acc.y += f.y;
+          acc.z += f.z;
+          acc.w += f.w;
+        }
+        if (j < ph.n_out) {
+          const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = 4 * g + i;
+            if (m < p.M) {
+              const int64_t o = (int64_t)m * ph.ldo + j;
+              if constexpr (EPI == EPI_STORE_F32)
+                reinterpret_cast<float*>(ph.out)[o] = a4[i];
+              else if constexpr (EPI == EPI_STORE)
+                ph.out[o] = f2bf(a4[i]);
+              else
+                ph.out[o] = f2bf(rv[i] + rbf(a4[i]));
+            }
+          }
+        }
+      }
+      epi_bar();
+      if (r == 0 && atomicAdd(&dep[t], 1) == nq - 1) {
+        arr[t] = 0;  // every contributor has left
+        dep[t] = 0;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(CH_THREADS, 2)
+    fused_layer_kernel(const __grid_constant__ ChMaps maps, const __grid_constant__ ChParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ ChSmem sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pc = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&sh.full_bar[s], 1);
+      mbar_init(&sh.empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.tfull_bar[i], 1);
+      mbar_init(&sh.tempty_bar[i], 4);
+    }
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                 "r"(2 * p.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  uint8_t* a_smem = smem;
+  uint8_t* b_smem = smem + p.stages * A_STAGE;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- TMA producer: every GEMM phase's tiles, in order -------
+    if (lane == 0) {
+      bool ok = true, waited = false;
+      int i = 0;  // ring position (stages issued so far, over all phases)
+      for (int f = 0; ok && f < p.nph; ++f) {
+        const ChPhase& ph = p.ph[f];
+        if (ph.kind != CH_GEMM) continue;
+        const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+        if (b >= e) continue;
+        const CUtensorMap* am = &maps.a[f];
+        const CUtensorMap* bm = &maps.b[f];
+        prefetch_tmap(am);
+        prefetch_tmap(bm);
+        const int KT = ph.KT;
+        const bool swiglu = ph.epi == EPI_SWIGLU;
+        auto load_a = [&](int it, int s) {
+          const int t = it / KT, kt = it % KT;
+          const int row0 = swiglu ? t * 64 : t * TILE_J;
+          const int row1 = swiglu ? ph.up_off + t * 64 : t * TILE_J + 64;
+          tma_load_2d(a_smem + s * A_STAGE, am, &sh.full_bar[s], kt * BK, row0);
+          tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, am, &sh.full_bar[s], kt * BK, row1);
+        };
+        auto load_b = [&](int it, int s) {
+          tma_load_2d(b_smem + s * p.b_stage_bytes, bm, &sh.full_bar[s], (it % KT) * BK, 0);
+        };
+        // weight tiles first: they do not depend on the earlier phases
+        const int npre = (e - b) < p.stages ? (e - b) : p.stages;
+        for (int k = 0; k < npre; ++k) {
+          const int s = (i + k) % p.stages, rnd = (i + k) / p.stages;
+          if ((rnd > 0 && !mbar_wait(&sh.empty_bar[s], (rnd - 1) & 1)) || *(volatile int*)&sh.abort) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+          load_a(b + k, s);
+        }
+        if (!ok) break;
+        // activations: written by the previous kernel (f == 0) or by phase f-1
+        if (!waited) {
+          pdl_wait();
+          waited = true;
+        }
+        if (f > 0) {
+          if (!wait_count(&p.gbar[0], p.P * f)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
+        for (int k = 0; k < npre; ++k) load_b(b + k, (i + k) % p.stages);
+        for (int k = npre; k < e - b; ++k) {
+          const int s = (i + k) % p.stages, rnd = (i + k) / p.stages;
+          if (!mbar_wait(&sh.empty_bar[s], (rnd - 1) & 1) || *(volatile int*)&sh.abort) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+          load_a(b + k, s);
+          load_b(b + k, s);
+        }
+        i += e - b;
+      }
+      if (!ok) {
+        atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+      if (!waited) pdl_wait();
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int i = 0, seg = 0;
+      bool ok = true;
+      for (int f = 0; ok && f < p.nph; ++f) {
+        const ChPhase& ph = p.ph[f];
+        if (ph.kind != CH_GEMM) continue;
+        const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+        if (b >= e) continue;
+        const int KT = ph.KT;
+        for (int t = b / KT; ok && t <= (e - 1) / KT; ++t, ++seg) {
+          const int tb = t * KT;
+          const int k0 = (b > tb ? b : tb) - tb;
+          const int k1 = (e < tb + KT ? e : tb + KT) - tb;
+          const int buf = seg & 1, use = seg >> 1;
+          if (use > 0 && !mbar_wait(&sh.tempty_bar[buf], (use - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * p.tmem_cols;
+          for (int kt = k0; kt < k1; ++kt, ++i) {
+            const int s = i % p.stages, rnd = i / p.stages;
+            if (!mbar_wait(&sh.full_bar[s], rnd & 1) || *(volatile int*)&sh.abort) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(a_smem + s * A_STAGE);
+            const uint32_t b_base = smem_u32(b_smem + s * p.b_stage_bytes);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                        (kt > k0 || kk > 0) ? 1u : 0u);
+            umma_commit(&sh.empty_bar[s]);
+          }
+          if (!ok) break;
+          umma_commit(&sh.tfull_bar[buf]);
+        }
+      }
+      if (!ok) {
+        atomicExch(p.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps (2-5): GEMM epilogues and row phases ----
+    pdl_wait();
+    const int r = (warp & 3) * 32 + lane;
+    int seg = 0;
+    bool alive = true;
+    for (int f = 0; alive && f < p.nph; ++f) {
+      const ChPhase& ph = p.ph[f];
+      if (f > 0) {  // phase f-1 complete on every CTA: its outputs are this phase's inputs
+        if (r == 0) {
+          const bool ok = wait_count(&p.gbar[0], p.P * f);
+          if (!ok) atomicExch(p.status, TSDS_E_TIMEOUT);
+          sh.go = ok && !*(volatile int*)&sh.abort;
+        }
+        epi_bar();
+        alive = sh.go;
+        epi_bar();
+        if (!alive) break;
+      }
+      if (ph.kind == CH_NORM) {
+        ch_norm(p, ph, sh, pc, r);
+      } else {
+        switch (ph.epi) {
+          case EPI_STORE: ch_gemm_epilogue<EPI_STORE>(p, ph, sh, tmem, pc, r, seg, alive); break;
+          case EPI_RESIDUAL: ch_gemm_epilogue<EPI_RESIDUAL>(p, ph, sh, tmem, pc, r, seg, alive); break;
+          case EPI_SWIGLU: ch_gemm_epilogue<EPI_SWIGLU>(p, ph, sh, tmem, pc, r, seg, alive); break;
+          case EPI_STORE_F32: ch_gemm_epilogue<EPI_STORE_F32>(p, ph, sh, tmem, pc, r, seg, alive); break;
+          default: ch_gemm_epilogue<EPI_QKROPE>(p, ph, sh, tmem, pc, r, seg, alive); break;
+        }
+      }
+      if (!alive) break;
+      // publish this phase: its global writes before the arrival, for both
+      // plain loads and TMA reads of the next phases
+      fence_proxy_async_global();
+      __threadfence();
+      epi_bar();
+      if (r == 0) atomicAdd(&p.gbar[0], 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+  }
+  // the last CTA out resets the phase counter for the next launch (every CTA
+  // has finished waiting on it by then)
+  if (threadIdx.x == 0 && atomicAdd(&p.gbar[1], 1) == p.P - 1) {
+    p.gbar[0] = 0;
+    p.gbar[1] = 0;
+    __threadfence();
+  }
+}
+
+int pow2_at_least(int x) {
+  int v = 32;
+  while (v < x) v <<= 1;
+  return v;
+}
+
+size_t partial_bytes(int M) {
+  const int npad = M <= 0 ? 0 : (M + 15) / 16 * 16;
+  return (size_t)tsds_tc_num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" size_t tsds_fused_layer_workspace_bytes(int M) {
+  if (M <= 0 || M > 256) return 0;
+  return 64 + (size_t)CH_MAX_COUNTERS * sizeof(int) + partial_bytes(M);
+}
+
+extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
+                          void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
+  TSDS_RETURN_IF(!phases || n_phases < 1 || n_phases > CH_MAX_PHASES || M <= 0 || M > 256, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!workspace || workspace_bytes < tsds_fused_layer_workspace_bytes(M), TSDS_E_WORKSPACE);
+  TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
+  ChParams p = {};
+  ChMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  p.M = M;
+  p.Npad = (M + 15) / 16 * 16;
+  p.tmem_cols = pow2_at_least(p.Npad);
+  int ctas = tsds_tc_ctas_setting();
+  while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
+  p.P = tsds_tc_num_sms() * ctas;
+  p.nph = n_phases;
+  p.status = (int32_t*)workspace;
+  p.gbar = (int*)((char*)workspace + 4);
+  p.counters = (int*)((char*)workspace + 64);
+  p.ws = (float*)((char*)workspace + 64 + (size_t)CH_MAX_COUNTERS * sizeof(int));
+  p.b_stage_bytes = p.Npad * BK * 2;
+  int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
+  if (budget > CH_SMEM_BUDGET) budget = CH_SMEM_BUDGET;
+  p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
+  if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
+  TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) | ((uint32_t)(TILE_J >> 4) << 24);
+  int ctr = 0;
+  bool rope = false;
+  for (int f = 0; f < n_phases; ++f) {
+    const tsds_fused_phase& in = phases[f];
+    ChPhase& ph = p.ph[f];
+    ph.kind = in.kind;
+    ph.epi = in.epi;
+    if (in.kind == TSDS_PHASE_NORM) {
+      TSDS_RETURN_IF(!in.x || !in.w || !in.out || in.K <= 0 || (in.K % 8) != 0, TSDS_E_INVALID);
+      TSDS_RETURN_IF(in.ldx < in.K || in.ldo < in.K, TSDS_E_INVALID);
+      TSDS_RETURN_IF(!tsds_aligned16(in.x) || !tsds_aligned16(in.w) || !tsds_aligned16(in.out) || (in.ldx % 8) ||
+                         (in.ldo % 8),
+                     TSDS_E_ALIGN);
+      ph.x = (const bf16*)in.x;
+      ph.w = (const bf16*)in.w;
+      ph.out = (bf16*)in.out;
+      ph.n = in.K;
+      ph.ldx = in.ldx;
+      ph.ldo = in.ldo;
+      ph.eps = in.eps;
+      continue;
+    }
+    TSDS_RETURN_IF(in.kind != TSDS_PHASE_GEMM, TSDS_E_INVALID);
+    TSDS_RETURN_IF(in.epi != EPI_STORE && in.epi != EPI_RESIDUAL && in.epi != EPI_SWIGLU && in.epi != EPI_STORE_F32 &&
+                       in.epi != EPI_QKROPE,
+                   TSDS_E_INVALID);
+    TSDS_RETURN_IF(!in.x || !in.w || in.n_out <= 0 || in.K <= 0 || in.ldx < in.K, TSDS_E_INVALID);
+    TSDS_RETURN_IF(in.epi != EPI_QKROPE && !in.out, TSDS_E_INVALID);
+    TSDS_RETURN_IF(in.epi == EPI_RESIDUAL && (!in.res || in.res_ld < in.n_out), TSDS_E_INVALID);
+    TSDS_RETURN_IF(in.epi != EPI_QKROPE && in.ldo < in.n_out, TSDS_E_INVALID);
+    TSDS_RETURN_IF(!tsds_aligned16(in.x) || !tsds_aligned16(in.w) || (in.ldx % 8) || (in.K % 8), TSDS_E_ALIGN);
+    ph.n_out = in.n_out;
+    ph.K = in.K;
+    ph.KT = (in.K + BK - 1) / BK;
+    ph.tiles = in.epi == EPI_SWIGLU ? (in.n_out + 63) / 64 : (in.n_out + TILE_J - 1) / TILE_J;
+    const long long W64 = (long long)ph.tiles * ph.KT;
+    TSDS_RETURN_IF(W64 * p.P >= (1ll << 32), TSDS_E_UNSUPPORTED);
+    ph.W = (uint32_t)W64;
+    ph.up_off = in.n_out;
+    ph.ldo = in.ldo;
+    ph.res = (const bf16*)in.res;
+    ph.res_ld = in.res_ld;
+    ph.out = (bf16*)in.out;
+    ph.ctr = ctr;
+    ctr += 2 * ph.tiles;
+    TSDS_RETURN_IF(ctr > CH_MAX_COUNTERS, TSDS_E_UNSUPPORTED);
+    if (in.epi == EPI_QKROPE) {
+      TSDS_RETURN_IF(!qr || rope, TSDS_E_INVALID);  // one rope phase per launch (one parameter set)
+      rope = true;
+      TSDS_RETURN_IF(qr->T <= 0 || (M % qr->T) != 0 || qr->Hq <= 0 || qr->Hkv <= 0 || qr->S <= 0 ||
+                         qr->rope_len <= 0 || (qr->Hq % qr->Hkv) != 0,
+                     TSDS_E_INVALID);
+      TSDS_RETURN_IF(in.n_out != (qr->Hq + 2 * qr->Hkv) * 128, TSDS_E_INVALID);
+      TSDS_RETURN_IF(!qr->cos || !qr->sin || !qr->positions || !qr->starts || !qr->q_out || !qr->k_cache ||
+                         !qr->v_cache,
+                     TSDS_E_INVALID);
+      p.qr.qn = (const bf16*)qr->q_norm_w;
+      p.qr.kn = (const bf16*)qr->k_norm_w;
+      p.qr.cos_t = (const bf16*)qr->cos;
+      p.qr.sin_t = (const bf16*)qr->sin;
+      p.qr.pos = qr->positions;
+      p.qr.starts = qr->starts;
+      p.qr.q_out = (bf16*)qr->q_out;
+      p.qr.k_cache = (bf16*)qr->k_cache;
+      p.qr.v_cache = (bf16*)qr->v_cache;
+      p.qr.T = qr->T;
+      p.qr.Hq = qr->Hq;
+      p.qr.Hkv = qr->Hkv;
+      p.qr.S = qr->S;
+      p.qr.rope_len = qr->rope_len;
+      p.qr.eps = qr->eps;
+    }
+    const int w_rows = in.epi == EPI_SWIGLU ? 2 * in.n_out : in.n_out;
+    int st = tsds_make_tmap_2d_bf16(&maps.a[f], in.w, in.K, w_rows, (uint64_t)in.K * 2, BK, 64, 1);
+    if (st != TSDS_OK) return st;
+    st = tsds_make_tmap_2d_bf16(&maps.b[f], in.x, in.K, M, (uint64_t)in.ldx * 2, BK, p.Npad, 1);
+    if (st != TSDS_OK) return st;
+  }
+  static bool attr[TSDS_MAX_DEVICES] = {};
+  const int st = tsds_smem_limit_once(fused_layer_kernel, CH_SMEM_BUDGET, attr);
+  if (st != TSDS_OK) return st;
+  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  tsds_launch(fused_layer_kernel, dim3(p.P), dim3(CH_THREADS), smem, stream, maps, p);
+  return tsds_launch_status();
+}

@@ -25,15 +25,13 @@
 // TSDS_E_TIMEOUT in the status word and unwinds.
 #include "common.cuh"
 #include "linear.cuh"
+#include "tc_core.cuh"
 
 using namespace tsds;
+using namespace tsds::tc;
 
 namespace {
 
-constexpr int BK = 64;                     // k per stage: one 128-byte swizzle row
-constexpr int TILE_J = 128;                // MMA M
-constexpr int A_STAGE = TILE_J * BK * 2;   // 16 KB
-constexpr int MAX_STAGES = 16;
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_BUDGET = 220 * 1024;
 
@@ -53,69 +51,6 @@ struct TcParams {
   uint32_t idesc;
   int tmem_cols;
 };
-
-// ---- tcgen05 / descriptor helpers ------------------------------------------
-// Shared-memory matrix descriptor: K-major operand in 128-byte-swizzled
-// rows, 8-row core groups 1024 bytes apart (SBO), descriptor version 1.
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
-  d |= (uint64_t)1 << 46;             // version
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
-  return d;
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accum) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// ---- stream-K bookkeeping ---------------------------------------------------
-// 32-bit arithmetic: W * P < 2^32 is checked on the host.
-__device__ __forceinline__ int it_begin(int p, int P, uint32_t W) { return (int)(((uint32_t)p * W) / (uint32_t)P); }
-
-// CTA whose range holds iteration x
-__device__ __forceinline__ int owner_of(int x, int P, uint32_t W) {
-  int q = (int)(((uint32_t)x * (uint32_t)P) / W);
-  if (q > P - 1) q = P - 1;
-  while (q + 1 < P && it_begin(q + 1, P, W) <= x) ++q;
-  while (q > 0 && it_begin(q, P, W) > x) --q;
-  return q;
-}
-
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 constexpr int MAX_TILES = 2048;   // tile counters; departure counters follow them
 
@@ -574,6 +509,8 @@ int num_sms() {
 }  // namespace
 
 extern "C" void tsds_set_gemm_ctas_per_sm(int n) { g_ctas_per_sm = n < 1 ? 1 : (n > 4 ? 4 : n); }
+int tsds_tc_num_sms() { return num_sms(); }
+int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
 
 namespace {
 

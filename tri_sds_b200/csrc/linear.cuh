@@ -19,3 +19,12 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
 
 // Row count up to which the CUDA-core GEMV is used instead of tcgen05.
 int tsds_gemv_rows_limit();
+
+// Launch shape of the tcgen05 kernels: SMs of the current device, and the
+// CTAs-per-SM setting (tsds_set_gemm_ctas_per_sm) before the TMEM cap.
+int tsds_tc_num_sms();
+int tsds_tc_ctas_setting();
+
+// Fused-layer kernel only: q/k/v projection whose epilogue applies QK-norm + RoPE
+// and writes q and the K/V cache rows (one 128-row tile = one head).
+enum { EPI_QKROPE = 5 };

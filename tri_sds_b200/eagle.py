@@ -43,7 +43,7 @@ class EagleHead:
         if weights is not None:
             lw = {"layers": [weights["layer"]], "embed": None, "lm_head": None, "norm": None}
         self.model = QwenModel(self.shape, batch=batch, max_seq=32, max_rows=batch * topk, device=dev, weights=lw,
-                               seed=seed, share_embeddings=target, rope_len=target.rope_len)
+                               seed=seed, share_embeddings=target, rope_len=target.rope_len, fused_layers=target.fused_layers)
         if weights is not None:
             self.fc_w = weights["fc"].to(dev, torch.bfloat16).contiguous()
             self.fc_b = weights["fc_bias"].to(dev, torch.bfloat16).contiguous()

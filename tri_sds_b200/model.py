@@ -37,6 +37,15 @@ def _p(t):
     return None if t is None else _VP(t.data_ptr())
 
 
+def _fused_args(phases: list, rope: dict | None, M: int, ws, ws_bytes: int) -> tuple:
+    """tsds_fused_layer arguments (after the name) from phase dicts of pointers and
+    sizes: a tsds_fused_phase array and a tsds_qk_rope, kept alive by the
+    argument tuple itself."""
+    arr = (_lib.FusedPhase * len(phases))(*[_lib.FusedPhase(**ph) for ph in phases])
+    qr = ctypes.pointer(_lib.QkRope(**rope)) if rope is not None else None
+    return (arr, len(phases), M, qr, ws, ws_bytes)
+
+
 def precompute_rope(dim: int, max_len: int, base: float, device) -> tuple[torch.Tensor, torch.Tensor]:
     """qwen_model.py:8-14: fp32 angles on the host, bf16 tables."""
     inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim))
@@ -122,7 +131,7 @@ class QwenModel:
                  weights: dict | None = None, seed: int = 0, split_keys: int = 128, qk_norm: bool | None = None,
                  share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
                  tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None,
-                 peer=None):
+                 peer=None, fused_layers: bool = False):
         self.shape = shape
         # tensor parallelism: layers and/or vocabulary sharded over tp_size ranks
         self.tp_rank = tp_rank
@@ -218,6 +227,12 @@ class QwenModel:
         self.lm_ws_bytes = max(_lib.query("tsds_lm_head_workspace_bytes", m, self.vocab_local)
                                for m in range(1, M + 1))
         self.lm_ws = torch.zeros(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
+        # fused-layer kernel (one launch for O -> norm -> gate/up -> down ->
+        # norm -> q/k/v of consecutive layers); its own zero-filled workspace
+        self.fused_layers = fused_layers and self.layer_tp == 1
+        if self.fused_layers:
+            self.fused_ws_bytes = _lib.query("tsds_fused_layer_workspace_bytes", M)
+            self.fused_ws = torch.zeros(self.fused_ws_bytes, dtype=torch.uint8, device=dev)
 
     # -- launch plans ---------------------------------------------------------
     def layers_plan(self, B: int, T: int, tree_mask: torch.Tensor | None = None, mask_origin: int = -1,
@@ -240,6 +255,8 @@ class QwenModel:
         st = self.starts if starts is None else starts
         ps = self.positions if positions is None else positions
         tp = self.layer_tp > 1
+        if self.fused_layers:
+            return self._fused_layers_plan(B, T, tree_mask, mask_origin, xb, st, ps)
         n_peer = [0]
 
         def row_parallel(src, ld_src, w, k_in):
@@ -280,6 +297,56 @@ class QwenModel:
                    ls.intermediate, s.hidden, _p(lw), lb)
             row_parallel(self.h, ls.intermediate, L.w_d, ls.intermediate)
         assert n_peer[0] % 2 == 0   # the next plan run starts on slot 0 again
+        return pl
+
+    def _fused_layers_plan(self, B: int, T: int, tree_mask, mask_origin: int, xb, st, ps) -> Plan:
+        """layers_plan with the fused-layer kernel: per layer one attention
+        launch and one fused launch [O (+res) -> norm -> gate/up -> down (+res) ->
+        next layer's norm -> q/k/v (+QK-norm, RoPE, KV write)]; the first
+        is [norm -> q/k/v] of layer 0.  Same rounding as the per-op
+        plan; tensor parallelism is not supported here."""
+        s, ls = self.shape, self.lshape
+        M = B * T
+        eps = s.eps
+        qn = self.qk_norm
+        pl = Plan()
+        N = s.hidden
+
+        def norm(w):
+            return dict(kind=_lib.PHASE_NORM, epi=0, x=_p(xb), ldx=N, K=N, w=_p(w), n_out=0, res_ld=0, res=None,
+                        out=_p(self.xn), ldo=N, eps=eps)
+
+        def gemm(epi, x, K, w, n_out, out=None, res=None):
+            return dict(kind=_lib.PHASE_GEMM, epi=epi, x=_p(x), ldx=K, K=K, w=_p(w), n_out=n_out,
+                        res_ld=N if res is not None else 0, res=_p(res), out=_p(out),
+                        ldo=n_out if out is not None else 0, eps=0.0)
+
+        def qkv(i):
+            L = self.layers[i]
+            rope = dict(q_norm_w=_p(L.q_norm) if qn else None, k_norm_w=_p(L.k_norm) if qn else None,
+                        cos=_p(self.cos), sin=_p(self.sin), positions=_p(ps), starts=_p(st), q_out=_p(self.q),
+                        k_cache=_p(self.k_cache[i]), v_cache=_p(self.v_cache[i]), T=T, Hq=ls.n_heads,
+                        Hkv=ls.n_kv_heads, S=self.max_seq, rope_len=self.rope_len, eps=eps)
+            return [norm(L.ln1), gemm(_lib.EPI_QKROPE, self.xn, N, L.w_qkv, ls.qkv_dim)], rope
+
+        phases, rope = qkv(0)
+        pl.add("tsds_fused_layer", *_fused_args(phases, rope, M, _p(self.fused_ws), self.fused_ws_bytes))
+        n = len(self.layers)
+        for i, L in enumerate(self.layers):
+            kc, vc = self.k_cache[i], self.v_cache[i]
+            pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(st),
+                   _p(tree_mask), mask_origin, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
+                   self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
+                   _p(self.status))
+            phases = [gemm(_lib.EPI_RESIDUAL, self.attn, ls.q_dim, L.w_o, N, out=xb, res=xb),
+                      norm(L.ln2),
+                      gemm(_lib.EPI_SWIGLU, self.xn, N, L.w_gu, ls.intermediate, out=self.h),
+                      gemm(_lib.EPI_RESIDUAL, self.h, ls.intermediate, L.w_d, N, out=xb, res=xb)]
+            rope = None
+            if i + 1 < n:
+                nxt, rope = qkv(i + 1)
+                phases += nxt
+            pl.add("tsds_fused_layer", *_fused_args(phases, rope, M, _p(self.fused_ws), self.fused_ws_bytes))
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,
