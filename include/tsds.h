@@ -266,11 +266,17 @@ int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shar
  *        _QKROPE (n_out = (Hq + 2*Hkv) * 128; outputs as tsds_qk_norm_rope_kv
  *        with the parameters in *qr; out unused; at most one such phase).
  *  NORM: out[m][0:K] = RMSNorm(x[m][0:K]) * w, eps.
+ *  PEER: tensor parallelism - out[m][0:K] (bf16, stride ldo) = bf16(out +
+ *        bf16(sum over ranks 0..tp-1 of slot n_out (0 or 1) of their peer
+ *        buffers, fp32 [M][K]))), the same on every rank; the preceding
+ *        STORE_F32 phase writes this rank's partial into that slot (ldo = K).
+ *        The peer buffers are those of tsds_peer_allreduce_residual (*peers);
+ *        the cross-rank wait is per CTA index and bounded (1 s).
  * Workspace: tsds_fused_layer_workspace_bytes(M) bytes, 16-byte aligned, zero-filled
  * once (every launch leaves its counters zero again); word 0 is the status
  * word (TSDS_E_TIMEOUT after a bounded device wait gave up).  M <= 256.
  */
-enum { TSDS_PHASE_GEMM = 0, TSDS_PHASE_NORM = 1 };
+enum { TSDS_PHASE_GEMM = 0, TSDS_PHASE_NORM = 1, TSDS_PHASE_PEER = 2 };
 enum {
   TSDS_EPI_STORE = 0,
   TSDS_EPI_RESIDUAL = 1,
@@ -281,14 +287,14 @@ enum {
 typedef struct {
   int kind;          /* TSDS_CHAIN_* */
   int epi;           /* GEMM: TSDS_EPI_* */
-  const void* x;     /* GEMM: activations [M][K] bf16; NORM: input rows */
+  const void* x;     /* GEMM: activations [M][K] bf16; NORM: input rows; PEER: unused */
   int ldx;           /* row stride of x (elements, multiple of 8) */
   int K;             /* GEMM: reduction length; NORM: row length */
   const void* w;     /* GEMM: weights [n_out][K] (SWIGLU [2*n_out][K]); NORM: gain [K] */
-  int n_out;         /* GEMM output columns */
+  int n_out;         /* GEMM output columns; PEER: the slot */
   int res_ld;        /* RESIDUAL: row stride of res */
   const void* res;   /* RESIDUAL: residual rows */
-  void* out;         /* output rows (fp32 for STORE_F32) */
+  void* out;         /* output rows (fp32 for STORE_F32); PEER: the residual, updated in place */
   int ldo;           /* row stride of out */
   float eps;         /* NORM */
 } tsds_fused_phase;
@@ -305,9 +311,15 @@ typedef struct {
   int T, Hq, Hkv, S, rope_len;
   float eps;
 } tsds_qk_rope;
+typedef struct {
+  void* const* bufs;   /* host array [tp]: every rank's peer buffer as mapped here, bufs[rank] its own */
+  int rank, tp;
+  int max_elems;       /* the buffers' slot size (tsds_peer_buffer_bytes) */
+} tsds_peer_group;
 size_t tsds_fused_layer_workspace_bytes(int M);
 int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
-               void* workspace, size_t workspace_bytes, tsds_stream_t stream);
+                     const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
+                     tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Peer (NVLink) all-reduce of row-parallel partials, fused with the residual
@@ -319,7 +331,7 @@ int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const 
  * tsds_peer_export (tsds_peer_handle_bytes() bytes, a CUDA IPC handle) and
  * maps every other rank's with tsds_peer_import (another process of the same
  * node; close with tsds_peer_close, free its own with tsds_peer_free).
- * Buffer layout: per-CTA call counters and flags in the first 16 KB, then two
+ * Buffer layout: per-CTA call counters and flags in the first 32 KB, then two
  * slots of max_elems fp32 at tsds_peer_slot_offset(max_elems, 0 / 1).
  *
  * tsds_peer_allreduce_residual: the partial [M][N] fp32 of every rank sits in

@@ -105,9 +105,13 @@ def extents(name, a):
 def fused_extents(a):
     """tsds_fused_layer with its phases / rope given as dicts (see _fused_args):
     [(ref, bytes)] pairs instead of argument indices."""
-    phases, n, M, rope, ws, wsb = a
+    phases, n, M, rope, peers, ws, wsb = a
     out = [(ws, wsb)]
     for ph in phases[:n]:
+        if ph["kind"] == 2:   # PEER: the residual updated in place (the slots are the peer group's)
+            assert peers is not None and ph["n_out"] in (0, 1) and M * ph["K"] <= peers.max_elems
+            out.append((ph["out"], ((M - 1) * ph["ldo"] + ph["K"]) * 2))
+            continue
         if ph["kind"] == 1:   # NORM
             K = ph["K"]
             out += [(ph["x"], ((M - 1) * ph["ldx"] + K) * 2), (ph["w"], K * 2), (ph["out"], ((M - 1) * ph["ldo"] + K) * 2)]

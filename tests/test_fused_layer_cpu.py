@@ -30,13 +30,14 @@ def recorded(monkeypatch):
     ref = lambda t: None if t is None else TRef(t)  # noqa: E731
     for mod in (model, eagle, engine):
         monkeypatch.setattr(mod, "_p", ref)
-    monkeypatch.setattr(model, "_fused_args", lambda phases, rope, M, ws, wsb: (phases, len(phases), M, rope, ws, wsb))
+    monkeypatch.setattr(model, "_fused_args",
+                        lambda phases, rope, peer, M, ws, wsb: (phases, len(phases), M, rope, peer, ws, wsb))
     yield
 
 
 def _phase_names(phases):
-    names = {(0, 0): "store", (0, 1): "res", (0, 2): "swiglu", (0, 4): "f32", (0, 5): "qkrope"}
-    return ["norm" if ph["kind"] == 1 else names[(0, ph["epi"])] for ph in phases]
+    names = {0: "store", 1: "res", 2: "swiglu", 4: "f32", 5: "qkrope"}
+    return [{1: "norm", 2: "peer"}.get(ph["kind"]) or names[ph["epi"]] for ph in phases]
 
 
 @pytest.mark.parametrize("B,T", [(1, 26), (8, 26), (2, 5)])
@@ -76,6 +77,52 @@ def test_eagle_engine_plans_with_fused_layers(recorded):
             check_call(n, a)
 
 
+class FakePeer:
+    """tp.PeerAllReduce's interface with host tensors as slots."""
+
+    def __init__(self, rank, size, max_elems):
+        self.rank, self.size, self.max_elems = rank, size, (max_elems + 63) // 64 * 64
+        self.slots = [torch.zeros(self.max_elems, dtype=torch.float32) for _ in range(2)]
+        self.bufs = (ctypes.c_void_p * size)(*[0x1000 * (p + 1) for p in range(size)])
+
+    def slot_ptr(self, slot):
+        return TRef(self.slots[slot])
+
+
+@pytest.mark.parametrize("tp,rank", [(2, 1), (8, 6)])
+def test_tensor_parallel_fused_plan_with_peer_phases(recorded, tp, rank):
+    from tri_sds_b200.model import QwenModel
+
+    class _Comm:
+        def __init__(self):
+            self.rank, self.size = rank, tp
+
+    B, T = 2, 26
+    peer = FakePeer(rank, tp, B * T * SHAPE.hidden)
+    m = QwenModel(SHAPE, B, 96, B * T, device="cpu", tp_rank=rank, tp_size=tp, comm=_Comm(), peer=peer,
+                  fused_layers=True)
+    assert m.fused_layers
+    pl = m.layers_plan(B, T)
+    names = [n for n, fn, a in pl.calls]
+    assert names == ["tsds_fused_layer"] + ["tsds_verify_attention", "tsds_fused_layer"] * SHAPE.n_layers
+    fused = [a for n, fn, a in pl.calls if n == "tsds_fused_layer"]
+    mid = ["f32", "peer", "norm", "swiglu", "f32", "peer", "norm", "qkrope"]
+    for a in fused[1:-1]:
+        assert _phase_names(a[0]) == mid
+        o, red_o, _, _, d, red_d = a[0][:6]
+        # each partial goes to the slot its all-reduce phase reads
+        assert o["out"].t is peer.slots[0] and red_o["n_out"] == 0
+        assert d["out"].t is peer.slots[1] and red_d["n_out"] == 1
+        assert a[4] is peer
+    assert _phase_names(fused[-1][0]) == mid[:6]
+    # the rank's shard sizes: local heads and FFN columns
+    qk = fused[0][0][1]
+    assert qk["n_out"] == (SHAPE.n_heads + 2 * SHAPE.n_kv_heads) // tp * 128
+    assert fused[1][0][3]["n_out"] == SHAPE.intermediate // tp
+    for n, fn, a in pl.calls:
+        assert check_call(n, a) > 0
+
+
 def test_tensor_parallel_model_keeps_the_per_op_plan():
     from tri_sds_b200.model import QwenModel
 
@@ -93,17 +140,18 @@ def test_struct_layouts_match_the_header(tmp_path):
 #include <stdio.h>
 #include "{ROOT}/include/tsds.h"
 int main(void) {{
-  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(tsds_fused_phase), offsetof(tsds_fused_phase, w),
+  printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(tsds_fused_phase), offsetof(tsds_fused_phase, w),
          offsetof(tsds_fused_phase, res), offsetof(tsds_fused_phase, eps), sizeof(tsds_qk_rope),
-         offsetof(tsds_qk_rope, T));
+         offsetof(tsds_qk_rope, T), sizeof(tsds_peer_group), offsetof(tsds_peer_group, max_elems));
   return 0;
 }}
 ''')
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
-    P, Q = _lib.FusedPhase, _lib.QkRope
-    assert got == [ctypes.sizeof(P), P.w.offset, P.res.offset, P.eps.offset, ctypes.sizeof(Q), Q.T.offset]
+    P, Q, G = _lib.FusedPhase, _lib.QkRope, _lib.PeerGroup
+    assert got == [ctypes.sizeof(P), P.w.offset, P.res.offset, P.eps.offset, ctypes.sizeof(Q), Q.T.offset,
+                   ctypes.sizeof(G), G.max_elems.offset]
 
 
 def test_entry_point_rejects_bad_descriptors():
@@ -124,7 +172,7 @@ def test_entry_point_rejects_bad_descriptors():
 
     def run(phases, m=M, qr=None, wsb=nb):
         arr = (_lib.FusedPhase * max(1, len(phases)))(*phases)
-        return lib.tsds_fused_layer(arr, len(phases), m, qr, ws, wsb, None)
+        return lib.tsds_fused_layer(arr, len(phases), m, qr, None, ws, wsb, None)
 
     assert run([]) == 1                                   # no phase
     assert run([ph()] * 9) == 1                           # more than 8
@@ -139,3 +187,16 @@ def test_entry_point_rejects_bad_descriptors():
     assert run([ph(kind=1, K=250)]) == 1                  # norm row not a multiple of 8
     assert run([ph(kind=7)]) == 1
     assert run([ph(x=0x1008)]) == 2                       # x not 16-byte aligned
+    assert run([ph(kind=2, K=256, n_out=0)]) == 1         # an all-reduce phase without a peer group
+    bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+
+    def group(**kw):
+        d = dict(bufs=ctypes.cast(bufs, ctypes.c_void_p), rank=0, tp=2, max_elems=M * 256)
+        d.update(kw)
+        return ctypes.pointer(_lib.PeerGroup(**d))
+
+    arr = (_lib.FusedPhase * 1)(ph(kind=2, K=256, n_out=0))
+    for bad in (group(tp=9), group(rank=2), group(max_elems=M * 256 - 1)):
+        assert lib.tsds_fused_layer(arr, 1, M, None, bad, ws, nb, None) == 1
+    arr = (_lib.FusedPhase * 1)(ph(kind=2, K=256, n_out=2))  # slot not 0 / 1
+    assert lib.tsds_fused_layer(arr, 1, M, None, group(), ws, nb, None) == 1

@@ -2,9 +2,10 @@
 greedy speculative decoding (chain draft and EAGLE tree, whose commit
 compacts each rank's shard of the KV cache) == greedy autoregressive
 decoding under TP=2, with the row-parallel all-reduces by NCCL or by the
-library's peer-memory kernel.  Skipped with fewer than 2 GPUs; the
-peer-memory variant runs only with TSDS_TEST_PEER=1 until it has been
-validated on GPUs."""
+library's peer-memory kernel (standalone, or as phases of the fused-layer
+kernel).  Skipped with fewer than 2 GPUs; the peer-memory variants run only
+with TSDS_TEST_PEER=1 (and TSDS_TEST_FUSED=1) until they have been validated
+on GPUs."""
 import os
 import socket
 
@@ -34,7 +35,8 @@ def _worker(rank, port, q, allreduce):
         dev = torch.device("cuda", rank)
         comm = Comm()
         # one set of peer buffers for every TP model here (their calls run in stream order)
-        peer = PeerAllReduce(rank, 2, 2 * 26 * SMALL["hidden"]) if allreduce == "peer" else None
+        peer = PeerAllReduce(rank, 2, 2 * 26 * SMALL["hidden"]) if allreduce != "nccl" else None
+        fused = allreduce == "peer+fused"   # the all-reduces as phases of the fused-layer kernel
         oshape = oq.QwenShape(**SMALL)
         shape = QwenShape(**SMALL)
         w = oq.random_qwen_weights(oshape, seed=1, std=0.02)
@@ -43,7 +45,7 @@ def _worker(rank, port, q, allreduce):
         prompt = torch.randint(0, oshape.vocab, (B, P), generator=g)
         step = torch.randint(0, oshape.vocab, (B, T), generator=g)
         m = QwenModel(shape, B, 128, B * T, device=dev, weights=w, tp_rank=rank, tp_size=2, comm=comm,
-                      peer=peer)
+                      peer=peer, fused_layers=fused)
         m.prefill(prompt)
         logits = torch.zeros(B * T, oshape.vocab, dtype=torch.bfloat16, device=dev)
         am = torch.zeros(B * T, dtype=torch.int64, device=dev)
@@ -56,11 +58,11 @@ def _worker(rank, port, q, allreduce):
         dshape = QwenShape(**{**SMALL, "n_layers": 1})
         K = 4
         tgt = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
-                        peer=peer)
+                        peer=peer, fused_layers=fused)
         drf = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_size=2, tp_layers=False, tp_vocab=False)
         spec, _ = SpecEngine(tgt, drf, K).generate(prompt, 16)
         tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
-                         peer=peer)
+                         peer=peer, fused_layers=fused)
         ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
         out.update(spec=spec, ar=ar)
         # EAGLE tree, greedy: the head replicated, the target TP=2
@@ -68,7 +70,7 @@ def _worker(rank, port, q, allreduce):
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         we = oe.random_eagle_weights(oshape, seed=4, std=0.08)
         tgt3 = QwenModel(shape, B, 128, B * 26, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
-                         peer=peer)
+                         peer=peer, fused_layers=fused)
         eng = EagleEngine(tgt3, EagleHead(tgt3, B, weights=we), greedy=True)
         espec, _ = eng.generate(prompt, 16)
         out.update(espec=espec)
@@ -93,6 +95,9 @@ def _worker(rank, port, q, allreduce):
     "nccl",
     pytest.param("peer", marks=pytest.mark.skipif(os.environ.get("TSDS_TEST_PEER") != "1",
                                                   reason="peer all-reduce: set TSDS_TEST_PEER=1")),
+    pytest.param("peer+fused", marks=pytest.mark.skipif(
+        os.environ.get("TSDS_TEST_PEER") != "1" or os.environ.get("TSDS_TEST_FUSED") != "1",
+        reason="peer all-reduce in the fused-layer kernel: set TSDS_TEST_PEER=1 and TSDS_TEST_FUSED=1")),
 ])
 def test_tp2_verify_and_lossless_spec(allreduce):
     with socket.socket() as sk:

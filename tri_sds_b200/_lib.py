@@ -18,7 +18,7 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
 
-PHASE_GEMM, PHASE_NORM = 0, 1
+PHASE_GEMM, PHASE_NORM, PHASE_PEER = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32, EPI_QKROPE = 0, 1, 2, 4, 5
 
 
@@ -33,6 +33,11 @@ class QkRope(ctypes.Structure):
     _fields_ = [("q_norm_w", _P), ("k_norm_w", _P), ("cos", _P), ("sin", _P), ("positions", _P), ("starts", _P),
                 ("q_out", _P), ("k_cache", _P), ("v_cache", _P), ("T", _I), ("Hq", _I), ("Hkv", _I), ("S", _I),
                 ("rope_len", _I), ("eps", _F)]
+
+
+class PeerGroup(ctypes.Structure):
+    """tsds_peer_group (include/tsds.h)."""
+    _fields_ = [("bufs", _P), ("rank", _I), ("tp", _I), ("max_elems", _I)]
 
 
 # name -> (restype, argtypes); mirrors include/tsds.h
@@ -73,7 +78,7 @@ SIGNATURES = {
     "tsds_argmax_merge": (_I, [_P, _P, _I, _I, ctypes.c_int64, _P, _I, _P]),
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
     "tsds_fused_layer_workspace_bytes": (_Z, [_I]),
-    "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _Z, _P]),
+    "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _P, _Z, _P]),
     "tsds_peer_buffer_bytes": (_Z, [_I]),
     "tsds_peer_slot_offset": (_Z, [_I, _I]),
     "tsds_peer_handle_bytes": (_Z, []),

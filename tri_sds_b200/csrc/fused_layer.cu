@@ -15,12 +15,19 @@
 // the activation tiles wait for the barrier, so HBM keeps streaming across
 // phase boundaries instead of draining at every kernel edge.
 //
+// Under tensor parallelism the row-parallel projections store fp32 partials
+// into this rank's peer slot and a PEER phase all-reduces them across the
+// ranks over NVLink (plain peer loads, the flag protocol of peer.cuh run per
+// CTA index) and adds them to the residual: GEMM and all-reduce in one
+// kernel, no NCCL between them.
+//
 // Data produced inside the launch is read with L2-coherent loads (ld.cg) or
 // by TMA after a proxy fence, never through the non-coherent path.  Every
-// wait is bounded (2 s): a timeout records TSDS_E_TIMEOUT in the status word
-// and the CTA unwinds.  No TMA multicast, no peer memory.
+// wait is bounded (2 s; 1 s across ranks): a timeout records TSDS_E_TIMEOUT
+// in the status word and the CTA unwinds.  No TMA multicast.
 #include "common.cuh"
 #include "linear.cuh"
+#include "peer.cuh"
 #include "rowops.cuh"
 #include "tc_core.cuh"
 
@@ -28,6 +35,7 @@
 
 using namespace tsds;
 using namespace tsds::tc;
+using tsds::peer::PEER_MAX_RANKS;
 
 static_assert((int)TSDS_EPI_STORE == (int)EPI_STORE && (int)TSDS_EPI_RESIDUAL == (int)EPI_RESIDUAL &&
                   (int)TSDS_EPI_SWIGLU == (int)EPI_SWIGLU && (int)TSDS_EPI_STORE_F32 == (int)EPI_STORE_F32 &&
@@ -43,7 +51,7 @@ constexpr int CH_SMEM_BUDGET = 220 * 1024;
 constexpr int SMEM_PER_SM = 233472;
 constexpr int SMEM_RESERVE = 8192;
 constexpr uint64_t CH_WAIT_NS = 2000000000ull;
-enum { CH_GEMM = 0, CH_NORM = 1 };
+enum { CH_GEMM = 0, CH_NORM = 1, CH_PEER = 2 };
 
 struct ChPhase {
   int kind, epi;
@@ -54,10 +62,18 @@ struct ChPhase {
   const bf16* res;
   bf16* out;
   // NORM: out[m][0:n] (ldo) = RMSNorm(x[m][0:n]) * w
+  // PEER: out[m][0:n] (ldo) += sum over ranks of slot `slot` (fp32 [M][n])
   const bf16* x;
   const bf16* w;
-  int n, ldx;
+  int n, ldx, slot;
   float eps;
+};
+
+struct ChPeer {  // the ranks' peer buffers (see peer.cuh)
+  const float* slot[2][PEER_MAX_RANKS];
+  uint32_t* flags[PEER_MAX_RANKS];
+  uint32_t* counters;
+  int rank, tp;
 };
 
 struct ChRope {  // EPI_QKROPE: tile t = head slot t of [q heads | k heads | v heads]
@@ -83,6 +99,7 @@ struct ChParams {
   int32_t* status;
   ChPhase ph[CH_MAX_PHASES];
   ChRope qr;
+  ChPeer pr;
 };
 
 struct ChMaps {
@@ -101,6 +118,8 @@ struct ChSmem {
   int last;
   float xch[64][17];  // SwiGLU: up rows; QKROPE: a [128][8] exchange of 8 columns
   float red[8];
+  uint32_t epoch;
+  int peer_ok;
 };
 
 __device__ __forceinline__ bool wait_count(const int* c, int target) {
@@ -258,6 +277,59 @@ __device__ void ch_norm(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc
       *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
+}
+
+// ---- all-reduce phase (epilogue warps): x += sum of the ranks' partials ------
+// CTA pc meets CTA pc of every other rank (flags of peer.cuh), then sums its
+// slice of the float4 elements over the ranks in rank order - every rank
+// computes the same x.  Each rank's CTA pc reaches the meeting only after its
+// own grid barrier, i.e. after all of that rank's partial tiles are stored.
+__device__ bool ch_peer(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc, int r) {
+  using namespace tsds::peer;
+  const ChPeer& g = p.pr;
+  if (r == 0) {
+    const uint32_t e = g.counters[pc] + 1;
+    g.counters[pc] = e;
+    sh.epoch = e;
+    sh.peer_ok = 1;
+  }
+  epi_bar();
+  const uint32_t e = sh.epoch;
+  if (r < g.tp) {
+    __threadfence_system();
+    st_release_sys(g.flags[r] + pc * PEER_MAX_RANKS + g.rank, e);
+    if (!wait_flag(g.flags[g.rank] + pc * PEER_MAX_RANKS + r, e)) {
+      sh.peer_ok = 0;
+      atomicExch(p.status, TSDS_E_TIMEOUT);
+    }
+  }
+  epi_bar();
+  if (!sh.peer_ok) return false;
+  const int n4 = ph.n / 4;
+  const int64_t total = (int64_t)p.M * n4;
+  for (int64_t i = (int64_t)pc * 128 + r; i < total; i += (int64_t)p.P * 128) {
+    const int m = (int)(i / n4), c4 = (int)(i - (int64_t)m * n4);
+    float4 v[PEER_MAX_RANKS];
+#pragma unroll
+    for (int q = 0; q < PEER_MAX_RANKS; ++q)
+      if (q < g.tp) v[q] = ld_volatile_f4(g.slot[ph.slot][q] + (int64_t)m * ph.n + 4 * c4);
+    float4 s = v[0];
+#pragma unroll
+    for (int q = 1; q < PEER_MAX_RANKS; ++q)
+      if (q < g.tp) {
+        s.x += v[q].x;
+        s.y += v[q].y;
+        s.z += v[q].z;
+        s.w += v[q].w;
+      }
+    uint2* xp = reinterpret_cast<uint2*>(ph.out + (int64_t)m * ph.ldo) + c4;
+    const uint2 xv = __ldcg(xp);
+    uint2 o;
+    o.x = pack_bf2(bf_lo(xv.x) + rbf(s.x), bf_hi(xv.x) + rbf(s.y));
+    o.y = pack_bf2(bf_lo(xv.y) + rbf(s.z), bf_hi(xv.y) + rbf(s.w));
+    *xp = o;
+  }
+  return true;
 }
 
 // ---- one GEMM phase on the epilogue warps --------------------------------------
@@ -588,6 +660,8 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
       }
       if (ph.kind == CH_NORM) {
         ch_norm(p, ph, sh, pc, r);
+      } else if (ph.kind == CH_PEER) {
+        alive = ch_peer(p, ph, sh, pc, r);
       } else {
         switch (ph.epi) {
           case EPI_STORE: ch_gemm_epilogue<EPI_STORE>(p, ph, sh, tmem, pc, r, seg, alive); break;
@@ -640,7 +714,8 @@ extern "C" size_t tsds_fused_layer_workspace_bytes(int M) {
 }
 
 extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
-                          void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
+                                const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
+                                tsds_stream_t stream) {
   TSDS_RETURN_IF(!phases || n_phases < 1 || n_phases > CH_MAX_PHASES || M <= 0 || M > 256, TSDS_E_INVALID);
   TSDS_RETURN_IF(!workspace || workspace_bytes < tsds_fused_layer_workspace_bytes(M), TSDS_E_WORKSPACE);
   TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
@@ -672,6 +747,32 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     ChPhase& ph = p.ph[f];
     ph.kind = in.kind;
     ph.epi = in.epi;
+    if (in.kind == TSDS_PHASE_PEER) {
+      using namespace tsds::peer;
+      TSDS_RETURN_IF(!peers || !peers->bufs || peers->tp < 1 || peers->tp > PEER_MAX_RANKS || peers->rank < 0 ||
+                         peers->rank >= peers->tp || p.P > PEER_MAX_CTAS,
+                     TSDS_E_INVALID);
+      TSDS_RETURN_IF(!in.out || in.K <= 0 || (in.K % 4) != 0 || in.ldo < in.K || (in.n_out & ~1) != 0 ||
+                         (int64_t)M * in.K > peers->max_elems,
+                     TSDS_E_INVALID);
+      TSDS_RETURN_IF((reinterpret_cast<uintptr_t>(in.out) & 7u) != 0 || (in.ldo % 4) != 0, TSDS_E_ALIGN);
+      for (int q = 0; q < peers->tp; ++q) {
+        TSDS_RETURN_IF(!peers->bufs[q], TSDS_E_INVALID);
+        TSDS_RETURN_IF(!tsds_aligned16(peers->bufs[q]), TSDS_E_ALIGN);
+        char* base = static_cast<char*>(peers->bufs[q]);
+        p.pr.slot[0][q] = reinterpret_cast<const float*>(base + slot_offset(peers->max_elems, 0));
+        p.pr.slot[1][q] = reinterpret_cast<const float*>(base + slot_offset(peers->max_elems, 1));
+        p.pr.flags[q] = reinterpret_cast<uint32_t*>(base + PEER_FLAGS_OFF);
+      }
+      p.pr.counters = static_cast<uint32_t*>(peers->bufs[peers->rank]);
+      p.pr.rank = peers->rank;
+      p.pr.tp = peers->tp;
+      ph.out = (bf16*)in.out;
+      ph.n = in.K;
+      ph.ldo = in.ldo;
+      ph.slot = in.n_out;
+      continue;
+    }
     if (in.kind == TSDS_PHASE_NORM) {
       TSDS_RETURN_IF(!in.x || !in.w || !in.out || in.K <= 0 || (in.K % 8) != 0, TSDS_E_INVALID);
       TSDS_RETURN_IF(in.ldx < in.K || in.ldo < in.K, TSDS_E_INVALID);

@@ -2,11 +2,7 @@
 // with the residual add.
 //
 // Every rank owns one peer buffer (cudaMalloc'd here, shared with the other
-// ranks of the node through CUDA IPC):
-//
-//   [0, 1 KB)          counters[PEER_MAX_CTAS]  u32  this rank's per-CTA call count
-//   [1 KB, 9 KB)       flags[PEER_MAX_CTAS][8]  u32  flags[b][p] written by rank p
-//   [16 KB, ...)       slot 0, slot 1: max_elems fp32 each
+// ranks of the node through CUDA IPC; layout in peer.cuh).
 //
 // A row-parallel projection writes its fp32 partial [M][N] into this rank's
 // slot (calls alternate slots 0 / 1); tsds_peer_allreduce_residual then
@@ -25,24 +21,16 @@
 // Calls must be issued in the same order with the same (M, N) on every rank.
 // No TMA, no multicast: plain loads of peer memory.
 #include "common.cuh"
+#include "peer.cuh"
 
 #include <string.h>
 
 using namespace tsds;
+using namespace tsds::peer;
 
 namespace {
 
-constexpr int PEER_MAX_CTAS = 256;
-constexpr int PEER_MAX_RANKS = 8;
 constexpr int PEER_THREADS = 256;
-constexpr size_t PEER_FLAGS_OFF = 1024;
-constexpr size_t PEER_HEADER_BYTES = 16384;
-constexpr uint64_t PEER_WAIT_NS = 1000000000ull;
-
-static_assert(PEER_MAX_CTAS * 4 <= PEER_FLAGS_OFF, "counters overlap the flags");
-static_assert(PEER_FLAGS_OFF + PEER_MAX_CTAS * PEER_MAX_RANKS * 4 <= PEER_HEADER_BYTES, "flags overlap slot 0");
-
-size_t slot_bytes(int max_elems) { return ((size_t)max_elems * 4 + 255) / 256 * 256; }
 
 struct PeerArgs {
   const float* slot[PEER_MAX_RANKS];  // this call's slot in every rank's buffer
@@ -50,26 +38,6 @@ struct PeerArgs {
   uint32_t* counters;                 // this rank's counters
   int rank, tp;
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Peer data is read with volatile loads: never served from a stale cached line.
-__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.volatile.global.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(PEER_THREADS) peer_allreduce_residual_kernel(PeerArgs a, bf16* __restrict__ x,
                                                                                int64_t n4, int* __restrict__ status) {
@@ -88,15 +56,7 @@ __global__ void __launch_bounds__(PEER_THREADS) peer_allreduce_residual_kernel(P
   if (threadIdx.x < a.tp) {
     __threadfence_system();
     st_release_sys(a.flags[threadIdx.x] + b * PEER_MAX_RANKS + a.rank, e);
-    const uint32_t* f = a.flags[a.rank] + b * PEER_MAX_RANKS + threadIdx.x;
-    bool ok = (int)(ld_acquire_sys(f) - e) >= 0;
-    if (!ok) {
-      const uint64_t t0 = global_ns();
-      while (!(ok = (int)(ld_acquire_sys(f) - e) >= 0)) {
-        if (global_ns() - t0 > PEER_WAIT_NS) break;
-      }
-    }
-    if (!ok) {
+    if (!wait_flag(a.flags[a.rank] + b * PEER_MAX_RANKS + threadIdx.x, e)) {
       s_ok = 0;
       atomicExch(status, TSDS_E_TIMEOUT);
     }
@@ -133,9 +93,7 @@ extern "C" size_t tsds_peer_buffer_bytes(int max_elems) {
   return max_elems <= 0 ? 0 : PEER_HEADER_BYTES + 2 * slot_bytes(max_elems);
 }
 
-extern "C" size_t tsds_peer_slot_offset(int max_elems, int slot) {
-  return PEER_HEADER_BYTES + (size_t)(slot & 1) * slot_bytes(max_elems);
-}
+extern "C" size_t tsds_peer_slot_offset(int max_elems, int slot) { return slot_offset(max_elems, slot); }
 
 extern "C" size_t tsds_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
 

@@ -37,13 +37,18 @@ def _p(t):
     return None if t is None else _VP(t.data_ptr())
 
 
-def _fused_args(phases: list, rope: dict | None, M: int, ws, ws_bytes: int) -> tuple:
-    """tsds_fused_layer arguments (after the name) from phase dicts of pointers and
-    sizes: a tsds_fused_phase array and a tsds_qk_rope, kept alive by the
-    argument tuple itself."""
+def _fused_args(phases: list, rope: dict | None, peer, M: int, ws, ws_bytes: int) -> tuple:
+    """tsds_fused_layer arguments (after the name) from phase dicts of
+    pointers and sizes: a tsds_fused_phase array, a tsds_qk_rope and a
+    tsds_peer_group (tp.PeerAllReduce), kept alive by the argument tuple."""
     arr = (_lib.FusedPhase * len(phases))(*[_lib.FusedPhase(**ph) for ph in phases])
     qr = ctypes.pointer(_lib.QkRope(**rope)) if rope is not None else None
-    return (arr, len(phases), M, qr, ws, ws_bytes)
+    pg = None
+    if peer is not None:
+        pg = ctypes.pointer(_lib.PeerGroup(bufs=ctypes.cast(peer.bufs, ctypes.c_void_p), rank=peer.rank,
+                                           tp=peer.size, max_elems=peer.max_elems))
+        pg._bufs = peer.bufs
+    return (arr, len(phases), M, qr, pg, ws, ws_bytes)
 
 
 def precompute_rope(dim: int, max_len: int, base: float, device) -> tuple[torch.Tensor, torch.Tensor]:
@@ -228,8 +233,9 @@ class QwenModel:
                                for m in range(1, M + 1))
         self.lm_ws = torch.zeros(max(self.lm_ws_bytes, 16), dtype=torch.uint8, device=dev)
         # fused-layer kernel (one launch for O -> norm -> gate/up -> down ->
-        # norm -> q/k/v of consecutive layers); its own zero-filled workspace
-        self.fused_layers = fused_layers and self.layer_tp == 1
+        # norm -> q/k/v of consecutive layers, under tensor parallelism with
+        # the peer all-reduces as phases); its own zero-filled workspace
+        self.fused_layers = fused_layers and (self.layer_tp == 1 or peer is not None)
         if self.fused_layers:
             self.fused_ws_bytes = _lib.query("tsds_fused_layer_workspace_bytes", M)
             self.fused_ws = torch.zeros(self.fused_ws_bytes, dtype=torch.uint8, device=dev)
@@ -304,13 +310,24 @@ class QwenModel:
         launch and one fused launch [O (+res) -> norm -> gate/up -> down (+res) ->
         next layer's norm -> q/k/v (+QK-norm, RoPE, KV write)]; the first
         is [norm -> q/k/v] of layer 0.  Same rounding as the per-op
-        plan; tensor parallelism is not supported here."""
+        plan.  Under tensor parallelism O and down store fp32 partials into
+        this rank's peer slots (alternating) and a peer all-reduce phase
+        adds their sum over the ranks to the residual."""
         s, ls = self.shape, self.lshape
         M = B * T
         eps = s.eps
         qn = self.qk_norm
         pl = Plan()
         N = s.hidden
+        peer = self.peer if self.layer_tp > 1 else None
+
+        def row_parallel(src, K, w, slot):
+            if peer is None:
+                return [gemm(_lib.EPI_RESIDUAL, src, K, w, N, out=xb, res=xb)]
+            part = dict(gemm(_lib.EPI_STORE_F32, src, K, w, N), out=peer.slot_ptr(slot), ldo=N)
+            reduce = dict(kind=_lib.PHASE_PEER, epi=0, x=None, ldx=0, K=N, w=None, n_out=slot, res_ld=0, res=None,
+                          out=_p(xb), ldo=N, eps=0.0)
+            return [part, reduce]
 
         def norm(w):
             return dict(kind=_lib.PHASE_NORM, epi=0, x=_p(xb), ldx=N, K=N, w=_p(w), n_out=0, res_ld=0, res=None,
@@ -330,7 +347,7 @@ class QwenModel:
             return [norm(L.ln1), gemm(_lib.EPI_QKROPE, self.xn, N, L.w_qkv, ls.qkv_dim)], rope
 
         phases, rope = qkv(0)
-        pl.add("tsds_fused_layer", *_fused_args(phases, rope, M, _p(self.fused_ws), self.fused_ws_bytes))
+        pl.add("tsds_fused_layer", *_fused_args(phases, rope, peer, M, _p(self.fused_ws), self.fused_ws_bytes))
         n = len(self.layers)
         for i, L in enumerate(self.layers):
             kc, vc = self.k_cache[i], self.v_cache[i]
@@ -338,15 +355,14 @@ class QwenModel:
                    _p(tree_mask), mask_origin, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
                    self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
                    _p(self.status))
-            phases = [gemm(_lib.EPI_RESIDUAL, self.attn, ls.q_dim, L.w_o, N, out=xb, res=xb),
-                      norm(L.ln2),
-                      gemm(_lib.EPI_SWIGLU, self.xn, N, L.w_gu, ls.intermediate, out=self.h),
-                      gemm(_lib.EPI_RESIDUAL, self.h, ls.intermediate, L.w_d, N, out=xb, res=xb)]
+            phases = (row_parallel(self.attn, ls.q_dim, L.w_o, 0)
+                      + [norm(L.ln2), gemm(_lib.EPI_SWIGLU, self.xn, N, L.w_gu, ls.intermediate, out=self.h)]
+                      + row_parallel(self.h, ls.intermediate, L.w_d, 1))
             rope = None
             if i + 1 < n:
                 nxt, rope = qkv(i + 1)
                 phases += nxt
-            pl.add("tsds_fused_layer", *_fused_args(phases, rope, M, _p(self.fused_ws), self.fused_ws_bytes))
+            pl.add("tsds_fused_layer", *_fused_args(phases, rope, peer, M, _p(self.fused_ws), self.fused_ws_bytes))
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,
@@ -453,7 +469,14 @@ class QwenModel:
         return allv.reshape(self.vocab_tp, *loc.shape).permute(1, 0, 2).reshape(loc.shape[0], -1)
 
     def check_status(self):
-        st = int(self.status.item())
-        if st != 0:
-            self.status.zero_()
-            raise RuntimeError(f"device status {st}: {_lib.load().tsds_status_string(st).decode()}")
+        """Raise if a kernel recorded an error in a status word: attention's,
+        or word 0 of the tcgen05 GEMM, LM-head or fused-layer workspaces (a
+        bounded device wait that gave up)."""
+        words = [self.status, self.lin_ws[:4].view(torch.int32), self.lm_ws[:4].view(torch.int32)]
+        if self.fused_layers:
+            words.append(self.fused_ws[:4].view(torch.int32))
+        for w in words:
+            st = int(w.item())
+            if st != 0:
+                w.zero_()
+                raise RuntimeError(f"device status {st}: {_lib.load().tsds_status_string(st).decode()}")
