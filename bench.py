@@ -61,6 +61,9 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--breakdown", type=int, default=0, metavar="CYCLES",
+                    help="also time every library call of CYCLES eager cycles (CUDA events around each call) "
+                         "and add the per-entry-point totals to the JSON line")
     ap.add_argument("--fused-layers", action="store_true",
                     help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v (N = 1)")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
@@ -247,6 +250,41 @@ def run_reference(a, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def plan_breakdown(plan, cycles: int) -> dict:
+    """Device time of every call of a launch plan over `cycles` eager runs,
+    with CUDA events around each call (so neighbouring kernels cannot overlap
+    as they do under programmatic dependent launch in the graph: the sum
+    exceeds the cycle time).  Returns {"calls": [{"call", "per_cycle",
+    "us_per_cycle", "share"}] sorted by time, "sum_us_per_cycle"}."""
+    import ctypes
+
+    import torch
+    from tri_sds_b200 import _lib
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    marks = []
+    for _ in range(cycles):
+        for name, fn, args in plan.calls:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if fn is None:
+                args()
+            else:
+                st = fn(*args, s)
+                if st != 0:
+                    raise RuntimeError(f"{name} failed: {_lib.load().tsds_status_string(st).decode()}")
+            e1.record()
+            marks.append((name, e0, e1))
+    torch.cuda.synchronize()
+    tot, cnt = {}, {}
+    for name, e0, e1 in marks:
+        tot[name] = tot.get(name, 0.0) + e0.elapsed_time(e1) * 1e3 / cycles
+        cnt[name] = cnt.get(name, 0) + 1
+    total = sum(tot.values())
+    rows = [{"call": n, "per_cycle": cnt[n] // cycles, "us_per_cycle": round(tot[n], 1),
+             "share": round(tot[n] / total, 4)} for n in sorted(tot, key=tot.get, reverse=True)]
+    return {"calls": rows, "sum_us_per_cycle": round(total, 1)}
+
+
 def run_tsds(a, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -271,7 +309,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
     rows_verify = B * 26 if a.mode == "eagle" else B * (K + 1)
-    max_seq = P + (3 * a.warmup + 2 * a.steps) * per_cycle + 64 + 32
+    max_seq = P + (3 * a.warmup + 2 * a.steps + a.breakdown) * per_cycle + 64 + 32
     max_seq = (max_seq + 63) // 64 * 64
     # N > 1: the target is tensor-parallel over all ranks (shards drawn per
     # rank; replicated tensors from the same seed on every rank)
@@ -329,6 +367,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     ms_max, tokens_all = float(t[0]), tokens
     value = tokens_all / (ms_max / 1e3)
     launches_per_cycle = engine.plan_launches
+
+    breakdown = plan_breakdown(engine.plan, a.breakdown) if a.breakdown > 0 else None
 
     # ---- verify step alone (target forward over K+1 tokens) ------------------
     vplan = engine.verify_only_plan()
@@ -429,6 +469,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
         }
+        if breakdown is not None:
+            line["breakdown"] = breakdown
         print(json.dumps(line), flush=True)
     # CUDA graphs that hold NCCL calls go before the process group does
     engine.graph = None
