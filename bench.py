@@ -61,6 +61,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--pair-rows", type=int, default=None,
+                    help="token rows from which the tcgen05 GEMM runs on CTA pairs (library default 0: never)")
     ap.add_argument("--breakdown", type=int, default=0, metavar="CYCLES",
                     help="also time every library call of CYCLES eager cycles (CUDA events around each call) "
                          "and add the per-entry-point totals to the JSON line")
@@ -305,6 +307,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
     if a.no_pdl:
         _lib.load().tsds_set_pdl(0)
+    if a.pair_rows is not None:
+        _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
@@ -468,6 +472,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
+            "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
         }
         if breakdown is not None:
             line["breakdown"] = breakdown

@@ -130,6 +130,12 @@ int tsds_get_gemv_max_rows(void);
 /* Resident CTAs per SM of the tcgen05 GEMM (1..4, default 2; lowered
  * automatically when the accumulators would not fit in TMEM).  Tuning knob. */
 void tsds_set_gemm_ctas_per_sm(int n);
+/* Token rows M from which the tcgen05 GEMM runs on CTA pairs (two SMs per
+ * 256-row weight tile, tcgen05 cta_group::2, each SM staging half of the
+ * token rows; not the LM head); 0 (default): never.  Process-wide tuning
+ * switch for large M. */
+void tsds_set_gemm_pair_rows(int rows);
+int tsds_get_gemm_pair_rows(void);
 int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                 void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,

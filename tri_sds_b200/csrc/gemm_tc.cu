@@ -154,7 +154,15 @@ __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t,
   }
 }
 
-template <int EPI>
+// CG = 1: one CTA per tile of 128 weight rows.  CG = 2: a CTA pair on two
+// SMs (cluster of 2) per tile of 256 rows - each CTA stages its 128 weight
+// rows and half of the token rows, the leader (cluster rank 0) issues the
+// pair's MMAs (tcgen05 cta_group::2) and every CTA finishes its own half as
+// "virtual tile" vt = t * 2 + rank, so counters, partials and epilogues keep
+// their one-CTA meaning.  The pair halves the activation bytes each SM stages
+// per weight byte, which leaves room for more weight stages in flight when
+// the token count is large.
+template <int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -162,7 +170,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   __shared__ Smem sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pc = blockIdx.x;
-  const int b = it_begin(pc, p.P, p.W), e = it_begin(pc + 1, p.P, p.W);
+  const int crank = CG == 2 ? (int)cluster_ctarank() : 0;
+  const int unit = pc / CG, PU = p.P / CG;  // stream-K units: CTAs or CTA pairs
+  const int b = it_begin(unit, PU, p.W), e = it_begin(unit + 1, PU, p.W);
   const int KT = p.KT;
 
   if (threadIdx.x == 0) {
@@ -172,18 +182,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sh.tfull_bar[i], 1);
-      mbar_init(&sh.tempty_bar[i], 4);
+      mbar_init(&sh.tempty_bar[i], 4 * CG);  // every epilogue warp of the pair
     }
     sh.abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
-                 "r"(2 * p.tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (CG == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                   "r"(2 * p.tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                   "r"(2 * p.tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // both CTAs' barriers and TMEM exist before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
   uint8_t* a_smem = smem;
@@ -201,16 +218,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       const int npre = (e - b) < p.stages ? (e - b) : p.stages;
       auto load_a = [&](int it, int s) {
         const int t = it / KT, kt = it % KT;
-        const int row0 = EPI == EPI_SWIGLU ? t * 64 : t * TILE_J;
-        const int row1 = EPI == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
-        tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
-        tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
+        if constexpr (CG == 2) {
+          // this CTA's 128 rows of the pair's 256; bytes counted on the leader's barrier
+          const int row0 = EPI == EPI_SWIGLU ? t * 128 + crank * 64 : t * 256 + crank * 128;
+          const int row1 = EPI == EPI_SWIGLU ? p.up_off + t * 128 + crank * 64 : row0 + 64;
+          const uint32_t bar = mapa_shared(smem_u32(&sh.full_bar[s]), 0);
+          tma_load_2d_pair(a_smem + s * A_STAGE, &amap, bar, kt * BK, row0);
+          tma_load_2d_pair(a_smem + s * A_STAGE + A_STAGE / 2, &amap, bar, kt * BK, row1);
+        } else {
+          const int row0 = EPI == EPI_SWIGLU ? t * 64 : t * TILE_J;
+          const int row1 = EPI == EPI_SWIGLU ? p.up_off + t * 64 : t * TILE_J + 64;
+          tma_load_2d(a_smem + s * A_STAGE, &amap, &sh.full_bar[s], kt * BK, row0);
+          tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, &amap, &sh.full_bar[s], kt * BK, row1);
+        }
       };
       auto load_b = [&](int it, int s) {
-        tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], (it % KT) * BK, 0);
+        if constexpr (CG == 2)  // this CTA's half of the token rows
+          tma_load_2d_pair(b_smem + s * p.b_stage_bytes, &bmap, mapa_shared(smem_u32(&sh.full_bar[s]), 0),
+                           (it % KT) * BK, crank * (p.Npad / 2));
+        else
+          tma_load_2d(b_smem + s * p.b_stage_bytes, &bmap, &sh.full_bar[s], (it % KT) * BK, 0);
+      };
+      // the leader's full barrier counts both CTAs' bytes of a stage
+      auto expect = [&](int s) {
+        if (crank == 0) mbar_arrive_expect_tx(&sh.full_bar[s], CG * (A_STAGE + p.b_stage_bytes));
       };
       for (int i = 0; i < npre; ++i) {
-        mbar_arrive_expect_tx(&sh.full_bar[i], A_STAGE + p.b_stage_bytes);
+        expect(i);
         load_a(b + i, i);
       }
       pdl_wait();
@@ -224,7 +258,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           break;
         }
         if (*(volatile int*)&sh.abort) break;
-        mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+        expect(s);
         load_a(it, s);
         load_b(it, s);
       }
@@ -232,8 +266,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       pdl_wait();
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0 && b < e) {
+    // ---------------- MMA issuer (the pair's leader for CG = 2) ----------------
+    if (lane == 0 && b < e && crank == 0) {
       int i = 0, seg = 0;
       bool ok = true;
       for (int t = (int)(b / KT); ok && t <= (int)((e - 1) / KT); ++t, ++seg) {
@@ -257,13 +291,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           const uint32_t a_base = smem_u32(a_smem + s * A_STAGE);
           const uint32_t b_base = smem_u32(b_smem + s * p.b_stage_bytes);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
-                      (kt > k0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sh.empty_bar[s]);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            if constexpr (CG == 2)
+              umma_bf16_pair(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                             (kt > k0 || kk > 0) ? 1u : 0u);
+            else
+              umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                        (kt > k0 || kk > 0) ? 1u : 0u);
+          }
+          if constexpr (CG == 2)
+            umma_commit_pair(&sh.empty_bar[s]);  // frees stage s in both CTAs
+          else
+            umma_commit(&sh.empty_bar[s]);
         }
         if (!ok) break;
-        umma_commit(&sh.tfull_bar[buf]);
+        if constexpr (CG == 2)
+          umma_commit_pair(&sh.tfull_bar[buf]);
+        else
+          umma_commit(&sh.tfull_bar[buf]);
       }
       if (!ok) {
         atomicExch(p.status, TSDS_E_TIMEOUT);
@@ -286,6 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     bool alive = b < e;
     for (int t = (int)(b / KT); alive && t <= (int)((e - 1) / KT); ++t, ++seg) {
       const int tb = t * KT;
+      const int vt = t * CG + crank;  // this CTA's 128-row tile
       const int k0 = (int)((b > tb ? b : tb) - tb);
       const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
       const int buf = seg & 1, use = seg >> 1;
@@ -314,7 +360,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         float v[16];
         tmem_ld16(taddr + c * 16, v);
         if (full) {
-          finish_chunk<EPI>(p, sh, t, r, c * 16, v);
+          finish_chunk<EPI>(p, sh, vt, r, c * 16, v);
         } else {
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
@@ -323,23 +369,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.tempty_bar[buf]);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_remote(mapa_shared(smem_u32(&sh.tempty_bar[buf]), 0));  // the leader's MMA reuses it
+        else
+          mbar_arrive(&sh.tempty_bar[buf]);
+      }
       if (!full && DIST) {
         // arrive without waiting: a split tile is only a first or a last
         // segment, so there are at most two
         __threadfence();
         epi_bar();
-        if (r == 0) atomicAdd(&p.counters[t], 1);
+        if (r == 0) atomicAdd(&p.counters[vt], 1);
         if (npend++ == 0)
           pend0 = t;
         else
           pend1 = t;
       } else if (!full) {
-        // contributors of tile t: CTAs q_lo..q_hi, in order
-        const int q_lo = owner_of(tb, p.P, p.W), q_hi = owner_of(tb + KT - 1, p.P, p.W);
+        // contributors of tile t: units q_lo..q_hi, in order
+        const int q_lo = owner_of(tb, PU, p.W), q_hi = owner_of(tb + KT - 1, PU, p.W);
         __threadfence();
         epi_bar();
-        if (r == 0) sh.last = (atomicAdd(&p.counters[t], 1) == q_hi - q_lo);
+        if (r == 0) sh.last = (atomicAdd(&p.counters[vt], 1) == q_hi - q_lo);
         epi_bar();
         if (sh.last) {
           __threadfence();
@@ -350,7 +401,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           // holds it in slot 1 unless its range starts exactly at the tile.
           constexpr int FIX_Q = EPI == EPI_RESIDUAL ? 5 : 6;
           const int nq = q_hi - q_lo + 1;
-          const int lo_slot = it_begin(q_lo, p.P, p.W) < tb ? 1 : 0;
+          const int lo_slot = it_begin(q_lo, PU, p.W) < tb ? 1 : 0;
           for (int c = 0; c < nchunk; ++c) {
             float v[16];
 #pragma unroll
@@ -360,7 +411,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 #pragma unroll
               for (int i = 0; i < FIX_Q; ++i) {
                 if (q0 + i < nq) {
-                  const int q = q_lo + q0 + i;
+                  const int q = (q_lo + q0 + i) * CG + crank;  // the contributor's CTA for this half
                   const int qs = q0 + i == 0 ? lo_slot : 0;
                   const float4* src =
                       reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
@@ -383,9 +434,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                 }
               }
             }
-            finish_chunk<EPI>(p, sh, t, r, c * 16, v);
+            finish_chunk<EPI>(p, sh, vt, r, c * 16, v);
           }
-          if (r == 0) p.counters[t] = 0;  // ready for the next launch
+          if (r == 0) p.counters[vt] = 0;  // ready for the next launch
         }
       }
     }
@@ -396,16 +447,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       // partials in CTA order; the last to leave resets the counters.
       for (int pi = 0; alive && pi < npend; ++pi) {
         const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
-        const int q_lo = owner_of(tb, p.P, p.W), q_hi = owner_of(tb + KT - 1, p.P, p.W);
-        const int nq = q_hi - q_lo + 1, c = pc - q_lo;
-        const int lo_slot = it_begin(q_lo, p.P, p.W) < tb ? 1 : 0;
+        const int vt = t * CG + crank;
+        const int q_lo = owner_of(tb, PU, p.W), q_hi = owner_of(tb + KT - 1, PU, p.W);
+        const int nq = q_hi - q_lo + 1, c = unit - q_lo;
+        const int lo_slot = it_begin(q_lo, PU, p.W) < tb ? 1 : 0;
         const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
         const int nel = R * (p.Npad / 4);
         if (r == 0) {
           int ok = 1;
-          if (ld_acquire(&p.counters[t]) < nq) {
+          if (ld_acquire(&p.counters[vt]) < nq) {
             const uint64_t t0 = global_ns();
-            while (ld_acquire(&p.counters[t]) < nq) {
+            while (ld_acquire(&p.counters[vt]) < nq) {
               if (global_ns() - t0 > 2000000000ull) {
                 ok = 0;
                 break;
@@ -424,7 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
         for (int e0 = r; e0 < nel; e0 += 128) {
           const int rr = rlo + e0 % R, g = e0 / R;
-          const int j = t * TILE_J + rr;
+          const int j = vt * TILE_J + rr;
           float rv[4] = {0.f, 0.f, 0.f, 0.f};
           if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
@@ -438,7 +490,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 #pragma unroll
             for (int i = 0; i < QB; ++i)
               if (q0 + i < nq) {
-                const int q = q_lo + q0 + i;
+                const int q = (q_lo + q0 + i) * CG + crank;
                 const int qs = q0 + i == 0 ? lo_slot : 0;
                 f[i] = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
                               (size_t)g * TILE_J + rr);
@@ -470,18 +522,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           }
         }
         epi_bar();
-        if (r == 0 && atomicAdd(&p.counters[MAX_TILES + t], 1) == nq - 1) {
-          p.counters[t] = 0;  // every contributor has left: ready for the next launch
-          p.counters[MAX_TILES + t] = 0;
+        if (r == 0 && atomicAdd(&p.counters[MAX_TILES + vt], 1) == nq - 1) {
+          p.counters[vt] = 0;  // every contributor has left: ready for the next launch
+          p.counters[MAX_TILES + vt] = 0;
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // the pair is done with both TMEM halves
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
   }
 }
 
@@ -491,6 +547,8 @@ int g_num_sms = 0;
 // 5.5 TB/s for the bare TMA stream).  Capped so both fit in TMEM (512
 // columns) and shared memory.
 int g_ctas_per_sm = 2;
+// Token rows from which a projection runs on CTA pairs (CG = 2); 0: never.
+int g_pair_min_rows = 0;
 constexpr int SMEM_PER_SM = 233472;    // 228 KB
 constexpr int SMEM_RESERVE = 8192;     // static shared memory + per-CTA system reserve
 
@@ -509,17 +567,22 @@ int num_sms() {
 }  // namespace
 
 extern "C" void tsds_set_gemm_ctas_per_sm(int n) { g_ctas_per_sm = n < 1 ? 1 : (n > 4 ? 4 : n); }
+extern "C" void tsds_set_gemm_pair_rows(int rows) { g_pair_min_rows = rows < 0 ? 0 : rows; }
+extern "C" int tsds_get_gemm_pair_rows(void) { return g_pair_min_rows; }
 int tsds_tc_num_sms() { return num_sms(); }
 int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
 
 namespace {
 
-template <int EPI>
+template <int EPI, int CG>
 int launch_tc(const CUtensorMap& amap, const CUtensorMap& bmap, const TcParams& p, size_t smem, cudaStream_t stream) {
   static bool attr[TSDS_MAX_DEVICES] = {};
-  const int st = tsds_smem_limit_once(tc_gemm_kernel<EPI>, SMEM_BUDGET, attr);
+  const int st = tsds_smem_limit_once(tc_gemm_kernel<EPI, CG>, SMEM_BUDGET, attr);
   if (st != TSDS_OK) return st;
-  tsds_launch(tc_gemm_kernel<EPI>, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
+  if constexpr (CG == 2)
+    tsds_launch_cluster(tc_gemm_kernel<EPI, CG>, dim3(p.P), dim3(NUM_THREADS), smem, stream, 2, amap, bmap, p);
+  else
+    tsds_launch(tc_gemm_kernel<EPI, CG>, dim3(p.P), dim3(NUM_THREADS), smem, stream, amap, bmap, p);
   return tsds_launch_status();
 }
 
@@ -552,16 +615,21 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.n_out = n_out;
   p.K = K;
   p.KT = (K + BK - 1) / BK;
-  p.tiles = epi == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + TILE_J - 1) / TILE_J;
-  TSDS_RETURN_IF(p.tiles > MAX_TILES, TSDS_E_UNSUPPORTED);
+  // CTA pairs (256-row tiles, half the token rows per CTA) from g_pair_min_rows
+  // rows on; not for the LM head's argmax epilogue (its candidates are per
+  // 128-row tile of a vocabulary that need not fill whole pairs)
+  const int CG = (g_pair_min_rows > 0 && M >= g_pair_min_rows && epi != EPI_ARGMAX) ? 2 : 1;
+  p.tiles = epi == EPI_SWIGLU ? (n_out + 64 * CG - 1) / (64 * CG) : (n_out + TILE_J * CG - 1) / (TILE_J * CG);
+  TSDS_RETURN_IF(p.tiles * CG > MAX_TILES, TSDS_E_UNSUPPORTED);
   const long long W64 = (long long)p.tiles * p.KT;
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = g_ctas_per_sm;
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
-  const long long slots = (long long)num_sms() * ctas;
-  p.P = (int)(W64 < slots ? W64 : slots);
+  const long long units = (long long)num_sms() * ctas / CG;
+  const long long PU = W64 < units ? W64 : units;
+  p.P = (int)(PU * CG);
   // the kernel's stream-K bookkeeping is 32-bit
-  TSDS_RETURN_IF(W64 * p.P >= (1ll << 32), TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF(W64 * PU >= (1ll << 32), TSDS_E_UNSUPPORTED);
   p.W = (uint32_t)W64;
   p.up_off = n_out;
   p.ldo = ldo;
@@ -574,26 +642,38 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.cand_val = cand_val;
   p.cand_idx = cand_idx;
   p.ldc = ldc;
-  p.b_stage_bytes = p.Npad * BK * 2;
+  p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows
   int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
   if (budget > SMEM_BUDGET) budget = SMEM_BUDGET;
   p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
   if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
   TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
-  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) | ((uint32_t)(TILE_J >> 4) << 24);
+  // instruction descriptor: bf16 x bf16 -> fp32, K-major A and B, N = Npad,
+  // M = 128 rows per CTA (256 for a pair)
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) |
+            ((uint32_t)((TILE_J * CG) >> 4) << 24);
 
   CUtensorMap amap, bmap;
   int st = tsds_make_tmap_2d_bf16(&amap, W, K, w_rows, (uint64_t)K * 2, BK, 64, 1);
   if (st != TSDS_OK) return st;
-  st = tsds_make_tmap_2d_bf16(&bmap, x, K, M, (uint64_t)ldx * 2, BK, p.Npad, 1);
+  st = tsds_make_tmap_2d_bf16(&bmap, x, K, M, (uint64_t)ldx * 2, BK, p.Npad / CG, 1);
   if (st != TSDS_OK) return st;
   const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  if (CG == 2) {
+    switch (epi) {
+      case EPI_STORE: return launch_tc<EPI_STORE, 2>(amap, bmap, p, smem, stream);
+      case EPI_RESIDUAL: return launch_tc<EPI_RESIDUAL, 2>(amap, bmap, p, smem, stream);
+      case EPI_SWIGLU: return launch_tc<EPI_SWIGLU, 2>(amap, bmap, p, smem, stream);
+      case EPI_STORE_F32: return launch_tc<EPI_STORE_F32, 2>(amap, bmap, p, smem, stream);
+      default: return TSDS_E_INVALID;
+    }
+  }
   switch (epi) {
-    case EPI_STORE: return launch_tc<EPI_STORE>(amap, bmap, p, smem, stream);
-    case EPI_RESIDUAL: return launch_tc<EPI_RESIDUAL>(amap, bmap, p, smem, stream);
-    case EPI_SWIGLU: return launch_tc<EPI_SWIGLU>(amap, bmap, p, smem, stream);
-    case EPI_STORE_F32: return launch_tc<EPI_STORE_F32>(amap, bmap, p, smem, stream);
-    case EPI_ARGMAX: return launch_tc<EPI_ARGMAX>(amap, bmap, p, smem, stream);
+    case EPI_STORE: return launch_tc<EPI_STORE, 1>(amap, bmap, p, smem, stream);
+    case EPI_RESIDUAL: return launch_tc<EPI_RESIDUAL, 1>(amap, bmap, p, smem, stream);
+    case EPI_SWIGLU: return launch_tc<EPI_SWIGLU, 1>(amap, bmap, p, smem, stream);
+    case EPI_STORE_F32: return launch_tc<EPI_STORE_F32, 1>(amap, bmap, p, smem, stream);
+    case EPI_ARGMAX: return launch_tc<EPI_ARGMAX, 1>(amap, bmap, p, smem, stream);
     default: return TSDS_E_INVALID;
   }
 }
