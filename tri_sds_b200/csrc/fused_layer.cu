@@ -701,6 +701,28 @@ int pow2_at_least(int x) {
   return v;
 }
 
+// CTAs per SM that can be resident at once with `smem` dynamic bytes each:
+// the grid barrier needs the whole grid resident.  Cached per size (the
+// devices of one process are assumed alike).
+int resident_per_sm(size_t smem) {
+  static size_t keys[16];
+  static int vals[16];
+  static int n = 0;
+  for (int i = 0; i < n; ++i)
+    if (keys[i] == smem) return vals[i];
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fused_layer_kernel, CH_THREADS, smem) != cudaSuccess) {
+    cudaGetLastError();
+    blocks = 0;
+  }
+  if (n < 16) {
+    keys[n] = smem;
+    vals[n] = blocks;
+    ++n;
+  }
+  return blocks;
+}
+
 size_t partial_bytes(int M) {
   const int npad = M <= 0 ? 0 : (M + 15) / 16 * 16;
   return (size_t)tsds_tc_num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
@@ -727,7 +749,6 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = tsds_tc_ctas_setting();
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
-  p.P = tsds_tc_num_sms() * ctas;
   p.nph = n_phases;
   p.status = (int32_t*)workspace;
   p.gbar = (int*)((char*)workspace + 4);
@@ -740,6 +761,10 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
   if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
   TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) | ((uint32_t)(TILE_J >> 4) << 24);
+  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  // an upper bound while the phases are checked; lowered below to what can
+  // be resident at once (a smaller grid keeps every check valid)
+  p.P = tsds_tc_num_sms() * ctas;
   int ctr = 0;
   bool rope = false;
   for (int f = 0; f < n_phases; ++f) {
@@ -844,10 +869,14 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     st = tsds_make_tmap_2d_bf16(&maps.b[f], in.x, in.K, M, (uint64_t)in.ldx * 2, BK, p.Npad, 1);
     if (st != TSDS_OK) return st;
   }
-  static bool attr[TSDS_MAX_DEVICES] = {};
-  const int st = tsds_smem_limit_once(fused_layer_kernel, CH_SMEM_BUDGET, attr);
-  if (st != TSDS_OK) return st;
-  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  {
+    static bool attr[TSDS_MAX_DEVICES] = {};
+    const int st = tsds_smem_limit_once(fused_layer_kernel, CH_SMEM_BUDGET, attr);
+    if (st != TSDS_OK) return st;
+    const int resident = resident_per_sm(smem);
+    TSDS_RETURN_IF(resident < 1, TSDS_E_UNSUPPORTED);
+    if (resident < ctas) p.P = tsds_tc_num_sms() * resident;
+  }
   tsds_launch(fused_layer_kernel, dim3(p.P), dim3(CH_THREADS), smem, stream, maps, p);
   return tsds_launch_status();
 }

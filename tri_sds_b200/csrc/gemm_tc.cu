@@ -592,6 +592,54 @@ int pow2_at_least(int x) {
   return v;
 }
 
+// Clusters of two CTAs that can be resident at once with `smem` bytes each.
+// The split-tile reduction needs the whole grid resident, and a 2-CTA
+// cluster needs two SMs of one GPC, so the pair grid is sized from this
+// rather than from the SM count.  Cached per shared-memory size (the
+// devices of one process are assumed alike).
+template <int EPI>
+int max_pair_clusters(size_t smem) {
+  static size_t keys[16];
+  static int vals[16];
+  static int n = 0;
+  for (int i = 0; i < n; ++i)
+    if (keys[i] == smem) return vals[i];
+  static bool attr[TSDS_MAX_DEVICES] = {};
+  if (tsds_smem_limit_once(tc_gemm_kernel<EPI, 2>, SMEM_BUDGET, attr) != TSDS_OK) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute ca[1];
+  ca[0].id = cudaLaunchAttributeClusterDimension;
+  ca[0].val.clusterDim.x = 2;
+  ca[0].val.clusterDim.y = 1;
+  ca[0].val.clusterDim.z = 1;
+  cfg.attrs = ca;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_kernel<EPI, 2>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    clusters = 0;
+  }
+  if (n < 16) {
+    keys[n] = smem;
+    vals[n] = clusters;
+    ++n;
+  }
+  return clusters;
+}
+
+int pair_clusters(int epi, size_t smem) {
+  switch (epi) {
+    case EPI_STORE: return max_pair_clusters<EPI_STORE>(smem);
+    case EPI_RESIDUAL: return max_pair_clusters<EPI_RESIDUAL>(smem);
+    case EPI_SWIGLU: return max_pair_clusters<EPI_SWIGLU>(smem);
+    case EPI_STORE_F32: return max_pair_clusters<EPI_STORE_F32>(smem);
+    default: return 0;
+  }
+}
+
 }  // namespace
 
 // Workspace layout: [status int32, padding to 64 B][arrival counters: 2048 ints][departure counters:
@@ -625,7 +673,19 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = g_ctas_per_sm;
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
-  const long long units = (long long)num_sms() * ctas / CG;
+  p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows
+  int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
+  if (budget > SMEM_BUDGET) budget = SMEM_BUDGET;
+  p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
+  if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
+  TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
+  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  long long units = (long long)num_sms() * ctas / CG;
+  if (CG == 2) {
+    const int resident = pair_clusters(epi, smem);
+    TSDS_RETURN_IF(resident < 1, TSDS_E_UNSUPPORTED);
+    if (resident < units) units = resident;
+  }
   const long long PU = W64 < units ? W64 : units;
   p.P = (int)(PU * CG);
   // the kernel's stream-K bookkeeping is 32-bit
@@ -642,12 +702,6 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.cand_val = cand_val;
   p.cand_idx = cand_idx;
   p.ldc = ldc;
-  p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows
-  int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
-  if (budget > SMEM_BUDGET) budget = SMEM_BUDGET;
-  p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
-  if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
-  TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
   // instruction descriptor: bf16 x bf16 -> fp32, K-major A and B, N = Npad,
   // M = 128 rows per CTA (256 for a pair)
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) |
@@ -658,7 +712,6 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   if (st != TSDS_OK) return st;
   st = tsds_make_tmap_2d_bf16(&bmap, x, K, M, (uint64_t)ldx * 2, BK, p.Npad / CG, 1);
   if (st != TSDS_OK) return st;
-  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
   if (CG == 2) {
     switch (epi) {
       case EPI_STORE: return launch_tc<EPI_STORE, 2>(amap, bmap, p, smem, stream);
