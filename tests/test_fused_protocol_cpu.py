@@ -1,0 +1,274 @@
+"""Model check of the fused-layer kernel's synchronisation (CPU).
+
+The per-CTA roles of fused_layer.cu - TMA producer, MMA issuer, epilogue
+warps - are restated as generators that yield the condition they wait on,
+in the kernel's order: the ring of `stages` slots (full / empty barriers),
+the two TMEM accumulators (tfull / tempty), the stream-K split of each GEMM
+phase with its split-tile counters (arrive without waiting, reduce after
+all own arrivals; last arriver for whole-tile epilogues), the grid barrier
+between phases, and the per-CTA-index meetings of the peer all-reduce
+phase across ranks.  Random schedulers interleave every CTA of every rank;
+each run must finish (no deadlock) and respect the data dependencies:
+
+* a phase's activation tiles are loaded only after every CTA of the rank
+  has finished the previous phase;
+* a split tile is reduced only after all its contributors stored partials;
+* a rank's peer phase reads the other ranks' partials only after all of
+  their CTAs finished the GEMM phase that wrote them.
+"""
+import random
+
+import pytest
+
+
+def it_begin(p, P, W):
+    return p * W // P
+
+
+def phase_ctas(W, P):
+    """fused_layer.cu phase_range(): CTAs 0..Pf-1 split a phase's W, Pf = min(W, P)."""
+    return min(W, P)
+
+
+def phase_range(pc, Pf, W):
+    return (it_begin(pc, Pf, W), it_begin(pc + 1, Pf, W)) if pc < Pf else (0, 0)
+
+
+def owner_of(x, P, W):
+    q = min(x * P // W, P - 1)
+    while q + 1 < P and it_begin(q + 1, P, W) <= x:
+        q += 1
+    while q > 0 and it_begin(q, P, W) > x:
+        q -= 1
+    return q
+
+
+class Rank:
+    def __init__(self, P):
+        self.gbar = 0
+        self.counters = {}           # (phase, tile) -> arrivals
+        self.departed = {}
+        self.phase_done = [set() for _ in range(16)]   # CTAs finished with phase f
+        self.peer_ctr = [0] * P
+        self.flags = {}              # (cta, from_rank) -> epoch
+
+
+class CTA:
+    def __init__(self, rank, pc, stages):
+        self.rank, self.pc = rank, pc
+        self.full = [0] * stages     # completed phases of each full barrier
+        self.empty = [0] * stages
+        self.tfull = [0, 0]
+        self.tempty = [0, 0]         # arrivals / 4 warps -> completed phases
+
+
+def run(phases, P, stages, R, seed, split=phase_ctas):
+    """phases: list of ("gemm", W, KT, dist) | ("norm",) | ("peer",);
+    split(W, P): the number of CTAs sharing a GEMM phase's iterations."""
+    rnd = random.Random(seed)
+    ranks = [Rank(P) for _ in range(R)]
+    ctas = [[CTA(r, pc, stages) for pc in range(P)] for r in range(R)]
+
+    def producer(r, pc):
+        c = ctas[r][pc]
+        i = 0
+        for f, ph in enumerate(phases):
+            if ph[0] != "gemm":
+                continue
+            W, KT = ph[1], ph[2]
+            b, e = phase_range(pc, split(W, P), W)
+            if b >= e:
+                continue
+            npre = min(e - b, stages)
+            for k in range(npre):          # weight tiles first
+                s, rnd_ = (i + k) % stages, (i + k) // stages
+                if rnd_ > 0:
+                    yield lambda s=s, rnd_=rnd_: c.empty[s] >= rnd_
+            if f > 0:                      # activations after the grid barrier
+                yield lambda f=f: ranks[r].gbar >= P * f
+                assert len(ranks[r].phase_done[f - 1]) == P, "B tiles before the previous phase ended"
+            for k in range(npre):
+                c.full[(i + k) % stages] += 1
+            for k in range(npre, e - b):
+                s, rnd_ = (i + k) % stages, (i + k) // stages
+                yield lambda s=s, rnd_=rnd_: c.empty[s] >= rnd_
+                c.full[s] += 1
+            i += e - b
+
+    def mma(r, pc):
+        c = ctas[r][pc]
+        i = seg = 0
+        for f, ph in enumerate(phases):
+            if ph[0] != "gemm":
+                continue
+            W, KT = ph[1], ph[2]
+            b, e = phase_range(pc, split(W, P), W)
+            if b >= e:
+                continue
+            for t in range(b // KT, (e - 1) // KT + 1):
+                tb = t * KT
+                k0, k1 = max(b, tb) - tb, min(e, tb + KT) - tb
+                buf, use = seg & 1, seg >> 1
+                if use > 0:
+                    yield lambda buf=buf, use=use: c.tempty[buf] >= use
+                for _ in range(k0, k1):
+                    s, rnd_ = i % stages, i // stages
+                    yield lambda s=s, rnd_=rnd_: c.full[s] >= rnd_ + 1
+                    c.empty[s] += 1
+                    i += 1
+                c.tfull[buf] += 1
+                seg += 1
+
+    def epilogue(r, pc):
+        c = ctas[r][pc]
+        rk = ranks[r]
+        seg = 0
+        for f, ph in enumerate(phases):
+            if f > 0:
+                yield lambda f=f: rk.gbar >= P * f
+            if ph[0] == "peer":
+                e = rk.peer_ctr[pc] = rk.peer_ctr[pc] + 1
+                for q in range(R):
+                    ranks[q].flags[(pc, r)] = e
+                yield lambda e=e: all(rk.flags.get((pc, q), 0) >= e for q in range(R))
+                for q in range(R):   # the partials of every rank are complete
+                    assert len(ranks[q].phase_done[f - 1]) == P, "peer read before a rank's partials"
+            elif ph[0] == "gemm":
+                W, KT, dist = ph[1], ph[2], ph[3]
+                Pf = split(W, P)
+                b, e = phase_range(pc, Pf, W)
+                pend = []
+                if b < e:
+                    for t in range(b // KT, (e - 1) // KT + 1):
+                        tb = t * KT
+                        k0, k1 = max(b, tb) - tb, min(e, tb + KT) - tb
+                        buf, use = seg & 1, seg >> 1
+                        yield lambda buf=buf, use=use: c.tfull[buf] >= use + 1
+                        c.tempty[buf] += 1
+                        seg += 1
+                        if k0 == 0 and k1 == KT:
+                            continue
+                        key = (f, t)
+                        q_lo, q_hi = owner_of(tb, Pf, W), owner_of(tb + KT - 1, Pf, W)
+                        rk.counters[key] = rk.counters.get(key, 0) + 1
+                        if dist:
+                            pend.append((t, q_hi - q_lo + 1))
+                        elif rk.counters[key] == q_hi - q_lo + 1:
+                            rk.counters[key] = 0   # last arriver finishes the tile
+                for t, nq in pend:
+                    key = (f, t)
+                    yield lambda key=key, nq=nq: rk.counters[key] >= nq
+                    rk.departed[key] = rk.departed.get(key, 0) + 1
+                    if rk.departed[key] == nq:
+                        rk.counters[key] = rk.departed[key] = 0
+            rk.phase_done[f].add(pc)
+            rk.gbar += 1
+
+    actors = []
+    for r in range(R):
+        for pc in range(P):
+            for role in (producer, mma, epilogue):
+                actors.append([role(r, pc), None, False])
+    steps = 0
+    while True:
+        live = [a for a in actors if not a[2]]
+        if not live:
+            break
+        ready = [a for a in live if a[1] is None or a[1]()]
+        assert ready, "deadlock"
+        a = rnd.choice(ready)
+        try:
+            a[1] = next(a[0])
+        except StopIteration:
+            a[2] = True
+        steps += 1
+        assert steps < 2_000_000
+    for rk in ranks:
+        assert rk.gbar == P * len(phases)
+        assert all(v == 0 for v in rk.counters.values())
+
+
+# a decoder layer's phases; (W, KT) chosen so tiles split across CTAs
+LAYER = [("gemm", 5 * 4, 4, True), ("norm",), ("gemm", 9 * 4, 4, False), ("gemm", 5 * 6, 6, True), ("norm",),
+         ("gemm", 6 * 4, 4, False)]
+TP_LAYER = [("gemm", 5 * 4, 4, True), ("peer",), ("norm",), ("gemm", 9 * 4, 4, False), ("gemm", 5 * 6, 6, True),
+            ("peer",), ("norm",), ("gemm", 6 * 4, 4, False)]
+
+
+@pytest.mark.parametrize("P,stages", [(3, 2), (6, 3), (7, 5), (12, 2)])
+@pytest.mark.parametrize("seed", range(4))
+def test_single_rank_layer_never_deadlocks(P, stages, seed):
+    run(LAYER, P, stages, R=1, seed=seed)
+
+
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("seed", range(3))
+def test_tensor_parallel_layer_never_deadlocks(R, seed):
+    run(TP_LAYER, P=5, stages=3, R=R, seed=seed)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_fewer_iterations_than_ctas(seed):
+    """Phases with fewer iterations than CTAs (the small shapes of the tests):
+    the CTAs past Pf sit the phase out and every split tile's contributors
+    are consecutive CTAs that each own an iteration.  (Splitting over all P
+    CTAs instead counted CTAs with empty ranges as contributors, and their
+    tiles were never complete.)"""
+    run(SMALL_PHASES, P=8, stages=2, R=1, seed=seed)
+
+
+SMALL_PHASES = [("gemm", 4, 2, True), ("norm",), ("gemm", 3, 3, False), ("gemm", 6, 2, True)]
+
+
+def test_splitting_over_every_cta_deadlocks_small_phases():
+    """The check of the check: with all P CTAs sharing a phase of W < P
+    iterations, a split tile counts CTAs that own nothing as contributors
+    and its reduction waits for them forever."""
+    with pytest.raises(AssertionError, match="deadlock"):
+        run(SMALL_PHASES, P=8, stages=2, R=1, seed=0, split=lambda W, P: P)
+
+
+def test_the_model_catches_a_missing_barrier():
+    """Sanity check of the check: without the producer's barrier wait, some
+    schedule loads a phase's activations too early."""
+    import types
+    src = run.__code__
+    hit = False
+    for seed in range(40):
+        try:
+            _run_without_barrier(LAYER, P=4, stages=2, seed=seed)
+        except AssertionError as e:
+            hit = hit or "before the previous phase ended" in str(e)
+    assert hit and isinstance(src, types.CodeType)
+
+
+def _run_without_barrier(phases, P, stages, seed):
+    # the producer of run() with the grid-barrier wait removed
+    rnd = random.Random(seed)
+    rk = Rank(P)
+    done = [set() for _ in phases]
+
+    def producer(pc):
+        for f, ph in enumerate(phases):
+            if ph[0] != "gemm":
+                continue
+            yield lambda: True
+            if f > 0:
+                assert len(done[f - 1]) == P, "B tiles before the previous phase ended"
+
+    def epilogue(pc):
+        for f, ph in enumerate(phases):
+            if f > 0:
+                yield lambda f=f: rk.gbar >= P * f
+            yield lambda: True
+            done[f].add(pc)
+            rk.gbar += 1
+
+    actors = [[producer(pc), None, False] for pc in range(P)] + [[epilogue(pc), None, False] for pc in range(P)]
+    while any(not a[2] for a in actors):
+        ready = [a for a in actors if not a[2] and (a[1] is None or a[1]())]
+        a = rnd.choice(ready)
+        try:
+            a[1] = next(a[0])
+        except StopIteration:
+            a[2] = True

@@ -59,6 +59,7 @@ struct ChPhase {
   int n_out, K, KT, tiles;
   uint32_t W;                  // tiles x KT (host: W * P < 2^32)
   int up_off, ldo, res_ld, ctr;  // ctr: arrival counters at counters[ctr], departures at + tiles
+  int Pf;                        // CTAs sharing this phase's iterations: min(W, P), so each owns at least one
   const bf16* res;
   bf16* out;
   // NORM: out[m][0:n] (ldo) = RMSNorm(x[m][0:n]) * w
@@ -134,6 +135,14 @@ __device__ __forceinline__ bool wait_count(const int* c, int target) {
 // generic-proxy writes of this thread (and those it observed) before later
 // async-proxy (TMA) reads of the same global memory
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// This CTA's stream-K range of a GEMM phase: CTAs 0..Pf-1 split its W
+// iterations, every one of them owning at least one (so the contributors of
+// a split tile are consecutive CTAs); CTAs from Pf on sit the phase out.
+__device__ __forceinline__ void phase_range(const ChPhase& ph, int pc, int& b, int& e) {
+  b = pc < ph.Pf ? it_begin(pc, ph.Pf, ph.W) : 0;
+  e = pc < ph.Pf ? it_begin(pc + 1, ph.Pf, ph.W) : 0;
+}
 
 __device__ __forceinline__ float ldcg_bf(const bf16* p) {
   return __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(p)) << 16);
@@ -339,7 +348,8 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
   const int eq = r >> 5, lane = r & 31;
   const int nchunk = p.Npad / 16;
   const int KT = ph.KT;
-  const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+  int b, e;
+  phase_range(ph, pc, b, e);
   int* arr = p.counters + ph.ctr;
   int* dep = arr + ph.tiles;
   // STORE / RESIDUAL / STORE_F32: split tiles reduced by all contributors;
@@ -391,7 +401,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         else
           pend1 = t;
       } else if (!full) {
-        const int q_lo = owner_of(tb, p.P, ph.W), q_hi = owner_of(tb + KT - 1, p.P, ph.W);
+        const int q_lo = owner_of(tb, ph.Pf, ph.W), q_hi = owner_of(tb + KT - 1, ph.Pf, ph.W);
         __threadfence();
         epi_bar();
         if (r == 0) sh.last = (atomicAdd(&arr[t], 1) == q_hi - q_lo);
@@ -399,7 +409,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         if (sh.last) {
           __threadfence();
           const int nq = q_hi - q_lo + 1;
-          const int lo_slot = it_begin(q_lo, p.P, ph.W) < tb ? 1 : 0;
+          const int lo_slot = it_begin(q_lo, ph.Pf, ph.W) < tb ? 1 : 0;
           for (int c = 0; c < nchunk; ++c) {
             float v[16];
 #pragma unroll
@@ -428,9 +438,9 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
   if constexpr (DIST) {
     for (int pi = 0; alive && pi < npend; ++pi) {
       const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
-      const int q_lo = owner_of(tb, p.P, ph.W), q_hi = owner_of(tb + KT - 1, p.P, ph.W);
+      const int q_lo = owner_of(tb, ph.Pf, ph.W), q_hi = owner_of(tb + KT - 1, ph.Pf, ph.W);
       const int nq = q_hi - q_lo + 1, c = pc - q_lo;
-      const int lo_slot = it_begin(q_lo, p.P, ph.W) < tb ? 1 : 0;
+      const int lo_slot = it_begin(q_lo, ph.Pf, ph.W) < tb ? 1 : 0;
       const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
       const int nel = R * (p.Npad / 4);
       if (r == 0) {
@@ -532,7 +542,8 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
       for (int f = 0; ok && f < p.nph; ++f) {
         const ChPhase& ph = p.ph[f];
         if (ph.kind != CH_GEMM) continue;
-        const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+        int b, e;
+        phase_range(ph, pc, b, e);
         if (b >= e) continue;
         const CUtensorMap* am = &maps.a[f];
         const CUtensorMap* bm = &maps.b[f];
@@ -601,7 +612,8 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
       for (int f = 0; ok && f < p.nph; ++f) {
         const ChPhase& ph = p.ph[f];
         if (ph.kind != CH_GEMM) continue;
-        const int b = it_begin(pc, p.P, ph.W), e = it_begin(pc + 1, p.P, ph.W);
+        int b, e;
+        phase_range(ph, pc, b, e);
         if (b >= e) continue;
         const int KT = ph.KT;
         for (int t = b / KT; ok && t <= (e - 1) / KT; ++t, ++seg) {
@@ -829,6 +841,7 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     const long long W64 = (long long)ph.tiles * ph.KT;
     TSDS_RETURN_IF(W64 * p.P >= (1ll << 32), TSDS_E_UNSUPPORTED);
     ph.W = (uint32_t)W64;
+    ph.Pf = (int)(W64 < p.P ? W64 : p.P);  // lowered with P below
     ph.up_off = in.n_out;
     ph.ldo = in.ldo;
     ph.res = (const bf16*)in.res;
@@ -877,6 +890,8 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     TSDS_RETURN_IF(resident < 1, TSDS_E_UNSUPPORTED);
     if (resident < ctas) p.P = tsds_tc_num_sms() * resident;
   }
+  for (int f = 0; f < n_phases; ++f)
+    if (p.ph[f].kind == CH_GEMM && p.ph[f].Pf > p.P) p.ph[f].Pf = p.P;
   tsds_launch(fused_layer_kernel, dim3(p.P), dim3(CH_THREADS), smem, stream, maps, p);
   return tsds_launch_status();
 }
