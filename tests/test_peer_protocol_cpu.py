@@ -1,0 +1,131 @@
+"""Model check of the peer all-reduce protocol (CPU).
+
+tsds_peer_allreduce_residual (and the peer phase of the fused-layer kernel)
+rely on two claims: every rank's partial is complete when a CTA passes its
+meeting, and two alternating slots are enough - a rank writes slot s again
+only two calls later, when no rank can still be reading it.  Here each rank
+is a stream of kernels in order (the row-parallel GEMM writing slot i % 2 of
+call i, then the all-reduce whose CTAs meet the same CTA index of every
+rank through per-CTA call counters and flags, wait with `>=`, and read
+every rank's slot).  Random schedulers interleave the ranks' streams and
+the CTAs inside each all-reduce; every run must finish and:
+
+* a CTA reads a rank's slot only after that rank's GEMM for the call wrote it;
+* a rank's GEMM never overwrites a slot some rank is still to read.
+"""
+import random
+
+import pytest
+
+
+def run(R, G, calls, seed, grids=None):
+    """R ranks, all-reduce grids of G CTAs (grids[i] per call when given:
+    every rank uses the same grid for a call), `calls` calls."""
+    rnd = random.Random(seed)
+    written = {}                         # (rank, call) -> written
+    readers_left = {}                    # (rank, slot) -> set of (reader rank, cta) still to read it
+    counters = [[0] * 64 for _ in range(R)]
+    flags = [[[0] * R for _ in range(64)] for _ in range(R)]   # flags[owner][cta][from]
+
+    def stream(r):
+        for i in range(calls):
+            g = grids[i] if grids else G
+            slot = i % 2
+            # the GEMM of call i: every earlier kernel of this rank has finished
+            assert not readers_left.get((r, slot)), f"rank {r} overwrites slot {slot} still being read (call {i})"
+            written[(r, i)] = True
+            readers_left[(r, slot)] = {(q, b) for q in range(R) for b in range(g)}
+            yield None
+            # the all-reduce of call i: G CTAs, concurrent
+            ctas = [cta(r, b, i, slot) for b in range(g)]
+            pending = [[c, None] for c in ctas]
+            while pending:
+                ready = [p for p in pending if p[1] is None or p[1]()]
+                if not ready:
+                    yield lambda pending=pending: any(p[1] is None or p[1]() for p in pending)
+                    continue
+                p = rnd.choice(ready)
+                try:
+                    p[1] = next(p[0])
+                except StopIteration:
+                    pending.remove(p)
+                yield None
+
+    def cta(r, b, i, slot):
+        e = counters[r][b] = counters[r][b] + 1
+        for q in range(R):
+            flags[q][b][r] = e
+        yield lambda: all(flags[r][b][q] >= e for q in range(R))
+        for q in range(R):
+            assert written.get((q, i)), f"rank {r} cta {b} read rank {q}'s slot before call {i} wrote it"
+            readers_left[(q, slot)].discard((r, b))
+            yield None
+
+    actors = [[stream(r), None, False] for r in range(R)]
+    steps = 0
+    while any(not a[2] for a in actors):
+        ready = [a for a in actors if not a[2] and (a[1] is None or a[1]())]
+        assert ready, "deadlock"
+        a = rnd.choice(ready)
+        try:
+            a[1] = next(a[0])
+        except StopIteration:
+            a[2] = True
+        steps += 1
+        assert steps < 1_000_000
+
+
+@pytest.mark.parametrize("R,G", [(2, 1), (2, 4), (4, 3), (8, 2)])
+@pytest.mark.parametrize("seed", range(5))
+def test_two_slots_and_per_cta_meetings(R, G, seed):
+    run(R, G, calls=8, seed=seed)
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_grids_that_change_between_calls(seed):
+    """Calls of different sizes (different M) use different grids; a CTA
+    index skipped by a small call keeps its counter behind on every rank
+    alike, so the flags still agree."""
+    run(R=3, G=None, calls=9, seed=seed, grids=[4, 1, 3, 4, 2, 4, 1, 1, 3])
+
+
+def test_the_check_catches_a_single_slot():
+    """The check of the check: with one slot a rank overwrites partials that
+    a slower rank has not read yet."""
+    hit = False
+    for seed in range(30):
+        try:
+            _run_one_slot(R=3, G=2, calls=6, seed=seed)
+        except AssertionError as e:
+            hit = hit or "still being read" in str(e)
+    assert hit
+
+
+def _run_one_slot(R, G, calls, seed):
+    rnd = random.Random(seed)
+    readers_left = {}
+    counters = [[0] * G for _ in range(R)]
+    flags = [[[0] * R for _ in range(G)] for _ in range(R)]
+
+    def stream(r):
+        for i in range(calls):
+            assert not readers_left.get(r), f"rank {r} overwrites slot 0 still being read (call {i})"
+            readers_left[r] = {(q, b) for q in range(R) for b in range(G)}
+            yield None
+            for b in range(G):
+                e = counters[r][b] = counters[r][b] + 1
+                for q in range(R):
+                    flags[q][b][r] = e
+                yield lambda b=b, e=e: all(flags[r][b][q] >= e for q in range(R))
+                for q in range(R):
+                    readers_left[q].discard((r, b))
+                    yield None
+
+    actors = [[stream(r), None, False] for r in range(R)]
+    while any(not a[2] for a in actors):
+        ready = [a for a in actors if not a[2] and (a[1] is None or a[1]())]
+        a = rnd.choice(ready)
+        try:
+            a[1] = next(a[0])
+        except StopIteration:
+            a[2] = True
