@@ -62,21 +62,37 @@ class CTA:
         self.tempty = [0, 0]         # arrivals / 4 warps -> completed phases
 
 
-def run(phases, P, stages, R, seed, split=phase_ctas):
+def run(phases, P, stages, R, seed, split=phase_ctas, CG=1):
     """phases: list of ("gemm", W, KT, dist) | ("norm",) | ("peer",);
-    split(W, P): the number of CTAs sharing a GEMM phase's iterations."""
+    split(W, units): the number of units sharing a GEMM phase's iterations;
+    CG = 2: CTA pairs (cta_group::2) - both CTAs' loads complete on the
+    leader's full barrier, the leader alone issues MMAs and commits to both
+    CTAs, both epilogues arrive on the leader's accumulator-empty barrier."""
     rnd = random.Random(seed)
+    assert P % CG == 0
+    units = P // CG
+    per_round = 1 + 2 * CG           # leader's expect + A and B loads of every CTA of the unit
     ranks = [Rank(P) for _ in range(R)]
     ctas = [[CTA(r, pc, stages) for pc in range(P)] for r in range(R)]
+    for r in range(R):
+        for c in ctas[r]:
+            c.full_count = [0] * stages
+
+    def land(leader, s, rnd_):
+        # a transfer of round rnd_ must not reach the barrier before round rnd_-1 completed
+        assert leader.full_count[s] >= rnd_ * per_round, "a load reached the next round of a full barrier"
+        leader.full_count[s] += 1
 
     def producer(r, pc):
         c = ctas[r][pc]
+        unit, crank = pc // CG, pc % CG
+        leader = ctas[r][unit * CG]
         i = 0
         for f, ph in enumerate(phases):
             if ph[0] != "gemm":
                 continue
             W, KT = ph[1], ph[2]
-            b, e = phase_range(pc, split(W, P), W)
+            b, e = phase_range(unit, split(W, units), W)
             if b >= e:
                 continue
             npre = min(e - b, stages)
@@ -84,25 +100,36 @@ def run(phases, P, stages, R, seed, split=phase_ctas):
                 s, rnd_ = (i + k) % stages, (i + k) // stages
                 if rnd_ > 0:
                     yield lambda s=s, rnd_=rnd_: c.empty[s] >= rnd_
+                if crank == 0:
+                    land(leader, s, rnd_)  # expect
+                land(leader, s, rnd_)      # A
             if f > 0:                      # activations after the grid barrier
                 yield lambda f=f: ranks[r].gbar >= P * f
                 assert len(ranks[r].phase_done[f - 1]) == P, "B tiles before the previous phase ended"
             for k in range(npre):
-                c.full[(i + k) % stages] += 1
+                s, rnd_ = (i + k) % stages, (i + k) // stages
+                land(leader, s, rnd_)      # B
             for k in range(npre, e - b):
                 s, rnd_ = (i + k) % stages, (i + k) // stages
                 yield lambda s=s, rnd_=rnd_: c.empty[s] >= rnd_
-                c.full[s] += 1
+                if crank == 0:
+                    land(leader, s, rnd_)
+                land(leader, s, rnd_)
+                land(leader, s, rnd_)
             i += e - b
 
     def mma(r, pc):
+        if pc % CG:
+            return
         c = ctas[r][pc]
+        pair = [ctas[r][pc + q] for q in range(CG)]
+        unit = pc // CG
         i = seg = 0
         for f, ph in enumerate(phases):
             if ph[0] != "gemm":
                 continue
             W, KT = ph[1], ph[2]
-            b, e = phase_range(pc, split(W, P), W)
+            b, e = phase_range(unit, split(W, units), W)
             if b >= e:
                 continue
             for t in range(b // KT, (e - 1) // KT + 1):
@@ -110,18 +137,22 @@ def run(phases, P, stages, R, seed, split=phase_ctas):
                 k0, k1 = max(b, tb) - tb, min(e, tb + KT) - tb
                 buf, use = seg & 1, seg >> 1
                 if use > 0:
-                    yield lambda buf=buf, use=use: c.tempty[buf] >= use
+                    yield lambda buf=buf, use=use: c.tempty[buf] >= use * CG
                 for _ in range(k0, k1):
                     s, rnd_ = i % stages, i // stages
-                    yield lambda s=s, rnd_=rnd_: c.full[s] >= rnd_ + 1
-                    c.empty[s] += 1
+                    yield lambda s=s, rnd_=rnd_: c.full_count[s] >= (rnd_ + 1) * per_round
+                    for q in pair:         # commit to every CTA of the unit
+                        q.empty[s] += 1
                     i += 1
-                c.tfull[buf] += 1
+                for q in pair:
+                    q.tfull[buf] += 1
                 seg += 1
 
     def epilogue(r, pc):
         c = ctas[r][pc]
         rk = ranks[r]
+        unit, crank = pc // CG, pc % CG
+        leader = ctas[r][unit * CG]
         seg = 0
         for f, ph in enumerate(phases):
             if f > 0:
@@ -135,8 +166,8 @@ def run(phases, P, stages, R, seed, split=phase_ctas):
                     assert len(ranks[q].phase_done[f - 1]) == P, "peer read before a rank's partials"
             elif ph[0] == "gemm":
                 W, KT, dist = ph[1], ph[2], ph[3]
-                Pf = split(W, P)
-                b, e = phase_range(pc, Pf, W)
+                Pf = split(W, units)
+                b, e = phase_range(unit, Pf, W)
                 pend = []
                 if b < e:
                     for t in range(b // KT, (e - 1) // KT + 1):
@@ -144,19 +175,18 @@ def run(phases, P, stages, R, seed, split=phase_ctas):
                         k0, k1 = max(b, tb) - tb, min(e, tb + KT) - tb
                         buf, use = seg & 1, seg >> 1
                         yield lambda buf=buf, use=use: c.tfull[buf] >= use + 1
-                        c.tempty[buf] += 1
+                        leader.tempty[buf] += 1
                         seg += 1
                         if k0 == 0 and k1 == KT:
                             continue
-                        key = (f, t)
+                        key = (f, t * CG + crank)
                         q_lo, q_hi = owner_of(tb, Pf, W), owner_of(tb + KT - 1, Pf, W)
                         rk.counters[key] = rk.counters.get(key, 0) + 1
                         if dist:
-                            pend.append((t, q_hi - q_lo + 1))
+                            pend.append((key, q_hi - q_lo + 1))
                         elif rk.counters[key] == q_hi - q_lo + 1:
                             rk.counters[key] = 0   # last arriver finishes the tile
-                for t, nq in pend:
-                    key = (f, t)
+                for key, nq in pend:
                     yield lambda key=key, nq=nq: rk.counters[key] >= nq
                     rk.departed[key] = rk.departed.get(key, 0) + 1
                     if rk.departed[key] == nq:
@@ -205,6 +235,18 @@ def test_single_rank_layer_never_deadlocks(P, stages, seed):
 @pytest.mark.parametrize("seed", range(3))
 def test_tensor_parallel_layer_never_deadlocks(R, seed):
     run(TP_LAYER, P=5, stages=3, R=R, seed=seed)
+
+
+@pytest.mark.parametrize("P,stages", [(4, 2), (8, 3), (12, 5)])
+@pytest.mark.parametrize("seed", range(4))
+def test_cta_pairs_never_deadlock_or_mix_rounds(P, stages, seed):
+    """CG = 2: both CTAs' loads complete on the leader's full barrier, yet a
+    transfer of the next round never reaches it before the current round
+    completed (each CTA waits for its own empty barrier, which the leader's
+    commit releases only after consuming the round)."""
+    run(LAYER, P, stages, R=1, seed=seed, CG=2)
+    run(SMALL_PHASES, P, stages, R=1, seed=seed, CG=2)
+    run(TP_LAYER, P, stages, R=2, seed=seed, CG=2)
 
 
 @pytest.mark.parametrize("seed", range(4))

@@ -59,7 +59,7 @@ struct ChPhase {
   int n_out, K, KT, tiles;
   uint32_t W;                  // tiles x KT (host: W * P < 2^32)
   int up_off, ldo, res_ld, ctr;  // ctr: arrival counters at counters[ctr], departures at + tiles
-  int Pf;                        // CTAs sharing this phase's iterations: min(W, P), so each owns at least one
+  int Pf;                        // units sharing this phase's iterations: min(W, units), so each owns one or more
   const bf16* res;
   bf16* out;
   // NORM: out[m][0:n] (ldo) = RMSNorm(x[m][0:n]) * w
@@ -136,12 +136,13 @@ __device__ __forceinline__ bool wait_count(const int* c, int target) {
 // async-proxy (TMA) reads of the same global memory
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// This CTA's stream-K range of a GEMM phase: CTAs 0..Pf-1 split its W
-// iterations, every one of them owning at least one (so the contributors of
-// a split tile are consecutive CTAs); CTAs from Pf on sit the phase out.
-__device__ __forceinline__ void phase_range(const ChPhase& ph, int pc, int& b, int& e) {
-  b = pc < ph.Pf ? it_begin(pc, ph.Pf, ph.W) : 0;
-  e = pc < ph.Pf ? it_begin(pc + 1, ph.Pf, ph.W) : 0;
+// A unit's stream-K range of a GEMM phase (a unit is a CTA, or a CTA pair
+// when CG = 2): units 0..Pf-1 split its W iterations, every one of them
+// owning at least one (so the contributors of a split tile are consecutive
+// units); units from Pf on sit the phase out.
+__device__ __forceinline__ void phase_range(const ChPhase& ph, int unit, int& b, int& e) {
+  b = unit < ph.Pf ? it_begin(unit, ph.Pf, ph.W) : 0;
+  e = unit < ph.Pf ? it_begin(unit + 1, ph.Pf, ph.W) : 0;
 }
 
 __device__ __forceinline__ float ldcg_bf(const bf16* p) {
@@ -197,6 +198,7 @@ __device__ __forceinline__ void ch_finish(const ChParams& p, const ChPhase& ph, 
   } else {  // EPI_QKROPE: the arithmetic of qk_norm_rope_kv_kernel, lane for lane
     const ChRope& q = p.qr;
     constexpr int D = 128;
+    if (t >= q.Hq + 2 * q.Hkv) return;  // the second half of a CTA pair past the last head (uniform)
     float(*xq)[8] = reinterpret_cast<float(*)[8]>(&sh.xch[0][0]);
     const int w = r >> 5, lane = r & 31;
     for (int half = 0; half < 2; ++half) {
@@ -342,16 +344,17 @@ __device__ bool ch_peer(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc
 }
 
 // ---- one GEMM phase on the epilogue warps --------------------------------------
-template <int EPI>
-__device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& sh, uint32_t tmem, int pc, int r,
-                                 int& seg, bool& alive) {
+template <int EPI, int CG>
+__device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& sh, uint32_t tmem, int pc, int crank,
+                                 int r, int& seg, bool& alive) {
   const int eq = r >> 5, lane = r & 31;
   const int nchunk = p.Npad / 16;
   const int KT = ph.KT;
+  const int unit = pc / CG;
   int b, e;
-  phase_range(ph, pc, b, e);
-  int* arr = p.counters + ph.ctr;
-  int* dep = arr + ph.tiles;
+  phase_range(ph, unit, b, e);
+  int* arr = p.counters + ph.ctr;  // per 128-row (virtual) tile
+  int* dep = arr + ph.tiles * CG;
   // STORE / RESIDUAL / STORE_F32: split tiles reduced by all contributors;
   // SWIGLU / QKROPE need whole tiles: the last arriver finishes them
   constexpr bool DIST = EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32;
@@ -359,6 +362,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
   if (b < e) {
     for (int t = b / KT; alive && t <= (e - 1) / KT; ++t, ++seg) {
       const int tb = t * KT;
+      const int vt = t * CG + crank;  // this CTA's 128-row tile
       const int k0 = (b > tb ? b : tb) - tb;
       const int k1 = (e < tb + KT ? e : tb + KT) - tb;
       const int buf = seg & 1, use = seg >> 1;
@@ -382,7 +386,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         float v[16];
         tmem_ld16(taddr + c * 16, v);
         if (full) {
-          ch_finish<EPI>(p, ph, sh, t, r, c * 16, v);
+          ch_finish<EPI>(p, ph, sh, vt, r, c * 16, v);
         } else {
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
@@ -391,11 +395,16 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.tempty_bar[buf]);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_remote(mapa_shared(smem_u32(&sh.tempty_bar[buf]), 0));  // the leader's MMA reuses it
+        else
+          mbar_arrive(&sh.tempty_bar[buf]);
+      }
       if (!full && DIST) {
         __threadfence();
         epi_bar();
-        if (r == 0) atomicAdd(&arr[t], 1);
+        if (r == 0) atomicAdd(&arr[vt], 1);
         if (npend++ == 0)
           pend0 = t;
         else
@@ -404,7 +413,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         const int q_lo = owner_of(tb, ph.Pf, ph.W), q_hi = owner_of(tb + KT - 1, ph.Pf, ph.W);
         __threadfence();
         epi_bar();
-        if (r == 0) sh.last = (atomicAdd(&arr[t], 1) == q_hi - q_lo);
+        if (r == 0) sh.last = (atomicAdd(&arr[vt], 1) == q_hi - q_lo);
         epi_bar();
         if (sh.last) {
           __threadfence();
@@ -414,8 +423,8 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
             float v[16];
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
-            for (int qi = 0; qi < nq; ++qi) {  // CTA order: deterministic
-              const int q = q_lo + qi;
+            for (int qi = 0; qi < nq; ++qi) {  // unit order: deterministic
+              const int q = (q_lo + qi) * CG + crank;  // the contributor's CTA for this half
               const int qs = qi == 0 ? lo_slot : 0;
               const float4* src = reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
                                   (size_t)c * 4 * TILE_J + r;
@@ -428,9 +437,9 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
                 v[4 * q4 + 3] += f.w;
               }
             }
-            ch_finish<EPI>(p, ph, sh, t, r, c * 16, v);
+            ch_finish<EPI>(p, ph, sh, vt, r, c * 16, v);
           }
-          if (r == 0) arr[t] = 0;  // ready for the next launch
+          if (r == 0) arr[vt] = 0;  // ready for the next launch
         }
       }
     }
@@ -438,13 +447,14 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
   if constexpr (DIST) {
     for (int pi = 0; alive && pi < npend; ++pi) {
       const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
+      const int vt = t * CG + crank;
       const int q_lo = owner_of(tb, ph.Pf, ph.W), q_hi = owner_of(tb + KT - 1, ph.Pf, ph.W);
-      const int nq = q_hi - q_lo + 1, c = pc - q_lo;
+      const int nq = q_hi - q_lo + 1, c = unit - q_lo;
       const int lo_slot = it_begin(q_lo, ph.Pf, ph.W) < tb ? 1 : 0;
       const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
       const int nel = R * (p.Npad / 4);
       if (r == 0) {
-        const bool ok = wait_count(&arr[t], nq);
+        const bool ok = wait_count(&arr[vt], nq);
         if (!ok) atomicExch(p.status, TSDS_E_TIMEOUT);
         sh.go = ok;
       }
@@ -457,7 +467,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
       }
       for (int e0 = r; e0 < nel; e0 += 128) {
         const int rr = rlo + e0 % R, g = e0 / R;
-        const int j = t * TILE_J + rr;
+        const int j = vt * TILE_J + rr;
         float rv[4] = {0.f, 0.f, 0.f, 0.f};
         if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
@@ -466,7 +476,7 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int qi = 0; qi < nq; ++qi) {
-          const int q = q_lo + qi;
+          const int q = (q_lo + qi) * CG + crank;
           const int qs = qi == 0 ? lo_slot : 0;
           const float4 f = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
                                   (size_t)g * TILE_J + rr);
@@ -493,14 +503,18 @@ __device__ void ch_gemm_epilogue(const ChParams& p, const ChPhase& ph, ChSmem& s
         }
       }
       epi_bar();
-      if (r == 0 && atomicAdd(&dep[t], 1) == nq - 1) {
-        arr[t] = 0;  // every contributor has left
-        dep[t] = 0;
+      if (r == 0 && atomicAdd(&dep[vt], 1) == nq - 1) {
+        arr[vt] = 0;  // every contributor has left
+        dep[vt] = 0;
       }
     }
   }
 }
 
+// CG = 2: CTA pairs (clusters of 2) for the GEMM phases - each CTA stages
+// its 128 weight rows of a 256-row tile and half of the token rows, the
+// leader issues the pair's MMAs (see gemm_tc.cu); row phases stay per CTA.
+template <int CG>
 __global__ void __launch_bounds__(CH_THREADS, 2)
     fused_layer_kernel(const __grid_constant__ ChMaps maps, const __grid_constant__ ChParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -508,6 +522,8 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
   __shared__ ChSmem sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pc = blockIdx.x;
+  const int crank = CG == 2 ? (int)cluster_ctarank() : 0;
+  const int unit = pc / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -516,18 +532,25 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sh.tfull_bar[i], 1);
-      mbar_init(&sh.tempty_bar[i], 4);
+      mbar_init(&sh.tempty_bar[i], 4 * CG);  // every epilogue warp of the pair
     }
     sh.abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
-                 "r"(2 * p.tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (CG == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                   "r"(2 * p.tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                   "r"(2 * p.tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // both CTAs' barriers and TMEM exist before any cross-CTA use
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
   uint8_t* a_smem = smem;
@@ -543,7 +566,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
         const ChPhase& ph = p.ph[f];
         if (ph.kind != CH_GEMM) continue;
         int b, e;
-        phase_range(ph, pc, b, e);
+        phase_range(ph, unit, b, e);
         if (b >= e) continue;
         const CUtensorMap* am = &maps.a[f];
         const CUtensorMap* bm = &maps.b[f];
@@ -553,13 +576,28 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
         const bool swiglu = ph.epi == EPI_SWIGLU;
         auto load_a = [&](int it, int s) {
           const int t = it / KT, kt = it % KT;
-          const int row0 = swiglu ? t * 64 : t * TILE_J;
-          const int row1 = swiglu ? ph.up_off + t * 64 : t * TILE_J + 64;
-          tma_load_2d(a_smem + s * A_STAGE, am, &sh.full_bar[s], kt * BK, row0);
-          tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, am, &sh.full_bar[s], kt * BK, row1);
+          if constexpr (CG == 2) {  // this CTA's 128 rows of the pair's 256, counted on the leader's barrier
+            const int row0 = swiglu ? t * 128 + crank * 64 : t * 256 + crank * 128;
+            const int row1 = swiglu ? ph.up_off + t * 128 + crank * 64 : row0 + 64;
+            const uint32_t bar = mapa_shared(smem_u32(&sh.full_bar[s]), 0);
+            tma_load_2d_pair(a_smem + s * A_STAGE, am, bar, kt * BK, row0);
+            tma_load_2d_pair(a_smem + s * A_STAGE + A_STAGE / 2, am, bar, kt * BK, row1);
+          } else {
+            const int row0 = swiglu ? t * 64 : t * TILE_J;
+            const int row1 = swiglu ? ph.up_off + t * 64 : t * TILE_J + 64;
+            tma_load_2d(a_smem + s * A_STAGE, am, &sh.full_bar[s], kt * BK, row0);
+            tma_load_2d(a_smem + s * A_STAGE + A_STAGE / 2, am, &sh.full_bar[s], kt * BK, row1);
+          }
         };
         auto load_b = [&](int it, int s) {
-          tma_load_2d(b_smem + s * p.b_stage_bytes, bm, &sh.full_bar[s], (it % KT) * BK, 0);
+          if constexpr (CG == 2)  // this CTA's half of the token rows
+            tma_load_2d_pair(b_smem + s * p.b_stage_bytes, bm, mapa_shared(smem_u32(&sh.full_bar[s]), 0),
+                             (it % KT) * BK, crank * (p.Npad / 2));
+          else
+            tma_load_2d(b_smem + s * p.b_stage_bytes, bm, &sh.full_bar[s], (it % KT) * BK, 0);
+        };
+        auto expect = [&](int s) {  // the leader's full barrier counts both CTAs' bytes
+          if (crank == 0) mbar_arrive_expect_tx(&sh.full_bar[s], CG * (A_STAGE + p.b_stage_bytes));
         };
         // weight tiles first: they do not depend on the earlier phases
         const int npre = (e - b) < p.stages ? (e - b) : p.stages;
@@ -569,7 +607,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+          expect(s);
           load_a(b + k, s);
         }
         if (!ok) break;
@@ -592,7 +630,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&sh.full_bar[s], A_STAGE + p.b_stage_bytes);
+          expect(s);
           load_a(b + k, s);
           load_b(b + k, s);
         }
@@ -606,14 +644,14 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    if (lane == 0 && crank == 0) {
       int i = 0, seg = 0;
       bool ok = true;
       for (int f = 0; ok && f < p.nph; ++f) {
         const ChPhase& ph = p.ph[f];
         if (ph.kind != CH_GEMM) continue;
         int b, e;
-        phase_range(ph, pc, b, e);
+        phase_range(ph, unit, b, e);
         if (b >= e) continue;
         const int KT = ph.KT;
         for (int t = b / KT; ok && t <= (e - 1) / KT; ++t, ++seg) {
@@ -637,13 +675,24 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
             const uint32_t a_base = smem_u32(a_smem + s * A_STAGE);
             const uint32_t b_base = smem_u32(b_smem + s * p.b_stage_bytes);
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk)
-              umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
-                        (kt > k0 || kk > 0) ? 1u : 0u);
-            umma_commit(&sh.empty_bar[s]);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              if constexpr (CG == 2)
+                umma_bf16_pair(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                               (kt > k0 || kk > 0) ? 1u : 0u);
+              else
+                umma_bf16(d, sdesc_sw128(a_base + kk * 32), sdesc_sw128(b_base + kk * 32), p.idesc,
+                          (kt > k0 || kk > 0) ? 1u : 0u);
+            }
+            if constexpr (CG == 2)
+              umma_commit_pair(&sh.empty_bar[s]);  // frees stage s in both CTAs
+            else
+              umma_commit(&sh.empty_bar[s]);
           }
           if (!ok) break;
-          umma_commit(&sh.tfull_bar[buf]);
+          if constexpr (CG == 2)
+            umma_commit_pair(&sh.tfull_bar[buf]);
+          else
+            umma_commit(&sh.tfull_bar[buf]);
         }
       }
       if (!ok) {
@@ -676,11 +725,11 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
         alive = ch_peer(p, ph, sh, pc, r);
       } else {
         switch (ph.epi) {
-          case EPI_STORE: ch_gemm_epilogue<EPI_STORE>(p, ph, sh, tmem, pc, r, seg, alive); break;
-          case EPI_RESIDUAL: ch_gemm_epilogue<EPI_RESIDUAL>(p, ph, sh, tmem, pc, r, seg, alive); break;
-          case EPI_SWIGLU: ch_gemm_epilogue<EPI_SWIGLU>(p, ph, sh, tmem, pc, r, seg, alive); break;
-          case EPI_STORE_F32: ch_gemm_epilogue<EPI_STORE_F32>(p, ph, sh, tmem, pc, r, seg, alive); break;
-          default: ch_gemm_epilogue<EPI_QKROPE>(p, ph, sh, tmem, pc, r, seg, alive); break;
+          case EPI_STORE: ch_gemm_epilogue<EPI_STORE, CG>(p, ph, sh, tmem, pc, crank, r, seg, alive); break;
+          case EPI_RESIDUAL: ch_gemm_epilogue<EPI_RESIDUAL, CG>(p, ph, sh, tmem, pc, crank, r, seg, alive); break;
+          case EPI_SWIGLU: ch_gemm_epilogue<EPI_SWIGLU, CG>(p, ph, sh, tmem, pc, crank, r, seg, alive); break;
+          case EPI_STORE_F32: ch_gemm_epilogue<EPI_STORE_F32, CG>(p, ph, sh, tmem, pc, crank, r, seg, alive); break;
+          default: ch_gemm_epilogue<EPI_QKROPE, CG>(p, ph, sh, tmem, pc, crank, r, seg, alive); break;
         }
       }
       if (!alive) break;
@@ -694,9 +743,13 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // the pair is done with both TMEM halves
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
   }
   // the last CTA out resets the phase counter for the next launch (every CTA
   // has finished waiting on it by then)
@@ -713,26 +766,51 @@ int pow2_at_least(int x) {
   return v;
 }
 
-// CTAs per SM that can be resident at once with `smem` dynamic bytes each:
-// the grid barrier needs the whole grid resident.  Cached per size (the
-// devices of one process are assumed alike).
-int resident_per_sm(size_t smem) {
+// CTAs that can be resident at once with `smem` dynamic bytes each (CG = 2:
+// as 2-CTA clusters, which need two SMs of one GPC): the grid barrier needs
+// the whole grid resident.  Cached per (CG, size); the devices of one
+// process are assumed alike.
+int resident_ctas(int CG, size_t smem) {
   static size_t keys[16];
   static int vals[16];
   static int n = 0;
+  const size_t key = smem * 2 + (CG == 2);
   for (int i = 0; i < n; ++i)
-    if (keys[i] == smem) return vals[i];
-  int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fused_layer_kernel, CH_THREADS, smem) != cudaSuccess) {
-    cudaGetLastError();
-    blocks = 0;
+    if (keys[i] == key) return vals[i];
+  int ctas = 0;
+  if (CG == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(CH_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute ca[1];
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = 2;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = 1;
+    cfg.attrs = ca;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fused_layer_kernel<2>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    ctas = 2 * clusters;
+  } else {
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fused_layer_kernel<1>, CH_THREADS, smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      blocks = 0;
+    }
+    ctas = blocks * tsds_tc_num_sms();
   }
   if (n < 16) {
-    keys[n] = smem;
-    vals[n] = blocks;
+    keys[n] = key;
+    vals[n] = ctas;
     ++n;
   }
-  return blocks;
+  return ctas;
 }
 
 size_t partial_bytes(int M) {
@@ -761,18 +839,22 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
   p.tmem_cols = pow2_at_least(p.Npad);
   int ctas = tsds_tc_ctas_setting();
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
+  // CTA pairs for the GEMM phases from the tcgen05 GEMM's pair threshold on
+  const int pr = tsds_tc_pair_rows();
+  const int CG = (pr > 0 && M >= pr) ? 2 : 1;
   p.nph = n_phases;
   p.status = (int32_t*)workspace;
   p.gbar = (int*)((char*)workspace + 4);
   p.counters = (int*)((char*)workspace + 64);
   p.ws = (float*)((char*)workspace + 64 + (size_t)CH_MAX_COUNTERS * sizeof(int));
-  p.b_stage_bytes = p.Npad * BK * 2;
+  p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows
   int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
   if (budget > CH_SMEM_BUDGET) budget = CH_SMEM_BUDGET;
   p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
   if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
   TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
-  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) | ((uint32_t)(TILE_J >> 4) << 24);
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) |
+            ((uint32_t)((TILE_J * CG) >> 4) << 24);
   const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
   // an upper bound while the phases are checked; lowered below to what can
   // be resident at once (a smaller grid keeps every check valid)
@@ -837,18 +919,20 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     ph.n_out = in.n_out;
     ph.K = in.K;
     ph.KT = (in.K + BK - 1) / BK;
-    ph.tiles = in.epi == EPI_SWIGLU ? (in.n_out + 63) / 64 : (in.n_out + TILE_J - 1) / TILE_J;
+    ph.tiles = in.epi == EPI_SWIGLU ? (in.n_out + 64 * CG - 1) / (64 * CG)
+                                    : (in.n_out + TILE_J * CG - 1) / (TILE_J * CG);
     const long long W64 = (long long)ph.tiles * ph.KT;
-    TSDS_RETURN_IF(W64 * p.P >= (1ll << 32), TSDS_E_UNSUPPORTED);
+    const int units = p.P / CG;
+    TSDS_RETURN_IF(W64 * units >= (1ll << 32), TSDS_E_UNSUPPORTED);
     ph.W = (uint32_t)W64;
-    ph.Pf = (int)(W64 < p.P ? W64 : p.P);  // lowered with P below
+    ph.Pf = (int)(W64 < units ? W64 : units);  // lowered with P below
     ph.up_off = in.n_out;
     ph.ldo = in.ldo;
     ph.res = (const bf16*)in.res;
     ph.res_ld = in.res_ld;
     ph.out = (bf16*)in.out;
     ph.ctr = ctr;
-    ctr += 2 * ph.tiles;
+    ctr += 2 * ph.tiles * CG;  // arrival and departure counters per 128-row tile
     TSDS_RETURN_IF(ctr > CH_MAX_COUNTERS, TSDS_E_UNSUPPORTED);
     if (in.epi == EPI_QKROPE) {
       TSDS_RETURN_IF(!qr || rope, TSDS_E_INVALID);  // one rope phase per launch (one parameter set)
@@ -879,19 +963,23 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     const int w_rows = in.epi == EPI_SWIGLU ? 2 * in.n_out : in.n_out;
     int st = tsds_make_tmap_2d_bf16(&maps.a[f], in.w, in.K, w_rows, (uint64_t)in.K * 2, BK, 64, 1);
     if (st != TSDS_OK) return st;
-    st = tsds_make_tmap_2d_bf16(&maps.b[f], in.x, in.K, M, (uint64_t)in.ldx * 2, BK, p.Npad, 1);
+    st = tsds_make_tmap_2d_bf16(&maps.b[f], in.x, in.K, M, (uint64_t)in.ldx * 2, BK, p.Npad / CG, 1);
     if (st != TSDS_OK) return st;
   }
   {
-    static bool attr[TSDS_MAX_DEVICES] = {};
-    const int st = tsds_smem_limit_once(fused_layer_kernel, CH_SMEM_BUDGET, attr);
+    static bool attr1[TSDS_MAX_DEVICES] = {}, attr2[TSDS_MAX_DEVICES] = {};
+    const int st = CG == 2 ? tsds_smem_limit_once(fused_layer_kernel<2>, CH_SMEM_BUDGET, attr2)
+                           : tsds_smem_limit_once(fused_layer_kernel<1>, CH_SMEM_BUDGET, attr1);
     if (st != TSDS_OK) return st;
-    const int resident = resident_per_sm(smem);
-    TSDS_RETURN_IF(resident < 1, TSDS_E_UNSUPPORTED);
-    if (resident < ctas) p.P = tsds_tc_num_sms() * resident;
+    const int resident = resident_ctas(CG, smem) / CG * CG;
+    TSDS_RETURN_IF(resident < CG, TSDS_E_UNSUPPORTED);
+    if (resident < p.P) p.P = resident;
   }
   for (int f = 0; f < n_phases; ++f)
-    if (p.ph[f].kind == CH_GEMM && p.ph[f].Pf > p.P) p.ph[f].Pf = p.P;
-  tsds_launch(fused_layer_kernel, dim3(p.P), dim3(CH_THREADS), smem, stream, maps, p);
+    if (p.ph[f].kind == CH_GEMM && p.ph[f].Pf > p.P / CG) p.ph[f].Pf = p.P / CG;
+  if (CG == 2)
+    tsds_launch_cluster(fused_layer_kernel<2>, dim3(p.P), dim3(CH_THREADS), smem, stream, 2, maps, p);
+  else
+    tsds_launch(fused_layer_kernel<1>, dim3(p.P), dim3(CH_THREADS), smem, stream, maps, p);
   return tsds_launch_status();
 }

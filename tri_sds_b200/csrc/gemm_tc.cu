@@ -571,6 +571,7 @@ extern "C" void tsds_set_gemm_pair_rows(int rows) { g_pair_min_rows = rows < 0 ?
 extern "C" int tsds_get_gemm_pair_rows(void) { return g_pair_min_rows; }
 int tsds_tc_num_sms() { return num_sms(); }
 int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
+int tsds_tc_pair_rows() { return g_pair_min_rows; }
 
 namespace {
 

@@ -24,6 +24,8 @@ int tsds_gemv_rows_limit();
 // CTAs-per-SM setting (tsds_set_gemm_ctas_per_sm) before the TMEM cap.
 int tsds_tc_num_sms();
 int tsds_tc_ctas_setting();
+// Token rows from which the tcgen05 kernels run on CTA pairs (0: never).
+int tsds_tc_pair_rows();
 
 // Fused-layer kernel only: q/k/v projection whose epilogue applies QK-norm + RoPE
 // and writes q and the K/V cache rows (one 128-row tile = one head).
