@@ -9,8 +9,8 @@
   of the oracle;
 * EAGLE greedy decoding with fused layers equals greedy autoregressive
   decoding.
-Runs only with TSDS_TEST_FUSED=1 until the kernel has been validated on a
-B200."""
+Runs only with TSDS_TEST_FUSED=1 (the CTA-pair case also with
+TSDS_TEST_PAIR=1) until the kernel has been validated on a B200."""
 import os
 
 import pytest
@@ -52,6 +52,23 @@ def _verify(m, ids, B, T, vocab):
 
 @pytest.mark.parametrize("B,T", [(1, 5), (8, 5), (1, 26), (8, 26)])
 def test_fused_equals_per_op_bitwise_qwen3_4b_shape(B, T):
+    _bitwise_case(B, T)
+
+
+@pytest.mark.skipif(os.environ.get("TSDS_TEST_PAIR") != "1", reason="CTA pairs: set TSDS_TEST_PAIR=1")
+@pytest.mark.parametrize("B,T", [(1, 26), (8, 26)])
+def test_fused_equals_per_op_bitwise_on_cta_pairs(B, T):
+    """Both plans' GEMMs on CTA pairs (the per-op GEMM and the fused
+    kernel's phases alike): still bit for bit."""
+    from tri_sds_b200 import _lib
+    _lib.load().tsds_set_gemm_pair_rows(1)
+    try:
+        _bitwise_case(B, T)
+    finally:
+        _lib.load().tsds_set_gemm_pair_rows(0)
+
+
+def _bitwise_case(B, T):
     S = 1024
     oshape, w, (ref, fus) = _models(Q4B, B, B * T, S, seed=B * 100 + T)
     g = torch.Generator().manual_seed(B + T)
