@@ -277,7 +277,11 @@ int tsds_gather_shards(const void* src, void* dst, int tp, int M, int vocab_shar
  *        buffers, fp32 [M][K]))), the same on every rank; the preceding
  *        STORE_F32 phase writes this rank's partial into that slot (ldo = K).
  *        The peer buffers are those of tsds_peer_allreduce_residual (*peers);
- *        the cross-rank wait is per CTA index and bounded (1 s).
+ *        the cross-rank wait is per CTA index and bounded (1 s).  epi 0:
+ *        one-shot (every rank reads every partial); epi 1: two-shot (each
+ *        rank reduces 1/tp of the elements, publishes them in its buffer,
+ *        and copies the others' after a second meeting) - same bits, a 1/tp
+ *        of the remote reads.
  * Workspace: tsds_fused_layer_workspace_bytes(M) bytes, 16-byte aligned, zero-filled
  * once (every launch leaves its counters zero again); word 0 is the status
  * word (TSDS_E_TIMEOUT after a bounded device wait gave up).  M <= 256.
@@ -338,7 +342,8 @@ int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const 
  * maps every other rank's with tsds_peer_import (another process of the same
  * node; close with tsds_peer_close, free its own with tsds_peer_free).
  * Buffer layout: per-CTA call counters and flags in the first 32 KB, then two
- * slots of max_elems fp32 at tsds_peer_slot_offset(max_elems, 0 / 1).
+ * slots of max_elems fp32 at tsds_peer_slot_offset(max_elems, 0 / 1), then
+ * max_elems bf16 published by the fused kernel's two-shot all-reduce.
  *
  * tsds_peer_allreduce_residual: the partial [M][N] fp32 of every rank sits in
  * slot `slot` of that rank's buffer (written there by tsds_linear_f32);

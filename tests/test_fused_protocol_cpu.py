@@ -157,13 +157,14 @@ def run(phases, P, stages, R, seed, split=phase_ctas, CG=1):
         for f, ph in enumerate(phases):
             if f > 0:
                 yield lambda f=f: rk.gbar >= P * f
-            if ph[0] == "peer":
-                e = rk.peer_ctr[pc] = rk.peer_ctr[pc] + 1
-                for q in range(R):
-                    ranks[q].flags[(pc, r)] = e
-                yield lambda e=e: all(rk.flags.get((pc, q), 0) >= e for q in range(R))
-                for q in range(R):   # the partials of every rank are complete
-                    assert len(ranks[q].phase_done[f - 1]) == P, "peer read before a rank's partials"
+            if ph[0] in ("peer", "peer2"):    # one-shot: one meeting; two-shot: two
+                for meeting in range(1 if ph[0] == "peer" else 2):
+                    e = rk.peer_ctr[pc] = rk.peer_ctr[pc] + 1
+                    for q in range(R):
+                        ranks[q].flags[(pc, r)] = e
+                    yield lambda e=e: all(rk.flags.get((pc, q), 0) >= e for q in range(R))
+                    for q in range(R):   # the partials of every rank are complete
+                        assert len(ranks[q].phase_done[f - 1]) == P, "peer read before a rank's partials"
             elif ph[0] == "gemm":
                 W, KT, dist = ph[1], ph[2], ph[3]
                 Pf = split(W, units)
@@ -235,6 +236,13 @@ def test_single_rank_layer_never_deadlocks(P, stages, seed):
 @pytest.mark.parametrize("seed", range(3))
 def test_tensor_parallel_layer_never_deadlocks(R, seed):
     run(TP_LAYER, P=5, stages=3, R=R, seed=seed)
+
+
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("seed", range(3))
+def test_tensor_parallel_layer_two_shot_never_deadlocks(R, seed):
+    layer = [("peer2",) if ph[0] == "peer" else ph for ph in TP_LAYER]
+    run(layer, P=5, stages=3, R=R, seed=seed)
 
 
 @pytest.mark.parametrize("P,stages", [(4, 2), (8, 3), (12, 5)])

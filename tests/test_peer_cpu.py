@@ -158,12 +158,13 @@ def test_peer_needs_matching_rank_and_room():
 
 def test_entry_point_checks_and_layout():
     """Argument checks return before any CUDA call; the layout is the
-    documented one (32 KB header, two 256-byte-rounded fp32 slots)."""
+    documented one (32 KB header, two 256-byte-rounded fp32 slots, then a
+    256-byte-rounded bf16 region published by the two-shot all-reduce)."""
     from tri_sds_b200 import _lib
     lib = _lib.load()
     assert lib.tsds_peer_handle_bytes() == 64
     assert lib.tsds_peer_buffer_bytes(0) == 0
-    assert lib.tsds_peer_buffer_bytes(1000) == 32768 + 2 * 4096
+    assert lib.tsds_peer_buffer_bytes(1000) == 32768 + 2 * 4096 + 2048
     assert lib.tsds_peer_slot_offset(1000, 0) == 32768 and lib.tsds_peer_slot_offset(1000, 1) == 32768 + 4096
     bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
     x = ctypes.c_void_p(0x30000)

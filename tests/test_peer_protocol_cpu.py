@@ -18,12 +18,17 @@ import random
 import pytest
 
 
-def run(R, G, calls, seed, grids=None):
+def run(R, G, calls, seed, grids=None, two_shot=False):
     """R ranks, all-reduce grids of G CTAs (grids[i] per call when given:
-    every rank uses the same grid for a call), `calls` calls."""
+    every rank uses the same grid for a call), `calls` calls.  two_shot: each
+    CTA reduces its share of its rank's chunk from every rank's slot,
+    publishes it, meets again, then copies the other ranks' published
+    chunks (the fused kernel's two-shot phase)."""
     rnd = random.Random(seed)
     written = {}                         # (rank, call) -> written
     readers_left = {}                    # (rank, slot) -> set of (reader rank, cta) still to read it
+    published = {}                       # (rank, cta) -> call whose chunk share is published
+    copiers_left = {}                    # (rank, cta) -> set of ranks still to copy that share
     counters = [[0] * 64 for _ in range(R)]
     flags = [[[0] * R for _ in range(64)] for _ in range(R)]   # flags[owner][cta][from]
 
@@ -51,14 +56,31 @@ def run(R, G, calls, seed, grids=None):
                     pending.remove(p)
                 yield None
 
-    def cta(r, b, i, slot):
+    def meet(r, b):
         e = counters[r][b] = counters[r][b] + 1
         for q in range(R):
             flags[q][b][r] = e
         yield lambda: all(flags[r][b][q] >= e for q in range(R))
+
+    def cta(r, b, i, slot):
+        yield from meet(r, b)
         for q in range(R):
             assert written.get((q, i)), f"rank {r} cta {b} read rank {q}'s slot before call {i} wrote it"
             readers_left[(q, slot)].discard((r, b))
+            yield None
+        if not two_shot:
+            return
+        # publish this CTA's share of the rank's chunk (the same share index
+        # is what CTA b of every other rank copies)
+        assert not copiers_left.get((r, b)), f"rank {r} cta {b} overwrites a published share still to be copied"
+        published[(r, b)] = i
+        copiers_left[(r, b)] = {q for q in range(R) if q != r}
+        yield from meet(r, b)
+        for q in range(R):
+            if q == r:
+                continue
+            assert published.get((q, b)) == i, f"rank {r} cta {b} copied rank {q}'s share before call {i} published it"
+            copiers_left[(q, b)].discard(r)
             yield None
 
     actors = [[stream(r), None, False] for r in range(R)]
@@ -79,6 +101,14 @@ def run(R, G, calls, seed, grids=None):
 @pytest.mark.parametrize("seed", range(5))
 def test_two_slots_and_per_cta_meetings(R, G, seed):
     run(R, G, calls=8, seed=seed)
+
+
+@pytest.mark.parametrize("R,G", [(2, 2), (4, 3), (8, 2)])
+@pytest.mark.parametrize("seed", range(5))
+def test_two_shot_publish_and_copy(R, G, seed):
+    """Two-shot: a share is copied only after this call published it, and
+    published again only after every rank copied it."""
+    run(R, G, calls=8, seed=seed, two_shot=True)
 
 
 @pytest.mark.parametrize("seed", range(5))

@@ -66,12 +66,13 @@ struct ChPhase {
   // PEER: out[m][0:n] (ldo) += sum over ranks of slot `slot` (fp32 [M][n])
   const bf16* x;
   const bf16* w;
-  int n, ldx, slot;
+  int n, ldx, slot, two_shot;
   float eps;
 };
 
 struct ChPeer {  // the ranks' peer buffers (see peer.cuh)
   const float* slot[2][PEER_MAX_RANKS];
+  bf16* published[PEER_MAX_RANKS];  // two-shot: each rank's final values of its chunk
   uint32_t* flags[PEER_MAX_RANKS];
   uint32_t* counters;
   int rank, tp;
@@ -291,11 +292,16 @@ __device__ void ch_norm(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc
 }
 
 // ---- all-reduce phase (epilogue warps): x += sum of the ranks' partials ------
-// CTA pc meets CTA pc of every other rank (flags of peer.cuh), then sums its
-// slice of the float4 elements over the ranks in rank order - every rank
-// computes the same x.  Each rank's CTA pc reaches the meeting only after its
-// own grid barrier, i.e. after all of that rank's partial tiles are stored.
-__device__ bool ch_peer(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc, int r) {
+// CTA pc meets CTA pc of every other rank (flags of peer.cuh).  Each rank's
+// CTA pc reaches a meeting only after its own grid barrier, i.e. after all
+// of that rank's partial tiles are stored.
+//  one-shot: every CTA then sums its slice of all elements over the ranks in
+//    rank order and updates x - every rank reads every rank's whole partial;
+//  two-shot: rank r sums only its chunk (elements [r*n/tp, (r+1)*n/tp)) in
+//    rank order, updates x there and publishes the bf16 result in its peer
+//    buffer; after a second meeting every rank copies the other chunks - a
+//    1/tp of the remote reads, the same bits.
+__device__ bool ch_meet(const ChParams& p, ChSmem& sh, int pc, int r) {
   using namespace tsds::peer;
   const ChPeer& g = p.pr;
   if (r == 0) {
@@ -315,30 +321,70 @@ __device__ bool ch_peer(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc
     }
   }
   epi_bar();
-  if (!sh.peer_ok) return false;
+  return sh.peer_ok != 0;
+}
+
+// x[i] (float4 index i of the [M][n] residual, stride ldo) += bf16(sum over ranks)
+__device__ __forceinline__ uint2 ch_reduce4(const ChPeer& g, const ChPhase& ph, int64_t i, uint2* xp) {
+  using namespace tsds::peer;
+  const int n4 = ph.n / 4;
+  const int m = (int)(i / n4), c4 = (int)(i - (int64_t)m * n4);
+  float4 v[PEER_MAX_RANKS];
+#pragma unroll
+  for (int q = 0; q < PEER_MAX_RANKS; ++q)
+    if (q < g.tp) v[q] = ld_volatile_f4(g.slot[ph.slot][q] + (int64_t)m * ph.n + 4 * c4);
+  float4 s = v[0];
+#pragma unroll
+  for (int q = 1; q < PEER_MAX_RANKS; ++q)
+    if (q < g.tp) {
+      s.x += v[q].x;
+      s.y += v[q].y;
+      s.z += v[q].z;
+      s.w += v[q].w;
+    }
+  const uint2 xv = __ldcg(xp);
+  uint2 o;
+  o.x = pack_bf2(bf_lo(xv.x) + rbf(s.x), bf_hi(xv.x) + rbf(s.y));
+  o.y = pack_bf2(bf_lo(xv.y) + rbf(s.z), bf_hi(xv.y) + rbf(s.w));
+  return o;
+}
+
+__device__ bool ch_peer(const ChParams& p, const ChPhase& ph, ChSmem& sh, int pc, int r) {
+  using namespace tsds::peer;
+  const ChPeer& g = p.pr;
+  if (!ch_meet(p, sh, pc, r)) return false;
   const int n4 = ph.n / 4;
   const int64_t total = (int64_t)p.M * n4;
-  for (int64_t i = (int64_t)pc * 128 + r; i < total; i += (int64_t)p.P * 128) {
+  auto x_at = [&](int64_t i) {
     const int m = (int)(i / n4), c4 = (int)(i - (int64_t)m * n4);
-    float4 v[PEER_MAX_RANKS];
-#pragma unroll
-    for (int q = 0; q < PEER_MAX_RANKS; ++q)
-      if (q < g.tp) v[q] = ld_volatile_f4(g.slot[ph.slot][q] + (int64_t)m * ph.n + 4 * c4);
-    float4 s = v[0];
-#pragma unroll
-    for (int q = 1; q < PEER_MAX_RANKS; ++q)
-      if (q < g.tp) {
-        s.x += v[q].x;
-        s.y += v[q].y;
-        s.z += v[q].z;
-        s.w += v[q].w;
-      }
-    uint2* xp = reinterpret_cast<uint2*>(ph.out + (int64_t)m * ph.ldo) + c4;
-    const uint2 xv = __ldcg(xp);
-    uint2 o;
-    o.x = pack_bf2(bf_lo(xv.x) + rbf(s.x), bf_hi(xv.x) + rbf(s.y));
-    o.y = pack_bf2(bf_lo(xv.y) + rbf(s.z), bf_hi(xv.y) + rbf(s.w));
+    return reinterpret_cast<uint2*>(ph.out + (int64_t)m * ph.ldo) + c4;
+  };
+  if (!ph.two_shot) {
+    for (int64_t i = (int64_t)pc * 128 + r; i < total; i += (int64_t)p.P * 128) {
+      uint2* xp = x_at(i);
+      *xp = ch_reduce4(g, ph, i, xp);
+    }
+    return true;
+  }
+  // two-shot: this rank's chunk, then publish
+  const int64_t c0 = total * g.rank / g.tp, c1 = total * (g.rank + 1) / g.tp;
+  uint2* mine = reinterpret_cast<uint2*>(g.published[g.rank]);
+  for (int64_t i = c0 + (int64_t)pc * 128 + r; i < c1; i += (int64_t)p.P * 128) {
+    uint2* xp = x_at(i);
+    const uint2 o = ch_reduce4(g, ph, i, xp);
     *xp = o;
+    mine[i] = o;
+  }
+  if (!ch_meet(p, sh, pc, r)) return false;  // every rank's chunk is published
+  for (int q = 0; q < g.tp; ++q) {
+    if (q == g.rank) continue;
+    const int64_t q0 = total * q / g.tp, q1 = total * (q + 1) / g.tp;
+    const uint2* theirs = reinterpret_cast<const uint2*>(g.published[q]);
+    for (int64_t i = q0 + (int64_t)pc * 128 + r; i < q1; i += (int64_t)p.P * 128) {
+      uint2 v;
+      asm volatile("ld.volatile.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(theirs + i) : "memory");
+      *x_at(i) = v;
+    }
   }
   return true;
 }
@@ -872,7 +918,7 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
                          peers->rank >= peers->tp || p.P > PEER_MAX_CTAS,
                      TSDS_E_INVALID);
       TSDS_RETURN_IF(!in.out || in.K <= 0 || (in.K % 4) != 0 || in.ldo < in.K || (in.n_out & ~1) != 0 ||
-                         (int64_t)M * in.K > peers->max_elems,
+                         (in.epi & ~1) != 0 || (int64_t)M * in.K > peers->max_elems,
                      TSDS_E_INVALID);
       TSDS_RETURN_IF((reinterpret_cast<uintptr_t>(in.out) & 7u) != 0 || (in.ldo % 4) != 0, TSDS_E_ALIGN);
       for (int q = 0; q < peers->tp; ++q) {
@@ -881,6 +927,7 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
         char* base = static_cast<char*>(peers->bufs[q]);
         p.pr.slot[0][q] = reinterpret_cast<const float*>(base + slot_offset(peers->max_elems, 0));
         p.pr.slot[1][q] = reinterpret_cast<const float*>(base + slot_offset(peers->max_elems, 1));
+        p.pr.published[q] = reinterpret_cast<bf16*>(base + published_offset(peers->max_elems));
         p.pr.flags[q] = reinterpret_cast<uint32_t*>(base + PEER_FLAGS_OFF);
       }
       p.pr.counters = static_cast<uint32_t*>(peers->bufs[peers->rank]);
@@ -890,6 +937,7 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
       ph.n = in.K;
       ph.ldo = in.ldo;
       ph.slot = in.n_out;
+      ph.two_shot = in.epi;
       continue;
     }
     if (in.kind == TSDS_PHASE_NORM) {

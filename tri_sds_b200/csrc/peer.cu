@@ -89,9 +89,7 @@ __global__ void __launch_bounds__(PEER_THREADS) peer_allreduce_residual_kernel(P
 
 }  // namespace
 
-extern "C" size_t tsds_peer_buffer_bytes(int max_elems) {
-  return max_elems <= 0 ? 0 : PEER_HEADER_BYTES + 2 * slot_bytes(max_elems);
-}
+extern "C" size_t tsds_peer_buffer_bytes(int max_elems) { return max_elems <= 0 ? 0 : buffer_bytes(max_elems); }
 
 extern "C" size_t tsds_peer_slot_offset(int max_elems, int slot) { return slot_offset(max_elems, slot); }
 

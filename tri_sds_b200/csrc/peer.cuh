@@ -5,6 +5,8 @@
 //   [0, 2 KB)       counters[PEER_MAX_CTAS]         u32  this rank's per-CTA call count
 //   [2 KB, 18 KB)   flags[PEER_MAX_CTAS][8]         u32  flags[b][p] written by rank p
 //   [32 KB, ...)    slot 0, slot 1: max_elems fp32 each
+//   then            published: max_elems bf16 - the two-shot all-reduce's
+//                   final values of this rank's chunk
 #pragma once
 
 #include "common.cuh"
@@ -24,6 +26,12 @@ static_assert(PEER_FLAGS_OFF + PEER_MAX_CTAS * PEER_MAX_RANKS * 4 <= PEER_HEADER
 __host__ __device__ inline size_t slot_bytes(int max_elems) { return ((size_t)max_elems * 4 + 255) / 256 * 256; }
 __host__ __device__ inline size_t slot_offset(int max_elems, int slot) {
   return PEER_HEADER_BYTES + (size_t)(slot & 1) * slot_bytes(max_elems);
+}
+__host__ __device__ inline size_t published_offset(int max_elems) {
+  return PEER_HEADER_BYTES + 2 * slot_bytes(max_elems);
+}
+__host__ __device__ inline size_t buffer_bytes(int max_elems) {
+  return published_offset(max_elems) + ((size_t)max_elems * 2 + 255) / 256 * 256;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -37,6 +37,13 @@ def _p(t):
     return None if t is None else _VP(t.data_ptr())
 
 
+# Remote bytes per rank above which the fused kernel's peer all-reduce runs
+# two-shot (each rank reduces 1/tp of the elements and publishes them) rather
+# than one-shot (every rank reads every partial): 2 MB, between B=1 at TP=4
+# (1.6 MB one-shot) and TP=8 (3.7 MB) for the 32B hidden size.
+TWO_SHOT_BYTES = 2 << 20
+
+
 def _fused_args(phases: list, rope: dict | None, peer, M: int, ws, ws_bytes: int) -> tuple:
     """tsds_fused_layer arguments (after the name) from phase dicts of
     pointers and sizes: a tsds_fused_phase array, a tsds_qk_rope and a
@@ -320,13 +327,16 @@ class QwenModel:
         pl = Plan()
         N = s.hidden
         peer = self.peer if self.layer_tp > 1 else None
+        # two-shot all-reduce once a rank would pull more than TWO_SHOT_BYTES
+        # of the other ranks' partials in one shot (same bits either way)
+        two_shot = peer is not None and M * N * 4 * (peer.size - 1) > TWO_SHOT_BYTES
 
         def row_parallel(src, K, w, slot):
             if peer is None:
                 return [gemm(_lib.EPI_RESIDUAL, src, K, w, N, out=xb, res=xb)]
             part = dict(gemm(_lib.EPI_STORE_F32, src, K, w, N), out=peer.slot_ptr(slot), ldo=N)
-            reduce = dict(kind=_lib.PHASE_PEER, epi=0, x=None, ldx=0, K=N, w=None, n_out=slot, res_ld=0, res=None,
-                          out=_p(xb), ldo=N, eps=0.0)
+            reduce = dict(kind=_lib.PHASE_PEER, epi=int(two_shot), x=None, ldx=0, K=N, w=None, n_out=slot, res_ld=0,
+                          res=None, out=_p(xb), ldo=N, eps=0.0)
             return [part, reduce]
 
         def norm(w):
