@@ -123,6 +123,24 @@ def test_tensor_parallel_fused_plan_with_peer_phases(recorded, tp, rank):
         assert check_call(n, a) > 0
 
 
+@pytest.mark.parametrize("threshold,epi", [(1 << 40, 0), (0, 1)])
+def test_peer_phases_pick_one_or_two_shot(recorded, monkeypatch, threshold, epi):
+    """PEER phases run two-shot (epi 1) once a rank would pull more than
+    TWO_SHOT_BYTES of the others' partials one-shot."""
+    import tri_sds_b200.model as model
+    from tri_sds_b200.model import QwenModel
+    monkeypatch.setattr(model, "TWO_SHOT_BYTES", threshold)
+
+    class _Comm:
+        rank, size = 0, 4
+
+    peer = FakePeer(0, 4, 26 * SHAPE.hidden)
+    m = QwenModel(SHAPE, 1, 96, 26, device="cpu", tp_rank=0, tp_size=4, comm=_Comm(), peer=peer, fused_layers=True)
+    peers = [ph for n, fn, a in m.layers_plan(1, 26).calls if n == "tsds_fused_layer" for ph in a[0]
+             if ph["kind"] == 2]
+    assert peers and all(ph["epi"] == epi for ph in peers)
+
+
 def test_tensor_parallel_model_keeps_the_per_op_plan():
     from tri_sds_b200.model import QwenModel
 
