@@ -51,7 +51,11 @@ def _args():
     ap.add_argument("--impl", default="tsds", choices=["tsds", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--k", type=int, default=4)
-    ap.add_argument("--mode", default="eagle", choices=["eagle", "chain"])
+    ap.add_argument("--mode", default="eagle", choices=["eagle", "chain", "attention", "layer"],
+                    help="eagle / chain: the spec-decode cycle; attention: verify attention alone over a "
+                         "--kv-len cache (B x (K+1) queries, 32B heads); layer: Qwen3-4B-shape decoder layers "
+                         "alone over B x (K+1) rows")
+    ap.add_argument("--kv-len", type=int, default=4096, help="attention mode: keys per sequence")
     ap.add_argument("--greedy", action="store_true", help="eagle mode: greedy acceptance instead of sampling")
     ap.add_argument("--prompt", type=int, default=512)
     # smaller depth for profiler captures only (never for reported numbers)
@@ -82,6 +86,11 @@ DATA = "synthetic: seeded uniform prompt ids, random-init N(0,0.02) weights (no 
 
 
 def _workload(a) -> str:
+    if a.mode == "attention":
+        return (f"verify attention: B={a.batch} x {a.k + 1} queries x 64 q heads over {a.kv_len} cached keys x 8 kv "
+                f"heads, head dim 128, causal among the new tokens")
+    if a.mode == "layer":
+        return f"Qwen3-4B-shape decoder layers (36) over B={a.batch} x {a.k + 1} rows at 512 cached tokens"
     if a.mode == "eagle":
         acc = "greedy" if a.greedy else "rejection sampling T=1.0"
         return (f"EAGLE tree spec decode: head fc 2x5120->5120 + 1 Qwen3-32B-shape layer, tree depth 5 / top-4 / "
@@ -231,6 +240,10 @@ def run_reference(a, rank: int, world: int):
     """--impl reference: the reference's CPU path (oracle port), rank 0 only."""
     if rank != 0:
         return
+    if a.mode in ("attention", "layer"):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the spec-decode cycle "
+                                                              "(--mode eagle / chain)"}), flush=True)
+        return
     cc = CpuCycle(a)
     threads, sample = cc.threads, cc.sample
     times = []
@@ -285,6 +298,110 @@ def plan_breakdown(plan, cycles: int) -> dict:
     rows = [{"call": n, "per_cycle": cnt[n] // cycles, "us_per_cycle": round(tot[n], 1),
              "share": round(tot[n] / total, 4)} for n in sorted(tot, key=tot.get, reverse=True)]
     return {"calls": rows, "sum_us_per_cycle": round(total, 1)}
+
+
+def _graph_time_us(run_once, reps: int, warm: int = 3):
+    """Capture run_once() in a CUDA graph, replay it `warm` times, then time
+    `reps` replays with CUDA events; returns (us per replay, clocks)."""
+    import torch
+    run_once()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run_once()
+    for _ in range(warm):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps, clocks.summary()
+
+
+def run_attention(a):
+    """--mode attention: tsds_verify_attention alone at the verify-attention
+    configuration (q [B, K+1, 64, 128], K/V caches [B, 8, kv_len, 128], the new
+    tokens the last K+1 rows, causal among them).  Enough cache sets rotate
+    that the timed launches read more than twice the L2 size, so every
+    launch streams its K/V from HBM."""
+    import torch
+    from tri_sds_b200 import _lib, ops
+    dev = torch.device("cuda", 0)
+    B, T, L, Hq, Hkv, D = a.batch, a.k + 1, a.kv_len, 64, 8, 128
+    kv_bytes = B * Hkv * L * D * 2 * 2
+    sets = max(1, -(-(2 * 126 * 2 ** 20) // kv_bytes))
+    g = torch.Generator(device=dev).manual_seed(11)
+    caches = [(torch.randn(B, Hkv, L, D, device=dev, generator=g).to(torch.bfloat16),
+               torch.randn(B, Hkv, L, D, device=dev, generator=g).to(torch.bfloat16)) for _ in range(sets)]
+    q = torch.randn(B, T, Hq, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    starts = torch.full((B,), L - T, dtype=torch.int32, device=dev)
+    lc0 = _lib.query("tsds_launch_count")
+
+    def once():
+        for k, v in caches:
+            ops.verify_attention(q, k, v, starts, out=out)
+
+    us, clocks = _graph_time_us(once, reps=max(1, a.steps))
+    launches = (_lib.query("tsds_launch_count") - lc0) // 2   # eager warm-up + capture
+    us_launch = us / sets
+    nbytes = kv_bytes + 2 * B * T * Hq * D * 2
+    peak, peak_kind = _peaks()
+    achieved = nbytes / (us_launch * 1e-6) / 1e9
+    line = {"metric": "verify attention GB/s", "value": achieved, "unit": "GB/s", "n_gpus": 1, "steps": a.steps,
+            "warmup": 3, "ms_per_step": us_launch / 1e3, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: N(0,1) q / K / V",
+            "config": {"workload": _workload(a), "global_batch": B, "seq_len": L, "parallelism": "none",
+                       "l2": f"{sets} cache sets rotate ({sets * kv_bytes / 2**20:.0f} MB > 2 x L2)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": nbytes,
+                         "launch_us": us_launch},
+            "clocks": clocks, "gpu_launches": launches * max(1, a.steps)}
+    print(json.dumps(line), flush=True)
+
+
+def run_layer(a):
+    """--mode layer: the decoder layers of a Qwen3-4B-shape model (36, random
+    weights) over B x (K+1) rows at 512 cached tokens per sequence - the
+    decode-layer primitives' configuration - as one graph; reports the time
+    per layer against its weight bytes."""
+    import torch
+    from tri_sds_b200 import _lib
+    from tri_sds_b200.model import Plan, QwenModel, _p
+    from tri_sds_b200.shapes import QWEN3_4B
+    dev = torch.device("cuda", 0)
+    B, T = a.batch, a.k + 1
+    m = QwenModel(QWEN3_4B, B, 1024, B * T, device=dev, seed=5, fused_layers=a.fused_layers)
+    m.lengths.fill_(512)
+    m.x[:B * T].copy_(torch.randn(B * T, QWEN3_4B.hidden, device=dev).to(torch.bfloat16))
+    pl = Plan()
+    pl.add("tsds_prep_chain", _p(m.lengths), 0, B, T, _p(m.starts), _p(m.positions))
+    pl.extend(m.layers_plan(B, T))
+    lc0 = _lib.query("tsds_launch_count")
+    us, clocks = _graph_time_us(pl.run, reps=max(1, a.steps))
+    launches = (_lib.query("tsds_launch_count") - lc0) // 2
+    m.check_status()
+    L0 = m.layers[0]
+    wbytes = sum(t.numel() * 2 for t in (L0.w_qkv, L0.w_o, L0.w_gu, L0.w_d))
+    us_layer = us / QWEN3_4B.n_layers
+    peak, peak_kind = _peaks()
+    achieved = wbytes / (us_layer * 1e-6) / 1e9
+    line = {"metric": "decode layer us", "value": us_layer, "unit": "us", "n_gpus": 1, "steps": a.steps,
+            "warmup": 3, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "none",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random-init N(0,0.02) weights",
+            "config": {"workload": _workload(a), "global_batch": B, "seq_len": 512, "rows": B * T,
+                       "parallelism": "none", "fused_layers": bool(m.fused_layers),
+                       "l2": "no flush: 7.3 GB of weights per pass >> 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": wbytes,
+                         "launch_us": us_layer},
+            "clocks": clocks, "gpu_launches": launches * max(1, a.steps)}
+    print(json.dumps(line), flush=True)
 
 
 def run_tsds(a, rank: int, world: int, local_rank: int):
@@ -504,6 +621,13 @@ def main():
     try:
         if a.impl == "reference":
             run_reference(a, rank, world)
+        elif a.mode in ("attention", "layer"):
+            if world > 1:
+                raise SystemExit("--mode attention / layer run on one GPU")
+            if a.pair_rows is not None:
+                from tri_sds_b200 import _lib
+                _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+            (run_attention if a.mode == "attention" else run_layer)(a)
         else:
             run_tsds(a, rank, world, local_rank)
     except BaseException:
