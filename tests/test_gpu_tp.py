@@ -81,7 +81,19 @@ def _worker(rank, port, q, allreduce):
         for mdl in (m, tgt, tgt2, tgt3):
             mdl.check_status()
         if peer is not None:
-            dist.barrier()   # neither rank reads the other's buffer any more
+            # the op-level all-reduce on a group of its own: x = 1 + (1 + 2) on both ranks
+            import tri_sds_b200.torch_ops  # noqa: F401
+            from tri_sds_b200.tp import register_peer_group
+            op_peer = PeerAllReduce(rank, 2, 64 * 256)
+            gid = register_peer_group(op_peer)
+            xo = torch.ones(64, 256, dtype=torch.bfloat16, device=dev)
+            for _ in range(3):   # both slots, then the first again
+                xo.fill_(1.0)
+                torch.ops.tsds.allreduce_oneshot(xo, torch.full((64, 256), float(rank + 1), device=dev), gid)
+            torch.cuda.synchronize()
+            out.update(op_allreduce=xo.cpu())
+            dist.barrier()   # neither rank reads the other's buffers any more
+            op_peer.close()
             peer.close()
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001
@@ -134,3 +146,6 @@ def test_tp2_verify_and_lossless_spec(allreduce):
     assert torch.equal(res[0]["spec"], res[0]["ar"])
     assert torch.equal(res[0]["espec"], res[1]["espec"])
     assert torch.equal(res[0]["espec"], res[0]["ar"])
+    if allreduce != "nccl":
+        for r in (0, 1):
+            assert torch.equal(res[r]["op_allreduce"], torch.full((64, 256), 4.0, dtype=torch.bfloat16))

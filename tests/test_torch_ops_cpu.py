@@ -38,6 +38,7 @@ def test_every_op_is_registered_with_its_mutations():
         "accept_greedy": {"lengths", "last", "cur"},
         "accept_rejection": set(),
         "kv_compact": {"k_cache", "v_cache", "lengths", "root_feat"},
+        "allreduce_oneshot": {"x"},
     }
 
 
@@ -197,6 +198,47 @@ def test_kv_compact_checks_its_indices(recorded, field, index, value):
     assert recorded.calls == []
 
 
+class _FakeGroup:
+    """tp.PeerAllReduce's op-level interface with host tensors as slots."""
+
+    def __init__(self, rank, size, max_elems):
+        import ctypes
+        import tri_sds_b200.tp as tp
+        self.rank, self.size, self.max_elems = rank, size, max_elems
+        self.slots = [torch.zeros(max_elems, dtype=torch.float32) for _ in range(2)]
+        self.bufs = (ctypes.c_void_p * size)(*[0x1000 * (q + 1) for q in range(size)])
+        self.next_slot = tp.PeerAllReduce.next_slot.__get__(self)
+
+    def slot_tensor(self, slot, n):
+        return self.slots[slot][:n]
+
+
+def test_allreduce_oneshot_alternates_slots(recorded):
+    import tri_sds_b200.tp as tp
+    M, N = 26, 256
+    grp = _FakeGroup(1, 4, M * N)
+    gid = tp.register_peer_group(grp)
+    x = _r(M, N)
+    seen = []
+    for i in range(3):
+        part = torch.full((M, N), float(i + 1))
+        _ops().allreduce_oneshot(x, part, gid)
+        seen.append(float(grp.slots[i % 2][0]))
+    # the partial of call i sits in slot i % 2 when its kernel runs
+    assert seen == [1.0, 2.0, 3.0] and float(grp.slots[0][0]) == 3.0 and float(grp.slots[1][0]) == 2.0
+    assert recorded.calls == ["tsds_peer_allreduce_residual"] * 3
+
+
+def test_allreduce_oneshot_checks_shapes(recorded):
+    import tri_sds_b200.tp as tp
+    gid = tp.register_peer_group(_FakeGroup(0, 2, 64))
+    with pytest.raises(ValueError):
+        _ops().allreduce_oneshot(_r(4, 32), torch.zeros(4, 32), gid)     # M * N > the group's slots
+    with pytest.raises(ValueError):
+        _ops().allreduce_oneshot(_r(2, 8), torch.zeros(2, 4), gid)       # partial of another shape
+    assert recorded.calls == []
+
+
 def test_host_tensors_are_refused():
     """No CPU implementation: the device checks reject host tensors before any
     pointer reaches the library."""
@@ -215,6 +257,7 @@ def test_host_tensors_are_refused():
         lambda: tsds.accept_rejection(_r(B * NN, V), _r(2, V), ids, hrow, children, torch.rand(B, depth + 1, k + 1),
                                       None, depth),
         lambda: tsds.kv_compact(*_commit_args()),
+        lambda: tsds.allreduce_oneshot(_r(4, 32), torch.zeros(4, 32), 0),
     ]
     for case in cases:
         with pytest.raises(ValueError, match="CUDA"):

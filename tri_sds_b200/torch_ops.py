@@ -24,10 +24,13 @@ accept_rejection   tree acceptance: rejection sampling at temperature 1 with
                    given uniforms, or greedy
 kv_compact         KV rows of the accepted path -> consecutive rows, lengths
                    += accepted + 1, next root feature
+allreduce_oneshot  x += sum over the TP ranks of their fp32 partials (the
+                   all-reduce after O / down; no reference counterpart)
 =================  =========================================================
 
-The cross-rank all-reduce of tensor parallelism is NCCL's
-(``torch.distributed``); it has no op here.  ``accept_rejection`` and
+``allreduce_oneshot`` is tensor parallelism's row-parallel all-reduce + residual
+add over NVLink peer memory (a ``tp.PeerAllReduce`` group, registered with
+``tp.register_peer_group``).  ``accept_rejection`` and
 ``kv_compact`` check their index arguments on the host before the launch
 (a device-to-host copy, so they do not belong in a captured CUDA graph); the
 engines call the C ABI directly with indices their own kernels produced.
@@ -202,5 +205,25 @@ def kv_compact(k_cache: Tensor, v_cache: Tensor, lengths: Tensor, path: Tensor, 
               depth, _p(hidden), NN - 1, N, _p(root_feat), _s())
 
 
+@torch.library.custom_op("tsds::allreduce_oneshot", mutates_args=("x",))
+def allreduce_oneshot(x: Tensor, partial: Tensor, group: int) -> None:
+    """Tensor parallelism: x [M, N] bf16 = bf16(x + bf16(sum over the ranks of
+    their fp32 partial [M, N])), the same on every rank, over NVLink peer
+    memory (tsds_peer_allreduce_residual).  `group` is the id from
+    tp.register_peer_group of a tp.PeerAllReduce; every rank makes the same
+    sequence of calls with the same shapes."""
+    from . import tp
+    ops._bf16_cuda(x)
+    ops._cuda(torch.float32, partial)
+    peer = tp.peer_group(group)
+    M, N = x.shape
+    ops._need(partial.shape == (M, N) and x.is_contiguous() and M * N <= peer.max_elems and N % 4 == 0,
+              "bad shapes")
+    slot = peer.next_slot()
+    peer.slot_tensor(slot, M * N).copy_(partial.reshape(-1))
+    _lib.call("tsds_peer_allreduce_residual", _p(x), peer.bufs, peer.rank, peer.size, slot, M, N, peer.max_elems,
+              _p(ops._scratch.status_word(x.device)), _s())
+
+
 OPS = ("qkv_rope_fused", "verify_attention", "oproj_fused", "mlp_fused", "lm_head_topk", "eagle_fc", "accept_greedy",
-       "accept_rejection", "kv_compact")
+       "accept_rejection", "kv_compact", "allreduce_oneshot")

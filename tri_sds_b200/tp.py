@@ -85,6 +85,31 @@ class LocalComm:
         out.copy_(inp)
 
 
+class _CudaView:
+    """__cuda_array_interface__ of n fp32 at a device address (torch.as_tensor
+    wraps it without a copy or ownership)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+_GROUPS: dict = {}
+
+
+def register_peer_group(peer: "PeerAllReduce") -> int:
+    """Id under which torch.ops.tsds.allreduce_oneshot finds `peer`.  A group
+    used by the op should not also serve a model's launch plans (the slot
+    alternation is per user)."""
+    gid = len(_GROUPS)
+    _GROUPS[gid] = peer
+    return gid
+
+
+def peer_group(gid: int) -> "PeerAllReduce":
+    return _GROUPS[gid]
+
+
 class PeerAllReduce:
     """Peer buffers of the ranks of one node, for tsds_peer_allreduce_residual.
 
@@ -124,6 +149,17 @@ class PeerAllReduce:
 
     def slot_ptr(self, slot: int) -> ctypes.c_void_p:
         return ctypes.c_void_p(self._own.value + _lib.query("tsds_peer_slot_offset", self.max_elems, slot))
+
+    def slot_tensor(self, slot: int, n: int) -> torch.Tensor:
+        """fp32 tensor view of the first n elements of this rank's slot (no copy)."""
+        assert 0 < n <= self.max_elems
+        return torch.as_tensor(_CudaView(self.slot_ptr(slot).value, n), device=torch.device("cuda"))
+
+    def next_slot(self) -> int:
+        """Slot for the next op-level all-reduce on this group (alternates;
+        every rank makes the same sequence of calls)."""
+        self._op_calls = getattr(self, "_op_calls", 0) + 1
+        return (self._op_calls - 1) % 2
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after every kernel
