@@ -439,7 +439,10 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         from tri_sds_b200.tp import Comm, PeerAllReduce
         comm = Comm()
         if a.allreduce == "peer":
-            peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden)
+            # with an exchange region for the vocab-parallel LM head's gathers
+            from tri_sds_b200.tp import lm_exchange_layout
+            peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden,
+                                 exchange_bytes=lm_exchange_layout(rows_verify, tshape.vocab // world)[2])
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
                        tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers)
     if a.mode == "eagle":

@@ -336,14 +336,17 @@ int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const 
  * add: the TP exchange after the O and down projections without NCCL.
  * Replaces the NCCL all-reduce + tsds_residual_add_f32 pair above.
  *
- * Each rank owns one peer buffer of tsds_peer_buffer_bytes(max_elems) bytes
+ * Each rank owns one peer buffer of tsds_peer_buffer_bytes(max_elems,
+ * exchange_bytes) bytes
  * (tsds_peer_alloc: cudaMalloc, zero-filled), exports it with
  * tsds_peer_export (tsds_peer_handle_bytes() bytes, a CUDA IPC handle) and
  * maps every other rank's with tsds_peer_import (another process of the same
  * node; close with tsds_peer_close, free its own with tsds_peer_free).
  * Buffer layout: per-CTA call counters and flags in the first 32 KB, then two
  * slots of max_elems fp32 at tsds_peer_slot_offset(max_elems, 0 / 1), then
- * max_elems bf16 published by the fused kernel's two-shot all-reduce.
+ * max_elems bf16 published by the fused kernel's two-shot all-reduce, then
+ * exchange_bytes at tsds_peer_exchange_offset(max_elems) for
+ * tsds_peer_lm_gather.
  *
  * tsds_peer_allreduce_residual: the partial [M][N] fp32 of every rank sits in
  * slot `slot` of that rank's buffer (written there by tsds_linear_f32);
@@ -356,8 +359,9 @@ int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const 
  * x is left unchanged.  tp <= 8, N % 4 == 0, M * N <= max_elems, x 8-byte
  * aligned, buffers 16-byte aligned.
  */
-size_t tsds_peer_buffer_bytes(int max_elems);
+size_t tsds_peer_buffer_bytes(int max_elems, size_t exchange_bytes);
 size_t tsds_peer_slot_offset(int max_elems, int slot);
+size_t tsds_peer_exchange_offset(int max_elems);
 size_t tsds_peer_handle_bytes(void);
 int tsds_peer_alloc(size_t bytes, void** buf);
 int tsds_peer_free(void* buf);
@@ -366,6 +370,20 @@ int tsds_peer_import(const void* handle, void** buf);
 int tsds_peer_close(void* buf);
 int tsds_peer_allreduce_residual(void* x, void* const* bufs, int rank, int tp, int slot, int M, int N,
                                  int max_elems, int* status, tsds_stream_t stream);
+/* Vocab-parallel LM head without NCCL (replaces the all-gathers +
+ * tsds_argmax_merge / tsds_gather_shards above): every rank's LM head has
+ * written, into the exchange region of its own peer buffer, its shard's
+ * argmax candidates - rows int64 local indices at offset 0 and rows fp32
+ * values at val_off (tsds_lm_head_argmax's argmax_out / argmax_val) - and,
+ * when logits_out is given, its logits shard [rows][vocab_shard] bf16 at
+ * log_off.  Writes argmax_out[m * argmax_stride] (best value, ties to the
+ * lowest global index) and logits_out [rows][tp * vocab_shard] on every rank.
+ * Meets the other ranks before reading and again after, so a rank may
+ * overwrite its region once this call has returned on its stream.  Bounded
+ * waits (1 s) report TSDS_E_TIMEOUT in *status. */
+int tsds_peer_lm_gather(void* const* bufs, int rank, int tp, int max_elems, size_t exchange_bytes, int rows,
+                        int vocab_shard, int64_t val_off, int64_t log_off, int64_t* argmax_out,
+                        int argmax_stride, void* logits_out, int* status, tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Tree speculative decoding (EAGLE draft tree, verified in one target pass).

@@ -79,6 +79,11 @@ def extents(name, a):
         x, ldx, W, logits, am, stride, av, M, V, K, ws, wsb = a
         return [(0, ((M - 1) * ldx + K) * 2), (2, V * K * 2), (3, M * V * 2), (4, ((M - 1) * stride + 1) * 8),
                 (6, M * 4), (10, wsb)]
+    if name == "tsds_peer_lm_gather":
+        bufs, rank, tp, max_elems, xb, rows, vl, val_off, log_off, out, stride, logits, status = a
+        assert 0 <= rank < tp and val_off >= 8 * rows
+        assert (log_off + 2 * rows * vl if logits is not None else val_off + 4 * rows) <= xb
+        return [(9, ((rows - 1) * stride + 1) * 8), (11, rows * tp * vl * 2), (12, 4)]
     if name == "tsds_peer_allreduce_residual":
         x, bufs, rank, tp, slot, M, N, max_elems, status = a
         assert 0 <= rank < tp and slot in (0, 1) and M * N <= max_elems

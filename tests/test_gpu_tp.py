@@ -35,7 +35,11 @@ def _worker(rank, port, q, allreduce):
         dev = torch.device("cuda", rank)
         comm = Comm()
         # one set of peer buffers for every TP model here (their calls run in stream order)
-        peer = PeerAllReduce(rank, 2, 2 * 26 * SMALL["hidden"]) if allreduce != "nccl" else None
+        from tri_sds_b200.tp import lm_exchange_layout
+        # with an exchange region: the vocab-parallel LM heads gather over peer memory too
+        peer = (PeerAllReduce(rank, 2, 2 * 26 * SMALL["hidden"],
+                              exchange_bytes=lm_exchange_layout(2 * 26, SMALL["vocab"] // 2)[2])
+                if allreduce != "nccl" else None)
         fused = allreduce == "peer+fused"   # the all-reduces as phases of the fused-layer kernel
         oshape = oq.QwenShape(**SMALL)
         shape = QwenShape(**SMALL)

@@ -146,6 +146,64 @@ def test_plan_uses_the_peer_slots(tensor_refs, tp, rank):
                 check_call(n, a)
 
 
+class FakeExchangePeer(FakePeer):
+    """FakePeer with an exchange region for the vocab-parallel LM head."""
+
+    def __init__(self, rank, size, max_elems, exchange_bytes):
+        super().__init__(rank, size, max_elems)
+        self.exchange_bytes = exchange_bytes
+        self.exchange = torch.zeros(exchange_bytes, dtype=torch.uint8)
+
+    def exchange_at(self, offset):
+        return TRef(self.exchange[offset:])
+
+
+@pytest.mark.parametrize("tp,rank", [(2, 0), (8, 7)])
+def test_lm_head_gathers_over_peer_memory(tensor_refs, tp, rank):
+    """With an exchange region, a tensor-parallel EAGLE cycle has no NCCL
+    step at all: the row-parallel all-reduces run on peer memory and every
+    vocab-parallel LM head (the target's and the head passes') writes its
+    candidates / logits into the exchange region that tsds_peer_lm_gather
+    reads."""
+    from tri_sds_b200.eagle import EagleEngine, EagleHead
+    from tri_sds_b200.model import QwenModel
+    from tri_sds_b200.tp import lm_exchange_layout
+    B = 2
+    rows = B * 26
+    xb = lm_exchange_layout(rows, SHAPE.vocab // tp)[2]
+    peer = FakeExchangePeer(rank, tp, rows * SHAPE.hidden, xb)
+    t = QwenModel(SHAPE, B, 96, rows, device="cpu", tp_rank=rank, tp_size=tp, comm=_Comm(rank, tp), peer=peer)
+    eng = EagleEngine(t, EagleHead(t, B), use_graph=False)
+    assert eng.head.model.lm_peer is peer
+    calls = eng.plan.calls
+    assert not any(fn is None for _, fn, _ in calls)          # no NCCL (Python collective) steps
+    names = [n for n, _, _ in calls]
+    assert "tsds_argmax_merge" not in names and "tsds_gather_shards" not in names
+    gathers = [i for i, n in enumerate(names) if n == "tsds_peer_lm_gather"]
+    assert len(gathers) == 6                                   # the target's verify + five head passes
+    for i in gathers:
+        n, fn, lm = calls[i - 1]
+        assert n == "tsds_lm_head_argmax" and lm[4].t.data_ptr() == peer.exchange.data_ptr()
+    for n, fn, a in calls:
+        check_call(n, a)
+
+
+def test_lm_gather_host_checks():
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    out, st = ctypes.c_void_p(0x30000), ctypes.c_void_p(0x40000)
+
+    def run(tp=2, rank=0, xb=4096, rows=4, vl=64, val_off=256, log_off=512, logits=None):
+        return lib.tsds_peer_lm_gather(bufs, rank, tp, 1024, xb, rows, vl, val_off, log_off, out, 1, logits, st, None)
+
+    assert run(tp=9) == 1 and run(rank=2) == 1 and run(rows=0) == 1
+    assert run(val_off=16) == 2                               # candidates overlap the values
+    assert run(xb=16) == 1                                    # the values do not fit the region
+    assert run(logits=ctypes.c_void_p(0x50000), log_off=256) == 1          # logits overlap the values
+    assert run(logits=ctypes.c_void_p(0x50000), xb=600) == 1               # logits do not fit
+
+
 def test_peer_needs_matching_rank_and_room():
     from tri_sds_b200.model import QwenModel
     with pytest.raises(AssertionError):
@@ -159,12 +217,15 @@ def test_peer_needs_matching_rank_and_room():
 def test_entry_point_checks_and_layout():
     """Argument checks return before any CUDA call; the layout is the
     documented one (32 KB header, two 256-byte-rounded fp32 slots, then a
-    256-byte-rounded bf16 region published by the two-shot all-reduce)."""
+    256-byte-rounded bf16 region published by the two-shot all-reduce, then
+    the LM head's exchange region)."""
     from tri_sds_b200 import _lib
     lib = _lib.load()
     assert lib.tsds_peer_handle_bytes() == 64
-    assert lib.tsds_peer_buffer_bytes(0) == 0
-    assert lib.tsds_peer_buffer_bytes(1000) == 32768 + 2 * 4096 + 2048
+    assert lib.tsds_peer_buffer_bytes(0, 0) == 0
+    assert lib.tsds_peer_buffer_bytes(1000, 0) == 32768 + 2 * 4096 + 2048
+    assert lib.tsds_peer_buffer_bytes(1000, 1000) == 32768 + 2 * 4096 + 2048 + 1024   # exchange, 256-aligned
+    assert lib.tsds_peer_exchange_offset(1000) == 32768 + 2 * 4096 + 2048
     assert lib.tsds_peer_slot_offset(1000, 0) == 32768 and lib.tsds_peer_slot_offset(1000, 1) == 32768 + 4096
     bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
     x = ctypes.c_void_p(0x30000)

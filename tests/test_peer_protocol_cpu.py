@@ -159,3 +159,76 @@ def _run_one_slot(R, G, calls, seed):
             a[1] = next(a[0])
         except StopIteration:
             a[2] = True
+
+
+def run_lm(R, G, calls, seed, exit_meeting=True):
+    """tsds_peer_lm_gather: each call, a rank's LM head writes its one exchange
+    region (stream order: after its previous gather kernel), then the gather
+    kernel's CTAs meet, read every rank's region, and meet again."""
+    rnd = random.Random(seed)
+    counters = [[0] * G for _ in range(R)]
+    flags = [[[0] * R for _ in range(G)] for _ in range(R)]
+    readers_left = {r: set() for r in range(R)}
+    version = {r: -1 for r in range(R)}
+
+    def meet(r, b):
+        e = counters[r][b] = counters[r][b] + 1
+        for q in range(R):
+            flags[q][b][r] = e
+        yield lambda: all(flags[r][b][q] >= e for q in range(R))
+
+    def cta(r, b, i):
+        yield from meet(r, b)
+        for q in range(R):
+            assert version[q] == i, f"rank {r} read rank {q}'s region of another call"
+            readers_left[q].discard((r, b))
+            yield None
+        if exit_meeting:
+            yield from meet(r, b)
+
+    def stream(r):
+        for i in range(calls):
+            assert not readers_left[r], f"rank {r} overwrote its exchange region still being read (call {i})"
+            version[r] = i
+            readers_left[r] = {(q, b) for q in range(R) for b in range(G)}
+            yield None
+            pending = [[cta(r, b, i), None] for b in range(G)]
+            while pending:
+                ready = [p for p in pending if p[1] is None or p[1]()]
+                if not ready:
+                    yield lambda pending=pending: any(p[1] is None or p[1]() for p in pending)
+                    continue
+                p = rnd.choice(ready)
+                try:
+                    p[1] = next(p[0])
+                except StopIteration:
+                    pending.remove(p)
+                yield None
+
+    actors = [[stream(r), None, False] for r in range(R)]
+    while any(not a[2] for a in actors):
+        ready = [a for a in actors if not a[2] and (a[1] is None or a[1]())]
+        assert ready, "deadlock"
+        a = rnd.choice(ready)
+        try:
+            a[1] = next(a[0])
+        except StopIteration:
+            a[2] = True
+
+
+@pytest.mark.parametrize("R,G", [(2, 1), (4, 3), (8, 2)])
+@pytest.mark.parametrize("seed", range(5))
+def test_lm_gather_one_region_with_exit_meeting(R, G, seed):
+    run_lm(R, G, calls=6, seed=seed)
+
+
+def test_lm_gather_without_exit_meeting_overwrites():
+    """The check of the check: without the second meeting a rank's next LM
+    head can overwrite the region a slower rank is still reading."""
+    hit = False
+    for seed in range(40):
+        try:
+            run_lm(3, 2, calls=5, seed=seed, exit_meeting=False)
+        except AssertionError as e:
+            hit = hit or "still being read" in str(e) or "of another call" in str(e)
+    assert hit

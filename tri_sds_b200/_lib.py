@@ -81,8 +81,10 @@ SIGNATURES = {
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
     "tsds_fused_layer_workspace_bytes": (_Z, [_I]),
     "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _P, _Z, _P]),
-    "tsds_peer_buffer_bytes": (_Z, [_I]),
+    "tsds_peer_buffer_bytes": (_Z, [_I, _Z]),
     "tsds_peer_slot_offset": (_Z, [_I, _I]),
+    "tsds_peer_exchange_offset": (_Z, [_I]),
+    "tsds_peer_lm_gather": (_I, [_P, _I, _I, _I, _Z, _I, _I, ctypes.c_int64, ctypes.c_int64, _P, _I, _P, _P, _P]),
     "tsds_peer_handle_bytes": (_Z, []),
     "tsds_peer_alloc": (_I, [_Z, ctypes.POINTER(_P)]),
     "tsds_peer_free": (_I, [_P]),

@@ -7,6 +7,8 @@
 //   [32 KB, ...)    slot 0, slot 1: max_elems fp32 each
 //   then            published: max_elems bf16 - the two-shot all-reduce's
 //                   final values of this rank's chunk
+//   then            exchange: exchange_bytes - a vocab-parallel LM head's
+//                   argmax candidates and logits shard (tsds_peer_lm_gather)
 #pragma once
 
 #include "common.cuh"
@@ -30,8 +32,11 @@ __host__ __device__ inline size_t slot_offset(int max_elems, int slot) {
 __host__ __device__ inline size_t published_offset(int max_elems) {
   return PEER_HEADER_BYTES + 2 * slot_bytes(max_elems);
 }
-__host__ __device__ inline size_t buffer_bytes(int max_elems) {
+__host__ __device__ inline size_t exchange_offset(int max_elems) {
   return published_offset(max_elems) + ((size_t)max_elems * 2 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t buffer_bytes(int max_elems, size_t exchange_bytes) {
+  return exchange_offset(max_elems) + (exchange_bytes + 255) / 256 * 256;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {

@@ -28,7 +28,7 @@ from dataclasses import replace
 
 from . import _lib
 from .shapes import QwenShape
-from .tp import LocalComm, local_dims, shard_layer, vocab_shard
+from .tp import LocalComm, lm_exchange_layout, local_dims, shard_layer, vocab_shard
 
 _VP = ctypes.c_void_p
 
@@ -158,6 +158,21 @@ class QwenModel:
         if peer is not None:
             assert tp_layers and tp_size > 1 and (peer.rank, peer.size) == (tp_rank, tp_size)
             assert peer.max_elems >= max_rows * shape.hidden
+        # the vocab-parallel LM head exchanges candidates / logits through the
+        # peer group's exchange region when it has one (the EAGLE head shares
+        # the target's LM head and so its group)
+        if share_embeddings is not None:
+            self.lm_peer = share_embeddings.lm_peer
+            self.lm_rows = share_embeddings.lm_rows
+        else:
+            vt = tp_size if tp_vocab else 1
+            use = peer is not None and vt > 1 and getattr(peer, "exchange_bytes", 0) > 0
+            self.lm_peer = peer if use else None
+            self.lm_rows = max_rows
+            if use:
+                assert peer.exchange_bytes >= lm_exchange_layout(max_rows, shape.vocab // vt)[2]
+        if self.lm_peer is not None:
+            assert max_rows <= self.lm_rows
         self.lshape = replace(shape, **local_dims(shape, self.layer_tp)) if self.layer_tp > 1 else shape
         self.vocab_local = shape.vocab // self.vocab_tp
         self.batch = batch
@@ -393,6 +408,18 @@ class QwenModel:
                    argmax_stride, None, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
             return pl
         tpv, vl = self.vocab_tp, self.vocab_local
+        if self.lm_peer is not None:
+            # the shard's candidates / logits straight into this rank's exchange
+            # region, gathered over peer memory (no NCCL)
+            g = self.lm_peer
+            val_off, log_off, _ = lm_exchange_layout(self.lm_rows, vl)
+            want = logits_out is not None
+            pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w),
+                   g.exchange_at(log_off) if want else None, g.exchange_at(0), 1, g.exchange_at(val_off), rows, vl,
+                   s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
+            pl.add("tsds_peer_lm_gather", g.bufs, g.rank, g.size, g.max_elems, g.exchange_bytes, rows, vl, val_off,
+                   log_off if want else 0, _p(argmax_out), argmax_stride, _p(logits_out), _p(self.status))
+            return pl
         loc = None
         if logits_out is not None:
             need = rows * vl

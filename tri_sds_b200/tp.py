@@ -85,6 +85,17 @@ class LocalComm:
         out.copy_(inp)
 
 
+def lm_exchange_layout(rows: int, vocab_shard: int) -> tuple[int, int, int]:
+    """(values offset, logits offset, bytes) of a vocab-parallel LM head's
+    exchange region for up to `rows` rows (tsds_peer_lm_gather): local
+    indices int64 at 0, values fp32, then the logits shard [rows][vocab_shard]
+    bf16, each 256-byte aligned."""
+    up = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    val_off = up(8 * rows)
+    log_off = val_off + up(4 * rows)
+    return val_off, log_off, log_off + up(2 * rows * vocab_shard)
+
+
 class _CudaView:
     """__cuda_array_interface__ of n fp32 at a device address (torch.as_tensor
     wraps it without a copy or ownership)."""
@@ -120,13 +131,15 @@ class PeerAllReduce:
     writes its partial for a call on slot s.  Every rank must construct it at
     the same point (the exchange is a collective)."""
 
-    def __init__(self, rank: int, size: int, max_elems: int, group=None):
+    def __init__(self, rank: int, size: int, max_elems: int, group=None, exchange_bytes: int = 0):
         assert 1 <= size <= 8 and 0 <= rank < size
         self.rank, self.size = rank, size
         self.max_elems = (max_elems + 63) // 64 * 64
+        self.exchange_bytes = exchange_bytes
         self._own = ctypes.c_void_p()
         self._imported: list[ctypes.c_void_p] = []
-        _lib.call("tsds_peer_alloc", _lib.query("tsds_peer_buffer_bytes", self.max_elems), ctypes.byref(self._own))
+        _lib.call("tsds_peer_alloc", _lib.query("tsds_peer_buffer_bytes", self.max_elems, exchange_bytes),
+                  ctypes.byref(self._own))
         try:
             hb = _lib.query("tsds_peer_handle_bytes")
             mine = (ctypes.c_uint8 * hb)()
@@ -149,6 +162,11 @@ class PeerAllReduce:
 
     def slot_ptr(self, slot: int) -> ctypes.c_void_p:
         return ctypes.c_void_p(self._own.value + _lib.query("tsds_peer_slot_offset", self.max_elems, slot))
+
+    def exchange_at(self, offset: int) -> ctypes.c_void_p:
+        """Address `offset` bytes into this rank's exchange region."""
+        assert 0 <= offset < max(self.exchange_bytes, 1)
+        return ctypes.c_void_p(self._own.value + _lib.query("tsds_peer_exchange_offset", self.max_elems) + offset)
 
     def slot_tensor(self, slot: int, n: int) -> torch.Tensor:
         """fp32 tensor view of the first n elements of this rank's slot (no copy)."""
