@@ -482,6 +482,9 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         torch.cuda.nvtx.range_pop()
     barrier()
     ms = ev0.elapsed_time(ev1)
+    # a device wait that gave up (status word set) invalidates the run: fail loudly
+    for mdl in (target, head.model if a.mode == "eagle" else draft):
+        mdl.check_status()
     acc = hist[a.warmup:].float().cpu()
     tokens = float((acc + 1).sum())
     t = torch.tensor([ms], dtype=torch.float64, device=dev)

@@ -87,3 +87,18 @@ def test_worker_without_engine_says_so(monkeypatch):
     monkeypatch.setenv("SDS_ENABLED", "1")
     with pytest.raises(RuntimeError, match="attach_engine"):
         TriSDSWorker().forward_batch_generation(ScheduleBatch(input_ids=torch.zeros(1, 3, dtype=torch.int64)))
+
+
+def test_status_watch_raises_on_a_device_error():
+    """The engines read their kernels' status words with every host-driven
+    cycle: a nonzero word (a bounded device wait that gave up) raises and is
+    cleared."""
+    from tri_sds_b200.model import StatusWatch
+    words = [torch.zeros(1, dtype=torch.int32), torch.tensor([5], dtype=torch.int32)]
+    w = StatusWatch(words)
+    w.copy()
+    with pytest.raises(RuntimeError, match="status 5"):
+        w.check()
+    assert int(words[1]) == 0
+    w.copy()
+    w.check()   # clean now

@@ -25,7 +25,7 @@ from dataclasses import replace
 
 import torch
 
-from .model import Plan, QwenModel, _p
+from .model import Plan, QwenModel, StatusWatch, _p
 from .shapes import QwenShape
 
 
@@ -170,7 +170,11 @@ class EagleEngine:
         self.step()
         tokens_host.copy_(self.tokens, non_blocking=True)
         accept_host.copy_(self.accept_len, non_blocking=True)
+        if getattr(self, "_watch", None) is None:
+            self._watch = StatusWatch(self.target.status_words() + self.head.model.status_words())
+        self._watch.copy()   # the kernels' status words, read with the results
         torch.cuda.current_stream().synchronize()
+        self._watch.check()
         return tokens_host, accept_host
 
     # -- driving -----------------------------------------------------------------

@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import torch
 
-from .model import Plan, QwenModel, _p
+from .model import Plan, QwenModel, StatusWatch, _p
 
 
 class SpecEngine:
@@ -129,7 +129,11 @@ class SpecEngine:
         self.step()
         tokens_host.copy_(self.tokens, non_blocking=True)
         accept_host.copy_(self.accept_len, non_blocking=True)
+        if getattr(self, "_watch", None) is None:
+            self._watch = StatusWatch(self.target.status_words() + self.draft.status_words())
+        self._watch.copy()   # the kernels' status words, read with the results
         torch.cuda.current_stream().synchronize()
+        self._watch.check()
         return tokens_host, accept_host
 
     def prepare(self, prompt: torch.Tensor):

@@ -44,6 +44,33 @@ def _p(t):
 TWO_SHOT_BYTES = 2 << 20
 
 
+def raise_status(word, st: int):
+    """Raise RuntimeError for a nonzero device status `st` read from `word`
+    (which is cleared so that the next check starts afresh)."""
+    if st != 0:
+        word.zero_()
+        raise RuntimeError(f"device status {st}: {_lib.load().tsds_status_string(st).decode()}")
+
+
+class StatusWatch:
+    """Reads a set of device status words together with a cycle's results:
+    `copy()` queues their copies into pinned host memory on the current
+    stream (after the cycle's kernels), `check()` - after the caller's
+    synchronize - raises on the first nonzero one."""
+
+    def __init__(self, words: list):
+        self.words = words
+        self.host = torch.zeros(len(words), dtype=torch.int32, pin_memory=bool(words) and words[0].is_cuda)
+
+    def copy(self):
+        for i, w in enumerate(self.words):
+            self.host[i:i + 1].copy_(w, non_blocking=True)
+
+    def check(self):
+        for i, w in enumerate(self.words):
+            raise_status(w, int(self.host[i]))
+
+
 def _fused_args(phases: list, rope: dict | None, peer, M: int, ws, ws_bytes: int) -> tuple:
     """tsds_fused_layer arguments (after the name) from phase dicts of
     pointers and sizes: a tsds_fused_phase array, a tsds_qk_rope and a
@@ -505,15 +532,16 @@ class QwenModel:
         self.comm.all_gather(allv, loc.contiguous().reshape(-1))
         return allv.reshape(self.vocab_tp, *loc.shape).permute(1, 0, 2).reshape(loc.shape[0], -1)
 
-    def check_status(self):
-        """Raise if a kernel recorded an error in a status word: attention's,
-        or word 0 of the tcgen05 GEMM, LM-head or fused-layer workspaces (a
-        bounded device wait that gave up)."""
+    def status_words(self) -> list:
+        """The device status words this model's kernels record errors in
+        (one int32 each): attention's, and word 0 of the tcgen05 GEMM, LM-head
+        and fused-layer workspaces (a bounded device wait that gave up)."""
         words = [self.status, self.lin_ws[:4].view(torch.int32), self.lm_ws[:4].view(torch.int32)]
         if self.fused_layers:
             words.append(self.fused_ws[:4].view(torch.int32))
-        for w in words:
-            st = int(w.item())
-            if st != 0:
-                w.zero_()
-                raise RuntimeError(f"device status {st}: {_lib.load().tsds_status_string(st).decode()}")
+        return words
+
+    def check_status(self):
+        """Raise if a kernel recorded an error in a status word (clears it)."""
+        for w in self.status_words():
+            raise_status(w, int(w.item()))
