@@ -74,6 +74,10 @@ def _args():
                     help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v (N = 1)")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
+    ap.add_argument("--attn-tc", action="store_true",
+                    help="verify attention on its tcgen05 variant (library default: off)")
+    ap.add_argument("--attn-split", type=int, default=128,
+                    help="keys per attention split of the target / draft (a multiple of 64; of 128 for --attn-tc)")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
                     help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 4)")
     return ap.parse_args()
@@ -345,7 +349,7 @@ def run_attention(a):
 
     def once():
         for k, v in caches:
-            ops.verify_attention(q, k, v, starts, out=out)
+            ops.verify_attention(q, k, v, starts, out=out, split_keys=a.attn_split)
 
     us, clocks = _graph_time_us(once, reps=max(1, a.steps))
     launches = (_lib.query("tsds_launch_count") - lc0) // 2   # eager warm-up + capture
@@ -357,7 +361,9 @@ def run_attention(a):
             "warmup": 3, "ms_per_step": us_launch / 1e3, "higher_is_better": True, "scaling": "none",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic: N(0,1) q / K / V",
             "config": {"workload": _workload(a), "global_batch": B, "seq_len": L, "parallelism": "none",
-                       "l2": f"{sets} cache sets rotate ({sets * kv_bytes / 2**20:.0f} MB > 2 x L2)"},
+                       "l2": f"{sets} cache sets rotate ({sets * kv_bytes / 2**20:.0f} MB > 2 x L2)",
+                       "attention": {"tcgen05": bool(_lib.query("tsds_get_attention_tc")),
+                                     "split_keys": a.attn_split}},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": nbytes,
                          "launch_us": us_launch},
@@ -376,7 +382,7 @@ def run_layer(a):
     from tri_sds_b200.shapes import QWEN3_4B
     dev = torch.device("cuda", 0)
     B, T = a.batch, a.k + 1
-    m = QwenModel(QWEN3_4B, B, 1024, B * T, device=dev, seed=5, fused_layers=a.fused_layers)
+    m = QwenModel(QWEN3_4B, B, 1024, B * T, device=dev, seed=5, fused_layers=a.fused_layers, split_keys=a.attn_split)
     m.lengths.fill_(512)
     m.x[:B * T].copy_(torch.randn(B * T, QWEN3_4B.hidden, device=dev).to(torch.bfloat16))
     pl = Plan()
@@ -426,6 +432,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_pdl(0)
     if a.pair_rows is not None:
         _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+    if a.attn_tc:
+        _lib.load().tsds_set_attention_tc(1)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
@@ -444,14 +452,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden,
                                  exchange_bytes=lm_exchange_layout(rows_verify, tshape.vocab // world)[2])
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
-                       tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers)
+                       tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers, split_keys=a.attn_split)
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         head = EagleHead(target, B, seed=2000)
         engine = EagleEngine(target, head, greedy=a.greedy, seed=3000)
     else:
         draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
-                          tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers)
+                          tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split)
         engine = SpecEngine(target, draft, K)
     # the same prompt on every rank: tensor-parallel ranks process the same tokens
     prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7))
@@ -596,6 +604,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
+            "attention": {"tcgen05": bool(_lib.load().tsds_get_attention_tc()), "split_keys": a.attn_split},
         }
         if breakdown is not None:
             line["breakdown"] = breakdown
@@ -630,9 +639,11 @@ def main():
         elif a.mode in ("attention", "layer"):
             if world > 1:
                 raise SystemExit("--mode attention / layer run on one GPU")
+            from tri_sds_b200 import _lib
             if a.pair_rows is not None:
-                from tri_sds_b200 import _lib
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+            if a.attn_tc:
+                _lib.load().tsds_set_attention_tc(1)
             (run_attention if a.mode == "attention" else run_layer)(a)
         else:
             run_tsds(a, rank, world, local_rank)

@@ -176,6 +176,14 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
                           int T, int Hq, int Hkv, int D, int S, int max_kv, int split_keys,
                           float scale, void* workspace, size_t workspace_bytes, int32_t* status,
                           tsds_stream_t stream);
+/* Process-wide switch (default 0): with 1, tsds_verify_attention runs its
+ * tcgen05 variant (S = Q K^T and O = P V on the 5th-generation tensor cores,
+ * TMEM accumulators, one softmax thread per query row, 128-key tiles) for
+ * every call whose split_keys is a multiple of 128; other calls keep the
+ * default kernel.  Same arguments, workspace and masking; results agree
+ * within fp32 rounding of the products, not bit for bit. */
+void tsds_set_attention_tc(int on);
+int tsds_get_attention_tc(void);
 
 /* ---------------------------------------------------------------------------
  * tsds_verify_attention for callers that cannot allocate device memory.

@@ -70,6 +70,8 @@ SIGNATURES = {
     "tsds_eagle_inputs": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "tsds_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
+    "tsds_set_attention_tc": (None, [_I]),
+    "tsds_get_attention_tc": (_I, []),
     "tsds_verify_attention_noalloc_limit": (_Z, []),
     "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_verify_attention_noalloc_status": (_I, [_P]),

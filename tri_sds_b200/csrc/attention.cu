@@ -22,6 +22,7 @@
 //   output is bit-identical whether it is verified with T tokens or decoded
 //   alone.
 #include "common.cuh"
+#include "tc_core.cuh"
 
 using namespace tsds;
 
@@ -359,7 +360,337 @@ constexpr int kStages = 2;
 
 size_t attn_smem_bytes() { return (size_t)kStages * TILE_BYTES + 1024; }
 
+// ---------------------------------------------------------------------------
+// tcgen05 variant: the same work units, split partials and combine pass, with
+// both products on the 5th-generation tensor cores and the softmax run one
+// thread per query row.
+//
+// * 192 threads.  Warp 0 (one lane) issues TMA loads of K and V tiles of 128
+//   keys (two 64-dim boxes each, 128-byte swizzle) into a 2-deep ring;
+//   warp 1 allocates TMEM and one lane issues the MMAs; warps 2-5 are the
+//   128 query rows of the block (thread = row = TMEM lane).
+// * S = Q K^T: M = 128 rows, N = 128 keys, K = 128 dims.  Q (staged by the
+//   row threads) and K are both K-major in shared memory; S lands in one of
+//   two TMEM buffers, so S of tile i+1 is computed while the rows run the
+//   softmax of tile i.
+// * Softmax: each thread reads its row of S from TMEM twice (row max, then
+//   exp2 and row sum) and writes P (bf16) into shared memory in the
+//   128-byte-swizzled K-major layout the next MMA reads.
+// * O_i = P V: M = 128 rows, N = 128 dims, K = 128 keys, with V read
+//   MN-major (dims contiguous) straight from its TMA tile.  Each thread folds
+//   its row of O_i into registers, o = o * alpha + O_i: an online softmax over
+//   the tiles of the key split, so one CTA can cover a long split without a
+//   combine pass.
+// Masking, the log2-domain softmax and the partial layout are those of
+// verify_attn_kernel, so the combine pass is shared.
+// ---------------------------------------------------------------------------
+constexpr int ATC_THREADS = 192;
+constexpr int ATC_TILE = 128;                  // keys per tile
+constexpr int ATC_BOX = ATC_TILE * 128;        // 128 rows x one 128-byte swizzle row: 16 KB
+constexpr int ATC_REGION = 2 * ATC_BOX;        // 128 rows x 128 dims (or keys) in bf16: 32 KB
+constexpr int ATC_STAGES = 2;
+constexpr int ATC_TMEM_COLS = 512;             // S buffers at columns 0 and 128, O_i at 256
+constexpr int ATC_O_COL = 256;
+
+struct AtcSmem {
+  uint64_t k_full[ATC_STAGES];
+  uint64_t v_full[ATC_STAGES];
+  uint64_t kv_empty[ATC_STAGES];
+  uint64_t s_full[2];
+  uint64_t s_free[2];
+  uint64_t q_full, p_full, o_full, o_free;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// byte offset of 16-byte chunk c (of 16) of row `row` in a 128 x 128 bf16
+// region stored as two 64-column boxes with the TMA 128-byte swizzle
+__device__ __forceinline__ uint32_t atc_off(int row, int c) {
+  return (c >> 3) * ATC_BOX + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+}
+
+// Shared-memory descriptor of an MN-major operand in 128-byte-swizzled rows:
+// 64-element blocks along N are `lbo` bytes apart, groups of 8 rows along K
+// 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__global__ void __launch_bounds__(ATC_THREADS, 1)
+    verify_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                          AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ AtcSmem sh;
+  uint8_t* q_s = smem;                    // Q rows of the block, kept for every tile
+  uint8_t* p_s = smem + ATC_REGION;       // P of the current tile
+  uint8_t* kv_s = smem + 2 * ATC_REGION;  // stage s: K at s * 2 * REGION, V after it
+  const int rb = blockIdx.x % a.nrb, split = blockIdx.x / a.nrb;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ATC_STAGES; ++s) {
+      mbar_init(&sh.k_full[s], 1);
+      mbar_init(&sh.v_full[s], 1);
+      mbar_init(&sh.kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.s_full[i], 1);
+      mbar_init(&sh.s_free[i], 128);
+    }
+    mbar_init(&sh.q_full, 128);
+    mbar_init(&sh.p_full, 128);
+    mbar_init(&sh.o_full, 1);
+    mbar_init(&sh.o_free, 128);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
+                 "r"(ATC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  pdl_wait();
+  pdl_trigger();
+  const int start = a.starts[b];
+  const int kv_len = start + a.T;
+  const int key_begin = split * a.split_keys;
+  const int key_end = min(key_begin + a.split_keys, kv_len);
+  const int ntiles = key_end > key_begin ? (key_end - key_begin + ATC_TILE - 1) / ATC_TILE : 0;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && ntiles > 0) {
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+      const int row0 = (int)(((int64_t)b * a.Hkv + kvh) * a.S) + key_begin;
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % ATC_STAGES;
+        if (i >= ATC_STAGES && !mbar_wait(&sh.kv_empty[s], ((i / ATC_STAGES) - 1) & 1)) {
+          atomicExch(a.status, TSDS_E_TIMEOUT);
+          sh.abort = 1;
+          break;
+        }
+        if (*(volatile int*)&sh.abort) break;
+        uint8_t* ks = kv_s + s * 2 * ATC_REGION;
+        const int row = row0 + i * ATC_TILE;
+        mbar_arrive_expect_tx(&sh.k_full[s], ATC_REGION);
+        tma_load_2d(ks, &kmap, &sh.k_full[s], 0, row);
+        tma_load_2d(ks + ATC_BOX, &kmap, &sh.k_full[s], 64, row);
+        mbar_arrive_expect_tx(&sh.v_full[s], ATC_REGION);
+        tma_load_2d(ks + ATC_REGION, &vmap, &sh.v_full[s], 0, row);
+        tma_load_2d(ks + ATC_REGION + ATC_BOX, &vmap, &sh.v_full[s], 64, row);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && ntiles > 0) {
+      // bf16 x bf16 -> fp32, M = 128, N = 128; PV reads B (V) MN-major
+      const uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                               ((uint32_t)(128 >> 4) << 24);
+      const uint32_t idesc_o = idesc_s | (1u << 16);
+      const uint32_t qa = smem_u32(q_s), pa = smem_u32(p_s);
+      auto issue_s = [&](int i) -> bool {
+        const int s = i % ATC_STAGES, sb = i & 1;
+        if (!mbar_wait(&sh.k_full[s], (i / ATC_STAGES) & 1)) return false;
+        if (i >= 2 && !mbar_wait(&sh.s_free[sb], ((i - 2) >> 1) & 1)) return false;
+        if (*(volatile int*)&sh.abort) return false;
+        tc::tc_fence_after();
+        const uint32_t kb = smem_u32(kv_s + s * 2 * ATC_REGION);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * ATC_BOX + (kk & 3) * 32;
+          tc::umma_bf16(tmem + sb * 128, tc::sdesc_sw128(qa + off), tc::sdesc_sw128(kb + off), idesc_s,
+                        kk > 0 ? 1u : 0u);
+        }
+        tc::umma_commit(&sh.s_full[sb]);
+        return true;
+      };
+      bool ok = mbar_wait(&sh.q_full, 0) && issue_s(0);
+      for (int i = 0; ok && i < ntiles; ++i) {
+        if (i + 1 < ntiles && !issue_s(i + 1)) {
+          ok = false;
+          break;
+        }
+        const int s = i % ATC_STAGES;
+        if (!mbar_wait(&sh.p_full, i & 1) || !mbar_wait(&sh.v_full[s], (i / ATC_STAGES) & 1) ||
+            (i > 0 && !mbar_wait(&sh.o_free, (i - 1) & 1)) || *(volatile int*)&sh.abort) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t vb = smem_u32(kv_s + s * 2 * ATC_REGION + ATC_REGION);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: two 8-key groups of 1024 bytes
+          tc::umma_bf16(tmem + ATC_O_COL, tc::sdesc_sw128(pa + (kk >> 2) * ATC_BOX + (kk & 3) * 32),
+                        sdesc_sw128_mn(vb + kk * 2048, ATC_BOX), idesc_o, kk > 0 ? 1u : 0u);
+        tc::umma_commit(&sh.kv_empty[s]);
+        tc::umma_commit(&sh.o_full);
+      }
+      if (!ok) {
+        atomicExch(a.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+      }
+    }
+  } else {
+    // ---------------- query rows (warps 2-5) ----------------
+    const int eq = warp & 3;
+    const int r = eq * 32 + lane;  // row of the block == TMEM lane
+    const int row = rb * 128 + r;
+    const bool valid = row < a.R;
+    const int t = valid ? row / a.G : 0, gh = valid ? row % a.G : 0;
+    {
+      const bf16* qrow = a.q + (((int64_t)b * a.T + t) * a.Hq + kvh * a.G + gh) * D;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = valid ? ldg16(qrow + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(q_s + atc_off(r, c)) = v;
+      }
+    }
+    fence_proxy_async();  // the MMA (async proxy) reads what these threads wrote
+    mbar_arrive(&sh.q_full);
+    // Visible keys of this row: every key below `lo`, and key mask_base + i
+    // for each bit i of `mbits` - the causal rule (keys up to start + t) or
+    // the tree rule (shared context below mask_base, then bit i of the row's
+    // mask for key mask_base + i, nothing from mask_base + 32 on), both cut
+    // at kv_len.
+    int lo = 0, mask_base = 0;
+    uint32_t mbits = 0u;
+    if (valid) {
+      if (a.tree_mask != nullptr) {
+        mask_base = a.mask_origin >= 0 ? a.mask_origin : start;
+        lo = min(mask_base, kv_len);
+        const int span = kv_len - mask_base;  // keys from mask_base below kv_len
+        mbits = span <= 0 ? 0u : (a.tree_mask[b * a.T + t] & (span >= 32 ? 0xffffffffu : ((1u << span) - 1u)));
+      } else {
+        lo = min(kv_len, start + t + 1);
+      }
+    }
+    auto visible = [lo, mask_base, mbits](int kabs) {
+      const uint32_t rel = (uint32_t)(kabs - mask_base);
+      return kabs < lo || (rel < 32u && ((mbits >> (rel & 31u)) & 1u));
+    };
+    const uint32_t lane_off = (uint32_t)(eq * 32) << 16;
+    float o[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool alive = true;
+    for (int i = 0; i < ntiles; ++i) {
+      const int sb = i & 1;
+      // the warp takes one decision (tcgen05.ld is warp-collective)
+      if (!__all_sync(0xffffffffu, mbar_wait(&sh.s_full[sb], (i >> 1) & 1) ? 1 : 0)) {
+        if (lane == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+        alive = false;
+        break;
+      }
+      tc::tc_fence_after();
+      const int key0 = key_begin + i * ATC_TILE;
+      const uint32_t sa = tmem + lane_off + sb * 128;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tc::tmem_ld16(sa + c * 16, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) mx = fmaxf(mx, visible(key0 + c * 16 + j) ? v[j] * a.scale_log2 : -INFINITY);
+      }
+      // rows with nothing visible so far keep m = -inf and p = 0
+      const float mn = fmaxf(m, mx);
+      const float al = mn == -INFINITY ? 1.f : exp2f(m - mn);
+      const float sub = mn == -INFINITY ? 0.f : mn;
+      m = mn;
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tc::tmem_ld16(sa + c * 16, v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const float s0 = visible(key0 + c * 16 + j) ? v[j] * a.scale_log2 : -INFINITY;
+          const float s1 = visible(key0 + c * 16 + j + 1) ? v[j + 1] * a.scale_log2 : -INFINITY;
+          const float p0 = exp2f(s0 - sub), p1 = exp2f(s1 - sub);
+          ps += p0 + p1;
+          pk[j >> 1] = pack_bf2(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(p_s + atc_off(r, 2 * c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(p_s + atc_off(r, 2 * c + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      l = l * al + ps;
+      tc::tc_fence_before();
+      mbar_arrive(&sh.s_free[sb]);  // S buffer sb may be overwritten
+      fence_proxy_async();
+      mbar_arrive(&sh.p_full);
+      if (!__all_sync(0xffffffffu, mbar_wait(&sh.o_full, i & 1) ? 1 : 0)) {
+        if (lane == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+        alive = false;
+        break;
+      }
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tc::tmem_ld16(tmem + lane_off + ATC_O_COL + c * 16, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[c * 16 + j] = o[c * 16 + j] * al + v[j];
+      }
+      tc::tc_fence_before();
+      mbar_arrive(&sh.o_free);
+    }
+    if (alive && valid) {
+      if (a.nsplit == 1) {
+        // single split: normalise in place (same expression as the combine pass)
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        bf16* dst = a.out + (((int64_t)b * a.T + t) * a.Hq + kvh * a.G + gh) * D;
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          *reinterpret_cast<uint4*>(dst + c * 8) =
+              make_uint4(pack_bf2(o[c * 8] * inv, o[c * 8 + 1] * inv), pack_bf2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv),
+                         pack_bf2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv),
+                         pack_bf2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv));
+      } else {
+        const int64_t unit = ((int64_t)b * a.Hkv + kvh) * a.nsplit + split;
+        float4* wo = reinterpret_cast<float4*>(a.ws_o + (unit * a.Rpad + row) * D);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) wo[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        a.ws_ml[unit * a.Rpad + row] = make_float2(m, l);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ATC_TMEM_COLS));
+  }
+}
+
+// alignment + Q + P + the K/V ring, then one region of slack behind the
+// last V tile: the PV operand descriptor spans at most one region from its
+// start whichever way its two strides are read, so every tensor-core read
+// stays inside the allocation
+constexpr size_t atc_smem_bytes() { return 1024 + 2 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION + ATC_REGION; }
+
+// Process-wide switch for the tcgen05 variant (off by default).
+int g_attn_tc = 0;
+
 }  // namespace
+
+extern "C" void tsds_set_attention_tc(int on) { g_attn_tc = on ? 1 : 0; }
+extern "C" int tsds_get_attention_tc(void) { return g_attn_tc; }
 
 extern "C" size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int Dd, int max_kv, int split_keys) {
   if (B <= 0 || T <= 0 || Hkv <= 0 || Hq % Hkv || Dd != D || split_keys <= 0) return 0;
@@ -420,6 +751,23 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.nrb = nrb;
   a.mask_origin = mask_origin;
   a.scale_log2 = scale * LOG2E;
+
+  if (g_attn_tc && split_keys % ATC_TILE == 0) {
+    // 128-key boxes for the tcgen05 variant
+    st = tsds_make_tmap_2d_bf16(&kmap, k_cache, D, rows, D * 2, 64, ATC_TILE, 1);
+    if (st != TSDS_OK) return st;
+    st = tsds_make_tmap_2d_bf16(&vmap, v_cache, D, rows, D * 2, 64, ATC_TILE, 1);
+    if (st != TSDS_OK) return st;
+    static bool tc_attr[TSDS_MAX_DEVICES] = {};
+    st = tsds_smem_limit_once(verify_attn_tc_kernel, (int)atc_smem_bytes(), tc_attr);
+    if (st != TSDS_OK) return st;
+    tsds_launch(verify_attn_tc_kernel, dim3(nsplit * nrb, Hkv, B), dim3(ATC_THREADS), atc_smem_bytes(), stream,
+                kmap, vmap, a);
+    st = tsds_launch_status();
+    if (st != TSDS_OK || nsplit == 1) return st;
+    tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);
+    return tsds_launch_status();
+  }
 
   const size_t smem = attn_smem_bytes();
   static bool attr_set[TSDS_MAX_DEVICES] = {};

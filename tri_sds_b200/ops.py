@@ -99,6 +99,16 @@ def set_gemv_max_rows(rows: int) -> None:
     _lib.load().tsds_set_gemv_max_rows(int(rows))
 
 
+def set_attention_tc(on: bool) -> None:
+    """Run verify attention on its tcgen05 variant (process-wide) for calls
+    whose split_keys is a multiple of 128; off: the default kernel."""
+    _lib.load().tsds_set_attention_tc(1 if on else 0)
+
+
+def attention_tc() -> bool:
+    return bool(_lib.load().tsds_get_attention_tc())
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None):
     """norm.py:61-72 over the rows of a 2-D tensor."""
     _bf16_cuda(x, weight, out)
