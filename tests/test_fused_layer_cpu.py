@@ -89,7 +89,7 @@ class FakePeer:
         return TRef(self.slots[slot])
 
 
-@pytest.mark.parametrize("tp,rank", [(2, 1), (8, 6)])
+@pytest.mark.parametrize("tp,rank", [(1, 0), (2, 1), (8, 6)])
 def test_tensor_parallel_fused_plan_with_peer_phases(recorded, tp, rank):
     from tri_sds_b200.model import QwenModel
 

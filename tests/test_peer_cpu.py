@@ -120,8 +120,9 @@ def tensor_refs(monkeypatch):
     yield
 
 
-@pytest.mark.parametrize("tp,rank", [(2, 1), (8, 5)])
+@pytest.mark.parametrize("tp,rank", [(1, 0), (2, 1), (8, 5)])
 def test_plan_uses_the_peer_slots(tensor_refs, tp, rank):
+    """(tp = 1: a one-rank group, the peer paths on one GPU.)"""
     from tri_sds_b200.eagle import EagleEngine, EagleHead
     from tri_sds_b200.model import QwenModel
     B = 2
@@ -158,7 +159,7 @@ class FakeExchangePeer(FakePeer):
         return TRef(self.exchange[offset:])
 
 
-@pytest.mark.parametrize("tp,rank", [(2, 0), (8, 7)])
+@pytest.mark.parametrize("tp,rank", [(1, 0), (2, 0), (8, 7)])
 def test_lm_head_gathers_over_peer_memory(tensor_refs, tp, rank):
     """With an exchange region, a tensor-parallel EAGLE cycle has no NCCL
     step at all: the row-parallel all-reduces run on peer memory and every

@@ -180,10 +180,12 @@ class QwenModel:
             comm = share_embeddings.comm if share_embeddings is not None else LocalComm()
         self.comm = comm
         # tp.PeerAllReduce: the row-parallel all-reduces run as this library's
-        # peer-memory kernel instead of NCCL's (layers sharded only)
+        # peer-memory kernel instead of NCCL's (layers sharded only).  A
+        # one-rank group (tp_size 1) runs the same kernels with nothing to
+        # exchange: the peer paths on one GPU, bit for bit the plain plan.
         self.peer = peer
         if peer is not None:
-            assert tp_layers and tp_size > 1 and (peer.rank, peer.size) == (tp_rank, tp_size)
+            assert tp_layers and (peer.rank, peer.size) == (tp_rank, tp_size)
             assert peer.max_elems >= max_rows * shape.hidden
         # the vocab-parallel LM head exchanges candidates / logits through the
         # peer group's exchange region when it has one (the EAGLE head shares
@@ -193,7 +195,7 @@ class QwenModel:
             self.lm_rows = share_embeddings.lm_rows
         else:
             vt = tp_size if tp_vocab else 1
-            use = peer is not None and vt > 1 and getattr(peer, "exchange_bytes", 0) > 0
+            use = peer is not None and getattr(peer, "exchange_bytes", 0) > 0
             self.lm_peer = peer if use else None
             self.lm_rows = max_rows
             if use:
@@ -315,7 +317,7 @@ class QwenModel:
         n_peer = [0]
 
         def row_parallel(src, ld_src, w, k_in):
-            if not tp:
+            if not tp and self.peer is None:
                 pl.add("tsds_linear_residual", _p(src), ld_src, _p(w), _p(xb), _p(xb), s.hidden, M, s.hidden, k_in,
                        _p(lw), lb)
                 return
@@ -368,7 +370,7 @@ class QwenModel:
         qn = self.qk_norm
         pl = Plan()
         N = s.hidden
-        peer = self.peer if self.layer_tp > 1 else None
+        peer = self.peer
         # two-shot all-reduce once a rank would pull more than TWO_SHOT_BYTES
         # of the other ranks' partials in one shot (same bits either way)
         two_shot = peer is not None and M * N * 4 * (peer.size - 1) > TWO_SHOT_BYTES
@@ -430,7 +432,7 @@ class QwenModel:
         rows, ld = (B, T * s.hidden) if last_only else (B * T, s.hidden)
         src = xb[T - 1:] if last_only else xb
         pl.add("tsds_rms_norm", _p(src), _p(self.norm_w), _p(self.xn), rows, s.hidden, ld, s.hidden, s.eps)
-        if self.vocab_tp == 1:
+        if self.vocab_tp == 1 and self.lm_peer is None:
             pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(logits_out), _p(argmax_out),
                    argmax_stride, None, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
             return pl

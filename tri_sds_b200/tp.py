@@ -145,7 +145,10 @@ class PeerAllReduce:
             mine = (ctypes.c_uint8 * hb)()
             _lib.call("tsds_peer_export", self._own, mine)
             handles = [None] * size
-            dist.all_gather_object(handles, bytes(mine), group=group)
+            if size == 1:   # one rank: nothing to exchange (no process group needed)
+                handles[0] = bytes(mine)
+            else:
+                dist.all_gather_object(handles, bytes(mine), group=group)
             ptrs = []
             for p, h in enumerate(handles):
                 if p == rank:
