@@ -167,7 +167,8 @@ int tsds_linear_bias(const void* x, int ldx, const void* W, const void* bias, vo
  * the split boundaries depend only on the key index, so a query's result
  * does not depend on T or B.  max_kv bounds starts[b]+T (sizes the grid).
  * Replaces attention_gqa / _decode_attn_gqa_kernel (attention.py:236-318)
- * and the verify SDPA of qwen_model.py:121-131.  D = 128, T*Hq/Hkv <= 1024.
+ * and the verify SDPA of qwen_model.py:121-131.  D = 128, T*Hq/Hkv <= 1024
+ * (<= 65536 on the tcgen05 variant below), B*Hkv*S < 2^31.
  */
 size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int max_kv,
                                       int split_keys);

@@ -5,7 +5,7 @@ kernel, for causal and tree masks, one and two 128-row query blocks, single
 splits that run the online softmax over many 128-key tiles (no combine pass),
 many short splits (with the combine pass), splits past the last key, and the
 32B-shape verify configurations (B=8 over 4096 keys; the EAGLE tree, 26 rows
-per sequence x 8 q heads per kv head).
+per sequence x 8 q heads per kv head), and the prompt prefill on it.
 Runs only with TSDS_TEST_ATTN_TC=1 until the kernel has been validated on a
 B200."""
 import os
@@ -146,6 +146,24 @@ def test_tc_attention_close_to_default_kernel(ops):
     ref = _run(ops, q, kc, vc, st).cpu().float()
     ops.set_attention_tc(True)
     assert (tc - ref).abs().max().item() <= TOL
+
+
+@pytest.mark.parametrize("B,P", [(1, 512), (2, 300)])
+def test_tc_prefill_matches_sdpa(ops, B, P):
+    """Prompt prefill with its attention on the tcgen05 kernel (every prompt
+    row of a kv head in one call, causal, one split) against the same
+    prefill on SDPA."""
+    from tri_sds_b200.model import QwenModel
+    from tri_sds_b200.shapes import QwenShape
+    kw = dict(hidden=512, n_heads=16, n_kv_heads=2, head_dim=128, intermediate=1024, n_layers=2, vocab=1000)
+    w = oq.random_qwen_weights(oq.QwenShape(**kw), seed=P, std=0.05)
+    m = QwenModel(QwenShape(**kw), batch=B, max_seq=P + 64, max_rows=B * 5, device=DEV, weights=w)
+    prompt = torch.randint(0, kw["vocab"], (B, P), generator=torch.Generator().manual_seed(B))
+    tc = m.prefill(prompt).float().cpu()
+    ops.set_attention_tc(False)
+    ref = m.prefill(prompt).float().cpu()
+    ops.set_attention_tc(True)
+    assert (tc - ref).abs().max().item() <= 5e-2
 
 
 def test_tc_attention_in_the_model(ops):

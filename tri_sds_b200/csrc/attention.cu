@@ -464,8 +464,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   pdl_trigger();
   const int start = a.starts[b];
   const int kv_len = start + a.T;
+  // causal rows see no key past start + t: the block's last token bounds the
+  // tiles it needs (a tile past it would only add exact zeros)
+  int vis_end = kv_len;
+  if (a.tree_mask == nullptr) vis_end = min(kv_len, start + (min(a.R, (rb + 1) * 128) - 1) / a.G + 1);
   const int key_begin = split * a.split_keys;
-  const int key_end = min(key_begin + a.split_keys, kv_len);
+  const int key_end = min(key_begin + a.split_keys, vis_end);
   const int ntiles = key_end > key_begin ? (key_end - key_begin + ATC_TILE - 1) / ATC_TILE : 0;
 
   if (warp == 0) {
@@ -713,8 +717,13 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   TSDS_RETURN_IF(!tsds_aligned16(q) || !tsds_aligned16(k_cache) || !tsds_aligned16(v_cache) || !tsds_aligned16(out),
                  TSDS_E_ALIGN);
   const int G = Hq / Hkv;
-  const int R = T * G;
-  TSDS_RETURN_IF(R > 1024, TSDS_E_UNSUPPORTED);
+  const long long R64 = (long long)T * G;
+  // the tcgen05 variant takes any number of 128-row blocks (a prompt's rows
+  // in one call); the default kernel up to 1024 rows per kv head
+  const bool tc = g_attn_tc && split_keys % ATC_TILE == 0;
+  TSDS_RETURN_IF(R64 > (tc ? 65536 : 1024), TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF((uint64_t)B * Hkv * S > (uint64_t)INT32_MAX, TSDS_E_UNSUPPORTED);  // cache rows are int
+  const int R = (int)R64;
   const int Rpad = (R + 15) / 16 * 16;
   const int nrb = (Rpad + 127) / 128;
   const int warps = Rpad >= 128 ? 8 : Rpad / 16;
@@ -752,7 +761,7 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.mask_origin = mask_origin;
   a.scale_log2 = scale * LOG2E;
 
-  if (g_attn_tc && split_keys % ATC_TILE == 0) {
+  if (tc) {
     // 128-key boxes for the tcgen05 variant
     st = tsds_make_tmap_2d_bf16(&kmap, k_cache, D, rows, D * 2, 64, ATC_TILE, 1);
     if (st != TSDS_OK) return st;

@@ -510,11 +510,19 @@ class QwenModel:
             ops.qk_norm_rope_kv(qkv, L.q_norm if self.qk_norm else None, L.k_norm if self.qk_norm else None,
                                 self.cos, self.sin, pos, starts, q, self.k_cache[i], self.v_cache[i], B, P,
                                 ls.n_heads, ls.n_kv_heads, s.eps)
-            qh = q.reshape(B, P, ls.n_heads, s.head_dim).transpose(1, 2)
-            kh = self.k_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
-            vh = self.v_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
-            a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True)
-            a = a.transpose(1, 2).reshape(B * P, ls.q_dim)
+            if ops.attention_tc():
+                # the prompt's causal attention on the library's tcgen05
+                # kernel: every prompt row of a kv head in one call, one key
+                # split (no combine pass)
+                a = ops.verify_attention(q.view(B, P, ls.n_heads, s.head_dim), self.k_cache[i], self.v_cache[i],
+                                         starts, max_kv=P, split_keys=(P + 127) // 128 * 128)
+                a = a.reshape(B * P, ls.q_dim)
+            else:
+                qh = q.reshape(B, P, ls.n_heads, s.head_dim).transpose(1, 2)
+                kh = self.k_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
+                vh = self.v_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
+                a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True)
+                a = a.transpose(1, 2).reshape(B * P, ls.q_dim)
             x = x + row_parallel(a, L.w_o)
             xn = ops.rms_norm(x, L.ln2, s.eps)
             gu = xn @ L.w_gu.T
