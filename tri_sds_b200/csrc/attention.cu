@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       const bf16* qrow = a.q + (((int64_t)b * a.T + t) * a.Hq + kvh * a.G + gh) * D;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const uint4 v = valid ? ldg16(qrow + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 v = valid ? *reinterpret_cast<const uint4*>(qrow + c * 8) : make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4*>(q_s + atc_off(r, c)) = v;
       }
     }
