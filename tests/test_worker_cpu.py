@@ -14,8 +14,9 @@ class FakeEngine:
         self.tokens = torch.full((B, width), -1, dtype=torch.int64)
         self.accept_len = torch.zeros(B, dtype=torch.int32)
 
-    def prepare(self, prompt):
+    def prepare(self, prompt, lengths=None):
         self.calls.append(("prepare", tuple(prompt.shape)))
+        self.prompt, self.lengths = prompt, lengths
         return prompt[:, -1]
 
     def step(self, U=None):
@@ -102,3 +103,27 @@ def test_status_watch_raises_on_a_device_error():
     assert int(words[1]) == 0
     w.copy()
     w.check()   # clean now
+
+
+def test_ragged_prompts_reach_the_engine_padded_with_their_lengths(monkeypatch):
+    """SGLang batches hold prompts of different lengths: a list of prompts is
+    padded behind each prompt and the lengths go with it; a padded [B, P]
+    tensor carries them in seq_lens; full rows need none."""
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker, prompt_tensor
+    monkeypatch.setenv("SDS_ENABLED", "1")
+    w = TriSDSWorker()
+    eng = FakeEngine()
+    w.attach_engine(eng)
+    w.forward_batch_generation(ScheduleBatch(input_ids=[[5, 6, 7], [8], [9, 10, 11, 12]]))
+    assert eng.calls[0] == ("prepare", (3, 4))
+    assert eng.prompt.tolist() == [[5, 6, 7, 0], [8, 0, 0, 0], [9, 10, 11, 12]]
+    assert eng.lengths.tolist() == [3, 1, 4]
+    ids, n = prompt_tensor(ScheduleBatch(input_ids=torch.ones(2, 6, dtype=torch.int64), seq_lens=[6, 2]))
+    assert ids.shape == (2, 6) and n.dtype == torch.int32 and n.tolist() == [6, 2]
+    ids, n = prompt_tensor(ScheduleBatch(input_ids=[[1, 2], [3, 4]]))
+    assert ids.tolist() == [[1, 2], [3, 4]] and n is None
+    ids, n = prompt_tensor(ScheduleBatch(input_ids=[1, 2, 3]))
+    assert ids.shape == (1, 3) and n is None
+    with pytest.raises(ValueError):
+        prompt_tensor(ScheduleBatch(input_ids=[[1], []]))

@@ -179,13 +179,17 @@ class EagleEngine:
 
     # -- driving -----------------------------------------------------------------
     @torch.no_grad()
-    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+    def prefill(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
+        """Prefill the target from a [B, P] prompt (ragged: ``lengths[b]``
+        real tokens per row); the root of the first tree is each sequence's
+        last prompt token's feature and argmax."""
         t = self.target
         prompt = prompt.to(t.device)
-        hidden = t.prefill(prompt)
-        first = t.logits_of(hidden[:, -1]).argmax(-1)
+        hidden = t.prefill(prompt, lengths)
+        last = t.last_rows(hidden, lengths)
+        first = t.logits_of(last).argmax(-1)
         self.cur.copy_(first)
-        self.root_feat.copy_(hidden[:, -1])
+        self.root_feat.copy_(last)
         return first
 
     def draw_uniforms(self, U: torch.Tensor | None = None):
@@ -205,11 +209,11 @@ class EagleEngine:
             self.plan.run()
         self.graph = g
 
-    def prepare(self, prompt: torch.Tensor) -> torch.Tensor:
+    def prepare(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
         if self.use_graph and self.graph is None:
-            self.prefill(prompt)
+            self.prefill(prompt, lengths)
             self._capture()
-        return self.prefill(prompt)
+        return self.prefill(prompt, lengths)
 
     def step(self, U: torch.Tensor | None = None):
         """One cycle -> (tokens [B, depth+2] padded -1, accept_len [B])."""
@@ -222,9 +226,9 @@ class EagleEngine:
         return self.tokens, self.accept_len
 
     @torch.no_grad()
-    def generate(self, prompt: torch.Tensor, n_new: int):
+    def generate(self, prompt: torch.Tensor, n_new: int, lengths: torch.Tensor | None = None):
         B = prompt.shape[0]
-        first = self.prepare(prompt).cpu()
+        first = self.prepare(prompt, lengths).cpu()
         out = [[int(first[b])] for b in range(B)]
         accepts = []
         while min(len(o) for o in out) < n_new:

@@ -78,17 +78,26 @@ class SpecEngine:
         return self.plan.kernel_count()
 
     @torch.no_grad()
-    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
-        """Fill both caches from a [B, P] prompt; returns the first token [B]."""
+    def prefill(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
+        """Fill both caches from a [B, P] prompt (ragged: ``lengths[b]`` real
+        tokens per row); returns the first token [B].  The draft caches every
+        prompt token but the last, which its first step consumes."""
         B, P = prompt.shape
-        prompt = prompt.to(self.target.device)
-        hidden = self.target.prefill(prompt)
-        first = self.target.logits_of(hidden[:, -1]).argmax(-1)
-        if P > 1:
-            self.draft.prefill(prompt[:, :P - 1])
-        self.last.copy_(prompt[:, -1])
+        dev = self.target.device
+        prompt = prompt.to(dev)
+        hidden = self.target.prefill(prompt, lengths)
+        first = self.target.logits_of(self.target.last_rows(hidden, lengths)).argmax(-1)
+        if lengths is None:
+            if P > 1:
+                self.draft.prefill(prompt[:, :P - 1])
+            self.last.copy_(prompt[:, -1])
+        else:
+            n = torch.as_tensor(lengths).to(device=dev, dtype=torch.int64)
+            if P > 1:
+                self.draft.prefill(prompt[:, :P - 1], torch.clamp(n - 1, min=1))
+                self.draft.lengths.copy_((n - 1).to(torch.int32))   # 0 for a one-token prompt
+            self.last.copy_(prompt[torch.arange(B, device=dev), n - 1])
         self.cur.copy_(first)
-        self.target.lengths.fill_(P)
         return first
 
     def _capture(self):
@@ -136,19 +145,19 @@ class SpecEngine:
         self._watch.check()
         return tokens_host, accept_host
 
-    def prepare(self, prompt: torch.Tensor):
+    def prepare(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None):
         """Prefill, capture the cycle graph (its warm-up run disturbs the
         caches, so the prefill is redone after capture), return first tokens."""
         if self.use_graph and self.graph is None:
-            self.prefill(prompt)
+            self.prefill(prompt, lengths)
             self._capture()
-        return self.prefill(prompt)
+        return self.prefill(prompt, lengths)
 
     @torch.no_grad()
-    def generate(self, prompt: torch.Tensor, n_new: int):
+    def generate(self, prompt: torch.Tensor, n_new: int, lengths: torch.Tensor | None = None):
         """Greedy speculative generation; returns ([B, n_new] tokens, accept lens per cycle)."""
         B = prompt.shape[0]
-        first = self.prepare(prompt).cpu()
+        first = self.prepare(prompt, lengths).cpu()
         out = [[int(first[b])] for b in range(B)]
         accepts = []
         while min(len(o) for o in out) < n_new:
@@ -180,12 +189,12 @@ class AutoregressiveEngine:
         self.graph = None
 
     @torch.no_grad()
-    def generate(self, prompt: torch.Tensor, n_new: int) -> torch.Tensor:
+    def generate(self, prompt: torch.Tensor, n_new: int, lengths: torch.Tensor | None = None) -> torch.Tensor:
         prompt = prompt.to(self.target.device)
 
         def prefill():
-            hidden = self.target.prefill(prompt)
-            self.cur.copy_(self.target.logits_of(hidden[:, -1]).argmax(-1))
+            hidden = self.target.prefill(prompt, lengths)
+            self.cur.copy_(self.target.logits_of(self.target.last_rows(hidden, lengths)).argmax(-1))
             return self.cur.clone()
 
         if self.use_graph and self.graph is None:

@@ -12,9 +12,9 @@ The device-side counterpart of ``QwenModelState`` + ``qwen_model_forward``
   pointer bound - so one speculative cycle can be captured in a CUDA graph;
 * Qwen3's QK-norm (HF order: projection -> q/k RMSNorm -> RoPE).
 
-The prompt prefill (untimed set-up) runs through cuBLAS GEMMs and SDPA,
-with the cache written by the same QK-norm/RoPE/KV kernel as the
-verify path.
+The prompt prefill (untimed set-up) runs through cuBLAS GEMMs and SDPA
+(or the library's tcgen05 attention when that is switched on), with the
+cache written by the same QK-norm/RoPE/KV kernel as the verify path.
 """
 from __future__ import annotations
 
@@ -483,11 +483,20 @@ class QwenModel:
 
     # -- prefill (untimed set-up: cuBLAS + SDPA) -------------------------------
     @torch.no_grad()
-    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+    def prefill(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
         """Process a [B, P] prompt from row 0; returns the hidden states
-        [B, P, N] (pre final norm) and sets lengths = P."""
+        [B, P, N] (pre final norm) and sets lengths = P.  Ragged prompts:
+        ``lengths[b]`` (1..P) real tokens at the start of row b, the rest
+        padding; the causal attention keeps every real token's state
+        independent of the padding behind it, and lengths = lengths (the
+        padding's cache rows lie past the sequence and are overwritten by the
+        next forward)."""
         s, ls = self.shape, self.lshape
         B, P = prompt.shape
+        if lengths is not None:
+            lengths = torch.as_tensor(lengths).to(torch.int32)
+            assert lengths.shape == (B,) and int(lengths.min()) >= 1 and int(lengths.max()) <= P, \
+                "prompt lengths must be in 1..P"
         dev = self.device
         prompt = prompt.to(dev)
         x = self.embed_w[prompt].reshape(B * P, s.hidden)
@@ -528,8 +537,20 @@ class QwenModel:
             gu = xn @ L.w_gu.T
             h = F.silu(gu[:, :ls.intermediate]) * gu[:, ls.intermediate:]
             x = x + row_parallel(h, L.w_d)
-        self.lengths.fill_(P)
+        if lengths is None:
+            self.lengths.fill_(P)
+        else:
+            self.lengths.copy_(lengths.to(dev))
         return x.reshape(B, P, s.hidden)
+
+    @staticmethod
+    def last_rows(hidden: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
+        """hidden[b, lengths[b] - 1] for every b (the last real token of
+        ragged prompts; the last column without lengths)."""
+        if lengths is None:
+            return hidden[:, -1]
+        idx = torch.as_tensor(lengths).to(device=hidden.device, dtype=torch.int64) - 1
+        return hidden[torch.arange(hidden.shape[0], device=hidden.device), idx]
 
     def logits_of(self, hidden: torch.Tensor) -> torch.Tensor:
         """Final norm + full bf16 logits (set-up / tests only)."""

@@ -35,9 +35,12 @@ except Exception:  # noqa: BLE001
 
     @dataclass
     class ScheduleBatch:
-        """The fields the spec worker reads: token ids [B, T] and positions."""
+        """The fields the spec worker reads: token ids [B, T] (or a list of
+        the sequences' prompts, ragged), positions, and seq_lens (real tokens
+        per row of a padded [B, P] prompt)."""
         input_ids: object = None
         positions: object = None
+        seq_lens: object = None
         extra: dict = field(default_factory=dict)
 
     class StandaloneWorker:

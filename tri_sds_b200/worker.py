@@ -25,6 +25,34 @@ import torch
 from .sglang_compat import ScheduleBatch, StandaloneWorker
 
 
+def prompt_tensor(batch: ScheduleBatch):
+    """The batch's prompts as a [B, P] id tensor and their lengths: a [B, P]
+    tensor (with ``seq_lens`` when its rows are padded) or one [P] prompt as
+    they are; a list of per-sequence prompts of different lengths is padded
+    with zeros behind each prompt (lengths then give the real tokens, None
+    when every row is full)."""
+    ids = batch.input_ids
+    lengths = getattr(batch, "seq_lens", None)
+    if isinstance(ids, (list, tuple)) and ids and not isinstance(ids[0], int):
+        seqs = [torch.as_tensor(x, dtype=torch.int64).reshape(-1) for x in ids]
+        n = [int(x.numel()) for x in seqs]
+        if min(n) < 1:
+            raise ValueError("every prompt needs at least one token")
+        P = max(n)
+        out = torch.zeros(len(seqs), P, dtype=torch.int64)
+        for b, x in enumerate(seqs):
+            out[b, :n[b]] = x
+        if lengths is None and min(n) < P:
+            lengths = torch.tensor(n, dtype=torch.int32)
+        return out, lengths
+    ids = torch.as_tensor(ids)
+    if ids.dim() == 1:
+        ids = ids.unsqueeze(0)
+    if lengths is not None:
+        lengths = torch.as_tensor(lengths).to(torch.int32).reshape(-1)
+    return ids, lengths
+
+
 class TriSDSWorker(StandaloneWorker):
     sds_enabled: bool = False
     engine = None
@@ -46,10 +74,8 @@ class TriSDSWorker(StandaloneWorker):
         if self.engine is None:
             self._init_engine()
         if not self._prefilled:
-            ids = torch.as_tensor(batch.input_ids)
-            if ids.dim() == 1:
-                ids = ids.unsqueeze(0)
-            self.engine.prepare(ids)
+            ids, lengths = prompt_tensor(batch)
+            self.engine.prepare(ids, lengths)
             self._prefilled = True
 
     # -- dispatch (worker.py:42-55) -------------------------------------------
