@@ -376,8 +376,9 @@ size_t attn_smem_bytes() { return (size_t)kStages * TILE_BYTES + 1024; }
 // * Softmax: each thread reads its row of S from TMEM twice (row max, then
 //   exp2 and row sum) and writes P (bf16) into shared memory in the
 //   128-byte-swizzled K-major layout the next MMA reads.
-// * O_i = P V: M = 128 rows, N = 128 dims, K = 128 keys, with V read
-//   MN-major (dims contiguous) straight from its TMA tile.  Each thread folds
+// * O_i = P V: M = 128 rows, K = 128 keys, as two MMAs of N = 64 dims, each
+//   reading one 64-dim box of the V tile MN-major (dims contiguous) straight
+//   from TMA's layout.  Each thread folds
 //   its row of O_i into registers, o = o * alpha + O_i: an online softmax over
 //   the tiles of the key split, so one CTA can cover a long split without a
 //   combine pass.
@@ -409,12 +410,14 @@ __device__ __forceinline__ uint32_t atc_off(int row, int c) {
   return (c >> 3) * ATC_BOX + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
-// Shared-memory descriptor of an MN-major operand in 128-byte-swizzled rows:
-// 64-element blocks along N are `lbo` bytes apart, groups of 8 rows along K
-// 1024 bytes apart.
-__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+// Shared-memory descriptor of an MN-major operand of one 64-element swizzle
+// atom along N (one 128-byte-swizzled row per K index, groups of 8 rows 1024
+// bytes apart along K).  With a single atom along N the two strides of the
+// descriptor have one meaning between them, the K-group stride, so both hold
+// 1024.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn64(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 16;
   d |= (uint64_t)(1024 >> 4) << 32;
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
@@ -499,10 +502,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && ntiles > 0) {
-      // bf16 x bf16 -> fp32, M = 128, N = 128; PV reads B (V) MN-major
+      // bf16 x bf16 -> fp32, M = 128: S with N = 128 keys; O in two MMAs of
+      // N = 64 dims (one V box each), B (V) read MN-major
       const uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
                                ((uint32_t)(128 >> 4) << 24);
-      const uint32_t idesc_o = idesc_s | (1u << 16);
+      const uint32_t idesc_o = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) |
+                               ((uint32_t)(128 >> 4) << 24);
       const uint32_t qa = smem_u32(q_s), pa = smem_u32(p_s);
       auto issue_s = [&](int i) -> bool {
         const int s = i % ATC_STAGES, sb = i & 1;
@@ -535,9 +540,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         tc::tc_fence_after();
         const uint32_t vb = smem_u32(kv_s + s * 2 * ATC_REGION + ATC_REGION);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: two 8-key groups of 1024 bytes
-          tc::umma_bf16(tmem + ATC_O_COL, tc::sdesc_sw128(pa + (kk >> 2) * ATC_BOX + (kk & 3) * 32),
-                        sdesc_sw128_mn(vb + kk * 2048, ATC_BOX), idesc_o, kk > 0 ? 1u : 0u);
+        for (int h = 0; h < 2; ++h)  // dims 64h..64h+63: O columns 64h.., V box h
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: two 8-key groups of 1024 bytes
+            tc::umma_bf16(tmem + ATC_O_COL + h * 64, tc::sdesc_sw128(pa + (kk >> 2) * ATC_BOX + (kk & 3) * 32),
+                          sdesc_sw128_mn64(vb + h * ATC_BOX + kk * 2048), idesc_o, kk > 0 ? 1u : 0u);
         tc::umma_commit(&sh.kv_empty[s]);
         tc::umma_commit(&sh.o_full);
       }
@@ -682,11 +689,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   }
 }
 
-// alignment + Q + P + the K/V ring, then one region of slack behind the
-// last V tile: the PV operand descriptor spans at most one region from its
-// start whichever way its two strides are read, so every tensor-core read
-// stays inside the allocation
-constexpr size_t atc_smem_bytes() { return 1024 + 2 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION + ATC_REGION; }
+// alignment + Q + P + the K/V ring
+constexpr size_t atc_smem_bytes() { return 1024 + 2 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION; }
 
 // Process-wide switch for the tcgen05 variant (off by default).
 int g_attn_tc = 0;
