@@ -74,8 +74,9 @@ def _args():
                     help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v (N = 1)")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
-    ap.add_argument("--attn-tc", action="store_true",
-                    help="verify attention on its tcgen05 variant (library default: off)")
+    ap.add_argument("--attn-tc", type=int, nargs="?", const=1, default=0, choices=[0, 1, 2],
+                    help="verify attention on its tcgen05 variant (1; 2: splits combined in a cluster; "
+                         "library default 0: off)")
     ap.add_argument("--attn-split", type=int, default=128,
                     help="keys per attention split of the target / draft (a multiple of 64; of 128 for --attn-tc)")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
@@ -362,7 +363,7 @@ def run_attention(a):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic: N(0,1) q / K / V",
             "config": {"workload": _workload(a), "global_batch": B, "seq_len": L, "parallelism": "none",
                        "l2": f"{sets} cache sets rotate ({sets * kv_bytes / 2**20:.0f} MB > 2 x L2)",
-                       "attention": {"tcgen05": bool(_lib.query("tsds_get_attention_tc")),
+                       "attention": {"tcgen05": _lib.query("tsds_get_attention_tc"),
                                      "split_keys": a.attn_split}},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": nbytes,
@@ -433,7 +434,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     if a.pair_rows is not None:
         _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
     if a.attn_tc:
-        _lib.load().tsds_set_attention_tc(1)
+        _lib.load().tsds_set_attention_tc(a.attn_tc)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
     dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
     per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
@@ -604,7 +605,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
-            "attention": {"tcgen05": bool(_lib.load().tsds_get_attention_tc()), "split_keys": a.attn_split},
+            "attention": {"tcgen05": _lib.load().tsds_get_attention_tc(), "split_keys": a.attn_split},
         }
         if breakdown is not None:
             line["breakdown"] = breakdown
@@ -643,7 +644,7 @@ def main():
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
             if a.attn_tc:
-                _lib.load().tsds_set_attention_tc(1)
+                _lib.load().tsds_set_attention_tc(a.attn_tc)
             (run_attention if a.mode == "attention" else run_layer)(a)
         else:
             run_tsds(a, rank, world, local_rank)

@@ -182,8 +182,11 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
  * TMEM accumulators, one softmax thread per query row, 128-key tiles) for
  * every call whose split_keys is a multiple of 128; other calls keep the
  * default kernel.  Same arguments, workspace and masking; results agree
- * within fp32 rounding of the products, not bit for bit. */
-void tsds_set_attention_tc(int on);
+ * within fp32 rounding of the products, not bit for bit.  With 2, calls of
+ * 2 to 8 key splits also run each row block's splits as one thread-block
+ * cluster that combines them through distributed shared memory instead of
+ * a second launch (same bits as 1). */
+void tsds_set_attention_tc(int mode);
 int tsds_get_attention_tc(void);
 
 /* ---------------------------------------------------------------------------

@@ -148,6 +148,34 @@ def test_tc_attention_close_to_default_kernel(ops):
     assert (tc - ref).abs().max().item() <= TOL
 
 
+def _tree_masks(B, T, seed):
+    g = torch.Generator().manual_seed(seed)
+    parent = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, T)]
+    masks = []
+    for t in range(T):
+        m, j = 0, t
+        while j >= 0:
+            m |= 1 << j
+            j = parent[j]
+        masks.append(m)
+    return torch.tensor([masks] * B, dtype=torch.int64).to(torch.int32)
+
+
+@pytest.mark.parametrize("B,T,starts,S,tree", [(1, 26, [512], 1024, True), (2, 26, [300, 700], 896, True),
+                                               (2, 5, [100, 517], 640, False), (3, 1, [0, 63, 200], 256, False)])
+def test_tc_cluster_combine_equals_combine_pass(ops, B, T, starts, S, tree):
+    """Mode 2: the 2 to 8 key splits of a row block as one cluster, combined
+    through distributed shared memory - the same bits as the combine pass."""
+    q, kc, vc, st = _case(B, T, 64, 8, S, starts, seed=S + T)
+    tm = _tree_masks(B, T, seed=T) if tree else None
+    one = _run(ops, q, kc, vc, st, tree_mask=tm)
+    ops.set_attention_tc(2)
+    two = _run(ops, q, kc, vc, st, tree_mask=tm)
+    ops.set_attention_tc(1)
+    assert torch.equal(one, two)
+    assert (two.cpu().float() - _ref_f32(q, kc, vc, st, tree_mask=tm)).abs().max().item() <= TOL
+
+
 @pytest.mark.parametrize("B,P", [(1, 512), (2, 300)])
 def test_tc_prefill_matches_sdpa(ops, B, P):
     """Prompt prefill with its attention on the tcgen05 kernel (every prompt
@@ -181,6 +209,7 @@ def test_tc_attention_in_the_model(ops):
     wt = oq.random_qwen_weights(oshape, seed=0, std=0.08)
     we = oe.random_eagle_weights(oshape, seed=1, std=0.08)
     prompt = torch.randint(0, oshape.vocab, (B, 10), generator=torch.Generator().manual_seed(2))
+    ops.set_attention_tc(2)   # with the clustered combine (max_seq 256: two splits)
     tgt = QwenModel(shape, batch=B, max_seq=256, max_rows=B * 26, device=DEV, weights=wt)
     eng = EagleEngine(tgt, EagleHead(tgt, B, weights=we), greedy=True)
     spec, _ = eng.generate(prompt, n_new)

@@ -77,6 +77,7 @@ struct AttnArgs {
   int32_t* status;
   int B, T, Hq, Hkv, S, G, R, Rpad, nsplit, split_keys, nrb, mask_origin;
   float scale_log2;
+  int cl;  // tcgen05 variant: the splits of a row block form a cluster and combine through shared memory
 };
 
 template <int STAGES>
@@ -392,6 +393,12 @@ constexpr int ATC_REGION = 2 * ATC_BOX;        // 128 rows x 128 dims (or keys) 
 constexpr int ATC_STAGES = 2;
 constexpr int ATC_TMEM_COLS = 512;             // S buffers at columns 0 and 128, O_i at 256
 constexpr int ATC_O_COL = 256;
+// cluster mode: row partials [128][ATC_PO_LD] fp32 (rows padded by 16 bytes
+// against bank conflicts) then (m, l) per row, in the idle K/V ring
+constexpr int ATC_PO_LD = 132;
+constexpr int ATC_PML_OFF = 128 * ATC_PO_LD * 4;
+constexpr int ATC_MAX_CLUSTER = 8;              // portable cluster size
+static_assert(ATC_PML_OFF + 128 * 8 <= ATC_STAGES * 2 * ATC_REGION, "cluster partials fit in the K/V ring");
 
 struct AtcSmem {
   uint64_t k_full[ATC_STAGES];
@@ -403,6 +410,20 @@ struct AtcSmem {
   uint32_t tmem_base;
   int abort;
 };
+
+__device__ __forceinline__ float2 ld_cluster_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 
 // byte offset of 16-byte chunk c (of 16) of row `row` in a 128 x 128 bf16
 // region stored as two 64-column boxes with the TMA 128-byte swizzle
@@ -433,7 +454,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   uint8_t* q_s = smem;                    // Q rows of the block, kept for every tile
   uint8_t* p_s = smem + ATC_REGION;       // P of the current tile
   uint8_t* kv_s = smem + 2 * ATC_REGION;  // stage s: K at s * 2 * REGION, V after it
-  const int rb = blockIdx.x % a.nrb, split = blockIdx.x / a.nrb;
+  // cluster mode: the nsplit splits of one row block are consecutive CTAs
+  const int rb = a.cl ? blockIdx.x / a.nsplit : blockIdx.x % a.nrb;
+  const int split = a.cl ? blockIdx.x % a.nsplit : blockIdx.x / a.nrb;
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -661,7 +684,16 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       tc::tc_fence_before();
       mbar_arrive(&sh.o_free);
     }
-    if (alive && valid) {
+    if (a.cl) {
+      // this row's partial into shared memory (the K/V ring is idle now)
+      // for the cluster's combine below
+      float* po = reinterpret_cast<float*>(kv_s) + r * ATC_PO_LD;
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        *reinterpret_cast<float4*>(po + 4 * c) = alive ? make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3])
+                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float2*>(kv_s + ATC_PML_OFF)[r] = alive ? make_float2(m, l) : make_float2(-INFINITY, 0.f);
+    } else if (alive && valid) {
       if (a.nsplit == 1) {
         // single split: normalise in place (same expression as the combine pass)
         const float inv = l > 0.f ? 1.0f / l : 0.f;
@@ -683,6 +715,47 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   }
   tc::tc_fence_before();
   __syncthreads();
+  if (a.cl) {
+    // Combine of the cluster's nsplit partials (the arithmetic and split
+    // order of attn_combine_kernel): CTA `split` finishes rows
+    // [split*128/n, (split+1)*128/n) of the block, a warp per row, a lane per
+    // 4 dims, reading every CTA's partials through distributed shared memory.
+    tc::cluster_sync_all();  // every CTA's partials are written
+    const int n = a.nsplit;
+    const uint32_t po0 = smem_u32(kv_s), pml0 = smem_u32(kv_s + ATC_PML_OFF);
+    for (int rr = split * 128 / n + warp; rr < (split + 1) * 128 / n; rr += ATC_THREADS / 32) {
+      const int row = rb * 128 + rr;
+      if (row >= a.R) break;  // uniform over the warp
+      float2 ml[ATC_MAX_CLUSTER];
+      float mmax = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < ATC_MAX_CLUSTER; ++q)
+        if (q < n) {
+          ml[q] = ld_cluster_f2(tc::mapa_shared(pml0 + rr * 8, q));
+          mmax = fmaxf(mmax, ml[q].x);
+        }
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float lsum = 0.f;
+      if (mmax != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < ATC_MAX_CLUSTER; ++q)
+          if (q < n && ml[q].x != -INFINITY) {
+            const float w = exp2f(ml[q].x - mmax);
+            lsum += w * ml[q].y;
+            const float4 v = ld_cluster_f4(tc::mapa_shared(po0 + (rr * ATC_PO_LD + 4 * lane) * 4, q));
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
+          }
+      }
+      const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+      const int t = row / a.G, gh = row % a.G;
+      bf16* dst = a.out + (((int64_t)b * a.T + t) * a.Hq + kvh * a.G + gh) * D + 4 * lane;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf2(acc.x * inv, acc.y * inv), pack_bf2(acc.z * inv, acc.w * inv));
+    }
+    tc::cluster_sync_all();  // no CTA leaves while another still reads its shared memory
+  }
   if (warp == 1) {
     tc::tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ATC_TMEM_COLS));
@@ -692,12 +765,39 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
 // alignment + Q + P + the K/V ring
 constexpr size_t atc_smem_bytes() { return 1024 + 2 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION; }
 
-// Process-wide switch for the tcgen05 variant (off by default).
+// Process-wide switch for the tcgen05 variant (off by default; 2: with the
+// clustered combine where the split count allows).
 int g_attn_tc = 0;
+
+// Whether clusters of n tcgen05-attention CTAs (a whole SM's shared memory
+// each) can be resident; cached per n.
+bool atc_clusters_fit(int n) {
+  static int known[ATC_MAX_CLUSTER + 1] = {};  // 0 unknown, 1 yes, 2 no
+  if (known[n] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n);
+    cfg.blockDim = dim3(ATC_THREADS);
+    cfg.dynamicSmemBytes = atc_smem_bytes();
+    cudaLaunchAttribute ca[1];
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = n;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = 1;
+    cfg.attrs = ca;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, verify_attn_tc_kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    known[n] = clusters > 0 ? 1 : 2;
+  }
+  return known[n] == 1;
+}
 
 }  // namespace
 
-extern "C" void tsds_set_attention_tc(int on) { g_attn_tc = on ? 1 : 0; }
+extern "C" void tsds_set_attention_tc(int mode) { g_attn_tc = mode < 0 ? 0 : (mode > 2 ? 2 : mode); }
 extern "C" int tsds_get_attention_tc(void) { return g_attn_tc; }
 
 extern "C" size_t tsds_attention_workspace_bytes(int B, int T, int Hq, int Hkv, int Dd, int max_kv, int split_keys) {
@@ -764,6 +864,7 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.nrb = nrb;
   a.mask_origin = mask_origin;
   a.scale_log2 = scale * LOG2E;
+  a.cl = 0;
 
   if (tc) {
     // 128-key boxes for the tcgen05 variant
@@ -774,6 +875,13 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
     static bool tc_attr[TSDS_MAX_DEVICES] = {};
     st = tsds_smem_limit_once(verify_attn_tc_kernel, (int)atc_smem_bytes(), tc_attr);
     if (st != TSDS_OK) return st;
+    if (g_attn_tc == 2 && nsplit >= 2 && nsplit <= ATC_MAX_CLUSTER && atc_clusters_fit(nsplit)) {
+      // the splits of a row block as one cluster, combined in shared memory
+      a.cl = 1;
+      tsds_launch_cluster(verify_attn_tc_kernel, dim3(nrb * nsplit, Hkv, B), dim3(ATC_THREADS), atc_smem_bytes(),
+                          stream, nsplit, kmap, vmap, a);
+      return tsds_launch_status();
+    }
     tsds_launch(verify_attn_tc_kernel, dim3(nsplit * nrb, Hkv, B), dim3(ATC_THREADS), atc_smem_bytes(), stream,
                 kmap, vmap, a);
     st = tsds_launch_status();

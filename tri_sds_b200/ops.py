@@ -99,14 +99,15 @@ def set_gemv_max_rows(rows: int) -> None:
     _lib.load().tsds_set_gemv_max_rows(int(rows))
 
 
-def set_attention_tc(on: bool) -> None:
+def set_attention_tc(mode: int | bool) -> None:
     """Run verify attention on its tcgen05 variant (process-wide) for calls
-    whose split_keys is a multiple of 128; off: the default kernel."""
-    _lib.load().tsds_set_attention_tc(1 if on else 0)
+    whose split_keys is a multiple of 128: 1 / True; 2: also combine 2 to 8
+    key splits inside a thread-block cluster; 0 / False: the default kernel."""
+    _lib.load().tsds_set_attention_tc(int(mode))
 
 
-def attention_tc() -> bool:
-    return bool(_lib.load().tsds_get_attention_tc())
+def attention_tc() -> int:
+    return int(_lib.load().tsds_get_attention_tc())
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None):
