@@ -40,3 +40,31 @@ def test_argument_validation_without_gpu():
                                     1, 1, 8, 2, 64, 16, 16, 1e-6, None) == 6                 # UNSUPPORTED D
     assert lib.tsds_verify_attention(None, None, None, None, None, None, -1, 1, 4, 8, 2, 64, 64, 64, 64,
                                      0.1, None, 0, None, None) == 6                           # UNSUPPORTED D
+
+
+def test_attention_row_and_cache_limits_without_gpu():
+    """tsds_verify_attention's size checks (host only, before any device
+    call): the default kernel takes up to 1024 query rows per kv head, the
+    tcgen05 variant up to 65536; cache rows B*Hkv*S must fit an int."""
+    import ctypes
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    p = ctypes.c_void_p(0x1000)   # aligned stand-ins: the checks under test come first
+
+    def call(T, Hq=64, Hkv=8, B=1, S=4096, split=128):
+        return lib.tsds_verify_attention(p, p, p, p, p, None, -1, B, T, Hq, Hkv, 128, S, S, split, 0.1, p, 1 << 30,
+                                         p, None)
+
+    try:
+        lib.tsds_set_attention_tc(0)
+        assert call(T=129) == 6                     # 1032 rows: UNSUPPORTED on the default kernel
+        assert call(T=128, B=1 << 16, Hkv=8, S=4096) == 6   # 2^31 cache rows
+        lib.tsds_set_attention_tc(1)
+        assert lib.tsds_get_attention_tc() == 1
+        assert call(T=129) not in (1, 2, 6)        # past the row checks (fails later: no device here)
+        assert call(T=8193) == 6                    # 65544 rows
+        assert call(T=129, split=64) == 6           # 64-key splits keep the default kernel and its limit
+        lib.tsds_set_attention_tc(7)
+        assert lib.tsds_get_attention_tc() == 2     # clamped
+    finally:
+        lib.tsds_set_attention_tc(0)
