@@ -411,6 +411,22 @@ struct AtcSmem {
   int abort;
 };
 
+// 32 consecutive TMEM columns of this thread's lane, one wait for the load
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ float2 ld_cluster_f2(uint32_t addr) {
   float2 v;
   asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
@@ -634,11 +650,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       const uint32_t sa = tmem + lane_off + sb * 128;
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tc::tmem_ld16(sa + c * 16, v);
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(sa + c * 32, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) mx = fmaxf(mx, visible(key0 + c * 16 + j) ? v[j] * a.scale_log2 : -INFINITY);
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, visible(key0 + c * 32 + j) ? v[j] * a.scale_log2 : -INFINITY);
       }
       // rows with nothing visible so far keep m = -inf and p = 0
       const float mn = fmaxf(m, mx);
@@ -675,11 +691,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       }
       tc::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tc::tmem_ld16(tmem + lane_off + ATC_O_COL + c * 16, v);
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + ATC_O_COL + c * 32, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[c * 16 + j] = o[c * 16 + j] * al + v[j];
+        for (int j = 0; j < 32; ++j) o[c * 32 + j] = o[c * 32 + j] * al + v[j];
       }
       tc::tc_fence_before();
       mbar_arrive(&sh.o_free);
