@@ -71,7 +71,8 @@ def _args():
                     help="also time every library call of CYCLES eager cycles (CUDA events around each call) "
                          "and add the per-entry-point totals to the JSON line")
     ap.add_argument("--fused-layers", action="store_true",
-                    help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v (N = 1)")
+                    help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v "
+                         "(N > 1: with --allreduce peer, whose all-reduces become phases of it)")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
     ap.add_argument("--attn-tc", type=int, nargs="?", const=1, default=0, choices=[0, 1, 2],
@@ -80,7 +81,7 @@ def _args():
     ap.add_argument("--attn-split", type=int, default=128,
                     help="keys per attention split of the target / draft (a multiple of 64; of 128 for --attn-tc)")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
-                    help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 4)")
+                    help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 0)")
     return ap.parse_args()
 
 
