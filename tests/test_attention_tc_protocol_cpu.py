@@ -2,9 +2,11 @@
 
 verify_attn_tc_kernel (tri_sds_b200/csrc/attention.cu) runs three roles per
 CTA: the TMA producer (K and V tiles of 128 keys into a 2-deep ring), the MMA
-issuer (S_i = Q K_i^T into one of two TMEM buffers, O_i = P_i V_i into one)
-and four warps of query rows (softmax of S_i into P_i in shared memory, then
-O_i folded into registers).  Every hand-off is an mbarrier waited on by phase
+issuer (S_i = Q K_i^T into one of two TMEM buffers, O_i = P_i V_i into one
+of two) and four warps of query rows (softmax of S_i into one of two P
+buffers in shared memory; O_{i-1} is folded into registers after the
+softmax of tile i, so the P V product of one tile overlaps the softmax of
+the next).  Every hand-off is an mbarrier waited on by phase
 parity, as in the kernel: a wait for parity p returns once the barrier has
 completed a phase of that parity, so a waiter two phases behind would block.
 Each role is a generator yielding the condition it waits on; TMA loads
@@ -15,9 +17,10 @@ completion.  Every run must finish and respect:
 * S_i reads Q (every warp's rows written) and K_i (loaded into its stage);
 * S_i overwrites an S buffer only after every warp finished reading S_{i-2};
 * the warps read S_i only after S_i completed;
-* the warps write P_i only after O_{i-1} (the last reader of P) completed;
-* O_i reads P_i of all four warps and V_i, and overwrites O only after every
-  warp has read O_{i-1};
+* the warps write P_i only after O_{i-2} (the last reader of its buffer)
+  completed;
+* O_i reads P_i of all four warps and V_i, and overwrites its O buffer only
+  after every warp has read O_{i-2};
 * the warps read O_i only after it completed;
 * the producer reloads a stage only after O_{i-2}, its last reader, completed.
 """
@@ -61,9 +64,10 @@ def run(n, seed, skip=None):
     kv_empty = [Bar(1) for _ in range(STAGES)]
     s_full = [Bar(1), Bar(1)]
     s_free = [Bar(WARPS), Bar(WARPS)]
-    q_full, p_full, o_full, o_free = Bar(WARPS), Bar(WARPS), Bar(1), Bar(WARPS)
-    st = {"k": [None] * STAGES, "v": [None] * STAGES, "S": [None, None], "O": None,
-          "P": [None] * WARPS, "Q": [False] * WARPS}
+    q_full = Bar(WARPS)
+    p_full, o_full, o_free = [Bar(WARPS), Bar(WARPS)], [Bar(1), Bar(1)], [Bar(WARPS), Bar(WARPS)]
+    st = {"k": [None] * STAGES, "v": [None] * STAGES, "S": [None, None], "O": [None, None],
+          "P": [[None] * WARPS, [None] * WARPS], "Q": [False] * WARPS}
     s_read = {}                  # tile -> warps done reading S_i
     o_read = {}                  # tile -> warps done reading O_i
     done = {"S": set(), "O": set()}
@@ -89,7 +93,7 @@ def run(n, seed, skip=None):
         assert st["k"][s] == i, f"S_{i} reads stage {s} holding {st['k'][s]}"
 
     def check_o(i, s):
-        assert st["P"] == [i] * WARPS, f"O_{i} reads P {st['P']}"
+        assert st["P"][i & 1] == [i] * WARPS, f"O_{i} reads P {st['P'][i & 1]}"
         assert st["v"][s] == i, f"O_{i} reads V stage {s} holding {st['v'][s]}"
 
     def issue_s(i):
@@ -110,17 +114,28 @@ def run(n, seed, skip=None):
         for i in range(n):
             if i + 1 < n:
                 yield from issue_s(i + 1)
-            s = i % STAGES
+            s, pb = i % STAGES, i & 1
             if skip != "p_full":
-                yield lambda: p_full.ready(i & 1)
+                yield lambda: p_full[pb].ready((i >> 1) & 1)
             yield lambda: v_full[s].ready((i // STAGES) & 1)
-            if i > 0 and skip != "o_free":
-                yield lambda: o_free.ready((i - 1) & 1)
-            if i > 0:
-                assert len(o_read.get(i - 1, ())) == WARPS, f"O_{i} overwrites O_{i - 1} still being read"
+            if i >= 2 and skip != "o_free":
+                yield lambda: o_free[pb].ready(((i - 2) >> 1) & 1)
+            if i >= 2:
+                assert len(o_read.get(i - 2, ())) == WARPS, f"O_{i} overwrites O_{i - 2} still being read"
             check_o(i, s)
-            st["O"] = None
-            tensor.append(("O", i, s, None))
+            st["O"][pb] = None
+            tensor.append(("O", i, s, pb))
+
+    def fold(w, j):
+        """Warp w folds O_j (after the softmax of tile j + 1, or at the end)."""
+        ob = j & 1
+        if skip != "o_full":
+            yield lambda: o_full[ob].ready((j >> 1) & 1)
+        assert st["O"][ob] == j, f"warp {w} reads O buffer {ob} holding {st['O'][ob]} for tile {j}"
+        yield None
+        assert st["O"][ob] == j, f"warp {w}: O buffer {ob} overwritten while being read (tile {j})"
+        o_read.setdefault(j, set()).add(w)
+        o_free[ob].arrive()
 
     def warp(w):
         yield None
@@ -128,24 +143,21 @@ def run(n, seed, skip=None):
         q_full.arrive()
         yield None
         for i in range(n):
-            sb = i & 1
+            sb, pb = i & 1, i & 1
             yield lambda: s_full[sb].ready((i >> 1) & 1)
             assert st["S"][sb] == i, f"warp {w} reads S buffer {sb} holding {st['S'][sb]} for tile {i}"
             yield None                              # pass 1 (row max) ... pass 2
             assert st["S"][sb] == i, f"warp {w}: S buffer {sb} overwritten during the softmax of tile {i}"
-            if i > 0:
-                assert i - 1 in done["O"], f"warp {w} writes P_{i} while O_{i - 1} may read P"
-            st["P"][w] = i
+            if i >= 2:
+                assert i - 2 in done["O"], f"warp {w} writes P_{i} while O_{i - 2} may read its buffer"
+            st["P"][pb][w] = i
             s_read.setdefault(i, set()).add(w)
             s_free[sb].arrive()
-            p_full.arrive()
-            if skip != "o_full":
-                yield lambda: o_full.ready(i & 1)
-            assert st["O"] == i, f"warp {w} reads O holding {st['O']} for tile {i}"
-            yield None
-            assert st["O"] == i, f"warp {w}: O overwritten while being read (tile {i})"
-            o_read.setdefault(i, set()).add(w)
-            o_free.arrive()
+            p_full[pb].arrive()
+            if i >= 1:
+                yield from fold(w, i - 1)
+        if n:
+            yield from fold(w, n - 1)
 
     def complete_tensor():
         kind, i, s, sb = tensor.pop(0)
@@ -156,10 +168,10 @@ def run(n, seed, skip=None):
             s_full[sb].arrive()
         else:
             check_o(i, s)
-            st["O"] = i
+            st["O"][sb] = i
             done["O"].add(i)
             kv_empty[s].arrive()        # both commits follow O_i
-            o_full.arrive()
+            o_full[sb].arrive()
 
     def complete_tma(j):
         kind, s, i = tma.pop(j)
@@ -198,7 +210,7 @@ def test_tc_attention_pipeline(n, seed):
 @pytest.mark.parametrize("skip", ["s_free", "o_free"])
 @pytest.mark.parametrize("seed", range(20))
 def test_the_buffer_free_waits_are_implied(skip, seed):
-    """Every warp publishes P_i after its last read of S_{i-1} and of O_{i-1},
+    """Every warp publishes P_i after its last read of S_{i-1} and of O_{i-2},
     and the issuer waits for P_i before O_i (and for P_{i-1} before S_{i+1}):
     the kernel's s_free and o_free waits are second guards of orders the P
     hand-off already gives, and the model finishes without either."""

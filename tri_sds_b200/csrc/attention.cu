@@ -379,10 +379,11 @@ size_t attn_smem_bytes() { return (size_t)kStages * TILE_BYTES + 1024; }
 //   128-byte-swizzled K-major layout the next MMA reads.
 // * O_i = P V: M = 128 rows, K = 128 keys, as two MMAs of N = 64 dims, each
 //   reading one 64-dim box of the V tile MN-major (dims contiguous) straight
-//   from TMA's layout.  Each thread folds
-//   its row of O_i into registers, o = o * alpha + O_i: an online softmax over
-//   the tiles of the key split, so one CTA can cover a long split without a
-//   combine pass.
+//   from TMA's layout.  Each thread folds its row of O_i into registers,
+//   o = o * alpha + O_i: an online softmax over the tiles of the key split,
+//   so one CTA can cover a long split without a combine pass.  P and O are
+//   double-buffered and O_i is folded after the softmax of tile i+1, so the
+//   P V product of one tile overlaps the softmax of the next.
 // Masking, the log2-domain softmax and the partial layout are those of
 // verify_attn_kernel, so the combine pass is shared.
 // ---------------------------------------------------------------------------
@@ -391,7 +392,7 @@ constexpr int ATC_TILE = 128;                  // keys per tile
 constexpr int ATC_BOX = ATC_TILE * 128;        // 128 rows x one 128-byte swizzle row: 16 KB
 constexpr int ATC_REGION = 2 * ATC_BOX;        // 128 rows x 128 dims (or keys) in bf16: 32 KB
 constexpr int ATC_STAGES = 2;
-constexpr int ATC_TMEM_COLS = 512;             // S buffers at columns 0 and 128, O_i at 256
+constexpr int ATC_TMEM_COLS = 512;             // S buffers at columns 0 and 128, O buffers at 256 and 384
 constexpr int ATC_O_COL = 256;
 // cluster mode: row partials [128][ATC_PO_LD] fp32 (rows padded by 16 bytes
 // against bank conflicts) then (m, l) per row, in the idle K/V ring
@@ -406,7 +407,10 @@ struct AtcSmem {
   uint64_t kv_empty[ATC_STAGES];
   uint64_t s_full[2];
   uint64_t s_free[2];
-  uint64_t q_full, p_full, o_full, o_free;
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint64_t o_free[2];
+  uint64_t q_full;
   uint32_t tmem_base;
   int abort;
 };
@@ -468,8 +472,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ AtcSmem sh;
   uint8_t* q_s = smem;                    // Q rows of the block, kept for every tile
-  uint8_t* p_s = smem + ATC_REGION;       // P of the current tile
-  uint8_t* kv_s = smem + 2 * ATC_REGION;  // stage s: K at s * 2 * REGION, V after it
+  uint8_t* p_s = smem + ATC_REGION;       // P of tile i in buffer i & 1
+  uint8_t* kv_s = smem + 3 * ATC_REGION;  // stage s: K at s * 2 * REGION, V after it
   // cluster mode: the nsplit splits of one row block are consecutive CTAs
   const int rb = a.cl ? blockIdx.x / a.nsplit : blockIdx.x % a.nrb;
   const int split = a.cl ? blockIdx.x % a.nsplit : blockIdx.x / a.nrb;
@@ -487,9 +491,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       mbar_init(&sh.s_free[i], 128);
     }
     mbar_init(&sh.q_full, 128);
-    mbar_init(&sh.p_full, 128);
-    mbar_init(&sh.o_full, 1);
-    mbar_init(&sh.o_free, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.p_full[i], 128);
+      mbar_init(&sh.o_full[i], 1);
+      mbar_init(&sh.o_free[i], 128);
+    }
     sh.abort = 0;
     fence_barrier_init();
   }
@@ -570,22 +576,24 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           ok = false;
           break;
         }
-        const int s = i % ATC_STAGES;
-        if (!mbar_wait(&sh.p_full, i & 1) || !mbar_wait(&sh.v_full[s], (i / ATC_STAGES) & 1) ||
-            (i > 0 && !mbar_wait(&sh.o_free, (i - 1) & 1)) || *(volatile int*)&sh.abort) {
+        const int s = i % ATC_STAGES, pb = i & 1;
+        if (!mbar_wait(&sh.p_full[pb], (i >> 1) & 1) || !mbar_wait(&sh.v_full[s], (i / ATC_STAGES) & 1) ||
+            (i >= 2 && !mbar_wait(&sh.o_free[pb], ((i - 2) >> 1) & 1)) || *(volatile int*)&sh.abort) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
         const uint32_t vb = smem_u32(kv_s + s * 2 * ATC_REGION + ATC_REGION);
+        const uint32_t pbuf = pa + pb * ATC_REGION;
 #pragma unroll
         for (int h = 0; h < 2; ++h)  // dims 64h..64h+63: O columns 64h.., V box h
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: two 8-key groups of 1024 bytes
-            tc::umma_bf16(tmem + ATC_O_COL + h * 64, tc::sdesc_sw128(pa + (kk >> 2) * ATC_BOX + (kk & 3) * 32),
+            tc::umma_bf16(tmem + ATC_O_COL + pb * 128 + h * 64,
+                          tc::sdesc_sw128(pbuf + (kk >> 2) * ATC_BOX + (kk & 3) * 32),
                           sdesc_sw128_mn64(vb + h * ATC_BOX + kk * 2048), idesc_o, kk > 0 ? 1u : 0u);
         tc::umma_commit(&sh.kv_empty[s]);
-        tc::umma_commit(&sh.o_full);
+        tc::umma_commit(&sh.o_full[pb]);
       }
       if (!ok) {
         atomicExch(a.status, TSDS_E_TIMEOUT);
@@ -636,6 +644,29 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     for (int i = 0; i < 128; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f;
     bool alive = true;
+    // O_j = P_j V_j into o: o = o * alpha_j + O_j.  Runs after the softmax of
+    // tile j + 1 (or after the last tile), so the P V product of one tile
+    // overlaps the softmax of the next; the warp takes one decision.
+    auto fold = [&](int j, float alpha) -> bool {
+      const int ob = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sh.o_full[ob], (j >> 1) & 1) ? 1 : 0)) {
+        if (lane == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
+        sh.abort = 1;
+        return false;
+      }
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + ATC_O_COL + ob * 128 + c * 32, v);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) o[c * 32 + jj] = o[c * 32 + jj] * alpha + v[jj];
+      }
+      tc::tc_fence_before();
+      mbar_arrive(&sh.o_free[ob]);
+      return true;
+    };
+    float al_prev = 1.f;
     for (int i = 0; i < ntiles; ++i) {
       const int sb = i & 1;
       // the warp takes one decision (tcgen05.ld is warp-collective)
@@ -662,6 +693,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       const float sub = mn == -INFINITY ? 0.f : mn;
       m = mn;
       float ps = 0.f;
+      uint8_t* pbuf = p_s + (i & 1) * ATC_REGION;  // free: O_{i-2}, its last reader, was folded
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         float v[16];
@@ -675,31 +707,21 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           ps += p0 + p1;
           pk[j >> 1] = pack_bf2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(p_s + atc_off(r, 2 * c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(p_s + atc_off(r, 2 * c + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        *reinterpret_cast<uint4*>(pbuf + atc_off(r, 2 * c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(pbuf + atc_off(r, 2 * c + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       l = l * al + ps;
       tc::tc_fence_before();
       mbar_arrive(&sh.s_free[sb]);  // S buffer sb may be overwritten
       fence_proxy_async();
-      mbar_arrive(&sh.p_full);
-      if (!__all_sync(0xffffffffu, mbar_wait(&sh.o_full, i & 1) ? 1 : 0)) {
-        if (lane == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
-        sh.abort = 1;
+      mbar_arrive(&sh.p_full[i & 1]);
+      if (i >= 1 && !fold(i - 1, al_prev)) {
         alive = false;
         break;
       }
-      tc::tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(tmem + lane_off + ATC_O_COL + c * 32, v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) o[c * 32 + j] = o[c * 32 + j] * al + v[j];
-      }
-      tc::tc_fence_before();
-      mbar_arrive(&sh.o_free);
+      al_prev = al;
     }
+    if (alive && ntiles > 0 && !fold(ntiles - 1, al_prev)) alive = false;
     if (a.cl) {
       // this row's partial into shared memory (the K/V ring is idle now)
       // for the cluster's combine below
@@ -778,8 +800,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   }
 }
 
-// alignment + Q + P + the K/V ring
-constexpr size_t atc_smem_bytes() { return 1024 + 2 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION; }
+// alignment + Q + two P buffers + the K/V ring
+constexpr size_t atc_smem_bytes() { return 1024 + 3 * (size_t)ATC_REGION + (size_t)ATC_STAGES * 2 * ATC_REGION; }
 
 // Process-wide switch for the tcgen05 variant (off by default; 2: with the
 // clustered combine where the split count allows).
