@@ -159,7 +159,12 @@ __global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant_
     // every thread polls; the CTA agrees on the outcome before anyone moves on
     const int ok = mbar_wait(&full_bar[s], (tile / STAGES) & 1) ? 1 : 0;
     if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) atomicExch(a.status, TSDS_E_TIMEOUT);
+      if (threadIdx.x == 0) {
+        atomicExch(a.status, TSDS_E_TIMEOUT);
+        // tiles 0 .. tile + STAGES - 1 were requested: let the ones still in
+        // flight land (bounded) before the CTA exits
+        drain_tma_ring(full_bar, STAGES, min(ntiles, tile + STAGES));
+      }
       aborted = true;
       break;
     }
@@ -411,6 +416,7 @@ struct AtcSmem {
   uint64_t o_full[2];
   uint64_t o_free[2];
   uint64_t q_full;
+  uint64_t drain_bar;  // abort path: completion of the MMAs issued so far
   uint32_t tmem_base;
   int abort;
 };
@@ -496,6 +502,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       mbar_init(&sh.o_full[i], 1);
       mbar_init(&sh.o_free[i], 128);
     }
+    mbar_init(&sh.drain_bar, 1);
     sh.abort = 0;
     fence_barrier_init();
   }
@@ -519,6 +526,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const int key_begin = split * a.split_keys;
   const int key_end = min(key_begin + a.split_keys, vis_end);
   const int ntiles = key_end > key_begin ? (key_end - key_begin + ATC_TILE - 1) / ATC_TILE : 0;
+  int issued = 0;  // producer lane: K/V tiles requested; MMA lane: 1 once an MMA was issued
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -542,6 +550,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         mbar_arrive_expect_tx(&sh.v_full[s], ATC_REGION);
         tma_load_2d(ks + ATC_REGION, &vmap, &sh.v_full[s], 0, row);
         tma_load_2d(ks + ATC_REGION + ATC_BOX, &vmap, &sh.v_full[s], 64, row);
+        issued = i + 1;
       }
     }
   } else if (warp == 1) {
@@ -568,6 +577,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
                         kk > 0 ? 1u : 0u);
         }
         tc::umma_commit(&sh.s_full[sb]);
+        issued = 1;
         return true;
       };
       bool ok = mbar_wait(&sh.q_full, 0) && issue_s(0);
@@ -753,6 +763,16 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   }
   tc::tc_fence_before();
   __syncthreads();
+  if (sh.abort) {  // uniform: read after the barrier
+    // a CTA that gave up still lets its copies and MMAs in flight finish
+    // (bounded) before TMEM is freed and it exits
+    if (warp == 0 && lane == 0 && issued > 0) {
+      drain_tma_ring(sh.k_full, ATC_STAGES, issued);
+      drain_tma_ring(sh.v_full, ATC_STAGES, issued);
+    }
+    if (warp == 1 && lane == 0 && issued > 0) tc::drain_mma<1>(&sh.drain_bar);
+    __syncthreads();
+  }
   if (a.cl) {
     // Combine of the cluster's nsplit partials (the arithmetic and split
     // order of attn_combine_kernel): CTA `split` finishes rows

@@ -201,6 +201,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint64_
   return true;
 }
 
+// Abort paths only: a CTA that gave up on a wait still lets the TMA copies it
+// has in flight land before it frees TMEM or exits.  `full` is a ring of
+// `stages` barriers with one expect_tx per issued stage (ring index j uses
+// barrier j % stages, phase j / stages); only the last min(issued, stages)
+// issues can still be pending.  Bounded by `limit_ns` in total: a stage whose
+// bytes never arrive (its barrier never completes) costs at most that.
+__device__ __forceinline__ void drain_tma_ring(uint64_t* full, int stages, int issued,
+                                               uint64_t limit_ns = 20000000ull) {
+  const uint64_t t0 = global_ns();
+  for (int j = issued > stages ? issued - stages : 0; j < issued; ++j) {
+    while (!mbar_try_wait(&full[j % stages], (uint32_t)(j / stages) & 1u)) {
+      if (global_ns() - t0 > limit_ns) return;
+    }
+  }
+}
+
 // 2-D TMA tile load into shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(

@@ -114,6 +114,7 @@ struct ChSmem {
   uint64_t empty_bar[MAX_STAGES];
   uint64_t tfull_bar[2];
   uint64_t tempty_bar[2];
+  uint64_t drain_bar;  // abort path: completion of the MMAs issued so far
   uint32_t tmem_base;
   int abort;
   int go;
@@ -580,6 +581,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
       mbar_init(&sh.tfull_bar[i], 1);
       mbar_init(&sh.tempty_bar[i], 4 * CG);  // every epilogue warp of the pair
     }
+    mbar_init(&sh.drain_bar, 1);
     sh.abort = 0;
     fence_barrier_init();
   }
@@ -602,6 +604,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + p.stages * A_STAGE;
   pdl_trigger();
+  int issued = 0;  // producer lane: ring stages requested; MMA lane: stages consumed
 
   if (warp == 0) {
     // ---------------- TMA producer: every GEMM phase's tiles, in order -------
@@ -655,6 +658,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
           }
           expect(s);
           load_a(b + k, s);
+          issued = i + k + 1;
         }
         if (!ok) break;
         // activations: written by the previous kernel (f == 0) or by phase f-1
@@ -679,6 +683,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
           expect(s);
           load_a(b + k, s);
           load_b(b + k, s);
+          issued = i + k + 1;
         }
         i += e - b;
       }
@@ -741,6 +746,7 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
             umma_commit(&sh.tfull_bar[buf]);
         }
       }
+      issued = i;
       if (!ok) {
         atomicExch(p.status, TSDS_E_TIMEOUT);
         sh.abort = 1;
@@ -789,6 +795,15 @@ __global__ void __launch_bounds__(CH_THREADS, 2)
   }
   tc_fence_before();
   __syncthreads();
+  if (sh.abort) {  // uniform: read after the barrier
+    // a CTA that gave up still lets its copies and MMAs in flight finish
+    // (bounded) before TMEM is freed and it exits.  A pair's copies complete
+    // on the leader's barriers, which the leader drains; the other CTA
+    // leaves only after the leader (the cluster barrier below).
+    if (warp == 0 && lane == 0 && crank == 0 && issued > 0) drain_tma_ring(sh.full_bar, p.stages, issued);
+    if (warp == 1 && lane == 0 && crank == 0 && issued > 0) drain_mma<CG>(&sh.drain_bar);
+    __syncthreads();
+  }
   if constexpr (CG == 2) cluster_sync_all();  // the pair is done with both TMEM halves
   if (warp == 1) {
     tc_fence_after();

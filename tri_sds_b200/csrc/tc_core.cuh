@@ -129,5 +129,18 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Abort paths only: the MMA-issuing thread commits every tcgen05 operation
+// it has issued to `bar` (count 1, used for nothing else, phase 0) and
+// waits, bounded, until the tensor cores are done with TMEM and shared
+// memory.  CG = 2: the pair's MMAs, the commit arriving in both CTAs.
+template <int CG>
+__device__ __forceinline__ void drain_mma(uint64_t* bar, uint64_t limit_ns = 20000000ull) {
+  if constexpr (CG == 2)
+    umma_commit_pair(bar);
+  else
+    umma_commit(bar);
+  mbar_wait(bar, 0, limit_ns);
+}
+
 }  // namespace tc
 }  // namespace tsds
