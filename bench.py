@@ -20,7 +20,8 @@ i.e. sum over sequences of accept_len + 1 per cycle).
 
 N > 1 (torchrun): the target is tensor-parallel over the N GPUs (heads and
 FFN sharded, NCCL all-reduce after the O and down projections, vocab-parallel
-LM head); the draft model / EAGLE head is replicated.  The ranks serve the
+LM head); the EAGLE head is replicated, the chain draft model too unless
+``--draft-tp`` shards it over the same ranks.  The ranks serve the
 same B sequences, so the value is those tokens over the max-over-ranks time
 (strong scaling).
 
@@ -73,6 +74,9 @@ def _args():
     ap.add_argument("--fused-layers", action="store_true",
                     help="one persistent launch per layer for O -> norm -> gate/up -> down -> norm -> q/k/v "
                          "(N > 1: with --allreduce peer, whose all-reduces become phases of it)")
+    ap.add_argument("--draft-tp", action="store_true",
+                    help="chain mode, N > 1: the draft model tensor-parallel over the target's ranks (its "
+                         "all-reduces by --allreduce) instead of replicated")
     ap.add_argument("--allreduce", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: row-parallel all-reduce by NCCL, or by the library's peer-memory kernel")
     ap.add_argument("--attn-tc", type=int, nargs="?", const=1, default=0, choices=[0, 1, 2],
@@ -460,8 +464,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         head = EagleHead(target, B, seed=2000)
         engine = EagleEngine(target, head, greedy=a.greedy, seed=3000)
     else:
-        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
-                          tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split)
+        if a.draft_tp and world > 1:
+            # sharded like the target over the same ranks (and peer group)
+            draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_rank=rank,
+                              tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers,
+                              split_keys=a.attn_split)
+        else:
+            draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
+                              tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split)
         engine = SpecEngine(target, draft, K)
     # the same prompt on every rank: tensor-parallel ranks process the same tokens
     prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7))
@@ -590,6 +600,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": B, "seq_len": P,
                        "parallelism": f"tp{world}", "allreduce": a.allreduce if world > 1 else None,
+                       "draft_parallelism": (None if a.mode == "eagle" else
+                                             f"tp{world}" if a.draft_tp and world > 1 else "replicated"),
                        "fused_layers": bool(target.fused_layers),
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
                        "mode": a.mode, "target_layers": tshape.n_layers,

@@ -4,8 +4,9 @@ compacts each rank's shard of the KV cache) == greedy autoregressive
 decoding under TP=2, with the row-parallel all-reduces by NCCL or by the
 library's peer-memory kernel (standalone, or as phases of the fused-layer
 kernel).  Skipped with fewer than 2 GPUs; the peer-memory variants run only
-with TSDS_TEST_PEER=1 (and TSDS_TEST_FUSED=1) until they have been validated
-on GPUs."""
+with TSDS_TEST_PEER=1 (and TSDS_TEST_FUSED=1), and the chain leg with the
+draft model tensor-parallel too only with TSDS_TEST_DRAFT_TP=1, until they
+have been validated on GPUs."""
 import os
 import socket
 
@@ -65,6 +66,14 @@ def _worker(rank, port, q, allreduce):
                         peer=peer, fused_layers=fused)
         drf = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_size=2, tp_layers=False, tp_vocab=False)
         spec, _ = SpecEngine(tgt, drf, K).generate(prompt, 16)
+        if os.environ.get("TSDS_TEST_DRAFT_TP") == "1":
+            # the chain draft tensor-parallel over the same ranks (and peer group)
+            tgt4 = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2,
+                             comm=comm, peer=peer, fused_layers=fused)
+            drf4 = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_rank=rank, tp_size=2, comm=comm,
+                             peer=peer, fused_layers=fused)
+            spec4, _ = SpecEngine(tgt4, drf4, K).generate(prompt, 16)
+            out.update(spec_draft_tp=spec4)
         tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
                          peer=peer, fused_layers=fused)
         ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
@@ -148,6 +157,9 @@ def test_tp2_verify_and_lossless_spec(allreduce):
     assert (got - ref.float()).abs().max().item() <= 2e-2
     assert torch.equal(res[0]["am"], res[0]["logits"].float().argmax(-1))
     assert torch.equal(res[0]["spec"], res[0]["ar"])
+    if "spec_draft_tp" in res[0]:
+        assert torch.equal(res[0]["spec_draft_tp"], res[1]["spec_draft_tp"])
+        assert torch.equal(res[0]["spec_draft_tp"], res[0]["ar"])
     assert torch.equal(res[0]["espec"], res[1]["espec"])
     assert torch.equal(res[0]["espec"], res[0]["ar"])
     if allreduce != "nccl":

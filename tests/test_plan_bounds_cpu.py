@@ -57,15 +57,19 @@ def test_eagle_plans_fit_their_buffers(tensor_refs, tp, rank, B):
     _check(eng.verify_only_plan())
 
 
-@pytest.mark.parametrize("tp,rank", [(1, 0), (8, 3)])
+@pytest.mark.parametrize("tp,rank,draft_tp", [(1, 0, False), (8, 3, False), (2, 1, True), (8, 3, True)])
 @pytest.mark.parametrize("B", [1, 8])
-def test_chain_plans_fit_their_buffers(tensor_refs, tp, rank, B):
+def test_chain_plans_fit_their_buffers(tensor_refs, tp, rank, draft_tp, B):
+    """The draft replicated, or tensor-parallel over the target's ranks."""
     from tri_sds_b200.engine import SpecEngine
     from tri_sds_b200.model import QwenModel
     K = 4
-    t = QwenModel(SHAPE, B, 96, B * (K + 1), device="cpu", tp_rank=rank, tp_size=tp,
-                  comm=_Comm(rank, tp) if tp > 1 else None)
-    d = QwenModel(DRAFT, B, 96, B * 2, device="cpu", tp_size=tp, tp_layers=False, tp_vocab=False)
+    comm = _Comm(rank, tp) if tp > 1 else None
+    t = QwenModel(SHAPE, B, 96, B * (K + 1), device="cpu", tp_rank=rank, tp_size=tp, comm=comm)
+    if draft_tp:
+        d = QwenModel(DRAFT, B, 96, B * 2, device="cpu", tp_rank=rank, tp_size=tp, comm=comm)
+    else:
+        d = QwenModel(DRAFT, B, 96, B * 2, device="cpu", tp_size=tp, tp_layers=False, tp_vocab=False)
     eng = SpecEngine(t, d, K, use_graph=False)
     assert _check(eng.plan) > 50
     _check(eng.verify_only_plan())

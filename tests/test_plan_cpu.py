@@ -79,3 +79,26 @@ def test_tp8_chain_plan_shards_the_target_only():
             assert (a[9], a[10]) == (SHAPE.n_heads, SHAPE.n_kv_heads)
     vocabs = sorted({a[8] for a in _calls(eng.plan, "tsds_lm_head_argmax")})
     assert vocabs == [SHAPE.vocab // 8, SHAPE.vocab]
+
+
+def test_tp8_chain_plan_with_a_tensor_parallel_draft():
+    """The draft sharded over the target's ranks: its attention, RoPE and LM
+    head calls get the rank's shard sizes, and each of its K forwards adds
+    two all-reduces per layer."""
+    from tri_sds_b200.engine import SpecEngine
+    from tri_sds_b200.model import QwenModel
+    K = 4
+    comm = _Comm(0, 8)
+    t = QwenModel(SHAPE, 1, 64, 5, device="cpu", tp_rank=0, tp_size=8, comm=comm)
+    d = QwenModel(SHAPE, 1, 64, 2, device="cpu", tp_rank=0, tp_size=8, comm=comm)
+    eng = SpecEngine(t, d, K, use_graph=False)
+    attn = _calls(eng.plan, "tsds_verify_attention")
+    assert len(attn) == SHAPE.n_layers * (K + 1)
+    assert all((a[9], a[10]) == (SHAPE.n_heads // 8, SHAPE.n_kv_heads // 8) for a in attn)
+    for a in _calls(eng.plan, "tsds_qk_norm_rope_kv"):
+        assert (a[12], a[13]) == (SHAPE.n_heads // 8, SHAPE.n_kv_heads // 8)
+    assert {a[8] for a in _calls(eng.plan, "tsds_lm_head_argmax")} == {SHAPE.vocab // 8}
+    n_ar = sum(1 for n, fn, _ in eng.plan.calls if n == "all_reduce")
+    assert n_ar == 2 * SHAPE.n_layers * (K + 1)
+    # the draft's cache holds the rank's kv heads only
+    assert d.k_cache.shape[2] == SHAPE.n_kv_heads // 8
