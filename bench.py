@@ -66,6 +66,9 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--dp-rows", type=int, default=None,
+                    help="token rows from which a tcgen05 projection with at least one whole weight tile per CTA "
+                         "runs data-parallel instead of stream-K (library default 0: never)")
     ap.add_argument("--pair-rows", type=int, default=None,
                     help="token rows from which the tcgen05 GEMM runs on CTA pairs (library default 0: never)")
     ap.add_argument("--breakdown", type=int, default=0, metavar="CYCLES",
@@ -438,6 +441,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_pdl(0)
     if a.pair_rows is not None:
         _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+    if a.dp_rows is not None:
+        _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
     if a.attn_tc:
         _lib.load().tsds_set_attention_tc(a.attn_tc)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
@@ -618,6 +623,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
+            "gemm_dp_rows": _lib.load().tsds_get_gemm_dp_rows(),
             "attention": {"tcgen05": _lib.load().tsds_get_attention_tc(), "split_keys": a.attn_split},
         }
         if breakdown is not None:
@@ -656,6 +662,8 @@ def main():
             from tri_sds_b200 import _lib
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+            if a.dp_rows is not None:
+                _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
             if a.attn_tc:
                 _lib.load().tsds_set_attention_tc(a.attn_tc)
             (run_attention if a.mode == "attention" else run_layer)(a)

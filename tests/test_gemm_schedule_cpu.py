@@ -1,0 +1,129 @@
+"""The tcgen05 GEMM's two work schedules, restated on the CPU (nothing runs
+on a GPU): how tsds_tc_gemm (tri_sds_b200/csrc/gemm_tc.cu) sizes the grid
+and how each unit (a CTA, or a CTA pair) picks its (tile, k-block)
+iterations.
+
+* stream-K (default): unit u takes the contiguous iterations
+  [u*W/PU, (u+1)*W/PU) of the flattened W = tiles x KT space; a tile cut by
+  a range boundary is "split" and its contributors exchange fp32 partials.
+  The epilogue keeps at most two pending split tiles per unit (registers
+  pend0 / pend1) and finds a split tile's contributors as the consecutive
+  units owner_of(first k-block) .. owner_of(last k-block).
+* data-parallel (tsds_set_gemm_dp_rows; at least one tile per unit and at
+  most 15% lost to rounding up to whole tiles): unit u takes the whole tiles
+  [u*tiles/PU, (u+1)*tiles/PU); nothing is split.
+
+The checks pin the invariants the kernel relies on at the projection
+shapes of the Qwen3-32B-shape target and the Qwen3-4B-shape draft."""
+import pytest
+
+SMS = 148
+SMEM_PER_SM, SMEM_RESERVE, SMEM_BUDGET, A_STAGE, BK, MAX_STAGES = 233472, 8192, 220 * 1024, 16384, 64, 16
+
+
+def it_begin(p, P, W):
+    return p * W // P
+
+
+def owner_of(x, P, W):
+    q = min(x * P // W, P - 1)
+    while q + 1 < P and it_begin(q + 1, P, W) <= x:
+        q += 1
+    while q > 0 and it_begin(q, P, W) > x:
+        q -= 1
+    return q
+
+
+def pow2_at_least(x):
+    v = 32
+    while v < x:
+        v <<= 1
+    return v
+
+
+def plan(M, n_out, K, swiglu=False, ctas_setting=2, dp_rows=0, CG=1):
+    """tsds_tc_gemm's host arithmetic: (tiles, KT, PU, dp, stages)."""
+    npad = (M + 15) // 16 * 16
+    KT = (K + BK - 1) // BK
+    tiles = (n_out + 64 * CG - 1) // (64 * CG) if swiglu else (n_out + 128 * CG - 1) // (128 * CG)
+    tmem_cols = pow2_at_least(npad)
+    ctas = ctas_setting
+    while ctas > 1 and 2 * tmem_cols * ctas > 512:
+        ctas -= 1
+    budget = min(SMEM_PER_SM // ctas - SMEM_RESERVE, SMEM_BUDGET)
+    stages = min((budget - 1024) // (A_STAGE + npad // CG * BK * 2), MAX_STAGES)
+    W = tiles * KT
+    units = SMS * ctas // CG
+    PU = min(W, units)
+    assert W * PU < 2 ** 32
+    per_unit = -(-tiles // PU)
+    dp = dp_rows > 0 and M >= dp_rows and tiles >= PU and per_unit * PU * 20 <= tiles * 23
+    return tiles, KT, PU, dp, stages
+
+
+def ranges(tiles, KT, PU, dp):
+    W = tiles * KT
+    if dp:
+        return [((u * tiles // PU) * KT, ((u + 1) * tiles // PU) * KT) for u in range(PU)]
+    return [(it_begin(u, PU, W), it_begin(u + 1, PU, W)) for u in range(PU)]
+
+
+# (n_out, K, swiglu) of each projection: 32B q/k/v, O, gate/up, down, LM head; 4B q/k/v, gate/up, down
+PROJ = [(10240, 5120, False), (5120, 8192, False), (25600, 5120, True), (5120, 25600, False),
+        (151936, 5120, False), (6144, 2560, False), (9728, 2560, True), (2560, 9728, False)]
+
+
+@pytest.mark.parametrize("M", [1, 5, 26, 40, 208, 256])
+@pytest.mark.parametrize("n_out,K,swiglu", PROJ)
+@pytest.mark.parametrize("dp_rows", [0, 1])
+def test_every_iteration_once_and_split_tiles_as_the_epilogue_expects(M, n_out, K, swiglu, dp_rows):
+    tiles, KT, PU, dp, stages = plan(M, n_out, K, swiglu, dp_rows=dp_rows)
+    assert stages >= 2
+    rs = ranges(tiles, KT, PU, dp)
+    # the units' ranges tile the iteration space in order, none empty
+    assert rs[0][0] == 0 and rs[-1][1] == tiles * KT
+    assert all(rs[u][1] == rs[u + 1][0] for u in range(PU - 1))
+    assert all(b < e for b, e in rs)
+    for u, (b, e) in enumerate(rs):
+        split = []
+        for t in range(b // KT, (e - 1) // KT + 1):
+            tb = t * KT
+            k0, k1 = max(b, tb) - tb, min(e, tb + KT) - tb
+            if (k0, k1) != (0, KT):
+                split.append(t)
+                if not dp:   # contributors: consecutive units whose ranges cover the tile
+                    lo, hi = owner_of(tb, PU, tiles * KT), owner_of(tb + KT - 1, PU, tiles * KT)
+                    assert lo <= u <= hi
+                    assert rs[lo][0] <= tb < rs[lo][1] and rs[hi][0] <= tb + KT - 1 < rs[hi][1]
+        assert len(split) <= 2           # pend0 / pend1
+        if dp:
+            assert not split             # nothing to exchange
+
+
+@pytest.mark.parametrize("n_out,K,swiglu", PROJ)
+def test_data_parallel_only_with_whole_tiles_and_a_small_rounding_loss(n_out, K, swiglu):
+    for M in (1, 26, 208):
+        tiles, KT, PU, dp, _ = plan(M, n_out, K, swiglu, dp_rows=1)
+        if tiles < PU:
+            assert not dp
+        if dp:   # balanced to one tile, the longest unit within 15% of the mean
+            per = [e // KT - b // KT for b, e in ranges(tiles, KT, PU, True)]
+            assert min(per) >= 1 and max(per) - min(per) <= 1
+            assert max(per) <= 1.15 * tiles / PU
+        # off by default and below the row threshold
+        assert not plan(M, n_out, K, swiglu)[3]
+        assert not plan(M, n_out, K, swiglu, dp_rows=M + 1)[3]
+
+
+def test_the_large_token_count_gate_up_is_data_parallel():
+    """B=8 tree verify (M = 208): one CTA per SM (the accumulators fill TMEM),
+    400 SwiGLU tiles over 148 units - 2 or 3 whole tiles each."""
+    tiles, KT, PU, dp, stages = plan(208, 25600, 5120, True, dp_rows=128)
+    assert (tiles, KT, PU, dp) == (400, 80, 148, True)
+    per = sorted({e // KT - b // KT for b, e in ranges(tiles, KT, PU, True)})
+    assert per == [2, 3]
+    # at M = 26 (two CTAs per SM, 296 units) the 400 tiles would round up to
+    # 2 per unit against a mean of 1.35: stream-K stays
+    assert not plan(26, 25600, 5120, True, dp_rows=1)[3]
+    # the LM head at M = 208: 1187 tiles, 8 or 9 per unit
+    assert plan(208, 151936, 5120, dp_rows=128)[3]

@@ -50,6 +50,7 @@ struct TcParams {
   int stages, b_stage_bytes;
   uint32_t idesc;
   int tmem_cols;
+  int dp;  // 1: data-parallel schedule (whole tiles per unit), 0: stream-K
 };
 
 constexpr int MAX_TILES = 2048;   // tile counters; departure counters follow them
@@ -173,8 +174,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int pc = blockIdx.x;
   const int crank = CG == 2 ? (int)cluster_ctarank() : 0;
   const int unit = pc / CG, PU = p.P / CG;  // stream-K units: CTAs or CTA pairs
-  const int b = it_begin(unit, PU, p.W), e = it_begin(unit + 1, PU, p.W);
   const int KT = p.KT;
+  // stream-K: contiguous ranges of the (tile, k-block) iterations; data-parallel:
+  // whole tiles per unit (tiles >= units), so no tile is split and no partials
+  // are exchanged
+  const int b = p.dp ? (int)(((uint32_t)unit * (uint32_t)p.tiles) / (uint32_t)PU) * KT : it_begin(unit, PU, p.W);
+  const int e = p.dp ? (int)(((uint32_t)(unit + 1) * (uint32_t)p.tiles) / (uint32_t)PU) * KT
+                     : it_begin(unit + 1, PU, p.W);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -563,6 +569,9 @@ int g_num_sms = 0;
 int g_ctas_per_sm = 2;
 // Token rows from which a projection runs on CTA pairs (CG = 2); 0: never.
 int g_pair_min_rows = 0;
+// Token rows from which a projection with at least as many tiles as units
+// runs data-parallel instead of stream-K; 0: never.
+int g_dp_min_rows = 0;
 constexpr int SMEM_PER_SM = 233472;    // 228 KB
 constexpr int SMEM_RESERVE = 8192;     // static shared memory + per-CTA system reserve
 
@@ -583,6 +592,8 @@ int num_sms() {
 extern "C" void tsds_set_gemm_ctas_per_sm(int n) { g_ctas_per_sm = n < 1 ? 1 : (n > 4 ? 4 : n); }
 extern "C" void tsds_set_gemm_pair_rows(int rows) { g_pair_min_rows = rows < 0 ? 0 : rows; }
 extern "C" int tsds_get_gemm_pair_rows(void) { return g_pair_min_rows; }
+extern "C" void tsds_set_gemm_dp_rows(int rows) { g_dp_min_rows = rows < 0 ? 0 : rows; }
+extern "C" int tsds_get_gemm_dp_rows(void) { return g_dp_min_rows; }
 int tsds_tc_num_sms() { return num_sms(); }
 int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
 int tsds_tc_pair_rows() { return g_pair_min_rows; }
@@ -703,6 +714,14 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   }
   const long long PU = W64 < units ? W64 : units;
   p.P = (int)(PU * CG);
+  // data-parallel once every unit gets whole tiles and rounding the
+  // makespan up to whole tiles costs at most 15% (ceil(tiles / PU) * PU <=
+  // 1.15 tiles): no split tile's fp32 partials are then written, waited
+  // for and summed at the end of the kernel
+  const long long per_unit = (p.tiles + PU - 1) / PU;
+  p.dp = (g_dp_min_rows > 0 && M >= g_dp_min_rows && p.tiles >= PU && per_unit * PU * 20 <= (long long)p.tiles * 23)
+             ? 1
+             : 0;
   // the kernel's stream-K bookkeeping is 32-bit
   TSDS_RETURN_IF(W64 * PU >= (1ll << 32), TSDS_E_UNSUPPORTED);
   p.W = (uint32_t)W64;
