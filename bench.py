@@ -69,6 +69,9 @@ def _args():
     ap.add_argument("--dp-rows", type=int, default=None,
                     help="token rows from which a tcgen05 projection with at least one whole weight tile per CTA "
                          "runs data-parallel instead of stream-K (library default 0: never)")
+    ap.add_argument("--dp-slack", type=int, default=None,
+                    help="largest makespan increase (percent) the data-parallel schedule may cost over the ideal "
+                         "(library default 15; above 100 it may leave CTAs idle for fewer tiles than CTAs)")
     ap.add_argument("--pair-rows", type=int, default=None,
                     help="token rows from which the tcgen05 GEMM runs on CTA pairs (library default 0: never)")
     ap.add_argument("--breakdown", type=int, default=0, metavar="CYCLES",
@@ -443,6 +446,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
     if a.dp_rows is not None:
         _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
+    if a.dp_slack is not None:
+        _lib.load().tsds_set_gemm_dp_slack(a.dp_slack)
     if a.attn_tc:
         _lib.load().tsds_set_attention_tc(a.attn_tc)
     tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
@@ -624,6 +629,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
             "gemm_dp_rows": _lib.load().tsds_get_gemm_dp_rows(),
+            "gemm_dp_slack": _lib.load().tsds_get_gemm_dp_slack(),
             "attention": {"tcgen05": _lib.load().tsds_get_attention_tc(), "split_keys": a.attn_split},
         }
         if breakdown is not None:
@@ -664,6 +670,8 @@ def main():
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
             if a.dp_rows is not None:
                 _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
+            if a.dp_slack is not None:
+                _lib.load().tsds_set_gemm_dp_slack(a.dp_slack)
             if a.attn_tc:
                 _lib.load().tsds_set_attention_tc(a.attn_tc)
             (run_attention if a.mode == "attention" else run_layer)(a)

@@ -136,15 +136,19 @@ void tsds_set_gemm_ctas_per_sm(int n);
  * switch for large M. */
 void tsds_set_gemm_pair_rows(int rows);
 int tsds_get_gemm_pair_rows(void);
-/* Token rows M from which a tcgen05 projection runs data-parallel - whole
- * weight tiles per CTA (or CTA pair), no split tiles and so no fp32
- * partials exchanged at the end - instead of stream-K, where every CTA gets
- * at least one tile and rounding up to whole tiles costs at most 15%;
- * 0 (default): always stream-K.  Process-wide tuning
- * switch for large M.  The two schedules sum a split tile in a different
- * order, so results may differ in the last bit between them. */
+/* Token rows M from which a tcgen05 projection may run data-parallel -
+ * min(tiles, CTAs) CTAs (or CTA pairs) take whole weight tiles, no split
+ * tiles and so no fp32 partials exchanged at the end - instead of
+ * stream-K; 0 (default): always stream-K.  It is chosen where its makespan,
+ * ceil(tiles / used CTAs) tiles, exceeds the ideal tiles / CTAs by at most
+ * tsds_set_gemm_dp_slack percent (default 15; with fewer tiles than CTAs
+ * that allows leaving CTAs idle).  Process-wide tuning switches for large
+ * M.  The two schedules sum a split tile in a different order, so results
+ * may differ in the last bit between them. */
 void tsds_set_gemm_dp_rows(int rows);
 int tsds_get_gemm_dp_rows(void);
+void tsds_set_gemm_dp_slack(int percent);
+int tsds_get_gemm_dp_slack(void);
 int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                 void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,

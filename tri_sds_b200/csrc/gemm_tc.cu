@@ -572,6 +572,9 @@ int g_pair_min_rows = 0;
 // Token rows from which a projection with at least as many tiles as units
 // runs data-parallel instead of stream-K; 0: never.
 int g_dp_min_rows = 0;
+// Largest makespan increase (percent over the ideal tiles / units) the
+// data-parallel schedule may cost.
+int g_dp_slack_pct = 15;
 constexpr int SMEM_PER_SM = 233472;    // 228 KB
 constexpr int SMEM_RESERVE = 8192;     // static shared memory + per-CTA system reserve
 
@@ -594,6 +597,10 @@ extern "C" void tsds_set_gemm_pair_rows(int rows) { g_pair_min_rows = rows < 0 ?
 extern "C" int tsds_get_gemm_pair_rows(void) { return g_pair_min_rows; }
 extern "C" void tsds_set_gemm_dp_rows(int rows) { g_dp_min_rows = rows < 0 ? 0 : rows; }
 extern "C" int tsds_get_gemm_dp_rows(void) { return g_dp_min_rows; }
+extern "C" void tsds_set_gemm_dp_slack(int percent) {
+  g_dp_slack_pct = percent < 0 ? 0 : (percent > 1000 ? 1000 : percent);
+}
+extern "C" int tsds_get_gemm_dp_slack(void) { return g_dp_slack_pct; }
 int tsds_tc_num_sms() { return num_sms(); }
 int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
 int tsds_tc_pair_rows() { return g_pair_min_rows; }
@@ -712,16 +719,22 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
     TSDS_RETURN_IF(resident < 1, TSDS_E_UNSUPPORTED);
     if (resident < units) units = resident;
   }
-  const long long PU = W64 < units ? W64 : units;
+  long long PU = W64 < units ? W64 : units;
+  // Data-parallel: min(tiles, units) units take whole tiles, so no split
+  // tile's fp32 partials are written, waited for and summed at the end of
+  // the kernel.  Its makespan is ceil(tiles / PU) tiles against the ideal
+  // tiles / units; it is chosen when that costs at most g_dp_slack_pct
+  // percent more (fewer tiles than units: when tiles / units >= 1 / (1 + slack)).
+  p.dp = 0;
+  if (g_dp_min_rows > 0 && M >= g_dp_min_rows) {
+    const long long pu = p.tiles < units ? p.tiles : units;
+    const long long per_unit = (p.tiles + pu - 1) / pu;
+    if (per_unit * units * 100 <= (long long)p.tiles * (100 + g_dp_slack_pct)) {
+      p.dp = 1;
+      PU = pu;
+    }
+  }
   p.P = (int)(PU * CG);
-  // data-parallel once every unit gets whole tiles and rounding the
-  // makespan up to whole tiles costs at most 15% (ceil(tiles / PU) * PU <=
-  // 1.15 tiles): no split tile's fp32 partials are then written, waited
-  // for and summed at the end of the kernel
-  const long long per_unit = (p.tiles + PU - 1) / PU;
-  p.dp = (g_dp_min_rows > 0 && M >= g_dp_min_rows && p.tiles >= PU && per_unit * PU * 20 <= (long long)p.tiles * 23)
-             ? 1
-             : 0;
   // the kernel's stream-K bookkeeping is 32-bit
   TSDS_RETURN_IF(W64 * PU >= (1ll << 32), TSDS_E_UNSUPPORTED);
   p.W = (uint32_t)W64;
