@@ -7,7 +7,10 @@
  * The caller owns every buffer, including the workspace some entry points
  * take (query its size with the matching *_workspace_bytes function).
  * Calls on different streams with different workspaces may run
- * concurrently; calls that share a workspace must be ordered.
+ * concurrently, also from several host threads (the library's host-side
+ * caches are thread-safe); calls that share a workspace must be ordered.
+ * The tsds_set_* tuning switches are process-wide and apply to calls made
+ * after them.
  *
  * Element types: bf16 buffers are "const void*" / "void*" holding
  * __nv_bfloat16; token ids are int64 (torch.long); lengths, positions and

@@ -825,13 +825,13 @@ constexpr size_t atc_smem_bytes() { return 1024 + 3 * (size_t)ATC_REGION + (size
 
 // Process-wide switch for the tcgen05 variant (off by default; 2: with the
 // clustered combine where the split count allows).
-int g_attn_tc = 0;
+std::atomic<int> g_attn_tc{0};
 
 // Whether clusters of n tcgen05-attention CTAs (a whole SM's shared memory
 // each) can be resident; cached per n.
 bool atc_clusters_fit(int n) {
-  static int known[ATC_MAX_CLUSTER + 1] = {};  // 0 unknown, 1 yes, 2 no
-  if (known[n] == 0) {
+  static std::atomic<int> known[ATC_MAX_CLUSTER + 1];  // 0 unknown, 1 yes, 2 no
+  if (known[n].load(std::memory_order_acquire) == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n);
     cfg.blockDim = dim3(ATC_THREADS);
@@ -848,9 +848,9 @@ bool atc_clusters_fit(int n) {
       cudaGetLastError();
       clusters = 0;
     }
-    known[n] = clusters > 0 ? 1 : 2;
+    known[n].store(clusters > 0 ? 1 : 2, std::memory_order_release);
   }
-  return known[n] == 1;
+  return known[n].load(std::memory_order_acquire) == 1;
 }
 
 }  // namespace
@@ -930,7 +930,7 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
     if (st != TSDS_OK) return st;
     st = tsds_make_tmap_2d_bf16(&vmap, v_cache, D, rows, D * 2, 64, ATC_TILE, 1);
     if (st != TSDS_OK) return st;
-    static bool tc_attr[TSDS_MAX_DEVICES] = {};
+    static tsds_device_flags tc_attr;
     st = tsds_smem_limit_once(verify_attn_tc_kernel, (int)atc_smem_bytes(), tc_attr);
     if (st != TSDS_OK) return st;
     if (g_attn_tc == 2 && nsplit >= 2 && nsplit <= ATC_MAX_CLUSTER && atc_clusters_fit(nsplit)) {
@@ -949,7 +949,7 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   }
 
   const size_t smem = attn_smem_bytes();
-  static bool attr_set[TSDS_MAX_DEVICES] = {};
+  static tsds_device_flags attr_set;
   st = tsds_smem_limit_once(verify_attn_kernel<kStages>, (int)smem, attr_set);
   if (st != TSDS_OK) return st;
   dim3 grid(nsplit * nrb, Hkv, B);
@@ -990,7 +990,7 @@ constexpr int kNoAllocMaxDevices = 64;
 }  // namespace
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocHeader + kNoAllocScratch];
-static void* g_attn_noalloc_addr[kNoAllocMaxDevices];
+static std::atomic<void*> g_attn_noalloc_addr[kNoAllocMaxDevices];
 
 static int attn_noalloc_base(void** out) {
   int dev = 0;
@@ -999,16 +999,16 @@ static int attn_noalloc_base(void** out) {
     return TSDS_E_DEVICE;
   }
   if (dev < 0 || dev >= kNoAllocMaxDevices) return TSDS_E_DEVICE;
-  if (g_attn_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
+  void* p = g_attn_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {  // two threads may both look it up: the same address
     const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
       cudaGetLastError();
       return TSDS_E_DEVICE;
     }
-    g_attn_noalloc_addr[dev] = p;
+    g_attn_noalloc_addr[dev].store(p, std::memory_order_release);
   }
-  *out = g_attn_noalloc_addr[dev];
+  *out = p;
   return TSDS_OK;
 }
 

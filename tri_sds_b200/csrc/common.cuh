@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "../../include/tsds.h"
@@ -29,22 +31,30 @@ static inline int tsds_launch_status() {
 
 static inline bool tsds_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Host-side state of the library is safe under calls from several host
+// threads at once (the ABI allows concurrent calls on different streams):
+// per-device "done" records are atomics, and the small lookup caches of
+// occupancy results take this process-wide lock.
+std::mutex& tsds_host_cache_lock();
+
 // Raise a kernel's dynamic shared-memory limit on the current device, once per
 // device (the attribute is per device): `done` is the caller's per-kernel record.
+// Two threads may both set it the first time; the attribute is the same.
 constexpr int TSDS_MAX_DEVICES = 64;
+typedef std::atomic<bool> tsds_device_flags[TSDS_MAX_DEVICES];
 template <typename Kernel>
-static inline int tsds_smem_limit_once(Kernel kernel, int bytes, bool (&done)[TSDS_MAX_DEVICES]) {
+static inline int tsds_smem_limit_once(Kernel kernel, int bytes, tsds_device_flags& done) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= TSDS_MAX_DEVICES) {
     cudaGetLastError();
     return TSDS_E_DEVICE;
   }
-  if (!done[dev]) {
+  if (!done[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
       cudaGetLastError();
       return TSDS_E_LAUNCH;
     }
-    done[dev] = true;
+    done[dev].store(true, std::memory_order_release);
   }
   return TSDS_OK;
 }

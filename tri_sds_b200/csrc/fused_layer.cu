@@ -836,6 +836,7 @@ int resident_ctas(int CG, size_t smem) {
   static int vals[16];
   static int n = 0;
   const size_t key = smem * 2 + (CG == 2);
+  std::lock_guard<std::mutex> hold(tsds_host_cache_lock());
   for (int i = 0; i < n; ++i)
     if (keys[i] == key) return vals[i];
   int ctas = 0;
@@ -1030,7 +1031,7 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     if (st != TSDS_OK) return st;
   }
   {
-    static bool attr1[TSDS_MAX_DEVICES] = {}, attr2[TSDS_MAX_DEVICES] = {};
+    static tsds_device_flags attr1, attr2;
     const int st = CG == 2 ? tsds_smem_limit_once(fused_layer_kernel<2>, CH_SMEM_BUDGET, attr2)
                            : tsds_smem_limit_once(fused_layer_kernel<1>, CH_SMEM_BUDGET, attr1);
     if (st != TSDS_OK) return st;

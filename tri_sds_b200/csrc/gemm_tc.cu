@@ -561,33 +561,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   }
 }
 
-int g_num_sms = 0;
+std::atomic<int> g_num_sms{0};
 // CTAs per SM: two CTAs with half the pipeline each keep more weight bytes in
 // flight per SM than one CTA with a deep pipeline (measured on B200: 6.3 vs
 // 5.5 TB/s for the bare TMA stream).  Capped so both fit in TMEM (512
 // columns) and shared memory.
-int g_ctas_per_sm = 2;
+std::atomic<int> g_ctas_per_sm{2};
 // Token rows from which a projection runs on CTA pairs (CG = 2); 0: never.
-int g_pair_min_rows = 0;
-// Token rows from which a projection with at least as many tiles as units
-// runs data-parallel instead of stream-K; 0: never.
-int g_dp_min_rows = 0;
+std::atomic<int> g_pair_min_rows{0};
+// Token rows from which a projection may run data-parallel instead of
+// stream-K (when within the slack below); 0: never.
+std::atomic<int> g_dp_min_rows{0};
 // Largest makespan increase (percent over the ideal tiles / units) the
 // data-parallel schedule may cost.
-int g_dp_slack_pct = 15;
+std::atomic<int> g_dp_slack_pct{15};
 constexpr int SMEM_PER_SM = 233472;    // 228 KB
 constexpr int SMEM_RESERVE = 8192;     // static shared memory + per-CTA system reserve
 
 int num_sms() {
-  if (g_num_sms == 0) {
+  int n = g_num_sms.load(std::memory_order_relaxed);
+  if (n == 0) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
       cudaGetLastError();
-      g_num_sms = 148;
+      n = 148;
     }
+    g_num_sms.store(n, std::memory_order_relaxed);
   }
-  return g_num_sms;
+  return n;
 }
 
 }  // namespace
@@ -609,7 +610,7 @@ namespace {
 
 template <int EPI, int CG>
 int launch_tc(const CUtensorMap& amap, const CUtensorMap& bmap, const TcParams& p, size_t smem, cudaStream_t stream) {
-  static bool attr[TSDS_MAX_DEVICES] = {};
+  static tsds_device_flags attr;
   const int st = tsds_smem_limit_once(tc_gemm_kernel<EPI, CG>, SMEM_BUDGET, attr);
   if (st != TSDS_OK) return st;
   if constexpr (CG == 2)
@@ -635,9 +636,10 @@ int max_pair_clusters(size_t smem) {
   static size_t keys[16];
   static int vals[16];
   static int n = 0;
+  std::lock_guard<std::mutex> hold(tsds_host_cache_lock());
   for (int i = 0; i < n; ++i)
     if (keys[i] == smem) return vals[i];
-  static bool attr[TSDS_MAX_DEVICES] = {};
+  static tsds_device_flags attr;
   if (tsds_smem_limit_once(tc_gemm_kernel<EPI, 2>, SMEM_BUDGET, attr) != TSDS_OK) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2);

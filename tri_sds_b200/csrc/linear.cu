@@ -12,7 +12,7 @@ int check_linear(const void* x, int ldx, const void* W, const void* out, int ldo
 
 // Measured on B200: the TMA-fed tcgen05 GEMM streams weights faster than the
 // CUDA-core GEMV even at M = 1, so the GEMV is opt-in (tsds_set_gemv_max_rows).
-int g_gemv_max_rows = 0;
+std::atomic<int> g_gemv_max_rows{0};
 
 int run_linear(int epi, const void* x, int ldx, const void* W, const void* res, int res_ld, void* out, int ldo, int M,
                int n_out, int K, void* workspace, size_t workspace_bytes, cudaStream_t stream) {

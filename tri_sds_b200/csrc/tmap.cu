@@ -3,32 +3,41 @@
 
 #include "common.cuh"
 
-static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::mutex& tsds_host_cache_lock() {
+  static std::mutex m;
+  return m;
+}
 
-static int load_encode_tiled() {
-  if (g_encode_tiled) return TSDS_OK;
+// The driver's tensor-map encoder, looked up once (any thread may be first;
+// a second lookup finds the same entry point).
+static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode_tiled{nullptr};
+
+static PFN_cuTensorMapEncodeTiled_v12000 load_encode_tiled() {
+  PFN_cuTensorMapEncodeTiled_v12000 f = g_encode_tiled.load(std::memory_order_acquire);
+  if (f) return f;
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q;
   if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
       q != cudaDriverEntryPointSuccess || fn == nullptr) {
     cudaGetLastError();
-    return TSDS_E_DEVICE;
+    return nullptr;
   }
-  g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return TSDS_OK;
+  f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  g_encode_tiled.store(f, std::memory_order_release);
+  return f;
 }
 
 int tsds_make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                            uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                            int swizzle_128b) {
-  int st = load_encode_tiled();
-  if (st != TSDS_OK) return st;
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = load_encode_tiled();
+  if (!encode) return TSDS_E_DEVICE;
   if (!tsds_aligned16(base) || (row_stride_bytes % 16) != 0) return TSDS_E_ALIGN;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               swizzle_128b ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -53,11 +62,10 @@ extern "C" const char* tsds_status_string(int status) {
 
 extern "C" int tsds_abi_version(void) { return 1; }
 
-#include <atomic>
 static std::atomic<long long> g_launches{0};
 void tsds_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 extern "C" int64_t tsds_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-static int g_pdl = 1;
+static std::atomic<int> g_pdl{1};
 int tsds_pdl_enabled() { return g_pdl; }
 extern "C" void tsds_set_pdl(int on) { g_pdl = on ? 1 : 0; }

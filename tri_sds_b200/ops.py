@@ -12,6 +12,9 @@ Reference op (file:line)                                 -> here
 
 Like the reference wrappers these allocate their outputs with torch and
 launch on torch's current stream; errors raise (the reference asserts).
+The ops share one scratch workspace per device and op kind.  Calls that
+could overlap on the GPU (ops on different streams) must therefore not
+run at the same time.  The engines give every model workspaces of its own.
 Every op runs the sm_100a kernels of libtsds.so; there is no other path.
 Weights may be given in the reference's transposed ``[in, out]`` layout
 (``*_w_t`` arguments) or as the transposed view of an HF ``[out, in]``
