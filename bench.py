@@ -90,6 +90,8 @@ def _args():
                          "library default 0: off)")
     ap.add_argument("--attn-split", type=int, default=128,
                     help="keys per attention split of the target / draft (a multiple of 64; of 128 for --attn-tc)")
+    ap.add_argument("--gemv-splitk", action="store_true",
+                    help="the GEMV path (rows up to --gemv-max-rows) as its split-K variant")
     ap.add_argument("--gemv-max-rows", type=int, default=None,
                     help="rows up to which the CUDA-core GEMV runs instead of tcgen05 (library default 0)")
     return ap.parse_args()
@@ -438,6 +440,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     B, K, P = a.batch, a.k, a.prompt
     if a.gemv_max_rows is not None:
         _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
+    if a.gemv_splitk:
+        _lib.load().tsds_set_gemv_splitk(1)
     if a.ctas_per_sm is not None:
         _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
     if a.no_pdl:
@@ -627,6 +631,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_cycle * a.steps,
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
+            "gemv_splitk": _lib.load().tsds_get_gemv_splitk(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
             "gemm_dp_rows": _lib.load().tsds_get_gemm_dp_rows(),
             "gemm_dp_slack": _lib.load().tsds_get_gemm_dp_slack(),

@@ -130,6 +130,12 @@ size_t tsds_linear_workspace_bytes(int M, int n_out, int K);
  * *_workspace_bytes functions too. */
 void tsds_set_gemv_max_rows(int rows);
 int tsds_get_gemv_max_rows(void);
+/* 1: the GEMV path runs its split-K variant - a CTA per few weight rows,
+ * all its threads sweeping K, partials summed across the CTA's warps in a
+ * fixed order - so even the narrowest projections cover every SM; 0
+ * (default): one warp per weight rows.  Process-wide tuning switch. */
+void tsds_set_gemv_splitk(int on);
+int tsds_get_gemv_splitk(void);
 /* Resident CTAs per SM of the tcgen05 GEMM (1..4, default 2; lowered
  * automatically when the accumulators would not fit in TMEM).  Tuning knob. */
 void tsds_set_gemm_ctas_per_sm(int n);

@@ -53,6 +53,8 @@ SIGNATURES = {
     "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "tsds_set_gemv_max_rows": (None, [_I]),
     "tsds_get_gemv_max_rows": (_I, []),
+    "tsds_set_gemv_splitk": (None, [_I]),
+    "tsds_get_gemv_splitk": (_I, []),
     "tsds_set_gemm_ctas_per_sm": (None, [_I]),
     "tsds_set_gemm_pair_rows": (None, [_I]),
     "tsds_get_gemm_pair_rows": (_I, []),
