@@ -52,10 +52,13 @@ def _args():
     ap.add_argument("--impl", default="tsds", choices=["tsds", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--k", type=int, default=4)
-    ap.add_argument("--mode", default="eagle", choices=["eagle", "chain", "attention", "layer"],
+    ap.add_argument("--mode", default="eagle", choices=["eagle", "chain", "attention", "layer", "gemm"],
                     help="eagle / chain: the spec-decode cycle; attention: verify attention alone over a "
                          "--kv-len cache (B x (K+1) queries, 32B heads); layer: Qwen3-4B-shape decoder layers "
-                         "alone over B x (K+1) rows")
+                         "alone over B x (K+1) rows; gemm: each projection of a layer alone over --rows rows, "
+                         "back to back over several layers' weights")
+    ap.add_argument("--rows", type=int, default=26, help="gemm mode: token rows M")
+    ap.add_argument("--shape", default="32b", choices=["32b", "4b"], help="gemm mode: Qwen3-32B or -4B shape")
     ap.add_argument("--kv-len", type=int, default=4096, help="attention mode: keys per sequence")
     ap.add_argument("--greedy", action="store_true", help="eagle mode: greedy acceptance instead of sampling")
     ap.add_argument("--prompt", type=int, default=512)
@@ -258,7 +261,7 @@ def run_reference(a, rank: int, world: int):
     """--impl reference: the reference's CPU path (oracle port), rank 0 only."""
     if rank != 0:
         return
-    if a.mode in ("attention", "layer"):
+    if a.mode in ("attention", "layer", "gemm"):
         print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the spec-decode cycle "
                                                               "(--mode eagle / chain)"}), flush=True)
         return
@@ -421,6 +424,83 @@ def run_layer(a):
                          "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": wbytes,
                          "launch_us": us_layer},
             "clocks": clocks, "gpu_launches": launches * max(1, a.steps)}
+    print(json.dumps(line), flush=True)
+
+
+def run_gemm(a):
+    """--mode gemm: every projection of one decoder layer (q/k/v, O + residual,
+    gate/up + SwiGLU, down + residual) alone at M = --rows token rows, each
+    timed with CUDA events over back-to-back launches across the weights of
+    enough layers to exceed L2 several times (so every launch streams its
+    weights from HBM).  One JSON line: per projection the µs per launch and
+    its algorithmic bytes against the measured HBM peak, and the layer's sum.
+    The library's tuning switches (GEMV rows / split-K, CTA pairs,
+    data-parallel rows and slack) apply as set on the command line."""
+    import torch
+    from tri_sds_b200 import _lib, ops
+    from tri_sds_b200.shapes import QWEN3_4B, QWEN3_32B
+    dev = torch.device("cuda", 0)
+    sh = QWEN3_32B if a.shape == "32b" else QWEN3_4B
+    M, N, I = a.rows, sh.hidden, sh.intermediate
+    qd, kvd = sh.n_heads * sh.head_dim, sh.n_kv_heads * sh.head_dim
+    per_layer = 2 * N * (qd + 2 * kvd + qd + 2 * I + I)
+    nl = max(4, -(-(4 * 126 * 2 ** 20) // per_layer))   # > 4 x L2 of weights
+    g = torch.Generator(device=dev).manual_seed(3)
+
+    def w(rows, cols):
+        return (0.02 * torch.randn(rows, cols, device=dev, generator=g)).to(torch.bfloat16)
+    layers = [dict(qkv=w(qd + 2 * kvd, N), o=w(N, qd), gu=w(2 * I, N), d=w(N, I)) for _ in range(nl)]
+    x_n = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    x_q = torch.randn(M, qd, device=dev, generator=g).to(torch.bfloat16)
+    x_i = torch.randn(M, I, device=dev, generator=g).to(torch.bfloat16)
+    res = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+    o_qkv = torch.empty(M, qd + 2 * kvd, dtype=torch.bfloat16, device=dev)
+    o_n = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    o_i = torch.empty(M, I, dtype=torch.bfloat16, device=dev)
+    projs = {
+        "qkv": (lambda L: ops.linear(x_n, L["qkv"], out=o_qkv), (qd + 2 * kvd) * N, N, qd + 2 * kvd),
+        "o": (lambda L: ops.linear_residual(x_q, L["o"], res, out=o_n), N * qd, qd, N),
+        "gate_up": (lambda L: ops.linear_swiglu(x_n, L["gu"], out=o_i), 2 * I * N, N, I),
+        "down": (lambda L: ops.linear_residual(x_i, L["d"], res, out=o_n), N * I, I, N),
+    }
+    peak, peak_kind = _peaks()
+    reps = max(1, a.steps)
+    lc0 = _lib.query("tsds_launch_count")
+    out, tot_b, tot_us = {}, 0, 0.0
+    for name, (fn, wel, kin, kout) in projs.items():
+        for L in layers[:3]:
+            fn(L)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for L in layers:
+                fn(L)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * nl)
+        nbytes = 2 * wel + 2 * M * (kin + kout) + (2 * M * kout if name in ("o", "down") else 0)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 2), "bytes": nbytes, "gb_s": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        tot_b += nbytes
+        tot_us += us
+    launches = _lib.query("tsds_launch_count") - lc0
+    layer_gbs = tot_b / (tot_us * 1e-6) / 1e9
+    lib = _lib.load()
+    line = {"metric": "decode-layer projections GB/s", "value": layer_gbs, "unit": "GB/s", "n_gpus": 1,
+            "steps": reps, "warmup": 3, "ms_per_step": tot_us / 1e3, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random N(0,0.02) weights, N(0,1) activations",
+            "config": {"workload": f"Qwen3-{a.shape.upper()}-shape projections of one layer at M={M} rows",
+                       "rows": M, "layers_rotated": nl,
+                       "l2": f"no flush: {nl} layers' weights ({nl * per_layer / 2**30:.1f} GiB) rotate, > 4 x L2",
+                       "gemv_max_rows": lib.tsds_get_gemv_max_rows(), "gemv_splitk": lib.tsds_get_gemv_splitk(),
+                       "gemm_pair_rows": lib.tsds_get_gemm_pair_rows(), "gemm_dp_rows": lib.tsds_get_gemm_dp_rows(),
+                       "gemm_dp_slack": lib.tsds_get_gemm_dp_slack()},
+            "projections": out,
+            "roofline": {"bound": "hbm", "achieved": layer_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": layer_gbs / peak, "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_launch": tot_b, "launch_us": tot_us},
+            "gpu_launches": launches}
     print(json.dumps(line), flush=True)
 
 
@@ -667,9 +747,9 @@ def main():
     try:
         if a.impl == "reference":
             run_reference(a, rank, world)
-        elif a.mode in ("attention", "layer"):
+        elif a.mode in ("attention", "layer", "gemm"):
             if world > 1:
-                raise SystemExit("--mode attention / layer run on one GPU")
+                raise SystemExit("--mode attention / layer / gemm run on one GPU")
             from tri_sds_b200 import _lib
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
@@ -679,7 +759,11 @@ def main():
                 _lib.load().tsds_set_gemm_dp_slack(a.dp_slack)
             if a.attn_tc:
                 _lib.load().tsds_set_attention_tc(a.attn_tc)
-            (run_attention if a.mode == "attention" else run_layer)(a)
+            if a.gemv_max_rows is not None:
+                _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
+            if a.gemv_splitk:
+                _lib.load().tsds_set_gemv_splitk(1)
+            {"attention": run_attention, "layer": run_layer, "gemm": run_gemm}[a.mode](a)
         else:
             run_tsds(a, rank, world, local_rank)
     except BaseException:
