@@ -43,6 +43,22 @@ def owner_of(x, P, W):
     return q
 
 
+def unit_range(ph, unit, units, split):
+    """(b, e), Pf of a unit in a GEMM phase ("gemm", W, KT, dist[, dp]):
+    stream-K over Pf = split(W, units) units, or - data-parallel phases
+    (fused_layer.cu phase_range() with ph.dp) - whole tiles over
+    Pf = min(tiles, units) units."""
+    W, KT = ph[1], ph[2]
+    if len(ph) > 4 and ph[4]:
+        tiles = W // KT
+        pf = min(tiles, units)
+        if unit >= pf:
+            return (0, 0), pf
+        return ((unit * tiles // pf) * KT, ((unit + 1) * tiles // pf) * KT), pf
+    pf = split(W, units)
+    return phase_range(unit, pf, W), pf
+
+
 class Rank:
     def __init__(self, P):
         self.gbar = 0
@@ -92,7 +108,7 @@ def run(phases, P, stages, R, seed, split=phase_ctas, CG=1):
             if ph[0] != "gemm":
                 continue
             W, KT = ph[1], ph[2]
-            b, e = phase_range(unit, split(W, units), W)
+            (b, e), _ = unit_range(ph, unit, units, split)
             if b >= e:
                 continue
             npre = min(e - b, stages)
@@ -129,7 +145,7 @@ def run(phases, P, stages, R, seed, split=phase_ctas, CG=1):
             if ph[0] != "gemm":
                 continue
             W, KT = ph[1], ph[2]
-            b, e = phase_range(unit, split(W, units), W)
+            (b, e), _ = unit_range(ph, unit, units, split)
             if b >= e:
                 continue
             for t in range(b // KT, (e - 1) // KT + 1):
@@ -167,8 +183,7 @@ def run(phases, P, stages, R, seed, split=phase_ctas, CG=1):
                         assert len(ranks[q].phase_done[f - 1]) == P, "peer read before a rank's partials"
             elif ph[0] == "gemm":
                 W, KT, dist = ph[1], ph[2], ph[3]
-                Pf = split(W, units)
-                b, e = phase_range(unit, Pf, W)
+                (b, e), Pf = unit_range(ph, unit, units, split)
                 pend = []
                 if b < e:
                     for t in range(b // KT, (e - 1) // KT + 1):
@@ -268,6 +283,25 @@ def test_fewer_iterations_than_ctas(seed):
 
 
 SMALL_PHASES = [("gemm", 4, 2, True), ("norm",), ("gemm", 3, 3, False), ("gemm", 6, 2, True)]
+
+
+# the layer with its GEMM phases data-parallel (whole tiles per unit; fewer
+# tiles than units in some, so units sit phases out)
+LAYER_DP = [("gemm", 5 * 4, 4, True, True), ("norm",), ("gemm", 9 * 4, 4, False, True),
+            ("gemm", 5 * 6, 6, True, False), ("norm",), ("gemm", 6 * 4, 4, False, True)]
+
+
+@pytest.mark.parametrize("P,stages", [(3, 2), (6, 3), (7, 5), (12, 2)])
+@pytest.mark.parametrize("seed", range(3))
+def test_data_parallel_phases_never_deadlock(P, stages, seed):
+    """Data-parallel GEMM phases (no split tiles, no counters) mixed with
+    stream-K ones, on single CTAs, CTA pairs and two ranks."""
+    run(LAYER_DP, P, stages, R=1, seed=seed)
+    if P % 2 == 0:
+        run(LAYER_DP, P, stages, R=1, seed=seed, CG=2)
+    tp = [ph for ph in LAYER_DP]
+    tp.insert(1, ("peer",))
+    run(tp, P, stages, R=2, seed=seed)
 
 
 def test_splitting_over_every_cta_deadlocks_small_phases():

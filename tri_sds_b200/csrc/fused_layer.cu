@@ -60,6 +60,7 @@ struct ChPhase {
   uint32_t W;                  // tiles x KT (host: W * P < 2^32)
   int up_off, ldo, res_ld, ctr;  // ctr: arrival counters at counters[ctr], departures at + tiles
   int Pf;                        // units sharing this phase's iterations: min(W, units), so each owns one or more
+  int dp;                        // 1: data-parallel (whole tiles per unit, Pf = min(tiles, units)), 0: stream-K
   const bf16* res;
   bf16* out;
   // NORM: out[m][0:n] (ldo) = RMSNorm(x[m][0:n]) * w
@@ -138,11 +139,17 @@ __device__ __forceinline__ bool wait_count(const int* c, int target) {
 // async-proxy (TMA) reads of the same global memory
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// A unit's stream-K range of a GEMM phase (a unit is a CTA, or a CTA pair
-// when CG = 2): units 0..Pf-1 split its W iterations, every one of them
-// owning at least one (so the contributors of a split tile are consecutive
-// units); units from Pf on sit the phase out.
+// A unit's range of a GEMM phase (a unit is a CTA, or a CTA pair when
+// CG = 2): units 0..Pf-1 split its W iterations, every one of them owning at
+// least one (so the contributors of a split tile are consecutive units);
+// units from Pf on sit the phase out.  Data-parallel phases (the schedule of
+// gemm_tc.cu's tsds_set_gemm_dp_rows) hand out whole tiles instead.
 __device__ __forceinline__ void phase_range(const ChPhase& ph, int unit, int& b, int& e) {
+  if (ph.dp) {
+    b = unit < ph.Pf ? (int)(((uint32_t)unit * (uint32_t)ph.tiles) / (uint32_t)ph.Pf) * ph.KT : 0;
+    e = unit < ph.Pf ? (int)(((uint32_t)(unit + 1) * (uint32_t)ph.tiles) / (uint32_t)ph.Pf) * ph.KT : 0;
+    return;
+  }
   b = unit < ph.Pf ? it_begin(unit, ph.Pf, ph.W) : 0;
   e = unit < ph.Pf ? it_begin(unit + 1, ph.Pf, ph.W) : 0;
 }
@@ -1039,8 +1046,16 @@ extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, in
     TSDS_RETURN_IF(resident < CG, TSDS_E_UNSUPPORTED);
     if (resident < p.P) p.P = resident;
   }
-  for (int f = 0; f < n_phases; ++f)
-    if (p.ph[f].kind == CH_GEMM && p.ph[f].Pf > p.P / CG) p.ph[f].Pf = p.P / CG;
+  for (int f = 0; f < n_phases; ++f) {
+    ChPhase& ph = p.ph[f];
+    if (ph.kind != CH_GEMM) continue;
+    const int units = p.P / CG;
+    if (ph.Pf > units) ph.Pf = units;
+    // the data-parallel choice of tsds_tc_gemm, on the resident units
+    const int dp_units = tsds_tc_dp_units(M, ph.tiles, units);
+    ph.dp = dp_units > 0 ? 1 : 0;
+    if (ph.dp) ph.Pf = dp_units;
+  }
   if (CG == 2)
     tsds_launch_cluster(fused_layer_kernel<2>, dim3(p.P), dim3(CH_THREADS), smem, stream, 2, maps, p);
   else

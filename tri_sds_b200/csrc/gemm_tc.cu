@@ -603,6 +603,22 @@ extern "C" void tsds_set_gemm_dp_slack(int percent) {
 }
 extern "C" int tsds_get_gemm_dp_slack(void) { return g_dp_slack_pct; }
 int tsds_tc_num_sms() { return num_sms(); }
+
+// Data-parallel: min(tiles, units) units take whole tiles, so no split
+// tile's fp32 partials are written, waited for and summed at the end of the
+// kernel.  Its makespan is ceil(tiles / used units) tiles against the ideal
+// tiles / units; it is chosen when that costs at most g_dp_slack_pct percent
+// more (with fewer tiles than units: when tiles / units >= 1 / (1 + slack)).
+// Returns the units to use data-parallel, or 0 for stream-K.
+int tsds_tc_dp_units(int M, int tiles, int units) {
+  const int rows = g_dp_min_rows.load(std::memory_order_relaxed);
+  if (rows <= 0 || M < rows || tiles <= 0 || units <= 0) return 0;
+  const long long pu = tiles < units ? tiles : units;
+  const long long per_unit = (tiles + pu - 1) / pu;
+  return per_unit * units * 100 <= (long long)tiles * (100 + g_dp_slack_pct.load(std::memory_order_relaxed))
+             ? (int)pu
+             : 0;
+}
 int tsds_tc_ctas_setting() { return g_ctas_per_sm; }
 int tsds_tc_pair_rows() { return g_pair_min_rows; }
 
@@ -727,15 +743,9 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   // the kernel.  Its makespan is ceil(tiles / PU) tiles against the ideal
   // tiles / units; it is chosen when that costs at most g_dp_slack_pct
   // percent more (fewer tiles than units: when tiles / units >= 1 / (1 + slack)).
-  p.dp = 0;
-  if (g_dp_min_rows > 0 && M >= g_dp_min_rows) {
-    const long long pu = p.tiles < units ? p.tiles : units;
-    const long long per_unit = (p.tiles + pu - 1) / pu;
-    if (per_unit * units * 100 <= (long long)p.tiles * (100 + g_dp_slack_pct)) {
-      p.dp = 1;
-      PU = pu;
-    }
-  }
+  const int dp_units = tsds_tc_dp_units(M, p.tiles, (int)units);
+  p.dp = dp_units > 0 ? 1 : 0;
+  if (p.dp) PU = dp_units;
   p.P = (int)(PU * CG);
   // the kernel's stream-K bookkeeping is 32-bit
   TSDS_RETURN_IF(W64 * PU >= (1ll << 32), TSDS_E_UNSUPPORTED);

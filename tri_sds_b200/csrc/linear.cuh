@@ -26,6 +26,10 @@ int tsds_tc_num_sms();
 int tsds_tc_ctas_setting();
 // Token rows from which the tcgen05 kernels run on CTA pairs (0: never).
 int tsds_tc_pair_rows();
+// Units on which a tcgen05 projection of M rows and `tiles` weight tiles,
+// given `units` CTAs (or pairs), runs data-parallel; 0: stream-K
+// (tsds_set_gemm_dp_rows / _slack).
+int tsds_tc_dp_units(int M, int tiles, int units);
 
 // Fused-layer kernel only: q/k/v projection whose epilogue applies QK-norm + RoPE
 // and writes q and the K/V cache rows (one 128-row tile = one head).
