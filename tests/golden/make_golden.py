@@ -69,10 +69,18 @@ QWEN_CFG = dict(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidd
                 tie_word_embeddings=False)
 
 
-def _hf_qwen(dtype, seed=0, qk_norm_gain=None):
+# the library's kernels take head dim 128 only: the same reference path at
+# that head dim, for checking the device directly against the reference
+QWEN_D128_CFG = dict(vocab_size=512, hidden_size=256, intermediate_size=256, num_hidden_layers=2,
+                     num_attention_heads=2, num_key_value_heads=1, head_dim=128,
+                     max_position_embeddings=64, rope_theta=1.0e6, rms_norm_eps=1e-6,
+                     tie_word_embeddings=False)
+
+
+def _hf_qwen(dtype, seed=0, qk_norm_gain=None, cfg_dict=None):
     from transformers import Qwen3Config, Qwen3ForCausalLM
     torch.manual_seed(seed)
-    cfg = Qwen3Config(**QWEN_CFG)
+    cfg = Qwen3Config(**(cfg_dict or QWEN_CFG))
     m = Qwen3ForCausalLM(cfg)
     with torch.no_grad():
         for n, p in m.named_parameters():
@@ -83,10 +91,12 @@ def _hf_qwen(dtype, seed=0, qk_norm_gain=None):
     return m.to(dtype).eval()
 
 
-def make_qwen(dtype, tag):
+def make_qwen(dtype, tag, cfg_dict=None):
     """Reference Qwen path (QK-norm off): prefill T=12, verify T=5, decode T=1, B=2."""
     rq, _, _ = _import_reference()
-    m = _hf_qwen(dtype)
+    cfg_dict = cfg_dict or QWEN_CFG
+    m = _hf_qwen(dtype, cfg_dict=cfg_dict)
+    V = cfg_dict["vocab_size"]
     st = rq.QwenModelState(m, max_seq_len=64)
     if dtype != torch.bfloat16:
         # qwen_model.py:38 fixes the cache / RoPE-table dtype to bf16; the fp32
@@ -95,16 +105,16 @@ def make_qwen(dtype, tag):
         st.cos, st.sin = rq.precompute_rope(st.D, st.max_seq_len, base=1.0e6, device="cpu", dtype=dtype)
     st.reset_cache(batch_size=2)
     g = torch.Generator().manual_seed(1)
-    ids_prefill = torch.randint(0, 512, (2, 12), generator=g)
-    ids_verify = torch.randint(0, 512, (2, 5), generator=g)
-    ids_decode = torch.randint(0, 512, (2, 1), generator=g)
+    ids_prefill = torch.randint(0, V, (2, 12), generator=g)
+    ids_verify = torch.randint(0, V, (2, 5), generator=g)
+    ids_decode = torch.randint(0, V, (2, 1), generator=g)
     with torch.no_grad():
         lp, hp = rq.qwen_model_forward(ids_prefill, st, return_hidden=True)
         lv, hv = rq.qwen_model_forward(ids_verify, st, return_hidden=True)
         ld, hd = rq.qwen_model_forward(ids_decode, st, return_hidden=True)
     from oracle.qwen import weights_from_hf
     out = {
-        "config": QWEN_CFG, "dtype": str(dtype),
+        "config": cfg_dict, "dtype": str(dtype),
         "weights": weights_from_hf(m),
         "ids_prefill": ids_prefill, "ids_verify": ids_verify, "ids_decode": ids_decode,
         "logits_prefill": lp, "hidden_prefill": hp,
@@ -205,6 +215,7 @@ if __name__ == "__main__":
     sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
     make_qwen(torch.bfloat16, "bf16")
     make_qwen(torch.float32, "f32")
+    make_qwen(torch.bfloat16, "bf16_d128", QWEN_D128_CFG)
     make_qwen_hf_qknorm()
     make_eagle()
     make_gpt2()

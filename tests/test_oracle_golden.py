@@ -41,6 +41,19 @@ def test_qwen_reference_path_bf16_bitexact():
     assert torch.equal(st.v_caches[-1][:, :, :17], fx["v_cache_last"][:, :, :17])
 
 
+def test_qwen_reference_path_bf16_bitexact_head_dim_128():
+    """The same at the library kernels' head dim (128; 2 q heads, 1 kv head):
+    the fixture the device is checked against directly."""
+    fx = load_golden("qwen_ref_bf16_d128.pt")
+    assert fx["config"]["head_dim"] == 128
+    st, out = _run_ref_sequence(fx, torch.bfloat16)
+    for tag in ("prefill", "verify"):
+        assert torch.equal(out[tag][0], fx[f"logits_{tag}"]), tag
+        assert torch.equal(out[tag][1], fx[f"hidden_{tag}"]), tag
+    d = (out["decode"][0].float() - fx["logits_decode"].float()).abs().max().item()
+    assert d <= 2e-2, d
+
+
 def test_qwen_reference_path_f32():
     fx = load_golden("qwen_ref_f32.pt")
     st, out = _run_ref_sequence(fx, torch.float32)
