@@ -68,6 +68,22 @@ def test_fused_equals_per_op_bitwise_on_cta_pairs(B, T):
         _lib.load().tsds_set_gemm_pair_rows(0)
 
 
+@pytest.mark.skipif(os.environ.get("TSDS_TEST_DP") != "1", reason="data-parallel GEMMs: set TSDS_TEST_DP=1")
+@pytest.mark.parametrize("B,T", [(1, 26), (8, 26)])
+def test_fused_equals_per_op_bitwise_data_parallel(B, T):
+    """Both plans' GEMMs under the data-parallel schedule where it applies
+    (the per-op GEMM and the fused kernel's phases make the same choice):
+    still bit for bit."""
+    from tri_sds_b200 import _lib
+    _lib.load().tsds_set_gemm_dp_rows(1)
+    _lib.load().tsds_set_gemm_dp_slack(100)
+    try:
+        _bitwise_case(B, T)
+    finally:
+        _lib.load().tsds_set_gemm_dp_rows(0)
+        _lib.load().tsds_set_gemm_dp_slack(15)
+
+
 def _bitwise_case(B, T):
     S = 1024
     oshape, w, (ref, fus) = _models(Q4B, B, B * T, S, seed=B * 100 + T)

@@ -246,3 +246,31 @@ def test_entry_point_checks_and_layout():
     assert lib.tsds_peer_allreduce_residual(x, unaligned, 0, 2, 0, 1, 8, 64, st, None) == 2
     assert lib.tsds_peer_alloc(16, ctypes.byref(ctypes.c_void_p())) == 1     # smaller than the header
     assert lib.tsds_status_string(9) == b"CUDA runtime call (allocation / IPC) failed"
+
+
+@pytest.mark.parametrize("tp,rank", [(2, 1), (8, 3)])
+def test_sharded_chain_draft_shares_the_slot_alternation(tensor_refs, tp, rank):
+    """A chain draft sharded over the target's ranks with the target's peer
+    group: every peer all-reduce of the cycle - the draft's K forwards, then
+    the target's verify - takes slot 0, 1, 0, 1, ... in order, so no rank
+    writes a slot another rank may still read; no NCCL step remains, and
+    every call fits its buffers."""
+    from tri_sds_b200.engine import SpecEngine
+    from tri_sds_b200.model import QwenModel
+    from tri_sds_b200.tp import lm_exchange_layout
+    B, K = 2, 4
+    rows = B * (K + 1)
+    xb = lm_exchange_layout(rows, SHAPE.vocab // tp)[2]
+    peer = FakeExchangePeer(rank, tp, rows * SHAPE.hidden, xb)
+    comm = _Comm(rank, tp)
+    t = QwenModel(SHAPE, B, 96, rows, device="cpu", tp_rank=rank, tp_size=tp, comm=comm, peer=peer)
+    d = QwenModel(SHAPE, B, 96, B * 2, device="cpu", tp_rank=rank, tp_size=tp, comm=comm, peer=peer)
+    eng = SpecEngine(t, d, K, use_graph=False)
+    calls = eng.plan.calls
+    assert not any(fn is None for _, fn, _ in calls)
+    slots = [a[4] for n, _, a in calls if n == "tsds_peer_allreduce_residual"]
+    assert len(slots) == 2 * SHAPE.n_layers * (K + 1)
+    assert slots == [j % 2 for j in range(len(slots))]
+    assert sum(1 for n, _, _ in calls if n == "tsds_peer_lm_gather") == K + 1
+    for n, fn, a in calls:
+        check_call(n, a)
