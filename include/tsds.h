@@ -158,6 +158,15 @@ void tsds_set_gemm_dp_rows(int rows);
 int tsds_get_gemm_dp_rows(void);
 void tsds_set_gemm_dp_slack(int percent);
 int tsds_get_gemm_dp_slack(void);
+/* The launch shape the tcgen05 GEMM would take for one projection of M
+ * rows (epilogue code TSDS_EPI_STORE / _RESIDUAL / _SWIGLU / _STORE_F32, or
+ * 3 for the LM head's argmax epilogue; n_out outputs, K inputs)
+ * under the current switches: out[0..5] = weight tiles, k-blocks per tile,
+ * CTAs, data-parallel (1) or stream-K (0), pipeline stages, CTAs per tile
+ * (1, or 2 for a pair).  Host arithmetic only, except with CTA pairs (an
+ * occupancy query); no counterpart in the reference (a tuning and test
+ * aid). */
+int tsds_tc_gemm_plan(int epi, int M, int n_out, int K, int32_t* out);
 int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                 void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,

@@ -137,3 +137,39 @@ def test_the_large_token_count_gate_up_is_data_parallel():
     assert not plan(208, 10240, 5120, dp_rows=128)[3]
     assert plan(208, 10240, 5120, dp_rows=128, slack=84)[3] is False
     assert plan(208, 10240, 5120, dp_rows=128, slack=85)[2:4] == (80, True)
+
+
+def _library_plan(epi, M, n_out, K):
+    import ctypes
+
+    from tri_sds_b200 import _lib
+    out = (ctypes.c_int32 * 6)()
+    st = _lib.load().tsds_tc_gemm_plan(epi, M, n_out, K, out)
+    assert st == 0, st
+    return list(out)
+
+
+@pytest.fixture()
+def switches():
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    yield lib
+    lib.tsds_set_gemm_dp_rows(0)
+    lib.tsds_set_gemm_dp_slack(15)
+    lib.tsds_set_gemm_ctas_per_sm(2)
+
+
+@pytest.mark.parametrize("dp_rows,slack,ctas", [(0, 15, 2), (1, 15, 2), (128, 100, 2), (1, 15, 1), (1, 1000, 3)])
+def test_the_restatement_is_the_library_arithmetic(switches, dp_rows, slack, ctas):
+    """tsds_tc_gemm_plan (the host planning tsds_tc_gemm launches with) gives
+    the restatement's tiles, k-blocks, grid, schedule and stages at every
+    projection shape and row count (one-CTA tiles; the library assumes 148
+    SMs where no GPU answers, as here)."""
+    switches.tsds_set_gemm_dp_rows(dp_rows)
+    switches.tsds_set_gemm_dp_slack(slack)
+    switches.tsds_set_gemm_ctas_per_sm(ctas)
+    for n_out, K, swiglu in PROJ:
+        for M in (1, 5, 26, 40, 129, 208, 256):
+            tiles, KT, PU, dp, stages = plan(M, n_out, K, swiglu, ctas_setting=ctas, dp_rows=dp_rows, slack=slack)
+            got = _library_plan(2 if swiglu else 0, M, n_out, K)
+            assert got == [tiles, KT, PU, int(dp), stages, 1], (n_out, K, M, got)

@@ -62,6 +62,7 @@ SIGNATURES = {
     "tsds_get_gemm_dp_rows": (_I, []),
     "tsds_set_gemm_dp_slack": (None, [_I]),
     "tsds_get_gemm_dp_slack": (_I, []),
+    "tsds_tc_gemm_plan": (_I, [_I, _I, _I, _I, _P]),
     "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),

@@ -701,14 +701,16 @@ size_t tsds_tc_workspace_bytes(int M) {
   return 64 + 2 * MAX_TILES * sizeof(int) + (size_t)num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
 }
 
-int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
-                 int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
-                 int* cand_idx, int ldc, cudaStream_t stream) {
-  TSDS_RETURN_IF(M <= 0 || M > 256, TSDS_E_INVALID);
-  TSDS_RETURN_IF(workspace == nullptr || workspace_bytes < tsds_tc_workspace_bytes(M), TSDS_E_WORKSPACE);
-  TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
-  int32_t* status = (int32_t*)workspace;
-  TcParams p;
+namespace {
+
+// The launch shape of one projection: tile counts, CTA pair or single CTA,
+// pipeline stages and shared memory, stream-K or data-parallel units and the
+// grid.  Shared by tsds_tc_gemm and the tsds_tc_gemm_plan query so the two
+// cannot disagree.  CUDA is queried only for SM count and, with pairs, the
+// resident clusters.
+int plan_tc(int epi, int M, int n_out, int K, TcParams& p, int& CG, size_t& smem) {
+  TSDS_RETURN_IF(M <= 0 || M > 256 || n_out <= 0 || K <= 0, TSDS_E_INVALID);
+  p = TcParams{};
   p.M = M;
   p.Npad = (M + 15) / 16 * 16;
   p.n_out = n_out;
@@ -717,7 +719,7 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   // CTA pairs (256-row tiles, half the token rows per CTA) from g_pair_min_rows
   // rows on; not for the LM head's argmax epilogue (its candidates are per
   // 128-row tile of a vocabulary that need not fill whole pairs)
-  const int CG = (g_pair_min_rows > 0 && M >= g_pair_min_rows && epi != EPI_ARGMAX) ? 2 : 1;
+  CG = (g_pair_min_rows > 0 && M >= g_pair_min_rows && epi != EPI_ARGMAX) ? 2 : 1;
   p.tiles = epi == EPI_SWIGLU ? (n_out + 64 * CG - 1) / (64 * CG) : (n_out + TILE_J * CG - 1) / (TILE_J * CG);
   TSDS_RETURN_IF(p.tiles * CG > MAX_TILES, TSDS_E_UNSUPPORTED);
   const long long W64 = (long long)p.tiles * p.KT;
@@ -730,7 +732,7 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
   if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
   TSDS_RETURN_IF(p.stages < 2, TSDS_E_UNSUPPORTED);
-  const size_t smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
+  smem = (size_t)p.stages * (A_STAGE + p.b_stage_bytes) + 1024;
   long long units = (long long)num_sms() * ctas / CG;
   if (CG == 2) {
     const int resident = pair_clusters(epi, smem);
@@ -750,6 +752,45 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   // the kernel's stream-K bookkeeping is 32-bit
   TSDS_RETURN_IF(W64 * PU >= (1ll << 32), TSDS_E_UNSUPPORTED);
   p.W = (uint32_t)W64;
+  // instruction descriptor: bf16 x bf16 -> fp32, K-major A and B, N = Npad,
+  // M = 128 rows per CTA (256 for a pair)
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) |
+            ((uint32_t)((TILE_J * CG) >> 4) << 24);
+  return TSDS_OK;
+}
+
+}  // namespace
+
+extern "C" int tsds_tc_gemm_plan(int epi, int M, int n_out, int K, int32_t* out) {
+  TSDS_RETURN_IF(!out || (epi != EPI_STORE && epi != EPI_RESIDUAL && epi != EPI_SWIGLU && epi != EPI_ARGMAX &&
+                           epi != EPI_STORE_F32),
+                 TSDS_E_INVALID);
+  TcParams p;
+  int CG = 1;
+  size_t smem = 0;
+  const int st = plan_tc(epi, M, n_out, K, p, CG, smem);
+  if (st != TSDS_OK) return st;
+  out[0] = p.tiles;
+  out[1] = p.KT;
+  out[2] = p.P;
+  out[3] = p.dp;
+  out[4] = p.stages;
+  out[5] = CG;
+  return TSDS_OK;
+}
+
+int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
+                 int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
+                 int* cand_idx, int ldc, cudaStream_t stream) {
+  TSDS_RETURN_IF(M <= 0 || M > 256, TSDS_E_INVALID);
+  TSDS_RETURN_IF(workspace == nullptr || workspace_bytes < tsds_tc_workspace_bytes(M), TSDS_E_WORKSPACE);
+  TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
+  int32_t* status = (int32_t*)workspace;
+  TcParams p;
+  int CG = 1;
+  size_t smem = 0;
+  const int pst = plan_tc(epi, M, n_out, K, p, CG, smem);
+  if (pst != TSDS_OK) return pst;
   p.up_off = n_out;
   p.ldo = ldo;
   p.res_ld = res_ld;
@@ -761,10 +802,6 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.cand_val = cand_val;
   p.cand_idx = cand_idx;
   p.ldc = ldc;
-  // instruction descriptor: bf16 x bf16 -> fp32, K-major A and B, N = Npad,
-  // M = 128 rows per CTA (256 for a pair)
-  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.Npad >> 3) << 17) |
-            ((uint32_t)((TILE_J * CG) >> 4) << 24);
 
   CUtensorMap amap, bmap;
   int st = tsds_make_tmap_2d_bf16(&amap, W, K, w_rows, (uint64_t)K * 2, BK, 64, 1);
