@@ -176,8 +176,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int unit = pc / CG, PU = p.P / CG;  // stream-K units: CTAs or CTA pairs
   const int KT = p.KT;
   // stream-K: contiguous ranges of the (tile, k-block) iterations; data-parallel:
-  // whole tiles per unit (tiles >= units), so no tile is split and no partials
-  // are exchanged
+  // whole tiles per unit (PU = min(tiles, units) units), so no tile is split and
+  // no partials are exchanged
   const int b = p.dp ? (int)(((uint32_t)unit * (uint32_t)p.tiles) / (uint32_t)PU) * KT : it_begin(unit, PU, p.W);
   const int e = p.dp ? (int)(((uint32_t)(unit + 1) * (uint32_t)p.tiles) / (uint32_t)PU) * KT
                      : it_begin(unit + 1, PU, p.W);
@@ -740,11 +740,7 @@ int plan_tc(int epi, int M, int n_out, int K, TcParams& p, int& CG, size_t& smem
     if (resident < units) units = resident;
   }
   long long PU = W64 < units ? W64 : units;
-  // Data-parallel: min(tiles, units) units take whole tiles, so no split
-  // tile's fp32 partials are written, waited for and summed at the end of
-  // the kernel.  Its makespan is ceil(tiles / PU) tiles against the ideal
-  // tiles / units; it is chosen when that costs at most g_dp_slack_pct
-  // percent more (fewer tiles than units: when tiles / units >= 1 / (1 + slack)).
+  // stream-K over PU units, or data-parallel where tsds_tc_dp_units says so
   const int dp_units = tsds_tc_dp_units(M, p.tiles, (int)units);
   p.dp = dp_units > 0 ? 1 : 0;
   if (p.dp) PU = dp_units;
