@@ -68,3 +68,44 @@ def test_attention_row_and_cache_limits_without_gpu():
         assert lib.tsds_get_attention_tc() == 2     # clamped
     finally:
         lib.tsds_set_attention_tc(0)
+
+
+def test_tuning_switches_clamp_and_read_back():
+    """The process-wide GEMM / GEMV switches keep their documented ranges and
+    read back what was set (each restored afterwards)."""
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    try:
+        for v, want in [(-3, 0), (0, 0), (128, 128)]:
+            lib.tsds_set_gemm_dp_rows(v)
+            assert lib.tsds_get_gemm_dp_rows() == want
+            lib.tsds_set_gemm_pair_rows(v)
+            assert lib.tsds_get_gemm_pair_rows() == want
+        for v, want in [(-1, 0), (15, 15), (5000, 1000)]:
+            lib.tsds_set_gemm_dp_slack(v)
+            assert lib.tsds_get_gemm_dp_slack() == want
+        for v, want in [(0, 0), (7, 1), (1, 1)]:
+            lib.tsds_set_gemv_splitk(v)
+            assert lib.tsds_get_gemv_splitk() == want
+        for v, want in [(-2, 0), (3, 3), (99, 8)]:
+            lib.tsds_set_gemv_max_rows(v)
+            assert lib.tsds_get_gemv_max_rows() == want
+    finally:
+        lib.tsds_set_gemm_dp_rows(0)
+        lib.tsds_set_gemm_pair_rows(0)
+        lib.tsds_set_gemm_dp_slack(15)
+        lib.tsds_set_gemv_splitk(0)
+        lib.tsds_set_gemv_max_rows(0)
+
+
+def test_gemm_plan_query_checks_its_arguments():
+    import ctypes
+
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    out = (ctypes.c_int32 * 6)()
+    assert lib.tsds_tc_gemm_plan(0, 26, 5120, 8192, out) == 0
+    assert lib.tsds_tc_gemm_plan(7, 26, 5120, 8192, out) != 0      # no such epilogue
+    assert lib.tsds_tc_gemm_plan(0, 0, 5120, 8192, out) != 0       # no rows
+    assert lib.tsds_tc_gemm_plan(0, 257, 5120, 8192, out) != 0     # more rows than one launch takes
+    assert lib.tsds_tc_gemm_plan(0, 26, 5120, 8192, None) != 0
