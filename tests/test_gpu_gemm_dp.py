@@ -40,10 +40,14 @@ def _close_bf16(got, ref_f32, frac_exact=0.95):
 
 
 def _applies(M, n_out, K, swiglu=False):
-    """The host's choice of schedule, restated (tests/test_gemm_schedule_cpu.py)."""
-    from test_gemm_schedule_cpu import plan
-    assert torch.cuda.get_device_properties(0).multi_processor_count == 148
-    return plan(M, n_out, K, swiglu, dp_rows=1)[3]
+    """Whether the launch takes the data-parallel schedule (the library's own
+    planning, tsds_tc_gemm_plan, under the switches the fixture set)."""
+    import ctypes
+
+    from tri_sds_b200 import _lib
+    out = (ctypes.c_int32 * 6)()
+    assert _lib.load().tsds_tc_gemm_plan(2 if swiglu else 0, M, n_out, K, out) == 0
+    return out[3] == 1
 
 
 # (M, n_out, K) where the data-parallel schedule applies; ragged last tiles:
