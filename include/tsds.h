@@ -112,12 +112,12 @@ int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_no
  * Picks the CUDA-core GEMV for small M and the tcgen05 path above it.
  *
  * tsds_linear:           out = bf16(acc)                         (qwen_model.py:108,153)
- * tsds_linear_residual:  out = bf16(res + bf16(acc))              (fused_qwen_decode.py:308-324,
- *                                                                  422-438; qwen_model.py:133-134,143-144)
+ * tsds_linear_residual:  out = bf16(res + bf16(acc))              (fused_qwen_decode.py:179-204,
+ *                                                                  293-309; qwen_model.py:133-134,143-144)
  *                        out may alias res (in-place residual stream).
  * tsds_linear_swiglu:    W = [gate; up] ([2*n_out][K]);
  *                        out = bf16(bf16(silu(bf16(acc_g))) * bf16(acc_u))
- *                                                                 (fused_qwen_decode.py:371-387;
+ *                                                                 (fused_qwen_decode.py:242-265;
  *                                                                  qwen_model.py:139-142)
  */
 /* Workspace: 0 bytes on the GEMV path; otherwise a status word (int32 at
@@ -264,7 +264,7 @@ int tsds_lm_head_argmax(const void* x, int ldx, const void* W, void* logits_out,
 
 /* ---------------------------------------------------------------------------
  * Greedy acceptance + KV commit for one chain cycle (replaces the verify /
- * accept step that tri_sds/worker.py:76-78 leaves unimplemented).
+ * accept step that tri_sds/worker.py:66-68 leaves unimplemented).
  *   draft[B][K], target[B][K+1]  (argmax ids)
  *   n = longest prefix with draft[b][i] == target[b][i]
  *   accept_len[b] = n;  tokens[b][i] = target[b][i] for i <= n, else -1
@@ -432,7 +432,7 @@ int tsds_peer_lm_gather(void* const* bufs, int rank, int tp, int max_elems, size
  * Tree speculative decoding (EAGLE draft tree, verified in one target pass).
  * No counterpart in the reference: its chain draft (eagle_head.py:100-129)
  * stops at argmax tokens and tree drafting / acceptance / KV rollback live
- * in SGLang (worker.py:76-78 raises).  Semantics: oracle/eagle.py.
+ * in SGLang (worker.py:66-68 raises).  Semantics: oracle/eagle.py.
  *
  * tsds_logits_topk: per logits row (bf16, row stride ld): the k largest
  *   values (value desc, index asc) and log-sum-exp, fp32.  k in {1,2,4,8}.

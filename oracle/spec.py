@@ -1,7 +1,7 @@
 """CPU oracle of the chain speculative-decoding cycle (test infrastructure).
 
-The reference wires only ``draft`` (tri_sds/worker.py:63-74); ``verify``,
-acceptance and KV rollback raise or live in SGLang (worker.py:59-61,76-78),
+The reference wires only ``draft`` (tri_sds/worker.py:53-64); ``verify``,
+acceptance and KV rollback raise or live in SGLang (worker.py:49-51,66-68),
 which is not part of the reference tree.  The semantics are therefore
 written down here and pinned by properties (greedy spec output equals
 greedy autoregressive output), not by reference golden vectors.

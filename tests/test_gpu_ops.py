@@ -216,7 +216,7 @@ def test_verify_attention_tree_mask(ops):
 
 
 def test_attention_gqa_reference_signature(ops):
-    """attention.py:371 calling convention: q [B,Hq,1,D], one kv_len."""
+    """attention.py:299-318 calling convention: q [B,Hq,1,D], one kv_len."""
     B, S = 2, 300
     q, kc, vc, _ = _attn_case(B, 1, 64, 8, S, [0, 0], seed=13)
     qh = q.transpose(1, 2).contiguous()  # [B, Hq, 1, D]

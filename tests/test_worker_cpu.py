@@ -1,5 +1,5 @@
 """The drop-in boundary on CPU: plugin registration (tri_sds/__init__.py:1-10)
-and TriSDSWorker's dispatch (tri_sds/worker.py:19-78) with a stand-in engine
+and TriSDSWorker's dispatch (tri_sds/worker.py:9-68) with a stand-in engine
 that records its calls (no GPU, no kernels)."""
 import pytest
 import torch
@@ -23,6 +23,12 @@ class FakeEngine:
         self.calls.append(("step",))
         self.tokens[:, 0] = len(self.calls)
         return self.tokens, self.accept_len
+
+    def step_host(self, cur_host, tokens_host, accept_host):
+        self.calls.append(("step_host",))
+        tokens_host.copy_(self.tokens)
+        accept_host.copy_(self.accept_len)
+        return tokens_host, accept_host
 
     def run_draft(self):
         self.calls.append(("draft",))
@@ -113,7 +119,7 @@ def test_ragged_prompts_reach_the_engine_padded_with_their_lengths(monkeypatch):
     from tri_sds_b200.worker import TriSDSWorker, prompt_tensor
     monkeypatch.setenv("SDS_ENABLED", "1")
     w = TriSDSWorker()
-    eng = FakeEngine()
+    eng = FakeEngine(B=3)
     w.attach_engine(eng)
     w.forward_batch_generation(ScheduleBatch(input_ids=[[5, 6, 7], [8], [9, 10, 11, 12]]))
     assert eng.calls[0] == ("prepare", (3, 4))
@@ -127,3 +133,45 @@ def test_ragged_prompts_reach_the_engine_padded_with_their_lengths(monkeypatch):
     assert ids.shape == (1, 3) and n is None
     with pytest.raises(ValueError):
         prompt_tensor(ScheduleBatch(input_ids=[[1], []]))
+
+
+def test_worker_follows_the_batch_it_is_given(monkeypatch):
+    """A later batch with new prompts (or other request ids) prefills the
+    engine again; the same prompt or one current token per sequence
+    continues; a batch of another size is refused before anything runs."""
+    from types import SimpleNamespace
+
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
+    monkeypatch.setenv("SDS_ENABLED", "1")
+    w = TriSDSWorker()
+    eng = FakeEngine()
+    w.attach_engine(eng)
+    p1 = torch.randint(0, 100, (2, 5), generator=torch.Generator().manual_seed(1))
+    p2 = torch.randint(0, 100, (2, 6), generator=torch.Generator().manual_seed(2))
+    w.forward_batch_generation(ScheduleBatch(input_ids=p1))
+    w.forward_batch_generation(ScheduleBatch(input_ids=p1))
+    w.forward_batch_generation(ScheduleBatch(input_ids=torch.tensor([[3], [4]])))
+    assert [c for c in eng.calls if c[0] == "prepare"] == [("prepare", (2, 5))]
+    # new prompts: prepared again from them
+    w.forward_batch_generation(ScheduleBatch(input_ids=p2))
+    assert eng.calls[-2:] == [("prepare", (2, 6)), ("step",)]
+    assert torch.equal(eng.prompt, p2)
+    # the same prompt shape with other ids is a new batch too
+    p3 = p2.clone()
+    p3[0, 0] += 1
+    w.forward_batch_generation(ScheduleBatch(input_ids=p3))
+    assert eng.calls[-2] == ("prepare", (2, 6)) and torch.equal(eng.prompt, p3)
+    # request identities decide when the batch carries them
+    reqs = [SimpleNamespace(rid="a"), SimpleNamespace(rid="b")]
+    w.forward_batch_generation(ScheduleBatch(input_ids=p1, reqs=reqs))
+    n_prep = sum(c[0] == "prepare" for c in eng.calls)
+    w.forward_batch_generation(ScheduleBatch(input_ids=torch.tensor([[3], [4]]), reqs=list(reqs)))
+    assert sum(c[0] == "prepare" for c in eng.calls) == n_prep
+    w.forward_batch_generation(ScheduleBatch(input_ids=p1, reqs=[SimpleNamespace(rid="c"), reqs[1]]))
+    assert sum(c[0] == "prepare" for c in eng.calls) == n_prep + 1
+    # another batch size: refused, the engine untouched
+    before = list(eng.calls)
+    with pytest.raises(ValueError, match="engine serves 2"):
+        w.forward_batch_generation(ScheduleBatch(input_ids=torch.zeros(3, 4, dtype=torch.int64)))
+    assert eng.calls == before

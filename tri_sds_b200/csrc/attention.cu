@@ -4,7 +4,7 @@
 // rows that share a kv head (T new tokens x the q heads of the group) are
 // processed together, so every K/V byte is read from HBM once per step
 // (the reference's GQA kernel re-reads K/V once per q head,
-// attention.py:330-368; its verify path materialises repeat_interleave
+// attention.py:237-296; its verify path materialises repeat_interleave
 // copies, qwen_model.py:122-123).
 //
 // * K/V tiles of 64 keys x 128 dims are staged by TMA (cp.async.bulk.tensor,

@@ -2,12 +2,12 @@
 
 Reference op (file:line)                                 -> here
   norm.rms_norm (norm.py:61-72)                             rms_norm
-  attention.attention_gqa (attention.py:371-390)            attention_gqa
+  attention.attention_gqa (attention.py:299-318)            attention_gqa
   qwen_model verify SDPA (qwen_model.py:121-131)            verify_attention
-  fused_qwen_decode.fused_rmsnorm_qkv_rope (:253-274)       fused_rmsnorm_qkv_rope
-  fused_qwen_decode.fused_oproj_residual (:308-324)         fused_oproj_residual
-  fused_qwen_decode.fused_gateup_silu (:371-387)            fused_gateup_silu
-  fused_qwen_decode.fused_down_residual (:422-438)          fused_down_residual
+  fused_qwen_decode.fused_rmsnorm_qkv_rope (:124-149)       fused_rmsnorm_qkv_rope
+  fused_qwen_decode.fused_oproj_residual (:179-204)         fused_oproj_residual
+  fused_qwen_decode.fused_gateup_silu (:242-265)            fused_gateup_silu
+  fused_qwen_decode.fused_down_residual (:293-309)          fused_down_residual
   LM head + argmax (qwen_model.py:192; eagle_head.py:120)   lm_head_argmax
 
 Like the reference wrappers these allocate their outputs with torch and
@@ -181,17 +181,17 @@ def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
 
 
 def fused_oproj_residual(attn_flat, o_w_t, x):
-    """fused_qwen_decode.py:308-324: x + attn_flat @ o_w_t."""
+    """fused_qwen_decode.py:179-204: x + attn_flat @ o_w_t."""
     return linear_residual(attn_flat, _out_in(o_w_t), x)
 
 
 def fused_gateup_silu(x_norm2, gate_up_w_t):
-    """fused_qwen_decode.py:371-387: silu(x@W[:, :I]) * (x@W[:, I:])."""
+    """fused_qwen_decode.py:242-265: silu(x@W[:, :I]) * (x@W[:, I:])."""
     return linear_swiglu(x_norm2, _out_in(gate_up_w_t))
 
 
 def fused_down_residual(hidden, down_w_t, x_residual):
-    """fused_qwen_decode.py:422-438: x_residual + hidden @ down_w_t."""
+    """fused_qwen_decode.py:293-309: x_residual + hidden @ down_w_t."""
     return linear_residual(hidden, _out_in(down_w_t), x_residual)
 
 
@@ -247,7 +247,7 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
 
 
 def attention_gqa(q, k, v, kv_len, q_per_kv):
-    """attention.py:371-390: q [B, Hq, 1, D] over the first ``kv_len`` cache
+    """attention.py:299-318: q [B, Hq, 1, D] over the first ``kv_len`` cache
     rows (one length for the whole batch, a device int32 tensor)."""
     B, Hq, Tq, D = q.shape
     _need(Tq == 1, "GQA decode only")

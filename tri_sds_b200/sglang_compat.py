@@ -36,11 +36,13 @@ except Exception:  # noqa: BLE001
     @dataclass
     class ScheduleBatch:
         """The fields the spec worker reads: token ids [B, T] (or a list of
-        the sequences' prompts, ragged), positions, and seq_lens (real tokens
-        per row of a padded [B, P] prompt)."""
+        the sequences' prompts, ragged), positions, seq_lens (real tokens
+        per row of a padded [B, P] prompt) and reqs (requests, each with a
+        ``rid``: the batch's identity)."""
         input_ids: object = None
         positions: object = None
         seq_lens: object = None
+        reqs: list = field(default_factory=list)
         extra: dict = field(default_factory=dict)
 
     class StandaloneWorker:

@@ -1,20 +1,28 @@
-"""TriSDSWorker: the spec worker the plugin installs (tri_sds/worker.py:19-78).
+"""TriSDSWorker: the spec worker the plugin installs (tri_sds/worker.py:9-68).
 
 Same class name, base class, methods and ``SDS_ENABLED`` gate as the
-reference.  With ``SDS_ENABLED=1`` the three methods run this package's
-device path instead of SGLang's:
+reference (worker.py:19-21, 32-45).  With ``SDS_ENABLED=1`` the three
+methods run this package's device path instead of SGLang's:
 
 * ``forward_batch_generation(batch)``: one full speculative cycle (draft ->
   verify -> accept -> commit) for the batch's sequences; returns the
   emitted tokens ``[B, K+1]`` (-1 padded) and accept lengths ``[B]``.
-  (The reference raises NotImplementedError here, worker.py:59-61.)
+  (The reference raises NotImplementedError here, worker.py:49-51.)
 * ``draft(batch)``: the K draft tokens ``[B, K]`` of the next cycle
-  (the reference returns the GPT-2 draft's logits, worker.py:63-74).
+  (the reference returns the GPT-2 draft's logits, worker.py:53-64).
 * ``verify(batch)``: the target's verify pass + acceptance over the drafts
-  of the last ``draft`` call (the reference raises, worker.py:76-78).
+  of the last ``draft`` call (the reference raises, worker.py:66-68).
 
 The engine is attached with ``attach_engine`` (or built lazily by the
 subclass hook ``_init_engine``); it owns the weights and KV caches.
+
+The worker follows the batch it is given.  It remembers the request ids
+(``batch.reqs[i].rid`` when the batch carries SGLang requests), else the
+prompt it prepared the engine from.  A batch with other requests, or without
+requests a prompt other than the prepared one, prefills the engine again
+from that batch; one token per sequence (``input_ids`` [B, 1]) continues the
+prepared batch.  A batch whose size differs from the engine's raises
+``ValueError`` before anything runs.
 """
 from __future__ import annotations
 
@@ -53,6 +61,15 @@ def prompt_tensor(batch: ScheduleBatch):
     return ids, lengths
 
 
+def request_ids(batch: ScheduleBatch):
+    """The batch's request identities (SGLang's ``batch.reqs[i].rid``) as a
+    tuple, or None when the batch carries no requests."""
+    reqs = getattr(batch, "reqs", None)
+    if not reqs:
+        return None
+    return tuple(getattr(r, "rid", id(r)) for r in reqs)
+
+
 class TriSDSWorker(StandaloneWorker):
     sds_enabled: bool = False
     engine = None
@@ -61,24 +78,55 @@ class TriSDSWorker(StandaloneWorker):
         super().__init__(*args, **kwargs)
         self.sds_enabled = os.environ.get("SDS_ENABLED", "0") == "1"
         self._prefilled = False
+        self._rids = None
+        self._prompt = None
 
     # -- engine ----------------------------------------------------------------
     def attach_engine(self, engine):
         self.engine = engine
         self._prefilled = False
+        self._rids = None
+        self._prompt = None
 
     def _init_engine(self):
         raise RuntimeError("TriSDSWorker needs an engine: call attach_engine(SpecEngine(...))")
 
+    def _engine_batch(self) -> int:
+        return int(self.engine.tokens.shape[0])
+
+    def _is_new_batch(self, batch: ScheduleBatch, ids: torch.Tensor, lengths) -> bool:
+        """True when ``batch`` is not the continuation of the prepared one:
+        other request ids, or (without ids) a prompt other than the prepared
+        prompt.  One token per sequence ([B, 1]) is the current token of a
+        continuing batch."""
+        rids = request_ids(batch)
+        if rids is not None or self._rids is not None:
+            return rids != self._rids
+        if ids.shape[1] == 1 and not isinstance(batch.input_ids, (list, tuple)):
+            return False
+        key = (ids.detach().cpu(), None if lengths is None else lengths.detach().cpu())
+        old = self._prompt
+        return not (old is not None and old[0].shape == key[0].shape and torch.equal(old[0], key[0])
+                    and (old[1] is None) == (key[1] is None) and (old[1] is None or torch.equal(old[1], key[1])))
+
     def _ensure(self, batch: ScheduleBatch):
+        """Prefill the engine from ``batch`` on the first call and whenever
+        the batch is a new one; returns True when it did."""
         if self.engine is None:
             self._init_engine()
-        if not self._prefilled:
-            ids, lengths = prompt_tensor(batch)
-            self.engine.prepare(ids, lengths)
-            self._prefilled = True
+        ids, lengths = prompt_tensor(batch)
+        if ids.shape[0] != self._engine_batch():
+            raise ValueError(f"batch of {ids.shape[0]} sequences, but the engine serves "
+                             f"{self._engine_batch()}: attach an engine built for this batch size")
+        if self._prefilled and not self._is_new_batch(batch, ids, lengths):
+            return False
+        self.engine.prepare(ids, lengths)
+        self._prefilled = True
+        self._rids = request_ids(batch)
+        self._prompt = (ids.detach().cpu(), None if lengths is None else lengths.detach().cpu())
+        return True
 
-    # -- dispatch (worker.py:42-55) -------------------------------------------
+    # -- dispatch (worker.py:32-45) -------------------------------------------
     def forward_batch_generation(self, batch: ScheduleBatch):
         if not self.sds_enabled:
             return super().forward_batch_generation(batch)
@@ -102,15 +150,15 @@ class TriSDSWorker(StandaloneWorker):
         Later calls may carry the current token of each sequence
         (``input_ids`` of shape [B, 1], e.g. the previous cycle's bonus
         token, on the host); the results come back on the host then."""
-        first = not self._prefilled
-        self._ensure(batch)
+        first = self._ensure(batch)
         ids = batch.input_ids
         if not first and isinstance(ids, torch.Tensor) and not ids.is_cuda and ids.dim() == 2 and ids.shape[1] == 1:
             B, W = self.engine.tokens.shape
-            if getattr(self, "_host_bufs", None) is None:
-                self._host_bufs = (torch.empty(B, dtype=torch.int64).pin_memory(),
-                                   torch.empty(B, W, dtype=torch.int64).pin_memory(),
-                                   torch.empty(B, dtype=torch.int32).pin_memory())
+            if getattr(self, "_host_bufs", None) is None or self._host_bufs[1].shape != (B, W):
+                pin = torch.cuda.is_available()
+                self._host_bufs = (torch.empty(B, dtype=torch.int64, pin_memory=pin),
+                                   torch.empty(B, W, dtype=torch.int64, pin_memory=pin),
+                                   torch.empty(B, dtype=torch.int32, pin_memory=pin))
             cur_h, tok_h, acc_h = self._host_bufs
             cur_h.copy_(ids[:, 0])
             return self.engine.step_host(cur_h, tok_h, acc_h)
