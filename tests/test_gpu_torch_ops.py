@@ -122,14 +122,16 @@ def test_accept_greedy_op(tsds):
     draft[0, 0] += 1
     draft[1, 2] += 1
     draft[3, 3] += 1
-    lengths = torch.tensor([10, 20, 30, 40], dtype=torch.int32, device=DEV)
+    start = [10, 20, 30, 40]
+    lengths = torch.tensor(start, dtype=torch.int32, device=DEV)
     last = torch.zeros(B, dtype=torch.int64, device=DEV)
     cur = torch.zeros(B, dtype=torch.int64, device=DEV)
     n, tokens = tsds.accept_greedy(draft.to(DEV), tgt.to(DEV), lengths, last, cur)
     n_ref, tok_ref = osp.greedy_accept(draft, tgt)
     assert n.cpu().tolist() == n_ref.tolist()
     assert torch.equal(tokens.cpu(), tok_ref)
-    assert lengths.cpu().tolist() == [10 + int(a) + 1 for a in n_ref]
+    # each sequence commits its accepted drafts plus the bonus token
+    assert lengths.cpu().tolist() == [L0 + int(a) + 1 for L0, a in zip(start, n_ref)]
 
 
 def _random_trees(B, V, seed):
