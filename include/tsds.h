@@ -125,6 +125,18 @@ int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_no
  * must be zero before the first use (every launch leaves them zero) and
  * fp32 split-K partials.  Zero-fill a fresh workspace once. */
 size_t tsds_linear_workspace_bytes(int M, int n_out, int K);
+/* Leading bytes of a tcgen05 GEMM / LM-head workspace that hold the status
+ * word and the tile counters.  A launch that gave up on a device wait
+ * (status TSDS_E_TIMEOUT) may leave counters nonzero: zero these bytes
+ * before the workspace is used again.  No counterpart in the reference
+ * (its kernels have no device waits). */
+size_t tsds_linear_workspace_header_bytes(void);
+/* Limit of each bounded device wait of the tcgen05 GEMM and LM head, in
+ * nanoseconds (default 2e9, clamped to 1..1e10).  Process-wide; read at
+ * launch.  Lowering it makes every wait give up, which tests the timeout
+ * recovery; no counterpart in the reference. */
+void tsds_set_wait_limit_ns(unsigned long long ns);
+unsigned long long tsds_get_wait_limit_ns(void);
 /* Largest M served by the CUDA-core GEMV (0..8; above it the tcgen05 GEMM;
  * default 0: tcgen05 for every M).  Process-wide; read by the
  * *_workspace_bytes functions too. */
@@ -370,6 +382,9 @@ typedef struct {
   int max_elems;       /* the buffers' slot size (tsds_peer_buffer_bytes) */
 } tsds_peer_group;
 size_t tsds_fused_layer_workspace_bytes(int M);
+/* Leading bytes of the fused-layer workspace holding the status word and
+ * the phase counters: zero them after a TSDS_E_TIMEOUT before reuse. */
+size_t tsds_fused_layer_workspace_header_bytes(void);
 int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
                      const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
                      tsds_stream_t stream);

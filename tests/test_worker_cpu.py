@@ -175,3 +175,33 @@ def test_worker_follows_the_batch_it_is_given(monkeypatch):
     with pytest.raises(ValueError, match="engine serves 2"):
         w.forward_batch_generation(ScheduleBatch(input_ids=torch.zeros(3, 4, dtype=torch.int64)))
     assert eng.calls == before
+
+
+def test_status_error_clears_the_counters_and_retires_a_peer_group():
+    """After a device wait gave up, the word and the tile counters beside it
+    (the workspace header) are zeroed so the next launch starts afresh, and a
+    peer group is retired: its ranks' per-CTA epochs no longer agree."""
+    from tri_sds_b200.model import StatusWatch
+    ws = torch.arange(64, dtype=torch.uint8)           # header = first 32 bytes
+    ws[:4] = torch.tensor([5, 0, 0, 0], dtype=torch.uint8)
+    retired = []
+    w = StatusWatch([(ws[:4].view(torch.int32), ws[:32], lambda: retired.append(1))])
+    w.copy()
+    with pytest.raises(RuntimeError, match="status 5"):
+        w.check()
+    assert retired == [1]
+    assert int(ws[:32].sum()) == 0 and torch.equal(ws[32:], torch.arange(32, 64, dtype=torch.uint8))
+    w.copy()
+    w.check()
+
+
+def test_retired_peer_group_refuses_the_next_cycle():
+    from types import SimpleNamespace
+
+    from tri_sds_b200.model import QwenModel
+    m = QwenModel.__new__(QwenModel)
+    m.peer = SimpleNamespace(broken=False)
+    m.ensure_usable()
+    m._retire_peer()
+    with pytest.raises(RuntimeError, match="retired"):
+        m.ensure_usable()

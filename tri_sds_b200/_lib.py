@@ -51,6 +51,9 @@ SIGNATURES = {
     "tsds_prep_chain": (_I, [_P, _I, _I, _I, _P, _P, _P]),
     "tsds_qk_norm_rope_kv": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_linear_workspace_bytes": (_Z, [_I, _I, _I]),
+    "tsds_linear_workspace_header_bytes": (_Z, []),
+    "tsds_set_wait_limit_ns": (None, [ctypes.c_ulonglong]),
+    "tsds_get_wait_limit_ns": (ctypes.c_ulonglong, []),
     "tsds_set_gemv_max_rows": (None, [_I]),
     "tsds_get_gemv_max_rows": (_I, []),
     "tsds_set_gemv_splitk": (None, [_I]),
@@ -89,6 +92,7 @@ SIGNATURES = {
     "tsds_argmax_merge": (_I, [_P, _P, _I, _I, ctypes.c_int64, _P, _I, _P]),
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
     "tsds_fused_layer_workspace_bytes": (_Z, [_I]),
+    "tsds_fused_layer_workspace_header_bytes": (_Z, []),
     "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _P, _Z, _P]),
     "tsds_peer_buffer_bytes": (_Z, [_I, _Z]),
     "tsds_peer_slot_offset": (_Z, [_I, _I]),

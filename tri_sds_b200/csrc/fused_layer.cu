@@ -894,6 +894,9 @@ extern "C" size_t tsds_fused_layer_workspace_bytes(int M) {
   return 64 + (size_t)CH_MAX_COUNTERS * sizeof(int) + partial_bytes(M);
 }
 
+// The status word and the counters (see tsds_linear_workspace_header_bytes).
+extern "C" size_t tsds_fused_layer_workspace_header_bytes(void) { return 64 + (size_t)CH_MAX_COUNTERS * sizeof(int); }
+
 extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
                                 const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
                                 tsds_stream_t stream) {

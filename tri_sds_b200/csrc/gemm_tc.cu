@@ -51,6 +51,7 @@ struct TcParams {
   uint32_t idesc;
   int tmem_cols;
   int dp;  // 1: data-parallel schedule (whole tiles per unit), 0: stream-K
+  uint64_t wait_ns;  // limit of every bounded wait (tsds_set_wait_limit_ns)
 };
 
 constexpr int MAX_TILES = 2048;   // tile counters; departure counters follow them
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       int i = npre;
       for (int it = b + npre; it < e; ++it, ++i) {
         const int s = i % p.stages, r = i / p.stages;
-        if (!mbar_wait(&sh.empty_bar[s], (r - 1) & 1)) {
+        if (!mbar_wait(&sh.empty_bar[s], (r - 1) & 1, p.wait_ns)) {
           atomicExch(p.status, TSDS_E_TIMEOUT);
           sh.abort = 1;
           break;
@@ -285,7 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const int k0 = (int)((b > tb ? b : tb) - tb);
         const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
         const int buf = seg & 1, use = seg >> 1;
-        if (use > 0 && !mbar_wait(&sh.tempty_bar[buf], (use - 1) & 1)) {
+        if (use > 0 && !mbar_wait(&sh.tempty_bar[buf], (use - 1) & 1, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -293,7 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const uint32_t d = tmem + buf * p.tmem_cols;
         for (int kt = k0; kt < k1; ++kt, ++i) {
           const int s = i % p.stages, r = i / p.stages;
-          if (!mbar_wait(&sh.full_bar[s], r & 1) || *(volatile int*)&sh.abort) {
+          if (!mbar_wait(&sh.full_bar[s], r & 1, p.wait_ns) || *(volatile int*)&sh.abort) {
             ok = false;
             break;
           }
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       const int k0 = (int)((b > tb ? b : tb) - tb);
       const int k1 = (int)((e < tb + KT ? e : tb + KT) - tb);
       const int buf = seg & 1, use = seg >> 1;
-      const int ok = mbar_wait(&sh.tfull_bar[buf], use & 1) ? 1 : 0;
+      const int ok = mbar_wait(&sh.tfull_bar[buf], use & 1, p.wait_ns) ? 1 : 0;
       if (!ok) {
         atomicExch(p.status, TSDS_E_TIMEOUT);
         sh.abort = 1;
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           if (ld_acquire(&p.counters[vt]) < nq) {
             const uint64_t t0 = global_ns();
             while (ld_acquire(&p.counters[vt]) < nq) {
-              if (global_ns() - t0 > 2000000000ull) {
+              if (global_ns() - t0 > p.wait_ns) {
                 ok = 0;
                 break;
               }
@@ -575,6 +576,9 @@ std::atomic<int> g_dp_min_rows{0};
 // Largest makespan increase (percent over the ideal tiles / units) the
 // data-parallel schedule may cost.
 std::atomic<int> g_dp_slack_pct{15};
+// Limit of every bounded wait of the kernel, in ns of %globaltimer: far above
+// any legitimate wait; lowered only to test the recovery from a timeout.
+std::atomic<unsigned long long> g_wait_ns{2000000000ull};
 constexpr int SMEM_PER_SM = 233472;    // 228 KB
 constexpr int SMEM_RESERVE = 8192;     // static shared memory + per-CTA system reserve
 
@@ -602,6 +606,10 @@ extern "C" void tsds_set_gemm_dp_slack(int percent) {
   g_dp_slack_pct = percent < 0 ? 0 : (percent > 1000 ? 1000 : percent);
 }
 extern "C" int tsds_get_gemm_dp_slack(void) { return g_dp_slack_pct; }
+extern "C" void tsds_set_wait_limit_ns(unsigned long long ns) {
+  g_wait_ns = ns < 1 ? 1 : (ns > 10000000000ull ? 10000000000ull : ns);
+}
+extern "C" unsigned long long tsds_get_wait_limit_ns(void) { return g_wait_ns; }
 int tsds_tc_num_sms() { return num_sms(); }
 
 // Data-parallel: min(tiles, units) units take whole tiles, so no split
@@ -701,6 +709,11 @@ size_t tsds_tc_workspace_bytes(int M) {
   return 64 + 2 * MAX_TILES * sizeof(int) + (size_t)num_sms() * 4 * 2 * npad * TILE_J * sizeof(float);
 }
 
+// The status word and the counters: what must be zero before the next
+// launch after a launch that gave up on a wait (an aborted CTA leaves its
+// arrivals counted and departs without resetting them).
+extern "C" size_t tsds_linear_workspace_header_bytes(void) { return 64 + 2 * MAX_TILES * sizeof(int); }
+
 namespace {
 
 // The launch shape of one projection: tile counts, CTA pair or single CTA,
@@ -724,6 +737,7 @@ int plan_tc(int epi, int M, int n_out, int K, TcParams& p, int& CG, size_t& smem
   TSDS_RETURN_IF(p.tiles * CG > MAX_TILES, TSDS_E_UNSUPPORTED);
   const long long W64 = (long long)p.tiles * p.KT;
   p.tmem_cols = pow2_at_least(p.Npad);
+  p.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   int ctas = g_ctas_per_sm;
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
   p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows

@@ -171,7 +171,7 @@ class EagleEngine:
         tokens_host.copy_(self.tokens, non_blocking=True)
         accept_host.copy_(self.accept_len, non_blocking=True)
         if getattr(self, "_watch", None) is None:
-            self._watch = StatusWatch(self.target.status_words() + self.head.model.status_words())
+            self._watch = StatusWatch(self.target.status_regions() + self.head.model.status_regions())
         self._watch.copy()   # the kernels' status words, read with the results
         torch.cuda.current_stream().synchronize()
         self._watch.check()
@@ -217,6 +217,7 @@ class EagleEngine:
 
     def step(self, U: torch.Tensor | None = None):
         """One cycle -> (tokens [B, depth+2] padded -1, accept_len [B])."""
+        self.target.ensure_usable()
         if not self.greedy:
             self.draw_uniforms(U)
         if self.use_graph:

@@ -124,6 +124,7 @@ class SpecEngine:
 
     def step(self):
         """One cycle; returns device tensors (tokens [B,K+1] padded -1, accept_len [B])."""
+        self.target.ensure_usable()
         if self.use_graph:
             self.graph.replay()
         else:
@@ -139,7 +140,7 @@ class SpecEngine:
         tokens_host.copy_(self.tokens, non_blocking=True)
         accept_host.copy_(self.accept_len, non_blocking=True)
         if getattr(self, "_watch", None) is None:
-            self._watch = StatusWatch(self.target.status_words() + self.draft.status_words())
+            self._watch = StatusWatch(self.target.status_regions() + self.draft.status_regions())
         self._watch.copy()   # the kernels' status words, read with the results
         torch.cuda.current_stream().synchronize()
         self._watch.check()

@@ -44,11 +44,16 @@ def _p(t):
 TWO_SHOT_BYTES = 2 << 20
 
 
-def raise_status(word, st: int):
-    """Raise RuntimeError for a nonzero device status `st` read from `word`
-    (which is cleared so that the next check starts afresh)."""
+def raise_status(word, st: int, header=None, on_error=None):
+    """Raise RuntimeError for a nonzero device status `st` read from `word`.
+    The word - and `header`, the workspace bytes that hold it and the tile
+    counters a launch that gave up may have left nonzero - is cleared so the
+    next launch on the workspace starts afresh; `on_error()` runs first
+    (e.g. to retire a peer group whose cross-rank epochs have drifted)."""
     if st != 0:
-        word.zero_()
+        if on_error is not None:
+            on_error()
+        (header if header is not None else word).zero_()
         raise RuntimeError(f"device status {st}: {_lib.load().tsds_status_string(st).decode()}")
 
 
@@ -56,19 +61,23 @@ class StatusWatch:
     """Reads a set of device status words together with a cycle's results:
     `copy()` queues their copies into pinned host memory on the current
     stream (after the cycle's kernels), `check()` - after the caller's
-    synchronize - raises on the first nonzero one."""
+    synchronize - raises on the first nonzero one.  `regions` holds
+    (word, header, on_error) triples as QwenModel.status_regions returns
+    them, or bare status words."""
 
-    def __init__(self, words: list):
-        self.words = words
-        self.host = torch.zeros(len(words), dtype=torch.int32, pin_memory=bool(words) and words[0].is_cuda)
+    def __init__(self, regions: list):
+        self.regions = [r if isinstance(r, tuple) else (r, None, None) for r in regions]
+        self.words = [r[0] for r in self.regions]
+        self.host = torch.zeros(len(self.words), dtype=torch.int32,
+                                pin_memory=bool(self.words) and self.words[0].is_cuda)
 
     def copy(self):
         for i, w in enumerate(self.words):
             self.host[i:i + 1].copy_(w, non_blocking=True)
 
     def check(self):
-        for i, w in enumerate(self.words):
-            raise_status(w, int(self.host[i]))
+        for i, (w, header, on_error) in enumerate(self.regions):
+            raise_status(w, int(self.host[i]), header, on_error)
 
 
 def _fused_args(phases: list, rope: dict | None, peer, M: int, ws, ws_bytes: int) -> tuple:
@@ -563,16 +572,39 @@ class QwenModel:
         self.comm.all_gather(allv, loc.contiguous().reshape(-1))
         return allv.reshape(self.vocab_tp, *loc.shape).permute(1, 0, 2).reshape(loc.shape[0], -1)
 
-    def status_words(self) -> list:
-        """The device status words this model's kernels record errors in
-        (one int32 each): attention's, and word 0 of the tcgen05 GEMM, LM-head
-        and fused-layer workspaces (a bounded device wait that gave up)."""
-        words = [self.status, self.lin_ws[:4].view(torch.int32), self.lm_ws[:4].view(torch.int32)]
+    def status_regions(self) -> list:
+        """(status word, header, on_error) for each place this model's
+        kernels record errors (a bounded device wait that gave up): the
+        attention / peer status word, and word 0 of the tcgen05 GEMM, LM-head
+        and fused-layer workspaces, whose header (status + tile counters) is
+        cleared with the word.  A model with a peer group retires the group
+        on any error: the ranks' per-CTA epochs no longer agree."""
+        hl = _lib.query("tsds_linear_workspace_header_bytes")
+        on_error = self._retire_peer if self.peer is not None else None
+        regs = [(self.status, None, on_error),
+                (self.lin_ws[:4].view(torch.int32), self.lin_ws[:min(hl, self.lin_ws.numel())], on_error),
+                (self.lm_ws[:4].view(torch.int32), self.lm_ws[:min(hl, self.lm_ws.numel())], on_error)]
         if self.fused_layers:
-            words.append(self.fused_ws[:4].view(torch.int32))
-        return words
+            hf = _lib.query("tsds_fused_layer_workspace_header_bytes")
+            regs.append((self.fused_ws[:4].view(torch.int32), self.fused_ws[:min(hf, self.fused_ws.numel())],
+                         on_error))
+        return regs
+
+    def status_words(self) -> list:
+        """The device status words of status_regions (one int32 each)."""
+        return [r[0] for r in self.status_regions()]
+
+    def _retire_peer(self):
+        self.peer.broken = True
+
+    def ensure_usable(self):
+        """Raise before a launch on a peer group retired by a device error."""
+        if self.peer is not None and getattr(self.peer, "broken", False):
+            raise RuntimeError("the peer all-reduce group was retired after a device wait gave up (its ranks' "
+                               "epochs no longer agree): build a new PeerAllReduce on every rank")
 
     def check_status(self):
-        """Raise if a kernel recorded an error in a status word (clears it)."""
-        for w in self.status_words():
-            raise_status(w, int(w.item()))
+        """Raise if a kernel recorded an error in a status word (clears it
+        and the counters beside it)."""
+        for w, header, on_error in self.status_regions():
+            raise_status(w, int(w.item()), header, on_error)

@@ -87,6 +87,34 @@ class _Scratch:
 _scratch = _Scratch()
 
 
+def check_status(device=None) -> None:
+    """Raise RuntimeError if an op-level kernel on `device` (default: the
+    current one) recorded an error in its status word - a bounded device
+    wait that gave up.  Synchronises the device.  The op-level workspaces'
+    headers (status word + tile counters) and the status word are zeroed
+    first, so later calls start afresh."""
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    torch.cuda.synchronize(dev)
+    # the tcgen05 GEMM and LM-head workspaces carry a status word and tile
+    # counters; the attention workspace holds split partials only
+    hb = _lib.query("tsds_linear_workspace_header_bytes")
+    hdr = {"linear": hb, "lm_head": hb}
+    bad = 0
+    for (d, kind), b in _scratch.buf.items():
+        if d != dev or kind not in hdr:
+            continue
+        st = int(b[:4].view(torch.int32).item())
+        if st:
+            b[:min(hdr.get(kind, 4), b.numel())].zero_()
+            bad = bad or st
+    s = _scratch.status.get(dev)
+    if s is not None and int(s.item()):
+        bad = bad or int(s.item())
+        s.zero_()
+    if bad:
+        raise RuntimeError(f"device status {bad}: {_lib.load().tsds_status_string(bad).decode()}")
+
+
 def _out_in(w_t: torch.Tensor) -> torch.Tensor:
     """[in, out] weight argument -> contiguous [out, in] tensor."""
     if w_t.dim() == 2 and w_t.stride(0) == 1 and w_t.stride(1) == w_t.shape[0]:

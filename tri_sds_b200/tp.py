@@ -134,6 +134,7 @@ class PeerAllReduce:
     def __init__(self, rank: int, size: int, max_elems: int, group=None, exchange_bytes: int = 0):
         assert 1 <= size <= 8 and 0 <= rank < size
         self.rank, self.size = rank, size
+        self.broken = False   # set when a device wait on the group gave up: the group is then unusable
         self.max_elems = (max_elems + 63) // 64 * 64
         self.exchange_bytes = exchange_bytes
         self._own = ctypes.c_void_p()
