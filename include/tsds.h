@@ -385,6 +385,11 @@ size_t tsds_fused_layer_workspace_bytes(int M);
 /* Leading bytes of the fused-layer workspace holding the status word and
  * the phase counters: zero them after a TSDS_E_TIMEOUT before reuse. */
 size_t tsds_fused_layer_workspace_header_bytes(void);
+/* The grid tsds_fused_layer takes for M rows under the current switches:
+ * out[0..3] = CTAs, CTAs per weight tile (2: pairs), pipeline stages, CTAs
+ * per SM requested.  A tuning and test aid; no counterpart in the
+ * reference. */
+int tsds_fused_layer_grid(int M, int32_t* out);
 int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
                      const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
                      tsds_stream_t stream);

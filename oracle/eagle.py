@@ -351,22 +351,47 @@ def inverse_cdf(p: torch.Tensor, u: float) -> int:
     return i
 
 
+RULE_DRAFT, RULE_TARGET = 0, 1
+
+
 def accept_tree_rejection(tree: Tree, target_logits: torch.Tensor, head_logits: torch.Tensor, U: torch.Tensor,
-                          topk: int = 4):
+                          topk: int = 4, rule: int = RULE_DRAFT):
     """Rejection sampling at temperature 1 -> (accepted node indices, bonus token).
 
     target_logits [n, V] at the tree nodes; head_logits [rows, V] of the head
-    passes (row tree.head_row[n] is q of node n's children); U [depth+1, topk+1]."""
+    passes (row tree.head_row[n] is q of node n's children); U [depth+1, topk+1].
+
+    rule RULE_DRAFT (recursive rejection sampling against the draft's q):
+    accept child x when u * q(x) < p(x); on rejection p <- norm(max(p - q, 0))
+    and q <- q without x, renormalised.  The emitted token is distributed as
+    p when the children are drawn from q without replacement.
+
+    rule RULE_TARGET (the draft taken as deterministic, q one-hot on each
+    child in turn): accept child x when u < p(x); on rejection p <- p without
+    x, renormalised.  The emitted token is distributed as p for children
+    chosen by any rule that does not look at the uniforms - the tree's top-k
+    expansion included.  head_logits are not read.
+
+    Either way the bonus is the inverse-CDF draw of the final p with
+    U[depth, topk]."""
     node, path, d = 0, [], 0
     while True:
         p = torch.softmax(target_logits[node].float(), 0)
         kids = tree.children[node]
-        if kids:
+        if kids and rule == RULE_DRAFT:
             q = torch.softmax(head_logits[tree.head_row[node]].float(), 0)
         nxt = None
         for i, c in enumerate(kids):
             x = tree.tokens[c]
             u = float(U[d, i])
+            if rule == RULE_TARGET:
+                if u < float(p[x]):
+                    nxt = c
+                    break
+                p = p.clone()
+                p[x] = 0
+                p = p / p.sum()
+                continue
             if u * float(q[x]) < float(p[x]):
                 nxt = c
                 break

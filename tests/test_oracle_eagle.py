@@ -2,6 +2,7 @@
 tree verify == chain verify, rejection-sampling properties, KV compaction."""
 import math
 
+import pytest
 import torch
 
 from conftest import load_golden
@@ -160,3 +161,86 @@ def test_kv_compaction_equals_sequential_decode():
     a = len(path)
     for kc, sc in zip(tgt.k_caches, seq.k_caches):
         assert (kc[0, :, :L + a + 1] - sc[0, :, :L + a + 1]).abs().max().item() <= 1e-5
+
+
+def _one_level_tree(children_tokens):
+    """Root 0 with the given child tokens (draft-rank order), no deeper nodes."""
+    n = len(children_tokens)
+    return oe.Tree([0] + list(children_tokens), [-1] + [0] * n, [0] + [1] * n,
+                   [1] + [1 | (1 << (i + 1)) for i in range(n)], [0] + [-1] * n,
+                   [list(range(1, n + 1))] + [[] for _ in range(n)])
+
+
+def _first_token(path, bonus, tree):
+    return tree.tokens[path[0]] if path else bonus
+
+
+def _chi2(counts, p):
+    n = counts.sum()
+    return (((counts - n * p) ** 2) / (n * p)).sum().item()
+
+
+# chi-square thresholds at ~0.001 for V-1 degrees of freedom
+CHI2_999 = {5: 20.5, 7: 24.3}
+
+
+def _dists(V, seed):
+    g = torch.Generator().manual_seed(seed)
+    # skewed, unequal target and draft distributions over a tiny vocabulary
+    pl = torch.randn(V, generator=g) * 1.5
+    ql = torch.randn(V, generator=g) * 1.5
+    return pl, ql, torch.softmax(pl, 0), torch.softmax(ql, 0), g
+
+
+@pytest.mark.parametrize("k,seed", [(1, 1), (3, 2), (4, 3)])
+def test_draft_rule_is_lossless_for_children_drawn_from_q(k, seed):
+    """Recursive rejection sampling with k children drawn from q without
+    replacement: the first emitted token (the accepted child, or the bonus
+    from the residual p) is distributed as p (chi-square over 30000 trials)."""
+    V = 6
+    pl, ql, p, q, g = _dists(V, seed)
+    n = 30000
+    counts = torch.zeros(V)
+    U = torch.rand(n, 2, k + 1, generator=g)
+    for i in range(n):
+        kids = torch.multinomial(q, k, replacement=False, generator=g).tolist()
+        tr = _one_level_tree(kids)
+        tl = pl.expand(k + 1, V)
+        path, bonus = oe.accept_tree_rejection(tr, tl, ql.unsqueeze(0), U[i], topk=k, rule=oe.RULE_DRAFT)
+        counts[_first_token(path, bonus, tr)] += 1
+    assert _chi2(counts, p) < CHI2_999[V - 1]
+
+
+@pytest.mark.parametrize("k,seed", [(1, 4), (3, 5), (4, 6)])
+def test_target_rule_is_lossless_for_top_k_children(k, seed):
+    """The target-only rule with the tree's deterministic top-k children of
+    q: the first emitted token is distributed as p."""
+    V = 8
+    pl, ql, p, q, g = _dists(V, seed)
+    kids = oe.topk_desc(ql, k).tolist()
+    tr = _one_level_tree(kids)
+    tl = pl.expand(k + 1, V)
+    n = 30000
+    counts = torch.zeros(V)
+    U = torch.rand(n, 2, k + 1, generator=g)
+    for i in range(n):
+        path, bonus = oe.accept_tree_rejection(tr, tl, ql.unsqueeze(0), U[i], topk=k, rule=oe.RULE_TARGET)
+        counts[_first_token(path, bonus, tr)] += 1
+    assert _chi2(counts, p) < CHI2_999[V - 1]
+
+
+def test_draft_rule_with_top_k_children_is_not_lossless():
+    """Why the target-only rule exists: the draft rule assumes its children
+    were drawn from q; with the tree's top-k children its output is biased
+    away from p (here measurably, far beyond the chi-square bound)."""
+    V, k = 6, 2
+    pl, ql, p, q, g = _dists(V, 7)
+    kids = oe.topk_desc(ql, k).tolist()
+    tr = _one_level_tree(kids)
+    n = 30000
+    counts = torch.zeros(V)
+    U = torch.rand(n, 2, k + 1, generator=g)
+    for i in range(n):
+        path, bonus = oe.accept_tree_rejection(tr, pl.expand(k + 1, V), ql.unsqueeze(0), U[i], topk=k)
+        counts[_first_token(path, bonus, tr)] += 1
+    assert _chi2(counts, p) > 10 * CHI2_999[V - 1]

@@ -93,6 +93,7 @@ SIGNATURES = {
     "tsds_gather_shards": (_I, [_P, _P, _I, _I, _I, _P]),
     "tsds_fused_layer_workspace_bytes": (_Z, [_I]),
     "tsds_fused_layer_workspace_header_bytes": (_Z, []),
+    "tsds_fused_layer_grid": (_I, [_I, _P]),
     "tsds_fused_layer": (_I, [_P, _I, _I, _P, _P, _P, _Z, _P]),
     "tsds_peer_buffer_bytes": (_Z, [_I, _Z]),
     "tsds_peer_slot_offset": (_Z, [_I, _I]),

@@ -897,6 +897,40 @@ extern "C" size_t tsds_fused_layer_workspace_bytes(int M) {
 // The status word and the counters (see tsds_linear_workspace_header_bytes).
 extern "C" size_t tsds_fused_layer_workspace_header_bytes(void) { return 64 + (size_t)CH_MAX_COUNTERS * sizeof(int); }
 
+// The grid the fused kernel takes for M token rows under the current tuning
+// switches: out[0] CTAs, out[1] CTAs per weight tile (1, or 2 for pairs),
+// out[2] pipeline stages, out[3] CTAs per SM requested.  The same arithmetic
+// as tsds_fused_layer below (a test and tuning aid).
+extern "C" int tsds_fused_layer_grid(int M, int32_t* out) {
+  TSDS_RETURN_IF(!out || M <= 0 || M > 256, TSDS_E_INVALID);
+  const int npad = (M + 15) / 16 * 16;
+  const int tmem_cols = pow2_at_least(npad);
+  int ctas = tsds_tc_ctas_setting();
+  while (ctas > 1 && 2 * tmem_cols * ctas > 512) --ctas;
+  const int pr = tsds_tc_pair_rows();
+  const int CG = (pr > 0 && M >= pr) ? 2 : 1;
+  const int b_stage_bytes = npad / CG * BK * 2;
+  int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
+  if (budget > CH_SMEM_BUDGET) budget = CH_SMEM_BUDGET;
+  int stages = (budget - 1024) / (A_STAGE + b_stage_bytes);
+  if (stages > MAX_STAGES) stages = MAX_STAGES;
+  TSDS_RETURN_IF(stages < 2, TSDS_E_UNSUPPORTED);
+  const size_t smem = (size_t)stages * (A_STAGE + b_stage_bytes) + 1024;
+  static tsds_device_flags attr1, attr2;
+  const int st = CG == 2 ? tsds_smem_limit_once(fused_layer_kernel<2>, CH_SMEM_BUDGET, attr2)
+                         : tsds_smem_limit_once(fused_layer_kernel<1>, CH_SMEM_BUDGET, attr1);
+  if (st != TSDS_OK) return st;
+  int P = tsds_tc_num_sms() * ctas;
+  const int resident = resident_ctas(CG, smem) / CG * CG;
+  TSDS_RETURN_IF(resident < CG, TSDS_E_UNSUPPORTED);
+  if (resident < P) P = resident;
+  out[0] = P;
+  out[1] = CG;
+  out[2] = stages;
+  out[3] = ctas;
+  return TSDS_OK;
+}
+
 extern "C" int tsds_fused_layer(const tsds_fused_phase* phases, int n_phases, int M, const tsds_qk_rope* qr,
                                 const tsds_peer_group* peers, void* workspace, size_t workspace_bytes,
                                 tsds_stream_t stream) {
