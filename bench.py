@@ -62,12 +62,18 @@ def _args():
     ap.add_argument("--kv-len", type=int, default=4096, help="attention mode: keys per sequence")
     ap.add_argument("--greedy", action="store_true", help="eagle mode: greedy acceptance instead of sampling")
     ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--sub-batch", type=int, default=8,
+                    help="also measure this batch size over the same weights and report it as the line's "
+                         "sub_batch record (0: off; skipped when equal to --batch)")
     # smaller depth for profiler captures only (never for reported numbers)
     ap.add_argument("--target-layers", type=int, default=None)
     ap.add_argument("--draft-layers", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
+    ap.add_argument("--smem-slots", type=int, default=None,
+                    help="shared-memory slots per SM the tcgen05 GEMM pipeline is sized for (library default 0: "
+                         "its CTAs per SM; one more leaves room for the next kernel's first CTAs)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--dp-rows", type=int, default=None,
                     help="token rows from which a tcgen05 projection with at least one whole weight tile per CTA "
@@ -101,8 +107,13 @@ def _args():
 
 
 METRIC = "Qwen3-32B spec-decode tok/s at B={B} ({n} GPU); verify-step us"
-# (hidden, intermediate, rows) -> dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch
-MEASURED_TRAFFIC = {(5120, 25600, 26): 541.7e6}   # profiles/tc_gemm_gate_up_qwen3_32b_m26.md
+# samples of the CPU estimate in the device arm's cpu_baseline (the reference
+# arm takes --steps of them, with the same median estimator)
+CPU_REPS = 5
+# (hidden, intermediate, rows) -> DRAM read + write bytes per launch of the
+# target's gate/up GEMM at that shape, from an ncu capture of the kernel
+# (dram__bytes_read.sum + dram__bytes_write.sum): 1.03x the algorithmic bytes
+MEASURED_TRAFFIC = {(5120, 25600, 26): 541.7e6}
 DATA = "synthetic: seeded uniform prompt ids, random-init N(0,0.02) weights (no checkpoint offline)"
 
 
@@ -231,9 +242,13 @@ class CpuCycle:
             t_head = time.perf_counter() - t0
         return t_layer, t_head
 
-    def seconds(self) -> float:
+    def sample(self) -> tuple:
+        """Time one bounded sample; returns (projected full-cycle seconds,
+        sample wall seconds).  The projection scales each timed layer by
+        its model's layer count (and the draft by its K steps)."""
         import torch
         B, K, P = self.a.batch, self.a.k, self.a.prompt
+        w0 = time.perf_counter()
         if self.a.mode == "eagle":
             st, ids, n_layers = self.models["target"]
             t_layer, t_head = self._time(st, ids, 26, P, B)
@@ -246,13 +261,28 @@ class CpuCycle:
                     t_fc = time.perf_counter() - t0
                 h_layer, h_head = self._time(st, ids, T, P, B)
                 total += t_fc + h_layer + h_head
-            return total
+            return total, time.perf_counter() - w0
         total = 0.0
         for name, (st, ids, n_layers) in self.models.items():
             T = K + 1 if name == "target" else 1
             t_layer, t_head = self._time(st, ids, T, P, B)
             total += t_layer * n_layers + t_head if name == "target" else (t_layer * n_layers + t_head) * K
-        return total
+        return total, time.perf_counter() - w0
+
+    def estimate(self, reps: int, warm: int = 1) -> tuple:
+        """Median projected cycle seconds and median sample wall seconds over
+        `reps` samples after `warm` untimed ones: the same estimator for the
+        device arm's cpu_baseline and the reference arm."""
+        for _ in range(warm):
+            self.sample()
+        runs = [self.sample() for _ in range(max(1, reps))]
+        return statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)
+
+    def scale(self) -> dict:
+        if self.a.mode == "eagle":
+            return {"target_layers_per_timed_layer": self.models["target"][2], "head_passes": 5}
+        return {"target_layers_per_timed_layer": self.models["target"][2],
+                "draft_layers_per_timed_layer": self.models["draft"][2], "draft_steps": self.a.k}
 
 
 # ---------------------------------------------------------------------------
@@ -267,20 +297,19 @@ def run_reference(a, rank: int, world: int):
         return
     cc = CpuCycle(a)
     threads, sample = cc.threads, cc.sample
-    times = []
-    for i in range(a.warmup + a.steps):
-        t = cc.seconds()
-        if i >= a.warmup:
-            times.append(t)
-    cyc = statistics.mean(times)
+    # one step = one bounded sample (one layer of each model, the LM heads,
+    # the head passes); the cycle is projected from it by the layer counts
+    cyc, sample_s = cc.estimate(a.steps, warm=a.warmup)
     # tokens per cycle: one per sequence (the bonus) plus accepted drafts; with
     # independent random-init models the acceptance is ~0 (measured on the device arm)
     tok_s = a.batch / cyc
     line = {"impl": "reference", "metric": METRIC.format(B=a.batch, n=world), "value": tok_s, "unit": "tok/s",
-            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": cyc * 1e3,
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": sample_s * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": {"workload": _workload(a), "global_batch": a.batch, "seq_len": a.prompt,
                        "parallelism": "cpu"},
+            "projection": {"sample_ms": sample_s * 1e3, "projected_cycle_ms": cyc * 1e3, "scale": cc.scale(),
+                           "estimator": f"median of {a.steps} samples after {a.warmup} untimed"},
             "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -468,23 +497,19 @@ def run_gemm(a):
     lc0 = _lib.query("tsds_launch_count")
     out, tot_b, tot_us = {}, 0, 0.0
     for name, (fn, wel, kin, kout) in projs.items():
-        for L in layers[:3]:
-            fn(L)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
+        # one pass over the layers' weights as a CUDA graph (host launch cost
+        # out of the timing, launches back to back as in the cycle's graph)
+        def one_pass(fn=fn):
             for L in layers:
                 fn(L)
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * nl)
+        us_pass, _ = _graph_time_us(one_pass, reps=reps)
+        us = us_pass / nl
         nbytes = 2 * wel + 2 * M * (kin + kout) + (2 * M * kout if name in ("o", "down") else 0)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[name] = {"us": round(us, 2), "bytes": nbytes, "gb_s": round(gbs, 1), "frac": round(gbs / peak, 3)}
         tot_b += nbytes
         tot_us += us
-    launches = _lib.query("tsds_launch_count") - lc0
+    launches = (_lib.query("tsds_launch_count") - lc0) // 2 * reps   # eager warm-up + capture, then replays
     layer_gbs = tot_b / (tot_us * 1e-6) / 1e9
     lib = _lib.load()
     line = {"metric": "decode-layer projections GB/s", "value": layer_gbs, "unit": "GB/s", "n_gpus": 1,
@@ -504,80 +529,51 @@ def run_gemm(a):
     print(json.dumps(line), flush=True)
 
 
-def run_tsds(a, rank: int, world: int, local_rank: int):
-    import torch
-    import torch.distributed as dist
-    from dataclasses import replace
-    from tri_sds_b200 import _lib
+def _build_engine(a, B, tshape, dshape, dev, rank, world, comm, peer, share=None):
+    """Target (+ EAGLE head or draft model) and engine for B sequences;
+    `share` = an earlier (target, head_or_draft) whose weights to reuse."""
     from tri_sds_b200.engine import SpecEngine
     from tri_sds_b200.model import QwenModel
-    from tri_sds_b200.shapes import QWEN3_32B, QWEN3_4B
-    from tri_sds_b200.sglang_compat import ScheduleBatch
-    from tri_sds_b200.worker import TriSDSWorker
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    B, K, P = a.batch, a.k, a.prompt
-    if a.gemv_max_rows is not None:
-        _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
-    if a.gemv_splitk:
-        _lib.load().tsds_set_gemv_splitk(1)
-    if a.ctas_per_sm is not None:
-        _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
-    if a.no_pdl:
-        _lib.load().tsds_set_pdl(0)
-    if a.pair_rows is not None:
-        _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
-    if a.dp_rows is not None:
-        _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
-    if a.dp_slack is not None:
-        _lib.load().tsds_set_gemm_dp_slack(a.dp_slack)
-    if a.attn_tc:
-        _lib.load().tsds_set_attention_tc(a.attn_tc)
-    tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
-    dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
+    K, P = a.k, a.prompt
     per_cycle = 7 if a.mode == "eagle" else K + 1        # most tokens a cycle can commit
     rows_verify = B * 26 if a.mode == "eagle" else B * (K + 1)
     max_seq = P + (3 * a.warmup + 2 * a.steps + a.breakdown) * per_cycle + 64 + 32
     max_seq = (max_seq + 63) // 64 * 64
-    # N > 1: the target is tensor-parallel over all ranks (shards drawn per
-    # rank; replicated tensors from the same seed on every rank)
-    comm = peer = None
-    if world > 1:
-        from tri_sds_b200.tp import Comm, PeerAllReduce
-        comm = Comm()
-        if a.allreduce == "peer":
-            # with an exchange region for the vocab-parallel LM head's gathers
-            from tri_sds_b200.tp import lm_exchange_layout
-            peer = PeerAllReduce(rank, world, rows_verify * tshape.hidden,
-                                 exchange_bytes=lm_exchange_layout(rows_verify, tshape.vocab // world)[2])
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
-                       tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers, split_keys=a.attn_split)
+                       tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers, split_keys=a.attn_split,
+                       share_weights=None if share is None else share[0])
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
-        head = EagleHead(target, B, seed=2000)
-        engine = EagleEngine(target, head, greedy=a.greedy, seed=3000)
+        head = EagleHead(target, B, seed=2000, share=None if share is None else share[1])
+        return target, head, EagleEngine(target, head, greedy=a.greedy, seed=3000), rows_verify
+    if a.draft_tp and world > 1:
+        # sharded like the target over the same ranks (and peer group)
+        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_rank=rank,
+                          tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers,
+                          split_keys=a.attn_split, share_weights=None if share is None else share[1])
     else:
-        if a.draft_tp and world > 1:
-            # sharded like the target over the same ranks (and peer group)
-            draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_rank=rank,
-                              tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers,
-                              split_keys=a.attn_split)
-        else:
-            draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
-                              tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split)
-        engine = SpecEngine(target, draft, K)
-    # the same prompt on every rank: tensor-parallel ranks process the same tokens
-    prompt = torch.randint(0, tshape.vocab, (B, P), generator=torch.Generator().manual_seed(7))
-    lc0 = _lib.query("tsds_launch_count")
-    engine.prepare(prompt)
-    launches_per_cycle = None
+        draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
+                          tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split,
+                          share_weights=None if share is None else share[1])
+    return target, draft, SpecEngine(target, draft, K), rows_verify
+
+
+def _measure_engine(a, B, engine, target, other, rank, world, local_rank, dev, tshape, e2e_steps):
+    """Device-timed cycles (inputs resident), the verify step alone and the
+    end-to-end worker path with host buffers, for one engine.  Returns a dict
+    (every rank takes the same collective steps)."""
+    import torch
+    import torch.distributed as dist
+    from tri_sds_b200 import _lib
+    from tri_sds_b200.sglang_compat import ScheduleBatch
+    from tri_sds_b200.worker import TriSDSWorker
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # ---- device-timed cycles (inputs resident in HBM) -------------------------
+    prompt = torch.randint(0, tshape.vocab, (B, a.prompt), generator=torch.Generator().manual_seed(7))
+    engine.prepare(prompt)
     hist = torch.zeros(a.warmup + a.steps, B, dtype=torch.int32, device=dev)
     for i in range(a.warmup):
         engine.step()
@@ -597,21 +593,19 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     barrier()
     ms = ev0.elapsed_time(ev1)
     # a device wait that gave up (status word set) invalidates the run: fail loudly
-    for mdl in (target, head.model if a.mode == "eagle" else draft):
+    for mdl in (target, other.model if a.mode == "eagle" else other):
         mdl.check_status()
     acc = hist[a.warmup:].float().cpu()
     tokens = float((acc + 1).sum())
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    # the ranks serve the same B sequences together: tokens are counted once
-    ms_max, tokens_all = float(t[0]), tokens
-    value = tokens_all / (ms_max / 1e3)
-    launches_per_cycle = engine.plan_launches
+    ms_max = float(t[0])
+    out = {"value": tokens / (ms_max / 1e3), "ms_per_step": ms_max / a.steps, "tokens": tokens,
+           "accept_len_mean": float(acc.mean()), "clocks": clocks.summary(),
+           "gpu_launches": engine.plan_launches * a.steps}
 
-    breakdown = plan_breakdown(engine.plan, a.breakdown) if a.breakdown > 0 else None
-
-    # ---- verify step alone (target forward over K+1 tokens) ------------------
+    # ---- verify step alone (target forward over the verify rows) -----------
     vplan = engine.verify_only_plan()
     vplan.run()
     g = torch.cuda.CUDAGraph()
@@ -627,34 +621,14 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         g.replay()
     e1.record()
     torch.cuda.synchronize()
-    verify_us = e0.elapsed_time(e1) * 1e3 / nv
+    vt = torch.tensor([e0.elapsed_time(e1) * 1e3 / nv], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vt, op=dist.ReduceOp.MAX)
+    out["verify_step_us"] = float(vt[0])
     del g
 
-    # ---- dominant kernel: the target's gate/up + SiLU projection -------------
-    from tri_sds_b200 import ops
-    M = rows_verify
-    xin = torch.randn(M, tshape.hidden, device=dev).to(torch.bfloat16)
-    hout = torch.empty(M, tshape.intermediate, dtype=torch.bfloat16, device=dev)
-    for L in target.layers[:2]:
-        ops.linear_swiglu(xin, L.w_gu, out=hout)
-    torch.cuda.synchronize()
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0.record()
-    for L in target.layers:
-        ops.linear_swiglu(xin, L.w_gu, out=hout)
-    k1.record()
-    torch.cuda.synchronize()
-    kern_us = k0.elapsed_time(k1) * 1e3 / len(target.layers)
-    kbytes = target.layers[0].w_gu.numel() * 2 + xin.numel() * 2 + hout.numel() * 2
-    peak, peak_kind = _peaks()
-    achieved = kbytes / (kern_us * 1e-6) / 1e9
-    # DRAM read+write bytes per launch of this kernel at this shape, from the
-    # ncu capture summarised in profiles/ (None where no capture exists)
-    traffic = MEASURED_TRAFFIC.get((tshape.hidden, tshape.intermediate, M)) if world == 1 else None
-
-    # ---- end to end through the worker API (host buffers) --------------------
-    e2e = None
-    if not a.no_e2e:
+    # ---- end to end through the worker API (host buffers) ------------------
+    if e2e_steps > 0:
         os.environ["SDS_ENABLED"] = "1"
         worker = TriSDSWorker()
         worker.attach_engine(engine)
@@ -666,7 +640,7 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         barrier()
         t0 = time.perf_counter()
         e_tokens = 0
-        for _ in range(a.steps):
+        for _ in range(e2e_steps):
             toks, n = worker.forward_batch_generation(ScheduleBatch(input_ids=cur_host))
             cur_host = toks.gather(1, n.long().unsqueeze(1))
             e_tokens += int(n.sum()) + B
@@ -675,24 +649,132 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         if world > 1:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             el = float(tt[0])
-        e2e = {"value": e_tokens / el, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
-               "d2h_bytes_per_step": engine.tokens.numel() * 8 + 4 * B}
+        out["e2e"] = {"value": e_tokens / el, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
+                      "d2h_bytes_per_step": engine.tokens.numel() * 8 + 4 * B}
+    return out
+
+
+def _cycle_bytes(a, tshape, B, world, target) -> float:
+    """Algorithmic HBM bytes of one cycle on one rank: every weight the cycle
+    streams once (target layers + LM head, and the EAGLE head's fc + layer +
+    LM head per pass, or the draft model's K steps) plus the verify's K/V
+    reads at the prompt length."""
+    L0 = target.layers[0]
+    layer_b = sum(t.numel() * 2 for t in (L0.w_qkv, L0.w_o, L0.w_gu, L0.w_d))
+    lm_b = target.lm_head_w.numel() * 2
+    kv_row = 2 * target.k_cache.shape[2] * tshape.head_dim * 2   # K + V of one token, one layer, this rank
+    verify = tshape.n_layers * (layer_b + B * a.prompt * kv_row) + lm_b
+    if a.mode == "eagle":
+        fc_b = 2 * tshape.hidden * tshape.hidden * 2
+        return verify + 5 * (fc_b + layer_b + lm_b)
+    return verify
+
+
+def run_tsds(a, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    from dataclasses import replace
+    from tri_sds_b200 import _lib
+    from tri_sds_b200.shapes import QWEN3_32B, QWEN3_4B
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B = a.batch
+    if a.gemv_max_rows is not None:
+        _lib.load().tsds_set_gemv_max_rows(a.gemv_max_rows)
+    if a.gemv_splitk:
+        _lib.load().tsds_set_gemv_splitk(1)
+    if a.ctas_per_sm is not None:
+        _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
+    if a.smem_slots is not None:
+        _lib.load().tsds_set_gemm_smem_slots(a.smem_slots)
+    if a.no_pdl:
+        _lib.load().tsds_set_pdl(0)
+    if a.pair_rows is not None:
+        _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
+    if a.dp_rows is not None:
+        _lib.load().tsds_set_gemm_dp_rows(a.dp_rows)
+    if a.dp_slack is not None:
+        _lib.load().tsds_set_gemm_dp_slack(a.dp_slack)
+    if a.attn_tc:
+        _lib.load().tsds_set_attention_tc(a.attn_tc)
+    tshape = QWEN3_32B if a.target_layers is None else replace(QWEN3_32B, n_layers=a.target_layers)
+    dshape = QWEN3_4B if a.draft_layers is None else replace(QWEN3_4B, n_layers=a.draft_layers)
+    sub_B = a.sub_batch if (a.sub_batch and a.sub_batch != B) else 0
+    rows_max = max(B, sub_B) * (26 if a.mode == "eagle" else a.k + 1)
+    # N > 1: the target is tensor-parallel over all ranks (shards drawn per
+    # rank; replicated tensors from the same seed on every rank)
+    comm = peer = None
+    if world > 1:
+        from tri_sds_b200.tp import Comm, PeerAllReduce
+        comm = Comm()
+        if a.allreduce == "peer":
+            # with an exchange region for the vocab-parallel LM head's gathers
+            from tri_sds_b200.tp import lm_exchange_layout
+            peer = PeerAllReduce(rank, world, rows_max * tshape.hidden,
+                                 exchange_bytes=lm_exchange_layout(rows_max, tshape.vocab // world)[2])
+    target, other, engine, rows_verify = _build_engine(a, B, tshape, dshape, dev, rank, world, comm, peer)
+    res = _measure_engine(a, B, engine, target, other, rank, world, local_rank, dev, tshape,
+                          0 if a.no_e2e else a.steps)
+    breakdown = plan_breakdown(engine.plan, a.breakdown) if a.breakdown > 0 else None
+    peak, peak_kind = _peaks()
+    cycle_b = _cycle_bytes(a, tshape, B, world, target)
+
+    # ---- dominant kernel: the target's gate/up + SiLU projection -------------
+    from tri_sds_b200 import ops
+    M = rows_verify
+    xin = torch.randn(M, tshape.hidden, device=dev).to(torch.bfloat16)
+    hout = torch.empty(M, target.lshape.intermediate, dtype=torch.bfloat16, device=dev)
+    for L in target.layers[:2]:
+        ops.linear_swiglu(xin, L.w_gu, out=hout)
+    torch.cuda.synchronize()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for L in target.layers:
+        ops.linear_swiglu(xin, L.w_gu, out=hout)
+    k1.record()
+    torch.cuda.synchronize()
+    kern_us = k0.elapsed_time(k1) * 1e3 / len(target.layers)
+    kbytes = target.layers[0].w_gu.numel() * 2 + xin.numel() * 2 + hout.numel() * 2
+    achieved = kbytes / (kern_us * 1e-6) / 1e9
+    # DRAM read + write bytes per launch of this kernel at this shape from an
+    # ncu capture of it (None where none was taken): the traffic-to-algorithmic
+    # ratio, not a number of this run
+    traffic = MEASURED_TRAFFIC.get((tshape.hidden, tshape.intermediate, M)) if world == 1 else None
+
+    # ---- a second batch size over the same weights ---------------------------
+    sub = None
+    if sub_B:
+        engine.graph = None
+        t2, o2, eng2, _ = _build_engine(a, sub_B, tshape, dshape, dev, rank, world, comm, peer,
+                                        share=(target, other))
+        r2 = _measure_engine(a, sub_B, eng2, t2, o2, rank, world, local_rank, dev, tshape,
+                             0 if a.no_e2e else a.steps)
+        cb2 = _cycle_bytes(a, tshape, sub_B, world, t2)
+        sub = {"global_batch": sub_B, "value": r2["value"], "unit": "tok/s", "ms_per_step": r2["ms_per_step"],
+               "verify_step_us": r2["verify_step_us"], "accept_len_mean": r2["accept_len_mean"],
+               "e2e": r2.get("e2e"), "gpu_launches": r2["gpu_launches"], "clocks": r2["clocks"],
+               "cycle_hbm_frac": cb2 / (r2["ms_per_step"] * 1e-3) / 1e9 / peak}
+        eng2.graph = None
+        torch.cuda.synchronize()
 
     # ---- CPU baseline (rank 0, N=1) ------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cc = CpuCycle(a)
-        cyc = statistics.mean(cc.seconds() for _ in range(3))
-        mean_tok = tokens / a.steps
+        cyc, sample_s = cc.estimate(CPU_REPS, warm=1)
+        mean_tok = res["tokens"] / a.steps
         cpu = {"value": mean_tok / cyc, "unit": "tok/s", "cores": cc.threads, "kind": "port",
-               "sample": cc.sample + f"; {mean_tok:.2f} tokens per cycle as measured on the device"}
+               "sample": cc.sample + f"; {mean_tok:.2f} tokens per cycle as measured on the device",
+               "sample_ms": sample_s * 1e3, "projected_cycle_ms": cyc * 1e3, "scale": cc.scale(),
+               "estimator": f"median of {CPU_REPS} samples after 1 untimed"}
 
     if rank == 0:
         line = {
-            "metric": METRIC.format(B=B, n=world), "value": value, "unit": "tok/s", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True,
+            "metric": METRIC.format(B=B, n=world), "value": res["value"], "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
-            "config": {"workload": _workload(a), "global_batch": B, "seq_len": P,
+            "config": {"workload": _workload(a), "global_batch": B, "seq_len": a.prompt,
                        "parallelism": f"tp{world}", "allreduce": a.allreduce if world > 1 else None,
                        "draft_parallelism": (None if a.mode == "eagle" else
                                              f"tp{world}" if a.draft_tp and world > 1 else "replicated"),
@@ -700,23 +782,29 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
                        "l2": "no flush: 73 GB of weights per cycle >> 126 MB L2",
                        "mode": a.mode, "target_layers": tshape.n_layers,
                        "draft_layers": 0 if a.mode == "eagle" else dshape.n_layers},
-            "verify_step_us": verify_us,
-            "accept_len_mean": float(acc.mean()),
+            "verify_step_us": res["verify_step_us"],
+            "accept_len_mean": res["accept_len_mean"],
             "roofline": {"bound": "hbm", "kernel": "tsds_linear_swiglu (target gate/up, M=%d)" % M,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": kbytes,
-                         "launch_us": kern_us},
+                         "peak_kind": peak_kind, "traffic": traffic, "traffic_source": "ncu capture, not this run",
+                         "bytes_per_launch": kbytes, "launch_us": kern_us,
+                         "cycle": {"bytes_per_cycle": cycle_b,
+                                   "achieved": cycle_b / (res["ms_per_step"] * 1e-3) / 1e9,
+                                   "frac": cycle_b / (res["ms_per_step"] * 1e-3) / 1e9 / peak}},
             "cpu_baseline": cpu,
-            "e2e": e2e,
-            "clocks": clocks.summary(),
-            "gpu_launches": launches_per_cycle * a.steps,
+            "e2e": res.get("e2e"),
+            "clocks": res["clocks"],
+            "gpu_launches": res["gpu_launches"],
             "gemv_max_rows": _lib.load().tsds_get_gemv_max_rows(),
             "gemv_splitk": _lib.load().tsds_get_gemv_splitk(),
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
             "gemm_dp_rows": _lib.load().tsds_get_gemm_dp_rows(),
             "gemm_dp_slack": _lib.load().tsds_get_gemm_dp_slack(),
+            "gemm_smem_slots": _lib.load().tsds_get_gemm_smem_slots(),
             "attention": {"tcgen05": _lib.load().tsds_get_attention_tc(), "split_keys": a.attn_split},
         }
+        if sub is not None:
+            line["sub_batch"] = sub
         if breakdown is not None:
             line["breakdown"] = breakdown
         print(json.dumps(line), flush=True)
@@ -724,7 +812,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     engine.graph = None
     torch.cuda.synchronize()
     if peer is not None:
-        barrier()   # no rank reads a peer buffer any more
+        if world > 1:
+            dist.barrier()   # no rank reads a peer buffer any more
         peer.close()
 
 
@@ -751,6 +840,10 @@ def main():
             if world > 1:
                 raise SystemExit("--mode attention / layer / gemm run on one GPU")
             from tri_sds_b200 import _lib
+            if a.ctas_per_sm is not None:
+                _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
+            if a.smem_slots is not None:
+                _lib.load().tsds_set_gemm_smem_slots(a.smem_slots)
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
             if a.dp_rows is not None:

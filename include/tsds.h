@@ -151,6 +151,13 @@ int tsds_get_gemv_splitk(void);
 /* Resident CTAs per SM of the tcgen05 GEMM (1..4, default 2; lowered
  * automatically when the accumulators would not fit in TMEM).  Tuning knob. */
 void tsds_set_gemm_ctas_per_sm(int n);
+/* Shared-memory slots per SM the tcgen05 GEMM's pipeline is sized for
+ * (0..4; 0, the default: its CTAs per SM).  A value above the CTAs per SM
+ * leaves room on each SM for a CTA of the next kernel, which under
+ * programmatic dependent launch starts streaming its weights while this one
+ * drains.  Tuning knob; no counterpart in the reference. */
+void tsds_set_gemm_smem_slots(int n);
+int tsds_get_gemm_smem_slots(void);
 /* Token rows M from which the tcgen05 GEMM runs on CTA pairs (two SMs per
  * 256-row weight tile, tcgen05 cta_group::2, each SM staging half of the
  * token rows; not the LM head); 0 (default): never.  Process-wide tuning
@@ -473,6 +480,14 @@ int tsds_peer_lm_gather(void* const* bufs, int rank, int tp, int max_elems, size
  *   (child == target argmax).  Writes path node indices, accept lengths,
  *   emitted tokens (accepted + bonus, -1 padded) and cur <- bonus.
  *   scratch: unused (nothing of vocabulary size is stored); may be NULL.
+ *   The emitted token is distributed as p when the children were drawn
+ *   from q without replacement.
+ * tsds_accept_tree_rule: the same walk with the rule chosen per call:
+ *   TSDS_ACCEPT_DRAFT (0) is tsds_accept_tree's; TSDS_ACCEPT_TARGET (1)
+ *   takes the draft as deterministic (q one-hot on each child in turn):
+ *   accept child x if U < p(x); else p <- p without x, renormalised; bonus
+ *   by inverse CDF.  It is lossless for children chosen without looking at
+ *   U - the tree's top-k expansion - and reads no head logits (may be NULL).
  * tsds_tree_commit: move the accepted nodes' K/V rows L + path[j] -> L+1+j
  *   in every layer, copy the last accepted node's hidden state to
  *   root_feat, then lengths += accept_len + 1.
@@ -495,6 +510,11 @@ int tsds_accept_tree(const void* target_logits, const int64_t* target_argmax, co
                      const int64_t* ids, const int32_t* hrow, const int32_t* children, const float* U,
                      float* scratch, int32_t* path, int32_t* accept_len, int64_t* tokens, int64_t* cur,
                      int B, int n_nodes, int V, int k, int depth, tsds_stream_t stream);
+enum { TSDS_ACCEPT_DRAFT = 0, TSDS_ACCEPT_TARGET = 1 };
+int tsds_accept_tree_rule(const void* target_logits, const int64_t* target_argmax, const void* head_logits,
+                          const int64_t* ids, const int32_t* hrow, const int32_t* children, const float* U,
+                          int rule, int32_t* path, int32_t* accept_len, int64_t* tokens, int64_t* cur, int B,
+                          int n_nodes, int V, int k, int depth, tsds_stream_t stream);
 int tsds_tree_commit(void* k_cache, void* v_cache, int layers, int B, int Hkv, int S, int D,
                      int32_t* lengths, const int32_t* path, const int32_t* accept_len, int depth,
                      const void* hidden, int n_nodes, int N, void* root_feat, tsds_stream_t stream);

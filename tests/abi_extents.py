@@ -63,6 +63,13 @@ def extents(name, a):
         return [(0, B * NN * V * 2), (1, B * NN * 8), (2, V * 2), (3, B * NN * 8), (4, B * NN * 4),
                 (5, B * NN * k * 4), (6, B * (depth + 1) * (k + 1) * 4), (8, B * (depth + 1) * 4), (9, B * 4),
                 (10, B * (depth + 2) * 8), (11, B * 8)]
+    if name == "tsds_accept_tree_rule":
+        tl, ta, hl, ids, hrow, ch, U, rule, path, acc, tokens, cur, B, n_nodes, V, k, depth = a
+        assert rule in (0, 1)
+        NN = n_nodes + 1
+        return [(0, B * NN * V * 2), (1, B * NN * 8), (2, V * 2), (3, B * NN * 8), (4, B * NN * 4),
+                (5, B * NN * k * 4), (6, B * (depth + 1) * (k + 1) * 4), (8, B * (depth + 1) * 4), (9, B * 4),
+                (10, B * (depth + 2) * 8), (11, B * 8)]
     if name == "tsds_tree_commit":
         kc, vc, layers, B, Hkv, S, D, lengths, path, acc, depth, hidden, n_nodes, N, root = a
         return [(0, layers * B * Hkv * S * D * 2), (1, layers * B * Hkv * S * D * 2), (7, B * 4),

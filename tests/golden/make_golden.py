@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden/ from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference`` (override with TSDS_REFERENCE):
+Run where the reference checkout (read-only) is available, naming its
+root in TSDS_REFERENCE:
 
-    python tests/golden/make_golden.py
+    TSDS_REFERENCE=<path of the tri-sds checkout> python tests/golden/make_golden.py
 
 The reference's Python modules are imported unmodified.  Its two
 Triton-only ops cannot launch on a CPU, so they are replaced by torch
@@ -31,7 +31,7 @@ import torch
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("TSDS_REFERENCE", "/root/reference")
+REF = os.environ.get("TSDS_REFERENCE")
 
 
 def _torch_rms_norm(x, weight, eps=1e-6):
@@ -53,6 +53,8 @@ def _torch_attention_gqa(q, k, v, kv_len, q_per_kv):
 
 
 def _import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "tri_sds")):
+        raise SystemExit("set TSDS_REFERENCE to the root of the tri-sds checkout (the directory holding tri_sds/)")
     sys.path.insert(0, REF)
     import tri_sds.triton_kernels.qwen_model as rq
     import tri_sds.triton_kernels.eagle_head as re

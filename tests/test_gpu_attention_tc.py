@@ -190,14 +190,15 @@ def test_tc_prefill_attention_matches_f32(ops, B, P, Hq):
 def test_tc_prefill_matches_sdpa(ops, B, P):
     """Prompt prefill with its attention on the tcgen05 kernel against the
     same prefill on SDPA: layer 0's K/V cache (written before any attention)
-    equal, and the final logits within bf16 tolerance - two bf16 attention
-    implementations round P differently, and two layers of random weights
-    carry that into the hidden state - with the argmax equal wherever the
-    SDPA logits' top two are apart."""
+    equal, and the final logits as close to the fp32 oracle's as SDPA's are
+    (two bf16 attention implementations round P differently, and two layers
+    of random weights carry that into the logits by a few bf16 ulps either
+    way), with the argmax equal wherever the oracle's top two are apart."""
     from tri_sds_b200.model import QwenModel
     from tri_sds_b200.shapes import QwenShape
     kw = dict(hidden=512, n_heads=16, n_kv_heads=2, head_dim=128, intermediate=1024, n_layers=2, vocab=1000)
-    w = oq.random_qwen_weights(oq.QwenShape(**kw), seed=P, std=0.05)
+    oshape = oq.QwenShape(**kw)
+    w = oq.random_qwen_weights(oshape, seed=P, std=0.05)
     m = QwenModel(QwenShape(**kw), batch=B, max_seq=P + 64, max_rows=B * 5, device=DEV, weights=w)
     prompt = torch.randint(0, kw["vocab"], (B, P), generator=torch.Generator().manual_seed(B))
     h_tc = m.prefill(prompt)
@@ -205,13 +206,18 @@ def test_tc_prefill_matches_sdpa(ops, B, P):
     k0_tc = m.k_cache[0].clone()
     ops.set_attention_tc(False)
     h_ref = m.prefill(prompt)
-    lg_ref = m.logits_of(h_ref.reshape(-1, kw["hidden"])).float().cpu()
+    lg_sdpa = m.logits_of(h_ref.reshape(-1, kw["hidden"])).float().cpu()
     ops.set_attention_tc(True)
     assert torch.equal(k0_tc, m.k_cache[0])
-    assert (lg_tc - lg_ref).abs().max().item() <= 5e-2
-    top2 = lg_ref.topk(2, -1).values
-    clear = (top2[:, 0] - top2[:, 1]) > 5e-2
-    assert torch.equal(lg_tc.argmax(-1)[clear], lg_ref.argmax(-1)[clear])
+    ora = oq.QwenOracle(oshape, w, batch=B, max_seq=P + 64, dtype=torch.float32)
+    lg_f32, _ = ora.forward(prompt)
+    lg_f32 = lg_f32.float().reshape(B * P, -1)
+    err_tc = (lg_tc - lg_f32).abs().max().item()
+    err_sdpa = (lg_sdpa - lg_f32).abs().max().item()
+    assert err_tc <= 1.5 * err_sdpa + 1e-2, (err_tc, err_sdpa)
+    top2 = lg_f32.topk(2, -1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * err_sdpa + 2e-2
+    assert torch.equal(lg_tc.argmax(-1)[clear], lg_f32.argmax(-1)[clear])
 
 
 def test_tc_attention_in_the_model(ops):

@@ -1,10 +1,12 @@
 """The fused-layer kernel on the GPU (tsds_fused_layer: O -> RMSNorm -> gate/up
 -> down -> RMSNorm -> q/k/v with QK-norm + RoPE + KV write in one launch).
 
-* Qwen3-4B-shape layers, where every projection has at least as many
-  stream-K iterations as the kernel has CTAs: the fused plan reproduces the
-  per-op plan bit for bit (hidden state, q, K and V caches), since both
-  split and sum every tile the same way and round identically;
+* Qwen3-4B-shape layers: where the fused kernel's grid equals the per-op
+  GEMMs' (tsds_fused_layer_grid vs tsds_tc_gemm_plan), the fused plan
+  reproduces the per-op plan bit for bit (hidden state, q, K and V caches),
+  since both split and sum every tile the same way and round identically;
+  where the grids differ (one fused CTA per SM against the GEMMs' two at
+  small M), to bf16 rounding and the logit tolerance;
 * the small shape of the other GPU tests: logits within the bf16 tolerance
   of the oracle;
 * EAGLE greedy decoding with fused layers equals greedy autoregressive
@@ -99,8 +101,32 @@ def _bitwise_case(B, T):
         m.lengths.copy_(starts.to(DEV))
         logits, am = _verify(m, ids, B, T, oshape.vocab)
         outs.append((m.x[:B * T].clone(), m.q[:B * T].clone(), m.k_cache.clone(), m.v_cache.clone(), logits, am))
-    for a, b, what in zip(outs[0], outs[1], ("hidden", "q", "k cache", "v cache", "logits", "argmax")):
-        assert torch.equal(a, b), what
+    if _same_split(B * T):
+        for a, b, what in zip(outs[0], outs[1], ("hidden", "q", "k cache", "v cache", "logits", "argmax")):
+            assert torch.equal(a, b), what
+        return
+    # a different grid splits the reductions differently: the two plans then
+    # agree to bf16 rounding (hidden / q / caches) and the logits within the
+    # bf16 logit tolerance
+    for a, b, what in zip(outs[0][:4], outs[1][:4], ("hidden", "q", "k cache", "v cache")):
+        a, b = a.float(), b.float()
+        assert (a - b).abs().max().item() <= 3e-2 * max(1.0, a.abs().max().item()), what
+    assert (outs[0][4].float() - outs[1][4].float()).abs().max().item() <= 2e-2
+
+
+def _same_split(M):
+    """True when the fused kernel's grid equals the per-op GEMMs' at M rows,
+    so both plans split and sum every projection the same way."""
+    import ctypes
+    from tri_sds_b200 import _lib
+    out = (ctypes.c_int32 * 8)()
+    assert _lib.load().tsds_fused_layer_grid(M, out) == 0
+    fused_p = out[0]
+    same = True
+    for epi, n, k in ((0, 6144, 2560), (1, 2560, 4096), (2, 9728, 2560), (1, 2560, 9728)):
+        assert _lib.load().tsds_tc_gemm_plan(epi, M, n, k, out) == 0
+        same = same and out[2] == fused_p
+    return same
 
 
 @pytest.mark.parametrize("B,T", [(1, 1), (2, 5), (2, 26)])

@@ -155,7 +155,7 @@ def test_accept_rejection(recorded, greedy):
     path, acc, tokens, bonus = _ops().accept_rejection(_r(B * NN, V), _r(2, V), ids, hrow, children, U, am, depth)
     assert path.shape == (B, depth + 1) and acc.shape == (B,) and tokens.shape == (B, depth + 2)
     assert bonus.shape == (B,)
-    assert recorded.calls == ["tsds_accept_tree"]
+    assert recorded.calls == ["tsds_accept_tree_rule"]
 
 
 def test_accept_rejection_checks_its_indices(recorded):
@@ -172,7 +172,7 @@ def test_accept_rejection_checks_its_indices(recorded):
     bad[0, 1] = 1
     bad[0, 3] = 9            # node 3 is a leaf: its head row is never read
     _ops().accept_rejection(_r(B * NN, V), _r(2, V), ids, bad, children, U, None, depth)
-    assert recorded.calls == ["tsds_accept_tree"]
+    assert recorded.calls == ["tsds_accept_tree_rule"]
 
 
 def _commit_args(depth=2, NN=5, layers=3):

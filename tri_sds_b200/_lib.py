@@ -59,6 +59,8 @@ SIGNATURES = {
     "tsds_set_gemv_splitk": (None, [_I]),
     "tsds_get_gemv_splitk": (_I, []),
     "tsds_set_gemm_ctas_per_sm": (None, [_I]),
+    "tsds_set_gemm_smem_slots": (None, [_I]),
+    "tsds_get_gemm_smem_slots": (_I, []),
     "tsds_set_gemm_pair_rows": (None, [_I]),
     "tsds_get_gemm_pair_rows": (_I, []),
     "tsds_set_gemm_dp_rows": (None, [_I]),
@@ -76,6 +78,7 @@ SIGNATURES = {
     "tsds_tree_step": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P]),
     "tsds_tree_finalize": (_I, [_P, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _P]),
     "tsds_accept_tree": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "tsds_accept_tree_rule": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "tsds_tree_commit": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _I, _P, _P]),
     "tsds_eagle_inputs": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "tsds_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),

@@ -492,9 +492,19 @@ struct AccNode {
   float invQ[MAXK + 1];   // 1 / (1 - sum_{i<l} q_0(x_i)), invQ[0] = 1
 };
 
+// rule ACC_RULE_TARGET takes the draft as deterministic: q_l is one-hot on
+// the child x_l under test, so p_{l+1} = p_l without x_l, renormalised, the
+// acceptance test is u < p_l(x_l), and the head logits are not read.
+constexpr int ACC_RULE_DRAFT = 0, ACC_RULE_TARGET = 1;
+
+template <int RULE>
 __device__ __forceinline__ float acc_p(const AccNode& a, float tj, float hj, int j) {
   float p = expf(tj - a.lse_t);
   if (a.r == 0) return p;
+  if constexpr (RULE == ACC_RULE_TARGET) {
+    for (int l = 0; l < a.r; ++l) p = a.X[l] == j ? 0.f : p * a.invZ[l + 1];
+    return p;
+  }
   const float q0 = expf(hj - a.lse_h);
   bool ex = false;
   for (int l = 0; l < a.r; ++l) {
@@ -505,7 +515,10 @@ __device__ __forceinline__ float acc_p(const AccNode& a, float tj, float hj, int
   return p;
 }
 
-__device__ __forceinline__ float acc_q(const AccNode& a, float hj, int j) {
+// q_r(j) while child x is under test
+template <int RULE>
+__device__ __forceinline__ float acc_q(const AccNode& a, float hj, int j, int x) {
+  if constexpr (RULE == ACC_RULE_TARGET) return j == x ? 1.f : 0.f;
   for (int l = 0; l < a.r; ++l)
     if (a.X[l] == j) return 0.f;
   return expf(hj - a.lse_h) * a.invQ[a.r];
@@ -609,6 +622,7 @@ struct AcceptIO {
 };
 
 // grid (ACC_CL, B): blockIdx.x = rank in the sequence's cluster
+template <int RULE>
 __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io) {
   pdl_wait();
   pdl_trigger();
@@ -649,7 +663,9 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
     const float* u = io.U + ((size_t)b * (io.depth + 1) + d) * (k + 1);
     const bool has_kids = kids[0] >= 0;
     const bf16* trow = io.target_logits + ((size_t)b * NN + node) * V;
-    const bf16* hrow = has_kids ? io.head_logits + (size_t)io.hrow[(size_t)b * NN + node] * V : nullptr;
+    const bf16* hrow = has_kids && RULE == ACC_RULE_DRAFT
+                           ? io.head_logits + (size_t)io.hrow[(size_t)b * NN + node] * V
+                           : nullptr;
     // both log-sum-exps in one pass over this rank's slice, then across the cluster
     float mt = -INFINITY, st = 0.f, mh = -INFINITY, sh = 0.f;
     for_each_strided(trow, hrow, v0, v1, [&](int, float tj, float hj) {
@@ -689,8 +705,8 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
       // rank 0 decides and broadcasts: the ranks' control flow (and so their
       // cluster barriers) cannot diverge
       if (rank == 0 && threadIdx.x == 0) {
-        const float tx = bf2f(trow[xr]), hx = bf2f(hrow[xr]);
-        xch_publish(xch, phase)[0] = u[i] * acc_q(s_node, hx, x) < acc_p(s_node, tx, hx, x) ? 1.f : 0.f;
+        const float tx = bf2f(trow[xr]), hx = hrow ? bf2f(hrow[xr]) : 0.f;
+        xch_publish(xch, phase)[0] = u[i] * acc_q<RULE>(s_node, hx, x, x) < acc_p<RULE>(s_node, tx, hx, x) ? 1.f : 0.f;
       }
       cl.sync();
       const bool acc = xch_remote(cl, xch, phase, 0)[0] != 0.f;
@@ -702,7 +718,7 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
       // rejected: Z_{r+1} over the vocabulary, then record x
       float z = 0.f;
       for_each_strided(trow, hrow, v0, v1, [&](int j, float tj, float hj) {
-        z += fmaxf(acc_p(s_node, tj, hj, j) - acc_q(s_node, hj, j), 0.f);
+        z += fmaxf(acc_p<RULE>(s_node, tj, hj, j) - acc_q<RULE>(s_node, hj, j, x), 0.f);
       });
       z = block_sum(z, red);
       if (threadIdx.x == 0) xch_publish(xch, phase)[0] = z;
@@ -712,7 +728,7 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
       ++phase;
       if (threadIdx.x == 0) {
         const int r = s_node.r;
-        qrem -= expf(bf2f(hrow[xr]) - s_node.lse_h);
+        if (hrow) qrem -= expf(bf2f(hrow[xr]) - s_node.lse_h);
         s_node.invZ[r + 1] = z > 0.f ? 1.0f / z : 0.f;
         s_node.invQ[r + 1] = qrem > 0.f ? 1.0f / qrem : 0.f;
         s_node.X[r] = x;
@@ -735,7 +751,7 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
     float part = 0.f;
     int last = -1;
     for (int j = lo; j < hi; ++j) {
-      const float pj = acc_p(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
+      const float pj = acc_p<RULE>(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
       part += pj;
       if (pj > 0.f) last = j;
     }
@@ -787,7 +803,7 @@ __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1)
       float run = before;
       int pick = hi - 1;
       for (int j = lo; j < hi; ++j) {
-        run += acc_p(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
+        run += acc_p<RULE>(s_node, bf2f(trow[j]), hrow ? bf2f(hrow[j]) : 0.f, j);
         if (run > thr) {
           pick = j;
           break;
@@ -909,18 +925,33 @@ extern "C" int tsds_tree_finalize(const void* states, int n_nodes, int k, const 
   return tsds_launch_status();
 }
 
+extern "C" int tsds_accept_tree_rule(const void* target_logits, const int64_t* target_argmax,
+                                     const void* head_logits, const int64_t* ids, const int32_t* hrow,
+                                     const int32_t* children, const float* U, int rule, int32_t* path,
+                                     int32_t* accept_len, int64_t* tokens, int64_t* cur, int B, int n_nodes, int V,
+                                     int k, int depth, tsds_stream_t stream) {
+  TSDS_RETURN_IF(B <= 0 || n_nodes < 1 || V <= 0 || k < 1 || k > MAXK || depth < 1, TSDS_E_INVALID);
+  TSDS_RETURN_IF(rule != ACC_RULE_DRAFT && rule != ACC_RULE_TARGET, TSDS_E_INVALID);
+  TSDS_RETURN_IF(U != nullptr && !target_logits, TSDS_E_INVALID);
+  TSDS_RETURN_IF(U != nullptr && rule == ACC_RULE_DRAFT && !head_logits, TSDS_E_INVALID);
+  TSDS_RETURN_IF(U == nullptr && !target_argmax, TSDS_E_INVALID);
+  AcceptIO io{(const bf16*)target_logits, (const long long*)target_argmax, (const bf16*)head_logits,
+              (const long long*)ids, hrow, children, U, nullptr, path, accept_len, (long long*)tokens,
+              (long long*)cur, n_nodes + 1, V, k, depth};
+  if (rule == ACC_RULE_TARGET)
+    tsds_launch(accept_tree_kernel<ACC_RULE_TARGET>, dim3(ACC_CL, B), dim3(ACC_THREADS), 0, stream, io);
+  else
+    tsds_launch(accept_tree_kernel<ACC_RULE_DRAFT>, dim3(ACC_CL, B), dim3(ACC_THREADS), 0, stream, io);
+  return tsds_launch_status();
+}
+
 extern "C" int tsds_accept_tree(const void* target_logits, const int64_t* target_argmax, const void* head_logits,
                                 const int64_t* ids, const int32_t* hrow, const int32_t* children, const float* U,
                                 float* scratch, int32_t* path, int32_t* accept_len, int64_t* tokens, int64_t* cur,
                                 int B, int n_nodes, int V, int k, int depth, tsds_stream_t stream) {
-  TSDS_RETURN_IF(B <= 0 || n_nodes < 1 || V <= 0 || k < 1 || k > MAXK || depth < 1, TSDS_E_INVALID);
-  TSDS_RETURN_IF(U != nullptr && (!target_logits || !head_logits), TSDS_E_INVALID);
-  TSDS_RETURN_IF(U == nullptr && !target_argmax, TSDS_E_INVALID);
-  AcceptIO io{(const bf16*)target_logits, (const long long*)target_argmax, (const bf16*)head_logits,
-              (const long long*)ids, hrow, children, U, scratch, path, accept_len, (long long*)tokens,
-              (long long*)cur, n_nodes + 1, V, k, depth};
-  tsds_launch(accept_tree_kernel, dim3(ACC_CL, B), dim3(ACC_THREADS), 0, stream, io);
-  return tsds_launch_status();
+  (void)scratch;
+  return tsds_accept_tree_rule(target_logits, target_argmax, head_logits, ids, hrow, children, U, ACC_RULE_DRAFT,
+                               path, accept_len, tokens, cur, B, n_nodes, V, k, depth, stream);
 }
 
 extern "C" int tsds_tree_commit(void* k_cache, void* v_cache, int layers, int B, int Hkv, int S, int D,

@@ -13,8 +13,13 @@ then the target's final norm and LM head.  One cycle, for B sequences:
    log-sum-exp, ``tsds_tree_step`` (children, next frontier);
 3. ``tsds_tree_finalize``: the ``n_nodes`` best nodes + root, ancestor masks;
 4. one target pass over the tree (attention with the ancestor mask);
-5. ``tsds_accept_tree``: rejection sampling at temperature 1 with supplied
-   uniforms (or greedy), emitted tokens, ``cur`` <- bonus;
+5. ``tsds_accept_tree_rule``: rejection sampling at temperature 1 with
+   supplied uniforms (or greedy), emitted tokens, ``cur`` <- bonus.  The
+   tree's children are its top-k (chosen without the uniforms), so the
+   default rule is the target-only one (``ACCEPT_TARGET``: accept child x if
+   u < p(x), else drop x from p), under which the emitted tokens follow the
+   target's distribution; ``ACCEPT_DRAFT`` (u q(x) < p(x), residual
+   max(p - q, 0)) is lossless only for children drawn from q;
 6. ``tsds_tree_commit``: KV compaction, next root feature, lengths += a + 1.
 
 Semantics are the oracle's (oracle/eagle.py).
@@ -34,7 +39,10 @@ class EagleHead:
     embedding, final norm and LM head."""
 
     def __init__(self, target: QwenModel, batch: int, topk: int = 4, depth: int = 5, weights: dict | None = None,
-                 seed: int = 0):
+                 seed: int = 0, share: "EagleHead | None" = None):
+        """``share``: another head (same shape) whose fc and layer weights
+        this one uses, for a target over the same weights at another batch
+        size."""
         s = target.shape
         self.shape = replace(s, n_layers=1)
         self.rows_per_seq = 1 + topk * (depth - 1)
@@ -43,8 +51,11 @@ class EagleHead:
         if weights is not None:
             lw = {"layers": [weights["layer"]], "embed": None, "lm_head": None, "norm": None}
         self.model = QwenModel(self.shape, batch=batch, max_seq=32, max_rows=batch * topk, device=dev, weights=lw,
-                               seed=seed, share_embeddings=target, rope_len=target.rope_len, fused_layers=target.fused_layers)
-        if weights is not None:
+                               seed=seed, share_embeddings=target, rope_len=target.rope_len, fused_layers=target.fused_layers,
+                               share_weights=None if share is None else share.model)
+        if share is not None:
+            self.fc_w, self.fc_b = share.fc_w, share.fc_b
+        elif weights is not None:
             self.fc_w = weights["fc"].to(dev, torch.bfloat16).contiguous()
             self.fc_b = weights["fc_bias"].to(dev, torch.bfloat16).contiguous()
         else:
@@ -54,15 +65,20 @@ class EagleHead:
             self.fc_b = (torch.randn(s.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
 
 
+ACCEPT_DRAFT, ACCEPT_TARGET = 0, 1
+
+
 class EagleEngine:
     def __init__(self, target: QwenModel, head: EagleHead, topk: int = 4, depth: int = 5, n_nodes: int = 25,
-                 greedy: bool = False, use_graph: bool = True, seed: int = 0):
+                 greedy: bool = False, use_graph: bool = True, seed: int = 0, rule: int = ACCEPT_TARGET):
         B = target.batch
         s = target.shape
         NN = n_nodes + 1
         assert target.max_rows >= B * NN and NN <= 32
         self.target, self.head = target, head
         self.topk, self.depth, self.n_nodes, self.greedy = topk, depth, n_nodes, greedy
+        assert rule in (ACCEPT_DRAFT, ACCEPT_TARGET)
+        self.rule = rule
         dev = target.device
         R = B * head.rows_per_seq
         i64, i32, f32, bf = (dict(dtype=t, device=dev) for t in (torch.int64, torch.int32, torch.float32,
@@ -138,9 +154,9 @@ class EagleEngine:
         pl.add("tsds_embed", _p(self.ids), 1, _p(t.embed_w), _p(t.x), B * NN, s.hidden, s.vocab)
         pl.extend(t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1))
         pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits))
-        pl.add("tsds_accept_tree", _p(self.target_logits), _p(self.target_argmax), _p(self.head_logits),
+        pl.add("tsds_accept_tree_rule", _p(self.target_logits), _p(self.target_argmax), _p(self.head_logits),
                _p(self.ids), _p(self.hrow), _p(self.children), None if self.greedy else _p(self.U),
-               None, _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
+               self.rule, _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
                self.n_nodes, s.vocab, k, self.depth)
         # the cache's own kv-head count: under tensor parallelism a rank holds
         # only its shard of the kv heads

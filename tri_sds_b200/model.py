@@ -179,7 +179,10 @@ class QwenModel:
                  weights: dict | None = None, seed: int = 0, split_keys: int = 128, qk_norm: bool | None = None,
                  share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
                  tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None,
-                 peer=None, fused_layers: bool = False):
+                 peer=None, fused_layers: bool = False, share_weights: "QwenModel | None" = None):
+        """``share_weights``: another model of the same shape and tensor-parallel
+        layout whose layer weights, embedding, final norm and LM head this one
+        uses (no copy): a second batch size over the same weights."""
         self.shape = shape
         # tensor parallelism: layers and/or vocabulary sharded over tp_size ranks
         self.tp_rank = tp_rank
@@ -222,7 +225,11 @@ class QwenModel:
         s = shape
         ls = self.lshape
         dev = self.device
-        if weights is not None:
+        if share_weights is not None:
+            assert share_weights.shape == shape and share_weights.layer_tp == self.layer_tp
+            assert share_weights.tp_rank == tp_rank and share_weights.vocab_tp == self.vocab_tp
+            self.layers = share_weights.layers
+        elif weights is not None:
             self.layers = [pack_layer(shard_layer(L, s, tp_rank, self.layer_tp), dev) for L in weights["layers"]]
         else:
             gen = torch.Generator(device=dev)
@@ -230,10 +237,11 @@ class QwenModel:
             lgen = torch.Generator(device=dev)
             lgen.manual_seed(seed + 7919 * (1 + tp_rank) if self.layer_tp > 1 else seed + 1)
             self.layers = [random_layer_gpu(ls, lgen, dev) for _ in range(s.n_layers)]
-        if share_embeddings is not None:
-            # the EAGLE head runs on the target's embedding, final norm and LM head
-            self.embed_w, self.lm_head_w, self.norm_w = (share_embeddings.embed_w, share_embeddings.lm_head_w,
-                                                         share_embeddings.norm_w)
+        if share_embeddings is not None or share_weights is not None:
+            # the EAGLE head runs on the target's embedding, final norm and LM
+            # head; a shared-weights model on the other model's
+            src = share_embeddings if share_embeddings is not None else share_weights
+            self.embed_w, self.lm_head_w, self.norm_w = src.embed_w, src.lm_head_w, src.norm_w
         elif weights is not None:
             self.embed_w = weights["embed"].to(dev, torch.bfloat16).contiguous()
             lm = self.embed_w if weights["lm_head"] is weights["embed"] else weights["lm_head"].to(dev, torch.bfloat16)

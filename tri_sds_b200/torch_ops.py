@@ -147,12 +147,15 @@ def accept_greedy(draft: Tensor, target_argmax: Tensor, lengths: Tensor, last: T
 @torch.library.custom_op("tsds::accept_rejection", mutates_args=())
 def accept_rejection(target_logits: Tensor, head_logits: Tensor, ids: Tensor, hrow: Tensor, children: Tensor,
                      uniforms: Optional[Tensor], target_argmax: Optional[Tensor],
-                     depth: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+                     depth: int, rule: int = 0) -> tuple[Tensor, Tensor, Tensor, Tensor]:
     """Walk a verified tree of NN nodes per sequence: ids [B, NN] int64,
     children [B, NN, k] int32 (-1 padded), hrow [B, NN] int32 (head-logits
     row of each node's children), target_logits [B*NN, V] and head_logits
     [rows, V] bf16.  uniforms [B, depth+1, k+1] fp32 -> rejection sampling at
-    temperature 1; None -> greedy on target_argmax [B*NN] int64.
+    temperature 1; None -> greedy on target_argmax [B*NN] int64.  rule 0:
+    accept x if u q(x) < p(x), residual max(p - q, 0) (children drawn from
+    q); rule 1: accept x if u < p(x), drop x from p (deterministic children,
+    e.g. top-k; head_logits unread).
     -> (path [B, depth+1] int32 node indices, accept_len [B] int32,
     tokens [B, depth+2] int64 (accepted then the bonus, -1 padded), bonus [B])."""
     ops._bf16_cuda(target_logits, head_logits)
@@ -167,17 +170,18 @@ def accept_rejection(target_logits: Tensor, head_logits: Tensor, ids: Tensor, hr
     ops._need(children.shape == (B, NN, k) and hrow.shape == (B, NN) and depth >= 1, "bad shapes")
     ops._need(uniforms is None or uniforms.shape == (B, depth + 1, k + 1), "uniforms must be [B, depth+1, k+1]")
     ops._need(target_argmax is None or target_argmax.numel() == B * NN, "target_argmax must be [B*NN]")
+    ops._need(rule in (0, 1), "rule must be 0 (draft) or 1 (target-only)")
     _in_range(children, -1, NN, "children")
-    if uniforms is not None:   # the head-logits row of every node that has children
+    if uniforms is not None and rule == 0:   # the head-logits row of every node that has children
         _in_range(hrow[children[..., 0] >= 0], 0, head_logits.shape[0], "hrow")
     dev = ids.device
     path = torch.empty(B, depth + 1, dtype=torch.int32, device=dev)
     acc = torch.empty(B, dtype=torch.int32, device=dev)
     tokens = torch.empty(B, depth + 2, dtype=torch.int64, device=dev)
     bonus = torch.empty(B, dtype=torch.int64, device=dev)
-    _lib.call("tsds_accept_tree", _p(target_logits), _p(target_argmax), _p(head_logits), _p(ids), _p(hrow),
-              _p(children), _p(uniforms), None, _p(path), _p(acc), _p(tokens), _p(bonus), B, NN - 1, V, k, depth,
-              _s())
+    _lib.call("tsds_accept_tree_rule", _p(target_logits), _p(target_argmax), _p(head_logits), _p(ids), _p(hrow),
+              _p(children), _p(uniforms), int(rule), _p(path), _p(acc), _p(tokens), _p(bonus), B, NN - 1, V, k,
+              depth, _s())
     return path, acc, tokens, bonus
 
 
