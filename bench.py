@@ -71,9 +71,6 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
-    ap.add_argument("--smem-slots", type=int, default=None,
-                    help="shared-memory slots per SM the tcgen05 GEMM pipeline is sized for (library default 0: "
-                         "its CTAs per SM; one more leaves room for the next kernel's first CTAs)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--dp-rows", type=int, default=None,
                     help="token rows from which a tcgen05 projection with at least one whole weight tile per CTA "
@@ -242,7 +239,7 @@ class CpuCycle:
             t_head = time.perf_counter() - t0
         return t_layer, t_head
 
-    def sample(self) -> tuple:
+    def sample_once(self) -> tuple:
         """Time one bounded sample; returns (projected full-cycle seconds,
         sample wall seconds).  The projection scales each timed layer by
         its model's layer count (and the draft by its K steps)."""
@@ -274,8 +271,8 @@ class CpuCycle:
         `reps` samples after `warm` untimed ones: the same estimator for the
         device arm's cpu_baseline and the reference arm."""
         for _ in range(warm):
-            self.sample()
-        runs = [self.sample() for _ in range(max(1, reps))]
+            self.sample_once()
+        runs = [self.sample_once() for _ in range(max(1, reps))]
         return statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)
 
     def scale(self) -> dict:
@@ -686,8 +683,6 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
         _lib.load().tsds_set_gemv_splitk(1)
     if a.ctas_per_sm is not None:
         _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
-    if a.smem_slots is not None:
-        _lib.load().tsds_set_gemm_smem_slots(a.smem_slots)
     if a.no_pdl:
         _lib.load().tsds_set_pdl(0)
     if a.pair_rows is not None:
@@ -800,7 +795,6 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
             "gemm_pair_rows": _lib.load().tsds_get_gemm_pair_rows(),
             "gemm_dp_rows": _lib.load().tsds_get_gemm_dp_rows(),
             "gemm_dp_slack": _lib.load().tsds_get_gemm_dp_slack(),
-            "gemm_smem_slots": _lib.load().tsds_get_gemm_smem_slots(),
             "attention": {"tcgen05": _lib.load().tsds_get_attention_tc(), "split_keys": a.attn_split},
         }
         if sub is not None:
@@ -842,8 +836,6 @@ def main():
             from tri_sds_b200 import _lib
             if a.ctas_per_sm is not None:
                 _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
-            if a.smem_slots is not None:
-                _lib.load().tsds_set_gemm_smem_slots(a.smem_slots)
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
             if a.dp_rows is not None:

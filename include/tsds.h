@@ -151,13 +151,6 @@ int tsds_get_gemv_splitk(void);
 /* Resident CTAs per SM of the tcgen05 GEMM (1..4, default 2; lowered
  * automatically when the accumulators would not fit in TMEM).  Tuning knob. */
 void tsds_set_gemm_ctas_per_sm(int n);
-/* Shared-memory slots per SM the tcgen05 GEMM's pipeline is sized for
- * (0..4; 0, the default: its CTAs per SM).  A value above the CTAs per SM
- * leaves room on each SM for a CTA of the next kernel, which under
- * programmatic dependent launch starts streaming its weights while this one
- * drains.  Tuning knob; no counterpart in the reference. */
-void tsds_set_gemm_smem_slots(int n);
-int tsds_get_gemm_smem_slots(void);
 /* Token rows M from which the tcgen05 GEMM runs on CTA pairs (two SMs per
  * 256-row weight tile, tcgen05 cta_group::2, each SM staging half of the
  * token rows; not the LM head); 0 (default): never.  Process-wide tuning
@@ -251,7 +244,10 @@ int tsds_get_attention_tc(void);
  * The caller still passes inputs and outputs; arguments as for
  * tsds_verify_attention.
  *  - The first call on a device looks the array's device address up (that
- *    device must be current); make it before any stream capture.
+ *    device must be current) and keeps it with the current context; a call
+ *    in another context (after cudaDeviceReset) looks it up again.  Make
+ *    the first call on a device, and the first after a reset, before any
+ *    stream capture.
  *  - All calls share the array and it keeps the last call's contents; the
  *    status word is cleared at every call.  Calls that overlap on the GPU
  *    race: order them on one stream.

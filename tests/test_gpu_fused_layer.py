@@ -106,12 +106,13 @@ def _bitwise_case(B, T):
             assert torch.equal(a, b), what
         return
     # a different grid splits the reductions differently: the two plans then
-    # agree to bf16 rounding (hidden / q / caches) and the logits within the
-    # bf16 logit tolerance
+    # agree to bf16 rounding (hidden / q / caches), and their logits - each
+    # within the 2e-2 bf16 tolerance of the oracle (test_fused_verify_matches_
+    # oracle) - within twice that of each other
     for a, b, what in zip(outs[0][:4], outs[1][:4], ("hidden", "q", "k cache", "v cache")):
         a, b = a.float(), b.float()
         assert (a - b).abs().max().item() <= 3e-2 * max(1.0, a.abs().max().item()), what
-    assert (outs[0][4].float() - outs[1][4].float()).abs().max().item() <= 2e-2
+    assert (outs[0][4].float() - outs[1][4].float()).abs().max().item() <= 4e-2
 
 
 def _same_split(M):

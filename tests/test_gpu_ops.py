@@ -159,7 +159,7 @@ def test_verify_attention_vs_f32(ops, B, T, starts, S):
     assert (got - ref).abs().max().item() <= 1e-2
 
 
-@pytest.mark.parametrize("split_keys", [128, 64])
+@pytest.mark.parametrize("split_keys", [1024, 512, 256, 128, 64])
 def test_verify_attention_kv4096_b8(ops, split_keys):
     """The isolated verify-attention configuration at its largest batch: B=8,
     KV length 4096, 5 new tokens, 64/8 heads.  128-key splits give 32 splits
@@ -181,15 +181,39 @@ def test_verify_attention_vs_oracle(ops):
     assert (got.float() - ref.float()).abs().max().item() <= 2e-2
 
 
-def test_verify_attention_decode_equals_verify_bitwise(ops):
-    """A query's output does not depend on how many tokens share the call."""
+@pytest.mark.parametrize("split_keys", [128, 512, 64])
+def test_verify_attention_decode_equals_verify_bitwise(ops, split_keys):
+    """A query's output does not depend on how many tokens share the call
+    (its row block, the grid, the number of splits in use)."""
     B, T, S = 2, 5, 2048
     q, kc, vc, st = _attn_case(B, T, 64, 8, S, [1500, 700], seed=9)
     qd, kd, vd, sd = q.to(DEV), kc.to(DEV), vc.to(DEV), st.to(DEV)
-    full = ops.verify_attention(qd, kd, vd, sd)
+    full = ops.verify_attention(qd, kd, vd, sd, split_keys=split_keys)
     for t in range(T):
-        one = ops.verify_attention(qd[:, t:t + 1].contiguous(), kd, vd, sd + t)
+        one = ops.verify_attention(qd[:, t:t + 1].contiguous(), kd, vd, sd + t, split_keys=split_keys)
         assert torch.equal(one[:, 0], full[:, t]), t
+
+
+@pytest.mark.parametrize("split_keys", [128, 256])
+def test_verify_attention_tree_rows_32b_heads(ops, split_keys):
+    """The EAGLE tree verify's shape: 26 rows per sequence x 8 q heads per kv
+    head (208 rows, several row blocks), a branching tree mask, 32B heads."""
+    B, T, S = 2, 26, 1024
+    q, kc, vc, st = _attn_case(B, T, 64, 8, S, [512, 700], seed=21)
+    g = torch.Generator().manual_seed(22)
+    parent = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, T)]
+    masks = []
+    for t in range(T):
+        m, j = 0, t
+        while j >= 0:
+            m |= 1 << j
+            j = parent[j]
+        masks.append(m)
+    tm = torch.tensor([masks] * B, dtype=torch.int64).to(torch.int32)
+    got = ops.verify_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), st.to(DEV), tree_mask=tm.to(DEV),
+                               split_keys=split_keys).cpu().float()
+    ref = _attn_ref_f32(q, kc, vc, st, tree_mask=tm)
+    assert (got - ref).abs().max().item() <= 1e-2
 
 
 def test_verify_attention_tree_mask(ops):

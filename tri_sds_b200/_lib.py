@@ -59,8 +59,6 @@ SIGNATURES = {
     "tsds_set_gemv_splitk": (None, [_I]),
     "tsds_get_gemv_splitk": (_I, []),
     "tsds_set_gemm_ctas_per_sm": (None, [_I]),
-    "tsds_set_gemm_smem_slots": (None, [_I]),
-    "tsds_get_gemm_smem_slots": (_I, []),
     "tsds_set_gemm_pair_rows": (None, [_I]),
     "tsds_get_gemm_pair_rows": (_I, []),
     "tsds_set_gemm_dp_rows": (None, [_I]),

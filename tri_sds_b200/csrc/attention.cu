@@ -22,6 +22,7 @@
 //   output is bit-identical whether it is verified with T tokens or decoded
 //   alone.
 #include "common.cuh"
+#include "linear.cuh"
 #include "tc_core.cuh"
 
 using namespace tsds;
@@ -30,6 +31,8 @@ namespace {
 
 constexpr int D = 128;
 constexpr int TILE = 64;                    // keys per tile
+constexpr int ATT_MAX_WARPS = 8;            // consumer warps per CTA (row groups x key groups)
+constexpr int ATT_STAGES = 4;               // K/V tiles in flight per CTA
 constexpr int HALF_BYTES = TILE * 128;      // one 64x64 bf16 box = 8 KB
 constexpr int TILE_BYTES = 4 * HALF_BYTES;  // K lo/hi + V lo/hi = 32 KB
 constexpr float LOG2E = 1.4426950408889634f;
@@ -78,232 +81,353 @@ struct AttnArgs {
   int B, T, Hq, Hkv, S, G, R, Rpad, nsplit, split_keys, nrb, mask_origin;
   float scale_log2;
   int cl;  // tcgen05 variant: the splits of a row block form a cluster and combine through shared memory
+  int RG, KG;  // default kernel: 16-row groups per row block, key groups per split
 };
 
-template <int STAGES>
-__global__ void __launch_bounds__(256) verify_attn_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                          const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128B-swizzle atoms
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[STAGES];
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
-  // blockIdx.x = split * nrb + row block (128 query rows per row block)
-  const int rb = blockIdx.x % a.nrb, split = blockIdx.x / a.nrb;
-  const int kvh = blockIdx.y, b = blockIdx.z;
-  pdl_wait();
-  pdl_trigger();
+// named barrier that also ANDs a predicate over its threads: every thread
+// gets the same answer
+__device__ __forceinline__ bool named_bar_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+
+// Persistent, warp-specialised split-KV attention.  One CTA per SM walks the
+// work items (b, kv head, row block, key split) i = blockIdx.x, + gridDim.x,
+// ...  Warp 0 (one lane) streams every K/V tile of the CTA's items, item
+// after item, through a STAGES-deep ring (full / empty mbarriers), so the
+// next item's tiles arrive while the consumers finish the current one.
+// Consumer warp c owns 16 query rows (row group c % RG of the item's row
+// block) and the split's tiles of key group c / RG (tiles t = kg, kg + KG,
+// ... of the split); at the end of an item the KG key groups' (m, l, O) of a
+// row are merged in key-group order through shared memory, then the item's
+// rows are normalised in place (one split) or written as a split partial.
+// KG depends only on split_keys and a tile's key group only on its key
+// index, so a row's result never depends on T, on its row block or on the
+// grid.
+template <int STAGES>
+__global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
+    verify_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms; the merge area follows the ring
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* xs = reinterpret_cast<float*>(smem + STAGES * TILE_BYTES);
+  __shared__ uint64_t full_bar[STAGES];
+  __shared__ uint64_t empty_bar[STAGES];
+  __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tig = lane & 3;
-  const int start = a.starts[b];
-  const int kv_len = start + a.T;
-  const int key_begin = split * a.split_keys;
-  const int key_end = min(key_begin + a.split_keys, kv_len);
-  const int ntiles = key_end > key_begin ? (key_end - key_begin + TILE - 1) / TILE : 0;
-  const int64_t slab_row = ((int64_t)b * a.Hkv + kvh) * a.S;  // first cache row of this (b, kvh)
-  const int64_t unit = ((int64_t)b * a.Hkv + kvh) * a.nsplit + split;
+  const int RG = a.RG, KG = a.KG, NC = a.RG * a.KG;
+  const int items_per_b = a.Hkv * a.nrb * a.nsplit;
+  const int nitems = a.B * items_per_b;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&full_bar[s], 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], RG);  // the row groups of the tile's key group
+    }
+    s_abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
-  auto issue = [&](int tile) {
-    const int s = tile % STAGES;
-    uint8_t* dst = smem + s * TILE_BYTES;
-    const int row = (int)(slab_row + key_begin + tile * TILE);
-    mbar_arrive_expect_tx(&full_bar[s], TILE_BYTES);
-    tma_load_2d(dst + 0 * HALF_BYTES, &kmap, &full_bar[s], 0, row);
-    tma_load_2d(dst + 1 * HALF_BYTES, &kmap, &full_bar[s], 64, row);
-    tma_load_2d(dst + 2 * HALF_BYTES, &vmap, &full_bar[s], 0, row);
-    tma_load_2d(dst + 3 * HALF_BYTES, &vmap, &full_bar[s], 64, row);
+  // item -> (b, kvh, rb, split) and the key range it covers
+  struct Item {
+    int b, kvh, rb, split, key_begin, ntiles, kv_len;
   };
-  if (threadIdx.x == 0) {
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    for (int t = 0; t < ntiles && t < STAGES; ++t) issue(t);
-  }
+  auto decode = [&](int item) {
+    Item it;
+    it.b = item / items_per_b;
+    int r = item % items_per_b;
+    it.kvh = r / (a.nrb * a.nsplit);
+    r %= a.nrb * a.nsplit;
+    it.split = r / a.nrb;
+    it.rb = r % a.nrb;
+    it.kv_len = a.starts[it.b] + a.T;
+    it.key_begin = it.split * a.split_keys;
+    const int key_end = min(it.key_begin + a.split_keys, it.kv_len);
+    it.ntiles = key_end > it.key_begin ? (key_end - it.key_begin + TILE - 1) / TILE : 0;
+    return it;
+  };
 
-  // ---- this warp's 16 query rows: r = t*G + gh ------------------------------
-  const int r0 = rb * 128 + warp * 16 + g, r1 = r0 + 8;
-  const int t0 = r0 / a.G, t1 = r1 / a.G;
-  const bool v0 = r0 < a.R, v1 = r1 < a.R;
-  uint32_t qa[8][4];
-  {
-    const bf16* q0 = a.q + (((int64_t)b * a.T + (v0 ? t0 : 0)) * a.Hq + kvh * a.G + (v0 ? r0 % a.G : 0)) * D;
-    const bf16* q1 = a.q + (((int64_t)b * a.T + (v1 ? t1 : 0)) * a.Hq + kvh * a.G + (v1 ? r1 % a.G : 0)) * D;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int c = kk * 16 + 2 * tig;
-      qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-      qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-      qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-      qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
-    }
-  }
-  const int mask_base = a.mask_origin >= 0 ? a.mask_origin : start;
-  const uint32_t mask0 = (a.tree_mask && v0) ? a.tree_mask[b * a.T + t0] : 0u;
-  const uint32_t mask1 = (a.tree_mask && v1) ? a.tree_mask[b * a.T + t1] : 0u;
-  const bool tree = a.tree_mask != nullptr;
-
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-  const uint32_t smem_base = smem_u32(smem);
-  bool aborted = false;
-  for (int tile = 0; tile < ntiles; ++tile) {
-    const int s = tile % STAGES;
-    // every thread polls; the CTA agrees on the outcome before anyone moves on
-    const int ok = mbar_wait(&full_bar[s], (tile / STAGES) & 1) ? 1 : 0;
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) {
-        atomicExch(a.status, TSDS_E_TIMEOUT);
-        // tiles 0 .. tile + STAGES - 1 were requested: let the ones still in
-        // flight land (bounded) before the CTA exits
-        drain_tma_ring(full_bar, STAGES, min(ntiles, tile + STAGES));
-      }
-      aborted = true;
-      break;
-    }
-    const uint32_t kbase = smem_base + s * TILE_BYTES;
-    const uint32_t vbase = kbase + 2 * HALF_BYTES;
-    const int key0 = key_begin + tile * TILE;
-
-    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
-    float sc[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 8; kk += 2) {
-        const int mi = lane >> 3, ri = lane & 7;
-        const int key = j * 8 + ri;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + tile_off(key, 2 * kk + mi), b0, b1, b2, b3);
-        mma_bf16(sc[j], qa[kk], b0, b1);
-        mma_bf16(sc[j], qa[kk + 1], b2, b3);
-      }
-    }
-    // mask + row max
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int kabs = key0 + j * 8 + 2 * tig + e;
-        bool vis0 = v0 && kabs < kv_len, vis1 = v1 && kabs < kv_len;
-        if (tree) {
-          // bit i of a row's mask covers key mask_base + i; keys below are shared context
-          const int rel = kabs - mask_base;
-          if (rel >= 0) {
-            const bool in = rel < 32;
-            vis0 = vis0 && in && ((mask0 >> (rel & 31)) & 1u);
-            vis1 = vis1 && in && ((mask1 >> (rel & 31)) & 1u);
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+      int q = 0;  // ring sequence number of the next tile
+      bool stop = false;
+      for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+        const Item it = decode(item);
+        const int ntiles = it.ntiles, key_begin = it.key_begin;
+        const int64_t slab_row = ((int64_t)it.b * a.Hkv + it.kvh) * a.S;
+        for (int t = 0; t < ntiles; ++t, ++q) {
+          const int s = q % STAGES;
+          if (q >= STAGES && !mbar_wait(&empty_bar[s], ((q / STAGES) - 1) & 1)) {
+            atomicExch(a.status, TSDS_E_TIMEOUT);
+            s_abort = 1;
+            stop = true;
+            break;
           }
-        } else {
-          const int rel = kabs - start;
-          vis0 = vis0 && rel <= t0;
-          vis1 = vis1 && rel <= t1;
+          if (*(volatile int*)&s_abort) {
+            stop = true;
+            break;
+          }
+          uint8_t* dst = smem + s * TILE_BYTES;
+          const int row = (int)(slab_row + key_begin + t * TILE);
+          mbar_arrive_expect_tx(&full_bar[s], TILE_BYTES);
+          tma_load_2d(dst + 0 * HALF_BYTES, &kmap, &full_bar[s], 0, row);
+          tma_load_2d(dst + 1 * HALF_BYTES, &kmap, &full_bar[s], 64, row);
+          tma_load_2d(dst + 2 * HALF_BYTES, &vmap, &full_bar[s], 0, row);
+          tma_load_2d(dst + 3 * HALF_BYTES, &vmap, &full_bar[s], 64, row);
         }
-        sc[j][e] = vis0 ? sc[j][e] * a.scale_log2 : -INFINITY;
-        sc[j][2 + e] = vis1 ? sc[j][2 + e] * a.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, sc[j][e]);
-        mx1 = fmaxf(mx1, sc[j][2 + e]);
       }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    // rows with nothing visible so far keep m = -inf and p = 0
-    const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
-    const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
-    const float sub0 = mn0 == -INFINITY ? 0.f : mn0;
-    const float sub1 = mn1 == -INFINITY ? 0.f : mn1;
-    m0 = mn0;
-    m1 = mn1;
-    float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      sc[j][0] = exp2f(sc[j][0] - sub0);
-      sc[j][1] = exp2f(sc[j][1] - sub0);
-      sc[j][2] = exp2f(sc[j][2] - sub1);
-      sc[j][3] = exp2f(sc[j][3] - sub1);
-      ps0 += sc[j][0] + sc[j][1];
-      ps1 += sc[j][2] + sc[j][3];
-    }
-    l0 = l0 * al0 + ps0;
-    l1 = l1 * al1 + ps1;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= al0;
-      o[n][1] *= al0;
-      o[n][2] *= al1;
-      o[n][3] *= al1;
-    }
-    // O += P V: 4 k-steps of 16 keys, 16 n-tiles of 8 dims.
-#pragma unroll
-    for (int kq = 0; kq < 4; ++kq) {
-      uint32_t pa[4];
-      pa[0] = pack2(sc[2 * kq][0], sc[2 * kq][1]);
-      pa[1] = pack2(sc[2 * kq][2], sc[2 * kq][3]);
-      pa[2] = pack2(sc[2 * kq + 1][0], sc[2 * kq + 1][1]);
-      pa[3] = pack2(sc[2 * kq + 1][2], sc[2 * kq + 1][3]);
-#pragma unroll
-      for (int n = 0; n < 16; n += 2) {
-        const int mi = lane >> 3, ri = lane & 7;
-        const int key = kq * 16 + (mi & 1) * 8 + ri;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + tile_off(key, n + (mi >> 1)), b0, b1, b2, b3);
-        mma_bf16(o[n], pa, b0, b1);
-        mma_bf16(o[n + 1], pa, b2, b3);
-      }
-    }
-    __syncthreads();  // every warp is done with stage s
-    if (threadIdx.x == 0 && tile + STAGES < ntiles) issue(tile + STAGES);
-  }
-  if (aborted) return;
-
-  // quad-reduce the row sums
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
-  if (a.nsplit == 1) {
-    // single split: normalise in place (same expression as the combine pass)
-    const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
-    if (v0) {
-      bf16* dst = a.out + (((int64_t)b * a.T + t0) * a.Hq + kvh * a.G + r0 % a.G) * D;
-#pragma unroll
-      for (int n = 0; n < 16; ++n)
-        *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][0] * inv0, o[n][1] * inv0);
-    }
-    if (v1) {
-      bf16* dst = a.out + (((int64_t)b * a.T + t1) * a.Hq + kvh * a.G + r1 % a.G) * D;
-#pragma unroll
-      for (int n = 0; n < 16; ++n)
-        *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][2] * inv1, o[n][3] * inv1);
+      // every requested tile lands before the CTA can exit
+      drain_tma_ring(full_bar, STAGES, q);
     }
     return;
   }
-  float* wo = a.ws_o + unit * a.Rpad * D;
-  float2* wml = a.ws_ml + unit * a.Rpad;
-  if (v0) {
+
+  // ---------------- consumers ----------------
+  const int cw = warp - 1, rg = cw % RG, kg = cw / RG;
+  const int g = lane >> 2, tig = lane & 3;
+  const uint32_t smem_base = smem_u32(smem);
+  int q0 = 0;  // ring sequence number of the current item's first tile
+  for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+    const Item it = decode(item);
+    const int b = it.b, kvh = it.kvh, rb = it.rb, split = it.split;
+    const int key_begin = it.key_begin, ntiles = it.ntiles, kv_len = it.kv_len;
+    const int start = a.starts[b];
+    const int64_t unit = ((int64_t)b * a.Hkv + kvh) * a.nsplit + split;
+    const int r0 = rb * RG * 16 + rg * 16 + g, r1 = r0 + 8;
+    const int t0 = r0 / a.G, t1 = r1 / a.G;
+    const bool v0 = r0 < a.R, v1 = r1 < a.R;
+    uint32_t qa[8][4];
+    {
+      const bf16* qp0 = a.q + (((int64_t)b * a.T + (v0 ? t0 : 0)) * a.Hq + kvh * a.G + (v0 ? r0 % a.G : 0)) * D;
+      const bf16* qp1 = a.q + (((int64_t)b * a.T + (v1 ? t1 : 0)) * a.Hq + kvh * a.G + (v1 ? r1 % a.G : 0)) * D;
 #pragma unroll
-    for (int n = 0; n < 16; ++n)
-      *reinterpret_cast<float2*>(wo + (int64_t)r0 * D + n * 8 + 2 * tig) = make_float2(o[n][0], o[n][1]);
-    if (tig == 0) wml[r0] = make_float2(m0, l0);
-  }
-  if (v1) {
+      for (int kk = 0; kk < 8; ++kk) {
+        const int c = kk * 16 + 2 * tig;
+        qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(qp0 + c) : 0u;
+        qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(qp1 + c) : 0u;
+        qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(qp0 + c + 8) : 0u;
+        qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(qp1 + c + 8) : 0u;
+      }
+    }
+    const int mask_base = a.mask_origin >= 0 ? a.mask_origin : start;
+    const uint32_t mask0 = (a.tree_mask && v0) ? a.tree_mask[b * a.T + t0] : 0u;
+    const uint32_t mask1 = (a.tree_mask && v1) ? a.tree_mask[b * a.T + t1] : 0u;
+    const bool tree = a.tree_mask != nullptr;
+
+    float o[16][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n)
-      *reinterpret_cast<float2*>(wo + (int64_t)r1 * D + n * 8 + 2 * tig) = make_float2(o[n][2], o[n][3]);
-    if (tig == 0) wml[r1] = make_float2(m1, l1);
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int tile = kg; tile < ntiles; tile += KG) {
+      const int qs = q0 + tile, s = qs % STAGES;
+      const int ok = (!*(volatile int*)&s_abort && mbar_wait(&full_bar[s], (qs / STAGES) & 1)) ? 1 : 0;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) {
+          atomicExch(a.status, TSDS_E_TIMEOUT);
+          s_abort = 1;
+        }
+        break;
+      }
+      const uint32_t kbase = smem_base + s * TILE_BYTES;
+      const uint32_t vbase = kbase + 2 * HALF_BYTES;
+      const int key0 = key_begin + tile * TILE;
+
+      // S = Q K^T for 64 keys: 8 n-tiles of 8 keys.
+      float sc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk += 2) {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int key = j * 8 + ri;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + tile_off(key, 2 * kk + mi), b0, b1, b2, b3);
+          mma_bf16(sc[j], qa[kk], b0, b1);
+          mma_bf16(sc[j], qa[kk + 1], b2, b3);
+        }
+      }
+      // mask + row max
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kabs = key0 + j * 8 + 2 * tig + e;
+          bool vis0 = v0 && kabs < kv_len, vis1 = v1 && kabs < kv_len;
+          if (tree) {
+            // bit i of a row's mask covers key mask_base + i; keys below are shared context
+            const int rel = kabs - mask_base;
+            if (rel >= 0) {
+              const bool in = rel < 32;
+              vis0 = vis0 && in && ((mask0 >> (rel & 31)) & 1u);
+              vis1 = vis1 && in && ((mask1 >> (rel & 31)) & 1u);
+            }
+          } else {
+            const int rel = kabs - start;
+            vis0 = vis0 && rel <= t0;
+            vis1 = vis1 && rel <= t1;
+          }
+          sc[j][e] = vis0 ? sc[j][e] * a.scale_log2 : -INFINITY;
+          sc[j][2 + e] = vis1 ? sc[j][2 + e] * a.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sc[j][e]);
+          mx1 = fmaxf(mx1, sc[j][2 + e]);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      // rows with nothing visible so far keep m = -inf and p = 0
+      const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+      const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+      const float sub0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float sub1 = mn1 == -INFINITY ? 0.f : mn1;
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sc[j][0] = exp2f(sc[j][0] - sub0);
+        sc[j][1] = exp2f(sc[j][1] - sub0);
+        sc[j][2] = exp2f(sc[j][2] - sub1);
+        sc[j][3] = exp2f(sc[j][3] - sub1);
+        ps0 += sc[j][0] + sc[j][1];
+        ps1 += sc[j][2] + sc[j][3];
+      }
+      l0 = l0 * al0 + ps0;
+      l1 = l1 * al1 + ps1;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= al0;
+        o[n][1] *= al0;
+        o[n][2] *= al1;
+        o[n][3] *= al1;
+      }
+      // O += P V: 4 k-steps of 16 keys, 16 n-tiles of 8 dims.
+#pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {
+        uint32_t pa[4];
+        pa[0] = pack2(sc[2 * kq][0], sc[2 * kq][1]);
+        pa[1] = pack2(sc[2 * kq][2], sc[2 * kq][3]);
+        pa[2] = pack2(sc[2 * kq + 1][0], sc[2 * kq + 1][1]);
+        pa[3] = pack2(sc[2 * kq + 1][2], sc[2 * kq + 1][3]);
+#pragma unroll
+        for (int n = 0; n < 16; n += 2) {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int key = kq * 16 + (mi & 1) * 8 + ri;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + tile_off(key, n + (mi >> 1)), b0, b1, b2, b3);
+          mma_bf16(o[n], pa, b0, b1);
+          mma_bf16(o[n + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);  // this warp is done with stage s
+    }
+    q0 += ntiles;
+
+    // quad-reduce the row sums
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    if (KG > 1) {
+      // key groups 1..KG-1 hand (m, l, O) to key group 0 through the merge
+      // area ([slot][68 values][32 lanes]: consecutive lanes, no conflicts)
+      if (kg > 0) {
+        float* x = xs + (size_t)((kg - 1) * RG + rg) * 68 * 32 + lane;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[(n * 4 + e) * 32] = o[n][e];
+        x[64 * 32] = m0;
+        x[65 * 32] = m1;
+        x[66 * 32] = l0;
+        x[67 * 32] = l1;
+      }
+      // one decision for every consumer warp (the producer may set the abort
+      // flag at any time; the barrier's AND is the same for all)
+      if (!named_bar_and(1, NC * 32, !*(volatile int*)&s_abort)) break;
+      if (kg == 0) {
+        for (int k = 1; k < KG; ++k) {
+          const float* x = xs + (size_t)((k - 1) * RG + rg) * 68 * 32 + lane;
+          const float mk0 = x[64 * 32], mk1 = x[65 * 32];
+          const float mn0 = fmaxf(m0, mk0), mn1 = fmaxf(m1, mk1);
+          const float a0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+          const float a1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+          const float b0 = mn0 == -INFINITY ? 0.f : exp2f(mk0 - mn0);
+          const float b1 = mn1 == -INFINITY ? 0.f : exp2f(mk1 - mn1);
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            o[n][0] = o[n][0] * a0 + x[(n * 4 + 0) * 32] * b0;
+            o[n][1] = o[n][1] * a0 + x[(n * 4 + 1) * 32] * b0;
+            o[n][2] = o[n][2] * a1 + x[(n * 4 + 2) * 32] * b1;
+            o[n][3] = o[n][3] * a1 + x[(n * 4 + 3) * 32] * b1;
+          }
+          l0 = l0 * a0 + x[66 * 32] * b0;
+          l1 = l1 * a1 + x[67 * 32] * b1;
+          m0 = mn0;
+          m1 = mn1;
+        }
+      }
+      // the merge area is free again for the next item
+      named_bar_sync(1, NC * 32);
+      if (kg > 0) continue;
+    } else if (*(volatile int*)&s_abort) {
+      break;  // one warp per row group, no barrier among them: each decides alone
+    }
+
+    if (a.nsplit == 1) {
+      // single split: normalise in place (same expression as the combine pass)
+      const float inv0 = l0 > 0.f ? 1.0f / l0 : 0.f, inv1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+      if (v0) {
+        bf16* dst = a.out + (((int64_t)b * a.T + t0) * a.Hq + kvh * a.G + r0 % a.G) * D;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][0] * inv0, o[n][1] * inv0);
+      }
+      if (v1) {
+        bf16* dst = a.out + (((int64_t)b * a.T + t1) * a.Hq + kvh * a.G + r1 % a.G) * D;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<uint32_t*>(dst + n * 8 + 2 * tig) = pack2(o[n][2] * inv1, o[n][3] * inv1);
+      }
+      continue;
+    }
+    float* wo = a.ws_o + unit * a.Rpad * D;
+    float2* wml = a.ws_ml + unit * a.Rpad;
+    if (v0) {
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<float2*>(wo + (int64_t)r0 * D + n * 8 + 2 * tig) = make_float2(o[n][0], o[n][1]);
+      if (tig == 0) wml[r0] = make_float2(m0, l0);
+    }
+    if (v1) {
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+        *reinterpret_cast<float2*>(wo + (int64_t)r1 * D + n * 8 + 2 * tig) = make_float2(o[n][2], o[n][3]);
+      if (tig == 0) wml[r1] = make_float2(m1, l1);
+    }
   }
 }
 
@@ -362,9 +486,15 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
   a.out[(((int64_t)b * a.T + t) * a.Hq + kvh * a.G + r % a.G) * D + d] = f2bf(acc * inv);
 }
 
-constexpr int kStages = 2;
+// key groups of a split: a function of split_keys alone (so a row's
+// accumulation order never depends on the call's shape); two groups once a
+// split holds at least two tiles
+int attn_key_groups(int split_keys) { return split_keys >= 2 * TILE ? 2 : 1; }
 
-size_t attn_smem_bytes() { return (size_t)kStages * TILE_BYTES + 1024; }
+// ring + merge area ((KG - 1) x RG warps' 68 values per lane) + alignment
+size_t attn_smem_bytes(int RG, int KG) {
+  return 1024 + (size_t)ATT_STAGES * TILE_BYTES + (size_t)(KG - 1) * RG * 68 * 32 * sizeof(float);
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05 variant: the same work units, split partials and combine pass, with
@@ -887,8 +1017,10 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   TSDS_RETURN_IF((uint64_t)B * Hkv * S > (uint64_t)INT32_MAX, TSDS_E_UNSUPPORTED);  // cache rows are int
   const int R = (int)R64;
   const int Rpad = (R + 15) / 16 * 16;
-  const int nrb = (Rpad + 127) / 128;
-  const int warps = Rpad >= 128 ? 8 : Rpad / 16;
+  // default kernel: row blocks of RG 16-row groups, KG key groups per split
+  const int KG = attn_key_groups(split_keys);
+  const int RG = min(ATT_MAX_WARPS / KG, Rpad / 16);
+  const int nrb = tc ? (Rpad + 127) / 128 : (Rpad + RG * 16 - 1) / (RG * 16);
   const int nsplit = (max_kv + split_keys - 1) / split_keys;
   const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
   TSDS_RETURN_IF(need > workspace_bytes || (need > 0 && workspace == nullptr), TSDS_E_WORKSPACE);
@@ -923,6 +1055,8 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.mask_origin = mask_origin;
   a.scale_log2 = scale * LOG2E;
   a.cl = 0;
+  a.RG = RG;
+  a.KG = KG;
 
   if (tc) {
     // 128-key boxes for the tcgen05 variant
@@ -948,12 +1082,15 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
     return tsds_launch_status();
   }
 
-  const size_t smem = attn_smem_bytes();
+  const size_t smem = attn_smem_bytes(RG, KG);
   static tsds_device_flags attr_set;
-  st = tsds_smem_limit_once(verify_attn_kernel<kStages>, (int)smem, attr_set);
+  st = tsds_smem_limit_once(verify_attn_kernel<ATT_STAGES>, (int)attn_smem_bytes(ATT_MAX_WARPS / 2, 2), attr_set);
   if (st != TSDS_OK) return st;
-  dim3 grid(nsplit * nrb, Hkv, B);
-  tsds_launch(verify_attn_kernel<kStages>, grid, dim3(warps * 32), smem, stream, kmap, vmap, a);
+  // persistent: one CTA per SM (fewer when there are fewer work items)
+  const long long items = (long long)B * Hkv * nrb * nsplit;
+  TSDS_RETURN_IF(items > INT32_MAX, TSDS_E_UNSUPPORTED);
+  const int grid = (int)(items < tsds_tc_num_sms() ? items : tsds_tc_num_sms());
+  tsds_launch(verify_attn_kernel<ATT_STAGES>, dim3(grid), dim3(32 * (1 + RG * KG)), smem, stream, kmap, vmap, a);
   st = tsds_launch_status();
   if (st != TSDS_OK || nsplit == 1) return st;
   tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);
@@ -975,8 +1112,10 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
 // * Host code never passes the array's name to a kernel (on the host that
 //   name is only a stand-in, not a device address).  The first call on a
 //   device, with that device current, looks up the device address with
-//   cudaGetSymbolAddress and caches it; make that first call before any
-//   stream capture.
+//   cudaGetSymbolAddress and caches it with the current context; a call in
+//   another context (after cudaDeviceReset) looks it up again.  Make the
+//   first call on a device (and the first after a reset) before any stream
+//   capture.
 // * All calls share the array and it keeps the last call's contents: the
 //   status word is cleared at each call (the partials are fully rewritten
 //   before they are read), and calls that overlap on the GPU race with
@@ -990,7 +1129,37 @@ constexpr int kNoAllocMaxDevices = 64;
 }  // namespace
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocHeader + kNoAllocScratch];
-static std::atomic<void*> g_attn_noalloc_addr[kNoAllocMaxDevices];
+
+// The array's device address per device, with the context it was looked up
+// in: after cudaDeviceReset (or any re-creation of the primary context) the
+// module is loaded again, possibly elsewhere, so a changed current context
+// means a fresh lookup.
+struct NoAllocAddr {
+  void* ctx;
+  void* ptr;
+};
+static NoAllocAddr g_attn_noalloc_addr[kNoAllocMaxDevices];
+static std::mutex g_attn_noalloc_lock;
+
+typedef int (*CtxGetCurrentFn)(void**);
+
+static void* current_context() {
+  static std::atomic<CtxGetCurrentFn> fn{nullptr};
+  CtxGetCurrentFn f = fn.load(std::memory_order_acquire);
+  if (f == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    f = reinterpret_cast<CtxGetCurrentFn>(p);
+    fn.store(f, std::memory_order_release);
+  }
+  void* ctx = nullptr;
+  return f(&ctx) == 0 ? ctx : nullptr;
+}
 
 static int attn_noalloc_base(void** out) {
   int dev = 0;
@@ -999,16 +1168,24 @@ static int attn_noalloc_base(void** out) {
     return TSDS_E_DEVICE;
   }
   if (dev < 0 || dev >= kNoAllocMaxDevices) return TSDS_E_DEVICE;
-  void* p = g_attn_noalloc_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {  // two threads may both look it up: the same address
+  std::lock_guard<std::mutex> hold(g_attn_noalloc_lock);
+  NoAllocAddr& c = g_attn_noalloc_addr[dev];
+  // no context current yet (this thread's first CUDA work): the lookup below
+  // makes the device's primary context current
+  void* ctx = current_context();
+  if (c.ptr == nullptr || ctx == nullptr || c.ctx != ctx) {
+    void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
       cudaGetLastError();
       return TSDS_E_DEVICE;
     }
-    g_attn_noalloc_addr[dev].store(p, std::memory_order_release);
+    ctx = current_context();
+    if (ctx == nullptr) return TSDS_E_DEVICE;
+    c.ptr = p;
+    c.ctx = ctx;
   }
-  *out = p;
+  *out = c.ptr;
   return TSDS_OK;
 }
 

@@ -568,11 +568,6 @@ std::atomic<int> g_num_sms{0};
 // 5.5 TB/s for the bare TMA stream).  Capped so both fit in TMEM (512
 // columns) and shared memory.
 std::atomic<int> g_ctas_per_sm{2};
-// Shared-memory slots per SM the pipeline is sized for (0: the CTAs per SM).
-// Above the CTAs per SM it leaves room on every SM for a CTA of the next
-// kernel, which - launched early under programmatic dependent launch - then
-// streams its first weight tiles while this kernel drains.
-std::atomic<int> g_smem_slots{0};
 // Token rows from which a projection runs on CTA pairs (CG = 2); 0: never.
 std::atomic<int> g_pair_min_rows{0};
 // Token rows from which a projection may run data-parallel instead of
@@ -603,8 +598,6 @@ int num_sms() {
 }  // namespace
 
 extern "C" void tsds_set_gemm_ctas_per_sm(int n) { g_ctas_per_sm = n < 1 ? 1 : (n > 4 ? 4 : n); }
-extern "C" void tsds_set_gemm_smem_slots(int n) { g_smem_slots = n < 0 ? 0 : (n > 4 ? 4 : n); }
-extern "C" int tsds_get_gemm_smem_slots(void) { return g_smem_slots; }
 extern "C" void tsds_set_gemm_pair_rows(int rows) { g_pair_min_rows = rows < 0 ? 0 : rows; }
 extern "C" int tsds_get_gemm_pair_rows(void) { return g_pair_min_rows; }
 extern "C" void tsds_set_gemm_dp_rows(int rows) { g_dp_min_rows = rows < 0 ? 0 : rows; }
@@ -748,8 +741,7 @@ int plan_tc(int epi, int M, int n_out, int K, TcParams& p, int& CG, size_t& smem
   int ctas = g_ctas_per_sm;
   while (ctas > 1 && 2 * p.tmem_cols * ctas > 512) --ctas;
   p.b_stage_bytes = p.Npad / CG * BK * 2;  // this CTA's token rows
-  const int slots = g_smem_slots > ctas ? (int)g_smem_slots : ctas;
-  int budget = SMEM_PER_SM / slots - SMEM_RESERVE;
+  int budget = SMEM_PER_SM / ctas - SMEM_RESERVE;
   if (budget > SMEM_BUDGET) budget = SMEM_BUDGET;
   p.stages = (budget - 1024) / (A_STAGE + p.b_stage_bytes);
   if (p.stages > MAX_STAGES) p.stages = MAX_STAGES;
