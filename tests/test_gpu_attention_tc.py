@@ -5,19 +5,14 @@ kernel, for causal and tree masks, one and two 128-row query blocks, single
 splits that run the online softmax over many 128-key tiles (no combine pass),
 many short splits (with the combine pass), splits past the last key, and the
 32B-shape verify configurations (B=8 over 4096 keys; the EAGLE tree, 26 rows
-per sequence x 8 q heads per kv head), and the prompt prefill on it.
-Runs only with TSDS_TEST_ATTN_TC=1 until the kernel has been validated on a
-B200."""
-import os
+per sequence x 8 q heads per kv head), and the prompt prefill on it."""
 
 import pytest
 import torch
 
 from oracle import qwen as oq
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_ATTN_TC") != "1",
-                                 reason="tcgen05 attention: set TSDS_TEST_ATTN_TC=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 TOL = 1e-2
 

@@ -11,19 +11,14 @@
   of the oracle;
 * EAGLE greedy decoding with fused layers equals greedy autoregressive
   decoding.
-Runs only with TSDS_TEST_FUSED=1 (the CTA-pair case also with
-TSDS_TEST_PAIR=1) until the kernel has been validated on a B200."""
-import os
-
+"""
 import pytest
 import torch
 
 from oracle import eagle as oe
 from oracle import qwen as oq
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_FUSED") != "1",
-                                 reason="fused-layer kernel: set TSDS_TEST_FUSED=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 SMALL = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=2, vocab=1000)
 Q4B = dict(hidden=2560, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=9728, n_layers=2, vocab=1000)
@@ -57,7 +52,6 @@ def test_fused_equals_per_op_bitwise_qwen3_4b_shape(B, T):
     _bitwise_case(B, T)
 
 
-@pytest.mark.skipif(os.environ.get("TSDS_TEST_PAIR") != "1", reason="CTA pairs: set TSDS_TEST_PAIR=1")
 @pytest.mark.parametrize("B,T", [(1, 26), (8, 26)])
 def test_fused_equals_per_op_bitwise_on_cta_pairs(B, T):
     """Both plans' GEMMs on CTA pairs (the per-op GEMM and the fused
@@ -70,7 +64,6 @@ def test_fused_equals_per_op_bitwise_on_cta_pairs(B, T):
         _lib.load().tsds_set_gemm_pair_rows(0)
 
 
-@pytest.mark.skipif(os.environ.get("TSDS_TEST_DP") != "1", reason="data-parallel GEMMs: set TSDS_TEST_DP=1")
 @pytest.mark.parametrize("B,T", [(1, 26), (8, 26)])
 def test_fused_equals_per_op_bitwise_data_parallel(B, T):
     """Both plans' GEMMs under the data-parallel schedule where it applies

@@ -1,16 +1,12 @@
 """The tcgen05 GEMM's data-parallel schedule (tsds_set_gemm_dp_rows: whole
 weight tiles per CTA, no split tiles) vs torch fp32 references and vs the
 stream-K schedule.  The two schedules sum a split tile's k-blocks in a
-different order, so they agree to bf16 rounding, not bit for bit.  Runs only
-with TSDS_TEST_DP=1 until the schedule has been validated on a B200."""
-import os
+different order, so they agree to bf16 rounding, not bit for bit."""
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_DP") != "1",
-                                 reason="data-parallel GEMM schedule: set TSDS_TEST_DP=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

@@ -1,15 +1,11 @@
 """The tcgen05 GEMM on CTA pairs (tsds_set_gemm_pair_rows: two SMs per 256-row
 weight tile, tcgen05 cta_group::2) vs torch fp32 references and vs the
-one-CTA kernel.  Runs only with TSDS_TEST_PAIR=1 until the pair kernel has
-been validated on a B200."""
-import os
+one-CTA kernel."""
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_PAIR") != "1",
-                                 reason="CTA-pair GEMM: set TSDS_TEST_PAIR=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

@@ -1,16 +1,12 @@
 """The split-K variant of the CUDA-core GEMV (tsds_set_gemv_splitk: a CTA per
 few weight rows, its 256 threads sweeping K, partials summed across warps
 in a fixed order) against torch fp32 references of the same ops, and
-against the one-warp-per-rows GEMV.  Runs only with TSDS_TEST_GEMV_SPLITK=1
-until the variant has been validated on a B200."""
-import os
+against the one-warp-per-rows GEMV."""
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_GEMV_SPLITK") != "1",
-                                 reason="split-K GEMV: set TSDS_TEST_GEMV_SPLITK=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

@@ -4,18 +4,14 @@ kernels' head dim 128), with no oracle in between.  The CPU oracle
 reproduces the same fixture bit for bit (test_oracle_golden.py), so this
 pins the device to the reference directly: prefill (T=12), verify (T=5 over
 the cache) and decode (T=1), B=2, logits within 2e-2 (bf16) and the argmax
-equal wherever the reference's top two logits are more than 2e-2 apart.
-Runs only with TSDS_TEST_GOLDEN=1 until it has run on a B200."""
-import os
+equal wherever the reference's top two logits are more than 2e-2 apart."""
 
 import pytest
 import torch
 
 from conftest import load_golden
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_GOLDEN") != "1",
-                                 reason="device vs the reference's fixture: set TSDS_TEST_GOLDEN=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

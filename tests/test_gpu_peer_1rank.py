@@ -11,18 +11,14 @@ one partial - so its results equal the plain plan bit for bit:
   fused (one-shot and two-shot peer phases), with the LM head through the
   exchange region and tsds_peer_lm_gather, against the same model without a
   peer group: hidden state, q, caches, logits and argmax equal.
-The two-rank forms are in test_gpu_tp.py.  Runs only with TSDS_TEST_PEER=1
-until the peer kernels have been validated on a B200."""
-import os
+The two-rank forms are in test_gpu_tp.py."""
 
 import pytest
 import torch
 
 from oracle import qwen as oq
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_PEER") != "1",
-                                 reason="peer-memory kernels: set TSDS_TEST_PEER=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 Q4B = dict(hidden=2560, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=9728, n_layers=2, vocab=1000)
 

@@ -5,9 +5,7 @@ prefilled together, then decoded by EAGLE tree speculation, by chain
 speculation with a draft model and autoregressively.  Every sequence must
 continue exactly as the oracle continues its prompt alone (greedy), up to
 the first bf16 near-tie of the oracle's own logits; the speculative engines
-must equal the autoregressive one on the same ragged batch.
-Runs only with TSDS_TEST_RAGGED=1 until it has run on a B200."""
-import os
+must equal the autoregressive one on the same ragged batch."""
 
 import pytest
 import torch
@@ -16,9 +14,7 @@ from oracle import eagle as oe
 from oracle import qwen as oq
 from oracle.spec import autoregressive
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_RAGGED") != "1",
-                                 reason="ragged prompts: set TSDS_TEST_RAGGED=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 SMALL = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=2, vocab=1000)
 LENGTHS = [3, 11, 7]

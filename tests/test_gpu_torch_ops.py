@@ -2,8 +2,7 @@
 torch reference of the same computation, called through the op layer (not
 the engines).  The kernels behind the ops are the engines' kernels, covered
 by the other GPU tests; these checks cover the op layer's argument plumbing
-(shapes, strides, layouts, in-place arguments).
-Runs only with TSDS_TEST_TORCH_OPS=1 until it has run on a B200."""
+(shapes, strides, layouts, in-place arguments)."""
 import os
 
 import pytest
@@ -13,9 +12,7 @@ from oracle import eagle as oe
 from oracle import qwen as oq
 from oracle import spec as osp
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TSDS_TEST_TORCH_OPS") != "1",
-                                 reason="torch.ops layer on the GPU: set TSDS_TEST_TORCH_OPS=1")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 SMALL = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=1, vocab=1000)
 

@@ -504,24 +504,28 @@ __device__ __forceinline__ float acc_p(const AccNode& a, float tj, float hj, int
   if constexpr (RULE == ACC_RULE_TARGET) {
     for (int l = 0; l < a.r; ++l) p = a.X[l] == j ? 0.f : p * a.invZ[l + 1];
     return p;
+  } else {
+    const float q0 = expf(hj - a.lse_h);
+    bool ex = false;
+    for (int l = 0; l < a.r; ++l) {
+      const float ql = ex ? 0.f : q0 * a.invQ[l];
+      p = fmaxf(p - ql, 0.f) * a.invZ[l + 1];
+      ex |= a.X[l] == j;
+    }
+    return p;
   }
-  const float q0 = expf(hj - a.lse_h);
-  bool ex = false;
-  for (int l = 0; l < a.r; ++l) {
-    const float ql = ex ? 0.f : q0 * a.invQ[l];
-    p = fmaxf(p - ql, 0.f) * a.invZ[l + 1];
-    ex |= a.X[l] == j;
-  }
-  return p;
 }
 
 // q_r(j) while child x is under test
 template <int RULE>
 __device__ __forceinline__ float acc_q(const AccNode& a, float hj, int j, int x) {
-  if constexpr (RULE == ACC_RULE_TARGET) return j == x ? 1.f : 0.f;
-  for (int l = 0; l < a.r; ++l)
-    if (a.X[l] == j) return 0.f;
-  return expf(hj - a.lse_h) * a.invQ[a.r];
+  if constexpr (RULE == ACC_RULE_TARGET) {
+    return j == x ? 1.f : 0.f;
+  } else {
+    for (int l = 0; l < a.r; ++l)
+      if (a.X[l] == j) return 0.f;
+    return expf(hj - a.lse_h) * a.invQ[a.r];
+  }
 }
 
 // deterministic block reductions (fixed shuffle tree, then warp order)
