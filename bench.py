@@ -94,7 +94,7 @@ def _args():
     ap.add_argument("--attn-tc", type=int, nargs="?", const=1, default=0, choices=[0, 1, 2],
                     help="verify attention on its tcgen05 variant (1; 2: splits combined in a cluster; "
                          "library default 0: off)")
-    ap.add_argument("--attn-split", type=int, default=128,
+    ap.add_argument("--attn-split", type=int, default=1024,
                     help="keys per attention split of the target / draft (a multiple of 64; of 128 for --attn-tc)")
     ap.add_argument("--gemv-splitk", action="store_true",
                     help="the GEMV path (rows up to --gemv-max-rows) as its split-K variant")

@@ -47,7 +47,9 @@ enum {
   TSDS_E_UNSUPPORTED = 6, /* no kernel instantiated for this configuration */
   TSDS_E_DEVICE = 7,      /* device query failed / not an sm_100 device */
   TSDS_E_SCRATCH_LIMIT = 8, /* request larger than a built-in scratch area */
-  TSDS_E_RUNTIME = 9        /* a CUDA runtime call (allocation, IPC mapping) failed */
+  TSDS_E_RUNTIME = 9,       /* a CUDA runtime call (allocation, IPC mapping) failed */
+  TSDS_E_INDEX = 10         /* a device-side table entry (KV pool row) outside its pool:
+                               the access was redirected to row 0 (status word) */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -220,6 +222,13 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
                           int T, int Hq, int Hkv, int D, int S, int max_kv, int split_keys,
                           float scale, void* workspace, size_t workspace_bytes, int32_t* status,
                           tsds_stream_t stream);
+/* The default kernel's launch shape for a call of tsds_verify_attention /
+ * tsds_verify_attention_paged on num_sms SMs (0: the current device's):
+ * out[0..5] = {row groups per CTA, key groups per split, row blocks, key
+ * splits, ring stages, threads per CTA}.  The key-group count depends on
+ * split_keys alone and divides the ring depth. */
+int tsds_attention_plan(int B, int T, int Hq, int Hkv, int max_kv, int split_keys, int num_sms,
+                        int32_t* out);
 /* Process-wide switch (default 0): with 1, tsds_verify_attention runs its
  * tcgen05 variant (S = Q K^T and O = P V on the 5th-generation tensor cores,
  * TMEM accumulators, one softmax thread per query row, 128-key tiles) for
@@ -231,6 +240,62 @@ int tsds_verify_attention(const void* q, const void* k_cache, const void* v_cach
  * a second launch (same bits as 1). */
 void tsds_set_attention_tc(int mode);
 int tsds_get_attention_tc(void);
+
+/* ---------------------------------------------------------------------------
+ * Paged KV: SGLang's token pool layout, the KV memory its spec worker runs on
+ * (the reference's worker receives SGLang's ScheduleBatch, worker.py:3-4,
+ * 59-61, whose requests own rows of a req_to_token table into per-layer
+ * token_to_kv_pool buffers).  Per layer, k_pool / v_pool are
+ * [pool_rows][Hkv][D] bf16; position p of sequence b lives at pool row
+ * token_table[req(b) * table_ld + p], req(b) = req_rows[b] (the batch's
+ * req_pool_indices) or b when req_rows is NULL.  page_size: when a multiple
+ * of 64, every aligned run of 64 positions must occupy 64 consecutive pool
+ * rows (paged allocators with such pages) and tiles are staged by TMA;
+ * otherwise (1: one row per token) rows are gathered one by one.
+ * A table entry outside [0, pool_rows) is never dereferenced: row 0 is read
+ * instead and *status = TSDS_E_INDEX.
+ *
+ * tsds_verify_attention_paged: as tsds_verify_attention (same q / out /
+ * starts / masks / splits / workspace and bit-identical results for the same
+ * keys), the cache rows below starts[b]+T read through the table;
+ * max_kv <= table_ld.
+ */
+int tsds_verify_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out,
+                                const int32_t* starts, const uint32_t* tree_mask, int mask_origin,
+                                const int32_t* token_table, int64_t table_ld, const int64_t* req_rows,
+                                int64_t pool_rows, int page_size, int B, int T, int Hq, int Hkv, int D,
+                                int max_kv, int split_keys, float scale, void* workspace,
+                                size_t workspace_bytes, int32_t* status, tsds_stream_t stream);
+/* tsds_qk_norm_rope_kv into the pools: as tsds_qk_norm_rope_kv for M token
+ * rows, row m's K / V written to pool row out_loc[m] (SGLang's
+ * out_cache_loc); q into q_out [M][Hq][D].  Replaces the cache write of
+ * qwen_model.py:118-119 in the pool layout. */
+int tsds_qk_norm_rope_kv_paged(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                               const void* cos, const void* sin, const int32_t* positions,
+                               const int64_t* out_loc, void* q_out, void* k_pool, void* v_pool, int M,
+                               int Hq, int Hkv, int D, int64_t pool_rows, int rope_len, float eps,
+                               int32_t* status, tsds_stream_t stream);
+/* The new tokens' pool rows: out_loc[b*T + t] = token_table[req(b) *
+ * table_ld + starts[b] + t] (-1 past the table), the out_cache_loc of a
+ * forward for engines that keep their own table. */
+int tsds_table_rows(const int32_t* token_table, int64_t table_ld, const int64_t* req_rows,
+                    const int32_t* starts, int B, int T, int64_t* out_loc, tsds_stream_t stream);
+/* Tree commit in the pool layout: no K/V moves - the accepted nodes' pool
+ * rows become the sequence's next positions.  With L = lengths[b] (the
+ * tree's root at position L), a = accept_len[b] and path / accept_len as
+ * tsds_accept_tree writes them (accepted non-root nodes, [B][depth+1]):
+ * token_table[req(b) * table_ld + L + 1 + j] = old
+ * token_table[req(b) * table_ld + L + path[b][j]] for j < a, then
+ * lengths[b] += a + 1.  kept_rows (optional, [B][depth+2], -1 padded)
+ * receives the pool rows of positions L..L+a afterwards, so the caller can
+ * free the tree's other rows.  root_feat (optional) gets the hidden state of
+ * the last accepted node as tsds_tree_commit does (hidden [B][n_nodes+1][N]).
+ * Replaces tsds_tree_commit's row moves for pooled caches (the reference
+ * only advanced a length, qwen_model.py:190,206). */
+int tsds_tree_commit_paged(int32_t* token_table, int64_t table_ld, const int64_t* req_rows,
+                           int32_t* lengths, const int32_t* path, const int32_t* accept_len, int depth,
+                           int64_t* kept_rows, const void* hidden, int n_nodes, int N, void* root_feat,
+                           int B, tsds_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * tsds_verify_attention for callers that cannot allocate device memory.

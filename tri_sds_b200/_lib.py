@@ -17,6 +17,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
+_L = ctypes.c_int64
 
 PHASE_GEMM, PHASE_NORM, PHASE_PEER = 0, 1, 2
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32, EPI_QKROPE = 0, 1, 2, 4, 5
@@ -83,6 +84,13 @@ SIGNATURES = {
     "tsds_verify_attention": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _Z, _P, _P]),
     "tsds_set_attention_tc": (None, [_I]),
     "tsds_get_attention_tc": (_I, []),
+    "tsds_verify_attention_paged": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _L, _P, _L, _I, _I, _I, _I, _I, _I, _I,
+                                         _I, _F, _P, _Z, _P, _P]),
+    "tsds_qk_norm_rope_kv_paged": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _L, _I, _F, _P,
+                                        _P]),
+    "tsds_tree_commit_paged": (_I, [_P, _L, _P, _P, _P, _P, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "tsds_attention_plan": (_I, [_I, _I, _I, _I, _I, _I, _I, _P]),
+    "tsds_table_rows": (_I, [_P, _L, _P, _P, _I, _I, _P, _P]),
     "tsds_verify_attention_noalloc_limit": (_Z, []),
     "tsds_verify_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P]),
     "tsds_verify_attention_noalloc_status": (_I, [_P]),

@@ -33,6 +33,11 @@ constexpr int D = 128;
 constexpr int TILE = 64;                    // keys per tile
 constexpr int ATT_MAX_WARPS = 8;            // consumer warps per CTA (row groups x key groups)
 constexpr int ATT_STAGES = 4;               // K/V tiles in flight per CTA
+// Ring invariant: a consumer's next tile is KG tiles after its last one, and
+// it waits for that tile's full barrier by phase parity.  The wait is exact
+// only if the tile STAGES before it - the stage's previous use - has landed;
+// with KG dividing STAGES that tile belongs to the same key group, so the
+// waiting warp has already consumed it.  Every KG below divides ATT_STAGES.
 constexpr int HALF_BYTES = TILE * 128;      // one 64x64 bf16 box = 8 KB
 constexpr int TILE_BYTES = 4 * HALF_BYTES;  // K lo/hi + V lo/hi = 32 KB
 constexpr float LOG2E = 1.4426950408889634f;
@@ -82,7 +87,43 @@ struct AttnArgs {
   float scale_log2;
   int cl;  // tcgen05 variant: the splits of a row block form a cluster and combine through shared memory
   int RG, KG;  // default kernel: 16-row groups per row block, key groups per split
+  // Paged KV (default kernel): 0 = contiguous caches [B][Hkv][S][D] through
+  // the tensor maps; otherwise K/V live in token pools [pool_rows][Hkv][D]
+  // and key p of sequence b is pool row table[req(b) * table_ld + p]
+  // (req(b) = req_rows[b], or b without req_rows).  1: every aligned run of
+  // 64 keys sits in 64 consecutive pool rows (pages of a multiple of 64
+  // tokens), staged by TMA through tensor maps over the pools; 2: rows
+  // gathered one by one by the producer warp's 32 lanes (cp.async).
+  int paged;
+  const bf16* k_pool;
+  const bf16* v_pool;
+  const int32_t* table;
+  const int64_t* req_rows;
+  int64_t table_ld, pool_rows;
 };
+
+// 16-byte global -> shared copy (L2 only), completion tracked per thread
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// the calling thread's earlier cp.async copies arrive on the barrier when
+// they land (one arrival per thread, counted against the barrier's count)
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// pool row of key `pos` of sequence b (paged KV); a row outside the pool is
+// recorded as TSDS_E_INDEX and replaced by row 0 (never read out of range)
+__device__ __forceinline__ int64_t kv_slot(const AttnArgs& a, int b, int pos) {
+  const int64_t req = a.req_rows ? a.req_rows[b] : b;
+  const int64_t slot = a.table[req * a.table_ld + pos];
+  if (slot < 0 || slot >= a.pool_rows) {
+    atomicExch(a.status, TSDS_E_INDEX);
+    return 0;
+  }
+  return slot;
+}
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -131,7 +172,9 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      // a TMA stage completes on one arrival + its bytes; a gathered stage
+      // on the producer warp's 32 cp.async arrivals
+      mbar_init(&full_bar[s], a.paged == 2 ? 32 : 1);
       mbar_init(&empty_bar[s], RG);  // the row groups of the tile's key group
     }
     s_abort = 0;
@@ -162,6 +205,48 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
 
   if (warp == 0) {
     // ---------------- producer ----------------
+    if (a.paged == 2) {
+      // Gathered rows: lane l copies 16-byte chunk l % 16 of keys 2i + l / 16
+      // (i = 0..31) of K and of V, so a warp-wide copy moves two whole
+      // 256-byte rows; the chunks land where TMA's 128-byte swizzle would
+      // put them.  Keys past the sequence repeat its last row (masked).
+      int q = 0;
+      bool stop = false;
+      const int hw = lane >> 4, c16 = lane & 15;
+      for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+        const Item it = decode(item);
+        for (int t = 0; t < it.ntiles; ++t, ++q) {
+          const int s = q % STAGES;
+          const bool ok = q < STAGES || mbar_wait(&empty_bar[s], ((q / STAGES) - 1) & 1);
+          if (!__all_sync(0xffffffffu, ok && !*(volatile int*)&s_abort)) {
+            if (lane == 0 && !ok) {
+              atomicExch(a.status, TSDS_E_TIMEOUT);
+              s_abort = 1;
+            }
+            stop = true;
+            break;
+          }
+          const int key0 = it.key_begin + t * TILE;
+          // lane l looks up keys key0 + l and key0 + 32 + l; the others by shuffle
+          const int64_t sl0 = kv_slot(a, it.b, min(key0 + lane, it.kv_len - 1));
+          const int64_t sl1 = kv_slot(a, it.b, min(key0 + 32 + lane, it.kv_len - 1));
+          const uint32_t stage = smem_u32(smem + s * TILE_BYTES);
+#pragma unroll 4
+          for (int i = 0; i < 32; ++i) {
+            const int key = 2 * i + hw;
+            const int64_t slot = __shfl_sync(0xffffffffu, key < 32 ? sl0 : sl1, key & 31);
+            const int64_t off = (slot * a.Hkv + it.kvh) * D + c16 * 8;
+            const uint32_t d = stage + tile_off(key, c16);
+            cp_async16(d, a.k_pool + off);
+            cp_async16(d + 2 * HALF_BYTES, a.v_pool + off);
+          }
+          cp_async_arrive(&full_bar[s]);
+        }
+      }
+      // every lane's copies land before the CTA can exit
+      drain_tma_ring(full_bar, STAGES, q);
+      return;
+    }
     if (lane == 0) {
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
@@ -184,12 +269,15 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
             break;
           }
           uint8_t* dst = smem + s * TILE_BYTES;
-          const int row = (int)(slab_row + key_begin + t * TILE);
+          // contiguous: the slab's rows; paged (64-key pages): the page's
+          // first pool row, the kv head's 128 columns of the pool row
+          const int row = a.paged ? (int)kv_slot(a, it.b, key_begin + t * TILE) : (int)(slab_row + key_begin + t * TILE);
+          const int col = a.paged ? it.kvh * D : 0;
           mbar_arrive_expect_tx(&full_bar[s], TILE_BYTES);
-          tma_load_2d(dst + 0 * HALF_BYTES, &kmap, &full_bar[s], 0, row);
-          tma_load_2d(dst + 1 * HALF_BYTES, &kmap, &full_bar[s], 64, row);
-          tma_load_2d(dst + 2 * HALF_BYTES, &vmap, &full_bar[s], 0, row);
-          tma_load_2d(dst + 3 * HALF_BYTES, &vmap, &full_bar[s], 64, row);
+          tma_load_2d(dst + 0 * HALF_BYTES, &kmap, &full_bar[s], col, row);
+          tma_load_2d(dst + 1 * HALF_BYTES, &kmap, &full_bar[s], col + 64, row);
+          tma_load_2d(dst + 2 * HALF_BYTES, &vmap, &full_bar[s], col, row);
+          tma_load_2d(dst + 3 * HALF_BYTES, &vmap, &full_bar[s], col + 64, row);
         }
       }
       // every requested tile lands before the CTA can exit
@@ -205,6 +293,11 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
   int q0 = 0;  // ring sequence number of the current item's first tile
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     const Item it = decode(item);
+    // a split past the end of its sequence holds no keys: the combine pass
+    // reads only splits below the sequence's length, so it is skipped whole
+    // (every consumer warp takes the same decision; the producer streams no
+    // tiles for it)
+    if (it.ntiles == 0) continue;
     const int b = it.b, kvh = it.kvh, rb = it.rb, split = it.split;
     const int key_begin = it.key_begin, ntiles = it.ntiles, kv_len = it.kv_len;
     const int start = a.starts[b];
@@ -487,14 +580,34 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
 }
 
 // key groups of a split: a function of split_keys alone (so a row's
-// accumulation order never depends on the call's shape); two groups once a
-// split holds at least two tiles
-int attn_key_groups(int split_keys) { return split_keys >= 2 * TILE ? 2 : 1; }
+// accumulation order never depends on the call's shape): the largest divisor
+// of ATT_STAGES (1, 2, 4) that does not exceed the split's tiles.  Long
+// splits spread over four warps, so a short context (one split of up to 1024
+// keys) takes a few tiles per warp instead of a chain of them.
+int attn_key_groups(int split_keys) {
+  const int tiles = split_keys / TILE;
+  return tiles >= 4 ? 4 : (tiles >= 2 ? 2 : 1);
+}
+static_assert(ATT_STAGES % 4 == 0, "every key-group count must divide the ring depth");
+
+// row groups per CTA: the most (up to ATT_MAX_WARPS / KG) that still give
+// every SM a work item, else one (a short batch then spreads its rows over
+// more CTAs; the K/V tiles they share come from L2).  Row blocks never change
+// a row's arithmetic.
+int attn_row_groups(int KG, int Rpad, long long per_rb_items, int num_sms) {
+  const int groups = Rpad / 16;
+  int RG = ATT_MAX_WARPS / KG < groups ? ATT_MAX_WARPS / KG : groups;
+  while (RG > 1 && per_rb_items * ((groups + RG - 1) / RG) < num_sms) RG /= 2;
+  return RG;
+}
 
 // ring + merge area ((KG - 1) x RG warps' 68 values per lane) + alignment
 size_t attn_smem_bytes(int RG, int KG) {
   return 1024 + (size_t)ATT_STAGES * TILE_BYTES + (size_t)(KG - 1) * RG * 68 * 32 * sizeof(float);
 }
+
+// the largest merge area of any (RG, KG) with RG * KG <= ATT_MAX_WARPS, KG <= 4: KG = 4, RG = 2
+size_t attn_smem_bytes_max() { return attn_smem_bytes(ATT_MAX_WARPS / 4, 4); }
 
 // ---------------------------------------------------------------------------
 // tcgen05 variant: the same work units, split partials and combine pass, with
@@ -985,6 +1098,27 @@ bool atc_clusters_fit(int n) {
 
 }  // namespace
 
+// The default kernel's launch shape for a call (num_sms 0: the current
+// device's): out = {RG, KG, row blocks, key splits, ring stages, threads}.
+extern "C" int tsds_attention_plan(int B, int T, int Hq, int Hkv, int max_kv, int split_keys, int num_sms,
+                                   int32_t* out) {
+  TSDS_RETURN_IF(!out || B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(max_kv <= 0 || split_keys <= 0 || (split_keys % TILE) != 0 || num_sms < 0, TSDS_E_INVALID);
+  const long long R = (long long)T * (Hq / Hkv);
+  TSDS_RETURN_IF(R > 1024, TSDS_E_UNSUPPORTED);
+  const int Rpad = (int)((R + 15) / 16 * 16);
+  const int KG = attn_key_groups(split_keys);
+  const int nsplit = (max_kv + split_keys - 1) / split_keys;
+  const int RG = attn_row_groups(KG, Rpad, (long long)B * Hkv * nsplit, num_sms > 0 ? num_sms : tsds_tc_num_sms());
+  out[0] = RG;
+  out[1] = KG;
+  out[2] = (Rpad + RG * 16 - 1) / (RG * 16);
+  out[3] = nsplit;
+  out[4] = ATT_STAGES;
+  out[5] = 32 * (1 + RG * KG);
+  return TSDS_OK;
+}
+
 extern "C" void tsds_set_attention_tc(int mode) { g_attn_tc = mode < 0 ? 0 : (mode > 2 ? 2 : mode); }
 extern "C" int tsds_get_attention_tc(void) { return g_attn_tc; }
 
@@ -1019,9 +1153,9 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   const int Rpad = (R + 15) / 16 * 16;
   // default kernel: row blocks of RG 16-row groups, KG key groups per split
   const int KG = attn_key_groups(split_keys);
-  const int RG = min(ATT_MAX_WARPS / KG, Rpad / 16);
-  const int nrb = tc ? (Rpad + 127) / 128 : (Rpad + RG * 16 - 1) / (RG * 16);
   const int nsplit = (max_kv + split_keys - 1) / split_keys;
+  const int RG = attn_row_groups(KG, Rpad, (long long)B * Hkv * nsplit, tsds_tc_num_sms());
+  const int nrb = tc ? (Rpad + 127) / 128 : (Rpad + RG * 16 - 1) / (RG * 16);
   const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
   TSDS_RETURN_IF(need > workspace_bytes || (need > 0 && workspace == nullptr), TSDS_E_WORKSPACE);
 
@@ -1057,6 +1191,11 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
   a.cl = 0;
   a.RG = RG;
   a.KG = KG;
+  a.paged = 0;
+  a.k_pool = a.v_pool = nullptr;
+  a.table = nullptr;
+  a.req_rows = nullptr;
+  a.table_ld = a.pool_rows = 0;
 
   if (tc) {
     // 128-key boxes for the tcgen05 variant
@@ -1084,13 +1223,109 @@ extern "C" int tsds_verify_attention(const void* q, const void* k_cache, const v
 
   const size_t smem = attn_smem_bytes(RG, KG);
   static tsds_device_flags attr_set;
-  st = tsds_smem_limit_once(verify_attn_kernel<ATT_STAGES>, (int)attn_smem_bytes(ATT_MAX_WARPS / 2, 2), attr_set);
+  st = tsds_smem_limit_once(verify_attn_kernel<ATT_STAGES>, (int)attn_smem_bytes_max(), attr_set);
   if (st != TSDS_OK) return st;
   // persistent: one CTA per SM (fewer when there are fewer work items)
   const long long items = (long long)B * Hkv * nrb * nsplit;
   TSDS_RETURN_IF(items > INT32_MAX, TSDS_E_UNSUPPORTED);
   const int grid = (int)(items < tsds_tc_num_sms() ? items : tsds_tc_num_sms());
   tsds_launch(verify_attn_kernel<ATT_STAGES>, dim3(grid), dim3(32 * (1 + RG * KG)), smem, stream, kmap, vmap, a);
+  st = tsds_launch_status();
+  if (st != TSDS_OK || nsplit == 1) return st;
+  tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);
+  return tsds_launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Verify attention over paged token pools (SGLang's token_to_kv_pool layout:
+// per layer K and V pools [pool_rows][Hkv][D], a request-to-token table
+// giving the pool row of every position of a sequence).  The default
+// kernel's work items, masks, key groups and split partials, with the K/V
+// tiles staged from the pools: by TMA when pages hold a multiple of 64
+// tokens (each aligned run of 64 keys is 64 consecutive pool rows), else
+// gathered row by row by the producer warp.  The arithmetic is the
+// contiguous path's, so a sequence gives bit-identical outputs whichever
+// layout holds its keys.
+// ---------------------------------------------------------------------------
+extern "C" int tsds_verify_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out,
+                                           const int32_t* starts, const uint32_t* tree_mask, int mask_origin,
+                                           const int32_t* token_table, int64_t table_ld, const int64_t* req_rows,
+                                           int64_t pool_rows, int page_size, int B, int T, int Hq, int Hkv, int Dd,
+                                           int max_kv, int split_keys, float scale, void* workspace,
+                                           size_t workspace_bytes, int32_t* status, tsds_stream_t stream) {
+  TSDS_RETURN_IF(Dd != D, TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF(B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(tree_mask != nullptr && mask_origin < 0 && T > 32, TSDS_E_INVALID);
+  TSDS_RETURN_IF(max_kv <= 0 || max_kv > table_ld || split_keys <= 0 || (split_keys % TILE) != 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(pool_rows <= 0 || page_size <= 0 || pool_rows > (int64_t)INT32_MAX, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!q || !k_pool || !v_pool || !out || !starts || !status || !token_table, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!tsds_aligned16(q) || !tsds_aligned16(k_pool) || !tsds_aligned16(v_pool) || !tsds_aligned16(out),
+                 TSDS_E_ALIGN);
+  const int G = Hq / Hkv;
+  const long long R64 = (long long)T * G;
+  TSDS_RETURN_IF(R64 > 1024, TSDS_E_UNSUPPORTED);
+  const int R = (int)R64;
+  const int Rpad = (R + 15) / 16 * 16;
+  const int KG = attn_key_groups(split_keys);
+  const int nsplit = (max_kv + split_keys - 1) / split_keys;
+  const int RG = attn_row_groups(KG, Rpad, (long long)B * Hkv * nsplit, tsds_tc_num_sms());
+  const int nrb = (Rpad + RG * 16 - 1) / (RG * 16);
+  const size_t need = tsds_attention_workspace_bytes(B, T, Hq, Hkv, Dd, max_kv, split_keys);
+  TSDS_RETURN_IF(need > workspace_bytes || (need > 0 && workspace == nullptr), TSDS_E_WORKSPACE);
+
+  AttnArgs a;
+  a.q = (const bf16*)q;
+  a.out = (bf16*)out;
+  a.starts = starts;
+  a.tree_mask = tree_mask;
+  a.ws_o = (float*)workspace;
+  a.ws_ml = nsplit > 1 ? reinterpret_cast<float2*>((char*)workspace + (size_t)B * Hkv * nsplit * Rpad * D * sizeof(float))
+                       : nullptr;
+  a.status = status;
+  a.B = B;
+  a.T = T;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.S = table_ld < (int64_t)INT32_MAX ? (int)table_ld : INT32_MAX;
+  a.G = G;
+  a.R = R;
+  a.Rpad = Rpad;
+  a.nsplit = nsplit;
+  a.split_keys = split_keys;
+  a.nrb = nrb;
+  a.mask_origin = mask_origin;
+  a.scale_log2 = scale * LOG2E;
+  a.cl = 0;
+  a.RG = RG;
+  a.KG = KG;
+  a.paged = page_size % TILE == 0 ? 1 : 2;
+  a.k_pool = (const bf16*)k_pool;
+  a.v_pool = (const bf16*)v_pool;
+  a.table = token_table;
+  a.req_rows = req_rows;
+  a.table_ld = table_ld;
+  a.pool_rows = pool_rows;
+
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  if (a.paged == 1) {
+    // the pools as [pool_rows][Hkv * D]: a box is 64 pool rows x one 64-column half of a kv head
+    int st = tsds_make_tmap_2d_bf16(&kmap, k_pool, (uint64_t)Hkv * D, (uint64_t)pool_rows, (uint64_t)Hkv * D * 2, 64,
+                                    TILE, 1);
+    if (st != TSDS_OK) return st;
+    st = tsds_make_tmap_2d_bf16(&vmap, v_pool, (uint64_t)Hkv * D, (uint64_t)pool_rows, (uint64_t)Hkv * D * 2, 64,
+                                TILE, 1);
+    if (st != TSDS_OK) return st;
+  }
+  static tsds_device_flags attr_set;
+  int st = tsds_smem_limit_once(verify_attn_kernel<ATT_STAGES>, (int)attn_smem_bytes_max(), attr_set);
+  if (st != TSDS_OK) return st;
+  const long long items = (long long)B * Hkv * nrb * nsplit;
+  TSDS_RETURN_IF(items > INT32_MAX, TSDS_E_UNSUPPORTED);
+  const int grid = (int)(items < tsds_tc_num_sms() ? items : tsds_tc_num_sms());
+  tsds_launch(verify_attn_kernel<ATT_STAGES>, dim3(grid), dim3(32 * (1 + RG * KG)), attn_smem_bytes(RG, KG), stream,
+              kmap, vmap, a);
   st = tsds_launch_status();
   if (st != TSDS_OK || nsplit == 1) return st;
   tsds_launch(attn_combine_kernel, dim3(R, Hkv, B), dim3(128), 0, stream, a);

@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const bf16* __restrict__ qkv, const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w,
     const bf16* __restrict__ cos_t, const bf16* __restrict__ sin_t, const int32_t* __restrict__ positions,
     const int32_t* __restrict__ starts, bf16* __restrict__ q_out, bf16* __restrict__ k_cache,
-    bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, int rope_len, float eps) {
+    bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, int rope_len, float eps,
+    const int64_t* __restrict__ out_loc, int64_t pool_rows, int32_t* __restrict__ status) {
   constexpr int D = 128;
   pdl_wait();
   pdl_trigger();
@@ -139,14 +140,29 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   const uint32_t c = *reinterpret_cast<const uint32_t*>(src + 64 + 2 * lane);
   float v[4] = {bf_lo(a), bf_hi(a), bf_lo(c), bf_hi(c)};
   const int b = m / T, t = m - b * T;
-  const int row_in_seq = starts[b] + t;
   const int pos = positions[m];
+  // K/V row of head kvh: the contiguous cache's row starts[b] + t of slab
+  // (b, kvh), or (pooled caches, out_loc given) pool row out_loc[m], head kvh
+  int64_t slot = 0;
+  int row_in_seq = 0;
+  if (out_loc) {
+    slot = out_loc[m];
+    if (slot < 0 || slot >= pool_rows) {  // never written out of the pool
+      if (lane == 0 && h == Hq) atomicExch(status, TSDS_E_INDEX);
+      return;
+    }
+  } else {
+    row_in_seq = starts[b] + t;
+  }
   // rows / positions past the cache or the RoPE table are never written
   // (the host keeps lengths below S; this only prevents out-of-range stores)
   if (row_in_seq < 0 || row_in_seq >= S || pos < 0 || pos >= rope_len) return;
+  auto kv_row = [&](int kvh) -> int64_t {
+    return out_loc ? slot * Hkv + kvh : ((int64_t)b * Hkv + kvh) * S + row_in_seq;
+  };
   if (h >= Hq + Hkv) {  // v head: copy into the cache
     const int kvh = h - Hq - Hkv;
-    const int64_t row = ((int64_t)b * Hkv + kvh) * S + row_in_seq;
+    const int64_t row = kv_row(kvh);
     bf16* dst = v_cache + row * D;
     *reinterpret_cast<uint32_t*>(dst + 2 * lane) = a;
     *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = c;
@@ -160,7 +176,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     dst = q_out + ((int64_t)m * Hq + h) * D;
   } else {
     const int kvh = h - Hq;
-    dst = k_cache + (((int64_t)b * Hkv + kvh) * S + row_in_seq) * D;
+    dst = k_cache + kv_row(kvh) * D;
   }
   rope_store(v, cos_t, sin_t, pos, lane, dst);
 }
@@ -176,7 +192,51 @@ extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const
   const int warps = M * (Hq + 2 * Hkv);
   tsds_launch(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream,
       (const bf16*)qkv, (const bf16*)q_norm_w, (const bf16*)k_norm_w, (const bf16*)cos, (const bf16*)sin, positions,
-      starts, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, M, T, Hq, Hkv, S, rope_len, eps);
+      starts, (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, M, T, Hq, Hkv, S, rope_len, eps, (const int64_t*)nullptr,
+      (int64_t)0, (int32_t*)nullptr);
+  return tsds_launch_status();
+}
+
+extern "C" int tsds_qk_norm_rope_kv_paged(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
+                                          const void* sin, const int32_t* positions, const int64_t* out_loc,
+                                          void* q_out, void* k_pool, void* v_pool, int M, int Hq, int Hkv, int D,
+                                          int64_t pool_rows, int rope_len, float eps, int32_t* status,
+                                          tsds_stream_t stream) {
+  TSDS_RETURN_IF(D != 128, TSDS_E_UNSUPPORTED);
+  TSDS_RETURN_IF(M <= 0 || Hq <= 0 || Hkv <= 0 || (Hq % Hkv) != 0 || pool_rows <= 0, TSDS_E_INVALID);
+  TSDS_RETURN_IF(!qkv || !cos || !sin || !positions || !out_loc || !q_out || !k_pool || !v_pool || !status,
+                 TSDS_E_INVALID);
+  const int warps = M * (Hq + 2 * Hkv);
+  // one "sequence" of M rows: row m's position comes from positions[m], its K/V row from out_loc[m]
+  tsds_launch(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream,
+      (const bf16*)qkv, (const bf16*)q_norm_w, (const bf16*)k_norm_w, (const bf16*)cos, (const bf16*)sin, positions,
+      (const int32_t*)nullptr, (bf16*)q_out, (bf16*)k_pool, (bf16*)v_pool, M, M, Hq, Hkv, 1, rope_len, eps, out_loc,
+      pool_rows, status);
+  return tsds_launch_status();
+}
+
+// Pooled KV: the pool rows of the new tokens, out_loc[b*T + t] =
+// table[req(b) * table_ld + starts[b] + t] (what SGLang hands a forward as
+// out_cache_loc), for engines that own their token table.
+__global__ void table_rows_kernel(const int32_t* __restrict__ table, int64_t table_ld,
+                                  const int64_t* __restrict__ req_rows, const int32_t* __restrict__ starts, int B,
+                                  int T, int64_t* __restrict__ out_loc) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * T) return;
+  const int b = i / T, t = i - b * T;
+  const int64_t p = (int64_t)starts[b] + t;
+  const int64_t req = req_rows ? req_rows[b] : b;
+  out_loc[i] = p < table_ld ? (int64_t)table[req * table_ld + p] : -1;
+}
+
+extern "C" int tsds_table_rows(const int32_t* table, int64_t table_ld, const int64_t* req_rows,
+                               const int32_t* starts, int B, int T, int64_t* out_loc, tsds_stream_t stream) {
+  TSDS_RETURN_IF(!table || table_ld <= 0 || !starts || !out_loc || B <= 0 || T <= 0, TSDS_E_INVALID);
+  const int n = B * T;
+  tsds_launch(table_rows_kernel, dim3((n + 127) / 128), dim3(128), 0, stream, table, table_ld, req_rows, starts, B, T,
+              out_loc);
   return tsds_launch_status();
 }
 

@@ -333,10 +333,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const int eq = warp & 3;
     const int r = eq * 32 + lane;  // tile row == TMEM lane
     const int nchunk = p.Npad / 16;
-    // STORE / RESIDUAL / STORE_F32: split tiles are reduced by all their
-    // contributors (each sums a slice of rows) once every partial is stored;
-    // SWIGLU / ARGMAX need whole tiles and keep the last-arriver reduction.
-    constexpr bool DIST = EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32;
+    // STORE / RESIDUAL / STORE_F32 / SWIGLU: split tiles are reduced by all
+    // their contributors (each sums a slice of rows - for SwiGLU a slice of
+    // gate rows together with their up rows) once every partial is stored;
+    // ARGMAX needs whole tiles and keeps the last-arriver reduction.
+    constexpr bool DIST = EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_STORE_F32 || EPI == EPI_SWIGLU;
     int pend0 = -1, pend1 = -1;  // split tiles of this CTA (registers, not an indexed array)
     int npend = 0;
     int seg = 0;
@@ -455,15 +456,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if constexpr (DIST) {
       // Every arrival of this CTA is done, so no wait below can block
       // another CTA's arrival (the grid is one resident wave).  Contributor
-      // c of nq sums rows [c*128/nq, (c+1)*128/nq) of the tile over all
+      // c of nq sums rows [c*128/nq, (c+1)*128/nq) of the tile (SwiGLU: gate
+      // rows [c*64/nq, (c+1)*64/nq) and the up rows 64 below them) over all
       // partials in CTA order; the last to leave resets the counters.
+      constexpr bool SW = EPI == EPI_SWIGLU;
+      constexpr int ROWS = SW ? 64 : TILE_J;  // rows (SwiGLU: gate rows) split among contributors
       for (int pi = 0; alive && pi < npend; ++pi) {
         const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
         const int vt = t * CG + crank;
         const int q_lo = owner_of(tb, PU, p.W), q_hi = owner_of(tb + KT - 1, PU, p.W);
         const int nq = q_hi - q_lo + 1, c = unit - q_lo;
         const int lo_slot = it_begin(q_lo, PU, p.W) < tb ? 1 : 0;
-        const int rlo = c * TILE_J / nq, R = (c + 1) * TILE_J / nq - rlo;
+        const int rlo = c * ROWS / nq, R = (c + 1) * ROWS / nq - rlo;
         const int nel = R * (p.Npad / 4);
         if (r == 0) {
           int ok = 1;
@@ -486,49 +490,107 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           alive = false;
           break;
         }
-        for (int e0 = r; e0 < nel; e0 += 128) {
-          const int rr = rlo + e0 % R, g = e0 / R;
-          const int j = vt * TILE_J + rr;
-          float rv[4] = {0.f, 0.f, 0.f, 0.f};
+        // element e = (row rr of the slice, 4-column group g).  A thread takes
+        // EU elements per pass and issues the loads of all their partials
+        // (QB partials per batch) before summing, so a pass costs one L2
+        // round trip instead of one per element; each element still sums its
+        // partials in CTA order from zero.
+        constexpr int EU = SW ? 2 : 4;  // elements per pass
+        constexpr int QB = 4;           // partials per batch
+        constexpr int NH = SW ? 2 : 1;  // rows per element: the gate row and its up row
+        for (int e0 = r; e0 < nel; e0 += 128 * EU) {
+          float4 acc[EU][NH];
+#pragma unroll
+          for (int u = 0; u < EU; ++u)
+#pragma unroll
+            for (int h = 0; h < NH; ++h) acc[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+          // the residual (possibly the output buffer itself) is read before
+          // any store, its loads in flight with the partials'
+          float rv[EU][4];
           if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (j < p.n_out && 4 * g + i < p.M) rv[i] = bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j]);
+            for (int u = 0; u < EU; ++u) {
+              const int e = e0 + u * 128;
+              const int rr = rlo + e % R, g = e / R, j = vt * TILE_J + rr;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                rv[u][i] = (e < nel && j < p.n_out && 4 * g + i < p.M) ? bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j])
+                                                                         : 0.f;
+            }
           }
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          constexpr int QB = 8;
           for (int q0 = 0; q0 < nq; q0 += QB) {
-            float4 f[QB];
+            float4 f[EU][QB][NH];
 #pragma unroll
-            for (int i = 0; i < QB; ++i)
-              if (q0 + i < nq) {
-                const int q = (q_lo + q0 + i) * CG + crank;
-                const int qs = q0 + i == 0 ? lo_slot : 0;
-                f[i] = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
-                              (size_t)g * TILE_J + rr);
+            for (int u = 0; u < EU; ++u) {
+              const int e = e0 + u * 128;
+              if (e < nel) {
+                const int rr = rlo + e % R, g = e / R;
+#pragma unroll
+                for (int i = 0; i < QB; ++i)
+                  if (q0 + i < nq) {
+                    const int q = (q_lo + q0 + i) * CG + crank;
+                    const int qs = q0 + i == 0 ? lo_slot : 0;
+                    const float4* src = reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                                        (size_t)g * TILE_J + rr;
+#pragma unroll
+                    for (int h = 0; h < NH; ++h) f[u][i][h] = __ldcg(src + h * 64);
+                  }
               }
+            }
 #pragma unroll
-            for (int i = 0; i < QB; ++i)
-              if (q0 + i < nq) {
-                acc.x += f[i].x;
-                acc.y += f[i].y;
-                acc.z += f[i].z;
-                acc.w += f[i].w;
+            for (int u = 0; u < EU; ++u)
+              if (e0 + u * 128 < nel) {
+#pragma unroll
+                for (int i = 0; i < QB; ++i)
+                  if (q0 + i < nq) {
+#pragma unroll
+                    for (int h = 0; h < NH; ++h) {
+                      acc[u][h].x += f[u][i][h].x;
+                      acc[u][h].y += f[u][i][h].y;
+                      acc[u][h].z += f[u][i][h].z;
+                      acc[u][h].w += f[u][i][h].w;
+                    }
+                  }
               }
           }
-          if (j < p.n_out) {
-            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int m = 4 * g + i;
-              if (m < p.M) {
-                const int64_t o = (int64_t)m * p.ldo + j;
-                if constexpr (EPI == EPI_STORE_F32)
-                  reinterpret_cast<float*>(p.out)[o] = a4[i];
-                else if constexpr (EPI == EPI_STORE)
-                  p.out[o] = f2bf(a4[i]);
-                else
-                  p.out[o] = f2bf(rv[i] + rbf(a4[i]));
+          for (int u = 0; u < EU; ++u) {
+            const int e = e0 + u * 128;
+            if (e >= nel) continue;
+            const int rr = rlo + e % R, g = e / R;
+            const float a4[4] = {acc[u][0].x, acc[u][0].y, acc[u][0].z, acc[u][0].w};
+            if constexpr (SW) {
+              // the SwiGLU of the whole-tile epilogue: gate and up rounded
+              // to bf16, silu(gate) rounded, the product rounded
+              const float b4[4] = {acc[u][NH - 1].x, acc[u][NH - 1].y, acc[u][NH - 1].z, acc[u][NH - 1].w};
+              const int j = vt * 64 + rr;
+              if (j < p.n_out) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int m = 4 * g + i;
+                  if (m < p.M) {
+                    const float gv = rbf(a4[i]);
+                    const float sv = rbf(gv / (1.0f + expf(-gv)));
+                    p.out[(int64_t)m * p.ldo + j] = f2bf(sv * rbf(b4[i]));
+                  }
+                }
+              }
+            } else {
+              const int j = vt * TILE_J + rr;
+              if (j < p.n_out) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int m = 4 * g + i;
+                  if (m < p.M) {
+                    const int64_t o = (int64_t)m * p.ldo + j;
+                    if constexpr (EPI == EPI_STORE_F32)
+                      reinterpret_cast<float*>(p.out)[o] = a4[i];
+                    else if constexpr (EPI == EPI_STORE)
+                      p.out[o] = f2bf(a4[i]);
+                    else
+                      p.out[o] = f2bf(rv[u][i] + rbf(a4[i]));
+                  }
+                }
               }
             }
           }

@@ -56,6 +56,7 @@ extern "C" const char* tsds_status_string(int status) {
     case TSDS_E_DEVICE: return "device / driver query failed";
     case TSDS_E_SCRATCH_LIMIT: return "request larger than the built-in scratch area";
     case TSDS_E_RUNTIME: return "CUDA runtime call (allocation / IPC) failed";
+    case TSDS_E_INDEX: return "KV pool row outside the pool (table entry)";
     default: return "unknown status";
   }
 }

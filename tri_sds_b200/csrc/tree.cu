@@ -974,6 +974,48 @@ extern "C" int tsds_tree_commit(void* k_cache, void* v_cache, int layers, int B,
   return tsds_launch_status();
 }
 
+// Pooled KV commit: one CTA per sequence.  Thread 0 moves the accepted
+// nodes' table entries down to the positions after the root (increasing j:
+// path[j'] > path[j] >= j + 1 for j' > j, so no entry is read after it was
+// overwritten), lists the kept pool rows and advances the length; the CTA
+// copies the last accepted node's hidden state to root_feat.
+__global__ void tree_commit_paged_kernel(int* __restrict__ table, long long table_ld,
+                                         const long long* __restrict__ req_rows, int* __restrict__ lengths,
+                                         const int* __restrict__ path, const int* __restrict__ accept_len, int depth,
+                                         long long* __restrict__ kept, const bf16* __restrict__ hidden, int NN, int N,
+                                         bf16* __restrict__ root_feat) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const int a = accept_len[b];
+  const int L = lengths[b];
+  if (root_feat) {
+    const int last = a > 0 ? path[b * (depth + 1) + a - 1] : 0;
+    const bf16* src = hidden + ((size_t)b * NN + last) * N;
+    for (int i = threadIdx.x; i < N / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(root_feat + (size_t)b * N)[i] = reinterpret_cast<const uint4*>(src)[i];
+  }
+  if (threadIdx.x != 0) return;
+  int* row = table + (req_rows ? req_rows[b] : (long long)b) * table_ld;
+  for (int j = 0; j < a; ++j) row[L + 1 + j] = row[L + path[b * (depth + 1) + j]];
+  if (kept)
+    for (int i = 0; i < depth + 2; ++i) kept[(long long)b * (depth + 2) + i] = i <= a ? row[L + i] : -1;
+  lengths[b] = L + a + 1;
+}
+
+extern "C" int tsds_tree_commit_paged(int32_t* token_table, int64_t table_ld, const int64_t* req_rows,
+                                      int32_t* lengths, const int32_t* path, const int32_t* accept_len, int depth,
+                                      int64_t* kept_rows, const void* hidden, int n_nodes, int N, void* root_feat,
+                                      int B, tsds_stream_t stream) {
+  TSDS_RETURN_IF(!token_table || table_ld <= 0 || !lengths || !path || !accept_len || depth < 1 || B <= 0,
+                 TSDS_E_INVALID);
+  TSDS_RETURN_IF(root_feat && (!hidden || n_nodes < 1 || N <= 0 || (N % 8) != 0), TSDS_E_INVALID);
+  tsds_launch(tree_commit_paged_kernel, dim3(B), dim3(128), 0, stream, (int*)token_table, (long long)table_ld,
+              (const long long*)req_rows, (int*)lengths, (const int*)path, (const int*)accept_len, depth,
+              (long long*)kept_rows, (const bf16*)hidden, n_nodes + 1, N, (bf16*)root_feat);
+  return tsds_launch_status();
+}
+
 // X2[m] = [feature | embedding(token)] for the head's pass rows m = b*T + t.
 __global__ void eagle_inputs_kernel(const bf16* __restrict__ root_feat, const bf16* __restrict__ head_feat,
                                     const int* __restrict__ featrow, const long long* __restrict__ tok,

@@ -20,7 +20,9 @@ then the target's final norm and LM head.  One cycle, for B sequences:
    u < p(x), else drop x from p), under which the emitted tokens follow the
    target's distribution; ``ACCEPT_DRAFT`` (u q(x) < p(x), residual
    max(p - q, 0)) is lossless only for children drawn from q;
-6. ``tsds_tree_commit``: KV compaction, next root feature, lengths += a + 1.
+6. ``tsds_tree_commit``: KV compaction, next root feature, lengths += a + 1
+   (with a target on paged KV, ``tsds_tree_commit_paged``: the accepted
+   nodes' pool rows take the next positions in the table, no K/V moves).
 
 Semantics are the oracle's (oracle/eagle.py).
 """
@@ -109,6 +111,8 @@ class EagleEngine:
         self.tokens = torch.zeros(B, depth + 2, **i64)
         self.cur = torch.zeros(B, **i64)
         self.root_feat = torch.zeros(B, s.hidden, **bf)
+        # pooled KV: the pool rows each commit keeps (root + accepted nodes, -1 padded)
+        self.kept_rows = torch.full((B, depth + 2), -1, **i64)
         self.gen = torch.Generator(device=dev)
         self.gen.manual_seed(seed)
         self.use_graph = use_graph
@@ -158,6 +162,14 @@ class EagleEngine:
                _p(self.ids), _p(self.hrow), _p(self.children), None if self.greedy else _p(self.U),
                self.rule, _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
                self.n_nodes, s.vocab, k, self.depth)
+        if t.kv is not None:
+            # pooled KV: the accepted nodes' pool rows become the next
+            # positions (table entries move, K/V stay); kept_rows lists them
+            kv = t.kv
+            pl.add("tsds_tree_commit_paged", _p(kv.table), kv.table_ld, _p(kv.req_rows), _p(t.lengths),
+                   _p(self.path), _p(self.accept_len), self.depth, _p(self.kept_rows), _p(t.x), self.n_nodes,
+                   s.hidden, _p(self.root_feat), B)
+            return pl
         # the cache's own kv-head count: under tensor parallelism a rank holds
         # only its shard of the kv heads
         pl.add("tsds_tree_commit", _p(t.k_cache), _p(t.v_cache), s.n_layers, B, t.k_cache.shape[2], t.max_seq,

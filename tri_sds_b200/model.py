@@ -22,11 +22,11 @@ import ctypes
 from dataclasses import dataclass, field
 
 import torch
-import torch.nn.functional as F
 
 from dataclasses import replace
 
 from . import _lib
+from .paged import PagedKV  # noqa: F401  (QwenModel's kv argument)
 from .shapes import QwenShape
 from .tp import LocalComm, lm_exchange_layout, local_dims, shard_layer, vocab_shard
 
@@ -176,13 +176,18 @@ class QwenModel:
     """
 
     def __init__(self, shape: QwenShape, batch: int, max_seq: int, max_rows: int, device="cuda",
-                 weights: dict | None = None, seed: int = 0, split_keys: int = 128, qk_norm: bool | None = None,
+                 weights: dict | None = None, seed: int = 0, split_keys: int = 1024, qk_norm: bool | None = None,
                  share_embeddings: "QwenModel | None" = None, rope_len: int | None = None,
                  tp_rank: int = 0, tp_size: int = 1, tp_layers: bool = True, tp_vocab: bool = True, comm=None,
-                 peer=None, fused_layers: bool = False, share_weights: "QwenModel | None" = None):
+                 peer=None, fused_layers: bool = False, share_weights: "QwenModel | None" = None,
+                 kv: "PagedKV | None" = None):
         """``share_weights``: another model of the same shape and tensor-parallel
         layout whose layer weights, embedding, final norm and LM head this one
-        uses (no copy): a second batch size over the same weights."""
+        uses (no copy): a second batch size over the same weights.
+        ``kv``: paged KV memory in SGLang's layout (tri_sds_b200.paged.PagedKV:
+        per-layer token pools + request-to-token table) used instead of the
+        model's own contiguous cache; the default kernels' path only (no
+        fused layers, no tcgen05 attention)."""
         self.shape = shape
         # tensor parallelism: layers and/or vocabulary sharded over tp_size ranks
         self.tp_rank = tp_rank
@@ -262,9 +267,16 @@ class QwenModel:
         # holds rows of a tree whose positions continue the sequence)
         self.rope_len = max_seq if rope_len is None else rope_len
         self.cos, self.sin = precompute_rope(s.head_dim, self.rope_len, s.rope_theta, dev)
-        self.k_cache = torch.zeros(s.n_layers, batch, ls.n_kv_heads, max_seq, s.head_dim, dtype=torch.bfloat16,
-                                   device=dev)
-        self.v_cache = torch.zeros_like(self.k_cache)
+        self.kv = kv
+        if kv is None:
+            self.k_cache = torch.zeros(s.n_layers, batch, ls.n_kv_heads, max_seq, s.head_dim, dtype=torch.bfloat16,
+                                       device=dev)
+            self.v_cache = torch.zeros_like(self.k_cache)
+        else:
+            assert not fused_layers, "paged KV runs the per-op plan"
+            assert len(kv.k_pools) == s.n_layers and kv.n_kv_heads == ls.n_kv_heads and kv.table_ld >= max_seq
+            self.k_cache = self.v_cache = None
+            self.out_loc = torch.zeros(max_rows, dtype=torch.int64, device=dev)   # the new tokens' pool rows
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=dev)   # committed rows per sequence
         M = max_rows
         bf = dict(dtype=torch.bfloat16, device=dev)
@@ -352,19 +364,34 @@ class QwenModel:
             pl.add_py("all_reduce", lambda part=part: self.comm.all_reduce(part))
             pl.add("tsds_residual_add_f32", _p(xb), _p(part), M, s.hidden)
 
+        kv = self.kv
+        if kv is not None:
+            # the new tokens' pool rows (SGLang's out_cache_loc) from the table
+            pl.add("tsds_table_rows", _p(kv.table), kv.table_ld, _p(kv.req_rows), _p(st), B, T, _p(self.out_loc))
         for i, L in enumerate(self.layers):
-            kc, vc = self.k_cache[i], self.v_cache[i]
             pl.add("tsds_rms_norm", _p(xb), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear", _p(self.xn), s.hidden, _p(L.w_qkv), _p(self.qkv), ls.qkv_dim, M, ls.qkv_dim,
                    s.hidden, _p(lw), lb)
-            pl.add("tsds_qk_norm_rope_kv", _p(self.qkv), _p(L.q_norm) if qn else None,
-                   _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(ps), _p(st),
-                   _p(self.q), _p(kc), _p(vc), B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
-                   self.rope_len, eps)
-            pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(st),
-                   _p(tree_mask), mask_origin, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
-                   self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes,
-                   _p(self.status))
+            if kv is None:
+                kc, vc = self.k_cache[i], self.v_cache[i]
+                pl.add("tsds_qk_norm_rope_kv", _p(self.qkv), _p(L.q_norm) if qn else None,
+                       _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(ps), _p(st),
+                       _p(self.q), _p(kc), _p(vc), B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
+                       self.rope_len, eps)
+                pl.add("tsds_verify_attention", _p(self.q), _p(kc), _p(vc), _p(self.attn), _p(st),
+                       _p(tree_mask), mask_origin, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq,
+                       self.max_seq, self.split_keys, float(s.head_dim ** -0.5), _p(self.attn_ws),
+                       self.attn_ws_bytes, _p(self.status))
+            else:
+                kp, vp = kv.k_pools[i], kv.v_pools[i]
+                pl.add("tsds_qk_norm_rope_kv_paged", _p(self.qkv), _p(L.q_norm) if qn else None,
+                       _p(L.k_norm) if qn else None, _p(self.cos), _p(self.sin), _p(ps), _p(self.out_loc),
+                       _p(self.q), _p(kp), _p(vp), M, ls.n_heads, ls.n_kv_heads, s.head_dim, kv.pool_rows,
+                       self.rope_len, eps, _p(self.status))
+                pl.add("tsds_verify_attention_paged", _p(self.q), _p(kp), _p(vp), _p(self.attn), _p(st),
+                       _p(tree_mask), mask_origin, _p(kv.table), kv.table_ld, _p(kv.req_rows), kv.pool_rows,
+                       kv.page_size, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq, self.split_keys,
+                       float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes, _p(self.status))
             row_parallel(self.attn, ls.q_dim, L.w_o, ls.q_dim)
             pl.add("tsds_rms_norm", _p(xb), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), ls.intermediate, M,
@@ -498,7 +525,7 @@ class QwenModel:
         pl.extend(self.head_plan(B, T, argmax_out, argmax_stride, last_only, logits_out))
         return pl
 
-    # -- prefill (untimed set-up: cuBLAS + SDPA) -------------------------------
+    # -- prefill (untimed set-up, on this library's kernels) ---------------------
     @torch.no_grad()
     def prefill(self, prompt: torch.Tensor, lengths: torch.Tensor | None = None) -> torch.Tensor:
         """Process a [B, P] prompt from row 0; returns the hidden states
@@ -507,53 +534,97 @@ class QwenModel:
         padding; the causal attention keeps every real token's state
         independent of the padding behind it, and lengths = lengths (the
         padding's cache rows lie past the sequence and are overwritten by the
-        next forward)."""
+        next forward).
+
+        Every step runs on this library's kernels (qwen_model.py:100-146 at
+        T = P): the embedding gather, RMSNorm, the tcgen05 GEMMs over row
+        chunks of at most 256 (their epilogues: plain, SwiGLU, residual; the
+        fp32 partial + all-reduce + residual add under tensor parallelism),
+        QK-norm/RoPE/KV write, and the prompt's causal attention - the
+        tcgen05 kernel in one call when it is switched on, else the verify
+        kernel over query chunks of at most 1024 / (q heads per kv head)
+        tokens, chunk c attending to the cache rows below it like a verify
+        step that starts at c."""
+        from . import ops
         s, ls = self.shape, self.lshape
         B, P = prompt.shape
+        assert P <= self.max_seq, "prompt longer than the cache"
         if lengths is not None:
             lengths = torch.as_tensor(lengths).to(torch.int32)
             assert lengths.shape == (B,) and int(lengths.min()) >= 1 and int(lengths.max()) <= P, \
                 "prompt lengths must be in 1..P"
         dev = self.device
-        prompt = prompt.to(dev)
-        x = self.embed_w[prompt].reshape(B * P, s.hidden)
+        M = B * P
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        x = ops.embed(prompt.to(dev, torch.int64).reshape(-1).contiguous(), self.embed_w)
         pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(B)
         starts = torch.zeros(B, dtype=torch.int32, device=dev)
-        from . import ops
-        q = torch.empty(B * P, ls.q_dim, dtype=torch.bfloat16, device=dev)
+        xn = torch.empty(M, s.hidden, **bf)
+        qkv = torch.empty(M, ls.qkv_dim, **bf)
+        q = torch.empty(M, ls.q_dim, **bf)
+        a = torch.empty(M, ls.q_dim, **bf)
+        h = torch.empty(M, ls.intermediate, **bf)
+        part = torch.empty(M, s.hidden, dtype=torch.float32, device=dev) if self.layer_tp > 1 else None
+        chunks = [(r, min(M, r + 256)) for r in range(0, M, 256)]
 
         def row_parallel(inp, w):
-            y = inp @ w.T
-            if self.layer_tp > 1:
-                y = y.float()
-                self.comm.all_reduce(y)
-                y = y.to(torch.bfloat16)
-            return y
+            """x += inp @ w^T (all-reduced over the tensor-parallel ranks)."""
+            for r0, r1 in chunks:
+                if part is None:
+                    ops.linear_residual(inp[r0:r1], w, x[r0:r1], out=x[r0:r1])
+                else:
+                    ops.linear_f32(inp[r0:r1], w, out=part[r0:r1])
+            if part is not None:
+                self.comm.all_reduce(part)
+                ops.residual_add_f32(x, part)
 
+        G = ls.n_heads // ls.n_kv_heads
+        Tc = max(1, 1024 // G)   # query tokens per call of the verify kernel
+        kv = self.kv
+        if kv is not None:
+            loc = torch.empty(M, dtype=torch.int64, device=dev)
+            _lib.call("tsds_table_rows", _p(kv.table), kv.table_ld, _p(kv.req_rows), _p(starts), B, P, _p(loc),
+                      ops._stream())
         for i, L in enumerate(self.layers):
-            xn = ops.rms_norm(x, L.ln1, s.eps)
-            qkv = xn @ L.w_qkv.T
-            ops.qk_norm_rope_kv(qkv, L.q_norm if self.qk_norm else None, L.k_norm if self.qk_norm else None,
-                                self.cos, self.sin, pos, starts, q, self.k_cache[i], self.v_cache[i], B, P,
-                                ls.n_heads, ls.n_kv_heads, s.eps)
+            ops.rms_norm(x, L.ln1, s.eps, out=xn)
+            for r0, r1 in chunks:
+                ops.linear(xn[r0:r1], L.w_qkv, out=qkv[r0:r1])
+            qn_w, kn_w = (L.q_norm, L.k_norm) if self.qk_norm else (None, None)
+            qv = q.view(B, P, ls.n_heads, s.head_dim)
+            av = a.view(B, P, ls.n_heads, s.head_dim)
+            if kv is not None:
+                kp, vp = kv.k_pools[i], kv.v_pools[i]
+                ops.qk_norm_rope_kv_paged(qkv, qn_w, kn_w, self.cos, self.sin, pos, loc, q, kp, vp, ls.n_heads,
+                                          ls.n_kv_heads, s.eps)
+                for c0 in range(0, P, Tc):
+                    c1 = min(P, c0 + Tc)
+                    st = torch.full((B,), c0, dtype=torch.int32, device=dev)
+                    av[:, c0:c1] = ops.verify_attention_paged(
+                        qv[:, c0:c1].contiguous(), kp, vp, st, kv.table, req_rows=kv.req_rows,
+                        page_size=kv.page_size, max_kv=c1, split_keys=self.split_keys)
+                row_parallel(a, L.w_o)
+                ops.rms_norm(x, L.ln2, s.eps, out=xn)
+                for r0, r1 in chunks:
+                    ops.linear_swiglu(xn[r0:r1], L.w_gu, out=h[r0:r1])
+                row_parallel(h, L.w_d)
+                continue
+            kc, vc = self.k_cache[i], self.v_cache[i]
+            ops.qk_norm_rope_kv(qkv, qn_w, kn_w, self.cos, self.sin, pos, starts, q, kc, vc, B, P, ls.n_heads,
+                                ls.n_kv_heads, s.eps)
             if ops.attention_tc():
-                # the prompt's causal attention on the library's tcgen05
-                # kernel: every prompt row of a kv head in one call, one key
-                # split (no combine pass)
-                a = ops.verify_attention(q.view(B, P, ls.n_heads, s.head_dim), self.k_cache[i], self.v_cache[i],
-                                         starts, max_kv=P, split_keys=(P + 127) // 128 * 128)
-                a = a.reshape(B * P, ls.q_dim)
+                # every prompt row of a kv head in one call, one key split (no combine pass)
+                ops.verify_attention(qv, kc, vc, starts, max_kv=P, split_keys=(P + 127) // 128 * 128, out=av)
             else:
-                qh = q.reshape(B, P, ls.n_heads, s.head_dim).transpose(1, 2)
-                kh = self.k_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
-                vh = self.v_cache[i][:, :, :P].repeat_interleave(s.q_per_kv, dim=1)
-                a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True)
-                a = a.transpose(1, 2).reshape(B * P, ls.q_dim)
-            x = x + row_parallel(a, L.w_o)
-            xn = ops.rms_norm(x, L.ln2, s.eps)
-            gu = xn @ L.w_gu.T
-            h = F.silu(gu[:, :ls.intermediate]) * gu[:, ls.intermediate:]
-            x = x + row_parallel(h, L.w_d)
+                for c0 in range(0, P, Tc):
+                    c1 = min(P, c0 + Tc)
+                    st = torch.full((B,), c0, dtype=torch.int32, device=dev)
+                    av[:, c0:c1] = ops.verify_attention(qv[:, c0:c1].contiguous(), kc, vc, st, max_kv=c1,
+                                                        split_keys=self.split_keys)
+            row_parallel(a, L.w_o)
+            ops.rms_norm(x, L.ln2, s.eps, out=xn)
+            for r0, r1 in chunks:
+                ops.linear_swiglu(xn[r0:r1], L.w_gu, out=h[r0:r1])
+            row_parallel(h, L.w_d)
         if lengths is None:
             self.lengths.fill_(P)
         else:
@@ -573,7 +644,8 @@ class QwenModel:
         """Final norm + full bf16 logits (set-up / tests only)."""
         from . import ops
         xn = ops.rms_norm(hidden.reshape(-1, self.shape.hidden).contiguous(), self.norm_w, self.shape.eps)
-        loc = xn @ self.lm_head_w.T
+        loc = torch.cat([ops.lm_head_argmax(xn[r:r + 256], self.lm_head_w, return_logits=True)[1]
+                         for r in range(0, xn.shape[0], 256)])
         if self.vocab_tp == 1:
             return loc
         allv = torch.empty(self.vocab_tp * loc.numel(), dtype=loc.dtype, device=loc.device)

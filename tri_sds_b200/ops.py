@@ -208,6 +208,31 @@ def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
     return out
 
 
+def linear_f32(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None):
+    """x @ w^T as an unrounded fp32 [M, n_out] partial: a row-parallel
+    shard's product before the all-reduce over the tensor-parallel ranks."""
+    _bf16_cuda(x, w)
+    _cuda(torch.float32, out)
+    M, K = x.shape
+    n_out = w.shape[0]
+    _need(w.shape[1] == K and w.is_contiguous(), "w must be contiguous [n_out, K]")
+    out = torch.empty(M, n_out, dtype=torch.float32, device=x.device) if out is None else out
+    ws, nb = _lin_ws(M, n_out, K, x.device)
+    _lib.call("tsds_linear_f32", _p(x), x.stride(0), _p(w), _p(out), out.stride(0), M, n_out, K, _p(ws), nb,
+              _stream())
+    return out
+
+
+def residual_add_f32(x: torch.Tensor, partial: torch.Tensor):
+    """x = bf16(x + bf16(partial)) in place (qwen_model.py:133-134,143-144
+    rounding) for the all-reduced fp32 partial of a row-parallel projection."""
+    _bf16_cuda(x)
+    _cuda(torch.float32, partial)
+    _need(x.is_contiguous() and partial.is_contiguous() and partial.shape == x.shape, "x / partial mismatch")
+    _lib.call("tsds_residual_add_f32", _p(x), _p(partial), x.shape[0], x.shape[1], _stream())
+    return x
+
+
 def fused_oproj_residual(attn_flat, o_w_t, x):
     """fused_qwen_decode.py:179-204: x + attn_flat @ o_w_t."""
     return linear_residual(attn_flat, _out_in(o_w_t), x)
@@ -272,6 +297,52 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     _lib.call("tsds_verify_attention", _p(q), _p(k_cache), _p(v_cache), _p(out), _p(starts), _p(tree_mask),
               int(mask_origin), B, T, Hq, Hkv, D, S, max_kv, split_keys, scale, _p(ws), nb, _p(status), _stream())
     return out
+
+
+def verify_attention_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, starts: torch.Tensor,
+                           token_table: torch.Tensor, req_rows: torch.Tensor | None = None, page_size: int = 1,
+                           tree_mask: torch.Tensor | None = None, max_kv: int | None = None, split_keys: int = 1024,
+                           scale: float | None = None, out: torch.Tensor | None = None, mask_origin: int = -1):
+    """verify_attention over SGLang-style token pools: k_pool / v_pool
+    [pool_rows, Hkv, D], position p of sequence b at pool row
+    token_table[req_rows[b] (or b), p] (int32 [reqs, table_ld])."""
+    _bf16_cuda(q, k_pool, v_pool, out)
+    _cuda(torch.int32, token_table)
+    _cuda(torch.int64, req_rows)
+    B, T, Hq, D = q.shape
+    pool_rows, Hkv = k_pool.shape[0], k_pool.shape[1]
+    _need(q.is_contiguous() and k_pool.is_contiguous() and v_pool.is_contiguous() and token_table.is_contiguous(),
+          "contiguous tensors expected")
+    _need(v_pool.shape == k_pool.shape and k_pool.shape[2] == D, "pool shape mismatch")
+    table_ld = token_table.shape[1]
+    starts = starts.to(device=q.device, dtype=torch.int32).contiguous()
+    if tree_mask is not None:
+        tree_mask = tree_mask.to(device=q.device, dtype=torch.int32).contiguous()
+    max_kv = table_ld if max_kv is None else int(max_kv)
+    scale = D ** -0.5 if scale is None else float(scale)
+    out = torch.empty_like(q) if out is None else out
+    nb = _lib.query("tsds_attention_workspace_bytes", B, T, Hq, Hkv, D, max_kv, split_keys)
+    ws = _scratch.get(nb, q.device, "attention") if nb else None
+    status = _scratch.status_word(q.device)
+    _lib.call("tsds_verify_attention_paged", _p(q), _p(k_pool), _p(v_pool), _p(out), _p(starts), _p(tree_mask),
+              int(mask_origin), _p(token_table), table_ld, _p(req_rows), pool_rows, int(page_size), B, T, Hq, Hkv, D,
+              max_kv, split_keys, scale, _p(ws), nb, _p(status), _stream())
+    return out
+
+
+def qk_norm_rope_kv_paged(qkv, q_norm_w, k_norm_w, cos, sin, positions, out_loc, q_out, k_pool, v_pool, Hq, Hkv,
+                          eps=1e-6):
+    """QK-norm + RoPE of the q/k heads of ``qkv`` [M, (Hq+2Hkv)*D]; q -> q_out,
+    row m's k/v -> pool row out_loc[m] (SGLang's out_cache_loc)."""
+    _bf16_cuda(qkv, q_norm_w, k_norm_w, cos, sin, q_out, k_pool, v_pool)
+    _cuda(torch.int32, positions)
+    _cuda(torch.int64, out_loc)
+    M = qkv.shape[0]
+    D = k_pool.shape[-1]
+    status = _scratch.status_word(qkv.device)
+    _lib.call("tsds_qk_norm_rope_kv_paged", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin), _p(positions),
+              _p(out_loc), _p(q_out), _p(k_pool), _p(v_pool), M, Hq, Hkv, D, k_pool.shape[0], cos.shape[0],
+              float(eps), _p(status), _stream())
 
 
 def attention_gqa(q, k, v, kv_len, q_per_kv):
