@@ -284,9 +284,10 @@ int tsds_table_rows(const int32_t* token_table, int64_t table_ld, const int64_t*
  * rows become the sequence's next positions.  With L = lengths[b] (the
  * tree's root at position L), a = accept_len[b] and path / accept_len as
  * tsds_accept_tree writes them (accepted non-root nodes, [B][depth+1]):
- * token_table[req(b) * table_ld + L + 1 + j] = old
- * token_table[req(b) * table_ld + L + path[b][j]] for j < a, then
- * lengths[b] += a + 1.  kept_rows (optional, [B][depth+2], -1 padded)
+ * for j = 0 .. a-1 the entries at positions L + 1 + j and L + path[b][j] of
+ * row req(b) of token_table are swapped (the table stays a permutation: the
+ * rejected nodes' rows land past the new length, where the next forward
+ * writes), then lengths[b] += a + 1.  kept_rows (optional, [B][depth+2], -1 padded)
  * receives the pool rows of positions L..L+a afterwards, so the caller can
  * free the tree's other rows.  root_feat (optional) gets the hidden state of
  * the last accepted node as tsds_tree_commit does (hidden [B][n_nodes+1][N]).

@@ -91,7 +91,7 @@ def test_tuning_switches_clamp_and_read_back():
             lib.tsds_set_gemv_max_rows(v)
             assert lib.tsds_get_gemv_max_rows() == want
     finally:
-        lib.tsds_set_gemm_dp_rows(0)
+        lib.tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
         lib.tsds_set_gemm_pair_rows(0)
         lib.tsds_set_gemm_dp_slack(15)
         lib.tsds_set_gemv_splitk(0)

@@ -154,7 +154,7 @@ def switches():
     from tri_sds_b200 import _lib
     lib = _lib.load()
     yield lib
-    lib.tsds_set_gemm_dp_rows(0)
+    lib.tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
     lib.tsds_set_gemm_dp_slack(15)
     lib.tsds_set_gemm_ctas_per_sm(2)
 

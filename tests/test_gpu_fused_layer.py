@@ -75,7 +75,7 @@ def test_fused_equals_per_op_bitwise_data_parallel(B, T):
     try:
         _bitwise_case(B, T)
     finally:
-        _lib.load().tsds_set_gemm_dp_rows(0)
+        _lib.load().tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
         _lib.load().tsds_set_gemm_dp_slack(15)
 
 

@@ -17,7 +17,7 @@ def dp_ops():
     _ops.set_gemv_max_rows(0)
     _lib.load().tsds_set_gemm_dp_rows(1)   # every M with a whole tile per CTA
     yield _ops
-    _lib.load().tsds_set_gemm_dp_rows(0)
+    _lib.load().tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
 
 
 def _data(M, n_out, K, seed, rows_mult=1):

@@ -9,8 +9,9 @@ against the contiguous ones on the same keys.
   tree masks, one split and several (combine pass).
 * tsds_qk_norm_rope_kv_paged writes q and the K/V rows exactly where the
   contiguous kernel writes them, only at the out_cache_loc pool rows.
-* tsds_tree_commit_paged moves table entries (no K/V) as tsds_tree_commit
-  moves rows, lists the kept pool rows and advances the lengths.
+* tsds_tree_commit_paged swaps table entries (no K/V moves) so the accepted
+  nodes take the positions tsds_tree_commit moves their rows to, lists the
+  kept pool rows and advances the lengths.
 * A table entry outside the pool is never dereferenced: the call reports
   TSDS_E_INDEX through the status word.
 """
@@ -125,7 +126,8 @@ def test_paged_tree_commit_moves_table_entries():
     for b in range(B):
         row, L, a = int(req[b]), int(lengths[b]), int(acc[b])
         for j in range(a):
-            want[row, L + 1 + j] = want[row, L + int(path[b, j])]
+            fr, to = L + int(path[b, j]), L + 1 + j
+            want[row, fr], want[row, to] = want[row, to].clone(), want[row, fr].clone()
         kept_want[b, :a + 1] = want[row, L:L + a + 1].to(torch.int64)
     d = {k: v.to(DEV) for k, v in dict(table=table, req=req, lengths=lengths, acc=acc, path=path,
                                         hidden=hidden).items()}

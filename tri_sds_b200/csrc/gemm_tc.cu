@@ -490,106 +490,119 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           alive = false;
           break;
         }
-        // element e = (row rr of the slice, 4-column group g).  A thread takes
-        // EU elements per pass and issues the loads of all their partials
-        // (QB partials per batch) before summing, so a pass costs one L2
-        // round trip instead of one per element; each element still sums its
-        // partials in CTA order from zero.
-        constexpr int EU = SW ? 2 : 4;  // elements per pass
-        constexpr int QB = 4;           // partials per batch
-        constexpr int NH = SW ? 2 : 1;  // rows per element: the gate row and its up row
-        for (int e0 = r; e0 < nel; e0 += 128 * EU) {
-          float4 acc[EU][NH];
+        if constexpr (SW) {
+          // element e = (gate row rr of the slice, 4-column group g): its gate
+          // row and its up row 64 below are summed over the partials in CTA
+          // order from zero.  A thread takes EU elements per pass and issues
+          // the loads of all their partials (QB per batch) before summing, so
+          // a pass costs one L2 round trip instead of one per element.
+          constexpr int EU = 2, QB = 4;
+          for (int e0 = r; e0 < nel; e0 += 128 * EU) {
+            float4 acc[EU][2];
 #pragma unroll
-          for (int u = 0; u < EU; ++u)
+            for (int u = 0; u < EU; ++u) acc[u][0] = acc[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q0 = 0; q0 < nq; q0 += QB) {
+              float4 f[EU][QB][2];
 #pragma unroll
-            for (int h = 0; h < NH; ++h) acc[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-          // the residual (possibly the output buffer itself) is read before
-          // any store, its loads in flight with the partials'
-          float rv[EU][4];
-          if constexpr (EPI == EPI_RESIDUAL) {
+              for (int u = 0; u < EU; ++u) {
+                const int e = e0 + u * 128;
+                if (e < nel) {
+                  const int rr = rlo + e % R, g = e / R;
 #pragma unroll
-            for (int u = 0; u < EU; ++u) {
-              const int e = e0 + u * 128;
-              const int rr = rlo + e % R, g = e / R, j = vt * TILE_J + rr;
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                rv[u][i] = (e < nel && j < p.n_out && 4 * g + i < p.M) ? bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j])
-                                                                         : 0.f;
-            }
-          }
-          for (int q0 = 0; q0 < nq; q0 += QB) {
-            float4 f[EU][QB][NH];
-#pragma unroll
-            for (int u = 0; u < EU; ++u) {
-              const int e = e0 + u * 128;
-              if (e < nel) {
-                const int rr = rlo + e % R, g = e / R;
-#pragma unroll
-                for (int i = 0; i < QB; ++i)
-                  if (q0 + i < nq) {
-                    const int q = (q_lo + q0 + i) * CG + crank;
-                    const int qs = q0 + i == 0 ? lo_slot : 0;
-                    const float4* src = reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
-                                        (size_t)g * TILE_J + rr;
-#pragma unroll
-                    for (int h = 0; h < NH; ++h) f[u][i][h] = __ldcg(src + h * 64);
-                  }
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < EU; ++u)
-              if (e0 + u * 128 < nel) {
-#pragma unroll
-                for (int i = 0; i < QB; ++i)
-                  if (q0 + i < nq) {
-#pragma unroll
-                    for (int h = 0; h < NH; ++h) {
-                      acc[u][h].x += f[u][i][h].x;
-                      acc[u][h].y += f[u][i][h].y;
-                      acc[u][h].z += f[u][i][h].z;
-                      acc[u][h].w += f[u][i][h].w;
+                  for (int i = 0; i < QB; ++i)
+                    if (q0 + i < nq) {
+                      const int q = (q_lo + q0 + i) * CG + crank;
+                      const int qs = q0 + i == 0 ? lo_slot : 0;
+                      const float4* src =
+                          reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                          (size_t)g * TILE_J + rr;
+                      f[u][i][0] = __ldcg(src);
+                      f[u][i][1] = __ldcg(src + 64);
                     }
-                  }
-              }
-          }
-#pragma unroll
-          for (int u = 0; u < EU; ++u) {
-            const int e = e0 + u * 128;
-            if (e >= nel) continue;
-            const int rr = rlo + e % R, g = e / R;
-            const float a4[4] = {acc[u][0].x, acc[u][0].y, acc[u][0].z, acc[u][0].w};
-            if constexpr (SW) {
-              // the SwiGLU of the whole-tile epilogue: gate and up rounded
-              // to bf16, silu(gate) rounded, the product rounded
-              const float b4[4] = {acc[u][NH - 1].x, acc[u][NH - 1].y, acc[u][NH - 1].z, acc[u][NH - 1].w};
-              const int j = vt * 64 + rr;
-              if (j < p.n_out) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int m = 4 * g + i;
-                  if (m < p.M) {
-                    const float gv = rbf(a4[i]);
-                    const float sv = rbf(gv / (1.0f + expf(-gv)));
-                    p.out[(int64_t)m * p.ldo + j] = f2bf(sv * rbf(b4[i]));
-                  }
                 }
               }
-            } else {
-              const int j = vt * TILE_J + rr;
-              if (j < p.n_out) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int m = 4 * g + i;
-                  if (m < p.M) {
-                    const int64_t o = (int64_t)m * p.ldo + j;
-                    if constexpr (EPI == EPI_STORE_F32)
-                      reinterpret_cast<float*>(p.out)[o] = a4[i];
-                    else if constexpr (EPI == EPI_STORE)
-                      p.out[o] = f2bf(a4[i]);
-                    else
-                      p.out[o] = f2bf(rv[u][i] + rbf(a4[i]));
-                  }
+              for (int u = 0; u < EU; ++u)
+                if (e0 + u * 128 < nel) {
+#pragma unroll
+                  for (int i = 0; i < QB; ++i)
+                    if (q0 + i < nq) {
+#pragma unroll
+                      for (int h = 0; h < 2; ++h) {
+                        acc[u][h].x += f[u][i][h].x;
+                        acc[u][h].y += f[u][i][h].y;
+                        acc[u][h].z += f[u][i][h].z;
+                        acc[u][h].w += f[u][i][h].w;
+                      }
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < EU; ++u) {
+              const int e = e0 + u * 128;
+              if (e >= nel) continue;
+              const int rr = rlo + e % R, g = e / R;
+              const int j = vt * 64 + rr;
+              if (j >= p.n_out) continue;
+              // the SwiGLU of the whole-tile epilogue: gate and up rounded to
+              // bf16, silu(gate) rounded, the product rounded
+              const float a4[4] = {acc[u][0].x, acc[u][0].y, acc[u][0].z, acc[u][0].w};
+              const float b4[4] = {acc[u][1].x, acc[u][1].y, acc[u][1].z, acc[u][1].w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int m = 4 * g + i;
+                if (m < p.M) {
+                  const float gv = rbf(a4[i]);
+                  const float sv = rbf(gv / (1.0f + expf(-gv)));
+                  p.out[(int64_t)m * p.ldo + j] = f2bf(sv * rbf(b4[i]));
+                }
+              }
+            }
+          }
+        } else {
+          for (int e0 = r; e0 < nel; e0 += 128) {
+            const int rr = rlo + e0 % R, g = e0 / R;
+            const int j = vt * TILE_J + rr;
+            float rv[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (j < p.n_out && 4 * g + i < p.M) rv[i] = bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j]);
+            }
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            constexpr int QB = 8;
+            for (int q0 = 0; q0 < nq; q0 += QB) {
+              float4 f[QB];
+#pragma unroll
+              for (int i = 0; i < QB; ++i)
+                if (q0 + i < nq) {
+                  const int q = (q_lo + q0 + i) * CG + crank;
+                  const int qs = q0 + i == 0 ? lo_slot : 0;
+                  f[i] = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)(q * 2 + qs) * p.Npad) * TILE_J) +
+                                (size_t)g * TILE_J + rr);
+                }
+#pragma unroll
+              for (int i = 0; i < QB; ++i)
+                if (q0 + i < nq) {
+                  acc.x += f[i].x;
+                  acc.y += f[i].y;
+                  acc.z += f[i].z;
+                  acc.w += f[i].w;
+                }
+            }
+            if (j < p.n_out) {
+              const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int m = 4 * g + i;
+                if (m < p.M) {
+                  const int64_t o = (int64_t)m * p.ldo + j;
+                  if constexpr (EPI == EPI_STORE_F32)
+                    reinterpret_cast<float*>(p.out)[o] = a4[i];
+                  else if constexpr (EPI == EPI_STORE)
+                    p.out[o] = f2bf(a4[i]);
+                  else
+                    p.out[o] = f2bf(rv[i] + rbf(a4[i]));
                 }
               }
             }
@@ -634,7 +647,9 @@ std::atomic<int> g_ctas_per_sm{2};
 std::atomic<int> g_pair_min_rows{0};
 // Token rows from which a projection may run data-parallel instead of
 // stream-K (when within the slack below); 0: never.
-std::atomic<int> g_dp_min_rows{0};
+// data-parallel schedule from 128 token rows on (the B=8 tree verify's 208
+// rows: gate/up 139 us instead of 161 us; below 128 rows stream-K stays)
+std::atomic<int> g_dp_min_rows{128};
 // Largest makespan increase (percent over the ideal tiles / units) the
 // data-parallel schedule may cost.
 std::atomic<int> g_dp_slack_pct{15};

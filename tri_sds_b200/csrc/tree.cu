@@ -974,11 +974,15 @@ extern "C" int tsds_tree_commit(void* k_cache, void* v_cache, int layers, int B,
   return tsds_launch_status();
 }
 
-// Pooled KV commit: one CTA per sequence.  Thread 0 moves the accepted
-// nodes' table entries down to the positions after the root (increasing j:
-// path[j'] > path[j] >= j + 1 for j' > j, so no entry is read after it was
-// overwritten), lists the kept pool rows and advances the length; the CTA
-// copies the last accepted node's hidden state to root_feat.
+// Pooled KV commit: one CTA per sequence.  Thread 0 swaps the accepted
+// nodes' table entries with the positions after the root, so the table stays
+// a permutation of its rows: the rejected nodes' rows move to the positions
+// past the new length, where the next forward writes, and no pool row ever
+// backs two positions.  Increasing j is safe: path[j] > path[j'] for j' < j,
+// and position L + path[j] is never one an earlier swap wrote (those are
+// L + 1 + j' < L + path[j] and L + path[j'] != L + path[j]).  It then lists
+// the kept pool rows and advances the length; the CTA copies the last
+// accepted node's hidden state to root_feat.
 __global__ void tree_commit_paged_kernel(int* __restrict__ table, long long table_ld,
                                          const long long* __restrict__ req_rows, int* __restrict__ lengths,
                                          const int* __restrict__ path, const int* __restrict__ accept_len, int depth,
@@ -997,7 +1001,12 @@ __global__ void tree_commit_paged_kernel(int* __restrict__ table, long long tabl
   }
   if (threadIdx.x != 0) return;
   int* row = table + (req_rows ? req_rows[b] : (long long)b) * table_ld;
-  for (int j = 0; j < a; ++j) row[L + 1 + j] = row[L + path[b * (depth + 1) + j]];
+  for (int j = 0; j < a; ++j) {
+    const int from = L + path[b * (depth + 1) + j], to = L + 1 + j;
+    const int r = row[from];
+    row[from] = row[to];
+    row[to] = r;
+  }
   if (kept)
     for (int i = 0; i < depth + 2; ++i) kept[(long long)b * (depth + 2) + i] = i <= a ? row[L + i] : -1;
   lengths[b] = L + a + 1;
