@@ -580,13 +580,15 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
 }
 
 // key groups of a split: a function of split_keys alone (so a row's
-// accumulation order never depends on the call's shape): the largest divisor
-// of ATT_STAGES (1, 2, 4) that does not exceed the split's tiles.  Long
-// splits spread over four warps, so a short context (one split of up to 1024
-// keys) takes a few tiles per warp instead of a chain of them.
+// accumulation order never depends on the call's shape), each a divisor of
+// ATT_STAGES.  Splits of 1024 keys or more spread over four warps, so a short
+// context (one split) takes a few tiles per warp instead of a chain of them;
+// shorter splits use two, which leaves room for up to four row groups, so a
+// few query rows over a long context (decode, K+1 = 5) share each K/V tile
+// within one CTA instead of re-reading it in several.
 int attn_key_groups(int split_keys) {
   const int tiles = split_keys / TILE;
-  return tiles >= 4 ? 4 : (tiles >= 2 ? 2 : 1);
+  return tiles >= 16 ? 4 : (tiles >= 2 ? 2 : 1);
 }
 static_assert(ATT_STAGES % 4 == 0, "every key-group count must divide the ring depth");
 
