@@ -76,7 +76,7 @@ def _args():
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--dp-rows", type=int, default=None,
                     help="token rows from which a tcgen05 projection with at least one whole weight tile per CTA "
-                         "runs data-parallel instead of stream-K (library default 0: never)")
+                         "runs data-parallel instead of stream-K (library default 128)")
     ap.add_argument("--dp-slack", type=int, default=None,
                     help="largest makespan increase (percent) the data-parallel schedule may cost over the ideal "
                          "(library default 15; above 100 it may leave CTAs idle for fewer tiles than CTAs)")

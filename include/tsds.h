@@ -162,7 +162,7 @@ int tsds_get_gemm_pair_rows(void);
 /* Token rows M from which a tcgen05 projection may run data-parallel -
  * min(tiles, CTAs) CTAs (or CTA pairs) take whole weight tiles, no split
  * tiles and so no fp32 partials exchanged at the end - instead of
- * stream-K; 0 (default): always stream-K.  It is chosen where its makespan,
+ * stream-K; 0: always stream-K (default 128).  It is chosen where its makespan,
  * ceil(tiles / used CTAs) tiles, exceeds the ideal tiles / CTAs by at most
  * tsds_set_gemm_dp_slack percent (default 15; with fewer tiles than CTAs
  * that allows leaving CTAs idle).  Process-wide tuning switches for large

@@ -707,9 +707,9 @@ std::atomic<int> g_ctas_per_sm{2};
 // Token rows from which a projection runs on CTA pairs (CG = 2); 0: never.
 std::atomic<int> g_pair_min_rows{0};
 // Token rows from which a projection may run data-parallel instead of
-// stream-K (when within the slack below); 0: never.
-// data-parallel schedule from 128 token rows on (the B=8 tree verify's 208
-// rows: gate/up 139 us instead of 161 us; below 128 rows stream-K stays)
+// stream-K (when within the slack below); 0: never.  Default 128: the B=8
+// tree verify's 208 rows run gate/up in 139 us instead of 161 us; below 128
+// rows stream-K stays.
 std::atomic<int> g_dp_min_rows{128};
 // Largest makespan increase (percent over the ideal tiles / units) the
 // data-parallel schedule may cost.
