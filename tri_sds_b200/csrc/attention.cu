@@ -15,12 +15,17 @@
 //   registers; K / V fragments come from the swizzled tiles by ldmatrix.
 // * fp32 online softmax in the exp2 domain; row max / sum across the four
 //   lanes sharing a row by shuffles.
-// * Keys are split into fixed chunks of `split_keys` rows.  A split writes
-//   its unnormalised O with (m, l) to the workspace and a combine pass merges
-//   the splits in index order.  Split boundaries depend only on the key
-//   index, and masked / empty splits contribute exact zeros, so a query's
-//   output is bit-identical whether it is verified with T tokens or decoded
-//   alone.
+// * Keys are split into fixed chunks of `split_keys` rows, and a split's
+//   tiles into KG key groups (a function of split_keys alone).  With one
+//   split the rows are normalised in place; otherwise a split writes its
+//   unnormalised O with (m, l) to the workspace and a combine pass merges
+//   the splits in index order.  Split and key-group boundaries depend only
+//   on the key index, and masked / empty splits contribute exact zeros, so a
+//   query's output is bit-identical whether it is verified with T tokens or
+//   decoded alone.
+// * The K/V cache is contiguous ([B][Hkv][S][D], tsds_verify_attention) or
+//   paged in token pools through a request-to-token table
+//   (tsds_verify_attention_paged); both feed the same consumers.
 #include "common.cuh"
 #include "linear.cuh"
 #include "tc_core.cuh"
