@@ -164,7 +164,7 @@ int tsds_get_gemm_pair_rows(void);
  * tiles and so no fp32 partials exchanged at the end - instead of
  * stream-K; 0: always stream-K (default 128).  It is chosen where its makespan,
  * ceil(tiles / used CTAs) tiles, exceeds the ideal tiles / CTAs by at most
- * tsds_set_gemm_dp_slack percent (default 15; with fewer tiles than CTAs
+ * tsds_set_gemm_dp_slack percent (default 100; with fewer tiles than CTAs
  * that allows leaving CTAs idle).  Process-wide tuning switches for large
  * M.  The two schedules sum a split tile in a different order, so results
  * may differ in the last bit between them. */

@@ -93,7 +93,7 @@ def test_tuning_switches_clamp_and_read_back():
     finally:
         lib.tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
         lib.tsds_set_gemm_pair_rows(0)
-        lib.tsds_set_gemm_dp_slack(15)
+        lib.tsds_set_gemm_dp_slack(_lib.GEMM_DP_SLACK_DEFAULT)
         lib.tsds_set_gemv_splitk(0)
         lib.tsds_set_gemv_max_rows(0)
 

@@ -155,7 +155,7 @@ def switches():
     lib = _lib.load()
     yield lib
     lib.tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
-    lib.tsds_set_gemm_dp_slack(15)
+    lib.tsds_set_gemm_dp_slack(_lib.GEMM_DP_SLACK_DEFAULT)
     lib.tsds_set_gemm_ctas_per_sm(2)
 
 

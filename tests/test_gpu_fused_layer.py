@@ -76,7 +76,7 @@ def test_fused_equals_per_op_bitwise_data_parallel(B, T):
         _bitwise_case(B, T)
     finally:
         _lib.load().tsds_set_gemm_dp_rows(_lib.GEMM_DP_ROWS_DEFAULT)
-        _lib.load().tsds_set_gemm_dp_slack(15)
+        _lib.load().tsds_set_gemm_dp_slack(_lib.GEMM_DP_SLACK_DEFAULT)
 
 
 def _bitwise_case(B, T):

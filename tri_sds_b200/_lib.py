@@ -22,6 +22,7 @@ _L = ctypes.c_int64
 PHASE_GEMM, PHASE_NORM, PHASE_PEER = 0, 1, 2
 # the library's default of tsds_set_gemm_dp_rows (tests restore it)
 GEMM_DP_ROWS_DEFAULT = 128
+GEMM_DP_SLACK_DEFAULT = 100
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_STORE_F32, EPI_QKROPE = 0, 1, 2, 4, 5
 
 
