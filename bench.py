@@ -845,6 +845,8 @@ def main():
             from tri_sds_b200 import _lib
             if a.ctas_per_sm is not None:
                 _lib.load().tsds_set_gemm_ctas_per_sm(a.ctas_per_sm)
+            if a.no_pdl:
+                _lib.load().tsds_set_pdl(0)
             if a.pair_rows is not None:
                 _lib.load().tsds_set_gemm_pair_rows(a.pair_rows)
             if a.dp_rows is not None:
