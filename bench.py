@@ -746,6 +746,18 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
     # ratio, not a number of this run
     traffic = MEASURED_TRAFFIC.get((tshape.hidden, tshape.intermediate, M)) if world == 1 else None
 
+    # ---- the projection furthest from the roofline: the target's q/k/v -------
+    # (the smallest weight matrix of a layer, where the GEMM's fixed cost per
+    # launch weighs most), timed the same way as one CUDA graph over the layers
+    qout = torch.empty(M, target.lshape.qkv_dim, dtype=torch.bfloat16, device=dev)
+
+    def qkv_pass():
+        for L in target.layers:
+            ops.linear(xin, L.w_qkv, out=qout)
+    q_us = _graph_time_us(qkv_pass, reps=3)[0] / len(target.layers)
+    q_bytes = target.layers[0].w_qkv.numel() * 2 + xin.numel() * 2 + qout.numel() * 2
+    q_ach = q_bytes / (q_us * 1e-6) / 1e9
+
     # ---- a second batch size over the same weights ---------------------------
     sub = None
     if sub_B:
@@ -792,6 +804,8 @@ def run_tsds(a, rank: int, world: int, local_rank: int):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic, "traffic_source": "ncu capture, not this run",
                          "bytes_per_launch": kbytes, "launch_us": kern_us,
+                         "lowest_gemm": {"kernel": "tsds_linear (target q/k/v, M=%d)" % M, "launch_us": q_us,
+                                         "bytes_per_launch": q_bytes, "achieved": q_ach, "frac": q_ach / peak},
                          "cycle": {"bytes_per_cycle": cycle_b,
                                    "achieved": cycle_b / (res["ms_per_step"] * 1e-3) / 1e9,
                                    "frac": cycle_b / (res["ms_per_step"] * 1e-3) / 1e9 / peak}},

@@ -243,3 +243,36 @@ def test_eagle_on_paged_kv_equals_contiguous(page, greedy, use_graph, mirror):
         n = int(pag.target.lengths[b])
         req = int(kv.req_rows[b])
         assert kept[b, :a + 1].tolist() == kv.table[req, n - a - 1:n].cpu().long().tolist()
+
+
+def test_chain_spec_on_paged_kv_equals_contiguous():
+    """The chain engine (a one-layer draft, K=4 greedy) with the target's KV
+    in token pools (one row per token, scattered) emits what it emits on the
+    contiguous cache, and greedy autoregressive decoding on the paged target
+    emits the same tokens: the commit of a chain is a length update, the
+    rejected rows' table entries are rewritten by the next forward."""
+    from oracle import qwen as oq
+    from tri_sds_b200 import ops
+    from tri_sds_b200.engine import AutoregressiveEngine, SpecEngine
+    from tri_sds_b200.model import QwenModel
+    from tri_sds_b200.paged import PagedKV
+    from tri_sds_b200.shapes import QwenShape
+    ops.set_gemv_max_rows(0)
+    small = dict(hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, intermediate=512, n_layers=2, vocab=1000)
+    wt = oq.random_qwen_weights(oq.QwenShape(**small), seed=3, std=0.08)
+    wd = {**wt, "layers": wt["layers"][:1]}
+    B, P, K, n_new = 2, 9, 4, 24
+    prompt = torch.randint(0, small["vocab"], (B, P), generator=torch.Generator().manual_seed(4))
+    outs = []
+    for paged in (False, True):
+        kv = PagedKV.allocate(2, B, 128, 2, 128, DEV, page_size=1, seed=6) if paged else None
+        tgt = QwenModel(QwenShape(**small), batch=B, max_seq=128, max_rows=B * (K + 1), device=DEV, weights=wt,
+                        kv=kv)
+        drf = QwenModel(QwenShape(**{**small, "n_layers": 1}), batch=B, max_seq=128, max_rows=B * 2, device=DEV,
+                        weights=wd)
+        outs.append(SpecEngine(tgt, drf, K).generate(prompt, n_new)[0])
+    assert torch.equal(outs[0], outs[1])
+    kv = PagedKV.allocate(2, B, 128, 2, 128, DEV, page_size=64, seed=7)
+    ar_model = QwenModel(QwenShape(**small), batch=B, max_seq=128, max_rows=B, device=DEV, weights=wt, kv=kv)
+    ar = AutoregressiveEngine(ar_model).generate(prompt, n_new)
+    assert torch.equal(outs[1], ar)
