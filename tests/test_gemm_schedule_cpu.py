@@ -8,10 +8,13 @@ iterations.
   a range boundary is "split" and its contributors exchange fp32 partials.
   The epilogue keeps at most two pending split tiles per unit (registers
   pend0 / pend1) and finds a split tile's contributors as the consecutive
-  units owner_of(first k-block) .. owner_of(last k-block).
+  units owner_of(first k-block) .. owner_of(last k-block).  Each split
+  tile's rows are summed by its reducers (split_reducers in
+  tri_sds_b200/csrc/tc_core.cuh), one slice each, and no unit reduces more
+  than one tile.
 * data-parallel (tsds_set_gemm_dp_rows, where its makespan of
   ceil(tiles / PU) tiles with PU = min(tiles, units) exceeds the ideal
-  tiles / units by at most the slack, tsds_set_gemm_dp_slack, default 15%):
+  tiles / units by at most the slack, tsds_set_gemm_dp_slack, default 100%):
   unit u takes the whole tiles [u*tiles/PU, (u+1)*tiles/PU); nothing is
   split.
 
@@ -34,6 +37,19 @@ def owner_of(x, P, W):
     while q > 0 and it_begin(q, P, W) > x:
         q -= 1
     return q
+
+
+def two_split(q, P, W, KT):
+    qb, qe = it_begin(q, P, W), it_begin(q + 1, P, W)
+    if qe <= qb:
+        return False
+    f, l = qb // KT, (qe - 1) // KT
+    return (f != l and owner_of(f * KT, P, W) != owner_of(f * KT + KT - 1, P, W)
+            and owner_of(l * KT, P, W) != owner_of(l * KT + KT - 1, P, W))
+
+
+def split_reducers(q_lo, q_hi, P, W, KT):
+    return q_hi - q_lo + 1 - (1 if q_hi != q_lo and two_split(q_hi, P, W, KT) else 0)
 
 
 def pow2_at_least(x):
@@ -173,3 +189,38 @@ def test_the_restatement_is_the_library_arithmetic(switches, dp_rows, slack, cta
             tiles, KT, PU, dp, stages = plan(M, n_out, K, swiglu, ctas_setting=ctas, dp_rows=dp_rows, slack=slack)
             got = _library_plan(2 if swiglu else 0, M, n_out, K)
             assert got == [tiles, KT, PU, int(dp), stages, 1], (n_out, K, M, got)
+
+
+@pytest.mark.parametrize("M", [1, 26, 208])
+@pytest.mark.parametrize("n_out,K,swiglu", PROJ)
+@pytest.mark.parametrize("CG", [1, 2])
+def test_each_split_tile_row_is_reduced_once_and_no_unit_reduces_twice(M, n_out, K, swiglu, CG):
+    """The DIST epilogue: a unit with two split tiles reduces a slice of its
+    last one only; reducer c of a tile's nr takes rows [c*R/nr, (c+1)*R/nr).
+    Every row of every split tile is summed exactly once, by one unit."""
+    tiles, KT, PU, dp, _ = plan(M, n_out, K, swiglu, CG=CG)
+    assert not dp
+    W = tiles * KT
+    rows = 64 if swiglu else 128
+    covered, per_unit = {}, [0] * PU
+    for u, (b, e) in enumerate(ranges(tiles, KT, PU, dp)):
+        pend = [t for t in range(b // KT, (e - 1) // KT + 1)
+                if (max(b, t * KT) - t * KT, min(e, t * KT + KT) - t * KT) != (0, KT)]
+        assert (len(pend) == 2) == two_split(u, PU, W, KT)
+        for t in (pend[1:] if len(pend) == 2 else pend):
+            lo, hi = owner_of(t * KT, PU, W), owner_of(t * KT + KT - 1, PU, W)
+            nr = split_reducers(lo, hi, PU, W, KT)
+            c = u - lo
+            assert 0 <= c < nr
+            covered.setdefault(t, []).append((c * rows // nr, (c + 1) * rows // nr))
+            per_unit[u] += 1
+    assert max(per_unit) <= 1
+    for t in range(tiles):
+        lo, hi = owner_of(t * KT, PU, W), owner_of(t * KT + KT - 1, PU, W)
+        if lo == hi:
+            assert t not in covered
+            continue
+        sl = sorted(covered[t])
+        assert len(sl) == split_reducers(lo, hi, PU, W, KT)
+        assert sl[0][0] == 0 and sl[-1][1] == rows
+        assert all(sl[i][1] == sl[i + 1][0] for i in range(len(sl) - 1))

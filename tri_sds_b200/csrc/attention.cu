@@ -186,8 +186,8 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
 
   // item -> (b, kvh, rb, split) and the key range it covers
   struct Item {
@@ -538,8 +538,8 @@ constexpr int CMB_REG = 32;
 __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
   const int r = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int d = threadIdx.x;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int t = r / a.G;
   const int start = a.starts[b];
   const int used = min(a.nsplit, (start + a.T + a.split_keys - 1) / a.split_keys);
@@ -765,8 +765,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int start = a.starts[b];
   const int kv_len = start + a.T;
   // causal rows see no key past start + t: the block's last token bounds the

@@ -62,8 +62,15 @@ static inline int tsds_smem_limit_once(Kernel kernel, int bytes, tsds_device_fla
 // Programmatic dependent launch: every kernel of the library is launched so
 // that it may start while the previous kernel in the stream drains; each
 // kernel executes griddepcontrol.wait before touching memory the previous
-// kernels write (and griddepcontrol.launch_dependents once all its CTAs are
-// resident).  tsds_set_pdl(0) turns the attribute off.
+// kernels write.  Each executes griddepcontrol.launch_dependents first (the
+// GEMM after its setup), so the next kernel is launched as soon as all of
+// this one's CTAs run and its CTAs take SMs as they free up: a GEMM after a
+// small kernel streams its first weight tiles while that kernel runs.  This
+// is safe because every kernel waits before it reads or writes anything an
+// earlier kernel touches (the GEMM reads only its weights before the wait),
+// and no kernel completes before its own wait has returned, so a wait covers
+// every earlier kernel of the stream, not only the previous one.
+// tsds_set_pdl(0) turns the attribute off.
 int tsds_pdl_enabled();
 
 template <typename... KArgs, typename... Args>

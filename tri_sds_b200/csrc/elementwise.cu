@@ -11,8 +11,8 @@ using namespace tsds;
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const int64_t* __restrict__ ids, int ids_stride, const bf16* __restrict__ table,
                              bf16* __restrict__ out, int N, int vocab) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x;
   const int64_t id = ids[(int64_t)m * ids_stride];
   const bool ok = id >= 0 && id < vocab;
@@ -49,10 +49,59 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(256) rms_norm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                        bf16* __restrict__ out, int n, int ldx, int ldo, float eps) {
   __shared__ float red[8];
-  pdl_wait();
+  constexpr int V = 4;  // 16-byte vectors a thread holds in registers: rows of n <= 8192
   pdl_trigger();
+  const int nv = n / 8;
   const bf16* xr = x + (int64_t)blockIdx.x * ldx;
   bf16* orow = out + (int64_t)blockIdx.x * ldo;
+  if (nv <= V * 256) {
+    // One read of the row into registers; the weights are constant and are
+    // read before the wait, so after it only the row's read is on the
+    // latency path.  Same arithmetic and order as the loop below.
+    uint4 g[V], xv[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = threadIdx.x + i * 256;
+      if (c < nv) g[i] = ldg16(w + c * 8);
+    }
+    pdl_wait();
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = threadIdx.x + i * 256;
+      if (c < nv) xv[i] = ldg16(xr + c * 8);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = threadIdx.x + i * 256;
+      if (c < nv) {
+        const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float a = bf_lo(u[k]), b = bf_hi(u[k]);
+          ss = fmaf(a, a, ss);
+          ss = fmaf(b, b, ss);
+        }
+      }
+    }
+    ss = block_sum<256>(ss, red);
+    const float rstd = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = threadIdx.x + i * 256;
+      if (c < nv) {
+        const uint32_t u[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+        const uint32_t gw[4] = {g[i].x, g[i].y, g[i].z, g[i].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          o[k] = pack_bf2(bf_lo(u[k]) * rstd * bf_lo(gw[k]), bf_hi(u[k]) * rstd * bf_hi(gw[k]));
+        *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    return;
+  }
+  pdl_wait();
   float ss = 0.f;
   for (int c = threadIdx.x; c < n / 8; c += 256) {
     uint4 v = ldg16(xr + c * 8);
@@ -94,8 +143,8 @@ extern "C" int tsds_rms_norm(const void* x, const void* w, void* out, int rows, 
 // ---------------------------------------------------------------------------
 __global__ void prep_chain_kernel(const int32_t* __restrict__ base, int offset, int B, int T,
                                   int32_t* __restrict__ starts, int32_t* __restrict__ positions) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= B * T) return;
   const int b = i / T, t = i - b * T;
@@ -127,13 +176,22 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     bf16* __restrict__ v_cache, int M, int T, int Hq, int Hkv, int S, int rope_len, float eps,
     const int64_t* __restrict__ out_loc, int64_t pool_rows, int32_t* __restrict__ status) {
   constexpr int D = 128;
-  pdl_wait();
   pdl_trigger();
   const int slots = Hq + 2 * Hkv;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= M * slots) return;
   const int lane = threadIdx.x & 31;
   const int m = gw / slots, h = gw - m * slots;
+  const bool is_q = h < Hq;
+  const bf16* nw = is_q ? q_norm_w : k_norm_w;
+  // the head's norm weights are constant: read before the wait, so only the
+  // previous kernels' outputs are on the latency path after it
+  uint32_t g0 = 0, g1 = 0;
+  if (gw < M * slots && h < Hq + Hkv && nw) {
+    g0 = *reinterpret_cast<const uint32_t*>(nw + 2 * lane);
+    g1 = *reinterpret_cast<const uint32_t*>(nw + 64 + 2 * lane);
+  }
+  pdl_wait();
+  if (gw >= M * slots) return;
   const int qkv_dim = slots * D;
   const bf16* src = qkv + (int64_t)m * qkv_dim + (int64_t)h * D;
   const uint32_t a = *reinterpret_cast<const uint32_t*>(src + 2 * lane);
@@ -141,6 +199,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
   float v[4] = {bf_lo(a), bf_hi(a), bf_lo(c), bf_hi(c)};
   const int b = m / T, t = m - b * T;
   const int pos = positions[m];
+  // the rotation of this position, requested before the norm needs the row
+  uint32_t cw = 0, sw = 0;
+  if (h < Hq + Hkv && pos >= 0 && pos < rope_len) {
+    cw = *reinterpret_cast<const uint32_t*>(cos_t + (int64_t)pos * (D / 2) + 2 * lane);
+    sw = *reinterpret_cast<const uint32_t*>(sin_t + (int64_t)pos * (D / 2) + 2 * lane);
+  }
   // K/V row of head kvh: the contiguous cache's row starts[b] + t of slab
   // (b, kvh), or (pooled caches, out_loc given) pool row out_loc[m], head kvh
   int64_t slot = 0;
@@ -168,9 +232,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = c;
     return;
   }
-  const bool is_q = h < Hq;
-  const bf16* nw = is_q ? q_norm_w : k_norm_w;
-  if (nw) qk_norm_pair(v, nw, lane, eps);
+  if (nw) qk_norm_pair_w(v, g0, g1, eps);
   bf16* dst;
   if (is_q) {
     dst = q_out + ((int64_t)m * Hq + h) * D;
@@ -178,7 +240,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(
     const int kvh = h - Hq;
     dst = k_cache + kv_row(kvh) * D;
   }
-  rope_store(v, cos_t, sin_t, pos, lane, dst);
+  rope_store_cs(v, cw, sw, lane, dst);
 }
 
 extern "C" int tsds_qk_norm_rope_kv(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
@@ -221,8 +283,8 @@ extern "C" int tsds_qk_norm_rope_kv_paged(const void* qkv, const void* q_norm_w,
 __global__ void table_rows_kernel(const int32_t* __restrict__ table, int64_t table_ld,
                                   const int64_t* __restrict__ req_rows, const int32_t* __restrict__ starts, int B,
                                   int T, int64_t* __restrict__ out_loc) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= B * T) return;
   const int b = i / T, t = i - b * T;
@@ -247,8 +309,8 @@ __global__ void accept_greedy_kernel(const int64_t* __restrict__ draft, const in
                                      int32_t* __restrict__ accept_len, int64_t* __restrict__ tokens,
                                      int32_t* __restrict__ target_len, int64_t* __restrict__ last,
                                      int64_t* __restrict__ cur, int B, int K) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int64_t* d = draft + (int64_t)b * K;
@@ -275,8 +337,8 @@ extern "C" int tsds_accept_greedy(const int64_t* draft, const int64_t* target, i
 __global__ void gather_ids_kernel(const int64_t* __restrict__ cur, const int64_t* __restrict__ last,
                                   const int64_t* __restrict__ draft, int64_t* __restrict__ verify_ids,
                                   int64_t* __restrict__ draft_ids2, int B, int K) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (verify_ids) {

@@ -17,10 +17,13 @@
 // * Warps 2-5 drain TMEM with tcgen05.ld (lane quarter = warp % 4) and run
 //   the epilogue: bf16 store, residual add, SwiGLU (gate rows 0-63 and up
 //   rows 64-127 of the same tile), or LM-head argmax candidates.
-// * A tile split across CTAs is finished by the last contributor (atomic
-//   counter): it sums the fp32 partials in CTA order, so the result is
-//   deterministic and - since the split depends only on (n_out, K, P) -
-//   a row's result never depends on M or on the other rows.
+// * A tile split across CTAs is finished from its contributors' fp32
+//   partials, summed in CTA order, so the result is deterministic and -
+//   since the split depends only on (n_out, K, P) - a row's result never
+//   depends on M or on the other rows.  The LM head's argmax tile is summed
+//   by its last contributor (atomic counter); the other epilogues spread a
+//   tile's rows over its reducers, at most one tile per CTA, so the
+//   kernel's tail is one slice of one tile long.
 // Every mbarrier wait is bounded; on a timeout the CTA records
 // TSDS_E_TIMEOUT in the status word and unwinds.
 #include "common.cuh"
@@ -455,19 +458,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     }
     if constexpr (DIST) {
       // Every arrival of this CTA is done, so no wait below can block
-      // another CTA's arrival (the grid is one resident wave).  Contributor
-      // c of nq sums rows [c*128/nq, (c+1)*128/nq) of the tile (SwiGLU: gate
-      // rows [c*64/nq, (c+1)*64/nq) and the up rows 64 below them) over all
-      // partials in CTA order; the last to leave resets the counters.
+      // another CTA's arrival (the grid is one resident wave).  The tile's
+      // nr reducers (split_reducers: its contributors, less the last one
+      // when that one holds two split tiles) each sum a slice of rows:
+      // reducer c takes rows [c*128/nr, (c+1)*128/nr) (SwiGLU: gate rows
+      // [c*64/nr, (c+1)*64/nr) and the up rows 64 below them) over all nq
+      // partials in CTA order; the last reducer to leave resets the
+      // counters.  A CTA with two split tiles reduces its last one only, so
+      // every CTA's tail is at most one slice long.
       constexpr bool SW = EPI == EPI_SWIGLU;
-      constexpr int ROWS = SW ? 64 : TILE_J;  // rows (SwiGLU: gate rows) split among contributors
-      for (int pi = 0; alive && pi < npend; ++pi) {
+      constexpr int ROWS = SW ? 64 : TILE_J;  // rows (SwiGLU: gate rows) split among reducers
+      for (int pi = npend == 2 ? 1 : 0; alive && pi < npend; ++pi) {
         const int t = pi == 0 ? pend0 : pend1, tb = t * KT;
         const int vt = t * CG + crank;
         const int q_lo = owner_of(tb, PU, p.W), q_hi = owner_of(tb + KT - 1, PU, p.W);
         const int nq = q_hi - q_lo + 1, c = unit - q_lo;
+        const int nr = split_reducers(q_lo, q_hi, PU, p.W, KT);
         const int lo_slot = it_begin(q_lo, PU, p.W) < tb ? 1 : 0;
-        const int rlo = c * ROWS / nq, R = (c + 1) * ROWS / nq - rlo;
+        const int rlo = c * ROWS / nr, R = (c + 1) * ROWS / nr - rlo;
         const int nel = R * (p.Npad / 4);
         if (r == 0) {
           int ok = 1;
@@ -496,7 +504,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           // order from zero.  A thread takes EU elements per pass and issues
           // the loads of all their partials (QB per batch) before summing, so
           // a pass costs one L2 round trip instead of one per element.
-          constexpr int EU = 2, QB = 4;
+          constexpr int EU = 4, QB = 3;
           for (int e0 = r; e0 < nel; e0 += 128 * EU) {
             float4 acc[EU][2];
 #pragma unroll
@@ -560,11 +568,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             }
           }
         } else if constexpr (EPI == EPI_STORE || EPI == EPI_STORE_F32) {
-          // plain stores: two elements per pass with all their partials'
+          // plain stores: EU elements per pass with all their partials'
           // loads in flight (measured faster at many token rows: q/k/v at
-          // M=208 55 us instead of 64 us); each element sums its partials in
-          // CTA order from zero, as below
-          constexpr int EU = 2, QB = 8;
+          // M=208 55 us instead of 64 us with two); each element sums its
+          // partials in CTA order from zero, as below
+          constexpr int EU = 3, QB = 6;
           for (int e0 = r; e0 < nel; e0 += 128 * EU) {
             float4 acc[EU];
 #pragma unroll
@@ -631,7 +639,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                 if (j < p.n_out && 4 * g + i < p.M) rv[i] = bf2f(p.res[(int64_t)(4 * g + i) * p.res_ld + j]);
             }
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            constexpr int QB = 8;
+            constexpr int QB = 10;
             for (int q0 = 0; q0 < nq; q0 += QB) {
               float4 f[QB];
 #pragma unroll
@@ -670,8 +678,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           }
         }
         epi_bar();
-        if (r == 0 && atomicAdd(&p.counters[MAX_TILES + vt], 1) == nq - 1) {
-          p.counters[vt] = 0;  // every contributor has left: ready for the next launch
+        if (r == 0 && atomicAdd(&p.counters[MAX_TILES + vt], 1) == nr - 1) {
+          p.counters[vt] = 0;  // every reducer has left: ready for the next launch
           p.counters[MAX_TILES + vt] = 0;
         }
       }

@@ -37,8 +37,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const bf16* __restrict__ x, i
                                                    int K) {
   constexpr int R = GemvCfg<MT>::R;
   constexpr int OUT_PER_WARP = EPI == EPI_SWIGLU ? R / 2 : R;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j0 = (blockIdx.x * 8 + warp) * OUT_PER_WARP;
   if (j0 >= n_out) return;
@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const bf16* __restrict
   constexpr int R = SplitCfg<MT>::R;
   constexpr int OUT = EPI == EPI_SWIGLU ? R / 2 : R;
   __shared__ float part[8][R * MT];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j0 = blockIdx.x * OUT;
   int64_t row_off[R];

@@ -29,8 +29,8 @@ __global__ void __launch_bounds__(256) lm_head_pass1(const bf16* __restrict__ x,
   constexpr int R = LmCfg<MT>::R;
   __shared__ float s_val[8][MT];
   __shared__ int s_idx[8][MT];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int v0 = (blockIdx.x * 8 + warp) * R;
   float2 acc[R][MT];
@@ -105,8 +105,8 @@ __global__ void __launch_bounds__(256) lm_head_pass2(const float* __restrict__ c
                                                      float* __restrict__ out_val) {
   __shared__ float s_val[256];
   __shared__ int s_idx[256];
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x;
   float bv = -INFINITY;
   int bi = 0x7fffffff;

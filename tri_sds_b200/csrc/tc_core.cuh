@@ -68,6 +68,24 @@ __device__ __forceinline__ int owner_of(int x, int P, uint32_t W) {
   return q;
 }
 
+// Whether unit q's range holds two split tiles (its first and its last tile
+// are both cut by a range boundary).
+__device__ __forceinline__ bool two_split(int q, int P, uint32_t W, int KT) {
+  const int qb = it_begin(q, P, W), qe = it_begin(q + 1, P, W);
+  if (qe <= qb) return false;
+  const int f = qb / KT, l = (qe - 1) / KT;
+  return f != l && owner_of(f * KT, P, W) != owner_of(f * KT + KT - 1, P, W) &&
+         owner_of(l * KT, P, W) != owner_of(l * KT + KT - 1, P, W);
+}
+
+// Units that sum the partials of the split tile starting at iteration tb,
+// whose contributors are q_lo..q_hi: all of them except q_hi when q_hi holds
+// two split tiles (it sums a slice of its last tile only, so no unit reduces
+// twice).  The reducers are q_lo .. q_lo + result - 1.
+__device__ __forceinline__ int split_reducers(int q_lo, int q_hi, int P, uint32_t W, int KT) {
+  return q_hi - q_lo + 1 - ((q_hi != q_lo && two_split(q_hi, P, W, KT)) ? 1 : 0);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {

@@ -9,16 +9,16 @@ namespace {
 // x = bf16(x + bf16(sum)): the reference's rounding of `x + proj` with proj the
 // bf16 product (qwen_model.py:133-134,143-144), proj summed across ranks in fp32.
 __global__ void residual_add_f32_kernel(bf16* __restrict__ x, const float* __restrict__ p, int64_t n) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     x[i] = f2bf(bf2f(x[i]) + rbf(p[i]));
 }
 
 __global__ void argmax_merge_kernel(const float* __restrict__ vals, const int64_t* __restrict__ idx, int M, int tp,
                                     int64_t shard, int64_t* __restrict__ out, int stride) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= M) return;
   float bv = -INFINITY;
@@ -36,8 +36,8 @@ __global__ void argmax_merge_kernel(const float* __restrict__ vals, const int64_
 
 // src [tp][M][Vs] -> dst [M][tp * Vs]; 16-byte moves when Vs % 8 == 0
 __global__ void gather_shards_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int tp, int M, int vs) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, r = blockIdx.y;
   const bf16* s = src + ((int64_t)r * M + m) * vs;
   bf16* d = dst + (int64_t)m * tp * vs + (int64_t)r * vs;

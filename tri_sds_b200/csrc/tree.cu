@@ -86,8 +86,8 @@ template <int K>
 __global__ void __cluster_dims__(TOPK_CL, 1, 1) __launch_bounds__(TOPK_THREADS, 1)
     topk_lse_kernel(const bf16* __restrict__ logits, int ld, int V, float* __restrict__ vals,
                     int* __restrict__ idx, float* __restrict__ lse) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   cg::cluster_group cl = cg::this_cluster();
   __shared__ float s_v[TOPK_WARPS][K];
   __shared__ int s_i[TOPK_WARPS][K];
@@ -282,8 +282,8 @@ __device__ void write_pass(TreeState& st, const PassIO& io, int b, int Tn, int L
 
 __global__ void tree_init_kernel(TreeState* __restrict__ states, const long long* __restrict__ cur,
                                  const int* __restrict__ lengths, PassIO io, int B) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   TreeState& st = states[b];
@@ -324,8 +324,8 @@ __global__ void __launch_bounds__(STATE_THREADS) tree_step_kernel(TreeState* __r
                                                                   const float* __restrict__ lse, int row_base, int T,
                                                                   int k, int next_T, const int* __restrict__ lengths,
                                                                   PassIO io, int B) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   __shared__ __align__(8) TreeState sst;
   const int b = blockIdx.x;
   state_copy(reinterpret_cast<uint32_t*>(&sst), reinterpret_cast<const uint32_t*>(&states[b]));
@@ -398,8 +398,8 @@ __global__ void __launch_bounds__(STATE_THREADS) tree_finalize_kernel(const Tree
                                                                       int n_nodes, int k,
                                                                       const int* __restrict__ lengths, VerifyIO io,
                                                                       int B) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   __shared__ __align__(8) TreeState st;
   __shared__ bool keep[MAXC];
   __shared__ int ch[32][MAXK];
@@ -628,8 +628,8 @@ struct AcceptIO {
 // grid (ACC_CL, B): blockIdx.x = rank in the sequence's cluster
 template <int RULE>
 __global__ void __cluster_dims__(ACC_CL, 1, 1) __launch_bounds__(ACC_THREADS, 1) accept_tree_kernel(AcceptIO io) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   cg::cluster_group cl = cg::this_cluster();
   __shared__ float red[64];
   __shared__ int s_next, s_idx, s_pick, s_last;
@@ -844,8 +844,8 @@ __global__ void tree_compact_kernel(bf16* __restrict__ k_cache, bf16* __restrict
                                     int Hkv, int S, const int* __restrict__ lengths, const int* __restrict__ path,
                                     const int* __restrict__ accept_len, int depth, const bf16* __restrict__ hidden,
                                     int NN, int N, bf16* __restrict__ root_feat) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   constexpr int D = 128;
   const int b = blockIdx.x, layer = blockIdx.y;
   const int a = accept_len[b];
@@ -875,8 +875,8 @@ __global__ void tree_compact_kernel(bf16* __restrict__ k_cache, bf16* __restrict
 }
 
 __global__ void tree_advance_kernel(int* __restrict__ lengths, const int* __restrict__ accept_len, int B) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) lengths[b] += accept_len[b] + 1;
 }
@@ -988,8 +988,8 @@ __global__ void tree_commit_paged_kernel(int* __restrict__ table, long long tabl
                                          const int* __restrict__ path, const int* __restrict__ accept_len, int depth,
                                          long long* __restrict__ kept, const bf16* __restrict__ hidden, int NN, int N,
                                          bf16* __restrict__ root_feat) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   const int a = accept_len[b];
   const int L = lengths[b];
@@ -1029,8 +1029,8 @@ extern "C" int tsds_tree_commit_paged(int32_t* token_table, int64_t table_ld, co
 __global__ void eagle_inputs_kernel(const bf16* __restrict__ root_feat, const bf16* __restrict__ head_feat,
                                     const int* __restrict__ featrow, const long long* __restrict__ tok,
                                     const bf16* __restrict__ embed, bf16* __restrict__ out, int T, int N, int vocab) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, b = m / T;
   const int fr = featrow[m];
   const bf16* f = fr < 0 ? root_feat + (size_t)b * N : head_feat + (size_t)fr * N;
