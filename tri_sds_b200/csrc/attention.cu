@@ -37,7 +37,7 @@ namespace {
 constexpr int D = 128;
 constexpr int TILE = 64;                    // keys per tile
 constexpr int ATT_MAX_WARPS = 8;            // consumer warps per CTA (row groups x key groups)
-constexpr int ATT_STAGES = 4;               // K/V tiles in flight per CTA
+constexpr int ATT_STAGES = 6;               // K/V tiles in flight per CTA
 // Ring invariant: a consumer's next tile is KG tiles after its last one, and
 // it waits for that tile's full barrier by phase parity.  The wait is exact
 // only if the tile STAGES before it - the stage's previous use - has landed;
@@ -257,11 +257,30 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
       prefetch_tmap(&vmap);
       int q = 0;  // ring sequence number of the next tile
       bool stop = false;
+      // The first tile of a first split is needed whatever the sequence's
+      // length (it holds at least one key): with the contiguous cache its
+      // rows are known from the indices alone, so it is requested before
+      // the sequence lengths are read.
+      bool first_early = false;
+      if (!a.paged && (int)blockIdx.x < nitems) {
+        const int item = blockIdx.x, b0 = item / items_per_b, r0 = item % items_per_b;
+        const int kvh0 = r0 / (a.nrb * a.nsplit), split0 = (r0 % (a.nrb * a.nsplit)) / a.nrb;
+        if (split0 == 0) {
+          const int row = (int)(((int64_t)b0 * a.Hkv + kvh0) * a.S);
+          mbar_arrive_expect_tx(&full_bar[0], TILE_BYTES);
+          tma_load_2d(smem + 0 * HALF_BYTES, &kmap, &full_bar[0], 0, row);
+          tma_load_2d(smem + 1 * HALF_BYTES, &kmap, &full_bar[0], 64, row);
+          tma_load_2d(smem + 2 * HALF_BYTES, &vmap, &full_bar[0], 0, row);
+          tma_load_2d(smem + 3 * HALF_BYTES, &vmap, &full_bar[0], 64, row);
+          first_early = true;
+        }
+      }
       for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
         const Item it = decode(item);
         const int ntiles = it.ntiles, key_begin = it.key_begin;
         const int64_t slab_row = ((int64_t)it.b * a.Hkv + it.kvh) * a.S;
         for (int t = 0; t < ntiles; ++t, ++q) {
+          if (q == 0 && first_early) continue;  // requested above
           const int s = q % STAGES;
           if (q >= STAGES && !mbar_wait(&empty_bar[s], ((q / STAGES) - 1) & 1)) {
             atomicExch(a.status, TSDS_E_TIMEOUT);
@@ -324,6 +343,7 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
       }
     }
     const int mask_base = a.mask_origin >= 0 ? a.mask_origin : start;
+    const int ctx_end = min(a.tree_mask ? mask_base : start, kv_len);
     const uint32_t mask0 = (a.tree_mask && v0) ? a.tree_mask[b * a.T + t0] : 0u;
     const uint32_t mask1 = (a.tree_mask && v1) ? a.tree_mask[b * a.T + t1] : 0u;
     const bool tree = a.tree_mask != nullptr;
@@ -362,8 +382,22 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
           mma_bf16(sc[j], qa[kk + 1], b2, b3);
         }
       }
-      // mask + row max
+      // mask + row max.  A tile wholly below ctx_end (shared context: keys
+      // below the tree's first key or the new tokens, and below kv_len) is
+      // visible to every valid row, so it skips the per-key tests.
       float mx0 = -INFINITY, mx1 = -INFINITY;
+      if (key0 + TILE <= ctx_end) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            sc[j][e] = v0 ? sc[j][e] * a.scale_log2 : -INFINITY;
+            sc[j][2 + e] = v1 ? sc[j][2 + e] * a.scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, sc[j][e]);
+            mx1 = fmaxf(mx1, sc[j][2 + e]);
+          }
+        }
+      } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
 #pragma unroll
@@ -388,6 +422,7 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
           mx0 = fmaxf(mx0, sc[j][e]);
           mx1 = fmaxf(mx1, sc[j][2 + e]);
         }
+      }
       }
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
@@ -450,25 +485,29 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
     if (KG > 1) {
-      // key groups 1..KG-1 hand (m, l, O) to key group 0 through the merge
-      // area ([slot][68 values][32 lanes]: consecutive lanes, no conflicts)
-      if (kg > 0) {
-        float* x = xs + (size_t)((kg - 1) * RG + rg) * 68 * 32 + lane;
+      // key groups 1..KG-1 hand (m, l, O) to key group 0 one after another
+      // through the merge area ([row group][68 values][32 lanes]:
+      // consecutive lanes, no conflicts); key group 0 merges them in order
+      float* x = xs + (size_t)rg * 68 * 32 + lane;
+      bool aborted = false;
+      for (int k = 1; k < KG; ++k) {
+        if (kg == k) {
 #pragma unroll
-        for (int n = 0; n < 16; ++n)
+          for (int n = 0; n < 16; ++n)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) x[(n * 4 + e) * 32] = o[n][e];
-        x[64 * 32] = m0;
-        x[65 * 32] = m1;
-        x[66 * 32] = l0;
-        x[67 * 32] = l1;
-      }
-      // one decision for every consumer warp (the producer may set the abort
-      // flag at any time; the barrier's AND is the same for all)
-      if (!named_bar_and(1, NC * 32, !*(volatile int*)&s_abort)) break;
-      if (kg == 0) {
-        for (int k = 1; k < KG; ++k) {
-          const float* x = xs + (size_t)((k - 1) * RG + rg) * 68 * 32 + lane;
+            for (int e = 0; e < 4; ++e) x[(n * 4 + e) * 32] = o[n][e];
+          x[64 * 32] = m0;
+          x[65 * 32] = m1;
+          x[66 * 32] = l0;
+          x[67 * 32] = l1;
+        }
+        // one decision for every consumer warp (the producer may set the
+        // abort flag at any time; the barrier's AND is the same for all)
+        if (!named_bar_and(1, NC * 32, !*(volatile int*)&s_abort)) {
+          aborted = true;
+          break;
+        }
+        if (kg == 0) {
           const float mk0 = x[64 * 32], mk1 = x[65 * 32];
           const float mn0 = fmaxf(m0, mk0), mn1 = fmaxf(m1, mk1);
           const float a0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
@@ -487,9 +526,10 @@ __global__ void __launch_bounds__(32 * (1 + ATT_MAX_WARPS), 1)
           m0 = mn0;
           m1 = mn1;
         }
+        // the merge area is free again for the next key group / item
+        named_bar_sync(1, NC * 32);
       }
-      // the merge area is free again for the next item
-      named_bar_sync(1, NC * 32);
+      if (aborted) break;
       if (kg > 0) continue;
     } else if (*(volatile int*)&s_abort) {
       break;  // one warp per row group, no barrier among them: each decides alone
@@ -586,35 +626,46 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
 
 // key groups of a split: a function of split_keys alone (so a row's
 // accumulation order never depends on the call's shape), each a divisor of
-// ATT_STAGES.  Splits of 1024 keys or more spread over four warps, so a short
-// context (one split) takes a few tiles per warp instead of a chain of them;
-// shorter splits use two, which leaves room for up to four row groups, so a
-// few query rows over a long context (decode, K+1 = 5) share each K/V tile
-// within one CTA instead of re-reading it in several.
+// ATT_STAGES.  Every key group has at least two ring stages, so a group
+// computes one tile while its next one lands (with one stage per group each
+// tile cost its compute plus the load's latency).  Splits of 768 keys or
+// more spread over three warps, so a short context (one split) takes a few
+// tiles per warp instead of a chain of them; shorter splits use two, which
+// leaves room for three row groups, so a few query rows over a long context
+// (decode, K+1 = 5) share each K/V tile within one CTA.
 int attn_key_groups(int split_keys) {
   const int tiles = split_keys / TILE;
-  return tiles >= 16 ? 4 : (tiles >= 2 ? 2 : 1);
+  return tiles >= 12 ? 3 : (tiles >= 2 ? 2 : 1);
 }
-static_assert(ATT_STAGES % 4 == 0, "every key-group count must divide the ring depth");
+static_assert(ATT_STAGES % 2 == 0 && ATT_STAGES % 3 == 0, "every key-group count must divide the ring depth");
 
-// row groups per CTA: the most (up to ATT_MAX_WARPS / KG) that still give
-// every SM a work item, else one (a short batch then spreads its rows over
-// more CTAs; the K/V tiles they share come from L2).  Row blocks never change
-// a row's arithmetic.
+// Row groups sharing the merge area: the ring's six 32 KB stages leave room
+// for three row groups' slots within the 227 KB a CTA may use.
+constexpr int ATT_MERGE_RG = 3;
+
+// row groups per CTA: the most (up to ATT_MAX_WARPS / KG, and with key
+// groups to merge up to ATT_MERGE_RG) that still give every SM a work item,
+// else one (a short batch then spreads its rows over more CTAs; the K/V tiles
+// they share come from L2).  Row blocks never change a row's arithmetic.
 int attn_row_groups(int KG, int Rpad, long long per_rb_items, int num_sms) {
   const int groups = Rpad / 16;
-  int RG = ATT_MAX_WARPS / KG < groups ? ATT_MAX_WARPS / KG : groups;
+  int cap = ATT_MAX_WARPS / KG;
+  if (KG > 1 && cap > ATT_MERGE_RG) cap = ATT_MERGE_RG;
+  int RG = cap < groups ? cap : groups;
   while (RG > 1 && per_rb_items * ((groups + RG - 1) / RG) < num_sms) RG /= 2;
   return RG;
 }
 
-// ring + merge area ((KG - 1) x RG warps' 68 values per lane) + alignment
+// ring + merge area (one slot of 68 values per lane for each row group; the
+// key groups take turns in it) + alignment
 size_t attn_smem_bytes(int RG, int KG) {
-  return 1024 + (size_t)ATT_STAGES * TILE_BYTES + (size_t)(KG - 1) * RG * 68 * 32 * sizeof(float);
+  return 1024 + (size_t)ATT_STAGES * TILE_BYTES + (size_t)(KG > 1 ? RG : 0) * 68 * 32 * sizeof(float);
 }
 
-// the largest merge area of any (RG, KG) with RG * KG <= ATT_MAX_WARPS, KG <= 4: KG = 4, RG = 2
-size_t attn_smem_bytes_max() { return attn_smem_bytes(ATT_MAX_WARPS / 4, 4); }
+// the largest of any plan: ATT_MERGE_RG row groups' merge slots
+size_t attn_smem_bytes_max() { return attn_smem_bytes(ATT_MERGE_RG, 2); }
+static_assert(1024 + ATT_STAGES * TILE_BYTES + ATT_MERGE_RG * 68 * 32 * 4 + 512 <= 232448,
+              "ring and merge area within a CTA's shared memory");
 
 // ---------------------------------------------------------------------------
 // tcgen05 variant: the same work units, split partials and combine pass, with
