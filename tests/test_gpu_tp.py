@@ -3,10 +3,8 @@ greedy speculative decoding (chain draft and EAGLE tree, whose commit
 compacts each rank's shard of the KV cache) == greedy autoregressive
 decoding under TP=2, with the row-parallel all-reduces by NCCL or by the
 library's peer-memory kernel (standalone, or as phases of the fused-layer
-kernel).  Skipped with fewer than 2 GPUs; the peer-memory variants run only
-with TSDS_TEST_PEER=1 (and TSDS_TEST_FUSED=1), and the chain leg with the
-draft model tensor-parallel too only with TSDS_TEST_DRAFT_TP=1, until they
-have been validated on GPUs."""
+kernel), and the chain leg once more with the draft model tensor-parallel
+over the same ranks.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -66,14 +64,13 @@ def _worker(rank, port, q, allreduce):
                         peer=peer, fused_layers=fused)
         drf = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_size=2, tp_layers=False, tp_vocab=False)
         spec, _ = SpecEngine(tgt, drf, K).generate(prompt, 16)
-        if os.environ.get("TSDS_TEST_DRAFT_TP") == "1":
-            # the chain draft tensor-parallel over the same ranks (and peer group)
-            tgt4 = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2,
-                             comm=comm, peer=peer, fused_layers=fused)
-            drf4 = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_rank=rank, tp_size=2, comm=comm,
-                             peer=peer, fused_layers=fused)
-            spec4, _ = SpecEngine(tgt4, drf4, K).generate(prompt, 16)
-            out.update(spec_draft_tp=spec4)
+        # the chain draft tensor-parallel over the same ranks (and peer group)
+        tgt4 = QwenModel(shape, B, 128, B * (K + 1), device=dev, weights=wt, tp_rank=rank, tp_size=2,
+                         comm=comm, peer=peer, fused_layers=fused)
+        drf4 = QwenModel(dshape, B, 128, B * 2, device=dev, weights=wd, tp_rank=rank, tp_size=2, comm=comm,
+                         peer=peer, fused_layers=fused)
+        spec4, _ = SpecEngine(tgt4, drf4, K).generate(prompt, 16)
+        out.update(spec_draft_tp=spec4)
         tgt2 = QwenModel(shape, B, 128, B, device=dev, weights=wt, tp_rank=rank, tp_size=2, comm=comm,
                          peer=peer, fused_layers=fused)
         ar = AutoregressiveEngine(tgt2).generate(prompt, 16)
@@ -116,14 +113,7 @@ def _worker(rank, port, q, allreduce):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("allreduce", [
-    "nccl",
-    pytest.param("peer", marks=pytest.mark.skipif(os.environ.get("TSDS_TEST_PEER") != "1",
-                                                  reason="peer all-reduce: set TSDS_TEST_PEER=1")),
-    pytest.param("peer+fused", marks=pytest.mark.skipif(
-        os.environ.get("TSDS_TEST_PEER") != "1" or os.environ.get("TSDS_TEST_FUSED") != "1",
-        reason="peer all-reduce in the fused-layer kernel: set TSDS_TEST_PEER=1 and TSDS_TEST_FUSED=1")),
-])
+@pytest.mark.parametrize("allreduce", ["nccl", "peer", "peer+fused"])
 def test_tp2_verify_and_lossless_spec(allreduce):
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
