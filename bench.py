@@ -70,6 +70,9 @@ def _args():
     # smaller depth for profiler captures only (never for reported numbers)
     ap.add_argument("--target-layers", type=int, default=None)
     ap.add_argument("--draft-layers", type=int, default=None)
+    ap.add_argument("--fuse-norm", action="store_true",
+                    help="the residual GEMMs also apply the RMSNorm that follows them "
+                         "(tsds_linear_residual_norm; opt-in: measured slower, 59.0 vs 61.6 tok/s at B=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--ctas-per-sm", type=int, default=None, help="tcgen05 GEMM CTAs per SM (library default 2)")
@@ -435,6 +438,7 @@ def run_layer(a):
     dev = torch.device("cuda", 0)
     B, T = a.batch, a.k + 1
     m = QwenModel(QWEN3_4B, B, 1024, B * T, device=dev, seed=5, fused_layers=a.fused_layers, split_keys=a.attn_split)
+    m.fuse_norm = a.fuse_norm
     m.lengths.fill_(512)
     m.x[:B * T].copy_(torch.randn(B * T, QWEN3_4B.hidden, device=dev).to(torch.bfloat16))
     pl = Plan()
@@ -548,9 +552,11 @@ def _build_engine(a, B, tshape, dshape, dev, rank, world, comm, peer, share=None
     target = QwenModel(tshape, B, max_seq, max_rows=rows_verify, device=dev, seed=1000, tp_rank=rank,
                        tp_size=world, comm=comm, peer=peer, fused_layers=a.fused_layers, split_keys=a.attn_split,
                        share_weights=None if share is None else share[0])
+    target.fuse_norm = a.fuse_norm
     if a.mode == "eagle":
         from tri_sds_b200.eagle import EagleEngine, EagleHead
         head = EagleHead(target, B, seed=2000, share=None if share is None else share[1])
+        head.model.fuse_norm = a.fuse_norm
         return target, head, EagleEngine(target, head, greedy=a.greedy, seed=3000), rows_verify
     if a.draft_tp and world > 1:
         # sharded like the target over the same ranks (and peer group)
@@ -561,6 +567,7 @@ def _build_engine(a, B, tshape, dshape, dev, rank, world, comm, peer, share=None
         draft = QwenModel(dshape, B, max_seq, max_rows=B * 2, device=dev, seed=2000, tp_size=world,
                           tp_layers=False, tp_vocab=False, fused_layers=a.fused_layers, split_keys=a.attn_split,
                           share_weights=None if share is None else share[1])
+    draft.fuse_norm = a.fuse_norm
     return target, draft, SpecEngine(target, draft, K), rows_verify
 
 

@@ -186,6 +186,19 @@ int tsds_linear(const void* x, int ldx, const void* W, void* out, int ldo, int M
 int tsds_linear_residual(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,
                          int M, int n_out, int K, void* workspace, size_t workspace_bytes,
                          tsds_stream_t stream);
+/* tsds_linear_residual, then RMSNorm of its n_out-wide output rows with
+ * weights norm_w into norm_out (row stride norm_ld), exactly as
+ * tsds_rms_norm(out, norm_w, norm_out, M, n_out, ldo, norm_ld, eps) would
+ * (bit for bit) - the residual add of a decoder layer followed by the next
+ * RMSNorm (qwen_model.py:133-136 then the next layer's norm, norm.py:42-72).  On the
+ * tcgen05 path (1 <= M <= 256) one launch: the first min(M, CTAs) CTAs
+ * normalise the rows once every CTA of the GEMM has stored its part, so
+ * the separate RMSNorm launch and its kernel boundary go away; uses two more
+ * words of the workspace header.  n_out, ldo and norm_ld multiples of 8,
+ * out / norm_w / norm_out 16-byte aligned. */
+int tsds_linear_residual_norm(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,
+                              int M, int n_out, int K, const void* norm_w, void* norm_out, int norm_ld,
+                              float eps, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out,
                        int K, void* workspace, size_t workspace_bytes, tsds_stream_t stream);
 /* out[m][j] = acc as fp32 (no rounding): a tensor-parallel rank's partial of

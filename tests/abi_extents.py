@@ -40,6 +40,10 @@ def extents(name, a):
         res_b = n_out * 2 if name == "tsds_linear_bias" else ((M - 1) * ldo + n_out) * 2
         return [(0, ((M - 1) * ldx + K) * 2), (2, n_out * K * 2), (3, res_b), (4, ((M - 1) * ldo + n_out) * 2),
                 (9, wsb)]
+    if name == "tsds_linear_residual_norm":
+        x, ldx, W, res, out, ldo, M, n_out, K, nw, nout, nld, eps, ws, wsb = a
+        return [(0, ((M - 1) * ldx + K) * 2), (2, n_out * K * 2), (3, ((M - 1) * ldo + n_out) * 2),
+                (4, ((M - 1) * ldo + n_out) * 2), (9, n_out * 2), (10, ((M - 1) * nld + n_out) * 2), (13, wsb)]
     if name == "tsds_logits_topk":
         lg, ld, M, V, k, vals, idx, lse = a
         return [(0, ((M - 1) * ld + V) * 2), (5, M * k * 4), (6, M * k * 4), (7, M * 4)]

@@ -59,9 +59,20 @@ def test_fused_plan_shape_and_extents(recorded, B, T):
         assert a[3]["T"] == T and a[2] == B * T
     for n, fn, a in pl.calls:
         assert check_call(n, a) > 0
-    # the per-op plan of the same model: 8 library calls per layer
+    # the per-op plan of the same model: 8 library calls per layer, or with
+    # the RMSNorms applied by the residual projections (fuse_norm) 7 for
+    # layer 0 and 6 for the others
     m.fused_layers = False
+    assert not m.fuse_norm   # the default
     assert len(m.layers_plan(B, T).calls) == 8 * L
+    m.fuse_norm = True
+    pn = m.layers_plan(B, T)
+    names = [n for n, _, _ in pn.calls]
+    assert len(names) == 6 * L + 1 and names.count("tsds_rms_norm") == 1
+    assert names.count("tsds_linear_residual_norm") == 2 * L - 1 and not pn.final_normed
+    assert m.layers_plan(B, T, final_norm=True).final_normed
+    for n, fn, a in pn.calls:
+        assert check_call(n, a) > 0
 
 
 def test_eagle_engine_plans_with_fused_layers(recorded):

@@ -72,6 +72,7 @@ SIGNATURES = {
     "tsds_tc_gemm_plan": (_I, [_I, _I, _I, _I, _P]),
     "tsds_linear": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_residual": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsds_linear_residual_norm": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _F, _P, _Z, _P]),
     "tsds_linear_swiglu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_linear_bias": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsds_logits_topk": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),

@@ -55,7 +55,20 @@ struct TcParams {
   int tmem_cols;
   int dp;  // 1: data-parallel schedule (whole tiles per unit), 0: stream-K
   uint64_t wait_ns;  // limit of every bounded wait (tsds_set_wait_limit_ns)
+  // residual epilogue only (tsds_linear_residual_norm): RMSNorm of the
+  // finished output rows into norm_out, or none (norm_out null)
+  const bf16* norm_w;
+  bf16* norm_out;
+  int norm_ld;
+  float norm_eps;
 };
+
+// Workspace header words of the RMSNorm tail (status is word 0 of the
+// 64-byte header): CTAs done, counted on HDR_NDONE words (CTA p on word
+// HDR_DONE + p % HDR_NDONE, so the P arrivals do not queue on one address),
+// and norm workers done.
+constexpr int HDR_DONE = 4, HDR_NDONE = 8, HDR_LEFT = HDR_DONE + HDR_NDONE;
+static_assert(HDR_LEFT < 16, "the tail's words within the 64-byte header");
 
 constexpr int MAX_TILES = 2048;   // tile counters; departure counters follow them
 
@@ -158,6 +171,73 @@ __device__ __forceinline__ void finish_chunk(const TcParams& p, Smem& sh, int t,
     }
     epi_bar();
   }
+}
+
+// RMSNorm of output rows m = row0, row0 + step, ... < M into norm_out
+// (tsds_linear_residual_norm): the arithmetic of rms_norm_kernel (256
+// threads) on the 128 epilogue threads, thread r playing threads r and
+// r + 128, so every partial sum and the block reduction's order are the
+// same and the result is bit for bit the separate kernel's.  The rows were
+// written by other CTAs of this launch: read through L2.
+// Rows of n <= NORM_V * 1024 (n / 8 vectors over 128 threads) stay in
+// registers: vector c = r + 128 i is thread r's i-th, which belongs to
+// virtual thread r (i even) or r + 128 (i odd), and each virtual thread's
+// vectors are summed in ascending order as in the separate kernel.  gw
+// holds the thread's norm-weight vectors, read by the caller.
+constexpr int NORM_V = 8;
+__device__ void norm_rows(const TcParams& p, Smem& sh, int r, int row0, int step, const uint4 (&gw)[NORM_V]) {
+  float* red = &sh.red_v[0][0];
+  const int n = p.n_out, nv = n / 8;
+  const int w = r >> 5, lane = r & 31;
+  for (int m = row0; m < p.M; m += step) {
+    const bf16* xr = p.out + (int64_t)m * p.ldo;
+    bf16* orow = p.norm_out + (int64_t)m * p.norm_ld;
+    uint4 v[NORM_V];
+#pragma unroll
+    for (int i = 0; i < NORM_V; ++i)
+      if (r + 128 * i < nv) v[i] = __ldcg(reinterpret_cast<const uint4*>(xr + (r + 128 * i) * 8));
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < NORM_V; ++i) {
+      if (r + 128 * i < nv) {
+        const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a = bf_lo(u[k]), b = bf_hi(u[k]);
+          ss[i & 1] = fmaf(a, a, ss[i & 1]);
+          ss[i & 1] = fmaf(b, b, ss[i & 1]);
+        }
+      }
+    }
+    const float s0 = warp_sum(ss[0]), s1 = warp_sum(ss[1]);
+    if (lane == 0) {
+      red[w] = s0;
+      red[w + 4] = s1;
+    }
+    epi_bar();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
+    epi_bar();
+    const float rstd = 1.0f / sqrtf(t / (float)n + p.norm_eps);
+#pragma unroll
+    for (int i = 0; i < NORM_V; ++i) {
+      const int c = r + 128 * i;
+      if (c < nv) {
+        const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        const uint32_t g4[4] = {gw[i].x, gw[i].y, gw[i].z, gw[i].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          o[k] = pack_bf2(bf_lo(u[k]) * rstd * bf_lo(g4[k]), bf_hi(u[k]) * rstd * bf_hi(g4[k]));
+        *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // CG = 1: one CTA per tile of 128 weight rows.  CG = 2: a CTA pair on two
@@ -704,6 +784,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     else
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * p.tmem_cols));
   }
+  if constexpr (EPI == EPI_RESIDUAL) {
+    // RMSNorm tail (tsds_linear_residual_norm): every CTA reports itself
+    // done; CTAs 0..NW-1 (NW = min(M, P)) wait (bounded) until all P have,
+    // then normalise rows blockIdx.x, + NW, ...; the last of them to finish
+    // resets the two header words.  The grid is one resident wave, so the
+    // wait always ends.  A CTA that gave up still reports itself done.
+    if (p.norm_out != nullptr) {
+      int* done = p.status + HDR_DONE;
+      int* left = p.status + HDR_LEFT;
+      // the barrier above orders this CTA's stores before thread 0's fence
+      // and release (the grid-barrier pattern)
+      if (threadIdx.x == 0) {
+        __threadfence();
+        red_release_add(done + blockIdx.x % HDR_NDONE, 1);
+      }
+      const int NW = p.M < p.P ? p.M : p.P;
+      if ((int)blockIdx.x < NW) {
+        const int nr = (warp & 3) * 32 + lane;
+        uint4 gw[NORM_V];  // the norm weights are constant: read before the wait
+        if (warp >= 2 && p.n_out / 8 <= NORM_V * 128) {
+#pragma unroll
+          for (int i = 0; i < NORM_V; ++i)
+            if (nr + 128 * i < p.n_out / 8) gw[i] = ldg16(p.norm_w + (nr + 128 * i) * 8);
+        }
+        if (threadIdx.x == 0) {
+          int ok = 1;
+          const uint64_t t0 = global_ns();
+          for (;;) {
+            int c[HDR_NDONE];  // every word's load in flight at once
+#pragma unroll
+            for (int k = 0; k < HDR_NDONE; ++k) c[k] = *(volatile int*)(done + k);
+            bool all = true;
+#pragma unroll
+            for (int k = 0; k < HDR_NDONE; ++k) all &= c[k] >= (p.P - k + HDR_NDONE - 1) / HDR_NDONE;
+            if (all) break;
+            if (global_ns() - t0 > p.wait_ns) {
+              ok = 0;
+              break;
+            }
+          }
+          __threadfence();  // acquire: the other CTAs' rows are read after this
+          if (!ok) atomicExch(p.status, TSDS_E_TIMEOUT);
+          sh.go = ok;
+        }
+        __syncthreads();
+        if (sh.go && warp >= 2 && p.n_out / 8 <= NORM_V * 128) norm_rows(p, sh, nr, (int)blockIdx.x, NW, gw);
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(left, 1) == NW - 1) {
+          // every worker has seen all P: ready for the next launch
+#pragma unroll
+          for (int k = 0; k < HDR_NDONE; ++k) atomicExch(done + k, 0);
+          atomicExch(left, 0);
+        }
+      }
+    }
+  }
 }
 
 std::atomic<int> g_num_sms{0};
@@ -937,9 +1073,11 @@ extern "C" int tsds_tc_gemm_plan(int epi, int M, int n_out, int K, int32_t* out)
   return TSDS_OK;
 }
 
-int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
+namespace {
+int tc_gemm_impl(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
                  int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
-                 int* cand_idx, int ldc, cudaStream_t stream) {
+                 int* cand_idx, int ldc, const bf16* norm_w, bf16* norm_out, int norm_ld, float norm_eps,
+                 cudaStream_t stream) {
   TSDS_RETURN_IF(M <= 0 || M > 256, TSDS_E_INVALID);
   TSDS_RETURN_IF(workspace == nullptr || workspace_bytes < tsds_tc_workspace_bytes(M), TSDS_E_WORKSPACE);
   TSDS_RETURN_IF(!tsds_aligned16(workspace), TSDS_E_ALIGN);
@@ -960,6 +1098,10 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
   p.cand_val = cand_val;
   p.cand_idx = cand_idx;
   p.ldc = ldc;
+  p.norm_w = norm_w;
+  p.norm_out = norm_out;
+  p.norm_ld = norm_ld;
+  p.norm_eps = norm_eps;
 
   CUtensorMap amap, bmap;
   int st = tsds_make_tmap_2d_bf16(&amap, W, K, w_rows, (uint64_t)K * 2, BK, 64, 1);
@@ -983,4 +1125,23 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
     case EPI_ARGMAX: return launch_tc<EPI_ARGMAX, 1>(amap, bmap, p, smem, stream);
     default: return TSDS_E_INVALID;
   }
+}
+}  // namespace
+
+int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, const bf16* res, int res_ld, bf16* out,
+                 int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
+                 int* cand_idx, int ldc, cudaStream_t stream) {
+  return tc_gemm_impl(epi, x, ldx, W, w_rows, res, res_ld, out, ldo, M, n_out, K, workspace, workspace_bytes, cand_val,
+                      cand_idx, ldc, nullptr, nullptr, 0, 0.f, stream);
+}
+
+int tsds_tc_gemm_residual_norm(const bf16* x, int ldx, const bf16* W, const bf16* res, int res_ld, bf16* out, int ldo,
+                               int M, int n_out, int K, const bf16* norm_w, bf16* norm_out, int norm_ld, float eps,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  TSDS_RETURN_IF(!norm_w || !norm_out || (n_out % 8) != 0 || (ldo % 8) != 0 || (norm_ld % 8) != 0 ||
+                     norm_ld < n_out || n_out > NORM_V * 1024,
+                 TSDS_E_INVALID);
+  TSDS_RETURN_IF(!tsds_aligned16(out) || !tsds_aligned16(norm_w) || !tsds_aligned16(norm_out), TSDS_E_ALIGN);
+  return tc_gemm_impl(EPI_RESIDUAL, x, ldx, W, n_out, res, res_ld, out, ldo, M, n_out, K, workspace, workspace_bytes,
+                      nullptr, nullptr, 0, norm_w, norm_out, norm_ld, eps, stream);
 }

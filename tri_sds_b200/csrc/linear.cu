@@ -62,6 +62,28 @@ extern "C" int tsds_linear_residual(const void* x, int ldx, const void* W, const
   return run_linear(EPI_RESIDUAL, x, ldx, W, res, ldo, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
 }
 
+extern "C" int tsds_linear_residual_norm(const void* x, int ldx, const void* W, const void* res, void* out, int ldo,
+                                         int M, int n_out, int K, const void* norm_w, void* norm_out, int norm_ld,
+                                         float eps, void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
+  int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);
+  if (st != TSDS_OK) return st;
+  TSDS_RETURN_IF(!res || !norm_w || !norm_out || (n_out % 8) != 0 || (ldo % 8) != 0 || (norm_ld % 8) != 0 ||
+                     norm_ld < n_out,
+                 TSDS_E_INVALID);
+  TSDS_RETURN_IF(!tsds_aligned16(out) || !tsds_aligned16(norm_w) || !tsds_aligned16(norm_out), TSDS_E_ALIGN);
+  if (M <= g_gemv_max_rows || M > 256 || n_out > 8192) {
+    // the GEMV path, more rows than one launch takes, or rows wider than the
+    // fused tail keeps in registers: the two steps apart
+    st = run_linear(EPI_RESIDUAL, x, ldx, W, res, ldo, out, ldo, M, n_out, K, workspace, workspace_bytes, stream);
+    if (st != TSDS_OK) return st;
+    return tsds_rms_norm(out, norm_w, norm_out, M, n_out, ldo, norm_ld, eps, stream);
+  }
+  TSDS_RETURN_IF(workspace == nullptr, TSDS_E_WORKSPACE);
+  return tsds_tc_gemm_residual_norm((const bf16*)x, ldx, (const bf16*)W, (const bf16*)res, ldo, (bf16*)out, ldo, M,
+                                    n_out, K, (const bf16*)norm_w, (bf16*)norm_out, norm_ld, eps, workspace,
+                                    workspace_bytes, stream);
+}
+
 extern "C" int tsds_linear_swiglu(const void* x, int ldx, const void* W, void* out, int ldo, int M, int n_out, int K,
                                   void* workspace, size_t workspace_bytes, tsds_stream_t stream) {
   int st = check_linear(x, ldx, W, out, ldo, M, n_out, K);

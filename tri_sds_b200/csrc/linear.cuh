@@ -17,6 +17,12 @@ int tsds_tc_gemm(int epi, const bf16* x, int ldx, const bf16* W, int w_rows, con
                  int ldo, int M, int n_out, int K, void* workspace, size_t workspace_bytes, float* cand_val,
                  int* cand_idx, int ldc, cudaStream_t stream);
 
+// The residual epilogue followed by RMSNorm of its output rows (weights
+// norm_w, eps) into norm_out, in one launch; M <= 256.
+int tsds_tc_gemm_residual_norm(const bf16* x, int ldx, const bf16* W, const bf16* res, int res_ld, bf16* out, int ldo,
+                               int M, int n_out, int K, const bf16* norm_w, bf16* norm_out, int norm_ld, float eps,
+                               void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 // Row count up to which the CUDA-core GEMV is used instead of tcgen05.
 int tsds_gemv_rows_limit();
 

@@ -133,10 +133,11 @@ class EagleEngine:
                _p(self.pass_tok), _p(t.embed_w), _p(self.x2), B, T, s.hidden, s.vocab)
         pl.add("tsds_linear_bias", _p(self.x2), 2 * s.hidden, _p(h.fc_w), _p(h.fc_b), _p(feat), s.hidden, M,
                s.hidden, 2 * s.hidden, _p(hm.lin_ws), hm.lin_ws_bytes)
-        pl.extend(hm.layers_plan(B, T, tree_mask=self.pass_mask, mask_origin=0, x=feat, starts=self.pass_starts,
-                                 positions=self.pass_pos))
+        lp = hm.layers_plan(B, T, tree_mask=self.pass_mask, mask_origin=0, x=feat, starts=self.pass_starts,
+                            positions=self.pass_pos, final_norm=True)
+        pl.extend(lp)
         pl.extend(hm.head_plan(B, T, self.head_argmax[base:], 1, last_only=False,
-                               logits_out=self.head_logits[base:], x=feat))
+                               logits_out=self.head_logits[base:], x=feat, normed=lp.final_normed))
         pl.add("tsds_logits_topk", _p(self.head_logits[base:]), s.vocab, M, s.vocab, k, _p(self.vals[base:]),
                _p(self.idx[base:]), _p(self.lse[base:]))
         next_T = k if d + 1 < self.depth else 0
@@ -156,8 +157,10 @@ class EagleEngine:
         pl.add("tsds_tree_finalize", _p(self.states), self.n_nodes, k, _p(t.lengths), _p(self.ids),
                _p(t.positions), _p(self.vmask), _p(self.hrow), _p(self.children), _p(t.starts), B)
         pl.add("tsds_embed", _p(self.ids), 1, _p(t.embed_w), _p(t.x), B * NN, s.hidden, s.vocab)
-        pl.extend(t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1))
-        pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits))
+        lp = t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1, final_norm=True)
+        pl.extend(lp)
+        pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits,
+                              normed=lp.final_normed))
         pl.add("tsds_accept_tree_rule", _p(self.target_logits), _p(self.target_argmax), _p(self.head_logits),
                _p(self.ids), _p(self.hrow), _p(self.children), None if self.greedy else _p(self.U),
                self.rule, _p(self.path), _p(self.accept_len), _p(self.tokens), _p(self.cur), B,
@@ -184,8 +187,10 @@ class EagleEngine:
         B, NN = t.batch, self.n_nodes + 1
         pl = Plan()
         pl.add("tsds_embed", _p(self.ids), 1, _p(t.embed_w), _p(t.x), B * NN, s.hidden, s.vocab)
-        pl.extend(t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1))
-        pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits))
+        lp = t.layers_plan(B, NN, tree_mask=self.vmask, mask_origin=-1, final_norm=True)
+        pl.extend(lp)
+        pl.extend(t.head_plan(B, NN, self.target_argmax, 1, last_only=False, logits_out=self.target_logits,
+                              normed=lp.final_normed))
         return pl
 
     @property

@@ -144,6 +144,8 @@ class Plan:
     tensor parallelism, collective steps (Python callables on the current
     stream)."""
     calls: list = field(default_factory=list)
+    # layers_plan(final_norm=True) that left the final RMSNorm of every row in xn
+    final_normed: bool = False
 
     def add(self, name: str, *args):
         self.calls.append((name, getattr(_lib.load(), name), args))
@@ -316,6 +318,14 @@ class QwenModel:
         # norm -> q/k/v of consecutive layers, under tensor parallelism with
         # the peer all-reduces as phases); its own zero-filled workspace
         self.fused_layers = fused_layers and (self.layer_tp == 1 or peer is not None)
+        # True: the per-op plan's residual GEMMs (O, down) also apply the
+        # RMSNorm that follows them (tsds_linear_residual_norm: one launch,
+        # the same bits as the two).  Off by default: measured slower on a
+        # B200 (B=1 EAGLE cycle 59.0 vs 61.6 tok/s) - the GEMM's tail (every
+        # CTA's fence and report, then a few CTAs normalising one row each
+        # while the next projection's CTAs stream their first weight tiles)
+        # costs more than the separate RMSNorm launch and its kernel boundary.
+        self.fuse_norm = False
         if self.fused_layers:
             self.fused_ws_bytes = _lib.query("tsds_fused_layer_workspace_bytes", M)
             self.fused_ws = torch.zeros(self.fused_ws_bytes, dtype=torch.uint8, device=dev)
@@ -323,13 +333,18 @@ class QwenModel:
     # -- launch plans ---------------------------------------------------------
     def layers_plan(self, B: int, T: int, tree_mask: torch.Tensor | None = None, mask_origin: int = -1,
                     x: torch.Tensor | None = None, starts: torch.Tensor | None = None,
-                    positions: torch.Tensor | None = None) -> Plan:
+                    positions: torch.Tensor | None = None, final_norm: bool = False) -> Plan:
         """All decoder layers over rows x[0:B*T] (embedded already), with
         starts/positions already prepared.  ``x`` / ``starts`` /
         ``positions`` default to the model's own buffers; ``tree_mask`` +
         ``mask_origin`` select the attention mask (see tsds_verify_attention).
         Under tensor parallelism the O and down projections produce fp32
-        partials that are all-reduced before the residual add."""
+        partials that are all-reduced before the residual add.  Without it
+        (``fuse_norm``) each O / down projection also applies the RMSNorm
+        that reads its output - the layer's post-attention norm, the next
+        layer's input norm and, with ``final_norm``, the final norm into
+        ``xn``; the returned plan's ``final_normed`` then tells head_plan to
+        skip its own."""
         s, ls = self.shape, self.lshape
         M = B * T
         assert M <= self.max_rows and B == self.batch
@@ -345,11 +360,17 @@ class QwenModel:
             return self._fused_layers_plan(B, T, tree_mask, mask_origin, xb, st, ps)
         n_peer = [0]
 
-        def row_parallel(src, ld_src, w, k_in):
+        def row_parallel(src, ld_src, w, k_in, norm_w=None):
+            """The row-parallel projection + residual add; True when it also
+            wrote RMSNorm(x) with norm_w into xn."""
             if not tp and self.peer is None:
+                if norm_w is not None and self.fuse_norm:
+                    pl.add("tsds_linear_residual_norm", _p(src), ld_src, _p(w), _p(xb), _p(xb), s.hidden, M, s.hidden,
+                           k_in, _p(norm_w), _p(self.xn), s.hidden, eps, _p(lw), lb)
+                    return True
                 pl.add("tsds_linear_residual", _p(src), ld_src, _p(w), _p(xb), _p(xb), s.hidden, M, s.hidden, k_in,
                        _p(lw), lb)
-                return
+                return False
             if self.peer is not None:
                 # the partial goes straight into this rank's peer slot; calls alternate slots
                 slot = n_peer[0] % 2
@@ -358,18 +379,22 @@ class QwenModel:
                        k_in, _p(lw), lb)
                 pl.add("tsds_peer_allreduce_residual", _p(xb), self.peer.bufs, self.tp_rank, self.layer_tp, slot, M,
                        s.hidden, self.peer.max_elems, _p(self.status))
-                return
+                return False
             part = self.part[:M]
             pl.add("tsds_linear_f32", _p(src), ld_src, _p(w), _p(part), s.hidden, M, s.hidden, k_in, _p(lw), lb)
             pl.add_py("all_reduce", lambda part=part: self.comm.all_reduce(part))
             pl.add("tsds_residual_add_f32", _p(xb), _p(part), M, s.hidden)
+            return False
 
         kv = self.kv
         if kv is not None:
             # the new tokens' pool rows (SGLang's out_cache_loc) from the table
             pl.add("tsds_table_rows", _p(kv.table), kv.table_ld, _p(kv.req_rows), _p(st), B, T, _p(self.out_loc))
+        normed = False   # xn already holds this layer's input norm
+        nl = len(self.layers)
         for i, L in enumerate(self.layers):
-            pl.add("tsds_rms_norm", _p(xb), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
+            if not normed:
+                pl.add("tsds_rms_norm", _p(xb), _p(L.ln1), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear", _p(self.xn), s.hidden, _p(L.w_qkv), _p(self.qkv), ls.qkv_dim, M, ls.qkv_dim,
                    s.hidden, _p(lw), lb)
             if kv is None:
@@ -392,12 +417,14 @@ class QwenModel:
                        _p(tree_mask), mask_origin, _p(kv.table), kv.table_ld, _p(kv.req_rows), kv.pool_rows,
                        kv.page_size, B, T, ls.n_heads, ls.n_kv_heads, s.head_dim, self.max_seq, self.split_keys,
                        float(s.head_dim ** -0.5), _p(self.attn_ws), self.attn_ws_bytes, _p(self.status))
-            row_parallel(self.attn, ls.q_dim, L.w_o, ls.q_dim)
-            pl.add("tsds_rms_norm", _p(xb), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
+            if not row_parallel(self.attn, ls.q_dim, L.w_o, ls.q_dim, norm_w=L.ln2):
+                pl.add("tsds_rms_norm", _p(xb), _p(L.ln2), _p(self.xn), M, s.hidden, s.hidden, s.hidden, eps)
             pl.add("tsds_linear_swiglu", _p(self.xn), s.hidden, _p(L.w_gu), _p(self.h), ls.intermediate, M,
                    ls.intermediate, s.hidden, _p(lw), lb)
-            row_parallel(self.h, ls.intermediate, L.w_d, ls.intermediate)
+            nxt = self.layers[i + 1].ln1 if i + 1 < nl else (self.norm_w if final_norm else None)
+            normed = row_parallel(self.h, ls.intermediate, L.w_d, ls.intermediate, norm_w=nxt)
         assert n_peer[0] % 2 == 0   # the next plan run starts on slot 0 again
+        pl.final_normed = bool(final_norm and normed)
         return pl
 
     def _fused_layers_plan(self, B: int, T: int, tree_mask, mask_origin: int, xb, st, ps) -> Plan:
@@ -464,18 +491,21 @@ class QwenModel:
         return pl
 
     def head_plan(self, B: int, T: int, argmax_out: torch.Tensor, argmax_stride: int, last_only: bool,
-                  logits_out: torch.Tensor | None = None, x: torch.Tensor | None = None) -> Plan:
+                  logits_out: torch.Tensor | None = None, x: torch.Tensor | None = None,
+                  normed: bool = False) -> Plan:
         """Final RMSNorm + LM head + argmax over all rows, or only the last
-        row of each sequence.  With a vocab-parallel LM head each rank picks
-        its shard's best (value, index), the candidates are all-gathered and
-        merged (ties: lowest global index); full logits, when requested, are
-        all-gathered and reassembled."""
+        row of each sequence (``normed``: xn already holds the final norm of
+        all rows, from layers_plan(final_norm=True)).  With a vocab-parallel
+        LM head each rank picks its shard's best (value, index), the
+        candidates are all-gathered and merged (ties: lowest global index);
+        full logits, when requested, are all-gathered and reassembled."""
         s = self.shape
         pl = Plan()
         xb = self.x if x is None else x
         rows, ld = (B, T * s.hidden) if last_only else (B * T, s.hidden)
         src = xb[T - 1:] if last_only else xb
-        pl.add("tsds_rms_norm", _p(src), _p(self.norm_w), _p(self.xn), rows, s.hidden, ld, s.hidden, s.eps)
+        if not (normed and not last_only):
+            pl.add("tsds_rms_norm", _p(src), _p(self.norm_w), _p(self.xn), rows, s.hidden, ld, s.hidden, s.eps)
         if self.vocab_tp == 1 and self.lm_peer is None:
             pl.add("tsds_lm_head_argmax", _p(self.xn), s.hidden, _p(self.lm_head_w), _p(logits_out), _p(argmax_out),
                    argmax_stride, None, rows, s.vocab, s.hidden, _p(self.lm_ws), self.lm_ws_bytes)
@@ -521,8 +551,9 @@ class QwenModel:
         pl = Plan()
         pl.add("tsds_prep_chain", _p(base), offset, B, T, _p(self.starts), _p(self.positions))
         pl.add("tsds_embed", _p(ids), ids_stride, _p(self.embed_w), _p(self.x), B * T, s.hidden, s.vocab)
-        pl.extend(self.layers_plan(B, T))
-        pl.extend(self.head_plan(B, T, argmax_out, argmax_stride, last_only, logits_out))
+        lp = self.layers_plan(B, T, final_norm=not last_only)
+        pl.extend(lp)
+        pl.extend(self.head_plan(B, T, argmax_out, argmax_stride, last_only, logits_out, normed=lp.final_normed))
         return pl
 
     # -- prefill (untimed set-up, on this library's kernels) ---------------------

@@ -195,6 +195,25 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, res: torch.Tensor, out: to
     return out
 
 
+def linear_residual_norm(x: torch.Tensor, w: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor,
+                         eps: float = 1e-6, out: torch.Tensor | None = None, norm_out: torch.Tensor | None = None):
+    """(res + x @ w^T, RMSNorm of that with norm_w): a decoder layer's residual
+    add and the RMSNorm that reads it, in one launch; both bit for bit what
+    linear_residual + rms_norm give."""
+    _bf16_cuda(x, w, res, norm_w, out, norm_out)
+    M, K = x.shape
+    n_out = w.shape[0]
+    _need(w.shape[1] == K and w.is_contiguous() and res.shape == (M, n_out), "shape mismatch")
+    _need(norm_w.shape == (n_out,) and norm_w.is_contiguous(), "norm_w must be [n_out]")
+    out = torch.empty_like(res) if out is None else out
+    norm_out = torch.empty_like(res) if norm_out is None else norm_out
+    _need(res.stride(0) == out.stride(0), "res and out must share a row stride")
+    ws, nb = _lin_ws(M, n_out, K, x.device)
+    _lib.call("tsds_linear_residual_norm", _p(x), x.stride(0), _p(w), _p(res), _p(out), out.stride(0), M, n_out, K,
+              _p(norm_w), _p(norm_out), norm_out.stride(0), float(eps), _p(ws), nb, _stream())
+    return out, norm_out
+
+
 def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | None = None):
     """silu(x @ gate^T) * (x @ up^T) for w_gate_up = [gate; up] ([2I, K])."""
     _bf16_cuda(x, w_gate_up, out)
