@@ -985,8 +985,8 @@ int pair_clusters(int epi, size_t smem) {
 
 }  // namespace
 
-// Workspace layout: [status int32, padding to 64 B][arrival counters: 2048 ints][departure counters:
-// 2048 ints][partials: P x 2 x Npad x 128 fp32].
+// Workspace layout: [status int32, the RMSNorm tail's words 4-12 (HDR_DONE..HDR_LEFT), padding to 64 B]
+// [arrival counters: 2048 ints][departure counters: 2048 ints][partials: P x 2 x Npad x 128 fp32].
 // The counters must be zero before the first use; every launch leaves them zero.
 size_t tsds_tc_workspace_bytes(int M) {
   const int npad = M <= 0 ? 0 : (M + 15) / 16 * 16;
