@@ -42,6 +42,28 @@ def test_argument_validation_without_gpu():
                                      0.1, None, 0, None, None) == 6                           # UNSUPPORTED D
 
 
+def test_residual_norm_argument_validation_without_gpu():
+    """tsds_linear_residual_norm's host checks: missing pointers, widths and
+    strides off the 8-element grid, misaligned buffers, a missing
+    workspace - all before any launch."""
+    import ctypes
+    from tri_sds_b200 import _lib
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    a = ctypes.addressof(buf)
+    al = (a + 255) // 256 * 256      # 16-byte aligned host addresses (never dereferenced)
+    P = ctypes.c_void_p
+    def call(x=al, w=al, res=al, out=al, ldo=64, n_out=64, nw=al, nout=al, nld=64, ws=al, wsb=4096, M=2, K=64):
+        return lib.tsds_linear_residual_norm(P(x), K, P(w), P(res), P(out), ldo, M, n_out, K, P(nw), P(nout), nld,
+                                             ctypes.c_float(1e-6), P(ws), wsb, None)
+    assert call(res=None) == 1             # INVALID: no residual
+    assert call(nw=None) == 1              # INVALID: no norm weights
+    assert call(n_out=60, ldo=64) == 1     # INVALID: width off the 8-element grid
+    assert call(nld=60) == 1               # INVALID: norm_out stride below the width
+    assert call(nout=al + 2) == 2          # ALIGN
+    assert call(ws=None) == 4              # WORKSPACE: the one-launch path needs one
+
+
 def test_attention_row_and_cache_limits_without_gpu():
     """tsds_verify_attention's size checks (host only, before any device
     call): the default kernel takes up to 1024 query rows per kv head, the
