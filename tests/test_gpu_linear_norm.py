@@ -53,12 +53,16 @@ def _check(ops, M, n_out, K, seed, eps=1e-6):
     assert (norm.float() - exp).abs().max().item() <= 2e-2 * exp.abs().max().item() + 1e-2
 
 
-@pytest.mark.parametrize("M", [1, 4, 26, 40, 208, 256])
-@pytest.mark.parametrize("n_out,K", [(5120, 8192), (2560, 4096), (1024, 512), (5120, 25600)])
+# (M, n_out, K): the 32B O and 4B O/down shapes and a small one at decode / tree
+# verify / B=8 verify row counts and the one-launch maximum; the 32B down
+# projection at the two verify row counts
+CASES = [(M, n, k) for M in (1, 4, 26, 40, 208, 256) for n, k in ((5120, 8192), (2560, 4096), (1024, 512))] + \
+        [(26, 5120, 25600), (208, 5120, 25600)]
+
+
+@pytest.mark.parametrize("M,n_out,K", CASES)
 def test_residual_norm_equals_the_two_launches(lib_ops, M, n_out, K):
     _, ops = lib_ops
-    if n_out == 5120 and K == 25600 and M not in (26, 208):
-        pytest.skip("the down projection's shape at the verify row counts only")
     _check(ops, M, n_out, K, seed=M * 31 + n_out)
 
 
